@@ -1,0 +1,444 @@
+"""CPU oracle for the PTCG policy-learning hot path.
+
+TEST INFRASTRUCTURE ONLY.  Nothing in the product path imports this module:
+only tests/, `__graft_entry__.smoke()` and bench.py's CPU-baseline /
+reference leg use it, and only as the checker or the timed CPU baseline.
+
+It restates, in functional fp32 torch on the CPU, the reference's own
+algorithm for every piece of the path:
+
+* `forward_core` / `oracle_value` / `forward_train` -- PTCGTransformer
+  (ptcg/rl/model.py:185-341), including its prefix slicing to the longest
+  valid token run (model.py:237-244) and the -1e9 logit mask (model.py:274);
+* `aux_loss` -- the belief / blind-V losses that the native backward applies
+  (native/model/ptcg_model2.cu:219-285, coefficients ptcg_model.cu:85-87);
+* `ppo_loss` -- the fused clipped-PPO kernel with its analytic gradients
+  (native/src/pufferlib.cu:1010-1248, advantage stats :1307-1363);
+* `adam_step` -- torch.nn.utils.clip_grad_norm_ + torch.optim.Adam, the
+  optimizer BASELINE.json mandates in place of muon_step;
+* `sample_logits` -- inverse-CDF masked sampling (pufferlib.cu:584-718) fed
+  with caller-supplied uniforms instead of curand Philox;
+* `negamax_advantage` -- seat-flipping GAE/V-trace (ptcg_model2.cu:288-321).
+
+Parity of this restatement with the reference is pinned by
+tests/test_oracle_golden.py against fixtures that tests/golden/make_golden.py
+produced by running the reference's ptcg/rl/model.py itself.
+"""
+from __future__ import annotations
+
+import math
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_PKG = os.path.join(os.path.dirname(_HERE), "kaggle-ptcg-ai-battle_b200")
+
+
+def _load_config():
+    # The shape/param-table definitions are plain Python shared with the
+    # package; load that file directly (no CUDA library involved).
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "_ptcg_oracle_config", os.path.join(_PKG, "config.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules.setdefault("_ptcg_oracle_config", mod)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+cfg = _load_config()
+Shape = cfg.Shape
+
+
+def params_from_blob(blob, s, requires_grad=False):
+    """name -> fp32 tensor view of the packed blob (PT_PARAMS order)."""
+    t = torch.as_tensor(np.asarray(blob, np.float32)).clone()
+    out, off = {}, 0
+    for name, shp in cfg.param_table(s):
+        n = int(np.prod(shp))
+        p = t[off:off + n].view(shp).clone()
+        p.requires_grad_(requires_grad)
+        out[name] = p
+        off += n
+    assert off == t.numel(), (off, t.numel())
+    return out
+
+
+def blob_from_params(P, s):
+    return np.concatenate([P[name].detach().reshape(-1).numpy()
+                           for name, _ in cfg.param_table(s)]).astype(np.float32)
+
+
+def tables_to_torch(tabs):
+    return {k: torch.as_tensor(v) for k, v in tabs.items()}
+
+
+def _lin(x, P, pre):
+    return F.linear(x, P[pre + "_w"], P[pre + "_b"])
+
+
+def _ln(x, P, pre):
+    return F.layer_norm(x, (x.shape[-1],), P[pre + "_w"], P[pre + "_b"], 1e-5)
+
+
+def _take(obs, s, name):
+    a, b = s.offsets[name]
+    return obs[:, a:b]
+
+
+def card_table(P, T, s):
+    """CardVec / AttackVec rebuilt every forward (model.py:185-205)."""
+    att = F.gelu(_lin(torch.cat([P["attack_id_emb"], T["att_static"],
+                                 T["att_text"]], -1), P, "attack_mlp"))
+    ca = T["card_attacks"].long()
+    a = att[ca]
+    a_mask = (ca > 0).unsqueeze(-1)
+    a_mean = (a * a_mask).sum(1) / a_mask.sum(1).clamp(min=1)
+    a_max = (a * a_mask).amax(1)
+    cs = T["card_skills"].long()
+    sk = F.gelu(_lin(torch.cat([P["skill_id_emb"], T["skill_text"]], -1),
+                     P, "skill_mlp"))[cs]
+    s_mask = (cs > 0).unsqueeze(-1)
+    s_mean = (sk * s_mask).sum(1) / s_mask.sum(1).clamp(min=1)
+    s_max = (sk * s_mask).amax(1)
+    cin = torch.cat([P["card_id_emb"], T["card_static"], T["card_text"],
+                     a_mean, a_max, s_mean, s_max], -1)
+    h = F.gelu(_lin(_ln(cin, P, "card_ln"), P, "card_mlp1"))
+    return _lin(h, P, "card_mlp2"), att
+
+
+def block(x, keep, P, pre, heads):
+    """Pre-LN block (model.py:70-91)."""
+    B, L, D = x.shape
+    h = _ln(x, P, pre + "ln1")
+    q, k, v = _lin(h, P, pre + "qkv").view(B, L, 3, heads, D // heads) \
+        .permute(2, 0, 3, 1, 4).unbind(0)
+    a = F.scaled_dot_product_attention(q, k, v, attn_mask=keep)
+    x = x + _lin(a.transpose(1, 2).reshape(B, L, D), P, pre + "proj")
+    h2 = F.gelu(_lin(_ln(x, P, pre + "ln2"), P, pre + "ffn1"))
+    return x + _lin(h2, P, pre + "ffn2")
+
+
+def forward_core(P, T, obs, s):
+    """model.py:207-276 (_core).  Returns the raw (unmasked) option scores as
+    well as the -1e9-masked logits."""
+    B = obs.shape[0]
+    NC, NA = s.n_cards, s.n_attacks
+    card_vec, att_vec = card_table(P, T, s)
+    tok_i = _take(obs, s, "tok_int").reshape(B, s.ltok, 5).long()
+    tok_f = _take(obs, s, "tok_float").reshape(B, s.ltok, s.tok_f)
+    cid = tok_i[:, :, 0].clamp(0, NC - 1)
+    t0, t1 = tok_i[:, :, 3], tok_i[:, :, 4]
+    tool_vec = card_vec[t0.clamp(0, NC - 1)] * (t0 > 0).unsqueeze(-1) + \
+        card_vec[t1.clamp(0, NC - 1)] * (t1 > 0).unsqueeze(-1)
+    x = _lin(torch.cat([
+        card_vec[cid], tool_vec, tok_f,
+        P["zone_emb"][tok_i[:, :, 1].clamp(0, cfg.N_ZONES - 1)],
+        P["owner_emb"][tok_i[:, :, 2].clamp(0, cfg.N_OWNERS - 1)]], -1),
+        P, "token_proj")
+    g = _lin(F.gelu(_lin(_take(obs, s, "global_f"), P, "global1")), P, "global2")
+    di = _take(obs, s, "dec_int").long()
+    dec_in = torch.cat([
+        P["sel_type_emb"][di[:, 0].clamp(0, cfg.N_SELECT_TYPES - 1)],
+        P["ctx_emb"][di[:, 1].clamp(0, cfg.N_CONTEXTS - 1)],
+        card_vec[di[:, 2].clamp(0, NC - 1)],
+        card_vec[di[:, 3].clamp(0, NC - 1)],
+        att_vec[di[:, 4].clamp(0, NA - 1)],
+        att_vec[di[:, 5].clamp(0, NA - 1)],
+        card_vec[di[:, 6].clamp(0, NC - 1)],
+        card_vec[di[:, 7].clamp(0, NC - 1)],
+        _take(obs, s, "dec_float")], -1)
+    d_vec = _lin(F.gelu(_lin(dec_in, P, "dec1")), P, "dec2")
+    x = x + _lin(torch.cat([g, d_vec], -1), P, "bcast").unsqueeze(1)
+
+    valid = tok_i[:, :, 1] > 0
+    L = int(valid.sum(1).max().item())
+    x = torch.cat([P["readout"].expand(B, 1, -1), x[:, :L]], 1)
+    keep = torch.cat([torch.ones(B, 1, dtype=torch.bool), valid[:, :L]],
+                     1).view(B, 1, 1, -1)
+    for i in range(s.layers):
+        x = block(x, keep, P, f"b{i}_", s.heads)
+    h = _ln(x, P, "lnf")
+    r = h[:, 0]
+
+    oi = _take(obs, s, "opt_int").reshape(B, s.nopt, 6).long()
+    of = _take(obs, s, "opt_float").reshape(B, s.nopt, cfg.OPT_F)
+    hz = torch.zeros(B, s.ltok + 1, s.d)
+    hz[:, 1:L + 1] = h[:, 1:]
+    i1 = oi[:, :, 1].clamp(0, s.ltok)
+    i2 = oi[:, :, 2].clamp(0, s.ltok)
+    p1 = hz.gather(1, i1.unsqueeze(-1).expand(-1, -1, s.d))
+    p2 = hz.gather(1, i2.unsqueeze(-1).expand(-1, -1, s.d))
+    q = _lin(F.gelu(_lin(torch.cat([
+        P["opt_type_emb"][oi[:, :, 0].clamp(0, cfg.N_OPT_TYPES - 1)],
+        p1, p2,
+        _lin(card_vec[oi[:, :, 3].clamp(0, NC - 1)], P, "opt_card"),
+        _lin(att_vec[oi[:, :, 4].clamp(0, NA - 1)], P, "opt_attack"),
+        of], -1), P, "q1")), P, "q2")
+    rr = r.unsqueeze(1).expand(-1, s.nopt, -1)
+    gg = g.unsqueeze(1).expand(-1, s.nopt, -1)
+    dd = d_vec.unsqueeze(1).expand(-1, s.nopt, -1)
+    scores = _lin(F.gelu(_lin(torch.cat([q, rr, gg, dd, q * rr], -1),
+                              P, "score1")), P, "score2").squeeze(-1)
+    logits = scores.masked_fill(_take(obs, s, "opt_mask") == 0, -1e9)
+    return dict(scores=scores, logits=logits, r=r, g=g, h=h, L=L,
+                valid=valid, card_vec=card_vec, tok_i=tok_i)
+
+
+def oracle_value(P, obs, c, s):
+    """Critic top over [critic_readout | trunk | oracle tokens]
+    (model.py:278-308)."""
+    B = obs.shape[0]
+    o = _take(obs, s, "oracle")
+    H, S_, Pz = cfg.ORACLE_HAND, cfg.ORACLE_SPLIT, cfg.ORACLE_PRIZE
+    hand = o[:, :H * 2].reshape(B, H, 2)
+    split = o[:, H * 2:H * 2 + S_ * 3].reshape(B, S_, 3)
+    prize = o[:, H * 2 + S_ * 3:].reshape(B, Pz, 2)
+    ids = torch.cat([hand[:, :, 0], split[:, :, 0], prize[:, :, 0]],
+                    1).long().clamp(0, s.n_cards - 1)
+    feats = torch.zeros(B, cfg.N_ORACLE_TOKENS, 6)
+    feats[:, :H, 0] = 1.0
+    feats[:, :H, 3] = hand[:, :, 1]
+    feats[:, H:H + S_, 1] = 1.0
+    feats[:, H:H + S_, 4] = split[:, :, 1]
+    feats[:, H:H + S_, 5] = split[:, :, 2]
+    feats[:, H + S_:, 2] = 1.0
+    feats[:, H + S_:, 3] = prize[:, :, 1]
+    otok = _lin(torch.cat([c["card_vec"][ids], feats], -1), P, "oracle_proj")
+    x = torch.cat([P["critic_readout"].expand(B, 1, -1), c["h"], otok], 1)
+    one = torch.ones(B, 1, dtype=torch.bool)
+    keep = torch.cat([one, one, c["valid"][:, :c["L"]], ids > 0],
+                     1).view(B, 1, 1, -1)
+    x = block(x, keep, P, "c0_", s.heads)
+    return _lin(F.gelu(_lin(torch.cat([x[:, 0], c["g"]], -1), P, "oracle_v1")),
+                P, "oracle_v2")
+
+
+def forward_eval(P, T, obs, s):
+    """(raw scores, masked logits, oracle value) -- model.py:315-321 with
+    critic="oracle"."""
+    c = forward_core(P, T, obs, s)
+    v = oracle_value(P, obs, c, s)
+    return c["scores"], c["logits"], v[:, 0]
+
+
+def forward_train(P, T, obs, s):
+    """model.py:326-341: all heads."""
+    c = forward_core(P, T, obs, s)
+    rg = torch.cat([c["r"], c["g"]], -1)
+    return dict(
+        scores=c["scores"], logits=c["logits"],
+        oracle_v=oracle_value(P, obs, c, s)[:, 0],
+        blind_v=_lin(F.gelu(_lin(rg, P, "value1")), P, "value2")[:, 0],
+        hand_lin=_lin(rg, P, "aux_hand"),
+        prize_logits=_lin(c["h"][:, 1:], P, "aux_prize").squeeze(-1),
+        L=c["L"], tok_i=c["tok_i"])
+
+
+def aux_targets(obs, s):
+    """Opponent-hand count targets and my-prize indicators
+    (ptcg_model2.cu:219-236)."""
+    B = obs.shape[0]
+    o = _take(obs, s, "oracle").numpy()
+    NC = s.n_cards
+    hand_tgt = np.zeros((B, NC), np.float32)
+    prized = np.zeros((B, NC), np.float32)
+    for n in range(B):
+        for k in range(cfg.ORACLE_HAND):
+            i = int(o[n, 2 * k]); cnt = np.float32(o[n, 2 * k + 1]) * np.float32(4.0)
+            if 0 < i < NC and i != NC - 1 and cnt != 0:
+                hand_tgt[n, i] += cnt
+        for k in range(cfg.ORACLE_PRIZE):
+            i = int(o[n, 120 + 2 * k]); cnt = o[n, 120 + 2 * k + 1]
+            if 0 < i < NC and cnt > 0:
+                prized[n, i] = 1.0
+    return torch.as_tensor(hand_tgt), torch.as_tensor(prized)
+
+
+def aux_loss(out, obs, returns, s):
+    """Blind-V MSE (x1.0), opp-hand softplus MSE (x0.1) and prize BCE over
+    MY_UNSEEN tokens (x0.1, averaged over the batch's unseen-token count)
+    -- the losses whose gradients ptcg_model4.cu:31-63 injects."""
+    B = obs.shape[0]
+    hand_tgt, prized = aux_targets(obs, s)
+    l_blind = cfg.AUX_VF_COEF * 0.5 * ((out["blind_v"] - returns) ** 2).mean()
+    pred = F.softplus(out["hand_lin"])
+    l_hand = cfg.AUX_HAND_COEF * ((pred - hand_tgt) ** 2).mean()
+    L = out["L"]
+    tok_i = out["tok_i"][:, :L]
+    unseen = tok_i[:, :, 1] == cfg.ZONE_MY_UNSEEN
+    cid = tok_i[:, :, 0].clamp(0, s.n_cards - 1)
+    tgt = prized.gather(1, cid)
+    cnt = max(float(unseen.sum()), 1.0)
+    bce = F.binary_cross_entropy_with_logits(out["prize_logits"], tgt,
+                                             reduction="none")
+    l_prize = cfg.AUX_PRIZE_COEF * (bce * unseen).sum() / cnt
+    return l_blind + l_hand + l_prize, dict(blind=l_blind, hand=l_hand,
+                                            prize=l_prize)
+
+
+# ------------------------------------------------------------------ PPO loss
+def ppo_loss(scores, mask, values_pred, actions, old_logp, adv, values,
+             returns, prio, n_seg, horizon, clip=0.2, vf_clip=0.2,
+             vf_coef=0.5, ent_coef=0.01):
+    """Restatement of ppo_var_mean + ppo_loss_compute (pufferlib.cu:1010-1248,
+    1307-1363) for one discrete head of NOPT options.  All arrays are
+    (n_seg*horizon, ...) in (segment, t) order; prio is per segment.
+    Returns (stats dict, d_scores, d_values) with d_scores the gradient w.r.t.
+    the raw scores (masked entries get the reference's -1e4 logit)."""
+    f32 = np.float32
+    scores = np.asarray(scores, f32); mask = np.asarray(mask, f32)
+    vp = np.asarray(values_pred, f32); act = np.asarray(actions).astype(np.int64)
+    old = np.asarray(old_logp, f32); adv = np.asarray(adv, f32)
+    val = np.asarray(values, f32); ret = np.asarray(returns, f32)
+    w = np.repeat(np.asarray(prio, f32), horizon)
+    NT = scores.shape[0]
+    inv = f32(1.0) / f32(NT)
+    a64 = adv.astype(np.float64)
+    mean = a64.mean()
+    var = ((a64 - mean) ** 2).sum() / (NT - 1)
+    adv_n = ((a64 - mean) / (np.sqrt(var) + 1e-8)).astype(np.float64)
+
+    vpd, vald, retd = vp.astype(np.float64), val.astype(np.float64), ret.astype(np.float64)
+    v_err = vpd - vald
+    v_clip = vald + np.clip(v_err, -vf_clip, vf_clip)
+    lu = (vpd - retd) ** 2
+    lc = (v_clip - retd) ** 2
+    v_loss = 0.5 * np.maximum(lu, lc)
+    use_c = lc > lu
+    inside = (v_err >= -vf_clip) & (v_err <= vf_clip)
+    dv = np.where(use_c, np.where(inside, v_clip - retd, 0.0), vpd - retd)
+    d_values = (inv * vf_coef * dv).astype(f32)
+
+    l = np.where(mask == 0, -1e4, scores.astype(np.float64))
+    m = l.max(1, keepdims=True)
+    lse = m[:, 0] + np.log(np.exp(l - m).sum(1))
+    logp = l - lse[:, None]
+    p = np.exp(logp)
+    ent = -(p * logp).sum(1)
+    new_logp = logp[np.arange(NT), act]
+    logratio = new_logp - old
+    ratio = np.exp(logratio)
+    rc = np.clip(ratio, 1 - clip, 1 + clip)
+    wa = -w * adv_n
+    pg1, pg2 = wa * ratio, wa * rc
+    pg = np.maximum(pg1, pg2)
+    d_ratio = wa * inv
+    zero = (pg2 > pg1) & ((ratio <= 1 - clip) | (ratio >= 1 + clip))
+    d_ratio = np.where(zero, 0.0, d_ratio)
+    d_nlp = d_ratio * ratio
+    d_ent = inv * (-ent_coef)
+    onehot = np.zeros_like(l); onehot[np.arange(NT), act] = 1.0
+    d_scores = onehot * d_nlp[:, None] - p * d_nlp[:, None] \
+        + d_ent * p * (-ent[:, None] - logp)
+    d_scores = np.where(mask == 0, 0.0, d_scores).astype(f32)
+    stats = dict(
+        pg=float((pg * inv).sum()), vf=float((v_loss * inv).sum()),
+        ent=float((ent * inv).sum()),
+        total=float(((pg + vf_coef * v_loss - ent_coef * ent) * inv).sum()),
+        old_approx_kl=float((-logratio * inv).sum()),
+        approx_kl=float((((ratio - 1) - logratio) * inv).sum()),
+        clipfrac=float(((np.abs(ratio - 1) > clip) * inv).sum()),
+        adv_mean=float(mean), adv_var=float(var))
+    return stats, d_scores, d_values, new_logp.astype(f32), ratio.astype(f32)
+
+
+def masked_logp(scores, mask):
+    l = np.where(np.asarray(mask) == 0, -1e4, np.asarray(scores, np.float64))
+    m = l.max(1, keepdims=True)
+    lse = m[:, 0] + np.log(np.exp(l - m).sum(1))
+    return l - lse[:, None]
+
+
+# ---------------------------------------------------------------- train step
+def train_grads(P, T, obs, s, actions, old_logp, adv, values, returns, prio,
+                n_seg, horizon, clip=0.2, vf_clip=0.2, vf_coef=0.5,
+                ent_coef=0.01):
+    """Full PPO minibatch gradient: forward_train, the PPO loss's analytic
+    gradient injected at (scores, oracle value), plus autograd of the aux
+    losses -- the same total the native backward accumulates
+    (ptcg_model4.cu:10-190 driven by pufferlib.cu:2039-2060)."""
+    obs_t = torch.as_tensor(obs)
+    out = forward_train(P, T, obs_t, s)
+    mask = _take(obs_t, s, "opt_mask").numpy()
+    stats, d_sc, d_v, _, _ = ppo_loss(
+        out["scores"].detach().numpy(), mask, out["oracle_v"].detach().numpy(),
+        actions, old_logp, adv, values, returns, prio, n_seg, horizon,
+        clip, vf_clip, vf_coef, ent_coef)
+    l_aux, parts = aux_loss(out, obs_t, torch.as_tensor(returns), s)
+    surrogate = (out["scores"] * torch.as_tensor(d_sc)).sum() + \
+        (out["oracle_v"] * torch.as_tensor(d_v)).sum() + l_aux
+    for p in P.values():
+        p.grad = None
+    surrogate.backward()
+    grads = {k: (p.grad if p.grad is not None else torch.zeros_like(p))
+             for k, p in P.items()}
+    stats.update({"aux_" + k: float(v) for k, v in parts.items()})
+    return out, stats, grads
+
+
+def adam_step(P, grads, state, lr=3e-4, betas=(0.9, 0.999), eps=1e-8,
+              max_norm=1.0):
+    """torch.nn.utils.clip_grad_norm_(max_norm) followed by torch.optim.Adam
+    `state` carries the optimizer across calls."""
+    names = [n for n in P]
+    if "opt" not in state:
+        state["opt"] = torch.optim.Adam([P[n] for n in names], lr=lr,
+                                        betas=betas, eps=eps, foreach=False)
+    for n in names:
+        P[n].grad = grads[n].clone()
+    norm = torch.nn.utils.clip_grad_norm_([P[n] for n in names], max_norm)
+    state["opt"].step()
+    return float(norm)
+
+
+# ------------------------------------------------------------------ sampling
+def sample_logits(scores, mask, uniforms):
+    """Inverse-CDF sample of the masked softmax (pufferlib.cu:614-708), the
+    masked logit being -1e4; falls back to the last legal slot when rounding
+    leaves the CDF short of u.  Returns (actions, logprob, margin) where
+    margin is |u - nearest CDF boundary| (float64), used by tests to skip
+    draws that sit on a rounding knife-edge."""
+    l = np.where(np.asarray(mask) == 0, -1e4, np.asarray(scores, np.float64))
+    m = l.max(1, keepdims=True)
+    lse = m[:, 0] + np.log(np.exp(l - m).sum(1))
+    p = np.exp(l - lse[:, None])
+    cdf = np.cumsum(p, 1)
+    u = np.asarray(uniforms, np.float64)
+    n, a_n = l.shape
+    act = np.full(n, -1, np.int64)
+    for i in range(n):
+        hit = np.nonzero(u[i] < cdf[i])[0]
+        if hit.size:
+            act[i] = hit[0]
+        else:
+            legal = np.nonzero(np.asarray(mask)[i] != 0)[0]
+            act[i] = legal[-1] if legal.size else a_n - 1
+    margin = np.abs(cdf - u[:, None]).min(1)
+    logp = l[np.arange(n), act] - lse
+    return act, logp.astype(np.float32), margin
+
+
+def negamax_advantage(values, rewards, dones, importance, seats, gamma, lam,
+                      rho_clip, c_clip):
+    """k_negamax_adv (ptcg_model2.cu:288-311): (B, T) arrays, seats (B, T) read
+    from the obs ACTOR_SEAT column; the sign flips when the actor changes."""
+    B, T = values.shape
+    adv = np.zeros((B, T), np.float32)
+    f = np.float32
+    for b in range(B):
+        last = f(0)
+        for t in range(T - 2, -1, -1):
+            sign = f(1) if seats[b, t] == seats[b, t + 1] else f(-1)
+            sg = sign * (f(1) - f(dones[b, t + 1]))
+            imp = f(importance[b, t])
+            rho = min(imp, f(rho_clip)); cc = min(imp, f(c_clip))
+            delta = rho * (f(rewards[b, t + 1]) + f(gamma) * f(values[b, t + 1]) * sg
+                           - f(values[b, t]))
+            last = f(delta + f(gamma) * f(lam) * cc * sg * last)
+            adv[b, t] = last
+    return adv
