@@ -1,0 +1,203 @@
+/*
+ * ptcg_b200.h -- C-ABI of the B200-native (sm_100a) PTCG policy-learning
+ * hot path.  Plain pointers and sizes only; every entry point returns 0 on
+ * success and a nonzero PTCG_E* code on failure, with a message retrievable
+ * from ptcg_last_error() (the reference aborts with a message to stderr).
+ *
+ * All device pointers are CUDA global memory on the model's device; `stream`
+ * is a cudaStream_t passed as void*.  Nothing in the forward / backward /
+ * loss / optimizer entry points allocates or synchronises, so a caller may
+ * capture them in a CUDA graph after ptcg_reserve().
+ *
+ * Each declaration names the reference interface it replaces
+ * (paths relative to the dipamc/kaggle-ptcg-ai-battle checkout).
+ */
+#ifndef PTCG_B200_H
+#define PTCG_B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PTCG_B200_ABI_VERSION 1
+
+enum {
+    PTCG_OK = 0,
+    PTCG_EINVAL = 1,     /* bad argument / shape */
+    PTCG_ECUDA = 2,      /* CUDA runtime error */
+    PTCG_ESTATE = 3,     /* call out of order (no weights, not reserved...) */
+    PTCG_ERANGE = 4      /* size beyond what was reserved */
+};
+
+enum { PTCG_FP32 = 0, PTCG_BF16 = 1 };
+
+/* Runtime model shape.  Replaces the compile-time PT_D/PT_H/PT_FFN/PT_LAYERS,
+ * PT_LTOK, PT_NOPT, PT_NC/PT_NA/PT_NS and the token feature width
+ * (native/model/ptcg_model.cu:14-82; native/tools/native_weights.py:24-37).
+ * d/heads must give a head width of 32. */
+typedef struct PtcgShape {
+    int d, heads, ffn, layers;
+    int ltok, nopt, tok_f;
+    int n_cards, n_attacks, n_skills;
+} PtcgShape;
+
+typedef struct PtcgModel PtcgModel;
+
+const char* ptcg_last_error(void);
+int ptcg_abi_version(void);
+
+/* ---- layout ------------------------------------------------------------
+ * Packed fp32 weight blob order = PT_PARAMS (native/model/ptcg_model.cu:95-126,
+ * mirrored by native/tools/native_weights.py:45-91).  cols == 0 for 1-D. */
+long ptcg_obs_size(const PtcgShape* s);
+int  ptcg_num_params(const PtcgShape* s);
+int  ptcg_param_info(const PtcgShape* s, int i, const char** name, long* rows, long* cols);
+long ptcg_param_total(const PtcgShape* s);
+
+/* ---- lifetime ------------------------------------------------------------
+ * ptcg_create replaces Encoder.create_weights + reg_params and the params /
+ * grads Allocator arenas (native/src/models.cu:35-76, ocean.cu:5-46,
+ * native/src/kernels.cu:412-474): it allocates the fp32 master-weight arena
+ * (16-byte aligned per tensor, PT_PARAMS order), the mirrored grad arena and
+ * the Adam moments on `device`.  precision = PTCG_FP32 (parity mode, SIMT fp32
+ * GEMMs) or PTCG_BF16 (tcgen05 bf16 GEMMs, fp32 accumulate). */
+int ptcg_create(const PtcgShape* s, int precision, int device, PtcgModel** out);
+int ptcg_destroy(PtcgModel* m);
+
+/* Static card/attack/skill tables, host pointers, row-major.  Replaces the
+ * pt_tab_* imports from native/ptcg/tables.c (native/model/ptcg_model2.cu:390-419).
+ * card_static NCx58, card_attacks NCx4 (int32), card_skills NCx2 (int32),
+ * att_static NAx15, card_text NCx128, att_text NAx64, skill_text NSx64. */
+int ptcg_set_tables(PtcgModel* m, const float* card_static, const int* card_attacks,
+                    const int* card_skills, const float* att_static,
+                    const float* card_text, const float* att_text,
+                    const float* skill_text);
+
+/* Packed fp32 blob <-> master weights (host pointer, n = ptcg_param_total).
+ * Replaces ptcg_load_init_weights_regs (native/model/ptcg_model4.cu:196-233)
+ * and the packed save path of native/src/bindings.cu:202-215.  Loading also
+ * refreshes the bf16 compute copies and resets nothing else. */
+int ptcg_load_weights(PtcgModel* m, const float* packed, long n);
+int ptcg_save_weights(PtcgModel* m, float* packed, long n);
+
+/* Size activation workspaces: rollout forward for up to `rollout_rows`
+ * observations and train forward/backward for up to `train_rows` rows per
+ * call (a minibatch larger than train_rows is processed in micro-batches by
+ * ptcg_train_step).  Replaces Encoder.reg_rollout / reg_train
+ * (native/model/ptcg_model4.cu:260-266; ptcg_model3.cu:112-210). */
+int ptcg_reserve(PtcgModel* m, int rollout_rows, int train_rows);
+
+/* ---- Encoder vtable slots ------------------------------------------------
+ * Rollout forward: obs (n x obs_size, fp32, ids stored as floats) ->
+ * out (n x (nopt+1)) = [raw option scores | oracle value].
+ * Replaces Encoder.forward with train=0 (native/model/ptcg_model4.cu:269-275,
+ * ptcg_forward_core native/model/ptcg_model3.cu:246-356). */
+int ptcg_forward(PtcgModel* m, const float* obs, int n, float* out, void* stream);
+
+/* Train-path forward (saves activations for ptcg_backward, adds blind-V and
+ * the belief aux heads).  Replaces policy_forward_train ->
+ * ptcg_forward_core(train=1) (native/src/models.cu:791-797;
+ * native/model/ptcg_model3.cu:357-369). */
+int ptcg_forward_train(PtcgModel* m, const float* obs, int n, float* out, void* stream);
+
+/* Backward of the last ptcg_forward_train: grad (n x (nopt+1)) =
+ * [d raw scores | d oracle value]; `returns` (n) feeds the blind-V aux loss
+ * (the reference binds it through ptcg_bind_train_graph,
+ * native/model/ptcg_model2.cu:323-330).  aux_norm_rows / prize_count give the
+ * minibatch-wide normalisers of the aux losses (rows of the whole minibatch;
+ * number of MY_UNSEEN tokens in it, <= 0 means "count these rows").
+ * accumulate = 0 zeroes the grad arena first (native/model/ptcg_model4.cu:15-21),
+ * 1 adds to it (micro-batching).  Replaces Encoder.backward + Decoder.backward
+ * (ptcg_model4.cu:10-190, 277-306). */
+int ptcg_backward(PtcgModel* m, const float* grad, const float* returns,
+                  int aux_norm_rows, float prize_count, int accumulate, void* stream);
+
+/* ---- trainer hooks ----------------------------------------------------------
+ * Fused clipped-PPO + clipped value loss + entropy over the masked legal
+ * logits, forward and backward in one kernel.  Replaces ppo_var_mean +
+ * ppo_loss_compute + ppo_loss_reduce (native/src/pufferlib.cu:1010-1449).
+ * dec_out (nt x (nopt+1)) [scores | value], mask (nt x nopt), rows ordered
+ * (segment, t) with nt = n_seg*horizon; prio per segment.  Writes
+ * grad_dec (nt x (nopt+1)), new_logp/ratio (nt), stats[8] = {total, pg, vf,
+ * entropy, old_approx_kl, approx_kl, clipfrac, adv_var} (sums over rows,
+ * already divided by nt).  `scratch` is PTCG_PPO_SCRATCH_FLOATS(nt) device
+ * floats. */
+#define PTCG_PPO_SCRATCH_FLOATS(nt) (16 + 7 * (((nt) + 7) / 8))
+int ptcg_ppo_loss(const float* dec_out, int nopt, const float* mask,
+                  const float* actions, const float* old_logp,
+                  const float* advantages, const float* values,
+                  const float* returns, const float* prio, int n_seg, int horizon,
+                  float clip_coef, float vf_clip_coef, float vf_coef, float ent_coef,
+                  float* grad_dec, float* new_logp, float* ratio, float* stats,
+                  float* scratch, void* stream);
+
+/* Global-norm clip + fused mixed-precision Adam over the whole arena
+ * (fp32 master weights and moments, bf16 compute copies refreshed in the
+ * same pass).  Replaces muon_step (native/src/muon.cu:209-297) with the
+ * optimizer BASELINE names: torch.nn.utils.clip_grad_norm_(max_norm) +
+ * torch.optim.Adam.  gate (device float or NULL) vetoes the step when it is
+ * 0 or when the grad norm is not finite (native/src/pufferlib.cu:1286-1302).
+ * stats (device, 2 floats) receives {grad_norm, applied}. */
+int ptcg_adam_step(PtcgModel* m, float lr, float beta1, float beta2, float eps,
+                   float max_norm, const float* gate, float* stats, void* stream);
+
+/* Masked inverse-CDF sampling of the option scores + logprob + value copy.
+ * Replaces sample_logits (native/src/pufferlib.cu:584-718); uniforms (n)
+ * are supplied by the caller instead of a curand Philox state.  Masked
+ * logits are -1e4.  actions are written as float (the trainer's precision_t). */
+int ptcg_sample_logits(const float* dec_out, int n, int nopt, const float* mask,
+                       long mask_stride, const float* uniforms, float* actions,
+                       float* logprobs, float* values, void* stream);
+
+/* Seat-flipping GAE / V-trace over (B, T) rollouts; seats are read from
+ * obs[:, :, seat_col].  Replaces ptcg_puff_advantage
+ * (native/model/ptcg_model2.cu:288-321). */
+int ptcg_puff_advantage(const float* values, const float* rewards,
+                        const float* dones, const float* importance,
+                        const float* obs, long obs_size, int seat_col, int B, int T,
+                        float gamma, float lambda, float rho_clip, float c_clip,
+                        float* advantages, void* stream);
+
+/* Gradient-bucket hook for data parallelism: called on the host, in backward
+ * order, each time the grads in arena floats [offset, offset+count) are final
+ * for this step (only during the last micro-batch), with the compute stream.
+ * The callee typically records an event and starts an all-reduce of that
+ * bucket on its own stream.  Replaces the post-backward ncclAllReduce of
+ * native/src/muon.cu:212-213. */
+typedef void (*ptcg_grad_hook)(void* user, long offset, long count, void* stream);
+int ptcg_set_grad_hook(PtcgModel* m, ptcg_grad_hook fn, void* user);
+
+/* One PPO minibatch step: micro-batched forward_train -> PPO loss ->
+ * backward (grads accumulated over micro-batches, normalised over the whole
+ * minibatch), optional grad hook, then clip + Adam.  Replaces the body of the
+ * minibatch loop of train_impl (native/src/pufferlib.cu:1964-2118).
+ * obs (nt x obs_size) device; per-row arrays (nt); prio (n_seg).
+ * stats (device, 16 floats): [0..7] PPO stats as in ptcg_ppo_loss,
+ * [8] grad norm, [9] step applied, [10..12] aux losses (blind, hand, prize).
+ * If skip_adam != 0 the optimizer is not run (the caller reduces the grads
+ * and calls ptcg_adam_step itself). */
+int ptcg_train_step(PtcgModel* m, const float* obs, const float* actions,
+                    const float* old_logp, const float* advantages,
+                    const float* values, const float* returns, const float* prio,
+                    int n_seg, int horizon, float clip_coef, float vf_clip_coef,
+                    float vf_coef, float ent_coef, float lr, float beta1,
+                    float beta2, float eps, float max_norm, int skip_adam,
+                    float* stats, void* stream);
+
+/* ---- arenas (device memory owned by the model) -------------------------------
+ * which: 0 = fp32 master params, 1 = fp32 grads, 2 = Adam m, 3 = Adam v.
+ * n_floats includes the 16-byte alignment padding; arena offsets of each
+ * parameter come from ptcg_param_offset. */
+int ptcg_arena(PtcgModel* m, int which, float** ptr, long* n_floats);
+long ptcg_param_offset(PtcgModel* m, int i);
+/* Adam step counter (for checkpoint/resume). */
+int ptcg_get_step(PtcgModel* m, long* step);
+int ptcg_set_step(PtcgModel* m, long step);
+/* 64-bit checksum of the master weights (device, written to out[0] as two
+ * uint32 halves) for the cross-rank "weights identical" check. */
+int ptcg_weights_checksum(PtcgModel* m, unsigned int* out_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PTCG_B200_H */

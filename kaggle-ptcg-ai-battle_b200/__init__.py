@@ -10,3 +10,14 @@ when the library is missing -- there is no CPU fallback.
 from . import config, synth  # noqa: F401
 
 __all__ = ["config", "synth"]
+
+
+def __getattr__(name):
+    # computing pieces import lazily so config / synth work without the .so
+    if name in ("native", "policy", "build", "smoke"):
+        import importlib
+        return importlib.import_module(f"{__name__}.{name}")
+    if name == "PTCGPolicy":
+        from .policy import PTCGPolicy
+        return PTCGPolicy
+    raise AttributeError(name)

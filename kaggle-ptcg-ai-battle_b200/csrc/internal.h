@@ -1,0 +1,52 @@
+// Internal launcher interfaces shared by the ptcg_b200 translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+enum { DT_F32 = 0, DT_BF16 = 1 };
+enum { ACT_NONE = 0, ACT_GELU = 1, ACT_GELU_BWD = 2 };
+
+// C[m, n] = epilogue( alpha * sum_k A(m, k) * B(n, k) )
+//   A(m,k) = a_kmajor ? A[m*lda + k] : A[k*lda + m]
+//   B(n,k) = b_kmajor ? B[n*ldb + k] : B[k*ldb + n]
+// epilogue, in order: + bias[n]; + bcast[(m / bcast_group) * ld_bcast + n];
+//   act (GELU: pre-activation to out2 if set; GELU_BWD: * gelu'(aux[m, n]));
+//   output row r = remap(m); + resid[r * ld_resid + n]; + out[r, n] if
+//   accumulate; store to out (f32 or operand dtype); for act != GELU an out2
+//   receives a second copy of the final value.
+struct GemmArgs {
+    int M = 0, N = 0, K = 0;
+    int dtype = DT_F32;                      // operand dtype (A and B)
+    const void* A = nullptr; long lda = 0; int a_kmajor = 1;
+    const void* B = nullptr; long ldb = 0; int b_kmajor = 1;
+    float alpha = 1.f;
+    const float* bias = nullptr;
+    const float* bcast = nullptr; long ld_bcast = 0; int bcast_group = 1;
+    int act = ACT_NONE;
+    const void* aux = nullptr; long ld_aux = 0; int aux_dtype = DT_F32;
+    int remap_group = 0, remap_stride = 0, remap_off = 0;
+    const float* resid = nullptr; long ld_resid = 0;
+    void* out = nullptr; long ldo = 0; int out_dtype = DT_F32; int accumulate = 0;
+    void* out2 = nullptr; long ldo2 = 0; int out2_dtype = DT_F32;
+    // colsum[n] += sum_m (final value) in fp32, before any rounding to the
+    // output dtype (bias gradients of the next Linear down)
+    float* colsum = nullptr;
+    // fp32 operands may run on TF32 tensor cores (10-bit mantissa); 0 = exact fp32
+    int allow_tf32 = 0;
+};
+
+void gemm_simt(const GemmArgs& a, cudaStream_t s);
+// tcgen05 path: returns false if the problem is not supported (caller falls
+// back to the SIMT kernel, which is also sm_100a code in this library)
+bool gemm_tc(const GemmArgs& a, cudaStream_t s);
+bool gemm_tc_available();
+
+// attention over packed qkv rows: qkv [(n*L + l) * ldqkv + {0,D,2D} + h*32 + d]
+void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
+              void* out, long ldo, float* lse, int nseq, int L, int H,
+              cudaStream_t s);
+// dbias (nullable, 3*H*32 floats): += column sums of dqkv in fp32
+void attn_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
+              const void* out, long ldo, const void* dout, long lddo,
+              const float* lse, void* dqkv, long lddqkv, float* dbias, int nseq, int L,
+              int H, cudaStream_t s);

@@ -1,0 +1,978 @@
+// Model-specific kernels of the PTCG policy path: observation gathers and
+// their gradient scatters, LayerNorm, N=1 heads, aux losses, PPO loss,
+// sampler, negamax advantage and the fused Adam.  Included once, by model.cu.
+//
+// Semantics follow the reference kernels cited per kernel; layouts are this
+// library's own (activations row-major with padded leading dimensions).
+#pragma once
+#include "common.cuh"
+#include "internal.h"
+
+// Observation-row field offsets, computed on the host from PtcgShape
+// (ptcg/rl/buffers.py:212-237).
+struct ObsLayout {
+    int obs, toki, tokf, opti, optf, mask, glob, deci, decf, orc;
+    int ltok, lseq, nopt, tok_f, nc, na, ns;
+};
+
+static inline __device__ void st(float* p, float v) { *p = v; }
+static inline __device__ void st(bf16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+// ------------------------------------------------------------ concat rows
+struct Seg { const float* src; int ld, src_off, width, dst_off; };
+struct Segs { Seg s[8]; int n; };
+
+// out[r, seg.dst_off + c] = seg.src[r * seg.ld + seg.src_off + c]
+// (k_att_in / k_sk_in / k_card_in, native/model/ptcg_model.cu:231-286)
+__global__ void k_concat_rows(float* out, int ldo, int rows, int width, Segs g) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)rows * width) return;
+    int r = (int)(i / width), c = (int)(i % width);
+    for (int k = 0; k < g.n; k++) {
+        const Seg& s = g.s[k];
+        if (c >= s.dst_off && c < s.dst_off + s.width) {
+            out[(long)r * ldo + c] = s.src[(long)r * s.ld + s.src_off + (c - s.dst_off)];
+            return;
+        }
+    }
+}
+
+// masked mean / max pools of gathered attack / skill vectors; masked slots
+// are 0-valued participants of the max (ptcg_model.cu:243-266,
+// model.py:194-204).  arg = first index attaining the max.
+__global__ void k_pool(float* mean, float* mx, int ldm, int8_t* arg,
+                       const float* tab, const int* idx, int NC, int K, int E) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)NC * E) return;
+    int n = (int)(i / E), e = (int)(i % E);
+    float s = 0.f, m2 = -INFINITY;
+    int cnt = 0, am = 0;
+    for (int k = 0; k < K; k++) {
+        int id = idx[n * K + k];
+        float v = id > 0 ? tab[(long)id * E + e] : 0.f;
+        if (id > 0) { cnt++; s += v; }
+        if (v > m2) { m2 = v; am = k; }
+    }
+    mean[(long)n * ldm + e] = s / (float)(cnt > 0 ? cnt : 1);
+    mx[(long)n * ldm + e] = m2;
+    arg[i] = (int8_t)am;
+}
+
+// pool backward (ptcg_model2.cu:15-33): d_mean spread over unmasked slots,
+// d_max to the arg-max slot when unmasked.
+__global__ void k_pool_bwd(float* d_tab, const float* dsrc, int ld, int off_mean,
+                           int off_max, const int8_t* arg, const int* idx,
+                           int NC, int K, int E) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)NC * E) return;
+    int n = (int)(i / E), e = (int)(i % E);
+    int cnt = 0;
+    for (int k = 0; k < K; k++) cnt += idx[n * K + k] > 0;
+    float dm = dsrc[(long)n * ld + off_mean + e] / (float)(cnt > 0 ? cnt : 1);
+    float dx = dsrc[(long)n * ld + off_max + e];
+    int am = arg[i];
+    for (int k = 0; k < K; k++) {
+        int id = idx[n * K + k];
+        if (id <= 0) continue;
+        float g = dm + (k == am ? dx : 0.f);
+        if (g != 0.f) atomicAdd(&d_tab[(long)id * E + e], g);
+    }
+}
+
+// ------------------------------------------------------------- LayerNorm
+// one warp per row, eps 1e-5 (torch nn.LayerNorm), two-pass statistics
+template <typename TO>
+__global__ void k_ln_fwd(TO* y, long ldy, float* mean, float* rstd, const float* x,
+                         long ldx, const float* w, const float* b, int rows, int D) {
+    int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* xr = x + (long)row * ldx;
+    float s = 0.f;
+    for (int i = lane; i < D; i += 32) s += xr[i];
+    float mu = warp_sum(s) / D;
+    float v = 0.f;
+    for (int i = lane; i < D; i += 32) { float d = xr[i] - mu; v += d * d; }
+    float rs = rsqrtf(warp_sum(v) / D + 1e-5f);
+    if (lane == 0) { mean[row] = mu; rstd[row] = rs; }
+    TO* yr = y + (long)row * ldy;
+    for (int i = lane; i < D; i += 32) st(&yr[i], (xr[i] - mu) * rs * w[i] + b[i]);
+}
+
+// dx = LN'(dy) (+ dx if accumulate), optional copy in T; dw/db accumulate.
+// dw/db: per-block shared partials then one atomicAdd per column per block.
+template <typename TC>
+__global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long lddxc,
+                         float* dw, float* db, const float* dy, long lddy,
+                         const float* x, long ldx, const float* w, const float* mean,
+                         const float* rstd, int rows, int D, int rows_per_block) {
+    extern __shared__ float sh[];               // [2][D]
+    float* sw = sh;
+    float* sb = sh + D;
+    for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) sh[i] = 0.f;
+    __syncthreads();
+    int nw = blockDim.x >> 5, wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int r0 = blockIdx.x * rows_per_block;
+    int r1 = min(rows, r0 + rows_per_block);
+    for (int row = r0 + wid; row < r1; row += nw) {
+        const float* xr = x + (long)row * ldx;
+        const float* dyr = dy + (long)row * lddy;
+        float mu = mean[row], rs = rstd[row];
+        float s1 = 0.f, s2 = 0.f;
+        for (int i = lane; i < D; i += 32) {
+            float xh = (xr[i] - mu) * rs;
+            float g = dyr[i] * w[i];
+            s1 += g; s2 += g * xh;
+            atomicAdd(&sw[i], dyr[i] * xh);
+            atomicAdd(&sb[i], dyr[i]);
+        }
+        float m1 = warp_sum(s1) / D, m2 = warp_sum(s2) / D;
+        float* dxr = dx + (long)row * lddx;
+        for (int i = lane; i < D; i += 32) {
+            float xh = (xr[i] - mu) * rs;
+            float v = (dyr[i] * w[i] - m1 - xh * m2) * rs;
+            if (accumulate) v += dxr[i];
+            dxr[i] = v;
+            if (dxc) st(&dxc[(long)row * lddxc + i], v);
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        if (sw[i] != 0.f) atomicAdd(&dw[i], sw[i]);
+        if (sb[i] != 0.f) atomicAdd(&db[i], sb[i]);
+    }
+}
+
+// ---------------------------------------------------------- token gather
+// [card_vec(cid) | sum tool card_vecs (id > 0) | tok_f | zone_emb | owner_emb]
+// (k_tok_cat, ptcg_model.cu:289-321; model.py:211-221)
+template <typename T>
+__global__ void k_tok_cat(T* out, long ldo, const float* obs, ObsLayout L,
+                          const float* cv, const float* zemb, const float* oemb,
+                          int R, int tok_in) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * L.ltok * tok_in) return;
+    int c = (int)(i % tok_in);
+    long nl = i / tok_in;
+    int l = (int)(nl % L.ltok), n = (int)(nl / L.ltok);
+    const float* row = obs + (long)n * L.obs;
+    const float* ti = row + L.toki + l * 5;
+    float v;
+    if (c < 128) {
+        v = cv[(long)id_clamp(ti[0], L.nc) * 128 + c];
+    } else if (c < 256) {
+        int e = c - 128;
+        int t0 = (int)ti[3], t1 = (int)ti[4];
+        float a = t0 > 0 ? cv[(long)(t0 >= L.nc ? L.nc - 1 : t0) * 128 + e] : 0.f;
+        float b = t1 > 0 ? cv[(long)(t1 >= L.nc ? L.nc - 1 : t1) * 128 + e] : 0.f;
+        v = a + b;
+    } else if (c < 256 + L.tok_f) {
+        v = row[L.tokf + l * L.tok_f + (c - 256)];
+    } else if (c < 256 + L.tok_f + 8) {
+        v = zemb[id_clamp(ti[1], 16) * 8 + (c - 256 - L.tok_f)];
+    } else {
+        v = oemb[id_clamp(ti[2], 4) * 4 + (c - 264 - L.tok_f)];
+    }
+    st(&out[nl * ldo + c], v);
+}
+
+// x0 readout rows + key mask keep = [1, zone > 0] (k_x0, ptcg_model.cu:348-368)
+__global__ void k_x0_readout(float* x0, uint8_t* keep, const float* readout,
+                             const float* obs, ObsLayout L, int R, int D) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    long nrd = (long)R * D;
+    if (i < nrd) {
+        int n = (int)(i / D), d = (int)(i % D);
+        x0[(long)n * L.lseq * D + d] = readout[d];
+    }
+    if (i < (long)R * L.lseq) {
+        int n = (int)(i / L.lseq), l = (int)(i % L.lseq);
+        uint8_t kp = 1;
+        if (l > 0) kp = obs[(long)n * L.obs + L.toki + (l - 1) * 5 + 1] > 0.f;
+        keep[i] = kp;
+    }
+}
+
+// decision-encoder input (696): [sel8, ctx32, cv_eff, cv_ctx, av_my, av_opp,
+// cv_msup, cv_osup, decf16] (k_dec_in, ptcg_model.cu:324-344)
+__global__ void k_dec_in(float* out, const float* obs, ObsLayout L, const float* cv,
+                         const float* av, const float* semb, const float* cemb, int R) {
+    const int W = 696;
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * W) return;
+    int n = (int)(i / W), c = (int)(i % W);
+    const float* row = obs + (long)n * L.obs;
+    const float* di = row + L.deci;
+    float v;
+    if (c < 8) v = semb[id_clamp(di[0], 29) * 8 + c];
+    else if (c < 40) v = cemb[id_clamp(di[1], 65) * 32 + (c - 8)];
+    else if (c < 168) v = cv[(long)id_clamp(di[2], L.nc) * 128 + (c - 40)];
+    else if (c < 296) v = cv[(long)id_clamp(di[3], L.nc) * 128 + (c - 168)];
+    else if (c < 360) v = av[(long)id_clamp(di[4], L.na) * 64 + (c - 296)];
+    else if (c < 424) v = av[(long)id_clamp(di[5], L.na) * 64 + (c - 360)];
+    else if (c < 552) v = cv[(long)id_clamp(di[6], L.nc) * 128 + (c - 424)];
+    else if (c < 680) v = cv[(long)id_clamp(di[7], L.nc) * 128 + (c - 552)];
+    else v = row[L.decf + (c - 680)];
+    out[i] = v;
+}
+
+__global__ void k_dec_in_bwd(float* d_cv, float* d_av, float* d_semb, float* d_cemb,
+                             const float* g, const float* obs, ObsLayout L, int R) {
+    const int W = 696;
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * W) return;
+    int n = (int)(i / W), c = (int)(i % W);
+    float v = g[i];
+    if (v == 0.f || c >= 680) return;
+    const float* di = obs + (long)n * L.obs + L.deci;
+    if (c < 8) atomicAdd(&d_semb[id_clamp(di[0], 29) * 8 + c], v);
+    else if (c < 40) atomicAdd(&d_cemb[id_clamp(di[1], 65) * 32 + (c - 8)], v);
+    else if (c < 168) atomicAdd(&d_cv[(long)id_clamp(di[2], L.nc) * 128 + (c - 40)], v);
+    else if (c < 296) atomicAdd(&d_cv[(long)id_clamp(di[3], L.nc) * 128 + (c - 168)], v);
+    else if (c < 360) atomicAdd(&d_av[(long)id_clamp(di[4], L.na) * 64 + (c - 296)], v);
+    else if (c < 424) atomicAdd(&d_av[(long)id_clamp(di[5], L.na) * 64 + (c - 360)], v);
+    else if (c < 552) atomicAdd(&d_cv[(long)id_clamp(di[6], L.nc) * 128 + (c - 424)], v);
+    else atomicAdd(&d_cv[(long)id_clamp(di[7], L.nc) * 128 + (c - 552)], v);
+}
+
+// ------------------------------------------------------------ options
+// q_in: [type16 | h(ptr1) | h(ptr2) | opt_card(cv(cid)) | opt_attack(av(aid)) | optf8]
+// ptr p in (0, LTOK] reads h row p, otherwise zeros (ptcg_model.cu:371-419).
+// The two projections are applied per table row beforehand (poc = opt_card
+// over all NC card vectors, poa = opt_attack over all NA attack vectors):
+// gathering a projected row equals projecting the gathered row.
+template <typename T>
+__global__ void k_q_in(T* out, long ldo, const float* obs, ObsLayout L, const float* h,
+                       int D, const float* temb, const float* poc, const float* poa,
+                       int R, int q_in) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * L.nopt * q_in) return;
+    int c = (int)(i % q_in);
+    long nj = i / q_in;
+    int j = (int)(nj % L.nopt), n = (int)(nj / L.nopt);
+    const float* row = obs + (long)n * L.obs;
+    const float* oi = row + L.opti + j * 6;
+    float v;
+    if (c < 16) v = temb[id_clamp(oi[0], 33) * 16 + c];
+    else if (c < 16 + 2 * D) {
+        int which = (c - 16) >= D;
+        int p = (int)oi[1 + which];
+        v = (p <= 0 || p > L.ltok) ? 0.f
+            : h[((long)n * L.lseq + p) * D + (c - 16 - which * D)];
+    } else if (c < 16 + 2 * D + 64) v = poc[(long)id_clamp(oi[3], L.nc) * 64 + (c - 16 - 2 * D)];
+    else if (c < 16 + 2 * D + 128) v = poa[(long)id_clamp(oi[4], L.na) * 64 + (c - 80 - 2 * D)];
+    else v = row[L.optf + j * 8 + (c - 144 - 2 * D)];
+    st(&out[nj * ldo + c], v);
+}
+
+__global__ void k_q_in_bwd(float* d_temb, float* d_h, float* d_poc, float* d_poa,
+                           const float* g, long ldg, const float* obs, ObsLayout L,
+                           int D, int R, int q_in) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * L.nopt * q_in) return;
+    int c = (int)(i % q_in);
+    long nj = i / q_in;
+    int j = (int)(nj % L.nopt), n = (int)(nj / L.nopt);
+    if (c >= 16 + 2 * D + 128) return;
+    float v = g[nj * ldg + c];
+    if (v == 0.f) return;
+    const float* oi = obs + (long)n * L.obs + L.opti + j * 6;
+    if (c < 16) atomicAdd(&d_temb[id_clamp(oi[0], 33) * 16 + c], v);
+    else if (c < 16 + 2 * D) {
+        int which = (c - 16) >= D;
+        int p = (int)oi[1 + which];
+        if (p > 0 && p <= L.ltok)
+            atomicAdd(&d_h[((long)n * L.lseq + p) * D + (c - 16 - which * D)], v);
+    } else if (c < 16 + 2 * D + 64)
+        atomicAdd(&d_poc[(long)id_clamp(oi[3], L.nc) * 64 + (c - 16 - 2 * D)], v);
+    else atomicAdd(&d_poa[(long)id_clamp(oi[4], L.na) * 64 + (c - 80 - 2 * D)], v);
+}
+
+// score input [q | r | g | dvec | q*r], r = h[n, 0] (k_sc_in, ptcg_model.cu:422-439)
+template <typename T>
+__global__ void k_sc_in(T* out, long ldo, const float* q, const float* h, const float* gd,
+                        int D, int lseq, int nopt, int R) {
+    const int W = 3 * D + 192;
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * nopt * W) return;
+    int c = (int)(i % W);
+    long nj = i / W;
+    int n = (int)(nj / nopt);
+    const float* r = h + (long)n * lseq * D;
+    float v;
+    if (c < D) v = q[nj * D + c];
+    else if (c < 2 * D) v = r[c - D];
+    else if (c < 2 * D + 192) v = gd[(long)n * 192 + (c - 2 * D)];
+    else v = q[nj * D + (c - 2 * D - 192)] * r[c - 2 * D - 192];
+    st(&out[nj * ldo + c], v);
+}
+
+// score-input backward, one block per sample (no atomics): d_q in T,
+// d_h[n, 0] += sum_j (ds_r + ds_qr * q), d_gd[n] += sum_j ds_{g,d}
+template <typename T>
+__global__ void k_sc_in_bwd(T* d_q, long lddq, float* d_h, float* d_gd, const float* ds,
+                            long ldds, const float* q, const float* h, int D, int lseq,
+                            int nopt, float* dq_colsum) {
+    int n = blockIdx.x;
+    const float* r = h + (long)n * lseq * D;
+    for (int c = threadIdx.x; c < D + 192; c += blockDim.x) {
+        if (c < D) {
+            float rr = r[c], acc = 0.f, cs = 0.f;
+            for (int j = 0; j < nopt; j++) {
+                long nj = (long)n * nopt + j;
+                const float* dr = ds + nj * ldds;
+                float qv = q[nj * D + c];
+                float dqv = dr[c] + dr[2 * D + 192 + c] * rr;
+                st(&d_q[nj * lddq + c], dqv);
+                cs += dqv;
+                acc += dr[D + c] + dr[2 * D + 192 + c] * qv;
+            }
+            d_h[(long)n * lseq * D + c] += acc;
+            if (dq_colsum) atomicAdd(&dq_colsum[c], cs);
+        } else {
+            int e = c - D;
+            float acc = 0.f;
+            for (int j = 0; j < nopt; j++)
+                acc += ds[((long)n * nopt + j) * ldds + 2 * D + e];
+            d_gd[(long)n * 192 + e] += acc;
+        }
+    }
+}
+
+// ------------------------------------------------------------ N=1 heads
+// out[r * os] = dot(in[inrow(r), :K], w) + b  (score2 / value2 / oracle_v2 /
+// aux_prize), warp per row.  inrow(r) = (r / g) * s + o + r % g when g > 0.
+template <typename TI>
+__global__ void k_rowdot(float* out, long os, const TI* in, long ldi, const float* w,
+                         const float* b, int rows, int K, int g, int gs, int go) {
+    int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    long ir = g > 0 ? (long)(r / g) * gs + go + (r % g) : r;
+    const TI* x = in + ir * ldi;
+    float s = 0.f;
+    for (int k = lane; k < K; k += 32) s += to_f<TI>(x[k]) * w[k];
+    s = warp_sum(s);
+    if (lane == 0) out[r * os] = s + b[0];
+}
+
+// backward of out = dot(gelu(pre), w) + b:  d_pre = d * w * gelu'(pre) (TO),
+// dw += sum_r d * in, db += sum_r d.  d from a strided buffer, or (mode 1,
+// blind-V aux) d = coef * (v - ret) / norm with v from the strided buffer.
+template <typename TI, typename TO>
+__global__ void k_rowdot_bwd(TO* d_pre, long ldd, const TI* pre, long ldp, const TI* in,
+                             long ldi, const float* w, float* dw, float* db, const float* dsrc,
+                             long ds_stride, const float* ret, float coef, int rows, int K,
+                             int rows_per_block, float* loss, float* dpre_colsum) {
+    extern __shared__ float shd[];             // [K] dw partials, [1] db
+    for (int k = threadIdx.x; k <= K; k += blockDim.x) shd[k] = 0.f;
+    __syncthreads();
+    int r0 = blockIdx.x * rows_per_block, r1 = min(rows, r0 + rows_per_block);
+    float dbp = 0.f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        float wk = w[k], acc = 0.f, csum = 0.f;
+        for (int r = r0; r < r1; r++) {
+            float d = dsrc[r * ds_stride];
+            if (ret) {
+                float e = d - ret[r];
+                if (loss && k == 0) atomicAdd(loss, 0.5f * coef * e * e);
+                d = coef * e;
+            }
+            acc += d * to_f<TI>(in[(long)r * ldi + k]);
+            float v = d * wk;
+            if (pre) v *= gelu_grad_f(to_f<TI>(pre[(long)r * ldp + k]));
+            st(&d_pre[(long)r * ldd + k], v);
+            csum += v;
+            if (k == 0) dbp += d;
+        }
+        shd[k] = acc;
+        if (dpre_colsum) atomicAdd(&dpre_colsum[k], csum);
+    }
+    if (threadIdx.x == 0) shd[K] = dbp;
+    __syncthreads();
+    for (int k = threadIdx.x; k < K; k += blockDim.x) atomicAdd(&dw[k], shd[k]);
+    if (threadIdx.x == 0) atomicAdd(db, shd[K]);
+}
+
+// ------------------------------------------------------------ critic
+// oracle tokens [card_vec(id) | is_hand, is_split, is_prize, f3, f4, f5] and
+// critic keep [1, keep(LSEQ), id > 0] (k_otok_in, ptcg_model.cu:442-490)
+template <typename T>
+__global__ void k_otok_in(T* out, long ldo, uint8_t* ckeep, const float* obs, ObsLayout L,
+                          const float* cv, const uint8_t* keep, int R) {
+    const int W = 134, NO = 56;
+    int lcrit = 1 + L.lseq + NO;
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * NO * W) return;
+    int c = (int)(i % W);
+    long nk = i / W;
+    int k = (int)(nk % NO), n = (int)(nk / NO);
+    const float* o = obs + (long)n * L.obs + L.orc;
+    float idf, f3 = 0.f, f4 = 0.f, f5 = 0.f;
+    int kind;
+    if (k < 24) { kind = 0; idf = o[k * 2]; f3 = o[k * 2 + 1]; }
+    else if (k < 48) { kind = 1; int s = k - 24; idf = o[48 + s * 3]; f4 = o[49 + s * 3]; f5 = o[50 + s * 3]; }
+    else { kind = 2; int s = k - 48; idf = o[120 + s * 2]; f3 = o[121 + s * 2]; }
+    float v;
+    if (c < 128) v = cv[(long)id_clamp(idf, L.nc) * 128 + c];
+    else if (c < 131) v = (c - 128) == kind ? 1.f : 0.f;
+    else if (c == 131) v = f3;
+    else if (c == 132) v = f4;
+    else v = f5;
+    st(&out[nk * ldo + c], v);
+    if (c == 0) {
+        uint8_t* ck = ckeep + (long)n * lcrit;
+        if (k == 0) {
+            ck[0] = 1;
+            for (int l = 0; l < L.lseq; l++) ck[1 + l] = keep[(long)n * L.lseq + l];
+        }
+        ck[1 + L.lseq + k] = (int)idf > 0;
+    }
+}
+
+__global__ void k_otok_bwd(float* d_cv, const float* g, long ldg, const float* obs,
+                           ObsLayout L, int R) {
+    const int NO = 56;
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * NO * 128) return;
+    int c = (int)(i % 128);
+    long nk = i / 128;
+    int k = (int)(nk % NO), n = (int)(nk / NO);
+    float v = g[nk * ldg + c];
+    if (v == 0.f) return;
+    const float* o = obs + (long)n * L.obs + L.orc;
+    float idf = k < 24 ? o[k * 2] : k < 48 ? o[48 + (k - 24) * 3] : o[120 + (k - 48) * 2];
+    atomicAdd(&d_cv[(long)id_clamp(idf, L.nc) * 128 + c], v);
+}
+
+// critic sequence rows 0 (critic readout) and 1..LSEQ (trunk output h);
+// rows 1+LSEQ.. are written by the oracle_proj GEMM (row remap)
+__global__ void k_xc_fill(float* xc, const float* h, const float* cread, int lseq,
+                          int lcrit, int D, int R) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    long per = (long)(1 + lseq) * D;
+    if (i >= (long)R * per) return;
+    int n = (int)(i / per);
+    long rem = i % per;
+    int l = (int)(rem / D), d = (int)(rem % D);
+    xc[((long)n * lcrit + l) * D + d] = l == 0 ? cread[d] : h[((long)n * lseq + l - 1) * D + d];
+}
+
+// [seq[n, 0] | g]  (k_val_in, ptcg_model.cu:500-506) in f32 and optional T copy
+template <typename T>
+__global__ void k_val_in(float* out, T* outc, long ldc, const float* seq, int seqlen, int D,
+                         const float* gd, int R) {
+    int W = D + 128;
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * W) return;
+    int n = (int)(i / W), c = (int)(i % W);
+    float v = c < D ? seq[(long)n * seqlen * D + c] : gd[(long)n * 192 + (c - D)];
+    out[i] = v;
+    if (outc) st(&outc[(long)n * ldc + c], v);
+}
+
+// d [seq0 | g] -> d_seq[n, 0] += , d_gd[n, :128] +=
+__global__ void k_val_in_bwd(float* d_seq, int seqlen, int D, float* d_gd, const float* g,
+                             int R, int accum_seq) {
+    int W = D + 128;
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * W) return;
+    int n = (int)(i / W), c = (int)(i % W);
+    float v = g[i];
+    if (c < D) {
+        float* p = &d_seq[(long)n * seqlen * D + c];
+        *p = accum_seq ? *p + v : v;
+    } else d_gd[(long)n * 192 + (c - D)] += v;
+}
+
+// critic input grad split: row 0 -> d_creadout, rows 1..LSEQ -> d_h +=,
+// rows 1+LSEQ.. -> d_otok (T, compact) (k_xc_bwd, ptcg_model2.cu:174-187)
+template <typename T>
+__global__ void k_xc_bwd(float* d_cread, float* d_h, T* d_otok, const float* dxc, int lseq,
+                         int lcrit, int D, int R) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * lcrit * D) return;
+    int d = (int)(i % D);
+    long nl = i / D;
+    int l = (int)(nl % lcrit), n = (int)(nl / lcrit);
+    float g = dxc[i];
+    if (l == 0) { if (g != 0.f) atomicAdd(&d_cread[d], g); }
+    else if (l <= lseq) d_h[((long)n * lseq + l - 1) * D + d] += g;
+    else st(&d_otok[((long)n * 56 + (l - 1 - lseq)) * D + d], g);
+}
+
+// trunk input grad split: row 0 -> d_readout; rows 1.. -> d_tokp (T, compact);
+// d_bc[n] = sum over token rows (one block per sample, no atomics on d_bc)
+template <typename T>
+__global__ void k_x0_bwd(float* d_read, T* d_tokp, float* d_bc, const float* dx0, int ltok,
+                         int D) {
+    int n = blockIdx.x;
+    int lseq = ltok + 1;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        const float* base = dx0 + (long)n * lseq * D + d;
+        atomicAdd(&d_read[d], base[0]);
+        float acc = 0.f;
+        for (int l = 1; l < lseq; l++) {
+            float g = base[(long)l * D];
+            acc += g;
+            st(&d_tokp[((long)n * ltok + l - 1) * D + d], g);
+        }
+        d_bc[(long)n * D + d] = acc;
+    }
+}
+
+__global__ void k_tok_cat_bwd(float* d_cv, float* d_zemb, float* d_oemb, const float* g,
+                              long ldg, const float* obs, ObsLayout L, int R, int tok_in) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * L.ltok * tok_in) return;
+    int c = (int)(i % tok_in);
+    long nl = i / tok_in;
+    int l = (int)(nl % L.ltok), n = (int)(nl / L.ltok);
+    float v = g[nl * ldg + c];
+    if (v == 0.f) return;
+    const float* ti = obs + (long)n * L.obs + L.toki + l * 5;
+    if (c < 128) atomicAdd(&d_cv[(long)id_clamp(ti[0], L.nc) * 128 + c], v);
+    else if (c < 256) {
+        int e = c - 128;
+        int t0 = (int)ti[3], t1 = (int)ti[4];
+        if (t0 > 0) atomicAdd(&d_cv[(long)(t0 >= L.nc ? L.nc - 1 : t0) * 128 + e], v);
+        if (t1 > 0) atomicAdd(&d_cv[(long)(t1 >= L.nc ? L.nc - 1 : t1) * 128 + e], v);
+    } else if (c < 256 + L.tok_f) {
+    } else if (c < 264 + L.tok_f) atomicAdd(&d_zemb[id_clamp(ti[1], 16) * 8 + (c - 256 - L.tok_f)], v);
+    else atomicAdd(&d_oemb[id_clamp(ti[2], 4) * 4 + (c - 264 - L.tok_f)], v);
+}
+
+// ------------------------------------------------------------ aux losses
+// opp-hand count MSE on softplus (ptcg_model2.cu:219-249): one block per row;
+// targets built in shared memory (ids 0 < id < NC, id != UNK, count != 0).
+template <typename TO>
+__global__ void k_hand_grad(TO* d_lin, long ldd, float* lin, long ldl,
+                            const float* obs, ObsLayout L, float scale, float* loss) {
+    extern __shared__ float tg[];
+    int n = blockIdx.x;
+    for (int c = threadIdx.x; c < L.nc; c += blockDim.x) tg[c] = 0.f;
+    __syncthreads();
+    const float* o = obs + (long)n * L.obs + L.orc;
+    if (threadIdx.x < 24) {
+        int k = threadIdx.x;
+        int id = (int)o[k * 2];
+        float cnt = o[k * 2 + 1] * 4.0f;
+        if (id > 0 && id < L.nc && id != L.nc - 1 && cnt != 0.f) atomicAdd(&tg[id], cnt);
+    }
+    __syncthreads();
+    float lsum = 0.f;
+    for (int c = threadIdx.x; c < L.nc; c += blockDim.x) {
+        float x = lin[(long)n * ldl + c];
+        float pred = softplus_f(x);
+        float e = pred - tg[c];
+        lsum += e * e;
+        float g = scale * 2.f * e;
+        g = x > 20.f ? g : g * sigmoid_f(x);
+        st(&d_lin[(long)n * ldd + c], g);
+        lin[(long)n * ldl + c] = g;             // fp32 copy (bias grad), logits no longer needed
+    }
+    lsum = warp_sum(lsum);
+    if ((threadIdx.x & 31) == 0) atomicAdd(loss, lsum * scale);
+}
+
+// number of MY_UNSEEN tokens (prize-loss normaliser, ptcg_model2.cu:251-267)
+__global__ void k_count_unseen(float* cnt, const float* obs, ObsLayout L, int R) {
+    float s = 0.f;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < (long)R * L.ltok;
+         i += (long)gridDim.x * blockDim.x) {
+        long n = i / L.ltok;
+        int l = (int)(i % L.ltok);
+        if ((int)obs[n * L.obs + L.toki + l * 5 + 1] == 9) s += 1.f;
+    }
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) atomicAdd(cnt, s);
+}
+
+// prize BCE grad over MY_UNSEEN tokens + aux_prize head backward
+// (k_prize_grad / k_prize_head_bwd, ptcg_model2.cu:269-281, ptcg_model3.cu:425-438).
+// One warp per token; target = my-prize indicator of the token's card.
+__global__ void k_prize_bwd(float* d_h, float* dw, float* db, const float* logit,
+                            const float* h, const float* w, const float* obs, ObsLayout L,
+                            const float* cnt_dev, float cnt_host, int D, int R, float* loss) {
+    int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (t >= R * L.ltok) return;
+    int n = t / L.ltok, l = t % L.ltok;
+    const float* row = obs + (long)n * L.obs;
+    if ((int)row[L.toki + l * 5 + 1] != 9) return;
+    int cid = id_clamp(row[L.toki + l * 5], L.nc);
+    float tgt = 0.f;
+    const float* o = row + L.orc;
+    for (int k = 0; k < 8; k++) {
+        int id = (int)o[120 + 2 * k];
+        if (id > 0 && id < L.nc && o[121 + 2 * k] > 0.f && id == cid) tgt = 1.f;
+    }
+    float c = cnt_host > 0.f ? cnt_host : (cnt_dev[0] > 0.f ? cnt_dev[0] : 1.f);
+    float x = logit[t];
+    float g = 0.1f * (sigmoid_f(x) - tgt) / c;
+    if (lane == 0) {
+        float bce = fmaxf(x, 0.f) - x * tgt + log1pf(expf(-fabsf(x)));
+        atomicAdd(loss, 0.1f * bce / c);
+        atomicAdd(db, g);
+    }
+    long hr = ((long)n * L.lseq + 1 + l) * D;
+    for (int d = lane; d < D; d += 32) {
+        atomicAdd(&d_h[hr + d], g * w[d]);
+        atomicAdd(&dw[d], g * h[hr + d]);
+    }
+}
+
+// ---------------------------------------------------------- misc helpers
+template <typename TI>
+__global__ void k_colsum(float* out, const TI* in, long ld, int rows, int cols,
+                         int rows_per_block) {
+    int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= cols) return;
+    int r0 = blockIdx.y * rows_per_block, r1 = min(rows, r0 + rows_per_block);
+    float s = 0.f;
+    for (int r = r0; r < r1; r++) s += to_f<TI>(in[(long)r * ld + c]);
+    atomicAdd(&out[c], s);
+}
+
+// out[c] += sum over groups g, rows r < rows_per_group of
+//           src[(g * group_stride + row_off + r) * ld + c]
+__global__ void k_colsum_groups(float* out, const float* src, long ld, int ngroups,
+                                int group_stride, int row_off, int rows_per_group, int cols,
+                                int groups_per_block) {
+    int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= cols) return;
+    int g0 = blockIdx.y * groups_per_block, g1 = min(ngroups, g0 + groups_per_block);
+    float s = 0.f;
+    for (int g = g0; g < g1; g++) {
+        const float* b = src + ((long)g * group_stride + row_off) * ld + c;
+        for (int r = 0; r < rows_per_group; r++) s += b[(long)r * ld];
+    }
+    atomicAdd(&out[c], s);
+}
+
+// dst[r, c] += src[r * lds + off + c]
+__global__ void k_slice_add(float* dst, const float* src, int rows, int width, long lds,
+                            int off) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)rows * width) return;
+    int r = (int)(i / width), c = (int)(i % width);
+    dst[i] += src[(long)r * lds + off + c];
+}
+
+__global__ void k_scale_copy(float* dst, long ldd, const float* src, long lds, int rows,
+                             int cols, float scale) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)rows * cols) return;
+    int r = (int)(i / cols), c = (int)(i % cols);
+    dst[(long)r * ldd + c] = src[(long)r * lds + c] * scale;
+}
+
+template <typename T>
+__global__ void k_cast(T* dst, long ldd, const float* src, long lds, int rows, int cols) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)rows * cols) return;
+    int r = (int)(i / cols), c = (int)(i % cols);
+    st(&dst[(long)r * ldd + c], src[(long)r * lds + c]);
+}
+
+// ------------------------------------------------------------ PPO loss
+// advantage mean / unbiased variance over the minibatch (ppo_var_mean,
+// pufferlib.cu:1307-1363), one block, fp64 accumulation.
+__global__ void k_adv_stats(float* out, const float* adv, int n) {
+    __shared__ double sh[32];
+    double s = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s += adv[i];
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0; for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += sh[i];
+        sh[31] = t / n;
+    }
+    __syncthreads();
+    double mean = sh[31];
+    __syncthreads();
+    double v = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) { double d = adv[i] - mean; v += d * d; }
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0; for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += sh[i];
+        out[0] = (float)mean;
+        out[1] = (float)(t / (n > 1 ? n - 1 : 1));
+    }
+}
+
+// Fused clipped PPO + clipped value loss + entropy, forward and backward,
+// one warp per row (ppo_loss_compute, pufferlib.cu:1010-1248).  Masked
+// logits are -1e4.  Writes the gradient w.r.t. the fused decoder output
+// [scores | value] and 7 per-block partial stats.
+constexpr int PPO_ROWS_PER_BLOCK = 8;
+__global__ void k_ppo_loss(const float* dec, int nopt, const float* mask, long mstride,
+                           const float* actions, const float* old_logp, const float* adv,
+                           const float* values, const float* returns, const float* prio,
+                           int horizon, int row0, int nt, int nt_norm, const float* adv_stats,
+                           float clip, float vclip, float vf_coef, float ent_coef,
+                           float* grad, float* new_logp, float* ratio_out, float* partials) {
+    __shared__ float sp[PPO_ROWS_PER_BLOCK][8];
+    int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int r = blockIdx.x * PPO_ROWS_PER_BLOCK + wid;
+    float st7[7] = {0, 0, 0, 0, 0, 0, 0};
+    if (r < nt) {
+        const int W = nopt + 1;
+        const float inv = 1.f / (float)nt_norm;
+        const float* lg = dec + (long)r * W;
+        const float* mk = mask + (long)r * mstride;
+        int act = (int)actions[r];
+        float mx = -INFINITY;
+        for (int a = lane; a < nopt; a += 32) {
+            float l = mk[a] == 0.f ? -1e4f : lg[a];
+            mx = fmaxf(mx, l);
+        }
+        mx = warp_max(mx);
+        float se = 0.f;
+        for (int a = lane; a < nopt; a += 32) {
+            float l = mk[a] == 0.f ? -1e4f : lg[a];
+            se += expf(l - mx);
+        }
+        se = warp_sum(se);
+        float lse = mx + logf(se);
+        float ent = 0.f;
+        for (int a = lane; a < nopt; a += 32) {
+            float l = mk[a] == 0.f ? -1e4f : lg[a];
+            float lp = l - lse;
+            ent -= expf(lp) * lp;
+        }
+        ent = warp_sum(ent);
+        float act_l = (act >= 0 && act < nopt) ? (mk[act] == 0.f ? -1e4f : lg[act]) : -1e4f;
+        float logp = act_l - lse;
+        float mean = adv_stats[0], var = adv_stats[1];
+        float advn = (adv[r] - mean) / (sqrtf(var) + 1e-8f);
+        float w = prio[(row0 + r) / horizon];
+        float val = values[r], ret = returns[r], vp = lg[nopt];
+        float verr = vp - val;
+        float vcl = val + fmaxf(-vclip, fminf(vclip, verr));
+        float lu = (vp - ret) * (vp - ret), lc = (vcl - ret) * (vcl - ret);
+        float vloss = 0.5f * fmaxf(lu, lc);
+        float dv;
+        if (lc > lu) dv = (verr >= -vclip && verr <= vclip) ? vcl - ret : 0.f;
+        else dv = vp - ret;
+        float logratio = logp - old_logp[r];
+        float ratio = expf(logratio);
+        float rc = fmaxf(1.f - clip, fminf(1.f + clip, ratio));
+        float wa = -w * advn;
+        float pg1 = wa * ratio, pg2 = wa * rc;
+        float pg = fmaxf(pg1, pg2);
+        float dr = wa * inv;
+        if (pg2 > pg1 && (ratio <= 1.f - clip || ratio >= 1.f + clip)) dr = 0.f;
+        float dnlp = dr * ratio;
+        float dent = inv * (-ent_coef);
+        float* gr = grad + (long)r * W;
+        for (int a = lane; a < nopt; a += 32) {
+            float g = 0.f;
+            if (mk[a] != 0.f) {
+                float lp = lg[a] - lse;
+                float p = expf(lp);
+                g = (a == act ? dnlp : 0.f) - p * dnlp + dent * p * (-ent - lp);
+            }
+            gr[a] = g;
+        }
+        if (lane == 0) {
+            gr[nopt] = inv * vf_coef * dv;
+            new_logp[r] = logp;
+            ratio_out[r] = ratio;
+        }
+        st7[0] = (pg + vf_coef * vloss - ent_coef * ent) * inv;
+        st7[1] = pg * inv;
+        st7[2] = vloss * inv;
+        st7[3] = ent * inv;
+        st7[4] = -logratio * inv;
+        st7[5] = ((ratio - 1.f) - logratio) * inv;
+        st7[6] = (fabsf(ratio - 1.f) > clip ? 1.f : 0.f) * inv;
+    }
+    if (lane == 0) for (int k = 0; k < 7; k++) sp[wid][k] = st7[k];
+    __syncthreads();
+    if (threadIdx.x < 7) {
+        float s = 0.f;
+        for (int w2 = 0; w2 < PPO_ROWS_PER_BLOCK; w2++) s += sp[w2][threadIdx.x];
+        partials[(long)blockIdx.x * 7 + threadIdx.x] = s;
+    }
+}
+
+// deterministic reduction of the block partials (ppo_loss_reduce,
+// pufferlib.cu:1254-1284); stats[7] = advantage variance
+__global__ void k_ppo_reduce(float* stats, const float* partials, int nblocks,
+                             const float* adv_stats, int accumulate) {
+    int c = threadIdx.x;
+    if (c < 7) {
+        double s = 0.0;
+        for (int b = 0; b < nblocks; b++) s += partials[(long)b * 7 + c];
+        stats[c] = accumulate ? stats[c] + (float)s : (float)s;
+    }
+    if (c == 7) stats[7] = adv_stats[1];
+}
+
+// ------------------------------------------------------------ sampler
+// masked online log-sum-exp, inverse-CDF draw, fallback to the last legal
+// slot, logprob, value copy (sample_logits, pufferlib.cu:584-718); one warp per row.
+__global__ void k_sample(const float* dec, int n, int nopt, const float* mask, long mstride,
+                         const float* uni, float* actions, float* logprobs, float* values) {
+    int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (r >= n) return;
+    const float* lg = dec + (long)r * (nopt + 1);
+    const float* mk = mask + (long)r * mstride;
+    float mx = -INFINITY;
+    for (int a = lane; a < nopt; a += 32) mx = fmaxf(mx, mk[a] == 0.f ? -1e4f : lg[a]);
+    mx = warp_max(mx);
+    float se = 0.f;
+    for (int a = lane; a < nopt; a += 32) se += expf((mk[a] == 0.f ? -1e4f : lg[a]) - mx);
+    se = warp_sum(se);
+    float lse = mx + logf(se);
+    if (lane == 0) {
+        float u = uni[r], cum = 0.f;
+        int pick = -1;
+        for (int a = 0; a < nopt; a++) {
+            float l = mk[a] == 0.f ? -1e4f : lg[a];
+            cum += expf(l - lse);
+            if (u < cum) { pick = a; break; }
+        }
+        if (pick < 0) {
+            pick = nopt - 1;
+            for (int a = nopt - 1; a >= 0; a--) if (mk[a] != 0.f) { pick = a; break; }
+        }
+        float l = mk[pick] == 0.f ? -1e4f : lg[pick];
+        actions[r] = (float)pick;
+        logprobs[r] = l - lse;
+        values[r] = lg[nopt];
+    }
+}
+
+// seat-flipping GAE / V-trace (k_negamax_adv, ptcg_model2.cu:288-311)
+__global__ void k_negamax_adv(const float* values, const float* rewards, const float* dones,
+                              const float* imp, const float* obs, long obs_size, int seat_col,
+                              float* adv, float gamma, float lambda, float rho_clip,
+                              float c_clip, int B, int T) {
+    int row = blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= B) return;
+    long o = (long)row * T;
+    const float* ob = obs + (long)row * T * obs_size;
+    float last = 0.f;
+    for (int t = T - 2; t >= 0; t--) {
+        float st_ = ob[(long)t * obs_size + seat_col];
+        float sn = ob[(long)(t + 1) * obs_size + seat_col];
+        float sign = st_ == sn ? 1.f : -1.f;
+        float s = sign * (1.f - dones[o + t + 1]);
+        float im = imp[o + t];
+        float rho = im < rho_clip ? im : rho_clip;
+        float cc = im < c_clip ? im : c_clip;
+        float delta = rho * (rewards[o + t + 1] + gamma * values[o + t + 1] * s - values[o + t]);
+        last = delta + gamma * lambda * cc * s * last;
+        adv[o + t] = last;
+    }
+}
+
+// ------------------------------------------------------------ Adam
+// pass 1: per-block partial sum of squared grads (fp64 accumulation)
+__global__ void k_sumsq(double* partials, const float* g, long n) {
+    __shared__ double sh[32];
+    double s = 0.0;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
+         i += (long)gridDim.x * blockDim.x) {
+        double v = g[i];
+        s += v * v;
+    }
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0; for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += sh[i];
+        partials[blockIdx.x] = t;
+    }
+}
+
+// A weight matrix whose bf16 compute copy the Adam pass refreshes.
+struct BfCopy { long off, n; int cols, ldp; bf16* dst; };
+
+// pass 2: every block re-reduces the partials (deterministic), then
+// clip coef = min(1, max_norm / (norm + 1e-6)) (clip_grad_norm_), torch Adam:
+//   m = b1 m + (1-b1) g; v = b2 v + (1-b2) g^2;
+//   p -= (lr / (1-b1^t)) * m / (sqrt(v) / sqrt(1-b2^t) + eps)
+// skipped (no state change) when the gate is 0 or the norm is not finite.
+__global__ void k_adam(float* p, float* m, float* v, const float* g, long n,
+                       const double* partials, int nparts, float lr, float b1, float b2,
+                       float eps, float max_norm, const long long* step_dev,
+                       const float* gate, float* stats, const BfCopy* copies, int ncopies,
+                       const int* chunk_copy, int chunk) {
+    __shared__ float s_coef, s_bc1, s_bc2sqrt;
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        double t_step = (double)(step_dev[0] + 1);
+        s_bc1 = (float)(1.0 - pow((double)b1, t_step));
+        s_bc2sqrt = (float)sqrt(1.0 - pow((double)b2, t_step));
+        double t = 0.0;
+        for (int i = 0; i < nparts; i++) t += partials[i];
+        float norm = (float)sqrt(t);
+        int ok = isfinite(norm) && (gate == nullptr || gate[0] != 0.f);
+        float coef = max_norm / (norm + 1e-6f);
+        s_coef = coef < 1.f ? coef : 1.f;
+        s_ok = ok;
+        if (blockIdx.x == 0 && stats) { stats[0] = norm; stats[1] = ok ? 1.f : 0.f; }
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    float coef = s_coef;
+    float step_size = lr / s_bc1;
+    float bc2sqrt = s_bc2sqrt;
+    for (long c0 = (long)blockIdx.x * chunk; c0 < n; c0 += (long)gridDim.x * chunk) {
+        // first bf16 copy that ends after the chunk start (copies sorted by off)
+        int ci = chunk_copy ? chunk_copy[c0 / chunk] : ncopies;
+        long c1 = min(n, c0 + chunk);
+        for (long i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
+            float gi = g[i] * coef;
+            float mi = b1 * m[i] + (1.f - b1) * gi;
+            float vi = b2 * v[i] + (1.f - b2) * gi * gi;
+            m[i] = mi; v[i] = vi;
+            float pi = p[i] - step_size * mi / (sqrtf(vi) / bc2sqrt + eps);
+            p[i] = pi;
+            while (ci < ncopies && i >= copies[ci].off + copies[ci].n) ci++;
+            if (ci < ncopies && i >= copies[ci].off) {
+                const BfCopy& cp = copies[ci];
+                long j = i - cp.off;
+                cp.dst[(j / cp.cols) * cp.ldp + (j % cp.cols)] = __float2bfloat16_rn(pi);
+            }
+        }
+    }
+}
+
+// advance the Adam step counter when the step was applied (after k_adam)
+__global__ void k_step_inc(long long* step_dev, const float* stats) {
+    if (stats[1] != 0.f) step_dev[0] += 1;
+}
+
+__global__ void k_gelu_bwd(float* d, const float* pre, long n) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i < n) d[i] *= gelu_grad_f(pre[i]);
+}
+
+// refresh bf16 copies from the master weights (after a load)
+__global__ void k_refresh_copies(const float* p, const BfCopy* copies, int ncopies) {
+    const BfCopy& cp = copies[blockIdx.y];
+    for (long j = blockIdx.x * (long)blockDim.x + threadIdx.x; j < cp.n;
+         j += (long)gridDim.x * blockDim.x)
+        cp.dst[(j / cp.cols) * cp.ldp + (j % cp.cols)] = __float2bfloat16_rn(p[cp.off + j]);
+}
+
+// 64-bit weight checksum: wrapping sums of the raw fp32 bit patterns, one
+// weighted by position, so a swap of two values changes it
+__global__ void k_checksum(unsigned int* out, const float* p, long n) {
+    unsigned long long s1 = 0, s2 = 0;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
+         i += (long)gridDim.x * blockDim.x) {
+        unsigned int b = __float_as_uint(p[i]);
+        s1 += b;
+        s2 += (unsigned long long)b * (unsigned long long)(i + 1);
+    }
+    atomicAdd((unsigned long long*)out, s1 ^ (s2 << 1));
+}

@@ -1,0 +1,1413 @@
+// ptcg_b200: model state, workspaces, forward / backward orchestration and
+// the extern "C" entry points declared in include/ptcg_b200.h.
+//
+// Dataflow follows ptcg_forward_core / ptcg_backward_core of the reference
+// (native/model/ptcg_model3.cu:246-369, ptcg_model4.cu:10-190) and the torch
+// model (ptcg/rl/model.py:185-341); the kernels and layouts are this
+// library's own:
+//  * activations are row-major with leading dimensions padded to 8 elements
+//    (16-byte rows for TMA); GEMM operands are bf16 in PTCG_BF16 mode and fp32
+//    in PTCG_FP32 mode, the residual stream, LayerNorm statistics, heads and
+//    all gradients of the residual stream stay fp32;
+//  * attention never materialises probabilities (online softmax, LSE saved);
+//  * concat-then-Linear of gathered table rows becomes Linear-per-table-row
+//    then gather where the table is small (opt_card / opt_attack);
+//  * the static card / attack / skill tables are built once per train step
+//    and their gradient is accumulated across micro-batches.
+#include "kernels.cuh"
+#include "ptcg_b200.h"
+
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+#include <vector>
+#include <unordered_map>
+
+// ------------------------------------------------------------------ errors
+static thread_local char g_err[1024];
+static void set_err(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+}
+#define CK(x) do { cudaError_t _e = (x); if (_e != cudaSuccess) { \
+    set_err("%s failed: %s (%s:%d)", #x, cudaGetErrorString(_e), __FILE__, __LINE__); \
+    return PTCG_ECUDA; } } while (0)
+#define CKL() CK(cudaGetLastError())
+#define REQ(cond, code, ...) do { if (!(cond)) { set_err(__VA_ARGS__); return code; } } while (0)
+
+static const int TPB = 256;
+static inline long rup(long x, long a) { return (x + a - 1) / a * a; }
+
+// ------------------------------------------------------------- param table
+struct ParamDef { std::string name; long r, c; };
+
+static void blk_defs(std::vector<ParamDef>& v, const std::string& p, int d, int f) {
+    v.push_back({p + "ln1_w", d, 0}); v.push_back({p + "ln1_b", d, 0});
+    v.push_back({p + "qkv_w", 3L * d, d}); v.push_back({p + "qkv_b", 3L * d, 0});
+    v.push_back({p + "proj_w", d, d}); v.push_back({p + "proj_b", d, 0});
+    v.push_back({p + "ln2_w", d, 0}); v.push_back({p + "ln2_b", d, 0});
+    v.push_back({p + "ffn1_w", f, d}); v.push_back({p + "ffn1_b", f, 0});
+    v.push_back({p + "ffn2_w", d, f}); v.push_back({p + "ffn2_b", d, 0});
+}
+
+// PT_PARAMS order (native/model/ptcg_model.cu:95-126)
+static std::vector<ParamDef> param_defs(const PtcgShape& s) {
+    const int d = s.d, dc = 128, da = 64, g = 128;
+    const int tok_in = 2 * dc + s.tok_f + 12, q_in = 16 + 2 * d + 136;
+    const int score_in = 3 * d + 192, val_in = d + 128;
+    std::vector<ParamDef> v = {
+        {"card_id_emb", s.n_cards, 64}, {"attack_id_emb", s.n_attacks, 48},
+        {"skill_id_emb", s.n_skills, 48},
+        {"attack_mlp_w", da, 127}, {"attack_mlp_b", da, 0},
+        {"skill_mlp_w", dc, 112}, {"skill_mlp_b", dc, 0},
+        {"card_ln_w", 634, 0}, {"card_ln_b", 634, 0},
+        {"card_mlp1_w", 256, 634}, {"card_mlp1_b", 256, 0},
+        {"card_mlp2_w", dc, 256}, {"card_mlp2_b", dc, 0},
+        {"zone_emb", 16, 8}, {"owner_emb", 4, 4},
+        {"token_proj_w", d, tok_in}, {"token_proj_b", d, 0},
+        {"readout", d, 0},
+        {"global1_w", g, 64}, {"global1_b", g, 0}, {"global2_w", g, g}, {"global2_b", g, 0},
+        {"sel_type_emb", 29, 8}, {"ctx_emb", 65, 32},
+        {"dec1_w", 64, 696}, {"dec1_b", 64, 0}, {"dec2_w", 64, 64}, {"dec2_b", 64, 0},
+        {"bcast_w", d, 192}, {"bcast_b", d, 0},
+    };
+    for (int i = 0; i < s.layers; i++) blk_defs(v, "b" + std::to_string(i) + "_", d, s.ffn);
+    std::vector<ParamDef> t2 = {
+        {"lnf_w", d, 0}, {"lnf_b", d, 0},
+        {"opt_type_emb", 33, 16},
+        {"opt_card_w", 64, dc}, {"opt_card_b", 64, 0},
+        {"opt_attack_w", 64, da}, {"opt_attack_b", 64, 0},
+        {"q1_w", d, q_in}, {"q1_b", d, 0}, {"q2_w", d, d}, {"q2_b", d, 0},
+        {"score1_w", 256, score_in}, {"score1_b", 256, 0},
+        {"score2_w", 1, 256}, {"score2_b", 1, 0},
+        {"value1_w", 256, val_in}, {"value1_b", 256, 0},
+        {"value2_w", 1, 256}, {"value2_b", 1, 0},
+        {"oracle_proj_w", d, 134}, {"oracle_proj_b", d, 0},
+        {"critic_readout", d, 0},
+    };
+    v.insert(v.end(), t2.begin(), t2.end());
+    blk_defs(v, "c0_", d, s.ffn);
+    std::vector<ParamDef> t3 = {
+        {"oracle_v1_w", 256, val_in}, {"oracle_v1_b", 256, 0},
+        {"oracle_v2_w", 1, 256}, {"oracle_v2_b", 1, 0},
+        {"aux_hand_w", s.n_cards, val_in}, {"aux_hand_b", s.n_cards, 0},
+        {"aux_prize_w", 1, d}, {"aux_prize_b", 1, 0},
+    };
+    v.insert(v.end(), t3.begin(), t3.end());
+    return v;
+}
+
+static long numel(const ParamDef& p) { return p.c > 0 ? p.r * p.c : p.r; }
+
+// ------------------------------------------------------------ model state
+struct Dims {
+    int D, H, FFN, LAYERS, LTOK, LSEQ, NOPT, LCRIT, NC, NA, NS, TOKF;
+    int TOK_IN, Q_IN, SCORE_IN, VAL_IN;
+    ObsLayout ol;
+};
+
+struct W { float* p; float* g; const void* op; long ld; };   // param + GEMM operand
+
+struct BlkW { W ln1w, ln1b, qkvw, qkvb, projw, projb, ln2w, ln2b, f1w, f1b, f2w, f2b; };
+
+struct BlkAct {
+    float *x_in, *x_out;
+    void *ln1, *qkv, *att, *ln2, *fpre, *fpost;
+    float *mu1, *rs1, *mu2, *rs2, *lse, *xm;
+};
+
+struct Work {
+    int R = 0, train = 0;
+    void* base = nullptr; size_t bytes = 0;
+    // per-sample / token buffers
+    void* tokcat; uint8_t* keep; uint8_t* ckeep;
+    float *g1pre, *g1, *gd, *decin, *d1pre, *d1, *bc;
+    std::vector<float*> x;              // trunk states (LAYERS+1 train, 2 rollout)
+    std::vector<BlkAct> blk;            // per layer (train) / 1 shared (rollout)
+    float* h; float *muf, *rsf;
+    void *qin, *q1pre, *q1; float* q; void *scin, *s1pre, *s1;
+    void* otokin; float* xc[2]; BlkAct cblk;
+    float *ovin, *ov1pre, *ov1; float* out;
+    // train-only heads
+    float *bvin; void* bvinc; float *bv1pre, *bv1, *blind_v, *hand_lin, *prize_logit;
+    // backward scratch
+    float *dh, *dgd, *dbvin, *d_v1pre, *dscores, *dscin, *dqin, *dtokcat, *ddecin, *dd1,
+          *dg1, *dbc, *dotokin, *dx, *dln;
+    void *dxc, *dhand, *ds1pre, *dq, *dq1, *dotok, *dtokp, *df, *datt, *dqkv;
+    float* dgrad;                       // PPO grad for one micro-batch (train_step)
+    float* fused;                       // fused [scores | value] of one micro-batch
+    float *ppo_scratch, *nlp, *ratio;
+};
+
+struct Tab {                            // batch-independent table activations + grads
+    float *att_in, *att_pre, *att_tab, *sk_in, *sk_pre, *sk_tab;
+    float *a_mean_max_dummy;
+    float *card_in, *card_ln, *ln_mu, *ln_rs, *h1pre, *h1, *card_vec, *poc, *poa;
+    int8_t *a_arg, *s_arg;
+    float *d_cv, *d_att, *d_sk, *d_poc, *d_poa, *d_h1, *d_cardln, *d_cardin, *d_attin, *d_skin;
+};
+
+struct PtcgModel {
+    PtcgShape s;
+    Dims z;
+    int prec, dev;
+    std::vector<ParamDef> defs;
+    std::vector<long> off;
+    std::unordered_map<std::string, int> idx;
+    long n_arena = 0;
+    float *params = nullptr, *grads = nullptr, *am = nullptr, *av = nullptr;
+    long long* step_dev = nullptr;
+    // bf16 compute copies
+    std::vector<BfCopy> copies;
+    std::vector<long> copy_ld;          // per param: ld of its copy (0 = none)
+    std::vector<bf16*> copy_ptr;
+    bf16* wbf = nullptr;
+    BfCopy* d_copies = nullptr;
+    int* d_chunk_copy = nullptr;
+    int adam_chunk = 4096, adam_grid = 0, sumsq_grid = 0;
+    double* d_partials = nullptr;
+    float* d_misc = nullptr;            // [0..1] adv stats, [2] prize count, [4..19] stats, [32..] adam stats
+    unsigned int* d_ck = nullptr;
+    // static tables
+    float *card_static = nullptr, *att_static = nullptr, *card_text = nullptr,
+          *att_text = nullptr, *skill_text = nullptr;
+    int *card_attacks = nullptr, *card_skills = nullptr;
+    bool tables_ready = false, weights_ready = false;
+    Tab tab;
+    void* tab_base = nullptr;
+    Work roll, trn;
+    ptcg_grad_hook hook = nullptr;
+    void* hook_user = nullptr;
+    const float* trn_last_obs = nullptr;
+    int trn_last_n = 0;
+    int esz() const { return prec == PTCG_BF16 ? 2 : 4; }
+    int dt() const { return prec == PTCG_BF16 ? DT_BF16 : DT_F32; }
+    W w(const char* name) const {
+        auto it = idx.find(name);
+        int i = it->second;
+        W r;
+        r.p = params + off[i];
+        r.g = grads + off[i];
+        if (prec == PTCG_BF16 && copy_ptr[i]) { r.op = copy_ptr[i]; r.ld = copy_ld[i]; }
+        else { r.op = r.p; r.ld = defs[i].c; }
+        return r;
+    }
+    BlkW blk(const std::string& p) const {
+        BlkW b;
+        b.ln1w = w((p + "ln1_w").c_str()); b.ln1b = w((p + "ln1_b").c_str());
+        b.qkvw = w((p + "qkv_w").c_str()); b.qkvb = w((p + "qkv_b").c_str());
+        b.projw = w((p + "proj_w").c_str()); b.projb = w((p + "proj_b").c_str());
+        b.ln2w = w((p + "ln2_w").c_str()); b.ln2b = w((p + "ln2_b").c_str());
+        b.f1w = w((p + "ffn1_w").c_str()); b.f1b = w((p + "ffn1_b").c_str());
+        b.f2w = w((p + "ffn2_w").c_str()); b.f2b = w((p + "ffn2_b").c_str());
+        return b;
+    }
+};
+
+// ---------------------------------------------------------------- helpers
+static void gemm(const PtcgModel* M, const GemmArgs& a, cudaStream_t s) {
+    if (a.dtype == DT_BF16 && gemm_tc_available() && gemm_tc(a, s)) return;
+    gemm_simt(a, s);
+}
+
+// C[M,N] (+)= op(A) op(B)^T helpers for the three GEMM shapes of a Linear
+// y = x W^T + b with W [out, in]:
+//   fwd : y[M=rows, N=out]   = x[rows, in] . W[out, in]^T
+//   dX  : dx[M=rows, N=in]   = dy[rows, out] . W[out, in]
+//   dW  : dW[M=out, N=in]   += dy[rows, out]^T . x[rows, in]
+static GemmArgs lin_fwd(int dt, int rows, int in, int out, const void* x, long ldx, const W& w,
+                        void* y, long ldy, int y_dt) {
+    GemmArgs a;
+    a.M = rows; a.N = out; a.K = in; a.dtype = dt;
+    a.A = x; a.lda = ldx; a.a_kmajor = 1;
+    a.B = w.op; a.ldb = w.ld; a.b_kmajor = 1;
+    a.bias = w.p == nullptr ? nullptr : nullptr;
+    a.out = y; a.ldo = ldy; a.out_dtype = y_dt;
+    return a;
+}
+static GemmArgs lin_dx(int dt, int rows, int in, int out, const void* dy, long lddy, const W& w,
+                       void* dx, long lddx, int dx_dt) {
+    GemmArgs a;
+    a.M = rows; a.N = in; a.K = out; a.dtype = dt;
+    a.A = dy; a.lda = lddy; a.a_kmajor = 1;
+    a.B = w.op; a.ldb = w.ld; a.b_kmajor = 0;
+    a.out = dx; a.ldo = lddx; a.out_dtype = dx_dt;
+    return a;
+}
+static GemmArgs lin_dw(int dt, int rows, int in, int out, const void* dy, long lddy,
+                       const void* x, long ldx, float* dw) {
+    GemmArgs a;
+    a.M = out; a.N = in; a.K = rows; a.dtype = dt;
+    a.A = dy; a.lda = lddy; a.a_kmajor = 0;
+    a.B = x; a.ldb = ldx; a.b_kmajor = 0;
+    a.out = dw; a.ldo = in; a.out_dtype = DT_F32; a.accumulate = 1;
+    return a;
+}
+// fp32 operand view of a parameter (per-sample / table GEMMs stay fp32)
+static W f32w(const W& w, long cols) { W r = w; r.op = w.p; r.ld = cols; return r; }
+
+template <typename T> static void colsum(float* out, const T* in, long ld, int rows, int cols,
+                                         cudaStream_t s) {
+    if (rows <= 0) return;
+    int rpb = 256;
+    dim3 g(cdiv(cols, 128), cdiv(rows, rpb));
+    k_colsum<T><<<g, 128, 0, s>>>(out, in, ld, rows, cols, rpb);
+}
+
+static void ln_fwd(int dt, void* y, long ldy, float* mu, float* rs, const float* x, long ldx,
+                   const float* w, const float* b, int rows, int D, cudaStream_t s) {
+    unsigned g = cdiv(rows, 8);
+    if (dt == DT_F32) k_ln_fwd<float><<<g, 256, 0, s>>>((float*)y, ldy, mu, rs, x, ldx, w, b, rows, D);
+    else k_ln_fwd<bf16><<<g, 256, 0, s>>>((bf16*)y, ldy, mu, rs, x, ldx, w, b, rows, D);
+}
+// dx (f32, ld D) = LN'(dy) (+ dx), copy to dxc (T) unless dxc == nullptr
+static void ln_bwd(int dt, float* dx, int accumulate, void* dxc, float* dw, float* db,
+                   const float* dy, const float* x, const float* w, const float* mu,
+                   const float* rs, int rows, int D, cudaStream_t s) {
+    int rpb = 64;
+    unsigned g = cdiv(rows, rpb);
+    size_t sm = 2 * D * sizeof(float);
+    if (dt == DT_F32 || dxc == nullptr)
+        k_ln_bwd<float><<<g, 256, sm, s>>>(dx, D, accumulate, (float*)dxc, D, dw, db, dy, D, x, D,
+                                          w, mu, rs, rows, D, rpb);
+    else
+        k_ln_bwd<bf16><<<g, 256, sm, s>>>(dx, D, accumulate, (bf16*)dxc, D, dw, db, dy, D, x, D,
+                                         w, mu, rs, rows, D, rpb);
+}
+
+// ---------------------------------------------------------- workspace plan
+struct Bump {
+    char* base; size_t off; bool measure;
+    void* take(size_t bytes) {
+        off = (off + 255) & ~(size_t)255;
+        void* p = measure ? nullptr : (void*)(base + off);
+        off += bytes;
+        return p;
+    }
+    float* f(long n) { return (float*)take((size_t)n * 4); }
+};
+
+static void plan_blk(BlkAct& b, Bump& m, int R, int L, const Dims& z, int esz, bool train,
+                     bool alloc_x) {
+    long NL = (long)R * L;
+    if (alloc_x) { b.x_in = m.f(NL * z.D); }
+    b.ln1 = m.take(NL * z.D * esz);
+    b.qkv = m.take(NL * 3 * z.D * esz);
+    b.att = m.take(NL * z.D * esz);
+    b.ln2 = m.take(NL * z.D * esz);
+    b.fpre = train ? m.take(NL * z.FFN * esz) : nullptr;
+    b.fpost = m.take(NL * z.FFN * esz);
+    b.mu1 = m.f(NL); b.rs1 = m.f(NL); b.mu2 = m.f(NL); b.rs2 = m.f(NL);
+    b.lse = m.f(NL * z.H);
+    b.xm = m.f(NL * z.D);
+}
+
+static void plan_work(Work& W, Bump& m, int R, bool train, const Dims& z, int esz,
+                      bool bf16mode) {
+    W.R = R; W.train = train;
+    long NT = (long)R * z.LTOK, NS = (long)R * z.LSEQ, NO = (long)R * z.NOPT,
+         NC = (long)R * z.LCRIT;
+    W.tokcat = m.take(NT * rup(z.TOK_IN, 8) * esz);
+    W.keep = (uint8_t*)m.take(NS);
+    W.ckeep = (uint8_t*)m.take(NC);
+    W.g1pre = m.f((long)R * 128); W.g1 = m.f((long)R * 128);
+    W.gd = m.f((long)R * 192);
+    W.decin = m.f((long)R * 696); W.d1pre = m.f((long)R * 64); W.d1 = m.f((long)R * 64);
+    W.bc = m.f((long)R * z.D);
+    int nx = train ? z.LAYERS + 1 : 2;
+    W.x.assign(nx, nullptr);
+    for (int i = 0; i < nx; i++) W.x[i] = m.f(NS * z.D);
+    int nb = train ? z.LAYERS : 1;
+    W.blk.assign(nb, BlkAct{});
+    for (int i = 0; i < nb; i++) plan_blk(W.blk[i], m, R, z.LSEQ, z, esz, train, false);
+    W.h = m.f(NS * z.D); W.muf = m.f(NS); W.rsf = m.f(NS);
+    // option scorer: fp32 operands in both modes (its gradients reduce over
+    // options whose inputs share a large per-sample component; bf16 operand
+    // rounding would dominate those sums)
+    W.qin = m.f(NO * rup(z.Q_IN, 8));
+    W.q1pre = train ? m.f(NO * z.D) : nullptr;
+    W.q1 = m.f(NO * z.D);
+    W.q = m.f(NO * z.D);
+    W.scin = m.f(NO * z.SCORE_IN);
+    W.s1pre = train ? m.f(NO * 256) : nullptr;
+    W.s1 = m.f(NO * 256);
+    W.otokin = m.take((long)R * 56 * 136 * esz);
+    W.xc[0] = m.f(NC * z.D); W.xc[1] = m.f(NC * z.D);
+    plan_blk(W.cblk, m, R, z.LCRIT, z, esz, train, false);
+    W.ovin = m.f((long)R * z.VAL_IN); W.ov1pre = m.f((long)R * 256); W.ov1 = m.f((long)R * 256);
+    W.out = m.f((long)R * (z.NOPT + 1));
+    if (!train) return;
+    W.bvin = m.f((long)R * z.VAL_IN);
+    W.bvinc = bf16mode ? m.take((long)R * z.VAL_IN * esz) : nullptr;
+    W.bv1pre = m.f((long)R * 256); W.bv1 = m.f((long)R * 256); W.blind_v = m.f(R);
+    W.hand_lin = m.f((long)R * z.NC);
+    W.prize_logit = m.f(NT);
+    // backward
+    W.dh = m.f(NS * z.D);
+    W.dgd = m.f((long)R * 192);
+    W.dbvin = m.f((long)R * z.VAL_IN);
+    W.d_v1pre = m.f((long)R * 256);
+    W.dscores = m.f(NO);
+    W.dscin = m.f(NO * z.SCORE_IN);
+    W.dqin = m.f(NO * z.Q_IN);
+    W.dtokcat = m.f(NT * z.TOK_IN);
+    W.ddecin = m.f((long)R * 696);
+    W.dd1 = m.f((long)R * 64);
+    W.dg1 = m.f((long)R * 128);
+    W.dbc = m.f((long)R * z.D);
+    W.dotokin = m.f((long)R * 56 * 134);
+    W.dx = m.f(NC * z.D);
+    W.dln = m.f(NC * z.D);
+    W.dxc = bf16mode ? m.take(NC * z.D * esz) : (void*)W.dx;
+    W.dhand = m.take((long)R * z.NC * esz);
+    W.ds1pre = m.f(NO * 256);
+    W.dq = m.f(NO * z.D);
+    W.dq1 = m.f(NO * z.D);
+    W.dotok = m.take((long)R * 56 * z.D * esz);
+    W.dtokp = m.take(NT * z.D * esz);
+    W.df = m.take(NC * z.FFN * esz);
+    W.datt = m.take(NC * z.D * esz);
+    W.dqkv = m.take(NC * 3 * z.D * esz);
+    W.dgrad = m.f((long)R * (z.NOPT + 1));
+    W.fused = m.f((long)R * (z.NOPT + 1));
+    W.ppo_scratch = m.f(16 + 7 * ((R + 7) / 8));
+    W.nlp = m.f(R); W.ratio = m.f(R);
+}
+
+static void plan_tab(Tab& t, Bump& m, const Dims& z) {
+    t.att_in = m.f((long)z.NA * 127); t.att_pre = m.f((long)z.NA * 64); t.att_tab = m.f((long)z.NA * 64);
+    t.sk_in = m.f((long)z.NS * 112); t.sk_pre = m.f((long)z.NS * 128); t.sk_tab = m.f((long)z.NS * 128);
+    t.card_in = m.f((long)z.NC * 634); t.card_ln = m.f((long)z.NC * 634);
+    t.ln_mu = m.f(z.NC); t.ln_rs = m.f(z.NC);
+    t.h1pre = m.f((long)z.NC * 256); t.h1 = m.f((long)z.NC * 256);
+    t.card_vec = m.f((long)z.NC * 128);
+    t.poc = m.f((long)z.NC * 64); t.poa = m.f((long)z.NA * 64);
+    t.a_arg = (int8_t*)m.take((size_t)z.NC * 64);
+    t.s_arg = (int8_t*)m.take((size_t)z.NC * 128);
+    t.d_cv = m.f((long)z.NC * 128); t.d_att = m.f((long)z.NA * 64); t.d_sk = m.f((long)z.NS * 128);
+    t.d_poc = m.f((long)z.NC * 64); t.d_poa = m.f((long)z.NA * 64);
+    t.d_h1 = m.f((long)z.NC * 256); t.d_cardln = m.f((long)z.NC * 634);
+    t.d_cardin = m.f((long)z.NC * 634); t.d_attin = m.f((long)z.NA * 127);
+    t.d_skin = m.f((long)z.NS * 112);
+}
+
+// --------------------------------------------------------------- forward
+static void tables_fwd(PtcgModel* M, cudaStream_t s) {
+    const Dims& z = M->z;
+    Tab& t = M->tab;
+    Segs g{};
+    g.n = 3;
+    g.s[0] = {M->w("attack_id_emb").p, 48, 0, 48, 0};
+    g.s[1] = {M->att_static, 15, 0, 15, 48};
+    g.s[2] = {M->att_text, 64, 0, 64, 63};
+    k_concat_rows<<<cdiv((long)z.NA * 127, TPB), TPB, 0, s>>>(t.att_in, 127, z.NA, 127, g);
+    GemmArgs a = lin_fwd(DT_F32, z.NA, 127, 64, t.att_in, 127, f32w(M->w("attack_mlp_w"), 127), t.att_tab, 64, DT_F32);
+    a.bias = M->w("attack_mlp_b").p; a.act = ACT_GELU; a.out2 = t.att_pre; a.ldo2 = 64;
+    gemm_simt(a, s);
+    g.n = 2;
+    g.s[0] = {M->w("skill_id_emb").p, 48, 0, 48, 0};
+    g.s[1] = {M->skill_text, 64, 0, 64, 48};
+    k_concat_rows<<<cdiv((long)z.NS * 112, TPB), TPB, 0, s>>>(t.sk_in, 112, z.NS, 112, g);
+    a = lin_fwd(DT_F32, z.NS, 112, 128, t.sk_in, 112, f32w(M->w("skill_mlp_w"), 112), t.sk_tab, 128, DT_F32);
+    a.bias = M->w("skill_mlp_b").p; a.act = ACT_GELU; a.out2 = t.sk_pre; a.ldo2 = 128;
+    gemm_simt(a, s);
+    // pools written straight into their card_in columns
+    k_pool<<<cdiv((long)z.NC * 64, TPB), TPB, 0, s>>>(t.card_in + 250, t.card_in + 314, 634, t.a_arg,
+        t.att_tab, M->card_attacks, z.NC, 4, 64);
+    k_pool<<<cdiv((long)z.NC * 128, TPB), TPB, 0, s>>>(t.card_in + 378, t.card_in + 506, 634, t.s_arg,
+        t.sk_tab, M->card_skills, z.NC, 2, 128);
+    g.n = 3;
+    g.s[0] = {M->w("card_id_emb").p, 64, 0, 64, 0};
+    g.s[1] = {M->card_static, 58, 0, 58, 64};
+    g.s[2] = {M->card_text, 128, 0, 128, 122};
+    k_concat_rows<<<cdiv((long)z.NC * 250, TPB), TPB, 0, s>>>(t.card_in, 634, z.NC, 250, g);
+    ln_fwd(DT_F32, t.card_ln, 634, t.ln_mu, t.ln_rs, t.card_in, 634, M->w("card_ln_w").p,
+           M->w("card_ln_b").p, z.NC, 634, s);
+    a = lin_fwd(DT_F32, z.NC, 634, 256, t.card_ln, 634, f32w(M->w("card_mlp1_w"), 634), t.h1, 256, DT_F32);
+    a.bias = M->w("card_mlp1_b").p; a.act = ACT_GELU; a.out2 = t.h1pre; a.ldo2 = 256;
+    gemm_simt(a, s);
+    a = lin_fwd(DT_F32, z.NC, 256, 128, t.h1, 256, f32w(M->w("card_mlp2_w"), 256), t.card_vec, 128, DT_F32);
+    a.bias = M->w("card_mlp2_b").p;
+    gemm_simt(a, s);
+    // option-scorer card / attack projections, per table row
+    a = lin_fwd(DT_F32, z.NC, 128, 64, t.card_vec, 128, f32w(M->w("opt_card_w"), 128), t.poc, 64, DT_F32);
+    a.bias = M->w("opt_card_b").p;
+    gemm_simt(a, s);
+    a = lin_fwd(DT_F32, z.NA, 64, 64, t.att_tab, 64, f32w(M->w("opt_attack_w"), 64), t.poa, 64, DT_F32);
+    a.bias = M->w("opt_attack_b").p;
+    gemm_simt(a, s);
+}
+
+static void block_fwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* keep, int R, int L,
+                      bool train, cudaStream_t s) {
+    const Dims& z = M->z;
+    const int dt = M->dt(), D = z.D;
+    const int NL = R * L;
+    ln_fwd(dt, b.ln1, D, b.mu1, b.rs1, b.x_in, D, P.ln1w.p, P.ln1b.p, NL, D, s);
+    GemmArgs a = lin_fwd(dt, NL, D, 3 * D, b.ln1, D, P.qkvw, b.qkv, 3 * D, dt);
+    a.bias = P.qkvb.p;
+    gemm(M, a, s);
+    attn_fwd(dt, b.qkv, 3 * D, keep, b.att, D, b.lse, R, L, z.H, s);
+    a = lin_fwd(dt, NL, D, D, b.att, D, P.projw, b.xm, D, DT_F32);
+    a.bias = P.projb.p; a.resid = b.x_in; a.ld_resid = D;
+    gemm(M, a, s);
+    ln_fwd(dt, b.ln2, D, b.mu2, b.rs2, b.xm, D, P.ln2w.p, P.ln2b.p, NL, D, s);
+    a = lin_fwd(dt, NL, D, z.FFN, b.ln2, D, P.f1w, b.fpost, z.FFN, dt);
+    a.bias = P.f1b.p; a.act = ACT_GELU;
+    if (train) { a.out2 = b.fpre; a.ldo2 = z.FFN; a.out2_dtype = dt; }
+    gemm(M, a, s);
+    a = lin_fwd(dt, NL, z.FFN, D, b.fpost, z.FFN, P.f2w, b.x_out, D, DT_F32);
+    a.bias = P.f2b.p; a.resid = b.xm; a.ld_resid = D;
+    gemm(M, a, s);
+}
+
+// rows-dot launcher
+template <typename TI>
+static void rowdot(float* out, long os, const TI* in, long ldi, const float* w, const float* b,
+                   int rows, int K, int g, int gs, int go, cudaStream_t s) {
+    k_rowdot<TI><<<cdiv(rows, 8), 256, 0, s>>>(out, os, in, ldi, w, b, rows, K, g, gs, go);
+}
+
+static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* out, bool train,
+                        bool do_tables, cudaStream_t s) {
+    const Dims& z = M->z;
+    const int dt = M->dt(), D = z.D, esz = M->esz();
+    const ObsLayout& ol = z.ol;
+    const int tf32 = M->prec == PTCG_BF16;   // fp32-operand GEMMs may use TF32 in bf16 mode
+    if (do_tables) tables_fwd(M, s);
+    const Tab& t = M->tab;
+    // --- token path
+    long ldtok = rup(z.TOK_IN, 8);
+    long ntc = (long)R * z.LTOK * z.TOK_IN;
+    if (dt == DT_F32)
+        k_tok_cat<float><<<cdiv(ntc, TPB), TPB, 0, s>>>((float*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
+            M->w("zone_emb").p, M->w("owner_emb").p, R, z.TOK_IN);
+    else
+        k_tok_cat<bf16><<<cdiv(ntc, TPB), TPB, 0, s>>>((bf16*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
+            M->w("zone_emb").p, M->w("owner_emb").p, R, z.TOK_IN);
+    k_x0_readout<<<cdiv((long)R * (z.LSEQ > D ? z.LSEQ : D), TPB), TPB, 0, s>>>(Wk.x[0], Wk.keep,
+        M->w("readout").p, obs, ol, R, D);
+    // --- global / decision encoders (fp32)
+    GemmArgs a = lin_fwd(DT_F32, R, 64, 128, obs + ol.glob, ol.obs, f32w(M->w("global1_w"), 64),
+                         Wk.g1, 128, DT_F32);
+    a.bias = M->w("global1_b").p; a.act = ACT_GELU; a.out2 = Wk.g1pre; a.ldo2 = 128;
+    gemm_simt(a, s);
+    a = lin_fwd(DT_F32, R, 128, 128, Wk.g1, 128, f32w(M->w("global2_w"), 128), Wk.gd, 192, DT_F32);
+    a.bias = M->w("global2_b").p;
+    gemm_simt(a, s);
+    k_dec_in<<<cdiv((long)R * 696, TPB), TPB, 0, s>>>(Wk.decin, obs, ol, t.card_vec, t.att_tab,
+        M->w("sel_type_emb").p, M->w("ctx_emb").p, R);
+    a = lin_fwd(DT_F32, R, 696, 64, Wk.decin, 696, f32w(M->w("dec1_w"), 696), Wk.d1, 64, DT_F32);
+    a.bias = M->w("dec1_b").p; a.act = ACT_GELU; a.out2 = Wk.d1pre; a.ldo2 = 64;
+    gemm_simt(a, s);
+    a = lin_fwd(DT_F32, R, 64, 64, Wk.d1, 64, f32w(M->w("dec2_w"), 64), Wk.gd + 128, 192, DT_F32);
+    a.bias = M->w("dec2_b").p;
+    gemm_simt(a, s);
+    a = lin_fwd(DT_F32, R, 192, D, Wk.gd, 192, f32w(M->w("bcast_w"), 192), Wk.bc, D, DT_F32);
+    a.bias = M->w("bcast_b").p;
+    gemm_simt(a, s);
+    // token_proj + broadcast, written into trunk rows 1..LTOK
+    a = lin_fwd(dt, R * z.LTOK, z.TOK_IN, D, Wk.tokcat, ldtok, M->w("token_proj_w"), Wk.x[0], D, DT_F32);
+    a.bias = M->w("token_proj_b").p;
+    a.bcast = Wk.bc; a.ld_bcast = D; a.bcast_group = z.LTOK;
+    a.remap_group = z.LTOK; a.remap_stride = z.LSEQ; a.remap_off = 1;
+    gemm(M, a, s);
+    // --- trunk
+    const float* xl = Wk.x[0];
+    for (int i = 0; i < z.LAYERS; i++) {
+        BlkAct& b = train ? Wk.blk[i] : Wk.blk[0];
+        b.x_in = train ? Wk.x[i] : Wk.x[i % 2];
+        b.x_out = train ? Wk.x[i + 1] : Wk.x[(i + 1) % 2];
+        block_fwd(M, M->blk("b" + std::to_string(i) + "_"), b, Wk.keep, R, z.LSEQ, train, s);
+        xl = b.x_out;
+    }
+    ln_fwd(DT_F32, Wk.h, D, Wk.muf, Wk.rsf, xl, D, M->w("lnf_w").p, M->w("lnf_b").p, R * z.LSEQ, D, s);
+    // --- option scorer
+    long NO = (long)R * z.NOPT;
+    long ldq = rup(z.Q_IN, 8);
+    k_q_in<float><<<cdiv(NO * z.Q_IN, TPB), TPB, 0, s>>>((float*)Wk.qin, ldq, obs, ol, Wk.h, D,
+        M->w("opt_type_emb").p, t.poc, t.poa, R, z.Q_IN);
+    a = lin_fwd(DT_F32, (int)NO, z.Q_IN, D, Wk.qin, ldq, f32w(M->w("q1_w"), z.Q_IN), Wk.q1, D, DT_F32);
+    a.bias = M->w("q1_b").p; a.act = ACT_GELU; a.allow_tf32 = tf32;
+    if (train) { a.out2 = Wk.q1pre; a.ldo2 = D; }
+    gemm(M, a, s);
+    a = lin_fwd(DT_F32, (int)NO, D, D, Wk.q1, D, f32w(M->w("q2_w"), D), Wk.q, D, DT_F32);
+    a.bias = M->w("q2_b").p; a.allow_tf32 = tf32;
+    gemm(M, a, s);
+    long nsc = NO * z.SCORE_IN;
+    k_sc_in<float><<<cdiv(nsc, TPB), TPB, 0, s>>>((float*)Wk.scin, z.SCORE_IN, Wk.q, Wk.h, Wk.gd,
+        D, z.LSEQ, z.NOPT, R);
+    a = lin_fwd(DT_F32, (int)NO, z.SCORE_IN, 256, Wk.scin, z.SCORE_IN,
+                f32w(M->w("score1_w"), z.SCORE_IN), Wk.s1, 256, DT_F32);
+    a.bias = M->w("score1_b").p; a.act = ACT_GELU; a.allow_tf32 = tf32;
+    if (train) { a.out2 = Wk.s1pre; a.ldo2 = 256; }
+    gemm(M, a, s);
+    // score2 -> out[n, j]  (out row stride NOPT+1): rows r = n*NOPT + j map to
+    // n*(NOPT+1) + j, i.e. group NOPT of output stride NOPT+1
+    {
+        int rows = (int)NO;
+        unsigned g = cdiv(rows, 8);
+        k_rowdot<float><<<g, 256, 0, s>>>(Wk.out, 1, (const float*)Wk.s1, 256,
+            M->w("score2_w").p, M->w("score2_b").p, rows, 256, 0, 0, 0);
+    }
+    // (scores are staged contiguous (R*NOPT) at the head of Wk.out and
+    //  expanded to the fused layout at the end)
+    // --- oracle critic top
+    long ldo_t = rup(134, 8);
+    long no = (long)R * 56 * 134;
+    if (dt == DT_F32)
+        k_otok_in<float><<<cdiv(no, TPB), TPB, 0, s>>>((float*)Wk.otokin, ldo_t, Wk.ckeep, obs, ol,
+            t.card_vec, Wk.keep, R);
+    else
+        k_otok_in<bf16><<<cdiv(no, TPB), TPB, 0, s>>>((bf16*)Wk.otokin, ldo_t, Wk.ckeep, obs, ol,
+            t.card_vec, Wk.keep, R);
+    k_xc_fill<<<cdiv((long)R * (1 + z.LSEQ) * D, TPB), TPB, 0, s>>>(Wk.xc[0], Wk.h,
+        M->w("critic_readout").p, z.LSEQ, z.LCRIT, D, R);
+    a = lin_fwd(dt, R * 56, 134, D, Wk.otokin, ldo_t, M->w("oracle_proj_w"), Wk.xc[0], D, DT_F32);
+    a.bias = M->w("oracle_proj_b").p;
+    a.remap_group = 56; a.remap_stride = z.LCRIT; a.remap_off = 1 + z.LSEQ;
+    gemm(M, a, s);
+    Wk.cblk.x_in = Wk.xc[0]; Wk.cblk.x_out = Wk.xc[1];
+    block_fwd(M, M->blk("c0_"), Wk.cblk, Wk.ckeep, R, z.LCRIT, train, s);
+    k_val_in<float><<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.ovin, nullptr, 0, Wk.xc[1],
+        z.LCRIT, D, Wk.gd, R);
+    a = lin_fwd(DT_F32, R, z.VAL_IN, 256, Wk.ovin, z.VAL_IN, f32w(M->w("oracle_v1_w"), z.VAL_IN),
+                Wk.ov1, 256, DT_F32);
+    a.bias = M->w("oracle_v1_b").p; a.act = ACT_GELU; a.out2 = Wk.ov1pre; a.ldo2 = 256;
+    gemm_simt(a, s);
+    // fused output [scores | value]: expand staged scores, then the value column
+    k_scale_copy<<<cdiv(NO, TPB), TPB, 0, s>>>(out, z.NOPT + 1, Wk.out, z.NOPT, R, z.NOPT, 1.f);
+    rowdot<float>(out + z.NOPT, z.NOPT + 1, Wk.ov1, 256, M->w("oracle_v2_w").p,
+                  M->w("oracle_v2_b").p, R, 256, 0, 0, 0, s);
+    if (!train) return 0;
+    // --- train-only heads: blind V, opp-hand counts, prize logits
+    if (dt == DT_F32)
+        k_val_in<float><<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.bvin, nullptr, 0, Wk.h,
+            z.LSEQ, D, Wk.gd, R);
+    else
+        k_val_in<bf16><<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.bvin, (bf16*)Wk.bvinc,
+            z.VAL_IN, Wk.h, z.LSEQ, D, Wk.gd, R);
+    a = lin_fwd(DT_F32, R, z.VAL_IN, 256, Wk.bvin, z.VAL_IN, f32w(M->w("value1_w"), z.VAL_IN),
+                Wk.bv1, 256, DT_F32);
+    a.bias = M->w("value1_b").p; a.act = ACT_GELU; a.out2 = Wk.bv1pre; a.ldo2 = 256;
+    gemm_simt(a, s);
+    rowdot<float>(Wk.blind_v, 1, Wk.bv1, 256, M->w("value2_w").p, M->w("value2_b").p, R, 256,
+                  0, 0, 0, s);
+    a = lin_fwd(dt, R, z.VAL_IN, z.NC, dt == DT_F32 ? (const void*)Wk.bvin : Wk.bvinc, z.VAL_IN,
+                M->w("aux_hand_w"), Wk.hand_lin, z.NC, DT_F32);
+    a.bias = M->w("aux_hand_b").p;
+    gemm(M, a, s);
+    rowdot<float>(Wk.prize_logit, 1, Wk.h, D, M->w("aux_prize_w").p, M->w("aux_prize_b").p,
+                  R * z.LTOK, D, z.LTOK, z.LSEQ, 1, s);
+    (void)esz;
+    return 0;
+}
+
+// --------------------------------------------------------------- backward
+static void fire_hook(PtcgModel* M, const char* first, const char* last_excl, cudaStream_t s) {
+    if (!M->hook) return;
+    long a = M->off[M->idx[first]];
+    long b = last_excl ? M->off[M->idx[last_excl]] : M->n_arena;
+    if (b > a) M->hook(M->hook_user, a, b - a, (void*)s);
+}
+
+static void block_bwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* keep, Work& Wk,
+                      int R, int L, cudaStream_t s) {
+    const Dims& z = M->z;
+    const int dt = M->dt(), D = z.D, F = z.FFN;
+    const int NL = R * L;
+    const bool bf = dt == DT_BF16;
+    float* dx = Wk.dx;                 // f32, holds d(x_out) on entry
+    void* dxc = Wk.dxc;                // operand-dtype copy of dx
+    // FFN2
+    colsum<float>(P.f2b.g, dx, D, NL, D, s);
+    gemm(M, lin_dw(dt, NL, F, D, dxc, D, b.fpost, F, P.f2w.g), s);
+    GemmArgs a = lin_dx(dt, NL, F, D, dxc, D, P.f2w, Wk.df, F, dt);
+    a.act = ACT_GELU_BWD; a.aux = b.fpre; a.ld_aux = F; a.aux_dtype = dt;
+    a.colsum = P.f1b.g;                 // FFN1 bias grad, fp32 before rounding
+    gemm(M, a, s);
+    // FFN1
+    gemm(M, lin_dw(dt, NL, D, F, Wk.df, F, b.ln2, D, P.f1w.g), s);
+    gemm(M, lin_dx(dt, NL, D, F, Wk.df, F, P.f1w, Wk.dln, D, DT_F32), s);
+    // LN2: dx <- d(x_mid) = dx + LN2'(dln)
+    ln_bwd(dt, dx, 1, bf ? dxc : nullptr, P.ln2w.g, P.ln2b.g, Wk.dln, b.xm, P.ln2w.p, b.mu2,
+           b.rs2, NL, D, s);
+    // proj
+    colsum<float>(P.projb.g, dx, D, NL, D, s);
+    gemm(M, lin_dw(dt, NL, D, D, dxc, D, b.att, D, P.projw.g), s);
+    gemm(M, lin_dx(dt, NL, D, D, dxc, D, P.projw, Wk.datt, D, dt), s);
+    // attention
+    attn_bwd(dt, b.qkv, 3 * D, keep, b.att, D, Wk.datt, D, b.lse, Wk.dqkv, 3 * D, P.qkvb.g,
+             R, L, z.H, s);
+    // QKV
+    gemm(M, lin_dw(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, b.ln1, D, P.qkvw.g), s);
+    gemm(M, lin_dx(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, P.qkvw, Wk.dln, D, DT_F32), s);
+    // LN1: dx <- d(x_in) = dx + LN1'(dln)
+    ln_bwd(dt, dx, 1, bf ? dxc : nullptr, P.ln1w.g, P.ln1b.g, Wk.dln, b.x_in, P.ln1w.p, b.mu1,
+           b.rs1, NL, D, s);
+}
+
+static void tables_bwd(PtcgModel* M, cudaStream_t s) {
+    const Dims& z = M->z;
+    Tab& t = M->tab;
+    // card_mlp2
+    colsum<float>(M->w("card_mlp2_b").g, t.d_cv, 128, z.NC, 128, s);
+    gemm_simt(lin_dw(DT_F32, z.NC, 256, 128, t.d_cv, 128, t.h1, 256, M->w("card_mlp2_w").g), s);
+    GemmArgs a = lin_dx(DT_F32, z.NC, 256, 128, t.d_cv, 128, f32w(M->w("card_mlp2_w"), 256),
+                        t.d_h1, 256, DT_F32);
+    a.act = ACT_GELU_BWD; a.aux = t.h1pre; a.ld_aux = 256; a.aux_dtype = DT_F32;
+    gemm_simt(a, s);
+    // card_mlp1
+    colsum<float>(M->w("card_mlp1_b").g, t.d_h1, 256, z.NC, 256, s);
+    gemm_simt(lin_dw(DT_F32, z.NC, 634, 256, t.d_h1, 256, t.card_ln, 634, M->w("card_mlp1_w").g), s);
+    gemm_simt(lin_dx(DT_F32, z.NC, 634, 256, t.d_h1, 256, f32w(M->w("card_mlp1_w"), 634),
+                     t.d_cardln, 634, DT_F32), s);
+    // card LayerNorm (input card_in, ld 634) -> d_cardin
+    {
+        int rpb = 64;
+        k_ln_bwd<float><<<cdiv(z.NC, rpb), 256, 2 * 634 * sizeof(float), s>>>(t.d_cardin, 634, 0,
+            nullptr, 634, M->w("card_ln_w").g, M->w("card_ln_b").g, t.d_cardln, 634, t.card_in, 634,
+            M->w("card_ln_w").p, t.ln_mu, t.ln_rs, z.NC, 634, rpb);
+    }
+    k_slice_add<<<cdiv((long)z.NC * 64, TPB), TPB, 0, s>>>(M->w("card_id_emb").g, t.d_cardin,
+        z.NC, 64, 634, 0);
+    k_pool_bwd<<<cdiv((long)z.NC * 64, TPB), TPB, 0, s>>>(t.d_att, t.d_cardin, 634, 250, 314,
+        t.a_arg, M->card_attacks, z.NC, 4, 64);
+    k_pool_bwd<<<cdiv((long)z.NC * 128, TPB), TPB, 0, s>>>(t.d_sk, t.d_cardin, 634, 378, 506,
+        t.s_arg, M->card_skills, z.NC, 2, 128);
+    // attack mlp
+    k_gelu_bwd<<<cdiv((long)z.NA * 64, TPB), TPB, 0, s>>>(t.d_att, t.att_pre, (long)z.NA * 64);
+    colsum<float>(M->w("attack_mlp_b").g, t.d_att, 64, z.NA, 64, s);
+    gemm_simt(lin_dw(DT_F32, z.NA, 127, 64, t.d_att, 64, t.att_in, 127, M->w("attack_mlp_w").g), s);
+    gemm_simt(lin_dx(DT_F32, z.NA, 127, 64, t.d_att, 64, f32w(M->w("attack_mlp_w"), 127),
+                     t.d_attin, 127, DT_F32), s);
+    k_slice_add<<<cdiv((long)z.NA * 48, TPB), TPB, 0, s>>>(M->w("attack_id_emb").g, t.d_attin,
+        z.NA, 48, 127, 0);
+    // skill mlp
+    k_gelu_bwd<<<cdiv((long)z.NS * 128, TPB), TPB, 0, s>>>(t.d_sk, t.sk_pre, (long)z.NS * 128);
+    colsum<float>(M->w("skill_mlp_b").g, t.d_sk, 128, z.NS, 128, s);
+    gemm_simt(lin_dw(DT_F32, z.NS, 112, 128, t.d_sk, 128, t.sk_in, 112, M->w("skill_mlp_w").g), s);
+    gemm_simt(lin_dx(DT_F32, z.NS, 112, 128, t.d_sk, 128, f32w(M->w("skill_mlp_w"), 112),
+                     t.d_skin, 112, DT_F32), s);
+    k_slice_add<<<cdiv((long)z.NS * 48, TPB), TPB, 0, s>>>(M->w("skill_id_emb").g, t.d_skin,
+        z.NS, 48, 112, 0);
+}
+
+static void zero_table_grads(PtcgModel* M, cudaStream_t s) {
+    const Dims& z = M->z;
+    Tab& t = M->tab;
+    cudaMemsetAsync(t.d_cv, 0, (size_t)z.NC * 128 * 4, s);
+    cudaMemsetAsync(t.d_att, 0, (size_t)z.NA * 64 * 4, s);
+    cudaMemsetAsync(t.d_sk, 0, (size_t)z.NS * 128 * 4, s);
+}
+
+// aux_norm_rows: rows of the whole minibatch; prize_cnt_dev: device count of
+// MY_UNSEEN tokens in the whole minibatch (or nullptr + prize_cnt_host)
+static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* grad,
+                         const float* returns, int R, int norm_rows, const float* prize_cnt_dev,
+                         float prize_cnt_host, float* aux_loss, bool last, cudaStream_t s) {
+    const Dims& z = M->z;
+    const int dt = M->dt(), D = z.D;
+    const bool bf = dt == DT_BF16;
+    const int tf32 = bf;
+    const ObsLayout& ol = z.ol;
+    Tab& t = M->tab;
+    long NS = (long)R * z.LSEQ, NO = (long)R * z.NOPT;
+    cudaMemsetAsync(Wk.dh, 0, NS * D * 4, s);
+    cudaMemsetAsync(Wk.dgd, 0, (size_t)R * 192 * 4, s);
+    cudaMemsetAsync(t.d_poc, 0, (size_t)z.NC * 64 * 4, s);
+    cudaMemsetAsync(t.d_poa, 0, (size_t)z.NA * 64 * 4, s);
+    // ---- aux: opponent-hand counts
+    float hscale = 0.1f / ((float)norm_rows * (float)z.NC);
+    if (bf)
+        k_hand_grad<bf16><<<R, 256, z.NC * sizeof(float), s>>>((bf16*)Wk.dhand, z.NC, Wk.hand_lin,
+            z.NC, obs, ol, hscale, aux_loss + 1);
+    else
+        k_hand_grad<float><<<R, 256, z.NC * sizeof(float), s>>>((float*)Wk.dhand, z.NC, Wk.hand_lin,
+            z.NC, obs, ol, hscale, aux_loss + 1);
+    W wh = M->w("aux_hand_w");
+    colsum<float>(M->w("aux_hand_b").g, Wk.hand_lin, z.NC, R, z.NC, s);   // fp32 grad copy
+    gemm(M, lin_dw(dt, R, z.VAL_IN, z.NC, Wk.dhand, z.NC, bf ? Wk.bvinc : (void*)Wk.bvin,
+                   z.VAL_IN, wh.g), s);
+    gemm(M, lin_dx(dt, R, z.VAL_IN, z.NC, Wk.dhand, z.NC, wh, Wk.dbvin, z.VAL_IN, DT_F32), s);
+    // ---- aux: blind V (0.5 * mean (v - R)^2)
+    {
+        int rpb = 64;
+        k_rowdot_bwd<float, float><<<cdiv(R, rpb), 256, (256 + 1) * sizeof(float), s>>>(
+            Wk.d_v1pre, 256, Wk.bv1pre, 256, Wk.bv1, 256, M->w("value2_w").p, M->w("value2_w").g,
+            M->w("value2_b").g, Wk.blind_v, 1, returns, 1.0f / (float)norm_rows, R, 256, rpb,
+            aux_loss + 0, M->w("value1_b").g);
+    }
+    gemm_simt(lin_dw(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, Wk.bvin, z.VAL_IN,
+                     M->w("value1_w").g), s);
+    {
+        GemmArgs a = lin_dx(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256,
+                            f32w(M->w("value1_w"), z.VAL_IN), Wk.dbvin, z.VAL_IN, DT_F32);
+        a.accumulate = 1;
+        gemm_simt(a, s);
+    }
+    k_val_in_bwd<<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.dh, z.LSEQ, D, Wk.dgd, Wk.dbvin, R, 1);
+    // ---- aux: prize BCE over MY_UNSEEN tokens
+    k_prize_bwd<<<cdiv((long)R * z.LTOK, 8), 256, 0, s>>>(Wk.dh, M->w("aux_prize_w").g,
+        M->w("aux_prize_b").g, Wk.prize_logit, Wk.h, M->w("aux_prize_w").p, obs, ol, prize_cnt_dev,
+        prize_cnt_host, D, R, aux_loss + 2);
+    // ---- oracle value head (PPO value grad = grad[:, NOPT])
+    {
+        int rpb = 64;
+        k_rowdot_bwd<float, float><<<cdiv(R, rpb), 256, (256 + 1) * sizeof(float), s>>>(
+            Wk.d_v1pre, 256, Wk.ov1pre, 256, Wk.ov1, 256, M->w("oracle_v2_w").p,
+            M->w("oracle_v2_w").g, M->w("oracle_v2_b").g, grad + z.NOPT, z.NOPT + 1, nullptr, 0.f,
+            R, 256, rpb, nullptr, M->w("oracle_v1_b").g);
+    }
+    gemm_simt(lin_dw(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, Wk.ovin, z.VAL_IN,
+                     M->w("oracle_v1_w").g), s);
+    gemm_simt(lin_dx(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, f32w(M->w("oracle_v1_w"), z.VAL_IN),
+                     Wk.dbvin, z.VAL_IN, DT_F32), s);
+    long NC_ = (long)R * z.LCRIT;
+    cudaMemsetAsync(Wk.dx, 0, NC_ * D * 4, s);
+    k_val_in_bwd<<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.dx, z.LCRIT, D, Wk.dgd, Wk.dbvin, R, 1);
+    if (bf) k_cast<bf16><<<cdiv(NC_ * D, TPB), TPB, 0, s>>>((bf16*)Wk.dxc, D, Wk.dx, D, (int)NC_, D);
+    // ---- critic block
+    block_bwd(M, M->blk("c0_"), Wk.cblk, Wk.ckeep, Wk, R, z.LCRIT, s);
+    long nxc = NC_ * D;
+    if (bf)
+        k_xc_bwd<bf16><<<cdiv(nxc, TPB), TPB, 0, s>>>(M->w("critic_readout").g, Wk.dh, (bf16*)Wk.dotok,
+            Wk.dx, z.LSEQ, z.LCRIT, D, R);
+    else
+        k_xc_bwd<float><<<cdiv(nxc, TPB), TPB, 0, s>>>(M->w("critic_readout").g, Wk.dh,
+            (float*)Wk.dotok, Wk.dx, z.LSEQ, z.LCRIT, D, R);
+    W wo = M->w("oracle_proj_w");
+    {   // oracle_proj bias grad: fp32 sum of the critic-input grad rows 1+LSEQ..
+        int gpb = 64;
+        dim3 g(cdiv(D, 128), cdiv(R, gpb));
+        k_colsum_groups<<<g, 128, 0, s>>>(M->w("oracle_proj_b").g, Wk.dx, D, R, z.LCRIT,
+                                          1 + z.LSEQ, 56, D, gpb);
+    }
+    gemm(M, lin_dw(dt, R * 56, 134, D, Wk.dotok, D, Wk.otokin, rup(134, 8), wo.g), s);
+    gemm(M, lin_dx(dt, R * 56, 134, D, Wk.dotok, D, wo, Wk.dotokin, 134, DT_F32), s);
+    k_otok_bwd<<<cdiv((long)R * 56 * 128, TPB), TPB, 0, s>>>(t.d_cv, Wk.dotokin, 134, obs, ol, R);
+    // ---- option scorer (d scores = grad[:, :NOPT])
+    k_scale_copy<<<cdiv(NO, TPB), TPB, 0, s>>>(Wk.dscores, z.NOPT, grad, z.NOPT + 1, R, z.NOPT, 1.f);
+    {
+        int rpb = 64;
+        unsigned g = cdiv(NO, rpb);
+        k_rowdot_bwd<float, float><<<g, 256, 257 * sizeof(float), s>>>((float*)Wk.ds1pre, 256,
+                (const float*)Wk.s1pre, 256, (const float*)Wk.s1, 256, M->w("score2_w").p,
+                M->w("score2_w").g, M->w("score2_b").g, Wk.dscores, 1, nullptr, 0.f, (int)NO, 256,
+                rpb, nullptr, M->w("score1_b").g);
+    }
+    W ws1 = f32w(M->w("score1_w"), z.SCORE_IN);
+    {
+        GemmArgs a = lin_dw(DT_F32, (int)NO, z.SCORE_IN, 256, Wk.ds1pre, 256, Wk.scin, z.SCORE_IN, ws1.g);
+        a.allow_tf32 = tf32;
+        gemm(M, a, s);
+        a = lin_dx(DT_F32, (int)NO, z.SCORE_IN, 256, Wk.ds1pre, 256, ws1, Wk.dscin, z.SCORE_IN, DT_F32);
+        a.allow_tf32 = tf32;
+        gemm(M, a, s);
+    }
+    k_sc_in_bwd<float><<<R, 256, 0, s>>>((float*)Wk.dq, D, Wk.dh, Wk.dgd, Wk.dscin, z.SCORE_IN,
+            Wk.q, Wk.h, D, z.LSEQ, z.NOPT, M->w("q2_b").g);
+    W wq2 = f32w(M->w("q2_w"), D), wq1 = f32w(M->w("q1_w"), z.Q_IN);
+    {
+        GemmArgs a = lin_dw(DT_F32, (int)NO, D, D, Wk.dq, D, Wk.q1, D, wq2.g);
+        a.allow_tf32 = tf32;
+        gemm(M, a, s);
+        a = lin_dx(DT_F32, (int)NO, D, D, Wk.dq, D, wq2, Wk.dq1, D, DT_F32);
+        a.act = ACT_GELU_BWD; a.aux = Wk.q1pre; a.ld_aux = D; a.aux_dtype = DT_F32;
+        a.colsum = M->w("q1_b").g; a.allow_tf32 = tf32;
+        gemm(M, a, s);
+    }
+    long ldq = rup(z.Q_IN, 8);
+    {
+        GemmArgs a = lin_dw(DT_F32, (int)NO, z.Q_IN, D, Wk.dq1, D, Wk.qin, ldq, wq1.g);
+        a.allow_tf32 = tf32;
+        gemm(M, a, s);
+        a = lin_dx(DT_F32, (int)NO, z.Q_IN, D, Wk.dq1, D, wq1, Wk.dqin, z.Q_IN, DT_F32);
+        a.allow_tf32 = tf32;
+        gemm(M, a, s);
+    }
+    k_q_in_bwd<<<cdiv(NO * z.Q_IN, TPB), TPB, 0, s>>>(M->w("opt_type_emb").g, Wk.dh, t.d_poc,
+        t.d_poa, Wk.dqin, z.Q_IN, obs, ol, D, R, z.Q_IN);
+    // opt_card / opt_attack per-table-row projections -> table grads
+    colsum<float>(M->w("opt_card_b").g, t.d_poc, 64, z.NC, 64, s);
+    gemm_simt(lin_dw(DT_F32, z.NC, 128, 64, t.d_poc, 64, t.card_vec, 128, M->w("opt_card_w").g), s);
+    {
+        GemmArgs a = lin_dx(DT_F32, z.NC, 128, 64, t.d_poc, 64, f32w(M->w("opt_card_w"), 128),
+                            t.d_cv, 128, DT_F32);
+        a.accumulate = 1;
+        gemm_simt(a, s);
+    }
+    colsum<float>(M->w("opt_attack_b").g, t.d_poa, 64, z.NA, 64, s);
+    gemm_simt(lin_dw(DT_F32, z.NA, 64, 64, t.d_poa, 64, t.att_tab, 64, M->w("opt_attack_w").g), s);
+    {
+        GemmArgs a = lin_dx(DT_F32, z.NA, 64, 64, t.d_poa, 64, f32w(M->w("opt_attack_w"), 64),
+                            t.d_att, 64, DT_F32);
+        a.accumulate = 1;
+        gemm_simt(a, s);
+    }
+    // ---- ln_f
+    ln_bwd(dt, Wk.dx, 0, bf ? Wk.dxc : nullptr, M->w("lnf_w").g, M->w("lnf_b").g, Wk.dh,
+           Wk.x[z.LAYERS], M->w("lnf_w").p, Wk.muf, Wk.rsf, (int)NS, D, s);
+    if (last) fire_hook(M, "lnf_w", nullptr, s);
+    // ---- trunk
+    for (int i = z.LAYERS - 1; i >= 0; i--) {
+        std::string p = "b" + std::to_string(i) + "_";
+        block_bwd(M, M->blk(p), Wk.blk[i], Wk.keep, Wk, R, z.LSEQ, s);
+        if (last) fire_hook(M, (p + "ln1_w").c_str(),
+                            i == z.LAYERS - 1 ? "lnf_w" : ("b" + std::to_string(i + 1) + "_ln1_w").c_str(), s);
+    }
+    // ---- x0 split, token projection, broadcast
+    if (bf)
+        k_x0_bwd<bf16><<<R, 256, 0, s>>>(M->w("readout").g, (bf16*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D);
+    else
+        k_x0_bwd<float><<<R, 256, 0, s>>>(M->w("readout").g, (float*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D);
+    W wt = M->w("token_proj_w");
+    long ldtok = rup(z.TOK_IN, 8);
+    colsum<float>(M->w("token_proj_b").g, Wk.dbc, D, R, D, s);
+    gemm(M, lin_dw(dt, R * z.LTOK, z.TOK_IN, D, Wk.dtokp, D, Wk.tokcat, ldtok, wt.g), s);
+    gemm(M, lin_dx(dt, R * z.LTOK, z.TOK_IN, D, Wk.dtokp, D, wt, Wk.dtokcat, z.TOK_IN, DT_F32), s);
+    k_tok_cat_bwd<<<cdiv((long)R * z.LTOK * z.TOK_IN, TPB), TPB, 0, s>>>(t.d_cv, M->w("zone_emb").g,
+        M->w("owner_emb").g, Wk.dtokcat, z.TOK_IN, obs, ol, R, z.TOK_IN);
+    colsum<float>(M->w("bcast_b").g, Wk.dbc, D, R, D, s);
+    gemm_simt(lin_dw(DT_F32, R, 192, D, Wk.dbc, D, Wk.gd, 192, M->w("bcast_w").g), s);
+    {
+        GemmArgs a = lin_dx(DT_F32, R, 192, D, Wk.dbc, D, f32w(M->w("bcast_w"), 192), Wk.dgd, 192, DT_F32);
+        a.accumulate = 1;
+        gemm_simt(a, s);
+    }
+    // ---- decision encoder
+    colsum<float>(M->w("dec2_b").g, Wk.dgd + 128, 192, R, 64, s);
+    gemm_simt(lin_dw(DT_F32, R, 64, 64, Wk.dgd + 128, 192, Wk.d1, 64, M->w("dec2_w").g), s);
+    {
+        GemmArgs a = lin_dx(DT_F32, R, 64, 64, Wk.dgd + 128, 192, f32w(M->w("dec2_w"), 64), Wk.dd1,
+                            64, DT_F32);
+        a.act = ACT_GELU_BWD; a.aux = Wk.d1pre; a.ld_aux = 64; a.aux_dtype = DT_F32;
+        gemm_simt(a, s);
+    }
+    colsum<float>(M->w("dec1_b").g, Wk.dd1, 64, R, 64, s);
+    gemm_simt(lin_dw(DT_F32, R, 696, 64, Wk.dd1, 64, Wk.decin, 696, M->w("dec1_w").g), s);
+    gemm_simt(lin_dx(DT_F32, R, 696, 64, Wk.dd1, 64, f32w(M->w("dec1_w"), 696), Wk.ddecin, 696,
+                     DT_F32), s);
+    k_dec_in_bwd<<<cdiv((long)R * 696, TPB), TPB, 0, s>>>(t.d_cv, t.d_att, M->w("sel_type_emb").g,
+        M->w("ctx_emb").g, Wk.ddecin, obs, ol, R);
+    // ---- global encoder
+    colsum<float>(M->w("global2_b").g, Wk.dgd, 192, R, 128, s);
+    gemm_simt(lin_dw(DT_F32, R, 128, 128, Wk.dgd, 192, Wk.g1, 128, M->w("global2_w").g), s);
+    {
+        GemmArgs a = lin_dx(DT_F32, R, 128, 128, Wk.dgd, 192, f32w(M->w("global2_w"), 128), Wk.dg1,
+                            128, DT_F32);
+        a.act = ACT_GELU_BWD; a.aux = Wk.g1pre; a.ld_aux = 128; a.aux_dtype = DT_F32;
+        gemm_simt(a, s);
+    }
+    colsum<float>(M->w("global1_b").g, Wk.dg1, 128, R, 128, s);
+    gemm_simt(lin_dw(DT_F32, R, 64, 128, Wk.dg1, 128, obs + ol.glob, ol.obs, M->w("global1_w").g), s);
+    if (last) fire_hook(M, "zone_emb", "b0_ln1_w", s);
+    return 0;
+}
+
+// ================================================================= C-ABI
+extern "C" {
+
+const char* ptcg_last_error(void) { return g_err; }
+int ptcg_abi_version(void) { return PTCG_B200_ABI_VERSION; }
+
+static int check_shape(const PtcgShape* s) {
+    REQ(s, PTCG_EINVAL, "null shape");
+    REQ(s->d > 0 && s->heads > 0 && s->d % s->heads == 0 && s->d / s->heads == 32, PTCG_EINVAL,
+        "head width d/heads must be 32 (d=%d heads=%d)", s->d, s->heads);
+    REQ(s->d % 8 == 0 && s->ffn % 8 == 0 && s->ffn > 0 && s->layers >= 1, PTCG_EINVAL,
+        "d and ffn must be multiples of 8, layers >= 1");
+    REQ(s->ltok >= 1 && s->ltok <= 256 && s->nopt >= 1 && s->nopt <= 1024 && s->tok_f >= 0,
+        PTCG_EINVAL, "ltok must be in [1, 256], nopt in [1, 1024]");
+    REQ(s->n_cards >= 2 && s->n_attacks >= 1 && s->n_skills >= 1, PTCG_EINVAL, "bad vocab sizes");
+    return PTCG_OK;
+}
+
+static ObsLayout make_layout(const PtcgShape& s) {
+    ObsLayout L;
+    L.toki = 0;
+    L.tokf = L.toki + s.ltok * 5;
+    L.opti = L.tokf + s.ltok * s.tok_f;
+    L.optf = L.opti + s.nopt * 6;
+    L.mask = L.optf + s.nopt * 8;
+    L.glob = L.mask + s.nopt;
+    L.deci = L.glob + 64;
+    L.decf = L.deci + 8;
+    L.orc = L.decf + 16;
+    L.obs = L.orc + 136;
+    L.ltok = s.ltok; L.lseq = s.ltok + 1; L.nopt = s.nopt; L.tok_f = s.tok_f;
+    L.nc = s.n_cards; L.na = s.n_attacks; L.ns = s.n_skills;
+    return L;
+}
+
+long ptcg_obs_size(const PtcgShape* s) {
+    if (check_shape(s)) return -1;
+    return make_layout(*s).obs;
+}
+
+int ptcg_num_params(const PtcgShape* s) {
+    if (check_shape(s)) return -1;
+    return (int)param_defs(*s).size();
+}
+
+int ptcg_param_info(const PtcgShape* s, int i, const char** name, long* rows, long* cols) {
+    int e = check_shape(s);
+    if (e) return e;
+    static thread_local std::vector<ParamDef> defs;
+    defs = param_defs(*s);
+    REQ(i >= 0 && i < (int)defs.size(), PTCG_EINVAL, "param index %d out of range", i);
+    // names are stable string literals per (process, index): keep a copy
+    static std::unordered_map<std::string, std::string> interned;
+    auto it = interned.find(defs[i].name);
+    if (it == interned.end()) it = interned.emplace(defs[i].name, defs[i].name).first;
+    if (name) *name = it->second.c_str();
+    if (rows) *rows = defs[i].r;
+    if (cols) *cols = defs[i].c;
+    return PTCG_OK;
+}
+
+long ptcg_param_total(const PtcgShape* s) {
+    if (check_shape(s)) return -1;
+    long n = 0;
+    for (auto& p : param_defs(*s)) n += numel(p);
+    return n;
+}
+
+int ptcg_create(const PtcgShape* s, int precision, int device, PtcgModel** out) {
+    int e = check_shape(s);
+    if (e) return e;
+    REQ(out, PTCG_EINVAL, "null out");
+    REQ(precision == PTCG_FP32 || precision == PTCG_BF16, PTCG_EINVAL, "bad precision %d", precision);
+    int ndev = 0;
+    CK(cudaGetDeviceCount(&ndev));
+    REQ(device >= 0 && device < ndev, PTCG_EINVAL, "device %d not present (%d devices)", device, ndev);
+    CK(cudaSetDevice(device));
+    PtcgModel* M = new PtcgModel();
+    M->s = *s; M->prec = precision; M->dev = device;
+    Dims& z = M->z;
+    z.D = s->d; z.H = s->heads; z.FFN = s->ffn; z.LAYERS = s->layers; z.LTOK = s->ltok;
+    z.LSEQ = s->ltok + 1; z.NOPT = s->nopt; z.LCRIT = 1 + z.LSEQ + 56; z.NC = s->n_cards;
+    z.NA = s->n_attacks; z.NS = s->n_skills; z.TOKF = s->tok_f;
+    z.TOK_IN = 256 + s->tok_f + 12; z.Q_IN = 16 + 2 * s->d + 136; z.SCORE_IN = 3 * s->d + 192;
+    z.VAL_IN = s->d + 128;
+    z.ol = make_layout(*s);
+    M->defs = param_defs(*s);
+    long off = 0;
+    for (size_t i = 0; i < M->defs.size(); i++) {
+        M->idx[M->defs[i].name] = (int)i;
+        M->off.push_back(off);
+        off += rup(numel(M->defs[i]), 4);          // 16-byte aligned per tensor
+    }
+    M->n_arena = off;
+    size_t ab = (size_t)off * 4;
+    CK(cudaMalloc(&M->params, ab)); CK(cudaMalloc(&M->grads, ab));
+    CK(cudaMalloc(&M->am, ab)); CK(cudaMalloc(&M->av, ab));
+    CK(cudaMemset(M->params, 0, ab)); CK(cudaMemset(M->grads, 0, ab));
+    CK(cudaMemset(M->am, 0, ab)); CK(cudaMemset(M->av, 0, ab));
+    CK(cudaMalloc(&M->step_dev, sizeof(long long)));
+    CK(cudaMemset(M->step_dev, 0, sizeof(long long)));
+    // bf16 compute copies of the matrices that feed tensor-core GEMMs
+    M->copy_ld.assign(M->defs.size(), 0);
+    M->copy_ptr.assign(M->defs.size(), nullptr);
+    if (precision == PTCG_BF16) {
+        std::vector<int> which;
+        for (size_t i = 0; i < M->defs.size(); i++) {
+            const std::string& n = M->defs[i].name;
+            bool blockmat = (n.size() > 3 && (n[0] == 'b' || n[0] == 'c') && n[1] >= '0' && n[1] <= '9' &&
+                             (n.find("qkv_w") != std::string::npos || n.find("proj_w") != std::string::npos ||
+                              n.find("ffn1_w") != std::string::npos || n.find("ffn2_w") != std::string::npos));
+            if (blockmat || n == "token_proj_w" || n == "oracle_proj_w" || n == "aux_hand_w")
+                which.push_back((int)i);
+        }
+        long tot = 0;
+        for (int i : which) tot += M->defs[i].r * rup(M->defs[i].c, 8);
+        CK(cudaMalloc(&M->wbf, (size_t)tot * 2));
+        CK(cudaMemset(M->wbf, 0, (size_t)tot * 2));
+        long o = 0;
+        for (int i : which) {
+            long ld = rup(M->defs[i].c, 8);
+            BfCopy c;
+            c.off = M->off[i]; c.n = numel(M->defs[i]); c.cols = (int)M->defs[i].c; c.ldp = (int)ld;
+            c.dst = M->wbf + o;
+            M->copies.push_back(c);
+            M->copy_ld[i] = ld; M->copy_ptr[i] = M->wbf + o;
+            o += M->defs[i].r * ld;
+        }
+        CK(cudaMalloc(&M->d_copies, sizeof(BfCopy) * M->copies.size()));
+        CK(cudaMemcpy(M->d_copies, M->copies.data(), sizeof(BfCopy) * M->copies.size(),
+                      cudaMemcpyHostToDevice));
+        long nchunks = (M->n_arena + M->adam_chunk - 1) / M->adam_chunk;
+        std::vector<int> cc(nchunks);
+        size_t ci = 0;
+        for (long c = 0; c < nchunks; c++) {
+            long c0 = c * M->adam_chunk;
+            while (ci < M->copies.size() && c0 >= M->copies[ci].off + M->copies[ci].n) ci++;
+            cc[c] = (int)ci;
+        }
+        CK(cudaMalloc(&M->d_chunk_copy, sizeof(int) * nchunks));
+        CK(cudaMemcpy(M->d_chunk_copy, cc.data(), sizeof(int) * nchunks, cudaMemcpyHostToDevice));
+    }
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, device));
+    M->sumsq_grid = prop.multiProcessorCount * 4;
+    M->adam_grid = prop.multiProcessorCount * 8;
+    CK(cudaMalloc(&M->d_partials, sizeof(double) * M->sumsq_grid));
+    CK(cudaMalloc(&M->d_misc, sizeof(float) * 64));
+    CK(cudaMemset(M->d_misc, 0, sizeof(float) * 64));
+    CK(cudaMalloc(&M->d_ck, 16));
+    // table activations
+    Bump b{nullptr, 0, true};
+    plan_tab(M->tab, b, z);
+    CK(cudaMalloc(&M->tab_base, b.off));
+    CK(cudaMemset(M->tab_base, 0, b.off));
+    Bump b2{(char*)M->tab_base, 0, false};
+    plan_tab(M->tab, b2, z);
+    *out = M;
+    return PTCG_OK;
+}
+
+static void free_work(Work& w) { if (w.base) cudaFree(w.base); w = Work(); }
+
+int ptcg_destroy(PtcgModel* M) {
+    if (!M) return PTCG_OK;
+    cudaSetDevice(M->dev);
+    cudaDeviceSynchronize();
+    free_work(M->roll); free_work(M->trn);
+    void* ptrs[] = {M->params, M->grads, M->am, M->av, M->step_dev, M->wbf, M->d_copies,
+                    M->d_chunk_copy, M->d_partials, M->d_misc, M->d_ck, M->card_static,
+                    M->att_static, M->card_text, M->att_text, M->skill_text, M->card_attacks,
+                    M->card_skills, M->tab_base};
+    for (void* p : ptrs) if (p) cudaFree(p);
+    delete M;
+    return PTCG_OK;
+}
+
+int ptcg_set_tables(PtcgModel* M, const float* card_static, const int* card_attacks,
+                    const int* card_skills, const float* att_static, const float* card_text,
+                    const float* att_text, const float* skill_text) {
+    REQ(M && card_static && card_attacks && card_skills && att_static && card_text && att_text &&
+        skill_text, PTCG_EINVAL, "null table pointer");
+    CK(cudaSetDevice(M->dev));
+    const Dims& z = M->z;
+    for (int k = 0; k < (long)z.NC * 4; k++)
+        REQ(card_attacks[k] >= 0 && card_attacks[k] < z.NA, PTCG_EINVAL,
+            "card_attacks[%d]=%d outside [0, %d)", k, card_attacks[k], z.NA);
+    for (int k = 0; k < (long)z.NC * 2; k++)
+        REQ(card_skills[k] >= 0 && card_skills[k] < z.NS, PTCG_EINVAL,
+            "card_skills[%d]=%d outside [0, %d)", k, card_skills[k], z.NS);
+#define UP(dst, src, n, T) do { if (!M->dst) CK(cudaMalloc(&M->dst, (size_t)(n) * sizeof(T))); \
+    CK(cudaMemcpy(M->dst, src, (size_t)(n) * sizeof(T), cudaMemcpyHostToDevice)); } while (0)
+    UP(card_static, card_static, (long)z.NC * 58, float);
+    UP(card_attacks, card_attacks, (long)z.NC * 4, int);
+    UP(card_skills, card_skills, (long)z.NC * 2, int);
+    UP(att_static, att_static, (long)z.NA * 15, float);
+    UP(card_text, card_text, (long)z.NC * 128, float);
+    UP(att_text, att_text, (long)z.NA * 64, float);
+    UP(skill_text, skill_text, (long)z.NS * 64, float);
+#undef UP
+    M->tables_ready = true;
+    return PTCG_OK;
+}
+
+static int refresh_copies(PtcgModel* M, cudaStream_t s) {
+    if (M->copies.empty()) return PTCG_OK;
+    dim3 g(64, (unsigned)M->copies.size());
+    k_refresh_copies<<<g, 256, 0, s>>>(M->params, M->d_copies, (int)M->copies.size());
+    CKL();
+    return PTCG_OK;
+}
+
+int ptcg_load_weights(PtcgModel* M, const float* packed, long n) {
+    REQ(M && packed, PTCG_EINVAL, "null argument");
+    long tot = 0;
+    for (auto& p : M->defs) tot += numel(p);
+    REQ(n == tot, PTCG_EINVAL, "blob has %ld floats, expected %ld", n, tot);
+    CK(cudaSetDevice(M->dev));
+    long o = 0;
+    for (size_t i = 0; i < M->defs.size(); i++) {
+        long k = numel(M->defs[i]);
+        CK(cudaMemcpy(M->params + M->off[i], packed + o, k * 4, cudaMemcpyHostToDevice));
+        o += k;
+    }
+    int e = refresh_copies(M, 0);
+    if (e) return e;
+    CK(cudaDeviceSynchronize());
+    M->weights_ready = true;
+    return PTCG_OK;
+}
+
+int ptcg_save_weights(PtcgModel* M, float* packed, long n) {
+    REQ(M && packed, PTCG_EINVAL, "null argument");
+    long tot = 0;
+    for (auto& p : M->defs) tot += numel(p);
+    REQ(n == tot, PTCG_EINVAL, "buffer has %ld floats, expected %ld", n, tot);
+    CK(cudaSetDevice(M->dev));
+    CK(cudaDeviceSynchronize());
+    long o = 0;
+    for (size_t i = 0; i < M->defs.size(); i++) {
+        long k = numel(M->defs[i]);
+        CK(cudaMemcpy(packed + o, M->params + M->off[i], k * 4, cudaMemcpyDeviceToHost));
+        o += k;
+    }
+    return PTCG_OK;
+}
+
+static int reserve_one(PtcgModel* M, Work& W, int rows, bool train) {
+    if (rows <= 0) { free_work(W); return PTCG_OK; }
+    if (W.base && W.R == rows) return PTCG_OK;
+    free_work(W);
+    Bump b{nullptr, 0, true};
+    plan_work(W, b, rows, train, M->z, M->esz(), M->prec == PTCG_BF16);
+    size_t bytes = b.off;
+    void* base = nullptr;
+    cudaError_t e = cudaMalloc(&base, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_err("reserve: cannot allocate %.2f GB for %d %s rows: %s", bytes / 1e9, rows,
+                train ? "train" : "rollout", cudaGetErrorString(e));
+        return PTCG_ECUDA;
+    }
+    CK(cudaMemset(base, 0, bytes));
+    Bump b2{(char*)base, 0, false};
+    plan_work(W, b2, rows, train, M->z, M->esz(), M->prec == PTCG_BF16);
+    W.base = base; W.bytes = bytes;
+    return PTCG_OK;
+}
+
+int ptcg_reserve(PtcgModel* M, int rollout_rows, int train_rows) {
+    REQ(M && rollout_rows >= 0 && train_rows >= 0, PTCG_EINVAL, "bad arguments");
+    CK(cudaSetDevice(M->dev));
+    int e = reserve_one(M, M->roll, rollout_rows, false);
+    if (e) return e;
+    return reserve_one(M, M->trn, train_rows, true);
+}
+
+static int ready(PtcgModel* M) {
+    REQ(M, PTCG_EINVAL, "null model");
+    REQ(M->tables_ready, PTCG_ESTATE, "static tables not set (ptcg_set_tables)");
+    REQ(M->weights_ready, PTCG_ESTATE, "weights not loaded (ptcg_load_weights)");
+    return PTCG_OK;
+}
+
+int ptcg_forward(PtcgModel* M, const float* obs, int n, float* out, void* stream) {
+    int e = ready(M);
+    if (e) return e;
+    REQ(obs && out && n >= 0, PTCG_EINVAL, "bad arguments");
+    REQ(M->roll.base && n <= M->roll.R, PTCG_ERANGE, "rollout batch %d exceeds reserved %d", n,
+        M->roll.R);
+    if (n == 0) return PTCG_OK;
+    CK(cudaSetDevice(M->dev));
+    forward_impl(M, M->roll, obs, n, out, false, true, (cudaStream_t)stream);
+    CKL();
+    return PTCG_OK;
+}
+
+int ptcg_forward_train(PtcgModel* M, const float* obs, int n, float* out, void* stream) {
+    int e = ready(M);
+    if (e) return e;
+    REQ(obs && out && n > 0, PTCG_EINVAL, "bad arguments");
+    REQ(M->trn.base && n <= M->trn.R, PTCG_ERANGE, "train batch %d exceeds reserved %d", n, M->trn.R);
+    CK(cudaSetDevice(M->dev));
+    forward_impl(M, M->trn, obs, n, out, true, true, (cudaStream_t)stream);
+    M->trn_last_obs = obs; M->trn_last_n = n;
+    CKL();
+    return PTCG_OK;
+}
+
+
+int ptcg_backward(PtcgModel* M, const float* grad, const float* returns, int aux_norm_rows,
+                  float prize_count, int accumulate, void* stream) {
+    int e = ready(M);
+    if (e) return e;
+    REQ(grad && returns, PTCG_EINVAL, "null argument");
+    REQ(M->trn_last_obs && M->trn_last_n > 0, PTCG_ESTATE,
+        "ptcg_backward needs a preceding ptcg_forward_train");
+    CK(cudaSetDevice(M->dev));
+    cudaStream_t s = (cudaStream_t)stream;
+    int R = M->trn_last_n;
+    int norm = aux_norm_rows > 0 ? aux_norm_rows : R;
+    float* cnt = M->d_misc + 2;
+    float* aux = M->d_misc + 16;
+    CK(cudaMemsetAsync(aux, 0, 3 * sizeof(float), s));
+    if (prize_count <= 0.f) {
+        CK(cudaMemsetAsync(cnt, 0, sizeof(float), s));
+        k_count_unseen<<<64, 256, 0, s>>>(cnt, M->trn_last_obs, M->z.ol, R);
+    }
+    if (!accumulate) CK(cudaMemsetAsync(M->grads, 0, (size_t)M->n_arena * 4, s));
+    zero_table_grads(M, s);
+    backward_impl(M, M->trn, M->trn_last_obs, grad, returns, R, norm,
+                  prize_count > 0.f ? nullptr : cnt, prize_count, aux, true, s);
+    tables_bwd(M, s);
+    if (M->hook) fire_hook(M, "card_id_emb", "zone_emb", s);
+    CKL();
+    return PTCG_OK;
+}
+
+int ptcg_ppo_loss(const float* dec_out, int nopt, const float* mask, const float* actions,
+                  const float* old_logp, const float* advantages, const float* values,
+                  const float* returns, const float* prio, int n_seg, int horizon,
+                  float clip_coef, float vf_clip_coef, float vf_coef, float ent_coef,
+                  float* grad_dec, float* new_logp, float* ratio, float* stats, float* scratch,
+                  void* stream) {
+    REQ(dec_out && mask && actions && old_logp && advantages && values && returns && prio &&
+        grad_dec && new_logp && ratio && stats && scratch, PTCG_EINVAL, "null argument");
+    REQ(n_seg > 0 && horizon > 0 && nopt > 0, PTCG_EINVAL, "bad sizes");
+    cudaStream_t s = (cudaStream_t)stream;
+    int nt = n_seg * horizon;
+    float* adv_stats = scratch;
+    float* partials = scratch + 16;
+    k_adv_stats<<<1, 1024, 0, s>>>(adv_stats, advantages, nt);
+    unsigned g = cdiv(nt, PPO_ROWS_PER_BLOCK);
+    k_ppo_loss<<<g, PPO_ROWS_PER_BLOCK * 32, 0, s>>>(dec_out, nopt, mask, nopt, actions, old_logp,
+        advantages, values, returns, prio, horizon, 0, nt, nt, adv_stats, clip_coef, vf_clip_coef,
+        vf_coef, ent_coef, grad_dec, new_logp, ratio, partials);
+    k_ppo_reduce<<<1, 32, 0, s>>>(stats, partials, (int)g, adv_stats, 0);
+    CKL();
+    return PTCG_OK;
+}
+
+static int adam_impl(PtcgModel* M, float lr, float b1, float b2, float eps, float max_norm,
+                     const float* gate, float* stats, cudaStream_t s) {
+    float* st = stats ? stats : M->d_misc + 32;
+    k_sumsq<<<M->sumsq_grid, 256, 0, s>>>(M->d_partials, M->grads, M->n_arena);
+    k_adam<<<M->adam_grid, 256, 0, s>>>(M->params, M->am, M->av, M->grads, M->n_arena,
+        M->d_partials, M->sumsq_grid, lr, b1, b2, eps, max_norm, M->step_dev, gate, st,
+        M->d_copies, (int)M->copies.size(), M->d_chunk_copy, M->adam_chunk);
+    k_step_inc<<<1, 1, 0, s>>>(M->step_dev, st);
+    CKL();
+    return PTCG_OK;
+}
+
+int ptcg_adam_step(PtcgModel* M, float lr, float beta1, float beta2, float eps, float max_norm,
+                   const float* gate, float* stats, void* stream) {
+    int e = ready(M);
+    if (e) return e;
+    CK(cudaSetDevice(M->dev));
+    return adam_impl(M, lr, beta1, beta2, eps, max_norm, gate, stats, (cudaStream_t)stream);
+}
+
+int ptcg_sample_logits(const float* dec_out, int n, int nopt, const float* mask, long mask_stride,
+                       const float* uniforms, float* actions, float* logprobs, float* values,
+                       void* stream) {
+    REQ(dec_out && mask && uniforms && actions && logprobs && values, PTCG_EINVAL, "null argument");
+    REQ(n >= 0 && nopt > 0 && mask_stride >= nopt, PTCG_EINVAL, "bad sizes");
+    if (n == 0) return PTCG_OK;
+    k_sample<<<cdiv(n, 8), 256, 0, (cudaStream_t)stream>>>(dec_out, n, nopt, mask, mask_stride,
+        uniforms, actions, logprobs, values);
+    CKL();
+    return PTCG_OK;
+}
+
+int ptcg_puff_advantage(const float* values, const float* rewards, const float* dones,
+                        const float* importance, const float* obs, long obs_size, int seat_col,
+                        int B, int T, float gamma, float lambda, float rho_clip, float c_clip,
+                        float* advantages, void* stream) {
+    REQ(values && rewards && dones && importance && obs && advantages, PTCG_EINVAL, "null argument");
+    REQ(B > 0 && T > 0 && seat_col >= 0 && seat_col < obs_size, PTCG_EINVAL, "bad sizes");
+    k_negamax_adv<<<cdiv(B, 128), 128, 0, (cudaStream_t)stream>>>(values, rewards, dones,
+        importance, obs, obs_size, seat_col, advantages, gamma, lambda, rho_clip, c_clip, B, T);
+    CKL();
+    return PTCG_OK;
+}
+
+int ptcg_set_grad_hook(PtcgModel* M, ptcg_grad_hook fn, void* user) {
+    REQ(M, PTCG_EINVAL, "null model");
+    M->hook = fn; M->hook_user = user;
+    return PTCG_OK;
+}
+
+int ptcg_train_step(PtcgModel* M, const float* obs, const float* actions, const float* old_logp,
+                    const float* advantages, const float* values, const float* returns,
+                    const float* prio, int n_seg, int horizon, float clip_coef,
+                    float vf_clip_coef, float vf_coef, float ent_coef, float lr, float beta1,
+                    float beta2, float eps, float max_norm, int skip_adam, float* stats,
+                    void* stream) {
+    int e = ready(M);
+    if (e) return e;
+    REQ(obs && actions && old_logp && advantages && values && returns && prio && stats,
+        PTCG_EINVAL, "null argument");
+    REQ(n_seg > 0 && horizon > 0, PTCG_EINVAL, "bad sizes");
+    REQ(M->trn.base, PTCG_ESTATE, "no train workspace (ptcg_reserve)");
+    CK(cudaSetDevice(M->dev));
+    cudaStream_t s = (cudaStream_t)stream;
+    const Dims& z = M->z;
+    Work& Wk = M->trn;
+    const int nt = n_seg * horizon, R = Wk.R;
+    float* adv_stats = M->d_misc;
+    float* cnt = M->d_misc + 2;
+    CK(cudaMemsetAsync(stats, 0, 16 * sizeof(float), s));
+    CK(cudaMemsetAsync(cnt, 0, sizeof(float), s));
+    k_adv_stats<<<1, 1024, 0, s>>>(adv_stats, advantages, nt);
+    k_count_unseen<<<128, 256, 0, s>>>(cnt, obs, z.ol, nt);
+    CK(cudaMemsetAsync(M->grads, 0, (size_t)M->n_arena * 4, s));
+    zero_table_grads(M, s);
+    tables_fwd(M, s);
+    int nmb = (nt + R - 1) / R;
+    for (int mb = 0; mb < nmb; mb++) {
+        int r0 = mb * R, rows = nt - r0 < R ? nt - r0 : R;
+        const float* ob = obs + (long)r0 * z.ol.obs;
+        forward_impl(M, Wk, ob, rows, Wk.fused, true, false, s);
+        unsigned g = cdiv(rows, PPO_ROWS_PER_BLOCK);
+        k_ppo_loss<<<g, PPO_ROWS_PER_BLOCK * 32, 0, s>>>(Wk.fused, z.NOPT, ob + z.ol.mask, z.ol.obs,
+            actions + r0, old_logp + r0, advantages + r0, values + r0, returns + r0, prio, horizon,
+            r0, rows, nt, adv_stats, clip_coef, vf_clip_coef, vf_coef, ent_coef, Wk.dgrad, Wk.nlp,
+            Wk.ratio, Wk.ppo_scratch);
+        k_ppo_reduce<<<1, 32, 0, s>>>(stats, Wk.ppo_scratch, (int)g, adv_stats, 1);
+        backward_impl(M, Wk, ob, Wk.dgrad, returns + r0, rows, nt, cnt, 0.f, stats + 10,
+                      mb == nmb - 1, s);
+    }
+    tables_bwd(M, s);
+    if (M->hook) fire_hook(M, "card_id_emb", "zone_emb", s);
+    if (!skip_adam) {
+        e = adam_impl(M, lr, beta1, beta2, eps, max_norm, nullptr, stats + 8, s);
+        if (e) return e;
+    }
+    CKL();
+    return PTCG_OK;
+}
+
+int ptcg_arena(PtcgModel* M, int which, float** ptr, long* n_floats) {
+    REQ(M && ptr && n_floats, PTCG_EINVAL, "null argument");
+    float* p[] = {M->params, M->grads, M->am, M->av};
+    REQ(which >= 0 && which < 4, PTCG_EINVAL, "bad arena %d", which);
+    *ptr = p[which];
+    *n_floats = M->n_arena;
+    return PTCG_OK;
+}
+
+long ptcg_param_offset(PtcgModel* M, int i) {
+    if (!M || i < 0 || i >= (int)M->defs.size()) return -1;
+    return M->off[i];
+}
+
+int ptcg_get_step(PtcgModel* M, long* step) {
+    REQ(M && step, PTCG_EINVAL, "null argument");
+    CK(cudaSetDevice(M->dev));
+    long long v = 0;
+    CK(cudaMemcpy(&v, M->step_dev, sizeof v, cudaMemcpyDeviceToHost));
+    *step = (long)v;
+    return PTCG_OK;
+}
+
+int ptcg_set_step(PtcgModel* M, long step) {
+    REQ(M && step >= 0, PTCG_EINVAL, "bad arguments");
+    CK(cudaSetDevice(M->dev));
+    long long v = step;
+    CK(cudaMemcpy(M->step_dev, &v, sizeof v, cudaMemcpyHostToDevice));
+    return PTCG_OK;
+}
+
+int ptcg_weights_checksum(PtcgModel* M, unsigned int* out_dev, void* stream) {
+    REQ(M && out_dev, PTCG_EINVAL, "null argument");
+    cudaStream_t s = (cudaStream_t)stream;
+    CK(cudaMemsetAsync(out_dev, 0, 8, s));
+    k_checksum<<<256, 256, 0, s>>>(out_dev, M->params, M->n_arena);
+    CKL();
+    return PTCG_OK;
+}
+
+}  // extern "C"

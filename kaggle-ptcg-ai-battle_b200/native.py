@@ -1,0 +1,104 @@
+"""ctypes binding of libptcg_b200.so (the C-ABI of include/ptcg_b200.h).
+
+`lib()` loads the in-tree library and raises if it is missing -- there is no
+CPU fallback for any computing entry point.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libptcg_b200.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "ptcg_b200.h")
+
+P = C.c_void_p
+F = C.c_float
+I = C.c_int
+L = C.c_long
+FP = C.POINTER(C.c_float)
+
+
+class PtcgShape(C.Structure):
+    _fields_ = [(n, C.c_int) for n in (
+        "d", "heads", "ffn", "layers", "ltok", "nopt", "tok_f",
+        "n_cards", "n_attacks", "n_skills")]
+
+    @classmethod
+    def from_shape(cls, s):
+        return cls(s.d, s.heads, s.ffn, s.layers, s.ltok, s.nopt, s.tok_f,
+                   s.n_cards, s.n_attacks, s.n_skills)
+
+
+GRAD_HOOK = C.CFUNCTYPE(None, C.c_void_p, C.c_long, C.c_long, C.c_void_p)
+
+_SIGS = {
+    "ptcg_last_error": (C.c_char_p, []),
+    "ptcg_abi_version": (I, []),
+    "ptcg_obs_size": (L, [C.POINTER(PtcgShape)]),
+    "ptcg_num_params": (I, [C.POINTER(PtcgShape)]),
+    "ptcg_param_info": (I, [C.POINTER(PtcgShape), I, C.POINTER(C.c_char_p),
+                            C.POINTER(C.c_long), C.POINTER(C.c_long)]),
+    "ptcg_param_total": (L, [C.POINTER(PtcgShape)]),
+    "ptcg_create": (I, [C.POINTER(PtcgShape), I, I, C.POINTER(P)]),
+    "ptcg_destroy": (I, [P]),
+    "ptcg_set_tables": (I, [P, P, P, P, P, P, P, P]),
+    "ptcg_load_weights": (I, [P, P, L]),
+    "ptcg_save_weights": (I, [P, P, L]),
+    "ptcg_reserve": (I, [P, I, I]),
+    "ptcg_forward": (I, [P, P, I, P, P]),
+    "ptcg_forward_train": (I, [P, P, I, P, P]),
+    "ptcg_backward": (I, [P, P, P, I, F, I, P]),
+    "ptcg_ppo_loss": (I, [P, I, P, P, P, P, P, P, P, I, I, F, F, F, F,
+                          P, P, P, P, P, P]),
+    "ptcg_adam_step": (I, [P, F, F, F, F, F, P, P, P]),
+    "ptcg_sample_logits": (I, [P, I, I, P, L, P, P, P, P, P]),
+    "ptcg_puff_advantage": (I, [P, P, P, P, P, L, I, I, I, F, F, F, F, P, P]),
+    "ptcg_set_grad_hook": (I, [P, GRAD_HOOK, P]),
+    "ptcg_train_step": (I, [P, P, P, P, P, P, P, P, I, I, F, F, F, F, F, F, F,
+                            F, F, I, P, P]),
+    "ptcg_arena": (I, [P, I, C.POINTER(FP), C.POINTER(C.c_long)]),
+    "ptcg_param_offset": (L, [P, I]),
+    "ptcg_get_step": (I, [P, C.POINTER(C.c_long)]),
+    "ptcg_set_step": (I, [P, L]),
+    "ptcg_weights_checksum": (I, [P, P, P]),
+}
+
+_lib = None
+
+
+class PtcgError(RuntimeError):
+    pass
+
+
+def header_symbols():
+    """Function names declared in include/ptcg_b200.h."""
+    txt = open(HEADER).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(ptcg_[a-z_0-9]+)\s*\(", txt)))
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise PtcgError(f"{LIB_PATH} is missing: build it with "
+                        "`python __graft_entry__.py build` (nvcc, sm_100a)")
+    h = C.CDLL(LIB_PATH)
+    for name, (res, args) in _SIGS.items():
+        fn = getattr(h, name)
+        fn.restype = res
+        fn.argtypes = args
+    missing = [s for s in header_symbols() if not hasattr(h, s)]
+    if missing:
+        raise PtcgError(f"libptcg_b200.so lacks declared symbols: {missing}")
+    _lib = h
+    return h
+
+
+def check(rc):
+    if rc != 0:
+        raise PtcgError(f"ptcg error {rc}: {lib().ptcg_last_error().decode()}")
+    return rc

@@ -1,0 +1,245 @@
+"""Python-side mirror of the reference's policy plug-in for this path.
+
+`PTCGPolicy` plays the role that the ptcg Encoder/Decoder/Network vtables
+(native/src/ocean.cu:5-46, native/model/ptcg_model4.cu:236-354) and the
+trainer hooks around them (ppo_loss_fwd_bwd / muon_step / sample_logits /
+ptcg_puff_advantage, native/src/pufferlib.cu) play for the reference, with
+the torch-facing conveniences of ptcg/rl/model.py (forward_eval /
+forward_policy / forward_train).  Device memory and streams are torch's; all
+computation goes through the CUDA C-ABI (native.py); errors raise
+`PtcgError` (the reference aborts / throws std::runtime_error).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import native
+from .config import Shape, param_count, param_table
+from .native import check
+
+PRECISIONS = {"fp32": 0, "bf16": 1}
+
+
+class _CudaArray:
+    def __init__(self, ptr, n, dtype="<f4"):
+        self.__cuda_array_interface__ = {
+            "shape": (n,), "typestr": dtype, "data": (ptr, False), "version": 3,
+            "strides": None}
+
+
+def _p(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream():
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _f32(t, device):
+    if isinstance(t, np.ndarray):
+        t = torch.from_numpy(np.ascontiguousarray(t, np.float32))
+    return t.to(device=device, dtype=torch.float32).contiguous()
+
+
+class PTCGPolicy:
+    def __init__(self, shape: Shape, precision="bf16", device=0, tables=None,
+                 weights=None, rollout_rows=0, train_rows=0):
+        self.lib = native.lib()
+        self.shape = shape
+        self.precision = precision
+        self.device = torch.device("cuda", device)
+        self._cs = native.PtcgShape.from_shape(shape)
+        h = C.c_void_p()
+        check(self.lib.ptcg_create(C.byref(self._cs), PRECISIONS[precision], device,
+                                   C.byref(h)))
+        self.h = h
+        self.obs_size = self.lib.ptcg_obs_size(C.byref(self._cs))
+        assert self.obs_size == shape.obs_size
+        self.n_params = param_count(shape)
+        self._hook_ref = None
+        if tables is not None:
+            self.set_tables(tables)
+        if weights is not None:
+            self.load_weights(weights)
+        if rollout_rows or train_rows:
+            self.reserve(rollout_rows, train_rows)
+
+    # ---------------------------------------------------------------- setup
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.ptcg_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_tables(self, t):
+        arrs = [np.ascontiguousarray(t["card_static"], np.float32),
+                np.ascontiguousarray(t["card_attacks"], np.int32),
+                np.ascontiguousarray(t["card_skills"], np.int32),
+                np.ascontiguousarray(t["att_static"], np.float32),
+                np.ascontiguousarray(t["card_text"], np.float32),
+                np.ascontiguousarray(t["att_text"], np.float32),
+                np.ascontiguousarray(t["skill_text"], np.float32)]
+        check(self.lib.ptcg_set_tables(self.h, *[a.ctypes.data_as(C.c_void_p) for a in arrs]))
+
+    def load_weights(self, blob):
+        b = np.ascontiguousarray(blob, np.float32)
+        check(self.lib.ptcg_load_weights(self.h, b.ctypes.data_as(C.c_void_p), b.size))
+
+    def save_weights(self):
+        b = np.empty(self.n_params, np.float32)
+        check(self.lib.ptcg_save_weights(self.h, b.ctypes.data_as(C.c_void_p), b.size))
+        return b
+
+    def reserve(self, rollout_rows, train_rows):
+        check(self.lib.ptcg_reserve(self.h, int(rollout_rows), int(train_rows)))
+        self.rollout_rows, self.train_rows = rollout_rows, train_rows
+
+    def arena(self, which):
+        """torch view of an arena: 0 params, 1 grads, 2 Adam m, 3 Adam v."""
+        p = C.POINTER(C.c_float)()
+        n = C.c_long()
+        check(self.lib.ptcg_arena(self.h, which, C.byref(p), C.byref(n)))
+        ptr = C.cast(p, C.c_void_p).value
+        return torch.as_tensor(_CudaArray(ptr, n.value), device=self.device)
+
+    def param_offsets(self):
+        return [self.lib.ptcg_param_offset(self.h, i) for i in range(len(param_table(self.shape)))]
+
+    def grads_packed(self):
+        """fp32 grads in packed PT_PARAMS order (numpy)."""
+        g = self.arena(1).cpu().numpy()
+        out = []
+        for (name, shp), off in zip(param_table(self.shape), self.param_offsets()):
+            n = int(np.prod(shp))
+            out.append(g[off:off + n])
+        return np.concatenate(out)
+
+    @property
+    def step(self):
+        v = C.c_long()
+        check(self.lib.ptcg_get_step(self.h, C.byref(v)))
+        return v.value
+
+    @step.setter
+    def step(self, v):
+        check(self.lib.ptcg_set_step(self.h, int(v)))
+
+    # -------------------------------------------------------- encoder slots
+    def forward(self, obs):
+        """Rollout forward -> (N, nopt+1) = [raw scores | oracle value]."""
+        obs = _f32(obs, self.device)
+        out = torch.empty(obs.shape[0], self.shape.nopt + 1, device=self.device)
+        check(self.lib.ptcg_forward(self.h, _p(obs), obs.shape[0], _p(out), _stream()))
+        return out
+
+    def forward_eval(self, obs):
+        """(masked logits (-1e9 on illegal slots), oracle value) like
+        PTCGTransformer.forward_eval (ptcg/rl/model.py:315-321)."""
+        obs = _f32(obs, self.device)
+        out = self.forward(obs)
+        a, b = self.shape.offsets["opt_mask"]
+        logits = out[:, :-1].masked_fill(obs[:, a:b] == 0, -1e9)
+        return logits, out[:, -1]
+
+    def forward_policy(self, obs):
+        return self.forward_eval(obs)[0]
+
+    def forward_train(self, obs):
+        obs = _f32(obs, self.device)
+        self._train_obs = obs            # keep alive for backward
+        out = torch.empty(obs.shape[0], self.shape.nopt + 1, device=self.device)
+        check(self.lib.ptcg_forward_train(self.h, _p(obs), obs.shape[0], _p(out), _stream()))
+        return out
+
+    def backward(self, grad, returns, aux_norm_rows=0, prize_count=0.0, accumulate=False):
+        grad = _f32(grad, self.device)
+        returns = _f32(returns, self.device)
+        check(self.lib.ptcg_backward(self.h, _p(grad), _p(returns), int(aux_norm_rows),
+                                     float(prize_count), int(accumulate), _stream()))
+
+    # -------------------------------------------------------- trainer hooks
+    def ppo_loss(self, dec_out, mask, actions, old_logp, advantages, values, returns,
+                 prio, n_seg, horizon, clip=0.2, vf_clip=0.2, vf_coef=0.5, ent_coef=0.01):
+        d = self.device
+        dec_out, mask = _f32(dec_out, d), _f32(mask, d)
+        args = [_f32(x, d) for x in (actions, old_logp, advantages, values, returns, prio)]
+        nt = n_seg * horizon
+        grad = torch.empty_like(dec_out)
+        nlp = torch.empty(nt, device=d)
+        ratio = torch.empty(nt, device=d)
+        stats = torch.zeros(8, device=d)
+        scratch = torch.empty(16 + 7 * ((nt + 7) // 8), device=d)
+        check(self.lib.ptcg_ppo_loss(_p(dec_out), self.shape.nopt, _p(mask),
+                                     *[_p(a) for a in args], n_seg, horizon, clip, vf_clip,
+                                     vf_coef, ent_coef, _p(grad), _p(nlp), _p(ratio),
+                                     _p(stats), _p(scratch), _stream()))
+        return grad, nlp, ratio, stats
+
+    def adam_step(self, lr=3e-4, betas=(0.9, 0.999), eps=1e-8, max_norm=1.0, gate=None):
+        stats = torch.zeros(2, device=self.device)
+        check(self.lib.ptcg_adam_step(self.h, lr, betas[0], betas[1], eps, max_norm,
+                                      _p(gate), _p(stats), _stream()))
+        return stats
+
+    def sample(self, dec_out, mask, uniforms):
+        d = self.device
+        dec_out, mask, uniforms = _f32(dec_out, d), _f32(mask, d), _f32(uniforms, d)
+        n = dec_out.shape[0]
+        act = torch.empty(n, device=d)
+        logp = torch.empty(n, device=d)
+        val = torch.empty(n, device=d)
+        check(self.lib.ptcg_sample_logits(_p(dec_out), n, self.shape.nopt, _p(mask),
+                                          mask.stride(0), _p(uniforms), _p(act), _p(logp),
+                                          _p(val), _stream()))
+        return act, logp, val
+
+    def advantage(self, values, rewards, dones, importance, obs, gamma=0.99, lam=0.95,
+                  rho_clip=1.0, c_clip=1.0):
+        d = self.device
+        values, rewards, dones, importance = [_f32(x, d) for x in (values, rewards, dones, importance)]
+        obs = _f32(obs, d)
+        B, T = values.shape
+        adv = torch.zeros(B, T, device=d)
+        check(self.lib.ptcg_puff_advantage(_p(values), _p(rewards), _p(dones), _p(importance),
+                                           _p(obs), self.obs_size, self.shape.seat_col, B, T,
+                                           gamma, lam, rho_clip, c_clip, _p(adv), _stream()))
+        return adv
+
+    def set_grad_hook(self, fn):
+        """fn(offset, count, stream_ptr) called when arena floats
+        [offset, offset+count) hold final grads (last micro-batch)."""
+        if fn is None:
+            self._hook_ref = None
+            check(self.lib.ptcg_set_grad_hook(self.h, native.GRAD_HOOK(), None))
+            return
+        cb = native.GRAD_HOOK(lambda user, off, cnt, stream: fn(off, cnt, stream))
+        self._hook_ref = cb
+        check(self.lib.ptcg_set_grad_hook(self.h, cb, None))
+
+    def train_step(self, obs, actions, old_logp, advantages, values, returns, prio,
+                   n_seg, horizon, clip=0.2, vf_clip=0.2, vf_coef=0.5, ent_coef=0.01,
+                   lr=3e-4, betas=(0.9, 0.999), eps=1e-8, max_norm=1.0, skip_adam=False,
+                   stats=None):
+        d = self.device
+        obs = _f32(obs, d)
+        args = [_f32(x, d) for x in (actions, old_logp, advantages, values, returns, prio)]
+        if stats is None:
+            stats = torch.zeros(16, device=d)
+        check(self.lib.ptcg_train_step(self.h, _p(obs), *[_p(a) for a in args], n_seg,
+                                       horizon, clip, vf_clip, vf_coef, ent_coef, lr, betas[0],
+                                       betas[1], eps, max_norm, int(skip_adam), _p(stats),
+                                       _stream()))
+        return stats
+
+    def weights_checksum(self):
+        out = torch.zeros(4, dtype=torch.int32, device=self.device)
+        check(self.lib.ptcg_weights_checksum(self.h, _p(out), _stream()))
+        return out[:2]

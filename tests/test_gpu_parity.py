@@ -1,0 +1,219 @@
+"""GPU parity of the CUDA path against the CPU oracle (through the C-ABI).
+
+Tolerances: fp32 mode <= 1e-4 relative on scores /
+values / gradients, bf16 mode <= 2e-2 relative; masking and indexing exact.
+Relative error = ||a - b||_2 / ||b||_2 over the compared entries.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"fp32": 1e-4, "bf16": 2e-2}
+ROWS = {"tiny": 9, "small": 12, "c0": 6, "default": 4, "c4": 2}
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64).ravel(); b = np.asarray(b, np.float64).ravel()
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def make(pkg, preset, prec, n, seed=3, edge=True):
+    s = pkg.config.PRESETS[preset]
+    tabs = pkg.synth.make_tables(s, 11)
+    blob = pkg.synth.make_weights(s, 21)
+    obs = pkg.synth.make_obs(s, n, seed, edge=edge)
+    pol = pkg.PTCGPolicy(s, precision=prec, tables=tabs, weights=blob,
+                         rollout_rows=n, train_rows=n)
+    return s, tabs, blob, obs, pol
+
+
+def oracle_fwd(oracle, s, tabs, blob, obs):
+    P = oracle.params_from_blob(blob, s)
+    T = oracle.tables_to_torch(tabs)
+    with torch.no_grad():
+        sc, lg, v = oracle.forward_eval(P, T, torch.from_numpy(obs), s)
+    return sc.numpy(), v.numpy()
+
+
+@pytest.mark.parametrize("prec", ["fp32", "bf16"])
+@pytest.mark.parametrize("preset", ["tiny", "small", "c0", "default", "c4"])
+def test_forward_parity(pkg, oracle, preset, prec):
+    torch.set_float32_matmul_precision("highest")
+    n = ROWS[preset]
+    s, tabs, blob, obs, pol = make(pkg, preset, prec, n)
+    out = pol.forward(obs).cpu().numpy()
+    sc, v = oracle_fwd(oracle, s, tabs, blob, obs)
+    a, b = s.offsets["opt_mask"]
+    legal = obs[:, a:b] != 0
+    assert np.isfinite(out).all()
+    assert rel(out[:, :-1][legal], sc[legal]) <= TOL[prec], rel(out[:, :-1][legal], sc[legal])
+    assert rel(out[:, -1], v) <= TOL[prec], rel(out[:, -1], v)
+    # forward_eval masks exactly the illegal slots with -1e9
+    lg, val = pol.forward_eval(obs)
+    lg = lg.cpu().numpy()
+    assert np.array_equal(lg <= -1e8, ~legal)
+    # rollout path == train path forward
+    ft = pol.forward_train(obs).cpu().numpy()
+    np.testing.assert_allclose(ft, out, rtol=0, atol=1e-6 if prec == "fp32" else 1e-3)
+
+
+def _rollout_tensors(pkg, oracle, s, obs, scores, seed):
+    n = obs.shape[0]
+    a, b = s.offsets["opt_mask"]
+    mask = obs[:, a:b]
+    rng = np.random.default_rng(seed)
+    u = rng.random(n)
+    act, logp, _ = oracle.sample_logits(scores, mask, u)
+    old = logp + rng.normal(0, 0.3, n).astype(np.float32)   # ratios away from 1
+    adv = rng.standard_normal(n).astype(np.float32)
+    ret = rng.standard_normal(n).astype(np.float32)
+    val = rng.standard_normal(n).astype(np.float32) * 0.1
+    return mask, act.astype(np.float32), old.astype(np.float32), adv, ret, val
+
+
+@pytest.mark.parametrize("prec", ["fp32", "bf16"])
+@pytest.mark.parametrize("preset", ["tiny", "small", "c0", "default"])
+def test_train_grads_parity(pkg, oracle, preset, prec):
+    torch.set_float32_matmul_precision("highest")
+    n = ROWS[preset]
+    s, tabs, blob, obs, pol = make(pkg, preset, prec, n)
+    sc, v = oracle_fwd(oracle, s, tabs, blob, obs)
+    mask, act, old, adv, ret, val = _rollout_tensors(pkg, oracle, s, obs, sc, 5)
+    n_seg, horizon = 1, n
+    prio = np.ones(n_seg, np.float32)
+    # CUDA: forward_train -> PPO loss -> backward
+    out = pol.forward_train(obs)
+    grad, nlp, ratio, stats = pol.ppo_loss(out, mask, act, old, adv, val, ret, prio, n_seg, horizon)
+    pol.backward(grad, ret)
+    g = pol.grads_packed()
+    # oracle
+    P = oracle.params_from_blob(blob, s, requires_grad=True)
+    T = oracle.tables_to_torch(tabs)
+    _, ostats, og = oracle.train_grads(P, T, obs, s, act, old, adv, val, ret, prio, n_seg, horizon)
+    st = stats.cpu().numpy()
+    for k, key in enumerate(["total", "pg", "vf", "ent", "old_approx_kl", "approx_kl"]):
+        assert abs(st[k] - ostats[key]) <= 50 * TOL[prec] * max(1e-3, abs(ostats[key])), (key, st[k], ostats[key])
+    off = 0
+    worst = []
+    ref = {name: og[name].detach().numpy().ravel() for name, _ in pkg.config.param_table(s)}
+    gnorm = np.sqrt(sum(float((v.astype(np.float64) ** 2).sum()) for v in ref.values()))
+    for name, shp in pkg.config.param_table(s):
+        k = int(np.prod(shp))
+        a = g[off:off + k]; off += k
+        b = ref[name]
+        if np.linalg.norm(b) <= 1e-6 * gnorm:
+            # analytically ~0 (e.g. score2_b: softmax logit grads sum to 0):
+            # only rounding noise on both sides, judged against the global norm
+            assert np.linalg.norm(a - b) <= TOL[prec] * 1e-2 * gnorm, name
+            continue
+        worst.append((rel(a, b), name))
+    worst.sort(reverse=True)
+    print(preset, prec, "worst grad rel errors:", worst[:4])
+    assert worst[0][0] <= TOL[prec] * (3 if prec == "bf16" else 1), worst[:5]
+
+
+def test_adam_matches_torch(pkg, oracle):
+    s, tabs, blob, obs, pol = make(pkg, "tiny", "fp32", 6)
+    rng = np.random.default_rng(0)
+    P = oracle.params_from_blob(blob, s)
+    state = {}
+    for it in range(3):
+        gw = [rng.standard_normal(int(np.prod(shp))).astype(np.float32) * (0.5 if it else 5.0)
+              for _, shp in pkg.config.param_table(s)]
+        grads = pol.arena(1)
+        grads.zero_()
+        for (name, shp), off, gg in zip(pkg.config.param_table(s), pol.param_offsets(), gw):
+            grads[off:off + gg.size] = torch.from_numpy(gg).cuda()
+        st = pol.adam_step(lr=3e-4, max_norm=1.0).cpu().numpy()
+        og = {name: torch.from_numpy(gg.reshape(shp)) for (name, shp), gg in
+              zip(pkg.config.param_table(s), gw)}
+        norm = oracle.adam_step(P, og, state)
+        assert abs(st[0] - norm) <= 1e-5 * norm and st[1] == 1.0
+    w = pol.save_weights()
+    ref = oracle.blob_from_params(P, s)
+    assert rel(w - blob, ref - blob) <= 1e-4
+    assert pol.step == 3
+
+
+def test_adam_gate_and_nonfinite(pkg, oracle):
+    s, tabs, blob, obs, pol = make(pkg, "tiny", "fp32", 4)
+    grads = pol.arena(1)
+    grads.fill_(0.01)
+    gate = torch.zeros(1, device="cuda")
+    st = pol.adam_step(gate=gate).cpu().numpy()
+    assert st[1] == 0.0
+    assert np.array_equal(pol.save_weights(), blob) and pol.step == 0
+    grads[5] = float("nan")
+    st = pol.adam_step().cpu().numpy()
+    assert st[1] == 0.0 and np.array_equal(pol.save_weights(), blob)
+
+
+@pytest.mark.parametrize("preset", ["small", "c4"])
+def test_sampler_parity(pkg, oracle, preset):
+    s = pkg.config.PRESETS[preset]
+    n = 512
+    rng = np.random.default_rng(1)
+    scores = rng.standard_normal((n, s.nopt)).astype(np.float32) * 2
+    mask = (rng.random((n, s.nopt)) < 0.3).astype(np.float32)
+    mask[np.arange(n), rng.integers(0, s.nopt, n)] = 1.0
+    mask[0] = 0; mask[0, 5] = 1
+    dec = np.concatenate([scores, rng.standard_normal((n, 1)).astype(np.float32)], 1)
+    u = rng.random(n).astype(np.float32)
+    u[1] = 0.9999999
+    pol = pkg.PTCGPolicy(s, precision="fp32")
+    act, logp, val = [t.cpu().numpy() for t in pol.sample(dec, mask, u)]
+    oact, ologp, margin = oracle.sample_logits(scores, mask, u)
+    ok = margin > 1e-5
+    assert np.array_equal(act[ok].astype(np.int64), oact[ok])
+    assert np.all(mask[np.arange(n), act.astype(np.int64)] == 1)      # always legal
+    np.testing.assert_allclose(logp[ok], ologp[ok], atol=1e-4)
+    np.testing.assert_array_equal(val, dec[:, -1])
+
+
+def test_advantage_parity(pkg, oracle):
+    s = pkg.config.PRESETS["tiny"]
+    B, T = 5, 16
+    rng = np.random.default_rng(2)
+    obs = pkg.synth.make_obs(s, B * T, 4).reshape(B, T, -1)
+    seats = obs[:, :, s.seat_col]
+    vals = rng.standard_normal((B, T)).astype(np.float32)
+    rew = rng.standard_normal((B, T)).astype(np.float32)
+    dones = (rng.random((B, T)) < 0.1).astype(np.float32)
+    imp = rng.uniform(0.5, 1.5, (B, T)).astype(np.float32)
+    pol = pkg.PTCGPolicy(s, precision="fp32")
+    adv = pol.advantage(vals, rew, dones, imp, obs, 0.99, 0.95, 1.0, 1.0).cpu().numpy()
+    ref = oracle.negamax_advantage(vals, rew, dones, imp, seats, 0.99, 0.95, 1.0, 1.0)
+    np.testing.assert_allclose(adv, ref, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("prec", ["fp32", "bf16"])
+def test_train_step_microbatch_equivalence(pkg, oracle, prec):
+    """ptcg_train_step over 3 micro-batches == one call over the whole
+    minibatch (advantage stats and aux normalisers are minibatch-wide)."""
+    s = pkg.config.PRESETS["tiny"]
+    n_seg, horizon = 3, 8
+    nt = n_seg * horizon
+    tabs = pkg.synth.make_tables(s, 11)
+    blob = pkg.synth.make_weights(s, 21)
+    obs = pkg.synth.make_obs(s, nt, 9)
+    rng = np.random.default_rng(3)
+    a, b = s.offsets["opt_mask"]
+    mask = obs[:, a:b]
+    act = np.array([rng.choice(np.nonzero(m)[0]) for m in mask], np.float32)
+    old = rng.normal(-1.5, 0.3, nt).astype(np.float32)
+    adv, ret = rng.standard_normal(nt).astype(np.float32), rng.standard_normal(nt).astype(np.float32)
+    val = rng.standard_normal(nt).astype(np.float32) * 0.1
+    prio = np.array([1.0, 0.5, 2.0], np.float32)
+    res = []
+    for rows in (nt, horizon):
+        pol = pkg.PTCGPolicy(s, precision=prec, tables=tabs, weights=blob, train_rows=rows)
+        st = pol.train_step(obs, act, old, adv, val, ret, prio, n_seg, horizon).cpu().numpy()
+        res.append((st, pol.grads_packed(), pol.save_weights()))
+    (s1, g1, w1), (s2, g2, w2) = res
+    tol = 1e-5 if prec == "fp32" else 5e-3
+    assert rel(g2, g1) <= tol
+    np.testing.assert_allclose(s2[:8], s1[:8], rtol=1e-4, atol=1e-6)
+    assert s1[9] == 1.0 and s2[9] == 1.0
+    assert rel(w2 - blob, w1 - blob) <= tol * 10
