@@ -1,0 +1,429 @@
+"""bench.py -- PPO train samples/s of the PTCG policy hot path on B200.
+
+Headline (BASELINE.json metric, config 2 / 3): one PPO minibatch step =
+forward (all heads) + fused clipped-PPO/value/entropy loss + backward +
+global-norm clip + fused Adam, 512 segments x 64 steps = 32768 samples per
+GPU of config-0-shaped observations (d256, 4 layers, 8 heads, FFN 1024,
+128 tokens, 64 options), bf16 tensor-core GEMMs with fp32 accumulation.
+Data parallel over N GPUs (torchrun, one process per GPU): every rank trains
+on its own minibatch (seed + rank); gradient buckets are all-reduced over
+NCCL on a side stream as the backward produces them, then every rank runs
+the same Adam; weights are checked identical across ranks each step.
+
+Also reported: rollout forward/s (config 1: 1024 agents x 64 env steps,
+forward + masked sampling), end-to-end numbers through the public API with
+host<->device copies, the roofline of the dominant kernel, and the CPU
+baseline (the CPU oracle on the host cores).
+
+--impl reference times the reference algorithm's CPU implementation (the
+oracle restatement of ptcg/rl/model.py + PPO + torch Adam) on the host cores.
+"""
+import argparse
+import datetime
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--preset", default="c0")
+    ap.add_argument("--segments", type=int, default=512)
+    ap.add_argument("--horizon", type=int, default=64)
+    ap.add_argument("--micro", type=int, default=8192, help="rows per micro-batch")
+    ap.add_argument("--rollout-agents", type=int, default=1024)
+    ap.add_argument("--rollout-steps", type=int, default=64)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-rollout", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1])); mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ---------------------------------------------------------------- reference
+def cpu_oracle_step_rate(pkg, s, rows, seconds, threads):
+    """Samples/s of the CPU oracle train step (forward_train + PPO loss +
+    backward + clip + Adam) on `rows` config-shaped observations."""
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ptcg_oracle as oracle
+    torch.set_num_threads(threads)
+    tabs = pkg.synth.make_tables(s, 11)
+    blob = pkg.synth.make_weights(s, 21)
+    obs = pkg.synth.make_obs_batch(s, rows, 5)
+    a, b = s.offsets["opt_mask"]
+    act = pkg.synth.sample_legal(obs[:, a:b], 1)
+    rng = np.random.default_rng(0)
+    P = oracle.params_from_blob(blob, s, requires_grad=True)
+    T = oracle.tables_to_torch(tabs)
+    state = {}
+    adv = rng.standard_normal(rows).astype(np.float32)
+    ret = rng.standard_normal(rows).astype(np.float32)
+    old = np.full(rows, -2.0, np.float32)
+    val = np.zeros(rows, np.float32)
+    prio = np.ones(1, np.float32)
+
+    def step():
+        _, _, g = oracle.train_grads(P, T, obs, s, act, old, adv, val, ret, prio, 1, rows)
+        oracle.adam_step(P, g, state)
+
+    step()                                  # warm-up
+    times = []
+    t_end = time.time() + seconds
+    while time.time() < t_end or len(times) < 2:
+        t0 = time.time(); step(); times.append(time.time() - t0)
+    med = float(np.median(times))
+    return rows / med, len(times), med
+
+
+def run_reference(args, pkg):
+    s = pkg.config.PRESETS[args.preset]
+    threads = os.cpu_count() or 1
+    rows = 64
+    rate, n, med = cpu_oracle_step_rate(pkg, s, rows, max(5.0, args.cpu_seconds), threads)
+    cpu = {"value": rate, "unit": "samples/s", "cores": threads, "kind": "port",
+           "sample": f"{rows}-row PPO train step (forward_train+loss+backward+Adam), "
+                     f"median of {n} steps, {med:.2f} s/step"}
+    line = {"impl": "reference", "metric": "PPO train samples/sec (config 2 shapes, aggregate)",
+            "value": rate, "unit": "samples/s", "n_gpus": args.gpus, "steps": n,
+            "warmup": 1, "ms_per_step": med * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"ppo_train_step {args.preset} (config 2), CPU sample of "
+                                   f"{rows} rows", "parallelism": "cpu"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": rate, "unit": "samples/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------- ours
+def main():
+    args = parse()
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args, pkg)
+        return
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    s = pkg.config.PRESETS[args.preset]
+    nt = args.segments * args.horizon
+    micro = min(args.micro, nt)
+    tabs = pkg.synth.make_tables(s, 11)
+    blob = pkg.synth.make_weights(s, 21)
+    pol = pkg.PTCGPolicy(s, precision="bf16", device=local, tables=tabs, weights=blob,
+                         rollout_rows=args.rollout_agents, train_rows=micro)
+
+    # --- this rank's minibatch (config 2/3): pool of distinct rows, tiled
+    pool_n = min(nt, 8192)
+    pool = pkg.synth.make_obs_batch(s, pool_n, 1000 + rank)
+    reps = (nt + pool_n - 1) // pool_n
+    order = np.random.default_rng(7 + rank).permutation(reps * pool_n)[:nt] % pool_n
+    obs_h = torch.from_numpy(pool[order]).pin_memory()
+    a, b = s.offsets["opt_mask"]
+    act_h = torch.from_numpy(pkg.synth.sample_legal(obs_h[:, a:b].numpy(), 3 + rank))
+    obs = obs_h.to(dev)
+    act = act_h.to(dev)
+    # old log-probs and values from the forward pass (rollout path)
+    old = torch.empty(nt, device=dev)
+    vals = torch.empty(nt, device=dev)
+    for c0 in range(0, nt, args.rollout_agents):
+        c1 = min(nt, c0 + args.rollout_agents)
+        out = pol.forward(obs[c0:c1])
+        m = obs[c0:c1, a:b]
+        lg = out[:, :-1].masked_fill(m == 0, -1e4)
+        lp = torch.log_softmax(lg, 1)
+        old[c0:c1] = lp.gather(1, act[c0:c1].long()[:, None])[:, 0]
+        vals[c0:c1] = out[:, -1]
+    g = torch.Generator(device="cpu").manual_seed(99 + rank)
+    adv = torch.randn(nt, generator=g).to(dev)
+    ret = torch.randn(nt, generator=g).to(dev)
+    prio = torch.ones(args.segments, device=dev)
+    hyper = dict(clip=0.2, vf_clip=0.2, vf_coef=0.5, ent_coef=0.01, lr=3e-4,
+                 betas=(0.9, 0.999), eps=1e-8, max_norm=1.0)
+
+    # --- data parallel: bucketed all-reduce overlapped with the backward
+    comm = torch.cuda.Stream(device=dev) if world > 1 else None
+    grads = pol.arena(1)
+    if world > 1:
+        def hook(off, cnt, stream_ptr):
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream())
+            comm.wait_event(ev)
+            with torch.cuda.stream(comm):
+                dist.all_reduce(grads[off:off + cnt], op=dist.ReduceOp.AVG)
+        pol.set_grad_hook(hook)
+    ck = torch.zeros(max(1, args.steps + args.warmup), 2, dtype=torch.int64, device=dev)
+    stats = torch.zeros(16, device=dev)
+
+    def step(i, o=obs, ac=act, ol=old, ad=adv, va=vals, re=ret):
+        pol.train_step(o, ac, ol, ad, va, re, prio, args.segments, args.horizon,
+                       skip_adam=world > 1, stats=stats, **hyper)
+        if world > 1:
+            torch.cuda.current_stream().wait_stream(comm)
+            pol.adam_step(lr=hyper["lr"], betas=hyper["betas"], eps=hyper["eps"],
+                          max_norm=hyper["max_norm"])
+            c = pol.weights_checksum().to(torch.int64) & 0xFFFFFFFF
+            v = c[0] | (c[1] << 32)
+            mn = v.clone(); mx = v.clone()
+            dist.all_reduce(mn, op=dist.ReduceOp.MIN)
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            ck[i, 0] = mn; ck[i, 1] = mx
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    use_tc = pol.lib.ptcg_launch_count  # noqa: F841 (symbol presence)
+    timer_mode = 1 if _tc_available(pol) else 2
+    pol.kernel_timer(timer_mode)
+    l0 = pol.lib.ptcg_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record()
+        for i in range(args.steps):
+            step(args.warmup + i)
+        e1.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches = pol.lib.ptcg_launch_count() - l0
+    kms, klaunch, kflops = pol.kernel_timer_read()
+    pol.kernel_timer(0)
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        lt = torch.tensor([launches], device=dev, dtype=torch.int64)
+        dist.all_reduce(lt)
+        launches = int(lt.item())
+        ok = bool((ck[:, 0] == ck[:, 1]).all().item())
+    else:
+        ok = True
+    ms_max = float(t.item())
+    ms_step = ms_max / args.steps
+    value = nt * world * args.steps / (ms_max / 1e3)
+    st = stats.cpu().numpy()
+
+    # --- end to end through the public API: pinned host inputs -> device,
+    #     train step, loss stats back to the host, every step
+    host = dict(obs=obs_h, act=act_h, old=old.cpu().pin_memory(), adv=adv.cpu().pin_memory(),
+                val=vals.cpu().pin_memory(), ret=ret.cpu().pin_memory())
+    bufs = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = 16 * 4
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for i in range(args.e2e_steps):
+        for k in host:
+            bufs[k].copy_(host[k], non_blocking=True)
+        step(0, bufs["obs"], bufs["act"], bufs["old"], bufs["adv"], bufs["val"], bufs["ret"])
+        _ = stats.cpu()
+    f1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([f0.elapsed_time(f1)], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e = nt * world * args.e2e_steps / (float(te.item()) / 1e3)
+
+    # --- rollout forward (config 1): fresh observations every env step
+    rollout = None
+    if not args.no_rollout:
+        A = args.rollout_agents
+        nroll = 8
+        ro_h = torch.from_numpy(pkg.synth.make_obs_batch(s, A * nroll, 500 + rank)).pin_memory()
+        ro = ro_h.to(dev)
+        uni = torch.rand(args.rollout_steps, A, device=dev)
+        buf = torch.empty(A, s.obs_size, device=dev)
+
+        def rstep(j, src):
+            out = pol.forward(src)
+            return pol.sample(out, src[:, a:b], uni[j])
+
+        for j in range(3):
+            rstep(j, ro[:A])
+        torch.cuda.synchronize()
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record()
+        for j in range(args.rollout_steps):
+            k = j % nroll
+            rstep(j, ro[k * A:(k + 1) * A])
+        r1.record()
+        torch.cuda.synchronize()
+        rms = r0.elapsed_time(r1)
+        # end to end: obs from pinned host each step, actions back to the host
+        q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        q0.record()
+        for j in range(args.rollout_steps):
+            k = j % nroll
+            buf.copy_(ro_h[k * A:(k + 1) * A], non_blocking=True)
+            acts, lp, v = rstep(j, buf)
+            acts.cpu()
+        q1.record()
+        torch.cuda.synchronize()
+        qms = q0.elapsed_time(q1)
+        tt = torch.tensor([rms, qms], device=dev)
+        if world > 1:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        rms, qms = [float(x) for x in tt.cpu()]
+        rollout = {"metric": "rollout forward/sec (config 1)", "unit": "obs/s",
+                   "value": A * args.rollout_steps * world / (rms / 1e3),
+                   "e2e": A * args.rollout_steps * world / (qms / 1e3),
+                   "agents_per_gpu": A, "env_steps": args.rollout_steps,
+                   "ms_per_env_step": rms / args.rollout_steps,
+                   "h2d_bytes_per_step": A * s.obs_size * 4, "d2h_bytes_per_step": A * 4}
+
+    if world > 1:
+        pol.set_grad_hook(None)
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    # --- roofline of the dominant kernel (the GEMM class timed above)
+    peaks, src = measured_peaks()
+    achieved = kflops / (kms / 1e3) / 1e12 if kms > 0 else 0.0
+    peak = peaks.get("bf16_tflops_sustained", 1400.0)
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    kname = "gemm_tc (tcgen05)" if timer_mode == 1 else "gemm_simt"
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get(kname)
+    roof = {"kernel": kname, "bound": "tensor", "achieved": achieved, "peak": peak,
+            "unit": "TFLOP/s", "frac": achieved / peak if peak else None, "traffic": traffic,
+            "peak_source": f"bf16_tflops_sustained ({src})", "launches": klaunch,
+            "device_ms": kms, "share_of_step_time": kms / ms if ms else None}
+
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        rate, n, med = cpu_oracle_step_rate(pkg, s, 64, args.cpu_seconds, threads)
+        cpu = {"value": rate, "unit": "samples/s", "cores": threads, "kind": "port",
+               "sample": f"64-row PPO train step of the CPU oracle (forward_train + loss + "
+                         f"backward + Adam), median of {n} steps ({med:.2f} s/step)"}
+    flops_sample = 3 * 1.295e9
+    line = {
+        "metric": "PPO train samples/sec (config 2 per GPU, aggregate)",
+        "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"ppo_train_step {args.preset}: {args.segments}x{args.horizon} "
+                               f"samples/GPU, micro-batch {micro}",
+                   "model": "PTCGTransformer d%d L%d h%d ffn%d ltok%d nopt%d" % (
+                       s.d, s.layers, s.heads, s.ffn, s.ltok, s.nopt),
+                   "global_batch": nt * world, "seq_len": s.lseq,
+                   "parallelism": f"dp{world}",
+                   "l2": "inputs larger than L2 (obs %.0f MB per step per GPU)" % (
+                       nt * s.obs_size * 4 / 1e6)},
+        "e2e": {"value": e2e, "unit": "samples/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": int(launches),
+        "roofline": roof,
+        "model_tflops": value * flops_sample / world / 1e12,
+        "rollout": rollout,
+        "cpu_baseline": cpu,
+        "clocks": clk.summary(),
+        "weights_identical_across_ranks": ok,
+        "loss_stats": {"total": float(st[0]), "approx_kl": float(st[5]),
+                       "grad_norm": float(st[8])},
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def _tc_available(pol):
+    return bool(getattr(pol.lib, "ptcg_tc_available", None) and pol.lib.ptcg_tc_available())
+
+
+if __name__ == "__main__":
+    main()

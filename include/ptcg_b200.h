@@ -197,6 +197,16 @@ int ptcg_set_step(PtcgModel* m, long step);
  * uint32 halves) for the cross-rank "weights identical" check. */
 int ptcg_weights_checksum(PtcgModel* m, unsigned int* out_dev, void* stream);
 
+/* CUDA-event timing of every launch of one GEMM kernel class (1 = tcgen05
+ * tensor-core GEMM, 2 = SIMT GEMM, 0 = off) until the next call; read back
+ * total device milliseconds, launch count and algorithmic FLOPs (2*M*N*K per
+ * launch).  The reference's analogue is its cudaEvent phase timing
+ * (ProfileT, native/src/pufferlib.cu:59-63, 1851-1953). */
+int ptcg_kernel_timer(PtcgModel* m, int mode);
+/* Number of CUDA kernels this library has launched in this process. */
+long long ptcg_launch_count(void);
+int ptcg_kernel_timer_read(PtcgModel* m, double* ms, long* launches, double* flops);
+
 #ifdef __cplusplus
 }
 #endif

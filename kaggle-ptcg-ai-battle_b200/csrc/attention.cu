@@ -198,11 +198,11 @@ void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
     size_t sm = fwd_smem(L);
     if (dtype == DT_F32) {
         set_smem(k_attn_fwd<float>, sm);
-        k_attn_fwd<float><<<nseq * H, NW * 32, sm, s>>>((const float*)qkv, ldqkv, keep,
+        ++g_ptcg_launches, k_attn_fwd<float><<<nseq * H, NW * 32, sm, s>>>((const float*)qkv, ldqkv, keep,
             (float*)out, ldo, lse, L, H);
     } else {
         set_smem(k_attn_fwd<bf16>, sm);
-        k_attn_fwd<bf16><<<nseq * H, NW * 32, sm, s>>>((const bf16*)qkv, ldqkv, keep,
+        ++g_ptcg_launches, k_attn_fwd<bf16><<<nseq * H, NW * 32, sm, s>>>((const bf16*)qkv, ldqkv, keep,
             (bf16*)out, ldo, lse, L, H);
     }
 }
@@ -215,11 +215,11 @@ void attn_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
     size_t sm = bwd_smem(L);
     if (dtype == DT_F32) {
         set_smem(k_attn_bwd<float>, sm);
-        k_attn_bwd<float><<<nseq * H, NW * 32, sm, s>>>((const float*)qkv, ldqkv, keep,
+        ++g_ptcg_launches, k_attn_bwd<float><<<nseq * H, NW * 32, sm, s>>>((const float*)qkv, ldqkv, keep,
             (const float*)out, ldo, (const float*)dout, lddo, lse, (float*)dqkv, lddqkv, dbias, L, H);
     } else {
         set_smem(k_attn_bwd<bf16>, sm);
-        k_attn_bwd<bf16><<<nseq * H, NW * 32, sm, s>>>((const bf16*)qkv, ldqkv, keep,
+        ++g_ptcg_launches, k_attn_bwd<bf16><<<nseq * H, NW * 32, sm, s>>>((const bf16*)qkv, ldqkv, keep,
             (const bf16*)out, ldo, (const bf16*)dout, lddo, lse, (bf16*)dqkv, lddqkv, dbias, L, H);
     }
 }

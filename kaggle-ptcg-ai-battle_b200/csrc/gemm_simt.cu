@@ -138,6 +138,6 @@ void gemm_simt(const GemmArgs& a, cudaStream_t s) {
         if (grid.z < 1) grid.z = 1;
         if (grid.z > 512) grid.z = 512;
     }
-    if (a.dtype == DT_F32) k_gemm_simt<float><<<grid, NT, 0, s>>>(a);
-    else k_gemm_simt<bf16><<<grid, NT, 0, s>>>(a);
+    if (a.dtype == DT_F32) ++g_ptcg_launches, k_gemm_simt<float><<<grid, NT, 0, s>>>(a);
+    else ++g_ptcg_launches, k_gemm_simt<bf16><<<grid, NT, 0, s>>>(a);
 }

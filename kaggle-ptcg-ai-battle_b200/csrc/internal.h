@@ -4,6 +4,9 @@
 #include <stdint.h>
 
 enum { DT_F32 = 0, DT_BF16 = 1 };
+
+// number of kernels this library has launched (every launch site increments it)
+extern long long g_ptcg_launches;
 enum { ACT_NONE = 0, ACT_GELU = 1, ACT_GELU_BWD = 2 };
 
 // C[m, n] = epilogue( alpha * sum_k A(m, k) * B(n, k) )

@@ -25,6 +25,8 @@
 #include <vector>
 #include <unordered_map>
 
+long long g_ptcg_launches = 0;
+
 // ------------------------------------------------------------------ errors
 static thread_local char g_err[1024];
 static void set_err(const char* fmt, ...) {
@@ -151,8 +153,18 @@ struct Tab {                            // batch-independent table activations +
     float *d_cv, *d_att, *d_sk, *d_poc, *d_poa, *d_h1, *d_cardln, *d_cardin, *d_attin, *d_skin;
 };
 
+// CUDA-event timing of one GEMM kernel class over a region (bench roofline)
+struct KTimer {
+    int mode = 0;                       // 0 off, 1 tensor-core GEMM, 2 SIMT GEMM
+    std::vector<cudaEvent_t> ev;
+    int used = 0;
+    double flops = 0.0;
+    long launches = 0;
+};
+
 struct PtcgModel {
     PtcgShape s;
+    KTimer kt;
     Dims z;
     int prec, dev;
     std::vector<ParamDef> defs;
@@ -209,9 +221,28 @@ struct PtcgModel {
 };
 
 // ---------------------------------------------------------------- helpers
-static void gemm(const PtcgModel* M, const GemmArgs& a, cudaStream_t s) {
-    if (a.dtype == DT_BF16 && gemm_tc_available() && gemm_tc(a, s)) return;
-    gemm_simt(a, s);
+static void kt_mark(PtcgModel* M, cudaStream_t s) {
+    KTimer& k = M->kt;
+    if (k.used >= (int)k.ev.size()) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        k.ev.push_back(e);
+    }
+    cudaEventRecord(k.ev[k.used++], s);
+}
+
+static void gemm(PtcgModel* M, const GemmArgs& a, cudaStream_t s) {
+    bool tc_ok = (a.dtype == DT_BF16 || a.allow_tf32) && gemm_tc_available();
+    int cls = tc_ok ? 1 : 2;
+    bool timed = M->kt.mode == cls;
+    if (timed) kt_mark(M, s);
+    bool done = tc_ok && gemm_tc(a, s);
+    if (!done) gemm_simt(a, s);
+    if (timed) {
+        kt_mark(M, s);
+        M->kt.flops += 2.0 * a.M * a.N * a.K;
+        M->kt.launches++;
+    }
 }
 
 // C[M,N] (+)= op(A) op(B)^T helpers for the three GEMM shapes of a Linear
@@ -255,14 +286,14 @@ template <typename T> static void colsum(float* out, const T* in, long ld, int r
     if (rows <= 0) return;
     int rpb = 256;
     dim3 g(cdiv(cols, 128), cdiv(rows, rpb));
-    k_colsum<T><<<g, 128, 0, s>>>(out, in, ld, rows, cols, rpb);
+    ++g_ptcg_launches, k_colsum<T><<<g, 128, 0, s>>>(out, in, ld, rows, cols, rpb);
 }
 
 static void ln_fwd(int dt, void* y, long ldy, float* mu, float* rs, const float* x, long ldx,
                    const float* w, const float* b, int rows, int D, cudaStream_t s) {
     unsigned g = cdiv(rows, 8);
-    if (dt == DT_F32) k_ln_fwd<float><<<g, 256, 0, s>>>((float*)y, ldy, mu, rs, x, ldx, w, b, rows, D);
-    else k_ln_fwd<bf16><<<g, 256, 0, s>>>((bf16*)y, ldy, mu, rs, x, ldx, w, b, rows, D);
+    if (dt == DT_F32) ++g_ptcg_launches, k_ln_fwd<float><<<g, 256, 0, s>>>((float*)y, ldy, mu, rs, x, ldx, w, b, rows, D);
+    else ++g_ptcg_launches, k_ln_fwd<bf16><<<g, 256, 0, s>>>((bf16*)y, ldy, mu, rs, x, ldx, w, b, rows, D);
 }
 // dx (f32, ld D) = LN'(dy) (+ dx), copy to dxc (T) unless dxc == nullptr
 static void ln_bwd(int dt, float* dx, int accumulate, void* dxc, float* dw, float* db,
@@ -272,10 +303,10 @@ static void ln_bwd(int dt, float* dx, int accumulate, void* dxc, float* dw, floa
     unsigned g = cdiv(rows, rpb);
     size_t sm = 2 * D * sizeof(float);
     if (dt == DT_F32 || dxc == nullptr)
-        k_ln_bwd<float><<<g, 256, sm, s>>>(dx, D, accumulate, (float*)dxc, D, dw, db, dy, D, x, D,
+        ++g_ptcg_launches, k_ln_bwd<float><<<g, 256, sm, s>>>(dx, D, accumulate, (float*)dxc, D, dw, db, dy, D, x, D,
                                           w, mu, rs, rows, D, rpb);
     else
-        k_ln_bwd<bf16><<<g, 256, sm, s>>>(dx, D, accumulate, (bf16*)dxc, D, dw, db, dy, D, x, D,
+        ++g_ptcg_launches, k_ln_bwd<bf16><<<g, 256, sm, s>>>(dx, D, accumulate, (bf16*)dxc, D, dw, db, dy, D, x, D,
                                          w, mu, rs, rows, D, rpb);
 }
 
@@ -404,27 +435,27 @@ static void tables_fwd(PtcgModel* M, cudaStream_t s) {
     g.s[0] = {M->w("attack_id_emb").p, 48, 0, 48, 0};
     g.s[1] = {M->att_static, 15, 0, 15, 48};
     g.s[2] = {M->att_text, 64, 0, 64, 63};
-    k_concat_rows<<<cdiv((long)z.NA * 127, TPB), TPB, 0, s>>>(t.att_in, 127, z.NA, 127, g);
+    ++g_ptcg_launches, k_concat_rows<<<cdiv((long)z.NA * 127, TPB), TPB, 0, s>>>(t.att_in, 127, z.NA, 127, g);
     GemmArgs a = lin_fwd(DT_F32, z.NA, 127, 64, t.att_in, 127, f32w(M->w("attack_mlp_w"), 127), t.att_tab, 64, DT_F32);
     a.bias = M->w("attack_mlp_b").p; a.act = ACT_GELU; a.out2 = t.att_pre; a.ldo2 = 64;
     gemm_simt(a, s);
     g.n = 2;
     g.s[0] = {M->w("skill_id_emb").p, 48, 0, 48, 0};
     g.s[1] = {M->skill_text, 64, 0, 64, 48};
-    k_concat_rows<<<cdiv((long)z.NS * 112, TPB), TPB, 0, s>>>(t.sk_in, 112, z.NS, 112, g);
+    ++g_ptcg_launches, k_concat_rows<<<cdiv((long)z.NS * 112, TPB), TPB, 0, s>>>(t.sk_in, 112, z.NS, 112, g);
     a = lin_fwd(DT_F32, z.NS, 112, 128, t.sk_in, 112, f32w(M->w("skill_mlp_w"), 112), t.sk_tab, 128, DT_F32);
     a.bias = M->w("skill_mlp_b").p; a.act = ACT_GELU; a.out2 = t.sk_pre; a.ldo2 = 128;
     gemm_simt(a, s);
     // pools written straight into their card_in columns
-    k_pool<<<cdiv((long)z.NC * 64, TPB), TPB, 0, s>>>(t.card_in + 250, t.card_in + 314, 634, t.a_arg,
+    ++g_ptcg_launches, k_pool<<<cdiv((long)z.NC * 64, TPB), TPB, 0, s>>>(t.card_in + 250, t.card_in + 314, 634, t.a_arg,
         t.att_tab, M->card_attacks, z.NC, 4, 64);
-    k_pool<<<cdiv((long)z.NC * 128, TPB), TPB, 0, s>>>(t.card_in + 378, t.card_in + 506, 634, t.s_arg,
+    ++g_ptcg_launches, k_pool<<<cdiv((long)z.NC * 128, TPB), TPB, 0, s>>>(t.card_in + 378, t.card_in + 506, 634, t.s_arg,
         t.sk_tab, M->card_skills, z.NC, 2, 128);
     g.n = 3;
     g.s[0] = {M->w("card_id_emb").p, 64, 0, 64, 0};
     g.s[1] = {M->card_static, 58, 0, 58, 64};
     g.s[2] = {M->card_text, 128, 0, 128, 122};
-    k_concat_rows<<<cdiv((long)z.NC * 250, TPB), TPB, 0, s>>>(t.card_in, 634, z.NC, 250, g);
+    ++g_ptcg_launches, k_concat_rows<<<cdiv((long)z.NC * 250, TPB), TPB, 0, s>>>(t.card_in, 634, z.NC, 250, g);
     ln_fwd(DT_F32, t.card_ln, 634, t.ln_mu, t.ln_rs, t.card_in, 634, M->w("card_ln_w").p,
            M->w("card_ln_b").p, z.NC, 634, s);
     a = lin_fwd(DT_F32, z.NC, 634, 256, t.card_ln, 634, f32w(M->w("card_mlp1_w"), 634), t.h1, 256, DT_F32);
@@ -469,7 +500,7 @@ static void block_fwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
 template <typename TI>
 static void rowdot(float* out, long os, const TI* in, long ldi, const float* w, const float* b,
                    int rows, int K, int g, int gs, int go, cudaStream_t s) {
-    k_rowdot<TI><<<cdiv(rows, 8), 256, 0, s>>>(out, os, in, ldi, w, b, rows, K, g, gs, go);
+    ++g_ptcg_launches, k_rowdot<TI><<<cdiv(rows, 8), 256, 0, s>>>(out, os, in, ldi, w, b, rows, K, g, gs, go);
 }
 
 static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* out, bool train,
@@ -484,12 +515,12 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     long ldtok = rup(z.TOK_IN, 8);
     long ntc = (long)R * z.LTOK * z.TOK_IN;
     if (dt == DT_F32)
-        k_tok_cat<float><<<cdiv(ntc, TPB), TPB, 0, s>>>((float*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
+        ++g_ptcg_launches, k_tok_cat<float><<<cdiv(ntc, TPB), TPB, 0, s>>>((float*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
             M->w("zone_emb").p, M->w("owner_emb").p, R, z.TOK_IN);
     else
-        k_tok_cat<bf16><<<cdiv(ntc, TPB), TPB, 0, s>>>((bf16*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
+        ++g_ptcg_launches, k_tok_cat<bf16><<<cdiv(ntc, TPB), TPB, 0, s>>>((bf16*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
             M->w("zone_emb").p, M->w("owner_emb").p, R, z.TOK_IN);
-    k_x0_readout<<<cdiv((long)R * (z.LSEQ > D ? z.LSEQ : D), TPB), TPB, 0, s>>>(Wk.x[0], Wk.keep,
+    ++g_ptcg_launches, k_x0_readout<<<cdiv((long)R * (z.LSEQ > D ? z.LSEQ : D), TPB), TPB, 0, s>>>(Wk.x[0], Wk.keep,
         M->w("readout").p, obs, ol, R, D);
     // --- global / decision encoders (fp32)
     GemmArgs a = lin_fwd(DT_F32, R, 64, 128, obs + ol.glob, ol.obs, f32w(M->w("global1_w"), 64),
@@ -499,7 +530,7 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     a = lin_fwd(DT_F32, R, 128, 128, Wk.g1, 128, f32w(M->w("global2_w"), 128), Wk.gd, 192, DT_F32);
     a.bias = M->w("global2_b").p;
     gemm_simt(a, s);
-    k_dec_in<<<cdiv((long)R * 696, TPB), TPB, 0, s>>>(Wk.decin, obs, ol, t.card_vec, t.att_tab,
+    ++g_ptcg_launches, k_dec_in<<<cdiv((long)R * 696, TPB), TPB, 0, s>>>(Wk.decin, obs, ol, t.card_vec, t.att_tab,
         M->w("sel_type_emb").p, M->w("ctx_emb").p, R);
     a = lin_fwd(DT_F32, R, 696, 64, Wk.decin, 696, f32w(M->w("dec1_w"), 696), Wk.d1, 64, DT_F32);
     a.bias = M->w("dec1_b").p; a.act = ACT_GELU; a.out2 = Wk.d1pre; a.ldo2 = 64;
@@ -529,7 +560,7 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     // --- option scorer
     long NO = (long)R * z.NOPT;
     long ldq = rup(z.Q_IN, 8);
-    k_q_in<float><<<cdiv(NO * z.Q_IN, TPB), TPB, 0, s>>>((float*)Wk.qin, ldq, obs, ol, Wk.h, D,
+    ++g_ptcg_launches, k_q_in<float><<<cdiv(NO * z.Q_IN, TPB), TPB, 0, s>>>((float*)Wk.qin, ldq, obs, ol, Wk.h, D,
         M->w("opt_type_emb").p, t.poc, t.poa, R, z.Q_IN);
     a = lin_fwd(DT_F32, (int)NO, z.Q_IN, D, Wk.qin, ldq, f32w(M->w("q1_w"), z.Q_IN), Wk.q1, D, DT_F32);
     a.bias = M->w("q1_b").p; a.act = ACT_GELU; a.allow_tf32 = tf32;
@@ -539,7 +570,7 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     a.bias = M->w("q2_b").p; a.allow_tf32 = tf32;
     gemm(M, a, s);
     long nsc = NO * z.SCORE_IN;
-    k_sc_in<float><<<cdiv(nsc, TPB), TPB, 0, s>>>((float*)Wk.scin, z.SCORE_IN, Wk.q, Wk.h, Wk.gd,
+    ++g_ptcg_launches, k_sc_in<float><<<cdiv(nsc, TPB), TPB, 0, s>>>((float*)Wk.scin, z.SCORE_IN, Wk.q, Wk.h, Wk.gd,
         D, z.LSEQ, z.NOPT, R);
     a = lin_fwd(DT_F32, (int)NO, z.SCORE_IN, 256, Wk.scin, z.SCORE_IN,
                 f32w(M->w("score1_w"), z.SCORE_IN), Wk.s1, 256, DT_F32);
@@ -551,7 +582,7 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     {
         int rows = (int)NO;
         unsigned g = cdiv(rows, 8);
-        k_rowdot<float><<<g, 256, 0, s>>>(Wk.out, 1, (const float*)Wk.s1, 256,
+        ++g_ptcg_launches, k_rowdot<float><<<g, 256, 0, s>>>(Wk.out, 1, (const float*)Wk.s1, 256,
             M->w("score2_w").p, M->w("score2_b").p, rows, 256, 0, 0, 0);
     }
     // (scores are staged contiguous (R*NOPT) at the head of Wk.out and
@@ -560,12 +591,12 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     long ldo_t = rup(134, 8);
     long no = (long)R * 56 * 134;
     if (dt == DT_F32)
-        k_otok_in<float><<<cdiv(no, TPB), TPB, 0, s>>>((float*)Wk.otokin, ldo_t, Wk.ckeep, obs, ol,
+        ++g_ptcg_launches, k_otok_in<float><<<cdiv(no, TPB), TPB, 0, s>>>((float*)Wk.otokin, ldo_t, Wk.ckeep, obs, ol,
             t.card_vec, Wk.keep, R);
     else
-        k_otok_in<bf16><<<cdiv(no, TPB), TPB, 0, s>>>((bf16*)Wk.otokin, ldo_t, Wk.ckeep, obs, ol,
+        ++g_ptcg_launches, k_otok_in<bf16><<<cdiv(no, TPB), TPB, 0, s>>>((bf16*)Wk.otokin, ldo_t, Wk.ckeep, obs, ol,
             t.card_vec, Wk.keep, R);
-    k_xc_fill<<<cdiv((long)R * (1 + z.LSEQ) * D, TPB), TPB, 0, s>>>(Wk.xc[0], Wk.h,
+    ++g_ptcg_launches, k_xc_fill<<<cdiv((long)R * (1 + z.LSEQ) * D, TPB), TPB, 0, s>>>(Wk.xc[0], Wk.h,
         M->w("critic_readout").p, z.LSEQ, z.LCRIT, D, R);
     a = lin_fwd(dt, R * 56, 134, D, Wk.otokin, ldo_t, M->w("oracle_proj_w"), Wk.xc[0], D, DT_F32);
     a.bias = M->w("oracle_proj_b").p;
@@ -573,23 +604,23 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     gemm(M, a, s);
     Wk.cblk.x_in = Wk.xc[0]; Wk.cblk.x_out = Wk.xc[1];
     block_fwd(M, M->blk("c0_"), Wk.cblk, Wk.ckeep, R, z.LCRIT, train, s);
-    k_val_in<float><<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.ovin, nullptr, 0, Wk.xc[1],
+    ++g_ptcg_launches, k_val_in<float><<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.ovin, nullptr, 0, Wk.xc[1],
         z.LCRIT, D, Wk.gd, R);
     a = lin_fwd(DT_F32, R, z.VAL_IN, 256, Wk.ovin, z.VAL_IN, f32w(M->w("oracle_v1_w"), z.VAL_IN),
                 Wk.ov1, 256, DT_F32);
     a.bias = M->w("oracle_v1_b").p; a.act = ACT_GELU; a.out2 = Wk.ov1pre; a.ldo2 = 256;
     gemm_simt(a, s);
     // fused output [scores | value]: expand staged scores, then the value column
-    k_scale_copy<<<cdiv(NO, TPB), TPB, 0, s>>>(out, z.NOPT + 1, Wk.out, z.NOPT, R, z.NOPT, 1.f);
+    ++g_ptcg_launches, k_scale_copy<<<cdiv(NO, TPB), TPB, 0, s>>>(out, z.NOPT + 1, Wk.out, z.NOPT, R, z.NOPT, 1.f);
     rowdot<float>(out + z.NOPT, z.NOPT + 1, Wk.ov1, 256, M->w("oracle_v2_w").p,
                   M->w("oracle_v2_b").p, R, 256, 0, 0, 0, s);
     if (!train) return 0;
     // --- train-only heads: blind V, opp-hand counts, prize logits
     if (dt == DT_F32)
-        k_val_in<float><<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.bvin, nullptr, 0, Wk.h,
+        ++g_ptcg_launches, k_val_in<float><<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.bvin, nullptr, 0, Wk.h,
             z.LSEQ, D, Wk.gd, R);
     else
-        k_val_in<bf16><<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.bvin, (bf16*)Wk.bvinc,
+        ++g_ptcg_launches, k_val_in<bf16><<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.bvin, (bf16*)Wk.bvinc,
             z.VAL_IN, Wk.h, z.LSEQ, D, Wk.gd, R);
     a = lin_fwd(DT_F32, R, z.VAL_IN, 256, Wk.bvin, z.VAL_IN, f32w(M->w("value1_w"), z.VAL_IN),
                 Wk.bv1, 256, DT_F32);
@@ -669,31 +700,31 @@ static void tables_bwd(PtcgModel* M, cudaStream_t s) {
     // card LayerNorm (input card_in, ld 634) -> d_cardin
     {
         int rpb = 64;
-        k_ln_bwd<float><<<cdiv(z.NC, rpb), 256, 2 * 634 * sizeof(float), s>>>(t.d_cardin, 634, 0,
+        ++g_ptcg_launches, k_ln_bwd<float><<<cdiv(z.NC, rpb), 256, 2 * 634 * sizeof(float), s>>>(t.d_cardin, 634, 0,
             nullptr, 634, M->w("card_ln_w").g, M->w("card_ln_b").g, t.d_cardln, 634, t.card_in, 634,
             M->w("card_ln_w").p, t.ln_mu, t.ln_rs, z.NC, 634, rpb);
     }
-    k_slice_add<<<cdiv((long)z.NC * 64, TPB), TPB, 0, s>>>(M->w("card_id_emb").g, t.d_cardin,
+    ++g_ptcg_launches, k_slice_add<<<cdiv((long)z.NC * 64, TPB), TPB, 0, s>>>(M->w("card_id_emb").g, t.d_cardin,
         z.NC, 64, 634, 0);
-    k_pool_bwd<<<cdiv((long)z.NC * 64, TPB), TPB, 0, s>>>(t.d_att, t.d_cardin, 634, 250, 314,
+    ++g_ptcg_launches, k_pool_bwd<<<cdiv((long)z.NC * 64, TPB), TPB, 0, s>>>(t.d_att, t.d_cardin, 634, 250, 314,
         t.a_arg, M->card_attacks, z.NC, 4, 64);
-    k_pool_bwd<<<cdiv((long)z.NC * 128, TPB), TPB, 0, s>>>(t.d_sk, t.d_cardin, 634, 378, 506,
+    ++g_ptcg_launches, k_pool_bwd<<<cdiv((long)z.NC * 128, TPB), TPB, 0, s>>>(t.d_sk, t.d_cardin, 634, 378, 506,
         t.s_arg, M->card_skills, z.NC, 2, 128);
     // attack mlp
-    k_gelu_bwd<<<cdiv((long)z.NA * 64, TPB), TPB, 0, s>>>(t.d_att, t.att_pre, (long)z.NA * 64);
+    ++g_ptcg_launches, k_gelu_bwd<<<cdiv((long)z.NA * 64, TPB), TPB, 0, s>>>(t.d_att, t.att_pre, (long)z.NA * 64);
     colsum<float>(M->w("attack_mlp_b").g, t.d_att, 64, z.NA, 64, s);
     gemm_simt(lin_dw(DT_F32, z.NA, 127, 64, t.d_att, 64, t.att_in, 127, M->w("attack_mlp_w").g), s);
     gemm_simt(lin_dx(DT_F32, z.NA, 127, 64, t.d_att, 64, f32w(M->w("attack_mlp_w"), 127),
                      t.d_attin, 127, DT_F32), s);
-    k_slice_add<<<cdiv((long)z.NA * 48, TPB), TPB, 0, s>>>(M->w("attack_id_emb").g, t.d_attin,
+    ++g_ptcg_launches, k_slice_add<<<cdiv((long)z.NA * 48, TPB), TPB, 0, s>>>(M->w("attack_id_emb").g, t.d_attin,
         z.NA, 48, 127, 0);
     // skill mlp
-    k_gelu_bwd<<<cdiv((long)z.NS * 128, TPB), TPB, 0, s>>>(t.d_sk, t.sk_pre, (long)z.NS * 128);
+    ++g_ptcg_launches, k_gelu_bwd<<<cdiv((long)z.NS * 128, TPB), TPB, 0, s>>>(t.d_sk, t.sk_pre, (long)z.NS * 128);
     colsum<float>(M->w("skill_mlp_b").g, t.d_sk, 128, z.NS, 128, s);
     gemm_simt(lin_dw(DT_F32, z.NS, 112, 128, t.d_sk, 128, t.sk_in, 112, M->w("skill_mlp_w").g), s);
     gemm_simt(lin_dx(DT_F32, z.NS, 112, 128, t.d_sk, 128, f32w(M->w("skill_mlp_w"), 112),
                      t.d_skin, 112, DT_F32), s);
-    k_slice_add<<<cdiv((long)z.NS * 48, TPB), TPB, 0, s>>>(M->w("skill_id_emb").g, t.d_skin,
+    ++g_ptcg_launches, k_slice_add<<<cdiv((long)z.NS * 48, TPB), TPB, 0, s>>>(M->w("skill_id_emb").g, t.d_skin,
         z.NS, 48, 112, 0);
 }
 
@@ -724,10 +755,10 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     // ---- aux: opponent-hand counts
     float hscale = 0.1f / ((float)norm_rows * (float)z.NC);
     if (bf)
-        k_hand_grad<bf16><<<R, 256, z.NC * sizeof(float), s>>>((bf16*)Wk.dhand, z.NC, Wk.hand_lin,
+        ++g_ptcg_launches, k_hand_grad<bf16><<<R, 256, z.NC * sizeof(float), s>>>((bf16*)Wk.dhand, z.NC, Wk.hand_lin,
             z.NC, obs, ol, hscale, aux_loss + 1);
     else
-        k_hand_grad<float><<<R, 256, z.NC * sizeof(float), s>>>((float*)Wk.dhand, z.NC, Wk.hand_lin,
+        ++g_ptcg_launches, k_hand_grad<float><<<R, 256, z.NC * sizeof(float), s>>>((float*)Wk.dhand, z.NC, Wk.hand_lin,
             z.NC, obs, ol, hscale, aux_loss + 1);
     W wh = M->w("aux_hand_w");
     colsum<float>(M->w("aux_hand_b").g, Wk.hand_lin, z.NC, R, z.NC, s);   // fp32 grad copy
@@ -737,7 +768,7 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     // ---- aux: blind V (0.5 * mean (v - R)^2)
     {
         int rpb = 64;
-        k_rowdot_bwd<float, float><<<cdiv(R, rpb), 256, (256 + 1) * sizeof(float), s>>>(
+        ++g_ptcg_launches, k_rowdot_bwd<float, float><<<cdiv(R, rpb), 256, (256 + 1) * sizeof(float), s>>>(
             Wk.d_v1pre, 256, Wk.bv1pre, 256, Wk.bv1, 256, M->w("value2_w").p, M->w("value2_w").g,
             M->w("value2_b").g, Wk.blind_v, 1, returns, 1.0f / (float)norm_rows, R, 256, rpb,
             aux_loss + 0, M->w("value1_b").g);
@@ -750,15 +781,15 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
         a.accumulate = 1;
         gemm_simt(a, s);
     }
-    k_val_in_bwd<<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.dh, z.LSEQ, D, Wk.dgd, Wk.dbvin, R, 1);
+    ++g_ptcg_launches, k_val_in_bwd<<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.dh, z.LSEQ, D, Wk.dgd, Wk.dbvin, R, 1);
     // ---- aux: prize BCE over MY_UNSEEN tokens
-    k_prize_bwd<<<cdiv((long)R * z.LTOK, 8), 256, 0, s>>>(Wk.dh, M->w("aux_prize_w").g,
+    ++g_ptcg_launches, k_prize_bwd<<<cdiv((long)R * z.LTOK, 8), 256, 0, s>>>(Wk.dh, M->w("aux_prize_w").g,
         M->w("aux_prize_b").g, Wk.prize_logit, Wk.h, M->w("aux_prize_w").p, obs, ol, prize_cnt_dev,
         prize_cnt_host, D, R, aux_loss + 2);
     // ---- oracle value head (PPO value grad = grad[:, NOPT])
     {
         int rpb = 64;
-        k_rowdot_bwd<float, float><<<cdiv(R, rpb), 256, (256 + 1) * sizeof(float), s>>>(
+        ++g_ptcg_launches, k_rowdot_bwd<float, float><<<cdiv(R, rpb), 256, (256 + 1) * sizeof(float), s>>>(
             Wk.d_v1pre, 256, Wk.ov1pre, 256, Wk.ov1, 256, M->w("oracle_v2_w").p,
             M->w("oracle_v2_w").g, M->w("oracle_v2_b").g, grad + z.NOPT, z.NOPT + 1, nullptr, 0.f,
             R, 256, rpb, nullptr, M->w("oracle_v1_b").g);
@@ -769,33 +800,33 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
                      Wk.dbvin, z.VAL_IN, DT_F32), s);
     long NC_ = (long)R * z.LCRIT;
     cudaMemsetAsync(Wk.dx, 0, NC_ * D * 4, s);
-    k_val_in_bwd<<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.dx, z.LCRIT, D, Wk.dgd, Wk.dbvin, R, 1);
-    if (bf) k_cast<bf16><<<cdiv(NC_ * D, TPB), TPB, 0, s>>>((bf16*)Wk.dxc, D, Wk.dx, D, (int)NC_, D);
+    ++g_ptcg_launches, k_val_in_bwd<<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.dx, z.LCRIT, D, Wk.dgd, Wk.dbvin, R, 1);
+    if (bf) ++g_ptcg_launches, k_cast<bf16><<<cdiv(NC_ * D, TPB), TPB, 0, s>>>((bf16*)Wk.dxc, D, Wk.dx, D, (int)NC_, D);
     // ---- critic block
     block_bwd(M, M->blk("c0_"), Wk.cblk, Wk.ckeep, Wk, R, z.LCRIT, s);
     long nxc = NC_ * D;
     if (bf)
-        k_xc_bwd<bf16><<<cdiv(nxc, TPB), TPB, 0, s>>>(M->w("critic_readout").g, Wk.dh, (bf16*)Wk.dotok,
+        ++g_ptcg_launches, k_xc_bwd<bf16><<<cdiv(nxc, TPB), TPB, 0, s>>>(M->w("critic_readout").g, Wk.dh, (bf16*)Wk.dotok,
             Wk.dx, z.LSEQ, z.LCRIT, D, R);
     else
-        k_xc_bwd<float><<<cdiv(nxc, TPB), TPB, 0, s>>>(M->w("critic_readout").g, Wk.dh,
+        ++g_ptcg_launches, k_xc_bwd<float><<<cdiv(nxc, TPB), TPB, 0, s>>>(M->w("critic_readout").g, Wk.dh,
             (float*)Wk.dotok, Wk.dx, z.LSEQ, z.LCRIT, D, R);
     W wo = M->w("oracle_proj_w");
     {   // oracle_proj bias grad: fp32 sum of the critic-input grad rows 1+LSEQ..
         int gpb = 64;
         dim3 g(cdiv(D, 128), cdiv(R, gpb));
-        k_colsum_groups<<<g, 128, 0, s>>>(M->w("oracle_proj_b").g, Wk.dx, D, R, z.LCRIT,
+        ++g_ptcg_launches, k_colsum_groups<<<g, 128, 0, s>>>(M->w("oracle_proj_b").g, Wk.dx, D, R, z.LCRIT,
                                           1 + z.LSEQ, 56, D, gpb);
     }
     gemm(M, lin_dw(dt, R * 56, 134, D, Wk.dotok, D, Wk.otokin, rup(134, 8), wo.g), s);
     gemm(M, lin_dx(dt, R * 56, 134, D, Wk.dotok, D, wo, Wk.dotokin, 134, DT_F32), s);
-    k_otok_bwd<<<cdiv((long)R * 56 * 128, TPB), TPB, 0, s>>>(t.d_cv, Wk.dotokin, 134, obs, ol, R);
+    ++g_ptcg_launches, k_otok_bwd<<<cdiv((long)R * 56 * 128, TPB), TPB, 0, s>>>(t.d_cv, Wk.dotokin, 134, obs, ol, R);
     // ---- option scorer (d scores = grad[:, :NOPT])
-    k_scale_copy<<<cdiv(NO, TPB), TPB, 0, s>>>(Wk.dscores, z.NOPT, grad, z.NOPT + 1, R, z.NOPT, 1.f);
+    ++g_ptcg_launches, k_scale_copy<<<cdiv(NO, TPB), TPB, 0, s>>>(Wk.dscores, z.NOPT, grad, z.NOPT + 1, R, z.NOPT, 1.f);
     {
         int rpb = 64;
         unsigned g = cdiv(NO, rpb);
-        k_rowdot_bwd<float, float><<<g, 256, 257 * sizeof(float), s>>>((float*)Wk.ds1pre, 256,
+        ++g_ptcg_launches, k_rowdot_bwd<float, float><<<g, 256, 257 * sizeof(float), s>>>((float*)Wk.ds1pre, 256,
                 (const float*)Wk.s1pre, 256, (const float*)Wk.s1, 256, M->w("score2_w").p,
                 M->w("score2_w").g, M->w("score2_b").g, Wk.dscores, 1, nullptr, 0.f, (int)NO, 256,
                 rpb, nullptr, M->w("score1_b").g);
@@ -809,7 +840,7 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
         a.allow_tf32 = tf32;
         gemm(M, a, s);
     }
-    k_sc_in_bwd<float><<<R, 256, 0, s>>>((float*)Wk.dq, D, Wk.dh, Wk.dgd, Wk.dscin, z.SCORE_IN,
+    ++g_ptcg_launches, k_sc_in_bwd<float><<<R, 256, 0, s>>>((float*)Wk.dq, D, Wk.dh, Wk.dgd, Wk.dscin, z.SCORE_IN,
             Wk.q, Wk.h, D, z.LSEQ, z.NOPT, M->w("q2_b").g);
     W wq2 = f32w(M->w("q2_w"), D), wq1 = f32w(M->w("q1_w"), z.Q_IN);
     {
@@ -830,7 +861,7 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
         a.allow_tf32 = tf32;
         gemm(M, a, s);
     }
-    k_q_in_bwd<<<cdiv(NO * z.Q_IN, TPB), TPB, 0, s>>>(M->w("opt_type_emb").g, Wk.dh, t.d_poc,
+    ++g_ptcg_launches, k_q_in_bwd<<<cdiv(NO * z.Q_IN, TPB), TPB, 0, s>>>(M->w("opt_type_emb").g, Wk.dh, t.d_poc,
         t.d_poa, Wk.dqin, z.Q_IN, obs, ol, D, R, z.Q_IN);
     // opt_card / opt_attack per-table-row projections -> table grads
     colsum<float>(M->w("opt_card_b").g, t.d_poc, 64, z.NC, 64, s);
@@ -862,15 +893,15 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     }
     // ---- x0 split, token projection, broadcast
     if (bf)
-        k_x0_bwd<bf16><<<R, 256, 0, s>>>(M->w("readout").g, (bf16*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D);
+        ++g_ptcg_launches, k_x0_bwd<bf16><<<R, 256, 0, s>>>(M->w("readout").g, (bf16*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D);
     else
-        k_x0_bwd<float><<<R, 256, 0, s>>>(M->w("readout").g, (float*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D);
+        ++g_ptcg_launches, k_x0_bwd<float><<<R, 256, 0, s>>>(M->w("readout").g, (float*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D);
     W wt = M->w("token_proj_w");
     long ldtok = rup(z.TOK_IN, 8);
     colsum<float>(M->w("token_proj_b").g, Wk.dbc, D, R, D, s);
     gemm(M, lin_dw(dt, R * z.LTOK, z.TOK_IN, D, Wk.dtokp, D, Wk.tokcat, ldtok, wt.g), s);
     gemm(M, lin_dx(dt, R * z.LTOK, z.TOK_IN, D, Wk.dtokp, D, wt, Wk.dtokcat, z.TOK_IN, DT_F32), s);
-    k_tok_cat_bwd<<<cdiv((long)R * z.LTOK * z.TOK_IN, TPB), TPB, 0, s>>>(t.d_cv, M->w("zone_emb").g,
+    ++g_ptcg_launches, k_tok_cat_bwd<<<cdiv((long)R * z.LTOK * z.TOK_IN, TPB), TPB, 0, s>>>(t.d_cv, M->w("zone_emb").g,
         M->w("owner_emb").g, Wk.dtokcat, z.TOK_IN, obs, ol, R, z.TOK_IN);
     colsum<float>(M->w("bcast_b").g, Wk.dbc, D, R, D, s);
     gemm_simt(lin_dw(DT_F32, R, 192, D, Wk.dbc, D, Wk.gd, 192, M->w("bcast_w").g), s);
@@ -892,7 +923,7 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     gemm_simt(lin_dw(DT_F32, R, 696, 64, Wk.dd1, 64, Wk.decin, 696, M->w("dec1_w").g), s);
     gemm_simt(lin_dx(DT_F32, R, 696, 64, Wk.dd1, 64, f32w(M->w("dec1_w"), 696), Wk.ddecin, 696,
                      DT_F32), s);
-    k_dec_in_bwd<<<cdiv((long)R * 696, TPB), TPB, 0, s>>>(t.d_cv, t.d_att, M->w("sel_type_emb").g,
+    ++g_ptcg_launches, k_dec_in_bwd<<<cdiv((long)R * 696, TPB), TPB, 0, s>>>(t.d_cv, t.d_att, M->w("sel_type_emb").g,
         M->w("ctx_emb").g, Wk.ddecin, obs, ol, R);
     // ---- global encoder
     colsum<float>(M->w("global2_b").g, Wk.dgd, 192, R, 128, s);
@@ -1116,7 +1147,7 @@ int ptcg_set_tables(PtcgModel* M, const float* card_static, const int* card_atta
 static int refresh_copies(PtcgModel* M, cudaStream_t s) {
     if (M->copies.empty()) return PTCG_OK;
     dim3 g(64, (unsigned)M->copies.size());
-    k_refresh_copies<<<g, 256, 0, s>>>(M->params, M->d_copies, (int)M->copies.size());
+    ++g_ptcg_launches, k_refresh_copies<<<g, 256, 0, s>>>(M->params, M->d_copies, (int)M->copies.size());
     CKL();
     return PTCG_OK;
 }
@@ -1235,7 +1266,7 @@ int ptcg_backward(PtcgModel* M, const float* grad, const float* returns, int aux
     CK(cudaMemsetAsync(aux, 0, 3 * sizeof(float), s));
     if (prize_count <= 0.f) {
         CK(cudaMemsetAsync(cnt, 0, sizeof(float), s));
-        k_count_unseen<<<64, 256, 0, s>>>(cnt, M->trn_last_obs, M->z.ol, R);
+        ++g_ptcg_launches, k_count_unseen<<<64, 256, 0, s>>>(cnt, M->trn_last_obs, M->z.ol, R);
     }
     if (!accumulate) CK(cudaMemsetAsync(M->grads, 0, (size_t)M->n_arena * 4, s));
     zero_table_grads(M, s);
@@ -1260,12 +1291,12 @@ int ptcg_ppo_loss(const float* dec_out, int nopt, const float* mask, const float
     int nt = n_seg * horizon;
     float* adv_stats = scratch;
     float* partials = scratch + 16;
-    k_adv_stats<<<1, 1024, 0, s>>>(adv_stats, advantages, nt);
+    ++g_ptcg_launches, k_adv_stats<<<1, 1024, 0, s>>>(adv_stats, advantages, nt);
     unsigned g = cdiv(nt, PPO_ROWS_PER_BLOCK);
-    k_ppo_loss<<<g, PPO_ROWS_PER_BLOCK * 32, 0, s>>>(dec_out, nopt, mask, nopt, actions, old_logp,
+    ++g_ptcg_launches, k_ppo_loss<<<g, PPO_ROWS_PER_BLOCK * 32, 0, s>>>(dec_out, nopt, mask, nopt, actions, old_logp,
         advantages, values, returns, prio, horizon, 0, nt, nt, adv_stats, clip_coef, vf_clip_coef,
         vf_coef, ent_coef, grad_dec, new_logp, ratio, partials);
-    k_ppo_reduce<<<1, 32, 0, s>>>(stats, partials, (int)g, adv_stats, 0);
+    ++g_ptcg_launches, k_ppo_reduce<<<1, 32, 0, s>>>(stats, partials, (int)g, adv_stats, 0);
     CKL();
     return PTCG_OK;
 }
@@ -1273,11 +1304,11 @@ int ptcg_ppo_loss(const float* dec_out, int nopt, const float* mask, const float
 static int adam_impl(PtcgModel* M, float lr, float b1, float b2, float eps, float max_norm,
                      const float* gate, float* stats, cudaStream_t s) {
     float* st = stats ? stats : M->d_misc + 32;
-    k_sumsq<<<M->sumsq_grid, 256, 0, s>>>(M->d_partials, M->grads, M->n_arena);
-    k_adam<<<M->adam_grid, 256, 0, s>>>(M->params, M->am, M->av, M->grads, M->n_arena,
+    ++g_ptcg_launches, k_sumsq<<<M->sumsq_grid, 256, 0, s>>>(M->d_partials, M->grads, M->n_arena);
+    ++g_ptcg_launches, k_adam<<<M->adam_grid, 256, 0, s>>>(M->params, M->am, M->av, M->grads, M->n_arena,
         M->d_partials, M->sumsq_grid, lr, b1, b2, eps, max_norm, M->step_dev, gate, st,
         M->d_copies, (int)M->copies.size(), M->d_chunk_copy, M->adam_chunk);
-    k_step_inc<<<1, 1, 0, s>>>(M->step_dev, st);
+    ++g_ptcg_launches, k_step_inc<<<1, 1, 0, s>>>(M->step_dev, st);
     CKL();
     return PTCG_OK;
 }
@@ -1296,7 +1327,7 @@ int ptcg_sample_logits(const float* dec_out, int n, int nopt, const float* mask,
     REQ(dec_out && mask && uniforms && actions && logprobs && values, PTCG_EINVAL, "null argument");
     REQ(n >= 0 && nopt > 0 && mask_stride >= nopt, PTCG_EINVAL, "bad sizes");
     if (n == 0) return PTCG_OK;
-    k_sample<<<cdiv(n, 8), 256, 0, (cudaStream_t)stream>>>(dec_out, n, nopt, mask, mask_stride,
+    ++g_ptcg_launches, k_sample<<<cdiv(n, 8), 256, 0, (cudaStream_t)stream>>>(dec_out, n, nopt, mask, mask_stride,
         uniforms, actions, logprobs, values);
     CKL();
     return PTCG_OK;
@@ -1308,7 +1339,7 @@ int ptcg_puff_advantage(const float* values, const float* rewards, const float* 
                         float* advantages, void* stream) {
     REQ(values && rewards && dones && importance && obs && advantages, PTCG_EINVAL, "null argument");
     REQ(B > 0 && T > 0 && seat_col >= 0 && seat_col < obs_size, PTCG_EINVAL, "bad sizes");
-    k_negamax_adv<<<cdiv(B, 128), 128, 0, (cudaStream_t)stream>>>(values, rewards, dones,
+    ++g_ptcg_launches, k_negamax_adv<<<cdiv(B, 128), 128, 0, (cudaStream_t)stream>>>(values, rewards, dones,
         importance, obs, obs_size, seat_col, advantages, gamma, lambda, rho_clip, c_clip, B, T);
     CKL();
     return PTCG_OK;
@@ -1341,8 +1372,8 @@ int ptcg_train_step(PtcgModel* M, const float* obs, const float* actions, const 
     float* cnt = M->d_misc + 2;
     CK(cudaMemsetAsync(stats, 0, 16 * sizeof(float), s));
     CK(cudaMemsetAsync(cnt, 0, sizeof(float), s));
-    k_adv_stats<<<1, 1024, 0, s>>>(adv_stats, advantages, nt);
-    k_count_unseen<<<128, 256, 0, s>>>(cnt, obs, z.ol, nt);
+    ++g_ptcg_launches, k_adv_stats<<<1, 1024, 0, s>>>(adv_stats, advantages, nt);
+    ++g_ptcg_launches, k_count_unseen<<<128, 256, 0, s>>>(cnt, obs, z.ol, nt);
     CK(cudaMemsetAsync(M->grads, 0, (size_t)M->n_arena * 4, s));
     zero_table_grads(M, s);
     tables_fwd(M, s);
@@ -1352,11 +1383,11 @@ int ptcg_train_step(PtcgModel* M, const float* obs, const float* actions, const 
         const float* ob = obs + (long)r0 * z.ol.obs;
         forward_impl(M, Wk, ob, rows, Wk.fused, true, false, s);
         unsigned g = cdiv(rows, PPO_ROWS_PER_BLOCK);
-        k_ppo_loss<<<g, PPO_ROWS_PER_BLOCK * 32, 0, s>>>(Wk.fused, z.NOPT, ob + z.ol.mask, z.ol.obs,
+        ++g_ptcg_launches, k_ppo_loss<<<g, PPO_ROWS_PER_BLOCK * 32, 0, s>>>(Wk.fused, z.NOPT, ob + z.ol.mask, z.ol.obs,
             actions + r0, old_logp + r0, advantages + r0, values + r0, returns + r0, prio, horizon,
             r0, rows, nt, adv_stats, clip_coef, vf_clip_coef, vf_coef, ent_coef, Wk.dgrad, Wk.nlp,
             Wk.ratio, Wk.ppo_scratch);
-        k_ppo_reduce<<<1, 32, 0, s>>>(stats, Wk.ppo_scratch, (int)g, adv_stats, 1);
+        ++g_ptcg_launches, k_ppo_reduce<<<1, 32, 0, s>>>(stats, Wk.ppo_scratch, (int)g, adv_stats, 1);
         backward_impl(M, Wk, ob, Wk.dgrad, returns + r0, rows, nt, cnt, 0.f, stats + 10,
                       mb == nmb - 1, s);
     }
@@ -1401,11 +1432,33 @@ int ptcg_set_step(PtcgModel* M, long step) {
     return PTCG_OK;
 }
 
+long long ptcg_launch_count(void) { return g_ptcg_launches; }
+
+int ptcg_kernel_timer(PtcgModel* M, int mode) {
+    REQ(M && mode >= 0 && mode <= 2, PTCG_EINVAL, "bad arguments");
+    M->kt.mode = mode; M->kt.used = 0; M->kt.flops = 0; M->kt.launches = 0;
+    return PTCG_OK;
+}
+
+int ptcg_kernel_timer_read(PtcgModel* M, double* ms, long* launches, double* flops) {
+    REQ(M && ms && launches && flops, PTCG_EINVAL, "null argument");
+    CK(cudaSetDevice(M->dev));
+    double t = 0.0;
+    for (int i = 0; i + 1 < M->kt.used; i += 2) {
+        float e = 0.f;
+        CK(cudaEventSynchronize(M->kt.ev[i + 1]));
+        CK(cudaEventElapsedTime(&e, M->kt.ev[i], M->kt.ev[i + 1]));
+        t += e;
+    }
+    *ms = t; *launches = M->kt.launches; *flops = M->kt.flops;
+    return PTCG_OK;
+}
+
 int ptcg_weights_checksum(PtcgModel* M, unsigned int* out_dev, void* stream) {
     REQ(M && out_dev, PTCG_EINVAL, "null argument");
     cudaStream_t s = (cudaStream_t)stream;
     CK(cudaMemsetAsync(out_dev, 0, 8, s));
-    k_checksum<<<256, 256, 0, s>>>(out_dev, M->params, M->n_arena);
+    ++g_ptcg_launches, k_checksum<<<256, 256, 0, s>>>(out_dev, M->params, M->n_arena);
     CKL();
     return PTCG_OK;
 }

@@ -63,6 +63,10 @@ _SIGS = {
     "ptcg_get_step": (I, [P, C.POINTER(C.c_long)]),
     "ptcg_set_step": (I, [P, L]),
     "ptcg_weights_checksum": (I, [P, P, P]),
+    "ptcg_kernel_timer": (I, [P, I]),
+    "ptcg_launch_count": (C.c_longlong, []),
+    "ptcg_kernel_timer_read": (I, [P, C.POINTER(C.c_double), C.POINTER(C.c_long),
+                                   C.POINTER(C.c_double)]),
 }
 
 _lib = None

@@ -239,6 +239,15 @@ class PTCGPolicy:
                                        _stream()))
         return stats
 
+    def kernel_timer(self, mode):
+        """mode 1 = tcgen05 GEMM, 2 = SIMT GEMM, 0 = off (resets counters)."""
+        check(self.lib.ptcg_kernel_timer(self.h, int(mode)))
+
+    def kernel_timer_read(self):
+        ms, n, fl = C.c_double(), C.c_long(), C.c_double()
+        check(self.lib.ptcg_kernel_timer_read(self.h, C.byref(ms), C.byref(n), C.byref(fl)))
+        return ms.value, n.value, fl.value
+
     def weights_checksum(self):
         out = torch.zeros(4, dtype=torch.int32, device=self.device)
         check(self.lib.ptcg_weights_checksum(self.h, _p(out), _stream()))

@@ -113,6 +113,71 @@ def make_obs(s: Shape, n: int, seed: int, edge: bool = False) -> np.ndarray:
     return obs
 
 
+def make_obs_batch(s: Shape, n: int, seed: int) -> np.ndarray:
+    """Vectorised `make_obs` (same distributions, its own random stream) for
+    minibatch-sized inputs."""
+    rng = np.random.default_rng(seed)
+    off = s.offsets
+    obs = np.zeros((n, s.obs_size), np.float32)
+    lo = int(np.ceil(0.6 * s.ltok))
+    hi = max(lo, int(np.floor(0.9 * s.ltok)))
+    nv = rng.integers(lo, hi + 1, n)
+    valid = np.arange(s.ltok)[None, :] < nv[:, None]                  # (n, ltok)
+    ti = np.zeros((n, s.ltok, TOK_INT), np.float32)
+    ti[:, :, 0] = rng.integers(0, s.n_cards, (n, s.ltok))
+    ti[:, :, 1] = rng.integers(1, N_ZONES, (n, s.ltok))
+    ti[:, :, 2] = rng.integers(0, 2, (n, s.ltok))
+    for c in (3, 4):
+        t = rng.integers(1, s.n_cards, (n, s.ltok))
+        t[rng.random((n, s.ltok)) < 0.5] = 0
+        ti[:, :, c] = t
+    ti *= valid[:, :, None]
+    tf = rng.standard_normal((n, s.ltok, s.tok_f)).astype(np.float32) * valid[:, :, None]
+    oi = np.zeros((n, s.nopt, OPT_INT), np.float32)
+    oi[:, :, 0] = rng.integers(0, N_OPT_TYPES, (n, s.nopt))
+    for c in (1, 2):
+        p = np.floor(rng.random((n, s.nopt)) * nv[:, None]).astype(np.int64) + 1
+        p[rng.random((n, s.nopt)) < 0.3] = 0
+        oi[:, :, c] = p
+    oi[:, :, 3] = rng.integers(0, s.n_cards, (n, s.nopt))
+    oi[:, :, 4] = rng.integers(0, s.n_attacks, (n, s.nopt))
+    oi[:, :, 5] = rng.integers(0, 30, (n, s.nopt))
+    of = rng.standard_normal((n, s.nopt, OPT_F)).astype(np.float32)
+    k = rng.integers(1, s.nopt + 1, n)
+    rank = np.argsort(rng.random((n, s.nopt)), axis=1).argsort(axis=1)
+    mask = (rank < k[:, None]).astype(np.float32)                      # k random legal slots
+    gf = rng.standard_normal((n, GLOBAL_F)).astype(np.float32)
+    gf[:, SEAT_GLOBAL_IDX] = rng.integers(0, 2, n)
+    gf[:, 54] = 0.0
+    di = np.stack([rng.integers(0, N_SELECT_TYPES, n), rng.integers(0, N_CONTEXTS, n),
+                   rng.integers(0, s.n_cards, n), rng.integers(0, s.n_cards, n),
+                   rng.integers(0, s.n_attacks, n), rng.integers(0, s.n_attacks, n),
+                   rng.integers(0, s.n_cards, n), rng.integers(0, s.n_cards, n)],
+                  1).astype(np.float32)
+    dfl = rng.standard_normal((n, DEC_F)).astype(np.float32)
+    cnts = np.array([0.25, 0.5, 0.75, 1.0], np.float32)
+    parts = []
+    for nslot, nf in ((ORACLE_HAND, 1), (ORACLE_SPLIT, 2), (ORACLE_PRIZE, 1)):
+        ids = rng.integers(0, s.n_cards, (n, nslot)).astype(np.float32)
+        ids[rng.random((n, nslot)) < 0.3] = 0
+        f = cnts[rng.integers(0, 4, (n, nslot, nf))]
+        parts.append(np.concatenate([ids[:, :, None], f], 2).reshape(n, -1))
+    orc = np.concatenate(parts, 1)
+    for name, v in (("tok_int", ti), ("tok_float", tf), ("opt_int", oi), ("opt_float", of),
+                    ("opt_mask", mask), ("global_f", gf), ("dec_int", di),
+                    ("dec_float", dfl), ("oracle", orc)):
+        a, b = off[name]
+        obs[:, a:b] = v.reshape(n, -1)
+    return obs
+
+
+def sample_legal(mask: np.ndarray, seed: int) -> np.ndarray:
+    """One uniformly drawn legal slot per row (float32 action ids)."""
+    rng = np.random.default_rng(seed)
+    r = rng.random(mask.shape) * (mask != 0)
+    return r.argmax(1).astype(np.float32)
+
+
 def make_tables(s: Shape, seed: int):
     """Seeded stand-ins for the engine-derived static tables
     (ptcg/rl/cards.py:39-82) and the text-embedding channels

@@ -377,7 +377,7 @@ def train_grads(P, T, obs, s, actions, old_logp, adv, values, returns, prio,
     surrogate.backward()
     grads = {k: (p.grad if p.grad is not None else torch.zeros_like(p))
              for k, p in P.items()}
-    stats.update({"aux_" + k: float(v) for k, v in parts.items()})
+    stats.update({"aux_" + k: float(v.detach()) for k, v in parts.items()})
     return out, stats, grads
 
 
