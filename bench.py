@@ -422,7 +422,7 @@ def main():
 
 
 def _tc_available(pol):
-    return bool(getattr(pol.lib, "ptcg_tc_available", None) and pol.lib.ptcg_tc_available())
+    return bool(pol.lib.ptcg_tensor_cores())
 
 
 if __name__ == "__main__":

@@ -205,6 +205,20 @@ int ptcg_weights_checksum(PtcgModel* m, unsigned int* out_dev, void* stream);
 int ptcg_kernel_timer(PtcgModel* m, int mode);
 /* Number of CUDA kernels this library has launched in this process. */
 long long ptcg_launch_count(void);
+
+/* ---- GEMM engine (exposed for tests and tools) -----------------------------
+ * C[M,N] (+)= sum_k A(m,k) B(n,k) in fp32; A(m,k) = a_kmajor ? A[m*lda+k] :
+ * A[k*lda+m], likewise B.  operand_dtype PTCG_BF16 or PTCG_FP32.  engine:
+ * 0 auto, 1 tcgen05 only (PTCG_EINVAL if the shape is unsupported), 2 SIMT.
+ * The reference calls cuBLAS for every GEMM (native/model/ptcg_kernels.cuh:42-108). */
+int ptcg_gemm(int M, int N, int K, const void* A, long lda, int a_kmajor, const void* B,
+              long ldb, int b_kmajor, int operand_dtype, float* C, long ldc, int accumulate,
+              int engine, void* stream);
+/* 1 when the tcgen05 engine is usable on the current device (sm_100). */
+int ptcg_tensor_cores(void);
+/* First error code a bounded device-side wait recorded since the last call
+ * (0 = none; the kernel that timed out returned early).  Resets the flag. */
+int ptcg_device_error(void);
 int ptcg_kernel_timer_read(PtcgModel* m, double* ms, long* launches, double* flops);
 
 #ifdef __cplusplus

@@ -1,6 +1,550 @@
-// tcgen05 / TMEM / TMA GEMM for sm_100a (bf16 operands, fp32 accumulate).
+// tcgen05 / TMEM / TMA GEMM for sm_100a: bf16 operands, fp32 accumulation
+// in tensor memory, the fused epilogue of GemmArgs.
+//
+//   C[M, N] = epilogue( sum_k A(m, k) * B(n, k) )
+//
+// * CTA tile 128 x BN (BN <= 256, multiple of 16; multiple of 64 when B is
+//   MN-major), K block 64 elements (one 128-byte swizzled row).
+// * Operands arrive by TMA (cp.async.bulk.tensor, 128B swizzle, no
+//   multicast) into a multi-stage shared-memory ring.  K-major operands load
+//   one box {64 K, rows}; MN-major operands (the transposed side of dX / dW
+//   GEMMs) load boxes {64 MN, 64 K}, so no operand is ever transposed in HBM.
+// * One elected thread issues tcgen05.mma.cta_group::1.kind::f16 (M=128,
+//   N=BN, K=16 per instruction) into a double-buffered TMEM accumulator and
+//   releases ring slots with tcgen05.commit.
+// * Four epilogue warps (one per TMEM lane quadrant) read the accumulator
+//   with tcgen05.ld.32x32b.x32 while the next tile's MMAs run, and apply
+//   bias / broadcast / GELU / GELU' / row remap / residual / accumulate /
+//   fp32 column sums before vectorised global stores.
+// * Persistent CTAs (one per SM) walk an M-major tile order so that the
+//   N-tiles of one A row-block run together and share it through L2; weight
+//   gradients (long K) are split over K with fp32 atomic accumulation.
+// * Every wait is bounded by a clock budget; on expiry the CTA records an
+//   error code in g_tc_error, drains its own in-flight copies and MMAs,
+//   frees its TMEM and returns.
 #include "common.cuh"
 #include "internal.h"
 
-bool gemm_tc_available() { return false; }
-bool gemm_tc(const GemmArgs&, cudaStream_t) { return false; }
+#include <cuda.h>
+#include <mutex>
+#include <stdlib.h>
+#include <string.h>
+
+namespace {
+
+constexpr int BM = 128, BK = 64;
+constexpr int NUM_THREADS = 192;             // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr long long WAIT_BUDGET = 4000000000LL;   // clock cycles (~2 s)
+
+__device__ int g_tc_error_dev;
+
+struct TcParams {
+    int M, N, K;
+    int bn;                  // CTA tile N
+    int b_rows;              // B rows resident per stage (bn, or bn rounded to 64)
+    int a_mn, b_mn;          // operand majorness (1 = MN-major)
+    int m_tiles, n_tiles, splits, kb_total, kb_per_split;
+    int stages;
+    uint32_t idesc;
+    uint32_t stage_bytes, a_bytes;
+    uint32_t tmem_cols, acc_stride;
+    GemmArgs ep;
+};
+
+// ------------------------------------------------------------ PTX wrappers
+PTCG_DEV uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+PTCG_DEV void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count));
+}
+PTCG_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
+}
+PTCG_DEV void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(bar) : "memory");
+}
+PTCG_DEV bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred P;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, P;\n\t}"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// bounded wait: false (and the abort flag set) when the budget runs out
+PTCG_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int code) {
+    long long t0 = clock64();
+    while (!mbar_try(bar, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > WAIT_BUDGET) {
+            *abort_flag = 1;
+            atomicCAS(&g_tc_error_dev, 0, code);
+            return false;
+        }
+    }
+    return true;
+}
+PTCG_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%3, %4}], [%2];"
+                 :: "r"(dst), "l"((uint64_t)map), "r"(bar), "r"(x), "r"(y) : "memory");
+}
+PTCG_DEV void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+PTCG_DEV void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+PTCG_DEV void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                 :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc) : "memory");
+}
+PTCG_DEV void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(bar) : "memory");
+}
+PTCG_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                 "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                   "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+                   "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]),
+                   "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+                   "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+                   "=r"(r[30]), "=r"(r[31])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// UMMA shared-memory descriptor, 128-byte swizzle, sm_100 version bits
+PTCG_DEV uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;                  // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;                  // SWIZZLE_128B
+    return d;
+}
+
+
+// 32 consecutive values of one row: vectorised when the whole chunk is in
+// range and 16-byte aligned, scalar (with zero fill) otherwise
+PTCG_DEV void load32(float (&d)[32], const void* p, long base, int dt, int nvalid) {
+    if (dt == DT_F32) {
+        const float* q = (const float*)p + base;
+        if (nvalid == 32 && ((uintptr_t)q & 15) == 0) {
+            #pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+                float4 t = *(const float4*)(q + j);
+                d[j] = t.x; d[j + 1] = t.y; d[j + 2] = t.z; d[j + 3] = t.w;
+            }
+        } else {
+            #pragma unroll
+            for (int j = 0; j < 32; j++) d[j] = j < nvalid ? q[j] : 0.f;
+        }
+    } else {
+        const bf16* q = (const bf16*)p + base;
+        if (nvalid == 32 && ((uintptr_t)q & 15) == 0) {
+            #pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+                uint4 t = *(const uint4*)(q + j);
+                const __nv_bfloat162* h = (const __nv_bfloat162*)&t;
+                #pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    float2 f = __bfloat1622float2(h[k]);
+                    d[j + 2 * k] = f.x; d[j + 2 * k + 1] = f.y;
+                }
+            }
+        } else {
+            #pragma unroll
+            for (int j = 0; j < 32; j++) d[j] = j < nvalid ? __bfloat162float(q[j]) : 0.f;
+        }
+    }
+}
+PTCG_DEV void store32(void* p, long base, int dt, const float (&v)[32], int nvalid) {
+    if (dt == DT_F32) {
+        float* q = (float*)p + base;
+        if (nvalid == 32 && ((uintptr_t)q & 15) == 0) {
+            #pragma unroll
+            for (int j = 0; j < 32; j += 4) *(float4*)(q + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+            #pragma unroll
+            for (int j = 0; j < 32; j++) if (j < nvalid) q[j] = v[j];
+        }
+    } else {
+        bf16* q = (bf16*)p + base;
+        if (nvalid == 32 && ((uintptr_t)q & 15) == 0) {
+            #pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+                uint4 t;
+                __nv_bfloat162* h = (__nv_bfloat162*)&t;
+                #pragma unroll
+                for (int k = 0; k < 4; k++) h[k] = __floats2bfloat162_rn(v[j + 2 * k], v[j + 2 * k + 1]);
+                *(uint4*)(q + j) = t;
+            }
+        } else {
+            #pragma unroll
+            for (int j = 0; j < 32; j++) if (j < nvalid) q[j] = __float2bfloat16_rn(v[j]);
+        }
+    }
+}
+
+// lane l ends with sum over the warp's lanes of v[l]  (transpose-reduce)
+PTCG_DEV float warp_colsum32(float (&v)[32], int lane) {
+    #pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) {
+        bool up = lane & s;
+        #pragma unroll
+        for (int i = 0; i < s; i++) {
+            float send = up ? v[i] : v[i + s];
+            float keep = up ? v[i + s] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+        }
+    }
+    return v[0];
+}
+
+// -------------------------------------------------------------- the kernel
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+          const __grid_constant__ TcParams P) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const int S = P.stages;
+    uint64_t* bars = (uint64_t*)(smem + (size_t)S * P.stage_bytes);
+    // bars: full[S], empty[S], tfull[2], tempty[2], drain[1]
+    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * S + 5);
+    volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+    int* n_issued = (int*)(tmem_slot + 2);     // ring slots filled by TMA
+    int* n_consumed = (int*)(tmem_slot + 3);   // ring slots read by the MMA warp
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
+    const uint32_t tfull0 = smem_u32(bars + 2 * S), tempty0 = smem_u32(bars + 2 * S + 2);
+    const uint32_t drain = smem_u32(bars + 2 * S + 4);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; i++) { mbar_init(full0 + 8 * i, 1); mbar_init(empty0 + 8 * i, 1); }
+        for (int i = 0; i < 2; i++) { mbar_init(tfull0 + 8 * i, 1); mbar_init(tempty0 + 8 * i, 4); }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        *n_issued = 0;
+        *n_consumed = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(tmem_slot)), "r"(P.tmem_cols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int ntiles = P.m_tiles * P.n_tiles * P.splits;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                int split = t % P.splits;
+                int mn = t / P.splits;
+                int mt = mn / P.n_tiles, nt = mn % P.n_tiles;
+                int kb0 = split * P.kb_per_split;
+                int kb1 = min(P.kb_total, kb0 + P.kb_per_split);
+                for (int kb = kb0; kb < kb1; kb++) {
+                    if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, 1)) { ok = false; break; }
+                    uint32_t fb = full0 + 8 * stage;
+                    mbar_expect_tx(fb, P.stage_bytes);
+                    uint32_t sa = smem_u32(smem + (size_t)stage * P.stage_bytes);
+                    uint32_t sb = sa + P.a_bytes;
+                    int k0 = kb * BK;
+                    if (P.a_mn) {
+                        tma_load_2d(sa, &map_a, fb, mt * BM, k0);
+                        tma_load_2d(sa + 8192, &map_a, fb, mt * BM + 64, k0);
+                    } else {
+                        tma_load_2d(sa, &map_a, fb, k0, mt * BM);
+                    }
+                    if (P.b_mn) {
+                        for (int j = 0; j < P.b_rows / 64; j++)
+                            tma_load_2d(sb + j * 8192, &map_b, fb, nt * P.bn + 64 * j, k0);
+                    } else {
+                        tma_load_2d(sb, &map_b, fb, k0, nt * P.bn);
+                    }
+                    if (++stage == S) { stage = 0; phase ^= 1; }
+                    (*n_issued)++;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, local++) {
+                int split = t % P.splits;
+                int kb0 = split * P.kb_per_split;
+                int kb1 = min(P.kb_total, kb0 + P.kb_per_split);
+                int buf = local & 1;
+                uint32_t tph = (local >> 1) & 1;
+                if (!mbar_wait(tempty0 + 8 * buf, tph ^ 1, abort_flag, 2)) { ok = false; break; }
+                fence_after();
+                uint32_t dcol = tmem + buf * P.acc_stride;
+                for (int kb = kb0; kb < kb1; kb++) {
+                    if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, 3)) { ok = false; break; }
+                    fence_after();
+                    uint32_t sa = smem_u32(smem + (size_t)stage * P.stage_bytes);
+                    uint32_t sb = sa + P.a_bytes;
+                    #pragma unroll
+                    for (int s = 0; s < BK / 16; s++) {
+                        uint64_t ad = P.a_mn ? make_desc(sa + s * 2048, 8192, 1024)
+                                             : make_desc(sa + s * 32, 16, 1024);
+                        uint64_t bd = P.b_mn ? make_desc(sb + s * 2048, 8192, 1024)
+                                             : make_desc(sb + s * 32, 16, 1024);
+                        mma_f16(dcol, ad, bd, P.idesc, (kb > kb0 || s > 0) ? 1u : 0u);
+                    }
+                    mma_commit(empty0 + 8 * stage);
+                    if (++stage == S) { stage = 0; phase ^= 1; }
+                    (*n_consumed)++;
+                }
+                if (!ok) break;
+                mma_commit(tfull0 + 8 * buf);
+            }
+            // make sure no MMA is in flight before TMEM is released
+            mma_commit(drain);
+            long long t0 = clock64();
+            while (!mbar_try(drain, 0) && clock64() - t0 < WAIT_BUDGET) {}
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ epilogue warps
+        const int quad = warp & 3;           // TMEM lane quadrant this warp may read
+        const int row_in_tile = quad * 32 + lane;
+        const GemmArgs& a = P.ep;
+        int local = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, local++) {
+            int split = t % P.splits;
+            int mn = t / P.splits;
+            int mt = mn / P.n_tiles, nt = mn % P.n_tiles;
+            int buf = local & 1;
+            uint32_t tph = (local >> 1) & 1;
+            if (!mbar_wait(tfull0 + 8 * buf, tph, abort_flag, 4)) break;
+            fence_after();
+            const int m = mt * BM + row_in_tile;
+            const bool row_ok = m < a.M;
+            long orow = m;
+            if (a.remap_group > 0)
+                orow = (long)(m / a.remap_group) * a.remap_stride + a.remap_off + (m % a.remap_group);
+            const uint32_t tbase = tmem + buf * P.acc_stride + ((uint32_t)(quad * 32) << 16);
+            for (int c0 = 0; c0 < P.bn; c0 += 32) {
+                uint32_t r[32];
+                tmem_ld32(tbase + c0, r);
+                const int n0 = nt * P.bn + c0;
+                float v[32];
+                #pragma unroll
+                for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]) * a.alpha;
+                int nvalid = a.N - n0;
+                if (nvalid > P.bn - c0) nvalid = P.bn - c0;
+                if (nvalid > 32) nvalid = 32;
+                if (nvalid <= 0) continue;                       // warp-uniform
+                if (P.splits > 1) {                              // warp-uniform
+                    if (row_ok) {
+                        float* o = (float*)a.out + orow * a.ldo + n0;
+                        #pragma unroll
+                        for (int j = 0; j < 32; j++) if (j < nvalid) atomicAdd(o + j, v[j]);
+                    }
+                    continue;
+                }
+                if (row_ok) {
+                float t[32];
+                if (a.bias) {
+                    #pragma unroll
+                    for (int j = 0; j < 32; j++) v[j] += j < nvalid ? a.bias[n0 + j] : 0.f;
+                }
+                if (a.bcast) {
+                    load32(t, a.bcast, (long)(m / a.bcast_group) * a.ld_bcast + n0, DT_F32, nvalid);
+                    #pragma unroll
+                    for (int j = 0; j < 32; j++) v[j] += t[j];
+                }
+                if (a.act == ACT_GELU) {
+                    if (a.out2) store32(a.out2, (long)m * a.ldo2 + n0, a.out2_dtype, v, nvalid);
+                    #pragma unroll
+                    for (int j = 0; j < 32; j++) v[j] = gelu_f(v[j]);
+                } else if (a.act == ACT_GELU_BWD) {
+                    load32(t, a.aux, (long)m * a.ld_aux + n0, a.aux_dtype, nvalid);
+                    #pragma unroll
+                    for (int j = 0; j < 32; j++) v[j] *= gelu_grad_f(t[j]);
+                }
+                if (a.resid) {
+                    load32(t, a.resid, orow * a.ld_resid + n0, DT_F32, nvalid);
+                    #pragma unroll
+                    for (int j = 0; j < 32; j++) v[j] += t[j];
+                }
+                if (a.accumulate) {
+                    load32(t, a.out, orow * a.ldo + n0, a.out_dtype, nvalid);
+                    #pragma unroll
+                    for (int j = 0; j < 32; j++) v[j] += t[j];
+                }
+                store32(a.out, orow * a.ldo + n0, a.out_dtype, v, nvalid);
+                if (a.act != ACT_GELU && a.out2)
+                    store32(a.out2, orow * a.ldo2 + n0, a.out2_dtype, v, nvalid);
+                }   // row_ok
+                #pragma unroll
+                for (int j = 0; j < 32; j++) if (j >= nvalid || !row_ok) v[j] = 0.f;
+                if (a.colsum) {
+                    float cs = warp_colsum32(v, lane);
+                    if (lane < nvalid) atomicAdd(&a.colsum[n0 + lane], cs);
+                }
+            }
+            (void)split;
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
+        }
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    if (threadIdx.x == 0 && *n_consumed < *n_issued) {
+        // aborted: wait (bounded) for the copies still in flight into the ring
+        for (int i = *n_consumed; i < *n_issued; i++) {
+            long long t0 = clock64();
+            while (!mbar_try(full0 + 8 * (i % S), (uint32_t)((i / S) & 1)) &&
+                   clock64() - t0 < WAIT_BUDGET) {}
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+                     :: "r"(tmem), "r"(P.tmem_cols) : "memory");
+    }
+}
+
+// ---------------------------------------------------------- host side
+typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                             const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                             const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                             CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeFn g_encode = nullptr;
+int g_sms = 0;
+bool g_ok = false;
+std::once_flag g_once;
+
+void init_once() {
+    int dev = 0, major = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (major != 10) return;
+    // diagnostic engine selector: PTCG_GEMM_ENGINE=simt runs every GEMM on
+    // the SIMT kernel (numerical A/B comparisons); the default uses tcgen05
+    const char* eng = getenv("PTCG_GEMM_ENGINE");
+    if (eng && strcmp(eng, "simt") == 0) return;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+        return;
+    g_encode = (EncodeFn)fn;
+    int zero = 0;
+    cudaMemcpyToSymbol(g_tc_error_dev, &zero, sizeof(int));
+    g_ok = true;
+}
+
+// 2-D bf16 tensor map: inner extent `inner` (contiguous), `outer` rows,
+// row pitch ld elements, box {box_in, box_out}
+bool make_map(CUtensorMap* m, const void* ptr, long inner, long outer, long ld, int box_in,
+              int box_out) {
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {(cuuint32_t)box_in, (cuuint32_t)box_out};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+                          strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+int ptcg_tc_error_read_reset() {
+    int v = 0, zero = 0;
+    cudaMemcpyFromSymbol(&v, g_tc_error_dev, sizeof(int));
+    cudaMemcpyToSymbol(g_tc_error_dev, &zero, sizeof(int));
+    return v;
+}
+
+bool gemm_tc_available() {
+    std::call_once(g_once, init_once);
+    return g_ok;
+}
+
+bool gemm_tc(const GemmArgs& a, cudaStream_t s) {
+    if (!gemm_tc_available()) return false;
+    if (a.dtype != DT_BF16) return false;            // tf32 kind not wired yet
+    if (a.M <= 0 || a.N <= 0 || a.K <= 0) return a.M <= 0 || a.N <= 0;
+    // TMA: 16-byte aligned base and row pitch
+    if (((uintptr_t)a.A & 15) || ((uintptr_t)a.B & 15) || (a.lda % 8) || (a.ldb % 8)) return false;
+    // small problems stay on the SIMT kernel
+    if ((long)a.M * a.N * a.K < (1L << 22)) return false;
+
+    TcParams P;
+    P.M = a.M; P.N = a.N; P.K = a.K;
+    P.a_mn = !a.a_kmajor; P.b_mn = !a.b_kmajor;
+    int ntl = (a.N + 255) / 256;
+    int bn = ((a.N + ntl - 1) / ntl + 15) / 16 * 16;
+    if (P.b_mn) bn = (bn + 63) / 64 * 64;
+    if (bn > 256) bn = 256;
+    P.bn = bn;
+    P.b_rows = bn;
+    P.m_tiles = (a.M + BM - 1) / BM;
+    P.n_tiles = (a.N + bn - 1) / bn;
+    P.kb_total = (a.K + BK - 1) / BK;
+    int tiles = P.m_tiles * P.n_tiles;
+    P.splits = 1;
+    bool plain = a.accumulate && a.out_dtype == DT_F32 && !a.bias && !a.bcast &&
+                 a.act == ACT_NONE && !a.resid && !a.out2 && a.remap_group == 0 && !a.colsum;
+    if (plain && tiles < g_sms && P.kb_total >= 8) {
+        int want = (g_sms + tiles - 1) / tiles;
+        int maxs = P.kb_total / 4;
+        P.splits = want < maxs ? want : maxs;
+        if (P.splits < 1) P.splits = 1;
+    }
+    P.kb_per_split = (P.kb_total + P.splits - 1) / P.splits;
+    P.splits = (P.kb_total + P.kb_per_split - 1) / P.kb_per_split;   // no empty splits
+    P.a_bytes = BM * BK * 2;
+    P.stage_bytes = P.a_bytes + P.b_rows * BK * 2;
+    int budget = 200 * 1024;
+    P.stages = budget / P.stage_bytes;
+    if (P.stages > 6) P.stages = 6;
+    if (P.stages < 2) return false;
+    P.acc_stride = bn <= 128 ? 128 : 256;
+    P.tmem_cols = 2 * P.acc_stride;
+    // instruction descriptor: f32 accumulate, bf16 A/B, majorness, N>>3, M>>4
+    P.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)P.a_mn << 15) |
+              ((uint32_t)P.b_mn << 16) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+    P.ep = a;
+
+    CUtensorMap ma, mb;
+    bool ok;
+    if (P.a_mn) ok = make_map(&ma, a.A, a.M, a.K, a.lda, 64, BK);
+    else ok = make_map(&ma, a.A, a.K, a.M, a.lda, BK, BM);
+    if (!ok) return false;
+    if (P.b_mn) ok = make_map(&mb, a.B, a.N, a.K, a.ldb, 64, BK);
+    else ok = make_map(&mb, a.B, a.K, a.N, a.ldb, BK, bn);
+    if (!ok) return false;
+
+    size_t smem = 1024 + (size_t)P.stages * P.stage_bytes + (2 * P.stages + 5) * 8 + 32;
+    cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int total = P.m_tiles * P.n_tiles * P.splits;
+    int grid = total < g_sms ? total : g_sms;
+    ++g_ptcg_launches, k_gemm_tc<<<grid, NUM_THREADS, smem, s>>>(ma, mb, P);
+    return true;
+}

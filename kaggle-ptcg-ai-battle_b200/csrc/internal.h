@@ -43,6 +43,8 @@ void gemm_simt(const GemmArgs& a, cudaStream_t s);
 // back to the SIMT kernel, which is also sm_100a code in this library)
 bool gemm_tc(const GemmArgs& a, cudaStream_t s);
 bool gemm_tc_available();
+// first error code recorded by a tcgen05 kernel since the last call (0 = none)
+int ptcg_tc_error_read_reset();
 
 // attention over packed qkv rows: qkv [(n*L + l) * ldqkv + {0,D,2D} + h*32 + d]
 void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,

@@ -1434,6 +1434,32 @@ int ptcg_set_step(PtcgModel* M, long step) {
 
 long long ptcg_launch_count(void) { return g_ptcg_launches; }
 
+int ptcg_tensor_cores(void) { return gemm_tc_available() ? 1 : 0; }
+
+int ptcg_device_error(void) { return ptcg_tc_error_read_reset(); }
+
+int ptcg_gemm(int M, int N, int K, const void* A, long lda, int a_kmajor, const void* B, long ldb,
+              int b_kmajor, int operand_dtype, float* C, long ldc, int accumulate, int engine,
+              void* stream) {
+    REQ(A && B && C && M >= 0 && N >= 0 && K >= 0, PTCG_EINVAL, "bad arguments");
+    REQ(operand_dtype == PTCG_FP32 || operand_dtype == PTCG_BF16, PTCG_EINVAL, "bad dtype");
+    REQ(engine >= 0 && engine <= 2, PTCG_EINVAL, "bad engine");
+    GemmArgs a;
+    a.M = M; a.N = N; a.K = K; a.dtype = operand_dtype == PTCG_BF16 ? DT_BF16 : DT_F32;
+    a.A = A; a.lda = lda; a.a_kmajor = a_kmajor;
+    a.B = B; a.ldb = ldb; a.b_kmajor = b_kmajor;
+    a.out = C; a.ldo = ldc; a.out_dtype = DT_F32; a.accumulate = accumulate;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (engine == 2) { gemm_simt(a, s); CKL(); return PTCG_OK; }
+    bool done = gemm_tc_available() && gemm_tc(a, s);
+    if (!done) {
+        REQ(engine == 0, PTCG_EINVAL, "tcgen05 GEMM does not support this problem");
+        gemm_simt(a, s);
+    }
+    CKL();
+    return PTCG_OK;
+}
+
 int ptcg_kernel_timer(PtcgModel* M, int mode) {
     REQ(M && mode >= 0 && mode <= 2, PTCG_EINVAL, "bad arguments");
     M->kt.mode = mode; M->kt.used = 0; M->kt.flops = 0; M->kt.launches = 0;

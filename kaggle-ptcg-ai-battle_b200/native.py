@@ -65,6 +65,9 @@ _SIGS = {
     "ptcg_weights_checksum": (I, [P, P, P]),
     "ptcg_kernel_timer": (I, [P, I]),
     "ptcg_launch_count": (C.c_longlong, []),
+    "ptcg_tensor_cores": (I, []),
+    "ptcg_device_error": (I, []),
+    "ptcg_gemm": (I, [I, I, I, P, L, I, P, L, I, I, P, L, I, I, P]),
     "ptcg_kernel_timer_read": (I, [P, C.POINTER(C.c_double), C.POINTER(C.c_long),
                                    C.POINTER(C.c_double)]),
 }

@@ -11,7 +11,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 TOL = {"fp32": 1e-4, "bf16": 2e-2}
-ROWS = {"tiny": 9, "small": 12, "c0": 6, "default": 4, "c4": 2}
+ROWS = {"tiny": 9, "small": 12, "c0": 6, "default": 4, "c4": 6}
 
 
 def rel(a, b):
