@@ -209,11 +209,27 @@ long long ptcg_launch_count(void);
 /* ---- GEMM engine (exposed for tests and tools) -----------------------------
  * C[M,N] (+)= sum_k A(m,k) B(n,k) in fp32; A(m,k) = a_kmajor ? A[m*lda+k] :
  * A[k*lda+m], likewise B.  operand_dtype PTCG_BF16 or PTCG_FP32.  engine:
- * 0 auto, 1 tcgen05 only (PTCG_EINVAL if the shape is unsupported), 2 SIMT.
+ * 0 auto, 1 tcgen05 only (PTCG_EINVAL if the shape is unsupported), 2 SIMT,
+ * 3 tcgen05 with fp32 operands read as TF32 (kind::tf32).
  * The reference calls cuBLAS for every GEMM (native/model/ptcg_kernels.cuh:42-108). */
 int ptcg_gemm(int M, int N, int K, const void* A, long lda, int a_kmajor, const void* B,
               long ldb, int b_kmajor, int operand_dtype, float* C, long ldc, int accumulate,
               int engine, void* stream);
+/* Masked multi-head attention over packed QKV rows ([nseq*L, >=3*H*32], head
+ * h of q/k/v at columns h*32, H*32 + h*32, 2*H*32 + h*32), key mask keep
+ * [nseq, L] (0 = masked), head width 32, L <= 320.  Forward writes out
+ * [nseq*L, >=H*32] and the row log-sum-exp lse [nseq, H, L]; backward writes
+ * dqkv in the qkv layout and adds the fp32 column sums of dqkv into dbias
+ * (3*H*32 floats, may be NULL).  bf16 runs on tensor cores, fp32 is exact.
+ * Replaces the materialised-probability attention of the reference
+ * (pt_attn_softmax_fwd/bwd + batched GEMMs, native/model/ptcg_kernels.cuh:223-289,
+ * native/model/ptcg_model3.cu:12-95). */
+int ptcg_attention_fwd(int operand_dtype, const void* qkv, long ldqkv, const unsigned char* keep,
+                       void* out, long ldo, float* lse, int nseq, int L, int H, void* stream);
+int ptcg_attention_bwd(int operand_dtype, const void* qkv, long ldqkv, const unsigned char* keep,
+                       const void* out, long ldo, const void* dout, long lddo, const float* lse,
+                       void* dqkv, long lddqkv, float* dbias, int nseq, int L, int H,
+                       void* stream);
 /* 1 when the tcgen05 engine is usable on the current device (sm_100). */
 int ptcg_tensor_cores(void);
 /* First error code a bounded device-side wait recorded since the last call

@@ -175,6 +175,408 @@ __global__ void __launch_bounds__(NW * 32) k_attn_bwd(
     }
 }
 
+
+// ===================================================================== bf16
+// Tensor-core (mma.sync m16n8k16 bf16, fp32 accumulate) flash attention.
+// One CTA per (sequence, head); Q/K/V (and dO in backward) of the head are
+// staged in shared memory as [Lp][40] bf16 rows (80-byte pitch: conflict-free
+// ldmatrix).  Softmax runs in the exp2 domain; key blocks whose 16 keys are
+// all masked are skipped (their probabilities are exactly 0).
+constexpr int RS = 40;                      // smem row stride (elements)
+
+PTCG_DEV uint32_t s_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+PTCG_DEV void ldsm4(uint32_t (&r)[4], uint32_t a) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+PTCG_DEV void ldsm4t(uint32_t (&r)[4], uint32_t a) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+PTCG_DEV void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+                 "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+PTCG_DEV uint32_t pack2(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *(uint32_t*)&v;
+}
+// A fragment of the 16x16 block at (r0, c0) of a row-major [rows][RS] tile
+PTCG_DEV void lda(uint32_t (&a)[4], const bf16* X, int r0, int c0, int lane) {
+    int mi = lane >> 3;
+    ldsm4(a, s_addr(X + (r0 + (mi & 1) * 8 + (lane & 7)) * RS + c0 + (mi >> 1) * 8));
+}
+// B fragments (b[0],b[1] for n-tile 0; b[2],b[3] for n-tile 1) of B[k][n] =
+// X[n][k]: 16 n-rows starting n0, 16 k-cols starting k0
+PTCG_DEV void ldb_nk(uint32_t (&b)[4], const bf16* X, int n0, int k0, int lane) {
+    int mi = lane >> 3;
+    ldsm4(b, s_addr(X + (n0 + (mi >> 1) * 8 + (lane & 7)) * RS + k0 + (mi & 1) * 8));
+}
+// B fragments of B[k][n] = X[k][n]: 16 k-rows from k0, 16 n-cols from n0
+PTCG_DEV void ldb_kn(uint32_t (&b)[4], const bf16* X, int k0, int n0, int lane) {
+    int mi = lane >> 3;
+    ldsm4t(b, s_addr(X + (k0 + (mi & 1) * 8 + (lane & 7)) * RS + n0 + (mi >> 1) * 8));
+}
+
+// load rows [0, L) of a 32-wide head slice into smem (zero rows L..Lp)
+PTCG_DEV void stage_rows(bf16* dst, const bf16* src, long ld, int L, int Lp) {
+    for (int i = threadIdx.x; i < Lp * 4; i += blockDim.x) {
+        int r = i >> 2, c = (i & 3) * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < L) v = *(const uint4*)(src + (long)r * ld + c);
+        *(uint4*)(dst + r * RS + c) = v;
+    }
+}
+
+constexpr float LOG2E = 1.4426950408889634f;
+
+__global__ void __launch_bounds__(128) k_attn_fwd_mma(
+        const bf16* __restrict__ qkv, long ldqkv, const uint8_t* __restrict__ keep,
+        bf16* __restrict__ out, long ldo, float* __restrict__ lse, int L, int H) {
+    extern __shared__ __align__(16) uint8_t smraw[];
+    const int nh = blockIdx.x, n = nh / H, h = nh % H, D = H * DH;
+    const int Lp = (L + 15) & ~15, nkb = Lp / 16;
+    bf16* Qs = (bf16*)smraw;
+    bf16* Ks = Qs + Lp * RS;
+    bf16* Vs = Ks + Lp * RS;
+    float* kb_bias = (float*)(Vs + Lp * RS);        // [Lp] 0 or -inf (log2 domain)
+    int* kb_any = (int*)(kb_bias + Lp);             // [nkb] block has a kept key
+    const bf16* base = qkv + (long)n * L * ldqkv + h * DH;
+    stage_rows(Qs, base, ldqkv, L, Lp);
+    stage_rows(Ks, base + D, ldqkv, L, Lp);
+    stage_rows(Vs, base + 2 * D, ldqkv, L, Lp);
+    const uint8_t* kp = keep + (long)n * L;
+    for (int i = threadIdx.x; i < nkb; i += blockDim.x) kb_any[i] = 0;
+    __syncthreads();
+    for (int j = threadIdx.x; j < Lp; j += blockDim.x) {
+        bool k = j < L && kp[j];
+        kb_bias[j] = k ? 0.f : -INFINITY;
+        if (k) kb_any[j >> 4] = 1;
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const float sc = 0.17677669529663687f * LOG2E;
+    for (int qb = warp; qb < nkb; qb += 4) {
+        uint32_t qa[2][4];
+        lda(qa[0], Qs, qb * 16, 0, lane);
+        lda(qa[1], Qs, qb * 16, 16, lane);
+        float o[4][4];
+        #pragma unroll
+        for (int i = 0; i < 4; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+        float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+        for (int kb = 0; kb < nkb; kb++) {
+            if (!kb_any[kb]) continue;
+            float s[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+            #pragma unroll
+            for (int ks = 0; ks < 2; ks++) {
+                uint32_t b[4];
+                ldb_nk(b, Ks, kb * 16, ks * 16, lane);
+                mma(s[0], qa[ks], b[0], b[1]);
+                mma(s[1], qa[ks], b[2], b[3]);
+            }
+            float bias[2][2];
+            #pragma unroll
+            for (int nt = 0; nt < 2; nt++) {
+                bias[nt][0] = kb_bias[kb * 16 + nt * 8 + 2 * t];
+                bias[nt][1] = kb_bias[kb * 16 + nt * 8 + 2 * t + 1];
+            }
+            float bm0 = -INFINITY, bm1 = -INFINITY;
+            #pragma unroll
+            for (int nt = 0; nt < 2; nt++) {
+                s[nt][0] = s[nt][0] * sc + bias[nt][0];
+                s[nt][1] = s[nt][1] * sc + bias[nt][1];
+                s[nt][2] = s[nt][2] * sc + bias[nt][0];
+                s[nt][3] = s[nt][3] * sc + bias[nt][1];
+                bm0 = fmaxf(bm0, fmaxf(s[nt][0], s[nt][1]));
+                bm1 = fmaxf(bm1, fmaxf(s[nt][2], s[nt][3]));
+            }
+            bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, 1));
+            bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, 2));
+            bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, 1));
+            bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, 2));
+            float nm0 = fmaxf(m0, bm0), nm1 = fmaxf(m1, bm1);
+            float c0 = nm0 == -INFINITY ? 1.f : exp2f(m0 - nm0);
+            float c1 = nm1 == -INFINITY ? 1.f : exp2f(m1 - nm1);
+            m0 = nm0; m1 = nm1;
+            l0 *= c0; l1 *= c1;
+            #pragma unroll
+            for (int i = 0; i < 4; i++) { o[i][0] *= c0; o[i][1] *= c0; o[i][2] *= c1; o[i][3] *= c1; }
+            float p[2][4];
+            #pragma unroll
+            for (int nt = 0; nt < 2; nt++) {
+                p[nt][0] = exp2f(s[nt][0] - m0); p[nt][1] = exp2f(s[nt][1] - m0);
+                p[nt][2] = exp2f(s[nt][2] - m1); p[nt][3] = exp2f(s[nt][3] - m1);
+                l0 += p[nt][0] + p[nt][1];
+                l1 += p[nt][2] + p[nt][3];
+            }
+            uint32_t pa[4] = {pack2(p[0][0], p[0][1]), pack2(p[0][2], p[0][3]),
+                              pack2(p[1][0], p[1][1]), pack2(p[1][2], p[1][3])};
+            #pragma unroll
+            for (int dn = 0; dn < 2; dn++) {
+                uint32_t b[4];
+                ldb_kn(b, Vs, kb * 16, dn * 16, lane);
+                mma(o[dn * 2], pa, b[0], b[1]);
+                mma(o[dn * 2 + 1], pa, b[2], b[3]);
+            }
+        }
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+        float i0 = 1.f / l0, i1 = 1.f / l1;
+        int r0 = qb * 16 + g, r1 = r0 + 8;
+        bf16* ob = out + (long)n * L * ldo + h * DH;
+        #pragma unroll
+        for (int i = 0; i < 4; i++) {
+            int c = i * 8 + 2 * t;
+            if (r0 < L) *(uint32_t*)(ob + (long)r0 * ldo + c) = pack2(o[i][0] * i0, o[i][1] * i0);
+            if (r1 < L) *(uint32_t*)(ob + (long)r1 * ldo + c) = pack2(o[i][2] * i1, o[i][3] * i1);
+        }
+        if (t == 0) {
+            float* lb = lse + ((long)n * H + h) * L;
+            if (r0 < L) lb[r0] = (m0 + log2f(l0)) * 0.6931471805599453f;
+            if (r1 < L) lb[r1] = (m1 + log2f(l1)) * 0.6931471805599453f;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(128) k_attn_bwd_mma(
+        const bf16* __restrict__ qkv, long ldqkv, const uint8_t* __restrict__ keep,
+        const bf16* __restrict__ out, long ldo, const bf16* __restrict__ dout, long lddo,
+        const float* __restrict__ lse, bf16* __restrict__ dqkv, long lddqkv,
+        float* __restrict__ dbias, int L, int H) {
+    extern __shared__ __align__(16) uint8_t smraw[];
+    const int nh = blockIdx.x, n = nh / H, h = nh % H, D = H * DH;
+    const int Lp = (L + 15) & ~15, nkb = Lp / 16;
+    bf16* Qs = (bf16*)smraw;
+    bf16* Ks = Qs + Lp * RS;
+    bf16* Vs = Ks + Lp * RS;
+    bf16* Gs = Vs + Lp * RS;                        // dO
+    float* kbias = (float*)(Gs + Lp * RS);          // [Lp] key mask (0 / -inf)
+    float* lse2 = kbias + Lp;                       // [Lp] lse (log2 domain), +inf past L
+    float* dl = lse2 + Lp;                          // [Lp] delta = dO . O
+    int* kany = (int*)(dl + Lp);                    // [nkb]
+    float* cs = (float*)(kany + nkb);               // [3][32] bias-grad column sums
+    const bf16* base = qkv + (long)n * L * ldqkv + h * DH;
+    stage_rows(Qs, base, ldqkv, L, Lp);
+    stage_rows(Ks, base + D, ldqkv, L, Lp);
+    stage_rows(Vs, base + 2 * D, ldqkv, L, Lp);
+    stage_rows(Gs, dout + (long)n * L * lddo + h * DH, lddo, L, Lp);
+    const uint8_t* kp = keep + (long)n * L;
+    for (int i = threadIdx.x; i < nkb; i += blockDim.x) kany[i] = 0;
+    for (int i = threadIdx.x; i < 96; i += blockDim.x) cs[i] = 0.f;
+    __syncthreads();
+    const float* lrow = lse + ((long)n * H + h) * L;
+    const bf16* orow = out + (long)n * L * ldo + h * DH;
+    for (int j = threadIdx.x; j < Lp; j += blockDim.x) {
+        bool k = j < L && kp[j];
+        kbias[j] = k ? 0.f : -INFINITY;
+        if (k) kany[j >> 4] = 1;
+        if (j < L) {
+            lse2[j] = lrow[j] * LOG2E;
+            float d = 0.f;
+            const bf16* orr = orow + (long)j * ldo;
+            const bf16* grr = Gs + j * RS;
+            #pragma unroll 8
+            for (int c = 0; c < DH; c++) d += __bfloat162float(orr[c]) * __bfloat162float(grr[c]);
+            dl[j] = d;
+        } else {
+            lse2[j] = INFINITY;
+            dl[j] = 0.f;
+        }
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const float sc = 0.17677669529663687f * LOG2E;
+    const float scale = 0.17677669529663687f;
+    bf16* db = dqkv + (long)n * L * lddqkv + h * DH;
+    float colk[8], colv[8], colq[8];
+    #pragma unroll
+    for (int i = 0; i < 8; i++) colk[i] = colv[i] = colq[i] = 0.f;
+    // ---- phase 1: dK, dV, one warp per 16-key block
+    for (int kb = warp; kb < nkb; kb += 4) {
+        float dk[4][4], dv[4][4];
+        #pragma unroll
+        for (int i = 0; i < 4; i++)
+            #pragma unroll
+            for (int j = 0; j < 4; j++) dk[i][j] = dv[i][j] = 0.f;
+        if (kany[kb]) {
+            uint32_t ka[2][4], va[2][4];
+            lda(ka[0], Ks, kb * 16, 0, lane);
+            lda(ka[1], Ks, kb * 16, 16, lane);
+            lda(va[0], Vs, kb * 16, 0, lane);
+            lda(va[1], Vs, kb * 16, 16, lane);
+            float kb0 = kbias[kb * 16 + g], kb1 = kbias[kb * 16 + g + 8];
+            for (int qb = 0; qb < nkb; qb++) {
+                float s[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+                float dp[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+                #pragma unroll
+                for (int ks = 0; ks < 2; ks++) {
+                    uint32_t b[4];
+                    ldb_nk(b, Qs, qb * 16, ks * 16, lane);   // S^T = K Q^T
+                    mma(s[0], ka[ks], b[0], b[1]);
+                    mma(s[1], ka[ks], b[2], b[3]);
+                    ldb_nk(b, Gs, qb * 16, ks * 16, lane);   // dP^T = V dO^T
+                    mma(dp[0], va[ks], b[0], b[1]);
+                    mma(dp[1], va[ks], b[2], b[3]);
+                }
+                float p[2][4], ds[2][4];
+                #pragma unroll
+                for (int nt = 0; nt < 2; nt++) {
+                    int q0 = qb * 16 + nt * 8 + 2 * t;
+                    float la = lse2[q0], lb = lse2[q0 + 1];
+                    float da = dl[q0], dd = dl[q0 + 1];
+                    p[nt][0] = exp2f(s[nt][0] * sc + kb0 - la);
+                    p[nt][1] = exp2f(s[nt][1] * sc + kb0 - lb);
+                    p[nt][2] = exp2f(s[nt][2] * sc + kb1 - la);
+                    p[nt][3] = exp2f(s[nt][3] * sc + kb1 - lb);
+                    ds[nt][0] = p[nt][0] * (dp[nt][0] - da);
+                    ds[nt][1] = p[nt][1] * (dp[nt][1] - dd);
+                    ds[nt][2] = p[nt][2] * (dp[nt][2] - da);
+                    ds[nt][3] = p[nt][3] * (dp[nt][3] - dd);
+                }
+                uint32_t pa[4] = {pack2(p[0][0], p[0][1]), pack2(p[0][2], p[0][3]),
+                                  pack2(p[1][0], p[1][1]), pack2(p[1][2], p[1][3])};
+                uint32_t sa[4] = {pack2(ds[0][0], ds[0][1]), pack2(ds[0][2], ds[0][3]),
+                                  pack2(ds[1][0], ds[1][1]), pack2(ds[1][2], ds[1][3])};
+                #pragma unroll
+                for (int dn = 0; dn < 2; dn++) {
+                    uint32_t b[4];
+                    ldb_kn(b, Gs, qb * 16, dn * 16, lane);   // dV += P^T dO
+                    mma(dv[dn * 2], pa, b[0], b[1]);
+                    mma(dv[dn * 2 + 1], pa, b[2], b[3]);
+                    ldb_kn(b, Qs, qb * 16, dn * 16, lane);   // dK += dS^T Q
+                    mma(dk[dn * 2], sa, b[0], b[1]);
+                    mma(dk[dn * 2 + 1], sa, b[2], b[3]);
+                }
+            }
+        }
+        int r0 = kb * 16 + g, r1 = r0 + 8;
+        #pragma unroll
+        for (int i = 0; i < 4; i++) {
+            int c = i * 8 + 2 * t;
+            float k00 = dk[i][0] * scale, k01 = dk[i][1] * scale;
+            float k10 = dk[i][2] * scale, k11 = dk[i][3] * scale;
+            if (r0 < L) {
+                *(uint32_t*)(db + (long)r0 * lddqkv + D + c) = pack2(k00, k01);
+                *(uint32_t*)(db + (long)r0 * lddqkv + 2 * D + c) = pack2(dv[i][0], dv[i][1]);
+                colk[2 * i] += k00; colk[2 * i + 1] += k01;
+                colv[2 * i] += dv[i][0]; colv[2 * i + 1] += dv[i][1];
+            }
+            if (r1 < L) {
+                *(uint32_t*)(db + (long)r1 * lddqkv + D + c) = pack2(k10, k11);
+                *(uint32_t*)(db + (long)r1 * lddqkv + 2 * D + c) = pack2(dv[i][2], dv[i][3]);
+                colk[2 * i] += k10; colk[2 * i + 1] += k11;
+                colv[2 * i] += dv[i][2]; colv[2 * i + 1] += dv[i][3];
+            }
+        }
+    }
+    // ---- phase 2: dQ, one warp per 16-query block
+    for (int qb = warp; qb < nkb; qb += 4) {
+        float dq[4][4];
+        #pragma unroll
+        for (int i = 0; i < 4; i++) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
+        uint32_t qa[2][4], ga[2][4];
+        lda(qa[0], Qs, qb * 16, 0, lane);
+        lda(qa[1], Qs, qb * 16, 16, lane);
+        lda(ga[0], Gs, qb * 16, 0, lane);
+        lda(ga[1], Gs, qb * 16, 16, lane);
+        int q0 = qb * 16 + g, q1 = q0 + 8;
+        float la = lse2[q0], lb = lse2[q1], da = dl[q0], dd = dl[q1];
+        for (int kb = 0; kb < nkb; kb++) {
+            if (!kany[kb]) continue;
+            float s[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+            float dp[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+            #pragma unroll
+            for (int ks = 0; ks < 2; ks++) {
+                uint32_t b[4];
+                ldb_nk(b, Ks, kb * 16, ks * 16, lane);       // S = Q K^T
+                mma(s[0], qa[ks], b[0], b[1]);
+                mma(s[1], qa[ks], b[2], b[3]);
+                ldb_nk(b, Vs, kb * 16, ks * 16, lane);       // dP = dO V^T
+                mma(dp[0], ga[ks], b[0], b[1]);
+                mma(dp[1], ga[ks], b[2], b[3]);
+            }
+            float ds[2][4];
+            #pragma unroll
+            for (int nt = 0; nt < 2; nt++) {
+                float b0 = kbias[kb * 16 + nt * 8 + 2 * t], b1 = kbias[kb * 16 + nt * 8 + 2 * t + 1];
+                float p0 = exp2f(s[nt][0] * sc + b0 - la), p1 = exp2f(s[nt][1] * sc + b1 - la);
+                float p2 = exp2f(s[nt][2] * sc + b0 - lb), p3 = exp2f(s[nt][3] * sc + b1 - lb);
+                ds[nt][0] = p0 * (dp[nt][0] - da);
+                ds[nt][1] = p1 * (dp[nt][1] - da);
+                ds[nt][2] = p2 * (dp[nt][2] - dd);
+                ds[nt][3] = p3 * (dp[nt][3] - dd);
+            }
+            uint32_t sa[4] = {pack2(ds[0][0], ds[0][1]), pack2(ds[0][2], ds[0][3]),
+                              pack2(ds[1][0], ds[1][1]), pack2(ds[1][2], ds[1][3])};
+            #pragma unroll
+            for (int dn = 0; dn < 2; dn++) {
+                uint32_t b[4];
+                ldb_kn(b, Ks, kb * 16, dn * 16, lane);       // dQ += dS K
+                mma(dq[dn * 2], sa, b[0], b[1]);
+                mma(dq[dn * 2 + 1], sa, b[2], b[3]);
+            }
+        }
+        #pragma unroll
+        for (int i = 0; i < 4; i++) {
+            int c = i * 8 + 2 * t;
+            float a0 = dq[i][0] * scale, a1 = dq[i][1] * scale;
+            float a2 = dq[i][2] * scale, a3 = dq[i][3] * scale;
+            if (q0 < L) {
+                *(uint32_t*)(db + (long)q0 * lddqkv + c) = pack2(a0, a1);
+                colq[2 * i] += a0; colq[2 * i + 1] += a1;
+            }
+            if (q1 < L) {
+                *(uint32_t*)(db + (long)q1 * lddqkv + c) = pack2(a2, a3);
+                colq[2 * i] += a2; colq[2 * i + 1] += a3;
+            }
+        }
+    }
+    if (dbias) {
+        // thread (g, t) holds columns i*8 + 2t + {0,1}: reduce over g (lanes
+        // with equal t), then one shared atomic per column per warp
+        #pragma unroll
+        for (int i = 0; i < 8; i++) {
+            #pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                colq[i] += __shfl_xor_sync(0xffffffffu, colq[i], o);
+                colk[i] += __shfl_xor_sync(0xffffffffu, colk[i], o);
+                colv[i] += __shfl_xor_sync(0xffffffffu, colv[i], o);
+            }
+        }
+        if (g == 0) {
+            #pragma unroll
+            for (int i = 0; i < 4; i++)
+                #pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    int c = i * 8 + 2 * t + e;
+                    atomicAdd(&cs[c], colq[2 * i + e]);
+                    atomicAdd(&cs[32 + c], colk[2 * i + e]);
+                    atomicAdd(&cs[64 + c], colv[2 * i + e]);
+                }
+        }
+        __syncthreads();
+        if (threadIdx.x < 96) {
+            int w = threadIdx.x / 32, c = threadIdx.x % 32;
+            atomicAdd(&dbias[w * D + h * DH + c], cs[threadIdx.x]);
+        }
+    }
+}
+
+size_t fwd_mma_smem(int L) {
+    int Lp = (L + 15) & ~15;
+    return (size_t)3 * Lp * RS * 2 + Lp * 4 + (Lp / 16) * 4 + 16;
+}
+size_t bwd_mma_smem(int L) {
+    int Lp = (L + 15) & ~15;
+    return (size_t)4 * Lp * RS * 2 + 3 * Lp * 4 + (Lp / 16) * 4 + 96 * 4 + 16;
+}
+
 size_t fwd_smem(int L) {
     int Lr = (L + 31) & ~31;
     return sizeof(float) * (2 * L * PADW + NW * DH + NW * Lr);
@@ -201,8 +603,9 @@ void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
         ++g_ptcg_launches, k_attn_fwd<float><<<nseq * H, NW * 32, sm, s>>>((const float*)qkv, ldqkv, keep,
             (float*)out, ldo, lse, L, H);
     } else {
-        set_smem(k_attn_fwd<bf16>, sm);
-        ++g_ptcg_launches, k_attn_fwd<bf16><<<nseq * H, NW * 32, sm, s>>>((const bf16*)qkv, ldqkv, keep,
+        size_t sm2 = fwd_mma_smem(L);
+        set_smem(k_attn_fwd_mma, sm2);
+        ++g_ptcg_launches, k_attn_fwd_mma<<<nseq * H, 128, sm2, s>>>((const bf16*)qkv, ldqkv, keep,
             (bf16*)out, ldo, lse, L, H);
     }
 }
@@ -218,8 +621,9 @@ void attn_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
         ++g_ptcg_launches, k_attn_bwd<float><<<nseq * H, NW * 32, sm, s>>>((const float*)qkv, ldqkv, keep,
             (const float*)out, ldo, (const float*)dout, lddo, lse, (float*)dqkv, lddqkv, dbias, L, H);
     } else {
-        set_smem(k_attn_bwd<bf16>, sm);
-        ++g_ptcg_launches, k_attn_bwd<bf16><<<nseq * H, NW * 32, sm, s>>>((const bf16*)qkv, ldqkv, keep,
+        size_t sm2 = bwd_mma_smem(L);
+        set_smem(k_attn_bwd_mma, sm2);
+        ++g_ptcg_launches, k_attn_bwd_mma<<<nseq * H, 128, sm2, s>>>((const bf16*)qkv, ldqkv, keep,
             (const bf16*)out, ldo, (const bf16*)dout, lddo, lse, (bf16*)dqkv, lddqkv, dbias, L, H);
     }
 }

@@ -9,9 +9,11 @@
 //   multicast) into a multi-stage shared-memory ring.  K-major operands load
 //   one box {64 K, rows}; MN-major operands (the transposed side of dX / dW
 //   GEMMs) load boxes {64 MN, 64 K}, so no operand is ever transposed in HBM.
-// * One elected thread issues tcgen05.mma.cta_group::1.kind::f16 (M=128,
-//   N=BN, K=16 per instruction) into a double-buffered TMEM accumulator and
-//   releases ring slots with tcgen05.commit.
+// * One elected thread issues tcgen05.mma.cta_group::1 (kind::f16 for bf16
+//   operands, K=16 per instruction; kind::tf32 for fp32 operands, K=8) with
+//   M=128, N=BN into a double-buffered TMEM accumulator and releases ring
+//   slots with tcgen05.commit.  A 128-byte swizzled row holds 64 bf16 or 32
+//   fp32 K-elements, so both kinds share one byte-level smem layout.
 // * Four epilogue warps (one per TMEM lane quadrant) read the accumulator
 //   with tcgen05.ld.32x32b.x32 while the next tile's MMAs run, and apply
 //   bias / broadcast / GELU / GELU' / row remap / residual / accumulate /
@@ -32,7 +34,7 @@
 
 namespace {
 
-constexpr int BM = 128, BK = 64;
+constexpr int BM = 128;
 constexpr int NUM_THREADS = 192;             // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr long long WAIT_BUDGET = 4000000000LL;   // clock cycles (~2 s)
 
@@ -92,11 +94,18 @@ PTCG_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, in
 }
 PTCG_DEV void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 PTCG_DEV void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-PTCG_DEV void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-    asm volatile("{\n\t.reg .pred p;\n\t"
-                 "setp.ne.b32 p, %4, 0;\n\t"
-                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-                 :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc) : "memory");
+template <int EB>
+PTCG_DEV void mma_issue(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    if (EB == 2)
+        asm volatile("{\n\t.reg .pred p;\n\t"
+                     "setp.ne.b32 p, %4, 0;\n\t"
+                     "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                     :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc) : "memory");
+    else
+        asm volatile("{\n\t.reg .pred p;\n\t"
+                     "setp.ne.b32 p, %4, 0;\n\t"
+                     "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+                     :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc) : "memory");
 }
 PTCG_DEV void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
@@ -116,14 +125,17 @@ PTCG_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// UMMA shared-memory descriptor, 128-byte swizzle, sm_100 version bits
-PTCG_DEV uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+// UMMA shared-memory descriptor, sm_100 version bits.  layout 2 = 128-byte
+// swizzle (16-byte granules, 8-row atoms); layout 1 = 128-byte swizzle with
+// 32-byte granules and 4-row atoms (the only MN-major layout for 32-bit
+// operands; TMA writes it with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B).
+PTCG_DEV uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout = 2) {
     uint64_t d = 0;
     d |= (uint64_t)((saddr >> 4) & 0x3FFF);
     d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
     d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
     d |= (uint64_t)1 << 46;                  // descriptor version (sm_100)
-    d |= (uint64_t)2 << 61;                  // SWIZZLE_128B
+    d |= (uint64_t)layout << 61;
     return d;
 }
 
@@ -206,9 +218,19 @@ PTCG_DEV float warp_colsum32(float (&v)[32], int lane) {
 }
 
 // -------------------------------------------------------------- the kernel
+// EB = operand element bytes (2: bf16 / kind::f16, 4: fp32 / kind::tf32)
+template <int EB>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
           const __grid_constant__ TcParams P) {
+    constexpr int BK = 128 / EB;            // K elements per 128-byte row
+    constexpr int ATOM = 128 / EB;          // MN elements per MN-major box
+    constexpr int KI = 32 / EB;             // K elements per MMA instruction
+    constexpr uint32_t BOX = BK * 128;      // bytes of one MN-major box {ATOM, BK}
+    // MN-major K-direction atom: 8 rows (bf16, 128B swizzle) or 4 rows
+    // (fp32, 128B swizzle with 32-byte base)
+    constexpr uint32_t MN_SBO = EB == 2 ? 1024 : 512;
+    constexpr uint32_t MN_LAYOUT = EB == 2 ? 2 : 1;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int S = P.stages;
@@ -264,14 +286,15 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     uint32_t sb = sa + P.a_bytes;
                     int k0 = kb * BK;
                     if (P.a_mn) {
-                        tma_load_2d(sa, &map_a, fb, mt * BM, k0);
-                        tma_load_2d(sa + 8192, &map_a, fb, mt * BM + 64, k0);
+                        #pragma unroll
+                        for (int j = 0; j < BM / ATOM; j++)
+                            tma_load_2d(sa + j * BOX, &map_a, fb, mt * BM + ATOM * j, k0);
                     } else {
                         tma_load_2d(sa, &map_a, fb, k0, mt * BM);
                     }
                     if (P.b_mn) {
-                        for (int j = 0; j < P.b_rows / 64; j++)
-                            tma_load_2d(sb + j * 8192, &map_b, fb, nt * P.bn + 64 * j, k0);
+                        for (int j = 0; j < P.b_rows / ATOM; j++)
+                            tma_load_2d(sb + j * BOX, &map_b, fb, nt * P.bn + ATOM * j, k0);
                     } else {
                         tma_load_2d(sb, &map_b, fb, k0, nt * P.bn);
                     }
@@ -302,12 +325,12 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     uint32_t sa = smem_u32(smem + (size_t)stage * P.stage_bytes);
                     uint32_t sb = sa + P.a_bytes;
                     #pragma unroll
-                    for (int s = 0; s < BK / 16; s++) {
-                        uint64_t ad = P.a_mn ? make_desc(sa + s * 2048, 8192, 1024)
+                    for (int s = 0; s < BK / KI; s++) {
+                        uint64_t ad = P.a_mn ? make_desc(sa + s * KI * 128, BOX, MN_SBO, MN_LAYOUT)
                                              : make_desc(sa + s * 32, 16, 1024);
-                        uint64_t bd = P.b_mn ? make_desc(sb + s * 2048, 8192, 1024)
+                        uint64_t bd = P.b_mn ? make_desc(sb + s * KI * 128, BOX, MN_SBO, MN_LAYOUT)
                                              : make_desc(sb + s * 32, 16, 1024);
-                        mma_f16(dcol, ad, bd, P.idesc, (kb > kb0 || s > 0) ? 1u : 0u);
+                        mma_issue<EB>(dcol, ad, bd, P.idesc, (kb > kb0 || s > 0) ? 1u : 0u);
                     }
                     mma_commit(empty0 + 8 * stage);
                     if (++stage == S) { stage = 0; phase ^= 1; }
@@ -457,20 +480,7 @@ void init_once() {
     g_ok = true;
 }
 
-// 2-D bf16 tensor map: inner extent `inner` (contiguous), `outer` rows,
-// row pitch ld elements, box {box_in, box_out}
-bool make_map(CUtensorMap* m, const void* ptr, long inner, long outer, long ld, int box_in,
-              int box_out) {
-    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
-    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-    cuuint32_t box[2] = {(cuuint32_t)box_in, (cuuint32_t)box_out};
-    cuuint32_t es[2] = {1, 1};
-    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
-                          strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
-}
+
 
 }  // namespace
 
@@ -486,21 +496,49 @@ bool gemm_tc_available() {
     return g_ok;
 }
 
-bool gemm_tc(const GemmArgs& a, cudaStream_t s) {
+namespace {
+
+// 2-D tensor map of `eb`-byte elements
+bool make_map_eb(CUtensorMap* m, const void* ptr, long inner, long outer, long ld, int box_in,
+                 int box_out, int eb, bool mn_major) {
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * eb};
+    cuuint32_t box[2] = {(cuuint32_t)box_in, (cuuint32_t)box_out};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = g_encode(m, eb == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                          2, const_cast<void*>(ptr), dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          (eb == 4 && mn_major) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                                : CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+struct TcPlan {
+    TcParams P;
+    int eb;
+    CUtensorMap ma, mb;
+};
+
+bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     if (!gemm_tc_available()) return false;
-    if (a.dtype != DT_BF16) return false;            // tf32 kind not wired yet
-    if (a.M <= 0 || a.N <= 0 || a.K <= 0) return a.M <= 0 || a.N <= 0;
+    int eb;
+    if (a.dtype == DT_BF16) eb = 2;
+    else if (a.dtype == DT_F32 && a.allow_tf32) eb = 4;
+    else return false;
+    if (a.M <= 0 || a.N <= 0 || a.K <= 0) return false;
     // TMA: 16-byte aligned base and row pitch
-    if (((uintptr_t)a.A & 15) || ((uintptr_t)a.B & 15) || (a.lda % 8) || (a.ldb % 8)) return false;
+    if (((uintptr_t)a.A & 15) || ((uintptr_t)a.B & 15) || ((a.lda * eb) % 16) || ((a.ldb * eb) % 16))
+        return false;
     // small problems stay on the SIMT kernel
     if ((long)a.M * a.N * a.K < (1L << 22)) return false;
-
-    TcParams P;
+    const int BK = 128 / eb, ATOM = 128 / eb;
+    TcParams& P = pl.P;
     P.M = a.M; P.N = a.N; P.K = a.K;
     P.a_mn = !a.a_kmajor; P.b_mn = !a.b_kmajor;
     int ntl = (a.N + 255) / 256;
     int bn = ((a.N + ntl - 1) / ntl + 15) / 16 * 16;
-    if (P.b_mn) bn = (bn + 63) / 64 * 64;
+    if (P.b_mn) bn = (bn + ATOM - 1) / ATOM * ATOM;
     if (bn > 256) bn = 256;
     P.bn = bn;
     P.b_rows = bn;
@@ -519,32 +557,54 @@ bool gemm_tc(const GemmArgs& a, cudaStream_t s) {
     }
     P.kb_per_split = (P.kb_total + P.splits - 1) / P.splits;
     P.splits = (P.kb_total + P.kb_per_split - 1) / P.kb_per_split;   // no empty splits
-    P.a_bytes = BM * BK * 2;
-    P.stage_bytes = P.a_bytes + P.b_rows * BK * 2;
+    P.a_bytes = BM * 128;
+    P.stage_bytes = P.a_bytes + P.b_rows * 128;
     int budget = 200 * 1024;
     P.stages = budget / P.stage_bytes;
     if (P.stages > 6) P.stages = 6;
     if (P.stages < 2) return false;
     P.acc_stride = bn <= 128 ? 128 : 256;
     P.tmem_cols = 2 * P.acc_stride;
-    // instruction descriptor: f32 accumulate, bf16 A/B, majorness, N>>3, M>>4
-    P.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)P.a_mn << 15) |
+    // instruction descriptor: f32 accumulate, A/B format (1 bf16, 2 tf32),
+    // majorness, N>>3, M>>4
+    uint32_t fmt = eb == 2 ? 1u : 2u;
+    P.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)P.a_mn << 15) |
               ((uint32_t)P.b_mn << 16) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
     P.ep = a;
-
-    CUtensorMap ma, mb;
+    pl.eb = eb;
     bool ok;
-    if (P.a_mn) ok = make_map(&ma, a.A, a.M, a.K, a.lda, 64, BK);
-    else ok = make_map(&ma, a.A, a.K, a.M, a.lda, BK, BM);
+    if (P.a_mn) ok = make_map_eb(&pl.ma, a.A, a.M, a.K, a.lda, ATOM, BK, eb, true);
+    else ok = make_map_eb(&pl.ma, a.A, a.K, a.M, a.lda, BK, BM, eb, false);
     if (!ok) return false;
-    if (P.b_mn) ok = make_map(&mb, a.B, a.N, a.K, a.ldb, 64, BK);
-    else ok = make_map(&mb, a.B, a.K, a.N, a.ldb, BK, bn);
-    if (!ok) return false;
+    if (P.b_mn) ok = make_map_eb(&pl.mb, a.B, a.N, a.K, a.ldb, ATOM, BK, eb, true);
+    else ok = make_map_eb(&pl.mb, a.B, a.K, a.N, a.ldb, BK, bn, eb, false);
+    return ok;
+}
 
+void launch_tc(const TcPlan& pl, cudaStream_t s) {
+    const TcParams& P = pl.P;
     size_t smem = 1024 + (size_t)P.stages * P.stage_bytes + (2 * P.stages + 5) * 8 + 32;
-    cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     int total = P.m_tiles * P.n_tiles * P.splits;
     int grid = total < g_sms ? total : g_sms;
-    ++g_ptcg_launches, k_gemm_tc<<<grid, NUM_THREADS, smem, s>>>(ma, mb, P);
+    if (pl.eb == 2) {
+        cudaFuncSetAttribute(k_gemm_tc<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        ++g_ptcg_launches, k_gemm_tc<2><<<grid, NUM_THREADS, smem, s>>>(pl.ma, pl.mb, P);
+    } else {
+        cudaFuncSetAttribute(k_gemm_tc<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        ++g_ptcg_launches, k_gemm_tc<4><<<grid, NUM_THREADS, smem, s>>>(pl.ma, pl.mb, P);
+    }
+}
+
+}  // namespace
+
+bool gemm_tc_supported(const GemmArgs& a) {
+    TcPlan pl;
+    return plan_tc(a, pl);
+}
+
+bool gemm_tc(const GemmArgs& a, cudaStream_t s) {
+    TcPlan pl;
+    if (!plan_tc(a, pl)) return false;
+    launch_tc(pl, s);
     return true;
 }

@@ -42,6 +42,7 @@ void gemm_simt(const GemmArgs& a, cudaStream_t s);
 // tcgen05 path: returns false if the problem is not supported (caller falls
 // back to the SIMT kernel, which is also sm_100a code in this library)
 bool gemm_tc(const GemmArgs& a, cudaStream_t s);
+bool gemm_tc_supported(const GemmArgs& a);
 bool gemm_tc_available();
 // first error code recorded by a tcgen05 kernel since the last call (0 = none)
 int ptcg_tc_error_read_reset();

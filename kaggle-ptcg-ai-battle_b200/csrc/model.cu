@@ -232,7 +232,7 @@ static void kt_mark(PtcgModel* M, cudaStream_t s) {
 }
 
 static void gemm(PtcgModel* M, const GemmArgs& a, cudaStream_t s) {
-    bool tc_ok = (a.dtype == DT_BF16 || a.allow_tf32) && gemm_tc_available();
+    bool tc_ok = (a.dtype == DT_BF16 || a.allow_tf32) && gemm_tc_supported(a);
     int cls = tc_ok ? 1 : 2;
     bool timed = M->kt.mode == cls;
     if (timed) kt_mark(M, s);
@@ -1434,6 +1434,28 @@ int ptcg_set_step(PtcgModel* M, long step) {
 
 long long ptcg_launch_count(void) { return g_ptcg_launches; }
 
+int ptcg_attention_fwd(int operand_dtype, const void* qkv, long ldqkv, const unsigned char* keep,
+                       void* out, long ldo, float* lse, int nseq, int L, int H, void* stream) {
+    REQ(qkv && keep && out && lse && nseq >= 0 && L > 0 && L <= 320 && H > 0, PTCG_EINVAL,
+        "bad arguments");
+    attn_fwd(operand_dtype == PTCG_BF16 ? DT_BF16 : DT_F32, qkv, ldqkv, keep, out, ldo, lse, nseq,
+             L, H, (cudaStream_t)stream);
+    CKL();
+    return PTCG_OK;
+}
+
+int ptcg_attention_bwd(int operand_dtype, const void* qkv, long ldqkv, const unsigned char* keep,
+                       const void* out, long ldo, const void* dout, long lddo, const float* lse,
+                       void* dqkv, long lddqkv, float* dbias, int nseq, int L, int H,
+                       void* stream) {
+    REQ(qkv && keep && out && dout && lse && dqkv && nseq >= 0 && L > 0 && L <= 320 && H > 0,
+        PTCG_EINVAL, "bad arguments");
+    attn_bwd(operand_dtype == PTCG_BF16 ? DT_BF16 : DT_F32, qkv, ldqkv, keep, out, ldo, dout, lddo,
+             lse, dqkv, lddqkv, dbias, nseq, L, H, (cudaStream_t)stream);
+    CKL();
+    return PTCG_OK;
+}
+
 int ptcg_tensor_cores(void) { return gemm_tc_available() ? 1 : 0; }
 
 int ptcg_device_error(void) { return ptcg_tc_error_read_reset(); }
@@ -1443,12 +1465,13 @@ int ptcg_gemm(int M, int N, int K, const void* A, long lda, int a_kmajor, const 
               void* stream) {
     REQ(A && B && C && M >= 0 && N >= 0 && K >= 0, PTCG_EINVAL, "bad arguments");
     REQ(operand_dtype == PTCG_FP32 || operand_dtype == PTCG_BF16, PTCG_EINVAL, "bad dtype");
-    REQ(engine >= 0 && engine <= 2, PTCG_EINVAL, "bad engine");
+    REQ(engine >= 0 && engine <= 3, PTCG_EINVAL, "bad engine");
     GemmArgs a;
     a.M = M; a.N = N; a.K = K; a.dtype = operand_dtype == PTCG_BF16 ? DT_BF16 : DT_F32;
     a.A = A; a.lda = lda; a.a_kmajor = a_kmajor;
     a.B = B; a.ldb = ldb; a.b_kmajor = b_kmajor;
     a.out = C; a.ldo = ldc; a.out_dtype = DT_F32; a.accumulate = accumulate;
+    if (engine == 3) { a.allow_tf32 = 1; engine = 1; }
     cudaStream_t s = (cudaStream_t)stream;
     if (engine == 2) { gemm_simt(a, s); CKL(); return PTCG_OK; }
     bool done = gemm_tc_available() && gemm_tc(a, s);

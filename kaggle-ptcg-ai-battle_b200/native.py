@@ -66,6 +66,8 @@ _SIGS = {
     "ptcg_kernel_timer": (I, [P, I]),
     "ptcg_launch_count": (C.c_longlong, []),
     "ptcg_tensor_cores": (I, []),
+    "ptcg_attention_fwd": (I, [I, P, L, P, P, L, P, I, I, I, P]),
+    "ptcg_attention_bwd": (I, [I, P, L, P, P, L, P, L, P, P, L, P, I, I, I, P]),
     "ptcg_device_error": (I, []),
     "ptcg_gemm": (I, [I, I, I, P, L, I, P, L, I, I, P, L, I, I, P]),
     "ptcg_kernel_timer_read": (I, [P, C.POINTER(C.c_double), C.POINTER(C.c_long),

@@ -1,0 +1,63 @@
+"""Attention kernels (fp32 SIMT and bf16 tensor-core flash attention) against
+torch scaled_dot_product_attention with a boolean key-padding mask."""
+import ctypes as C
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _p(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+@pytest.mark.parametrize("L,H", [(129, 8), (186, 8), (17, 2), (257, 16), (314, 16), (33, 4)])
+def test_attention_matches_sdpa(pkg, dtype, L, H):
+    import ptcg_b200.native as n
+    lib = n.lib()
+    torch.manual_seed(L * 10 + H)
+    nseq, D = 5, H * 32
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
+    qkv = torch.randn(nseq * L, 3 * D, device="cuda").to(tdt)
+    keep = torch.rand(nseq, L, device="cuda") < 0.7
+    keep[:, 0] = True
+    keep[1, L // 2:] = False                       # long masked tail
+    keep_u8 = keep.to(torch.uint8).contiguous()
+    out = torch.zeros(nseq * L, D, device="cuda", dtype=tdt)
+    lse = torch.zeros(nseq, H, L, device="cuda")
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    dt = 1 if dtype == "bf16" else 0
+    assert lib.ptcg_attention_fwd(dt, _p(qkv), 3 * D, _p(keep_u8), _p(out), D, _p(lse), nseq, L, H, s) == 0
+    q, k, v = qkv.float().view(nseq, L, 3, H, 32).permute(2, 0, 3, 1, 4).unbind(0)
+    q.requires_grad_(True); k.requires_grad_(True); v.requires_grad_(True)
+    ref = F.scaled_dot_product_attention(q, k, v, attn_mask=keep.view(nseq, 1, 1, L))
+    ref_o = ref.transpose(1, 2).reshape(nseq * L, D)
+    tol = 2e-2 if dtype == "bf16" else 1e-5
+    err = (out.float() - ref_o).abs().max().item() / ref_o.abs().max().item()
+    assert err < tol, err
+    sc = (q @ k.transpose(-1, -2)) / 32 ** 0.5
+    sc = sc.masked_fill(~keep.view(nseq, 1, 1, L), float("-inf"))
+    ref_lse = torch.logsumexp(sc, -1)
+    assert (lse - ref_lse).abs().max().item() < (2e-2 if dtype == "bf16" else 1e-4)
+    # backward
+    dout = torch.randn(nseq * L, D, device="cuda").to(tdt)
+    ref_o.backward(dout.float())
+    dqkv = torch.zeros_like(qkv)
+    dbias = torch.zeros(3 * D, device="cuda")
+    assert lib.ptcg_attention_bwd(dt, _p(qkv), 3 * D, _p(keep_u8), _p(out), D, _p(dout), D,
+                                  _p(lse), _p(dqkv), 3 * D, _p(dbias), nseq, L, H, s) == 0
+    torch.cuda.synchronize()
+    refd = torch.stack([q.grad, k.grad, v.grad], 2).permute(0, 3, 2, 1, 4).reshape(nseq * L, 3 * D)
+    for part in range(3):
+        a = dqkv.float()[:, part * D:(part + 1) * D]
+        b = refd[:, part * D:(part + 1) * D]
+        e = (a - b).norm().item() / b.norm().item()
+        assert e < (3e-2 if dtype == "bf16" else 1e-4), (part, e)
+        # fp32 column sums (bias grads); judged against the sum of |values|
+        # since the K part is analytically zero (softmax shift invariance)
+        cs = dbias[part * D:(part + 1) * D]
+        scale = b.abs().sum(0).norm().item()
+        assert (cs - b.sum(0)).norm().item() <= (3e-2 if dtype == "bf16" else 1e-4) * scale, part

@@ -9,10 +9,10 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def run_gemm(lib, M, N, K, a_k, b_k, engine, acc=False, seed=0):
+def run_gemm(lib, M, N, K, a_k, b_k, engine, acc=False, seed=0, dtype=torch.bfloat16):
     g = torch.Generator(device="cpu").manual_seed(seed)
-    A = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
-    B = torch.randn(N, K, generator=g).to(torch.bfloat16).cuda()
+    A = torch.randn(M, K, generator=g).to(dtype).cuda()
+    B = torch.randn(N, K, generator=g).to(dtype).cuda()
     # storage layouts: K-major = row-major [rows, K]; MN-major = [K, rows]
     As = A.contiguous() if a_k else A.t().contiguous()
     Bs = B.contiguous() if b_k else B.t().contiguous()
@@ -27,7 +27,8 @@ def run_gemm(lib, M, N, K, a_k, b_k, engine, acc=False, seed=0):
     Cm = torch.randn(M, N, generator=g).cuda() if acc else torch.zeros(M, N, device="cuda")
     ref = A.float() @ B.float().t() + (Cm if acc else 0)
     rc = lib.ptcg_gemm(M, N, K, C.c_void_p(As.data_ptr()), As.shape[1], int(a_k),
-                       C.c_void_p(Bs.data_ptr()), Bs.shape[1], int(b_k), 1,
+                       C.c_void_p(Bs.data_ptr()), Bs.shape[1], int(b_k),
+                       1 if dtype == torch.bfloat16 else 0,
                        C.c_void_p(Cm.data_ptr()), N, int(acc), engine,
                        C.c_void_p(torch.cuda.current_stream().cuda_stream))
     torch.cuda.synchronize()
@@ -62,3 +63,25 @@ def test_tc_gemm_split_k_accumulate(pkg, M, N, K):
     assert rc == 0, lib.ptcg_last_error()
     err = (out - ref).abs().max().item() / ref.abs().max().item()
     assert err < 1e-3, err
+
+
+def _tf32(x):
+    """round-toward-zero to the 10-bit TF32 mantissa (what kind::tf32 reads)"""
+    return (x.view(torch.int32) & ~0x1FFF).view(torch.float32)
+
+
+@pytest.mark.parametrize("a_k,b_k", [(1, 1), (1, 0), (0, 0), (0, 1)])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (300, 144, 200), (4096, 256, 664),
+                                   (1000, 960, 256), (256, 664, 40000)])
+def test_tc_gemm_tf32(pkg, a_k, b_k, M, N, K):
+    """fp32 operands on kind::tf32 (allowed through ptcg_gemm engine=3)"""
+    import ptcg_b200.native as n
+    lib = n.lib()
+    if not lib.ptcg_tensor_cores():
+        pytest.skip("no sm_100 device")
+    rc, out, ref = run_gemm(lib, M, N, K, a_k, b_k, engine=3, dtype=torch.float32,
+                            acc=(a_k == 0 and b_k == 0))
+    assert lib.ptcg_device_error() == 0
+    assert rc == 0, lib.ptcg_last_error()
+    err = (out - ref).norm().item() / ref.norm().item()
+    assert err < 2e-3, err
