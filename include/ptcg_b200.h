@@ -230,6 +230,10 @@ int ptcg_attention_bwd(int operand_dtype, const void* qkv, long ldqkv, const uns
                        const void* out, long ldo, const void* dout, long lddo, const float* lse,
                        void* dqkv, long lddqkv, float* dbias, int nseq, int L, int H,
                        void* stream);
+/* The GELU and GELU' that the tensor-core GEMM epilogues evaluate (erf by
+ * Abramowitz & Stegun 7.1.26), exposed so tests can bound their error
+ * against the exact erf form of torch nn.GELU. */
+int ptcg_eval_gelu(const float* x, float* gelu, float* gelu_grad, int n, void* stream);
 /* 1 when the tcgen05 engine is usable on the current device (sm_100). */
 int ptcg_tensor_cores(void);
 /* First error code a bounded device-side wait recorded since the last call

@@ -35,7 +35,8 @@
 namespace {
 
 constexpr int BM = 128;
-constexpr int NUM_THREADS = 192;             // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int NUM_EPI = 8;                   // epilogue warps (two per TMEM lane quadrant)
+constexpr int NUM_THREADS = 64 + 32 * NUM_EPI; // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
 constexpr long long WAIT_BUDGET = 4000000000LL;   // clock cycles (~2 s)
 
 __device__ int g_tc_error_dev;
@@ -247,7 +248,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; i++) { mbar_init(full0 + 8 * i, 1); mbar_init(empty0 + 8 * i, 1); }
-        for (int i = 0; i < 2; i++) { mbar_init(tfull0 + 8 * i, 1); mbar_init(tempty0 + 8 * i, 4); }
+        for (int i = 0; i < 2; i++) { mbar_init(tfull0 + 8 * i, 1); mbar_init(tempty0 + 8 * i, NUM_EPI); }
         mbar_init(drain, 1);
         *abort_flag = 0;
         *n_issued = 0;
@@ -348,6 +349,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     } else {
         // ------------------------------------------------ epilogue warps
         const int quad = warp & 3;           // TMEM lane quadrant this warp may read
+        const int half = (warp - 2) >> 2;    // which alternate 32-column chunks
         const int row_in_tile = quad * 32 + lane;
         const GemmArgs& a = P.ep;
         int local = 0;
@@ -365,13 +367,17 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             if (a.remap_group > 0)
                 orow = (long)(m / a.remap_group) * a.remap_stride + a.remap_off + (m % a.remap_group);
             const uint32_t tbase = tmem + buf * P.acc_stride + ((uint32_t)(quad * 32) << 16);
-            for (int c0 = 0; c0 < P.bn; c0 += 32) {
+            for (int c0 = half * 32; c0 < P.bn; c0 += 64) {
                 uint32_t r[32];
                 tmem_ld32(tbase + c0, r);
                 const int n0 = nt * P.bn + c0;
                 float v[32];
                 #pragma unroll
-                for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]) * a.alpha;
+                for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+                if (a.alpha != 1.f) {
+                    #pragma unroll
+                    for (int j = 0; j < 32; j++) v[j] *= a.alpha;
+                }
                 int nvalid = a.N - n0;
                 if (nvalid > P.bn - c0) nvalid = P.bn - c0;
                 if (nvalid > 32) nvalid = 32;
@@ -387,8 +393,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 if (row_ok) {
                 float t[32];
                 if (a.bias) {
+                    load32(t, a.bias, n0, DT_F32, nvalid);
                     #pragma unroll
-                    for (int j = 0; j < 32; j++) v[j] += j < nvalid ? a.bias[n0 + j] : 0.f;
+                    for (int j = 0; j < 32; j++) v[j] += t[j];
                 }
                 if (a.bcast) {
                     load32(t, a.bcast, (long)(m / a.bcast_group) * a.ld_bcast + n0, DT_F32, nvalid);
@@ -398,11 +405,11 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 if (a.act == ACT_GELU) {
                     if (a.out2) store32(a.out2, (long)m * a.ldo2 + n0, a.out2_dtype, v, nvalid);
                     #pragma unroll
-                    for (int j = 0; j < 32; j++) v[j] = gelu_f(v[j]);
+                    for (int j = 0; j < 32; j++) v[j] = gelu_fast(v[j]);
                 } else if (a.act == ACT_GELU_BWD) {
                     load32(t, a.aux, (long)m * a.ld_aux + n0, a.aux_dtype, nvalid);
                     #pragma unroll
-                    for (int j = 0; j < 32; j++) v[j] *= gelu_grad_f(t[j]);
+                    for (int j = 0; j < 32; j++) v[j] *= gelu_grad_fast(t[j]);
                 }
                 if (a.resid) {
                     load32(t, a.resid, orow * a.ld_resid + n0, DT_F32, nvalid);

@@ -100,8 +100,10 @@ __global__ void k_ln_fwd(TO* y, long ldy, float* mean, float* rstd, const float*
 }
 
 // dx = LN'(dy) (+ dx if accumulate), optional copy in T; dw/db accumulate.
-// dw/db: per-block shared partials then one atomicAdd per column per block.
-template <typename TC>
+// One warp per row; every lane owns columns lane + 32 i, so the dw/db
+// partials stay in registers across the block's rows and reach shared memory
+// once per warp, then global memory once per block.
+template <typename TC, int MAXC>
 __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long lddxc,
                          float* dw, float* db, const float* dy, long lddy,
                          const float* x, long ldx, const float* w, const float* mean,
@@ -111,29 +113,50 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
     float* sb = sh + D;
     for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) sh[i] = 0.f;
     __syncthreads();
+    // MAXC = columns per lane held in registers (D <= 32 * MAXC)
+    float pw[MAXC], pb[MAXC];
+    #pragma unroll
+    for (int c = 0; c < MAXC; c++) { pw[c] = 0.f; pb[c] = 0.f; }
+    const int nc = (D + 31) / 32;
     int nw = blockDim.x >> 5, wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int r0 = blockIdx.x * rows_per_block;
     int r1 = min(rows, r0 + rows_per_block);
-    for (int row = r0 + wid; row < r1; row += nw) {
-        const float* xr = x + (long)row * ldx;
-        const float* dyr = dy + (long)row * lddy;
-        float mu = mean[row], rs = rstd[row];
-        float s1 = 0.f, s2 = 0.f;
-        for (int i = lane; i < D; i += 32) {
-            float xh = (xr[i] - mu) * rs;
-            float g = dyr[i] * w[i];
-            s1 += g; s2 += g * xh;
-            atomicAdd(&sw[i], dyr[i] * xh);
-            atomicAdd(&sb[i], dyr[i]);
+    if (nc <= MAXC) {
+        for (int row = r0 + wid; row < r1; row += nw) {
+            const float* xr = x + (long)row * ldx;
+            const float* dyr = dy + (long)row * lddy;
+            float mu = mean[row], rs = rstd[row];
+            float xh[MAXC], g[MAXC];
+            float s1 = 0.f, s2 = 0.f;
+            #pragma unroll
+            for (int c = 0; c < MAXC; c++) {
+                int i = lane + 32 * c;
+                if (c < nc && i < D) {
+                    xh[c] = (xr[i] - mu) * rs;
+                    float dyv = dyr[i];
+                    g[c] = dyv * w[i];
+                    s1 += g[c]; s2 += g[c] * xh[c];
+                    pw[c] += dyv * xh[c];
+                    pb[c] += dyv;
+                }
+            }
+            float m1 = warp_sum(s1) / D, m2 = warp_sum(s2) / D;
+            float* dxr = dx + (long)row * lddx;
+            #pragma unroll
+            for (int c = 0; c < MAXC; c++) {
+                int i = lane + 32 * c;
+                if (c < nc && i < D) {
+                    float v = (g[c] - m1 - xh[c] * m2) * rs;
+                    if (accumulate) v += dxr[i];
+                    dxr[i] = v;
+                    if (dxc) st(&dxc[(long)row * lddxc + i], v);
+                }
+            }
         }
-        float m1 = warp_sum(s1) / D, m2 = warp_sum(s2) / D;
-        float* dxr = dx + (long)row * lddx;
-        for (int i = lane; i < D; i += 32) {
-            float xh = (xr[i] - mu) * rs;
-            float v = (dyr[i] * w[i] - m1 - xh * m2) * rs;
-            if (accumulate) v += dxr[i];
-            dxr[i] = v;
-            if (dxc) st(&dxc[(long)row * lddxc + i], v);
+        #pragma unroll
+        for (int c = 0; c < MAXC; c++) {
+            int i = lane + 32 * c;
+            if (c < nc && i < D) { atomicAdd(&sw[i], pw[c]); atomicAdd(&sb[i], pb[c]); }
         }
     }
     __syncthreads();

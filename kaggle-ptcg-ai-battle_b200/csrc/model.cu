@@ -302,12 +302,13 @@ static void ln_bwd(int dt, float* dx, int accumulate, void* dxc, float* dw, floa
     int rpb = 64;
     unsigned g = cdiv(rows, rpb);
     size_t sm = 2 * D * sizeof(float);
-    if (dt == DT_F32 || dxc == nullptr)
-        ++g_ptcg_launches, k_ln_bwd<float><<<g, 256, sm, s>>>(dx, D, accumulate, (float*)dxc, D, dw, db, dy, D, x, D,
-                                          w, mu, rs, rows, D, rpb);
-    else
-        ++g_ptcg_launches, k_ln_bwd<bf16><<<g, 256, sm, s>>>(dx, D, accumulate, (bf16*)dxc, D, dw, db, dy, D, x, D,
-                                         w, mu, rs, rows, D, rpb);
+#define LNB(TC, MC) ++g_ptcg_launches, k_ln_bwd<TC, MC><<<g, 256, sm, s>>>(dx, D, accumulate, \
+        (TC*)dxc, D, dw, db, dy, D, x, D, w, mu, rs, rows, D, rpb)
+    bool f = dt == DT_F32 || dxc == nullptr;
+    if (D <= 256) { if (f) LNB(float, 8); else LNB(bf16, 8); }
+    else if (D <= 512) { if (f) LNB(float, 16); else LNB(bf16, 16); }
+    else { if (f) LNB(float, 32); else LNB(bf16, 32); }
+#undef LNB
 }
 
 // ---------------------------------------------------------- workspace plan
@@ -700,7 +701,7 @@ static void tables_bwd(PtcgModel* M, cudaStream_t s) {
     // card LayerNorm (input card_in, ld 634) -> d_cardin
     {
         int rpb = 64;
-        ++g_ptcg_launches, k_ln_bwd<float><<<cdiv(z.NC, rpb), 256, 2 * 634 * sizeof(float), s>>>(t.d_cardin, 634, 0,
+        ++g_ptcg_launches, k_ln_bwd<float, 20><<<cdiv(z.NC, rpb), 256, 2 * 634 * sizeof(float), s>>>(t.d_cardin, 634, 0,
             nullptr, 634, M->w("card_ln_w").g, M->w("card_ln_b").g, t.d_cardln, 634, t.card_in, 634,
             M->w("card_ln_w").p, t.ln_mu, t.ln_rs, z.NC, 634, rpb);
     }
@@ -1452,6 +1453,19 @@ int ptcg_attention_bwd(int operand_dtype, const void* qkv, long ldqkv, const uns
         PTCG_EINVAL, "bad arguments");
     attn_bwd(operand_dtype == PTCG_BF16 ? DT_BF16 : DT_F32, qkv, ldqkv, keep, out, ldo, dout, lddo,
              lse, dqkv, lddqkv, dbias, nseq, L, H, (cudaStream_t)stream);
+    CKL();
+    return PTCG_OK;
+}
+
+static __global__ void k_eval_gelu(const float* x, float* g, float* dg, int n) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) { g[i] = gelu_fast(x[i]); dg[i] = gelu_grad_fast(x[i]); }
+}
+
+int ptcg_eval_gelu(const float* x, float* gelu, float* gelu_grad, int n, void* stream) {
+    REQ(x && gelu && gelu_grad && n >= 0, PTCG_EINVAL, "bad arguments");
+    if (n == 0) return PTCG_OK;
+    ++g_ptcg_launches, k_eval_gelu<<<cdiv(n, 256), 256, 0, (cudaStream_t)stream>>>(x, gelu, gelu_grad, n);
     CKL();
     return PTCG_OK;
 }

@@ -66,6 +66,7 @@ _SIGS = {
     "ptcg_kernel_timer": (I, [P, I]),
     "ptcg_launch_count": (C.c_longlong, []),
     "ptcg_tensor_cores": (I, []),
+    "ptcg_eval_gelu": (I, [P, P, P, I, P]),
     "ptcg_attention_fwd": (I, [I, P, L, P, P, L, P, I, I, I, P]),
     "ptcg_attention_bwd": (I, [I, P, L, P, P, L, P, L, P, P, L, P, I, I, I, P]),
     "ptcg_device_error": (I, []),

@@ -85,3 +85,20 @@ def test_tc_gemm_tf32(pkg, a_k, b_k, M, N, K):
     assert rc == 0, lib.ptcg_last_error()
     err = (out - ref).norm().item() / ref.norm().item()
     assert err < 2e-3, err
+
+
+def test_fast_gelu_error_bound(pkg):
+    """epilogue GELU / GELU' vs the exact erf form (torch, fp64)"""
+    import ptcg_b200.native as n
+    lib = n.lib()
+    x = torch.linspace(-12, 12, 2_000_001, dtype=torch.float32, device="cuda")
+    g = torch.empty_like(x); dg = torch.empty_like(x)
+    assert lib.ptcg_eval_gelu(C.c_void_p(x.data_ptr()), C.c_void_p(g.data_ptr()),
+                              C.c_void_p(dg.data_ptr()), x.numel(),
+                              C.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    xd = x.double()
+    cdf = 0.5 * (1 + torch.erf(xd / 2 ** 0.5))
+    pdf = torch.exp(-0.5 * xd * xd) / (2 * torch.pi) ** 0.5
+    ref_g, ref_dg = xd * cdf, cdf + xd * pdf
+    assert ((g.double() - ref_g).abs() / xd.abs().clamp(min=1)).max().item() < 5e-7
+    assert (dg.double() - ref_dg).abs().max().item() < 2e-6
