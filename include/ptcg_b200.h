@@ -203,6 +203,10 @@ int ptcg_weights_checksum(PtcgModel* m, unsigned int* out_dev, void* stream);
  * launch).  The reference's analogue is its cudaEvent phase timing
  * (ProfileT, native/src/pufferlib.cu:59-63, 1851-1953). */
 int ptcg_kernel_timer(PtcgModel* m, int mode);
+/* Per-launch record of the timed region (mode 3 times every GEMM): for up to
+ * max launches, ms[i] and meta[8 i ..] = {M, N, K, a_kmajor, b_kmajor, act,
+ * engine (1 tcgen05, 2 SIMT), operand dtype}; returns the count. */
+int ptcg_kernel_timer_entries(PtcgModel* m, int max, float* ms, int* meta);
 /* Number of CUDA kernels this library has launched in this process. */
 long long ptcg_launch_count(void);
 
@@ -234,6 +238,21 @@ int ptcg_attention_bwd(int operand_dtype, const void* qkv, long ldqkv, const uns
  * Abramowitz & Stegun 7.1.26), exposed so tests can bound their error
  * against the exact erf form of torch nn.GELU. */
 int ptcg_eval_gelu(const float* x, float* gelu, float* gelu_grad, int n, void* stream);
+/* tcgen05 GEMM role counters (clock cycles, summed over CTAs): {producer
+ * waiting for free ring slots, MMA waiting for loaded slots, MMA waiting for
+ * a free accumulator, epilogue waiting for a finished accumulator, epilogue
+ * working, CTA lifetime, tiles, launches, epilogue TMEM loads, epilogue math,
+ * epilogue store path} (12 counters).  Reads (if counters != NULL) and
+ * resets them, then enables (1) or disables (0) collection. */
+int ptcg_tc_profile(int enable, unsigned long long* counters);
+/* ptcg_gemm with the fused epilogue of the model's GEMMs: output dtype
+ * (PTCG_FP32 / PTCG_BF16), bias[N], act 1 = GELU (out2 <- GELU'(pre), may be
+ * NULL), act 2 = multiply by aux (the saved GELU'), colsum[N] += fp32 column
+ * sums (may be NULL).  aux / out2 use the output dtype. */
+int ptcg_gemm_ex(int M, int N, int K, const void* A, long lda, int a_kmajor, const void* B,
+                 long ldb, int b_kmajor, int operand_dtype, void* C, long ldc, int out_dtype,
+                 const float* bias, int act, const void* aux, long ld_aux, void* out2, long ldo2,
+                 float* colsum, int accumulate, int engine, void* stream);
 /* 1 when the tcgen05 engine is usable on the current device (sm_100). */
 int ptcg_tensor_cores(void);
 /* First error code a bounded device-side wait recorded since the last call

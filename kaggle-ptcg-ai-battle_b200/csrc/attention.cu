@@ -7,6 +7,8 @@
 // One CTA per (sequence, head); the whole K/V (and Q/dO in backward) of that
 // head stays in shared memory (L <= 257 -> <= 142 KB), so neither pass needs
 // atomics.  This SIMT version is the exact-fp32 path.
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -586,6 +588,201 @@ size_t bwd_smem(int L) {
     return sizeof(float) * (4 * L * PADW + 2 * Lr + 2 * NW * Lr);
 }
 
+// ============================================================ first row only
+// The critic block's output is read at its readout row alone
+// (ptcg/rl/model.py:305-308: oracle_v1(cat[x[:, 0], g])), so only query row
+// 0 of each sequence needs attention; keys and values still span every row.
+// One CTA per sequence, one warp per head, lane = key in the score pass and
+// lane = head dimension in the weighted sums.  fp32 arithmetic throughout
+// (memory-bound: it streams K and V once).
+
+PTCG_DEV void ld8(const float* p, float* f) {
+    float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+PTCG_DEV void ld8(const bf16* p, float* f) {
+    uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    #pragma unroll
+    for (int i = 0; i < 4; i++) {
+        float2 t = __bfloat1622float2(h[i]);
+        f[2 * i] = t.x; f[2 * i + 1] = t.y;
+    }
+}
+PTCG_DEV void st8(float* p, const float* f) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+}
+PTCG_DEV void st8(bf16* p, const float* f) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+    #pragma unroll
+    for (int i = 0; i < 4; i++) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+}
+
+// out[n, :] = softmax(q0 K^T / sqrt(32)) V per head; lse[n, h] natural-log
+// log-sum-exp of the scaled scores (-inf when every key is masked).
+template <typename T>
+__global__ void __launch_bounds__(512) k_attn_row0_fwd(
+        const T* __restrict__ qkv, long ldqkv, const uint8_t* __restrict__ keep,
+        T* __restrict__ out, long ldo, float* __restrict__ lse, int L, int H) {
+    extern __shared__ float sm[];
+    const int n = blockIdx.x, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int D = H * DH, Lr = (L + 31) & ~31;
+    float* qs = sm + h * DH;
+    float* p = sm + H * DH + h * Lr;
+    const T* base = qkv + (long)n * L * ldqkv;
+    const uint8_t* kp = keep + (long)n * L;
+    const float scale = 0.17677669529663687f;   // 1/sqrt(32)
+    qs[lane] = to_f<T>(base[h * DH + lane]) * scale;
+    __syncwarp();
+    float q[DH];
+    #pragma unroll
+    for (int d = 0; d < DH; d++) q[d] = qs[d];
+    float mx = -INFINITY;
+    for (int j = lane; j < L; j += 32) {
+        float s = -INFINITY;
+        if (kp[j]) {
+            const T* kr = base + (long)j * ldqkv + D + h * DH;
+            s = 0.f;
+            #pragma unroll
+            for (int c = 0; c < DH; c += 8) {
+                float k8[8];
+                ld8(kr + c, k8);
+                #pragma unroll
+                for (int e = 0; e < 8; e++) s = fmaf(q[c + e], k8[e], s);
+            }
+        }
+        p[j] = s;
+        mx = fmaxf(mx, s);
+    }
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int j = lane; j < L; j += 32) {
+        float e = p[j] == -INFINITY ? 0.f : expf(p[j] - mx);
+        p[j] = e;
+        sum += e;
+    }
+    sum = warp_sum(sum);
+    __syncwarp();
+    const T* vb = base + 2 * D + h * DH + lane;
+    float o = 0.f;
+    for (int j = 0; j < L; j++) {
+        float pj = p[j];
+        if (pj != 0.f) o = fmaf(pj, to_f<T>(vb[(long)j * ldqkv]), o);
+    }
+    out[(long)n * ldo + h * DH + lane] = from_f<T>(sum > 0.f ? o / sum : 0.f);
+    if (lane == 0) lse[(long)n * H + h] = sum > 0.f ? mx + logf(sum) : -INFINITY;
+}
+
+// Backward of k_attn_row0_fwd.  Writes every row of dqkv: dQ at row 0 and
+// zeros in the Q columns of rows 1.., dK / dV at every key (zero where
+// masked).  The QKV bias gradient (fp32, before rounding) accumulates into
+// dbias[3D]: per-thread partials over the sequences a CTA visits, one
+// atomic per column per CTA.
+template <typename T>
+__global__ void __launch_bounds__(512) k_attn_row0_bwd(
+        const T* __restrict__ qkv, long ldqkv, const uint8_t* __restrict__ keep,
+        const T* __restrict__ out, long ldo, const T* __restrict__ dout, long lddo,
+        const float* __restrict__ lse, T* __restrict__ dqkv, long lddqkv,
+        float* __restrict__ dbias, int R, int L, int H) {
+    extern __shared__ float sm[];
+    const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int D = H * DH, Lr = (L + 31) & ~31;
+    float* qs = sm + h * 2 * DH;
+    float* gs = qs + DH;
+    float* dsb = sm + H * 2 * DH + h * Lr;
+    const float scale = 0.17677669529663687f;
+    float cq = 0.f, ck = 0.f, cv = 0.f;
+    for (int n = blockIdx.x; n < R; n += gridDim.x) {
+        const T* base = qkv + (long)n * L * ldqkv;
+        T* dbase = dqkv + (long)n * L * lddqkv;
+        const uint8_t* kp = keep + (long)n * L;
+        float qd = to_f<T>(base[h * DH + lane]);
+        float gd = to_f<T>(dout[(long)n * lddo + h * DH + lane]);
+        float od = to_f<T>(out[(long)n * ldo + h * DH + lane]);
+        float delta = warp_sum(gd * od);
+        float l = lse[(long)n * H + h];
+        qs[lane] = qd; gs[lane] = gd;
+        __syncwarp();
+        float q[DH], g[DH];
+        #pragma unroll
+        for (int d = 0; d < DH; d++) { q[d] = qs[d]; g[d] = gs[d]; }
+        float sds = 0.f, sp = 0.f;
+        for (int j = lane; j < L; j += 32) {
+            float dsj = 0.f, pj = 0.f;
+            if (kp[j] && l != -INFINITY) {
+                const T* kr = base + (long)j * ldqkv + D + h * DH;
+                const T* vr = kr + D;
+                float s = 0.f, dp = 0.f;
+                #pragma unroll
+                for (int c = 0; c < DH; c += 8) {
+                    float k8[8], v8[8];
+                    ld8(kr + c, k8);
+                    ld8(vr + c, v8);
+                    #pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        s = fmaf(q[c + e], k8[e], s);
+                        dp = fmaf(g[c + e], v8[e], dp);
+                    }
+                }
+                pj = expf(s * scale - l);
+                dsj = pj * (dp - delta);
+            }
+            dsb[j] = dsj;
+            sds += dsj; sp += pj;
+            T* dr = dbase + (long)j * lddqkv + h * DH;
+            float t8[8];
+            #pragma unroll
+            for (int c = 0; c < DH; c += 8) {
+                #pragma unroll
+                for (int e = 0; e < 8; e++) t8[e] = scale * dsj * q[c + e];
+                st8(dr + D + c, t8);
+                #pragma unroll
+                for (int e = 0; e < 8; e++) t8[e] = pj * g[c + e];
+                st8(dr + 2 * D + c, t8);
+                if (j > 0) {
+                    #pragma unroll
+                    for (int e = 0; e < 8; e++) t8[e] = 0.f;
+                    st8(dr + c, t8);
+                }
+            }
+        }
+        __syncwarp();
+        const T* kb = base + D + h * DH + lane;
+        float dq = 0.f;
+        for (int j = 0; j < L; j++) {
+            float d = dsb[j];
+            if (d != 0.f) dq = fmaf(d, to_f<T>(kb[(long)j * ldqkv]), dq);
+        }
+        dq *= scale;
+        dbase[h * DH + lane] = from_f<T>(dq);
+        sds = warp_sum(sds);
+        sp = warp_sum(sp);
+        cq += dq;
+        ck += scale * sds * qd;
+        cv += sp * gd;
+        __syncwarp();
+    }
+    if (dbias) {
+        atomicAdd(&dbias[h * DH + lane], cq);
+        atomicAdd(&dbias[D + h * DH + lane], ck);
+        atomicAdd(&dbias[2 * D + h * DH + lane], cv);
+    }
+}
+
+int num_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 1;
+    }
+    return n;
+}
+
 template <typename K>
 void set_smem(K k, size_t bytes) {
     if (bytes > 48 * 1024)
@@ -607,6 +804,42 @@ void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
         set_smem(k_attn_fwd_mma, sm2);
         ++g_ptcg_launches, k_attn_fwd_mma<<<nseq * H, 128, sm2, s>>>((const bf16*)qkv, ldqkv, keep,
             (bf16*)out, ldo, lse, L, H);
+    }
+}
+
+void attn_row0_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
+                   void* out, long ldo, float* lse, int nseq, int L, int H, cudaStream_t s) {
+    if (nseq <= 0) return;
+    size_t sm = sizeof(float) * H * (DH + ((L + 31) & ~31));
+    if (dtype == DT_F32) {
+        set_smem(k_attn_row0_fwd<float>, sm);
+        ++g_ptcg_launches, k_attn_row0_fwd<float><<<nseq, H * 32, sm, s>>>((const float*)qkv, ldqkv,
+            keep, (float*)out, ldo, lse, L, H);
+    } else {
+        set_smem(k_attn_row0_fwd<bf16>, sm);
+        ++g_ptcg_launches, k_attn_row0_fwd<bf16><<<nseq, H * 32, sm, s>>>((const bf16*)qkv, ldqkv,
+            keep, (bf16*)out, ldo, lse, L, H);
+    }
+}
+
+void attn_row0_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
+                   const void* out, long ldo, const void* dout, long lddo,
+                   const float* lse, void* dqkv, long lddqkv, float* dbias, int nseq, int L,
+                   int H, cudaStream_t s) {
+    if (nseq <= 0) return;
+    size_t sm = sizeof(float) * H * (2 * DH + ((L + 31) & ~31));
+    int per_sm = H * 32 <= 256 ? 8 : 4;
+    unsigned grid = (unsigned)std::min<long>(nseq, (long)num_sms() * per_sm);
+    if (dtype == DT_F32) {
+        set_smem(k_attn_row0_bwd<float>, sm);
+        ++g_ptcg_launches, k_attn_row0_bwd<float><<<grid, H * 32, sm, s>>>((const float*)qkv, ldqkv,
+            keep, (const float*)out, ldo, (const float*)dout, lddo, lse, (float*)dqkv, lddqkv,
+            dbias, nseq, L, H);
+    } else {
+        set_smem(k_attn_row0_bwd<bf16>, sm);
+        ++g_ptcg_launches, k_attn_row0_bwd<bf16><<<grid, H * 32, sm, s>>>((const bf16*)qkv, ldqkv,
+            keep, (const bf16*)out, ldo, (const bf16*)dout, lddo, lse, (bf16*)dqkv, lddqkv,
+            dbias, nseq, L, H);
     }
 }
 

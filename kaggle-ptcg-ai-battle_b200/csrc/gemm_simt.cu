@@ -96,10 +96,10 @@ __global__ void __launch_bounds__(NT) k_gemm_simt(GemmArgs a) {
             if (a.bias) v += a.bias[n];
             if (a.bcast) v += a.bcast[(long)(m / a.bcast_group) * a.ld_bcast + n];
             if (a.act == ACT_GELU) {
-                if (a.out2) st_dt(a.out2, (long)m * a.ldo2 + n, a.out2_dtype, v);
+                if (a.out2) st_dt(a.out2, (long)m * a.ldo2 + n, a.out2_dtype, gelu_grad_f(v));
                 v = gelu_f(v);
             } else if (a.act == ACT_GELU_BWD) {
-                v *= gelu_grad_f(ld_dt(a.aux, (long)m * a.ld_aux + n, a.aux_dtype));
+                v *= ld_dt(a.aux, (long)m * a.ld_aux + n, a.aux_dtype);
             }
             if (a.resid) v += a.resid[orow * a.ld_resid + n];
             long oi = orow * a.ldo + n;

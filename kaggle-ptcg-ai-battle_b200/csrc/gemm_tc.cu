@@ -36,10 +36,17 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int NUM_EPI = 8;                   // epilogue warps (two per TMEM lane quadrant)
+constexpr int STAGE_W = 8192;                // TMA-store staging per epilogue warp (2 x 4 KB)
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI; // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
 constexpr long long WAIT_BUDGET = 4000000000LL;   // clock cycles (~2 s)
 
 __device__ int g_tc_error_dev;
+// optional per-role cycle counters (ptcg_tc_profile): 0 producer waiting on
+// free slots, 1 MMA waiting on loaded slots, 2 MMA waiting on a free TMEM
+// buffer, 3 epilogue waiting on a finished accumulator, 4 epilogue working,
+// 5 CTA lifetime, 6 tiles, 7 launches
+__device__ unsigned long long g_tc_prof[12];   // 8: TMEM load, 9: math, 10: store path
+__device__ int g_tc_prof_on;
 
 struct TcParams {
     int M, N, K;
@@ -51,6 +58,7 @@ struct TcParams {
     uint32_t idesc;
     uint32_t stage_bytes, a_bytes;
     uint32_t tmem_cols, acc_stride;
+    int tma_out;             // outputs leave through smem staging + TMA stores
     GemmArgs ep;
 };
 
@@ -76,23 +84,57 @@ PTCG_DEV bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 // bounded wait: false (and the abort flag set) when the budget runs out
-PTCG_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int code) {
+PTCG_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int code,
+                        long long* waited = nullptr) {
     long long t0 = clock64();
+    bool ok = true;
     while (!mbar_try(bar, parity)) {
-        if (*abort_flag) return false;
+        if (*abort_flag) { ok = false; break; }
         if (clock64() - t0 > WAIT_BUDGET) {
             *abort_flag = 1;
             atomicCAS(&g_tc_error_dev, 0, code);
-            return false;
+            ok = false;
+            break;
         }
     }
-    return true;
+    if (waited) *waited += clock64() - t0;
+    return ok;
 }
 PTCG_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
                  " [%0], [%1, {%3, %4}], [%2];"
                  :: "r"(dst), "l"((uint64_t)map), "r"(bar), "r"(x), "r"(y) : "memory");
 }
+PTCG_DEV void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 :: "l"((uint64_t)map), "r"(src), "r"(x), "r"(y) : "memory");
+}
+PTCG_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+PTCG_DEV void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+PTCG_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+PTCG_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Stage one warp's 32x32 chunk (lane = row) for a TMA store: fp32 rows of
+// 128 B in the 128-byte swizzle (16-byte granule g of row r at g ^ (r & 7)),
+// bf16 rows of 64 B in the 64-byte swizzle (granule g at g ^ ((r >> 1) & 3)).
+PTCG_DEV void stage32(uint8_t* buf, int lane, int dt, const float (&v)[32]) {
+    if (dt == DT_F32) {
+        #pragma unroll
+        for (int g = 0; g < 8; g++)
+            *(float4*)(buf + lane * 128 + ((g ^ (lane & 7)) << 4)) =
+                make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+    } else {
+        #pragma unroll
+        for (int g = 0; g < 4; g++) {
+            uint4 q;
+            __nv_bfloat162* h = (__nv_bfloat162*)&q;
+            #pragma unroll
+            for (int k = 0; k < 4; k++) h[k] = __floats2bfloat162_rn(v[8 * g + 2 * k], v[8 * g + 2 * k + 1]);
+            *(uint4*)(buf + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4)) = q;
+        }
+    }
+}
+
 PTCG_DEV void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 PTCG_DEV void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 template <int EB>
@@ -223,6 +265,7 @@ PTCG_DEV float warp_colsum32(float (&v)[32], int lane) {
 template <int EB>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+          const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_c2,
           const __grid_constant__ TcParams P) {
     constexpr int BK = 128 / EB;            // K elements per 128-byte row
     constexpr int ATOM = 128 / EB;          // MN elements per MN-major box
@@ -235,7 +278,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int S = P.stages;
-    uint64_t* bars = (uint64_t*)(smem + (size_t)S * P.stage_bytes);
+    uint8_t* staging = smem + (size_t)S * P.stage_bytes;          // NUM_EPI x 4 KB
+    uint64_t* bars = (uint64_t*)(staging + (P.tma_out ? NUM_EPI * STAGE_W : 0));
     // bars: full[S], empty[S], tfull[2], tempty[2], drain[1]
     uint32_t* tmem_slot = (uint32_t*)(bars + 2 * S + 5);
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
@@ -266,6 +310,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     fence_after();
     const uint32_t tmem = *tmem_slot;
     const int ntiles = P.m_tiles * P.n_tiles * P.splits;
+    const long long t_cta0 = clock64();
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
@@ -273,6 +318,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
+            long long w_empty = 0;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
                 int split = t % P.splits;
                 int mn = t / P.splits;
@@ -280,7 +326,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 int kb0 = split * P.kb_per_split;
                 int kb1 = min(P.kb_total, kb0 + P.kb_per_split);
                 for (int kb = kb0; kb < kb1; kb++) {
-                    if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, 1)) { ok = false; break; }
+                    if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, 1, &w_empty)) { ok = false; break; }
                     uint32_t fb = full0 + 8 * stage;
                     mbar_expect_tx(fb, P.stage_bytes);
                     uint32_t sa = smem_u32(smem + (size_t)stage * P.stage_bytes);
@@ -303,6 +349,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     (*n_issued)++;
                 }
             }
+            if (g_tc_prof_on) atomicAdd(&g_tc_prof[0], (unsigned long long)w_empty);
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
@@ -311,17 +358,18 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             uint32_t phase = 0;
             int local = 0;
             bool ok = true;
+            long long w_full = 0, w_tempty = 0;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, local++) {
                 int split = t % P.splits;
                 int kb0 = split * P.kb_per_split;
                 int kb1 = min(P.kb_total, kb0 + P.kb_per_split);
                 int buf = local & 1;
                 uint32_t tph = (local >> 1) & 1;
-                if (!mbar_wait(tempty0 + 8 * buf, tph ^ 1, abort_flag, 2)) { ok = false; break; }
+                if (!mbar_wait(tempty0 + 8 * buf, tph ^ 1, abort_flag, 2, &w_tempty)) { ok = false; break; }
                 fence_after();
                 uint32_t dcol = tmem + buf * P.acc_stride;
                 for (int kb = kb0; kb < kb1; kb++) {
-                    if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, 3)) { ok = false; break; }
+                    if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, 3, &w_full)) { ok = false; break; }
                     fence_after();
                     uint32_t sa = smem_u32(smem + (size_t)stage * P.stage_bytes);
                     uint32_t sb = sa + P.a_bytes;
@@ -340,6 +388,11 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 if (!ok) break;
                 mma_commit(tfull0 + 8 * buf);
             }
+            if (g_tc_prof_on) {
+                atomicAdd(&g_tc_prof[1], (unsigned long long)w_full);
+                atomicAdd(&g_tc_prof[2], (unsigned long long)w_tempty);
+                atomicAdd(&g_tc_prof[6], (unsigned long long)local);
+            }
             // make sure no MMA is in flight before TMEM is released
             mma_commit(drain);
             long long t0 = clock64();
@@ -353,13 +406,16 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
         const int row_in_tile = quad * 32 + lane;
         const GemmArgs& a = P.ep;
         int local = 0;
+        int nchunk = 0;
+        long long w_tfull = 0, busy = 0, c_ld = 0, c_math = 0, c_st = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, local++) {
             int split = t % P.splits;
             int mn = t / P.splits;
             int mt = mn / P.n_tiles, nt = mn % P.n_tiles;
             int buf = local & 1;
             uint32_t tph = (local >> 1) & 1;
-            if (!mbar_wait(tfull0 + 8 * buf, tph, abort_flag, 4)) break;
+            if (!mbar_wait(tfull0 + 8 * buf, tph, abort_flag, 4, &w_tfull)) break;
+            long long tb = clock64();
             fence_after();
             const int m = mt * BM + row_in_tile;
             const bool row_ok = m < a.M;
@@ -369,7 +425,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             const uint32_t tbase = tmem + buf * P.acc_stride + ((uint32_t)(quad * 32) << 16);
             for (int c0 = half * 32; c0 < P.bn; c0 += 64) {
                 uint32_t r[32];
+                long long ck0 = clock64();
                 tmem_ld32(tbase + c0, r);
+                long long ck1 = clock64();
+                c_ld += ck1 - ck0;
                 const int n0 = nt * P.bn + c0;
                 float v[32];
                 #pragma unroll
@@ -385,11 +444,30 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 if (P.splits > 1) {                              // warp-uniform
                     if (row_ok) {
                         float* o = (float*)a.out + orow * a.ldo + n0;
-                        #pragma unroll
-                        for (int j = 0; j < 32; j++) if (j < nvalid) atomicAdd(o + j, v[j]);
+                        if (nvalid == 32 && ((uintptr_t)o & 15) == 0) {
+                            #pragma unroll
+                            for (int j = 0; j < 32; j += 4)
+                                asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};"
+                                             :: "l"(o + j), "f"(v[j]), "f"(v[j + 1]), "f"(v[j + 2]),
+                                                "f"(v[j + 3]) : "memory");
+                        } else {
+                            #pragma unroll
+                            for (int j = 0; j < 32; j++) if (j < nvalid) atomicAdd(o + j, v[j]);
+                        }
                     }
                     continue;
                 }
+                // double-buffered staging: the buffer written now was last
+                // used two chunks ago; at most one store group may still read
+                uint8_t* sbuf = staging + (warp - 2) * STAGE_W + (nchunk & 1) * 4096;
+                nchunk++;
+                long long ck2 = clock64();
+                if (P.tma_out) {
+                    if (lane == 0) bulk_wait_read1();
+                    __syncwarp();
+                }
+                long long ck3 = clock64();
+                c_st += ck3 - ck2;
                 if (row_ok) {
                 float t[32];
                 if (a.bias) {
@@ -403,13 +481,24 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     for (int j = 0; j < 32; j++) v[j] += t[j];
                 }
                 if (a.act == ACT_GELU) {
-                    if (a.out2) store32(a.out2, (long)m * a.ldo2 + n0, a.out2_dtype, v, nvalid);
-                    #pragma unroll
-                    for (int j = 0; j < 32; j++) v[j] = gelu_fast(v[j]);
+                    if (a.out2) {
+                        #pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            float c, pd;
+                            gelu_parts_fast(v[j], c, pd);
+                            t[j] = fmaf(v[j], pd, c);         // GELU'(x), saved for backward
+                            v[j] *= c;
+                        }
+                        if (P.tma_out) stage32(sbuf + 2048, lane, DT_BF16, t);
+                        else store32(a.out2, (long)m * a.ldo2 + n0, a.out2_dtype, t, nvalid);
+                    } else {
+                        #pragma unroll
+                        for (int j = 0; j < 32; j++) v[j] = gelu_fast(v[j]);
+                    }
                 } else if (a.act == ACT_GELU_BWD) {
                     load32(t, a.aux, (long)m * a.ld_aux + n0, a.aux_dtype, nvalid);
                     #pragma unroll
-                    for (int j = 0; j < 32; j++) v[j] *= gelu_grad_fast(t[j]);
+                    for (int j = 0; j < 32; j++) v[j] *= t[j];
                 }
                 if (a.resid) {
                     load32(t, a.resid, orow * a.ld_resid + n0, DT_F32, nvalid);
@@ -421,10 +510,24 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     #pragma unroll
                     for (int j = 0; j < 32; j++) v[j] += t[j];
                 }
-                store32(a.out, orow * a.ldo + n0, a.out_dtype, v, nvalid);
-                if (a.act != ACT_GELU && a.out2)
+                if (P.tma_out) stage32(sbuf, lane, a.out_dtype, v);
+                else store32(a.out, orow * a.ldo + n0, a.out_dtype, v, nvalid);
+                if (!P.tma_out && a.act != ACT_GELU && a.out2)
                     store32(a.out2, orow * a.ldo2 + n0, a.out2_dtype, v, nvalid);
                 }   // row_ok
+                long long ck4 = clock64();
+                c_math += ck4 - ck3;
+                if (P.tma_out) {
+                    // rows past M and columns past N are clipped by the TMA unit
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        int y = mt * BM + quad * 32;
+                        tma_store_2d(&map_c, smem_u32(sbuf), n0, y);
+                        if (a.act == ACT_GELU && a.out2) tma_store_2d(&map_c2, smem_u32(sbuf + 2048), n0, y);
+                        bulk_commit();
+                    }
+                }
                 #pragma unroll
                 for (int j = 0; j < 32; j++) if (j >= nvalid || !row_ok) v[j] = 0.f;
                 if (a.colsum) {
@@ -436,6 +539,15 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
+            busy += clock64() - tb;
+        }
+        if (P.tma_out && lane == 0) bulk_wait_all();
+        if (g_tc_prof_on && lane == 0) {
+            atomicAdd(&g_tc_prof[3], (unsigned long long)w_tfull);
+            atomicAdd(&g_tc_prof[8], (unsigned long long)c_ld);
+            atomicAdd(&g_tc_prof[9], (unsigned long long)c_math);
+            atomicAdd(&g_tc_prof[10], (unsigned long long)c_st);
+            atomicAdd(&g_tc_prof[4], (unsigned long long)busy);
         }
     }
     fence_before();
@@ -450,6 +562,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
         }
     }
     __syncthreads();
+    if (threadIdx.x == 0 && g_tc_prof_on) {
+        atomicAdd(&g_tc_prof[5], (unsigned long long)(clock64() - t_cta0));
+        if (blockIdx.x == 0) atomicAdd(&g_tc_prof[7], 1ull);
+    }
     if (warp == 1) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
                      :: "r"(tmem), "r"(P.tmem_cols) : "memory");
@@ -491,6 +607,14 @@ void init_once() {
 
 }  // namespace
 
+int ptcg_tc_profile_ctl(int enable, unsigned long long* out8) {
+    if (out8) cudaMemcpyFromSymbol(out8, g_tc_prof, sizeof(unsigned long long) * 12);
+    unsigned long long z[12] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+    cudaMemcpyToSymbol(g_tc_prof, z, sizeof z);
+    cudaMemcpyToSymbol(g_tc_prof_on, &enable, sizeof(int));
+    return 0;
+}
+
 int ptcg_tc_error_read_reset() {
     int v = 0, zero = 0;
     cudaMemcpyFromSymbol(&v, g_tc_error_dev, sizeof(int));
@@ -524,8 +648,22 @@ bool make_map_eb(CUtensorMap* m, const void* ptr, long inner, long outer, long l
 struct TcPlan {
     TcParams P;
     int eb;
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, mc, mc2;
 };
+
+// output map for TMA stores: box {32 columns, 32 rows}
+bool make_out_map(CUtensorMap* m, void* ptr, long n, long rows, long ld, int dt) {
+    int eb = dt == DT_F32 ? 4 : 2;
+    cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * eb};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = g_encode(m, dt == DT_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                          2, ptr, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          dt == DT_F32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
 
 bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     if (!gemm_tc_available()) return false;
@@ -566,7 +704,14 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     P.splits = (P.kb_total + P.kb_per_split - 1) / P.kb_per_split;   // no empty splits
     P.a_bytes = BM * 128;
     P.stage_bytes = P.a_bytes + P.b_rows * 128;
-    int budget = 200 * 1024;
+    // outputs through smem + TMA store: plain row mapping, no read-modify-
+    // write, whole 32-column chunks per tile, 16-byte aligned pitch
+    int oeb = a.out_dtype == DT_F32 ? 4 : 2;
+    P.tma_out = P.splits == 1 && a.remap_group == 0 && !a.accumulate && (bn % 32) == 0 &&
+                !((uintptr_t)a.out & 15) && (a.ldo * oeb) % 16 == 0 &&
+                (!a.out2 || (a.act == ACT_GELU && a.out2_dtype == DT_BF16 && a.out_dtype == DT_BF16 &&
+                             !((uintptr_t)a.out2 & 15) && (a.ldo2 * 2) % 16 == 0));
+    int budget = 232448 - 1024 - 512 - (P.tma_out ? NUM_EPI * STAGE_W : 0);
     P.stages = budget / P.stage_bytes;
     if (P.stages > 6) P.stages = 6;
     if (P.stages < 2) return false;
@@ -585,20 +730,27 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     if (!ok) return false;
     if (P.b_mn) ok = make_map_eb(&pl.mb, a.B, a.N, a.K, a.ldb, ATOM, BK, eb, true);
     else ok = make_map_eb(&pl.mb, a.B, a.K, a.N, a.ldb, BK, bn, eb, false);
-    return ok;
+    if (!ok) return false;
+    pl.mc = pl.ma; pl.mc2 = pl.ma;
+    if (P.tma_out) {
+        if (!make_out_map(&pl.mc, a.out, a.N, a.M, a.ldo, a.out_dtype)) return false;
+        if (a.out2 && !make_out_map(&pl.mc2, a.out2, a.N, a.M, a.ldo2, DT_BF16)) return false;
+    }
+    return true;
 }
 
 void launch_tc(const TcPlan& pl, cudaStream_t s) {
     const TcParams& P = pl.P;
-    size_t smem = 1024 + (size_t)P.stages * P.stage_bytes + (2 * P.stages + 5) * 8 + 32;
+    size_t smem = 1024 + (size_t)P.stages * P.stage_bytes + (P.tma_out ? NUM_EPI * STAGE_W : 0) +
+                  (2 * P.stages + 5) * 8 + 32;
     int total = P.m_tiles * P.n_tiles * P.splits;
     int grid = total < g_sms ? total : g_sms;
     if (pl.eb == 2) {
         cudaFuncSetAttribute(k_gemm_tc<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        ++g_ptcg_launches, k_gemm_tc<2><<<grid, NUM_THREADS, smem, s>>>(pl.ma, pl.mb, P);
+        ++g_ptcg_launches, k_gemm_tc<2><<<grid, NUM_THREADS, smem, s>>>(pl.ma, pl.mb, pl.mc, pl.mc2, P);
     } else {
         cudaFuncSetAttribute(k_gemm_tc<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        ++g_ptcg_launches, k_gemm_tc<4><<<grid, NUM_THREADS, smem, s>>>(pl.ma, pl.mb, P);
+        ++g_ptcg_launches, k_gemm_tc<4><<<grid, NUM_THREADS, smem, s>>>(pl.ma, pl.mb, pl.mc, pl.mc2, P);
     }
 }
 

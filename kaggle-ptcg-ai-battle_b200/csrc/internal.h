@@ -13,7 +13,9 @@ enum { ACT_NONE = 0, ACT_GELU = 1, ACT_GELU_BWD = 2 };
 //   A(m,k) = a_kmajor ? A[m*lda + k] : A[k*lda + m]
 //   B(n,k) = b_kmajor ? B[n*ldb + k] : B[k*ldb + n]
 // epilogue, in order: + bias[n]; + bcast[(m / bcast_group) * ld_bcast + n];
-//   act (GELU: pre-activation to out2 if set; GELU_BWD: * gelu'(aux[m, n]));
+//   act (GELU: out2, if set, receives GELU'(pre-activation) -- the factor
+//   the backward needs, so it never re-evaluates erf; GELU_BWD: * aux[m, n],
+//   the saved GELU');
 //   output row r = remap(m); + resid[r * ld_resid + n]; + out[r, n] if
 //   accumulate; store to out (f32 or operand dtype); for act != GELU an out2
 //   receives a second copy of the final value.
@@ -46,11 +48,21 @@ bool gemm_tc_supported(const GemmArgs& a);
 bool gemm_tc_available();
 // first error code recorded by a tcgen05 kernel since the last call (0 = none)
 int ptcg_tc_error_read_reset();
+int ptcg_tc_profile_ctl(int enable, unsigned long long* out8);
 
 // attention over packed qkv rows: qkv [(n*L + l) * ldqkv + {0,D,2D} + h*32 + d]
 void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
               void* out, long ldo, float* lse, int nseq, int L, int H,
               cudaStream_t s);
+// first query row of each sequence only: out / dout [n * ldo + h*32 + d],
+// lse [n * H + h]; every row of dqkv is written (Q columns zero past row 0).
+// H <= 16.
+void attn_row0_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
+                   void* out, long ldo, float* lse, int nseq, int L, int H, cudaStream_t s);
+void attn_row0_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
+                   const void* out, long ldo, const void* dout, long lddo,
+                   const float* lse, void* dqkv, long lddqkv, float* dbias, int nseq, int L,
+                   int H, cudaStream_t s);
 // dbias (nullable, 3*H*32 floats): += column sums of dqkv in fp32
 void attn_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
               const void* out, long ldo, const void* dout, long lddo,

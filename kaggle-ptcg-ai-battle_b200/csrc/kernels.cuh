@@ -80,14 +80,50 @@ __global__ void k_pool_bwd(float* d_tab, const float* dsrc, int ld, int off_mean
 }
 
 // ------------------------------------------------------------- LayerNorm
-// one warp per row, eps 1e-5 (torch nn.LayerNorm), two-pass statistics
-template <typename TO>
+// one warp per row, eps 1e-5 (torch nn.LayerNorm), two-pass statistics.
+// VEC: D % 128 == 0 and 16-byte aligned rows -> each lane owns 4 consecutive
+// columns of every 128-column chunk (float4 loads, 8-byte bf16 stores).
+template <typename TO, int VEC>
 __global__ void k_ln_fwd(TO* y, long ldy, float* mean, float* rstd, const float* x,
                          long ldx, const float* w, const float* b, int rows, int D) {
     int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     int lane = threadIdx.x & 31;
     if (row >= rows) return;
     const float* xr = x + (long)row * ldx;
+    TO* yr = y + (long)row * ldy;
+    if (VEC > 0) {
+        float4 v[VEC > 0 ? VEC : 1];
+        float s = 0.f;
+        #pragma unroll
+        for (int c = 0; c < VEC; c++) {
+            v[c] = *(const float4*)(xr + c * 128 + lane * 4);
+            s += v[c].x + v[c].y + v[c].z + v[c].w;
+        }
+        float mu = warp_sum(s) / D;
+        float q = 0.f;
+        #pragma unroll
+        for (int c = 0; c < VEC; c++) {
+            float a0 = v[c].x - mu, a1 = v[c].y - mu, a2 = v[c].z - mu, a3 = v[c].w - mu;
+            q += a0 * a0 + a1 * a1 + a2 * a2 + a3 * a3;
+        }
+        float rs = rsqrtf(warp_sum(q) / D + 1e-5f);
+        if (lane == 0) { mean[row] = mu; rstd[row] = rs; }
+        #pragma unroll
+        for (int c = 0; c < VEC; c++) {
+            int i = c * 128 + lane * 4;
+            float4 wv = *(const float4*)(w + i), bv = *(const float4*)(b + i);
+            float o0 = (v[c].x - mu) * rs * wv.x + bv.x, o1 = (v[c].y - mu) * rs * wv.y + bv.y;
+            float o2 = (v[c].z - mu) * rs * wv.z + bv.z, o3 = (v[c].w - mu) * rs * wv.w + bv.w;
+            if (sizeof(TO) == 4) {
+                *(float4*)((float*)yr + i) = make_float4(o0, o1, o2, o3);
+            } else {
+                __nv_bfloat162 h0 = __floats2bfloat162_rn(o0, o1), h1 = __floats2bfloat162_rn(o2, o3);
+                uint2 u; u.x = *(uint32_t*)&h0; u.y = *(uint32_t*)&h1;
+                *(uint2*)((bf16*)yr + i) = u;
+            }
+        }
+        return;
+    }
     float s = 0.f;
     for (int i = lane; i < D; i += 32) s += xr[i];
     float mu = warp_sum(s) / D;
@@ -95,15 +131,17 @@ __global__ void k_ln_fwd(TO* y, long ldy, float* mean, float* rstd, const float*
     for (int i = lane; i < D; i += 32) { float d = xr[i] - mu; v += d * d; }
     float rs = rsqrtf(warp_sum(v) / D + 1e-5f);
     if (lane == 0) { mean[row] = mu; rstd[row] = rs; }
-    TO* yr = y + (long)row * ldy;
     for (int i = lane; i < D; i += 32) st(&yr[i], (xr[i] - mu) * rs * w[i] + b[i]);
 }
 
 // dx = LN'(dy) (+ dx if accumulate), optional copy in T; dw/db accumulate.
-// One warp per row; every lane owns columns lane + 32 i, so the dw/db
-// partials stay in registers across the block's rows and reach shared memory
-// once per warp, then global memory once per block.
-template <typename TC, int MAXC>
+// One warp per row with every load of the row (x, dy and the dx being
+// accumulated into) issued before the reductions; the dw/db partials stay in
+// registers across the block's rows, reach shared memory once per warp and
+// global memory once per block.  VEC > 0: D = 128 * VEC, float4 access (lane
+// owns 4 consecutive columns of each 128-column chunk); VEC == 0: generic D
+// (<= 32 * MAXC) with scalar access.
+template <typename TC, int VEC, int MAXC>
 __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long lddxc,
                          float* dw, float* db, const float* dy, long lddy,
                          const float* x, long ldx, const float* w, const float* mean,
@@ -113,20 +151,83 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
     float* sb = sh + D;
     for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) sh[i] = 0.f;
     __syncthreads();
-    // MAXC = columns per lane held in registers (D <= 32 * MAXC)
-    float pw[MAXC], pb[MAXC];
-    #pragma unroll
-    for (int c = 0; c < MAXC; c++) { pw[c] = 0.f; pb[c] = 0.f; }
-    const int nc = (D + 31) / 32;
     int nw = blockDim.x >> 5, wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int r0 = blockIdx.x * rows_per_block;
     int r1 = min(rows, r0 + rows_per_block);
-    if (nc <= MAXC) {
+    if (VEC > 0) {
+        float4 pw[VEC > 0 ? VEC : 1], pb[VEC > 0 ? VEC : 1], wv[VEC > 0 ? VEC : 1];
+        #pragma unroll
+        for (int c = 0; c < VEC; c++) {
+            pw[c] = make_float4(0, 0, 0, 0); pb[c] = make_float4(0, 0, 0, 0);
+            wv[c] = *(const float4*)(w + c * 128 + lane * 4);
+        }
         for (int row = r0 + wid; row < r1; row += nw) {
             const float* xr = x + (long)row * ldx;
             const float* dyr = dy + (long)row * lddy;
+            float* dxr = dx + (long)row * lddx;
+            float4 xv[VEC > 0 ? VEC : 1], gv[VEC > 0 ? VEC : 1], av[VEC > 0 ? VEC : 1];
+            #pragma unroll
+            for (int c = 0; c < VEC; c++) {
+                int i = c * 128 + lane * 4;
+                xv[c] = *(const float4*)(xr + i);
+                gv[c] = *(const float4*)(dyr + i);
+                av[c] = accumulate ? *(const float4*)(dxr + i) : make_float4(0, 0, 0, 0);
+            }
             float mu = mean[row], rs = rstd[row];
-            float xh[MAXC], g[MAXC];
+            float s1 = 0.f, s2 = 0.f;
+            #pragma unroll
+            for (int c = 0; c < VEC; c++) {
+                float h0 = (xv[c].x - mu) * rs, h1 = (xv[c].y - mu) * rs;
+                float h2 = (xv[c].z - mu) * rs, h3 = (xv[c].w - mu) * rs;
+                pw[c].x += gv[c].x * h0; pw[c].y += gv[c].y * h1;
+                pw[c].z += gv[c].z * h2; pw[c].w += gv[c].w * h3;
+                pb[c].x += gv[c].x; pb[c].y += gv[c].y; pb[c].z += gv[c].z; pb[c].w += gv[c].w;
+                float g0 = gv[c].x * wv[c].x, g1 = gv[c].y * wv[c].y;
+                float g2 = gv[c].z * wv[c].z, g3 = gv[c].w * wv[c].w;
+                s1 += g0 + g1 + g2 + g3;
+                s2 += g0 * h0 + g1 * h1 + g2 * h2 + g3 * h3;
+                xv[c] = make_float4(h0, h1, h2, h3);          // keep x-hat
+                gv[c] = make_float4(g0, g1, g2, g3);          // keep dy * w
+            }
+            float m1 = warp_sum(s1) / D, m2 = warp_sum(s2) / D;
+            #pragma unroll
+            for (int c = 0; c < VEC; c++) {
+                int i = c * 128 + lane * 4;
+                float o0 = (gv[c].x - m1 - xv[c].x * m2) * rs + av[c].x;
+                float o1 = (gv[c].y - m1 - xv[c].y * m2) * rs + av[c].y;
+                float o2 = (gv[c].z - m1 - xv[c].z * m2) * rs + av[c].z;
+                float o3 = (gv[c].w - m1 - xv[c].w * m2) * rs + av[c].w;
+                *(float4*)(dxr + i) = make_float4(o0, o1, o2, o3);
+                if (dxc) {
+                    if (sizeof(TC) == 4) {
+                        *(float4*)((float*)dxc + (long)row * lddxc + i) = make_float4(o0, o1, o2, o3);
+                    } else {
+                        __nv_bfloat162 q0 = __floats2bfloat162_rn(o0, o1), q1 = __floats2bfloat162_rn(o2, o3);
+                        uint2 u; u.x = *(uint32_t*)&q0; u.y = *(uint32_t*)&q1;
+                        *(uint2*)((bf16*)dxc + (long)row * lddxc + i) = u;
+                    }
+                }
+            }
+        }
+        #pragma unroll
+        for (int c = 0; c < VEC; c++) {
+            int i = c * 128 + lane * 4;
+            atomicAdd(&sw[i], pw[c].x); atomicAdd(&sw[i + 1], pw[c].y);
+            atomicAdd(&sw[i + 2], pw[c].z); atomicAdd(&sw[i + 3], pw[c].w);
+            atomicAdd(&sb[i], pb[c].x); atomicAdd(&sb[i + 1], pb[c].y);
+            atomicAdd(&sb[i + 2], pb[c].z); atomicAdd(&sb[i + 3], pb[c].w);
+        }
+    } else {
+        float pw[MAXC], pb[MAXC];
+        #pragma unroll
+        for (int c = 0; c < MAXC; c++) { pw[c] = 0.f; pb[c] = 0.f; }
+        const int nc = (D + 31) / 32;
+        for (int row = r0 + wid; row < r1; row += nw) {
+            const float* xr = x + (long)row * ldx;
+            const float* dyr = dy + (long)row * lddy;
+            float* dxr = dx + (long)row * lddx;
+            float mu = mean[row], rs = rstd[row];
+            float xh[MAXC], g[MAXC], acc[MAXC];
             float s1 = 0.f, s2 = 0.f;
             #pragma unroll
             for (int c = 0; c < MAXC; c++) {
@@ -134,6 +235,7 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
                 if (c < nc && i < D) {
                     xh[c] = (xr[i] - mu) * rs;
                     float dyv = dyr[i];
+                    acc[c] = accumulate ? dxr[i] : 0.f;
                     g[c] = dyv * w[i];
                     s1 += g[c]; s2 += g[c] * xh[c];
                     pw[c] += dyv * xh[c];
@@ -141,13 +243,11 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
                 }
             }
             float m1 = warp_sum(s1) / D, m2 = warp_sum(s2) / D;
-            float* dxr = dx + (long)row * lddx;
             #pragma unroll
             for (int c = 0; c < MAXC; c++) {
                 int i = lane + 32 * c;
                 if (c < nc && i < D) {
-                    float v = (g[c] - m1 - xh[c] * m2) * rs;
-                    if (accumulate) v += dxr[i];
+                    float v = (g[c] - m1 - xh[c] * m2) * rs + acc[c];
                     dxr[i] = v;
                     if (dxc) st(&dxc[(long)row * lddxc + i], v);
                 }
@@ -379,7 +479,8 @@ __global__ void k_rowdot(float* out, long os, const TI* in, long ldi, const floa
     if (lane == 0) out[r * os] = s + b[0];
 }
 
-// backward of out = dot(gelu(pre), w) + b:  d_pre = d * w * gelu'(pre) (TO),
+// backward of out = dot(gelu(pre), w) + b:  d_pre = d * w * gp (TO) where
+// gp = GELU'(pre) saved by the forward epilogue,
 // dw += sum_r d * in, db += sum_r d.  d from a strided buffer, or (mode 1,
 // blind-V aux) d = coef * (v - ret) / norm with v from the strided buffer.
 template <typename TI, typename TO>
@@ -403,7 +504,7 @@ __global__ void k_rowdot_bwd(TO* d_pre, long ldd, const TI* pre, long ldp, const
             }
             acc += d * to_f<TI>(in[(long)r * ldi + k]);
             float v = d * wk;
-            if (pre) v *= gelu_grad_f(to_f<TI>(pre[(long)r * ldp + k]));
+            if (pre) v *= to_f<TI>(pre[(long)r * ldp + k]);          // saved GELU'
             st(&d_pre[(long)r * ldd + k], v);
             csum += v;
             if (k == 0) dbp += d;
@@ -506,6 +607,15 @@ __global__ void k_val_in_bwd(float* d_seq, int seqlen, int D, float* d_gd, const
         float* p = &d_seq[(long)n * seqlen * D + c];
         *p = accum_seq ? *p + v : v;
     } else d_gd[(long)n * 192 + (c - D)] += v;
+}
+
+// dst[n * seq_stride + c] += src[n * D + c]: the readout-row residual grad
+// of a block computed on its first row only
+__global__ void k_add_rows(float* dst, long seq_stride, const float* src, int R, int D) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * D) return;
+    int n = (int)(i / D), c = (int)(i % D);
+    dst[(long)n * seq_stride + c] += src[i];
 }
 
 // critic input grad split: row 0 -> d_creadout, rows 1..LSEQ -> d_h +=,
@@ -976,7 +1086,7 @@ __global__ void k_step_inc(long long* step_dev, const float* stats) {
 
 __global__ void k_gelu_bwd(float* d, const float* pre, long n) {
     long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i < n) d[i] *= gelu_grad_f(pre[i]);
+    if (i < n) d[i] *= pre[i];                                    // saved GELU'
 }
 
 // refresh bf16 copies from the master weights (after a load)

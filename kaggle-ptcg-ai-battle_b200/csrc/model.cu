@@ -13,7 +13,9 @@
 //  * concat-then-Linear of gathered table rows becomes Linear-per-table-row
 //    then gather where the table is small (opt_card / opt_attack);
 //  * the static card / attack / skill tables are built once per train step
-//    and their gradient is accumulated across micro-batches.
+//    and their gradient is accumulated across micro-batches;
+//  * every GELU layer saves GELU'(pre-activation) (the buffers named *pre),
+//    so the backward multiplies instead of re-evaluating erf.
 #include "kernels.cuh"
 #include "ptcg_b200.h"
 
@@ -138,8 +140,8 @@ struct Work {
     float *bvin; void* bvinc; float *bv1pre, *bv1, *blind_v, *hand_lin, *prize_logit;
     // backward scratch
     float *dh, *dgd, *dbvin, *d_v1pre, *dscores, *dscin, *dqin, *dtokcat, *ddecin, *dd1,
-          *dg1, *dbc, *dotokin, *dx, *dln;
-    void *dxc, *dhand, *ds1pre, *dq, *dq1, *dotok, *dtokp, *df, *datt, *dqkv;
+          *dg1, *dbc, *dotokin, *dx, *dln, *dx0;
+    void *dx0c, *dxc, *dhand, *ds1pre, *dq, *dq1, *dotok, *dtokp, *df, *datt, *dqkv;
     float* dgrad;                       // PPO grad for one micro-batch (train_step)
     float* fused;                       // fused [scores | value] of one micro-batch
     float *ppo_scratch, *nlp, *ratio;
@@ -155,11 +157,12 @@ struct Tab {                            // batch-independent table activations +
 
 // CUDA-event timing of one GEMM kernel class over a region (bench roofline)
 struct KTimer {
-    int mode = 0;                       // 0 off, 1 tensor-core GEMM, 2 SIMT GEMM
+    int mode = 0;                       // 0 off, 1 tensor-core GEMM, 2 SIMT GEMM, 3 all GEMMs
     std::vector<cudaEvent_t> ev;
     int used = 0;
     double flops = 0.0;
     long launches = 0;
+    std::vector<int> meta;              // per timed launch: M N K a_kmajor b_kmajor act engine dtype
 };
 
 struct PtcgModel {
@@ -234,7 +237,7 @@ static void kt_mark(PtcgModel* M, cudaStream_t s) {
 static void gemm(PtcgModel* M, const GemmArgs& a, cudaStream_t s) {
     bool tc_ok = (a.dtype == DT_BF16 || a.allow_tf32) && gemm_tc_supported(a);
     int cls = tc_ok ? 1 : 2;
-    bool timed = M->kt.mode == cls;
+    bool timed = M->kt.mode == cls || M->kt.mode == 3;
     if (timed) kt_mark(M, s);
     bool done = tc_ok && gemm_tc(a, s);
     if (!done) gemm_simt(a, s);
@@ -242,6 +245,8 @@ static void gemm(PtcgModel* M, const GemmArgs& a, cudaStream_t s) {
         kt_mark(M, s);
         M->kt.flops += 2.0 * a.M * a.N * a.K;
         M->kt.launches++;
+        int meta[8] = {a.M, a.N, a.K, a.a_kmajor, a.b_kmajor, a.act, cls, a.dtype};
+        M->kt.meta.insert(M->kt.meta.end(), meta, meta + 8);
     }
 }
 
@@ -292,8 +297,12 @@ template <typename T> static void colsum(float* out, const T* in, long ld, int r
 static void ln_fwd(int dt, void* y, long ldy, float* mu, float* rs, const float* x, long ldx,
                    const float* w, const float* b, int rows, int D, cudaStream_t s) {
     unsigned g = cdiv(rows, 8);
-    if (dt == DT_F32) ++g_ptcg_launches, k_ln_fwd<float><<<g, 256, 0, s>>>((float*)y, ldy, mu, rs, x, ldx, w, b, rows, D);
-    else ++g_ptcg_launches, k_ln_fwd<bf16><<<g, 256, 0, s>>>((bf16*)y, ldy, mu, rs, x, ldx, w, b, rows, D);
+    bool vec = D % 128 == 0 && D <= 1024 && ldx % 4 == 0 && ldy % 4 == 0;
+#define LNF(TO, V) ++g_ptcg_launches, k_ln_fwd<TO, V><<<g, 256, 0, s>>>((TO*)y, ldy, mu, rs, x, ldx, w, b, rows, D)
+    if (vec && D == 256) { if (dt == DT_F32) LNF(float, 2); else LNF(bf16, 2); }
+    else if (vec && D == 512) { if (dt == DT_F32) LNF(float, 4); else LNF(bf16, 4); }
+    else { if (dt == DT_F32) LNF(float, 0); else LNF(bf16, 0); }
+#undef LNF
 }
 // dx (f32, ld D) = LN'(dy) (+ dx), copy to dxc (T) unless dxc == nullptr
 static void ln_bwd(int dt, float* dx, int accumulate, void* dxc, float* dw, float* db,
@@ -302,12 +311,14 @@ static void ln_bwd(int dt, float* dx, int accumulate, void* dxc, float* dw, floa
     int rpb = 64;
     unsigned g = cdiv(rows, rpb);
     size_t sm = 2 * D * sizeof(float);
-#define LNB(TC, MC) ++g_ptcg_launches, k_ln_bwd<TC, MC><<<g, 256, sm, s>>>(dx, D, accumulate, \
+#define LNB(TC, V, MC) ++g_ptcg_launches, k_ln_bwd<TC, V, MC><<<g, 256, sm, s>>>(dx, D, accumulate, \
         (TC*)dxc, D, dw, db, dy, D, x, D, w, mu, rs, rows, D, rpb)
     bool f = dt == DT_F32 || dxc == nullptr;
-    if (D <= 256) { if (f) LNB(float, 8); else LNB(bf16, 8); }
-    else if (D <= 512) { if (f) LNB(float, 16); else LNB(bf16, 16); }
-    else { if (f) LNB(float, 32); else LNB(bf16, 32); }
+    if (D == 256) { if (f) LNB(float, 2, 1); else LNB(bf16, 2, 1); }
+    else if (D == 512) { if (f) LNB(float, 4, 1); else LNB(bf16, 4, 1); }
+    else if (D <= 256) { if (f) LNB(float, 0, 8); else LNB(bf16, 0, 8); }
+    else if (D <= 512) { if (f) LNB(float, 0, 16); else LNB(bf16, 0, 16); }
+    else { if (f) LNB(float, 0, 32); else LNB(bf16, 0, 32); }
 #undef LNB
 }
 
@@ -323,19 +334,21 @@ struct Bump {
     float* f(long n) { return (float*)take((size_t)n * 4); }
 };
 
-static void plan_blk(BlkAct& b, Bump& m, int R, int L, const Dims& z, int esz, bool train,
-                     bool alloc_x) {
-    long NL = (long)R * L;
+// rows_out: rows per sequence computed past the attention (L, or 1 for a
+// block whose output is read at its first row only)
+static void plan_blk(BlkAct& b, Bump& m, int R, int L, int rows_out, const Dims& z, int esz,
+                     bool train, bool alloc_x) {
+    long NL = (long)R * L, NQ = (long)R * rows_out;
     if (alloc_x) { b.x_in = m.f(NL * z.D); }
     b.ln1 = m.take(NL * z.D * esz);
     b.qkv = m.take(NL * 3 * z.D * esz);
-    b.att = m.take(NL * z.D * esz);
-    b.ln2 = m.take(NL * z.D * esz);
-    b.fpre = train ? m.take(NL * z.FFN * esz) : nullptr;
-    b.fpost = m.take(NL * z.FFN * esz);
-    b.mu1 = m.f(NL); b.rs1 = m.f(NL); b.mu2 = m.f(NL); b.rs2 = m.f(NL);
-    b.lse = m.f(NL * z.H);
-    b.xm = m.f(NL * z.D);
+    b.att = m.take(NQ * z.D * esz);
+    b.ln2 = m.take(NQ * z.D * esz);
+    b.fpre = train ? m.take(NQ * z.FFN * esz) : nullptr;
+    b.fpost = m.take(NQ * z.FFN * esz);
+    b.mu1 = m.f(NL); b.rs1 = m.f(NL); b.mu2 = m.f(NQ); b.rs2 = m.f(NQ);
+    b.lse = m.f(NQ * z.H);
+    b.xm = m.f(NQ * z.D);
 }
 
 static void plan_work(Work& W, Bump& m, int R, bool train, const Dims& z, int esz,
@@ -355,7 +368,7 @@ static void plan_work(Work& W, Bump& m, int R, bool train, const Dims& z, int es
     for (int i = 0; i < nx; i++) W.x[i] = m.f(NS * z.D);
     int nb = train ? z.LAYERS : 1;
     W.blk.assign(nb, BlkAct{});
-    for (int i = 0; i < nb; i++) plan_blk(W.blk[i], m, R, z.LSEQ, z, esz, train, false);
+    for (int i = 0; i < nb; i++) plan_blk(W.blk[i], m, R, z.LSEQ, z.LSEQ, z, esz, train, false);
     W.h = m.f(NS * z.D); W.muf = m.f(NS); W.rsf = m.f(NS);
     // option scorer: fp32 operands in both modes (its gradients reduce over
     // options whose inputs share a large per-sample component; bf16 operand
@@ -368,8 +381,9 @@ static void plan_work(Work& W, Bump& m, int R, bool train, const Dims& z, int es
     W.s1pre = train ? m.f(NO * 256) : nullptr;
     W.s1 = m.f(NO * 256);
     W.otokin = m.take((long)R * 56 * 136 * esz);
-    W.xc[0] = m.f(NC * z.D); W.xc[1] = m.f(NC * z.D);
-    plan_blk(W.cblk, m, R, z.LCRIT, z, esz, train, false);
+    // critic block: read at its readout row only -> rows past attention = 1
+    W.xc[0] = m.f(NC * z.D); W.xc[1] = m.f((long)R * z.D);
+    plan_blk(W.cblk, m, R, z.LCRIT, 1, z, esz, train, false);
     W.ovin = m.f((long)R * z.VAL_IN); W.ov1pre = m.f((long)R * 256); W.ov1 = m.f((long)R * 256);
     W.out = m.f((long)R * (z.NOPT + 1));
     if (!train) return;
@@ -393,6 +407,8 @@ static void plan_work(Work& W, Bump& m, int R, bool train, const Dims& z, int es
     W.dbc = m.f((long)R * z.D);
     W.dotokin = m.f((long)R * 56 * 134);
     W.dx = m.f(NC * z.D);
+    W.dx0 = m.f((long)R * z.D);
+    W.dx0c = bf16mode ? m.take((long)R * z.D * esz) : (void*)W.dx0;
     W.dln = m.f(NC * z.D);
     W.dxc = bf16mode ? m.take(NC * z.D * esz) : (void*)W.dx;
     W.dhand = m.take((long)R * z.NC * esz);
@@ -493,6 +509,33 @@ static void block_fwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
     if (train) { a.out2 = b.fpre; a.ldo2 = z.FFN; a.out2_dtype = dt; }
     gemm(M, a, s);
     a = lin_fwd(dt, NL, z.FFN, D, b.fpost, z.FFN, P.f2w, b.x_out, D, DT_F32);
+    a.bias = P.f2b.p; a.resid = b.xm; a.ld_resid = D;
+    gemm(M, a, s);
+}
+
+// The same block evaluated at the first row of each sequence only (its
+// output is read there alone): LN1 and QKV over every row (keys / values),
+// then single-query attention, proj, LN2 and the FFN on R rows.  x_out and
+// the post-attention activations are compact [R, ...].
+static void block_fwd_row0(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* keep, int R,
+                           int L, bool train, cudaStream_t s) {
+    const Dims& z = M->z;
+    const int dt = M->dt(), D = z.D;
+    const int NL = R * L;
+    ln_fwd(dt, b.ln1, D, b.mu1, b.rs1, b.x_in, D, P.ln1w.p, P.ln1b.p, NL, D, s);
+    GemmArgs a = lin_fwd(dt, NL, D, 3 * D, b.ln1, D, P.qkvw, b.qkv, 3 * D, dt);
+    a.bias = P.qkvb.p;
+    gemm(M, a, s);
+    attn_row0_fwd(dt, b.qkv, 3 * D, keep, b.att, D, b.lse, R, L, z.H, s);
+    a = lin_fwd(dt, R, D, D, b.att, D, P.projw, b.xm, D, DT_F32);
+    a.bias = P.projb.p; a.resid = b.x_in; a.ld_resid = (long)L * D;
+    gemm(M, a, s);
+    ln_fwd(dt, b.ln2, D, b.mu2, b.rs2, b.xm, D, P.ln2w.p, P.ln2b.p, R, D, s);
+    a = lin_fwd(dt, R, D, z.FFN, b.ln2, D, P.f1w, b.fpost, z.FFN, dt);
+    a.bias = P.f1b.p; a.act = ACT_GELU;
+    if (train) { a.out2 = b.fpre; a.ldo2 = z.FFN; a.out2_dtype = dt; }
+    gemm(M, a, s);
+    a = lin_fwd(dt, R, z.FFN, D, b.fpost, z.FFN, P.f2w, b.x_out, D, DT_F32);
     a.bias = P.f2b.p; a.resid = b.xm; a.ld_resid = D;
     gemm(M, a, s);
 }
@@ -604,9 +647,9 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     a.remap_group = 56; a.remap_stride = z.LCRIT; a.remap_off = 1 + z.LSEQ;
     gemm(M, a, s);
     Wk.cblk.x_in = Wk.xc[0]; Wk.cblk.x_out = Wk.xc[1];
-    block_fwd(M, M->blk("c0_"), Wk.cblk, Wk.ckeep, R, z.LCRIT, train, s);
+    block_fwd_row0(M, M->blk("c0_"), Wk.cblk, Wk.ckeep, R, z.LCRIT, train, s);
     ++g_ptcg_launches, k_val_in<float><<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.ovin, nullptr, 0, Wk.xc[1],
-        z.LCRIT, D, Wk.gd, R);
+        1, D, Wk.gd, R);
     a = lin_fwd(DT_F32, R, z.VAL_IN, 256, Wk.ovin, z.VAL_IN, f32w(M->w("oracle_v1_w"), z.VAL_IN),
                 Wk.ov1, 256, DT_F32);
     a.bias = M->w("oracle_v1_b").p; a.act = ACT_GELU; a.out2 = Wk.ov1pre; a.ldo2 = 256;
@@ -683,6 +726,44 @@ static void block_bwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
            b.rs1, NL, D, s);
 }
 
+// Backward of block_fwd_row0.  On entry Wk.dx0 (f32) / Wk.dx0c (operand
+// dtype) hold d(x_out) [R, D]; on exit Wk.dx [R * L, D] holds d(x_in).
+static void block_bwd_row0(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* keep, Work& Wk,
+                           int R, int L, cudaStream_t s) {
+    const Dims& z = M->z;
+    const int dt = M->dt(), D = z.D, F = z.FFN;
+    const int NL = R * L;
+    const bool bf = dt == DT_BF16;
+    float* dx0 = Wk.dx0;
+    void* dx0c = Wk.dx0c;
+    // FFN2
+    colsum<float>(P.f2b.g, dx0, D, R, D, s);
+    gemm(M, lin_dw(dt, R, F, D, dx0c, D, b.fpost, F, P.f2w.g), s);
+    GemmArgs a = lin_dx(dt, R, F, D, dx0c, D, P.f2w, Wk.df, F, dt);
+    a.act = ACT_GELU_BWD; a.aux = b.fpre; a.ld_aux = F; a.aux_dtype = dt;
+    a.colsum = P.f1b.g;
+    gemm(M, a, s);
+    // FFN1
+    gemm(M, lin_dw(dt, R, D, F, Wk.df, F, b.ln2, D, P.f1w.g), s);
+    gemm(M, lin_dx(dt, R, D, F, Wk.df, F, P.f1w, Wk.dln, D, DT_F32), s);
+    ln_bwd(dt, dx0, 1, bf ? dx0c : nullptr, P.ln2w.g, P.ln2b.g, Wk.dln, b.xm, P.ln2w.p, b.mu2,
+           b.rs2, R, D, s);
+    // proj
+    colsum<float>(P.projb.g, dx0, D, R, D, s);
+    gemm(M, lin_dw(dt, R, D, D, dx0c, D, b.att, D, P.projw.g), s);
+    gemm(M, lin_dx(dt, R, D, D, dx0c, D, P.projw, Wk.datt, D, dt), s);
+    // attention: dQ at row 0, dK / dV at every key
+    attn_row0_bwd(dt, b.qkv, 3 * D, keep, b.att, D, Wk.datt, D, b.lse, Wk.dqkv, 3 * D, P.qkvb.g,
+                  R, L, z.H, s);
+    // QKV over every row
+    gemm(M, lin_dw(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, b.ln1, D, P.qkvw.g), s);
+    gemm(M, lin_dx(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, P.qkvw, Wk.dln, D, DT_F32), s);
+    // d(x_in) = LN1'(dln) + the residual grad at row 0
+    ln_bwd(dt, Wk.dx, 0, nullptr, P.ln1w.g, P.ln1b.g, Wk.dln, b.x_in, P.ln1w.p, b.mu1, b.rs1,
+           NL, D, s);
+    ++g_ptcg_launches, k_add_rows<<<cdiv((long)R * D, TPB), TPB, 0, s>>>(Wk.dx, (long)L * D, dx0, R, D);
+}
+
 static void tables_bwd(PtcgModel* M, cudaStream_t s) {
     const Dims& z = M->z;
     Tab& t = M->tab;
@@ -701,7 +782,7 @@ static void tables_bwd(PtcgModel* M, cudaStream_t s) {
     // card LayerNorm (input card_in, ld 634) -> d_cardin
     {
         int rpb = 64;
-        ++g_ptcg_launches, k_ln_bwd<float, 20><<<cdiv(z.NC, rpb), 256, 2 * 634 * sizeof(float), s>>>(t.d_cardin, 634, 0,
+        ++g_ptcg_launches, k_ln_bwd<float, 0, 20><<<cdiv(z.NC, rpb), 256, 2 * 634 * sizeof(float), s>>>(t.d_cardin, 634, 0,
             nullptr, 634, M->w("card_ln_w").g, M->w("card_ln_b").g, t.d_cardln, 634, t.card_in, 634,
             M->w("card_ln_w").p, t.ln_mu, t.ln_rs, z.NC, 634, rpb);
     }
@@ -800,11 +881,10 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     gemm_simt(lin_dx(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, f32w(M->w("oracle_v1_w"), z.VAL_IN),
                      Wk.dbvin, z.VAL_IN, DT_F32), s);
     long NC_ = (long)R * z.LCRIT;
-    cudaMemsetAsync(Wk.dx, 0, NC_ * D * 4, s);
-    ++g_ptcg_launches, k_val_in_bwd<<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.dx, z.LCRIT, D, Wk.dgd, Wk.dbvin, R, 1);
-    if (bf) ++g_ptcg_launches, k_cast<bf16><<<cdiv(NC_ * D, TPB), TPB, 0, s>>>((bf16*)Wk.dxc, D, Wk.dx, D, (int)NC_, D);
-    // ---- critic block
-    block_bwd(M, M->blk("c0_"), Wk.cblk, Wk.ckeep, Wk, R, z.LCRIT, s);
+    ++g_ptcg_launches, k_val_in_bwd<<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.dx0, 1, D, Wk.dgd, Wk.dbvin, R, 0);
+    if (bf) ++g_ptcg_launches, k_cast<bf16><<<cdiv((long)R * D, TPB), TPB, 0, s>>>((bf16*)Wk.dx0c, D, Wk.dx0, D, R, D);
+    // ---- critic block (evaluated at its readout row)
+    block_bwd_row0(M, M->blk("c0_"), Wk.cblk, Wk.ckeep, Wk, R, z.LCRIT, s);
     long nxc = NC_ * D;
     if (bf)
         ++g_ptcg_launches, k_xc_bwd<bf16><<<cdiv(nxc, TPB), TPB, 0, s>>>(M->w("critic_readout").g, Wk.dh, (bf16*)Wk.dotok,
@@ -951,6 +1031,7 @@ static int check_shape(const PtcgShape* s) {
     REQ(s, PTCG_EINVAL, "null shape");
     REQ(s->d > 0 && s->heads > 0 && s->d % s->heads == 0 && s->d / s->heads == 32, PTCG_EINVAL,
         "head width d/heads must be 32 (d=%d heads=%d)", s->d, s->heads);
+    REQ(s->heads <= 16, PTCG_EINVAL, "heads must be <= 16 (d <= 512), got %d", s->heads);
     REQ(s->d % 8 == 0 && s->ffn % 8 == 0 && s->ffn > 0 && s->layers >= 1, PTCG_EINVAL,
         "d and ffn must be multiples of 8, layers >= 1");
     REQ(s->ltok >= 1 && s->ltok <= 256 && s->nopt >= 1 && s->nopt <= 1024 && s->tok_f >= 0,
@@ -1435,6 +1516,32 @@ int ptcg_set_step(PtcgModel* M, long step) {
 
 long long ptcg_launch_count(void) { return g_ptcg_launches; }
 
+int ptcg_gemm_ex(int M, int N, int K, const void* A, long lda, int a_kmajor, const void* B,
+                 long ldb, int b_kmajor, int operand_dtype, void* C, long ldc, int out_dtype,
+                 const float* bias, int act, const void* aux, long ld_aux, void* out2, long ldo2,
+                 float* colsum, int accumulate, int engine, void* stream) {
+    REQ(A && B && C && M >= 0 && N >= 0 && K >= 0, PTCG_EINVAL, "bad arguments");
+    REQ(act >= 0 && act <= 2 && engine >= 0 && engine <= 3, PTCG_EINVAL, "bad act / engine");
+    GemmArgs a;
+    a.M = M; a.N = N; a.K = K; a.dtype = operand_dtype == PTCG_BF16 ? DT_BF16 : DT_F32;
+    a.A = A; a.lda = lda; a.a_kmajor = a_kmajor;
+    a.B = B; a.ldb = ldb; a.b_kmajor = b_kmajor;
+    a.out = C; a.ldo = ldc; a.out_dtype = out_dtype == PTCG_BF16 ? DT_BF16 : DT_F32;
+    a.accumulate = accumulate; a.bias = bias; a.act = act;
+    a.aux = aux; a.ld_aux = ld_aux; a.aux_dtype = a.out_dtype;
+    a.out2 = out2; a.ldo2 = ldo2; a.out2_dtype = a.out_dtype; a.colsum = colsum;
+    if (engine == 3) { a.allow_tf32 = 1; engine = 1; }
+    cudaStream_t s = (cudaStream_t)stream;
+    if (engine == 2) { gemm_simt(a, s); CKL(); return PTCG_OK; }
+    bool done = gemm_tc_available() && gemm_tc(a, s);
+    if (!done) {
+        REQ(engine == 0, PTCG_EINVAL, "tcgen05 GEMM does not support this problem");
+        gemm_simt(a, s);
+    }
+    CKL();
+    return PTCG_OK;
+}
+
 int ptcg_attention_fwd(int operand_dtype, const void* qkv, long ldqkv, const unsigned char* keep,
                        void* out, long ldo, float* lse, int nseq, int L, int H, void* stream) {
     REQ(qkv && keep && out && lse && nseq >= 0 && L > 0 && L <= 320 && H > 0, PTCG_EINVAL,
@@ -1470,6 +1577,13 @@ int ptcg_eval_gelu(const float* x, float* gelu, float* gelu_grad, int n, void* s
     return PTCG_OK;
 }
 
+int ptcg_tc_profile(int enable, unsigned long long* counters) {
+    CK(cudaDeviceSynchronize());
+    ptcg_tc_profile_ctl(enable, counters);
+    CKL();
+    return PTCG_OK;
+}
+
 int ptcg_tensor_cores(void) { return gemm_tc_available() ? 1 : 0; }
 
 int ptcg_device_error(void) { return ptcg_tc_error_read_reset(); }
@@ -1498,9 +1612,23 @@ int ptcg_gemm(int M, int N, int K, const void* A, long lda, int a_kmajor, const 
 }
 
 int ptcg_kernel_timer(PtcgModel* M, int mode) {
-    REQ(M && mode >= 0 && mode <= 2, PTCG_EINVAL, "bad arguments");
+    REQ(M && mode >= 0 && mode <= 3, PTCG_EINVAL, "bad arguments");
     M->kt.mode = mode; M->kt.used = 0; M->kt.flops = 0; M->kt.launches = 0;
+    M->kt.meta.clear();
     return PTCG_OK;
+}
+
+int ptcg_kernel_timer_entries(PtcgModel* M, int max, float* ms, int* meta) {
+    REQ(M && ms && meta && max >= 0, PTCG_EINVAL, "null argument");
+    CK(cudaSetDevice(M->dev));
+    int n = (int)(M->kt.meta.size() / 8);
+    if (n > max) n = max;
+    for (int i = 0; i < n; i++) {
+        CK(cudaEventSynchronize(M->kt.ev[2 * i + 1]));
+        CK(cudaEventElapsedTime(&ms[i], M->kt.ev[2 * i], M->kt.ev[2 * i + 1]));
+        for (int k = 0; k < 8; k++) meta[8 * i + k] = M->kt.meta[8 * i + k];
+    }
+    return n;
 }
 
 int ptcg_kernel_timer_read(PtcgModel* M, double* ms, long* launches, double* flops) {

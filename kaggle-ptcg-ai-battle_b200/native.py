@@ -65,12 +65,15 @@ _SIGS = {
     "ptcg_weights_checksum": (I, [P, P, P]),
     "ptcg_kernel_timer": (I, [P, I]),
     "ptcg_launch_count": (C.c_longlong, []),
+    "ptcg_kernel_timer_entries": (I, [P, I, P, P]),
     "ptcg_tensor_cores": (I, []),
+    "ptcg_tc_profile": (I, [I, P]),
     "ptcg_eval_gelu": (I, [P, P, P, I, P]),
     "ptcg_attention_fwd": (I, [I, P, L, P, P, L, P, I, I, I, P]),
     "ptcg_attention_bwd": (I, [I, P, L, P, P, L, P, L, P, P, L, P, I, I, I, P]),
     "ptcg_device_error": (I, []),
     "ptcg_gemm": (I, [I, I, I, P, L, I, P, L, I, I, P, L, I, I, P]),
+    "ptcg_gemm_ex": (I, [I, I, I, P, L, I, P, L, I, I, P, L, I, P, I, P, L, P, L, P, I, I, P]),
     "ptcg_kernel_timer_read": (I, [P, C.POINTER(C.c_double), C.POINTER(C.c_long),
                                    C.POINTER(C.c_double)]),
 }

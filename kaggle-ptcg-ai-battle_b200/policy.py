@@ -248,6 +248,17 @@ class PTCGPolicy:
         check(self.lib.ptcg_kernel_timer_read(self.h, C.byref(ms), C.byref(n), C.byref(fl)))
         return ms.value, n.value, fl.value
 
+    def kernel_timer_entries(self, max_entries=100000):
+        """[(ms, M, N, K, a_kmajor, b_kmajor, act, engine, dtype)] of the timed launches."""
+        ms = np.zeros(max_entries, np.float32)
+        meta = np.zeros(8 * max_entries, np.int32)
+        n = self.lib.ptcg_kernel_timer_entries(self.h, max_entries, ms.ctypes.data_as(C.c_void_p),
+                                               meta.ctypes.data_as(C.c_void_p))
+        if n < 0:
+            check(n)
+        meta = meta[:8 * n].reshape(n, 8)
+        return [(float(ms[i]), *[int(v) for v in meta[i]]) for i in range(n)]
+
     def weights_checksum(self):
         out = torch.zeros(4, dtype=torch.int32, device=self.device)
         check(self.lib.ptcg_weights_checksum(self.h, _p(out), _stream()))
