@@ -390,7 +390,9 @@ def main():
         cpu = {"value": rate, "unit": "samples/s", "cores": threads, "kind": "port",
                "sample": f"64-row PPO train step of the CPU oracle (forward_train + loss + "
                          f"backward + Adam), median of {n} steps ({med:.2f} s/step)"}
-    flops_sample = 3 * 1.295e9
+    from ptcg_b200.config import train_flops
+    flops_exec = train_flops(s, "first")       # what this build runs per sample
+    flops_ref = train_flops(s, "all")          # same step with the critic over every row
     line = {
         "metric": "PPO train samples/sec (config 2 per GPU, aggregate)",
         "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
@@ -408,7 +410,10 @@ def main():
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": int(launches),
         "roofline": roof,
-        "model_tflops": value * flops_sample / world / 1e12,
+        "model_tflops": {"executed": value * flops_exec / world / 1e12,
+                         "reference_equivalent": value * flops_ref / world / 1e12,
+                         "gflop_per_sample": {"executed": flops_exec / 1e9,
+                                              "reference_equivalent": flops_ref / 1e9}},
         "rollout": rollout,
         "cpu_baseline": cpu,
         "clocks": clk.summary(),

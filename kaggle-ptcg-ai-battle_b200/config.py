@@ -220,3 +220,37 @@ def packed_offsets(s: Shape):
         out[name] = (off, shp)
         off += k
     return out
+
+
+def forward_flops(s: Shape, critic_rows: str = "first"):
+    """Dense multiply-add FLOPs (2 per MAC) of one sample's policy forward at
+    the full padded lengths LSEQ / LCRIT, by part.  ``critic_rows="all"``
+    counts the critic block over every row, as the reference executes it
+    (ptcg_model3.cu:333-355); ``"first"`` counts what this build runs: the
+    critic output is read at its readout row only (model.py:305-308), so its
+    QKV covers every row (keys / values) and attention, proj and FFN cover
+    row 0.  Static-table MLPs are per call, not per sample, and excluded."""
+    D, F = s.d, s.ffn
+
+    def block(L, rows_out):
+        qkv = 2 * L * 3 * D * D
+        att = 4 * rows_out * L * D                    # QK^T and PV
+        post = 2 * rows_out * (D * D + 2 * D * F)     # proj + FFN
+        return qkv + att + post
+
+    L, LC = s.lseq, s.lcrit
+    parts = {
+        "token_proj": 2 * s.ltok * s.tok_in * D,
+        "trunk": s.layers * block(L, L),
+        "critic": block(LC, LC if critic_rows == "all" else 1)
+        + 2 * N_ORACLE_TOKENS * s.orc_in * D + 2 * s.val_in * 256 + 2 * 256,
+        "options": s.nopt * (2 * s.q_in * D + 2 * D * D + 2 * s.score_in * 256 + 2 * 256),
+    }
+    parts["total"] = sum(parts.values())
+    return parts
+
+
+def train_flops(s: Shape, critic_rows: str = "first"):
+    """Per-sample train-step FLOPs: forward plus a backward of twice the
+    forward (dX and dW GEMMs)."""
+    return 3 * forward_flops(s, critic_rows)["total"]

@@ -110,7 +110,11 @@ def test_train_grads_parity(pkg, oracle, preset, prec):
             continue
         worst.append((rel(a, b), name))
     worst.sort(reverse=True)
-    print(preset, prec, "worst grad rel errors:", worst[:4])
+    full = rel(g[:off], np.concatenate([ref[name] for name, _ in pkg.config.param_table(s)]))
+    print(preset, prec, "whole-gradient rel error %.3e; worst per-tensor:" % full, worst[:4])
+    # the whole gradient vector meets the stated tolerance; single tensors in
+    # bf16 mode (bf16-rounded operands, reductions over few rows) get 3x
+    assert full <= TOL[prec], full
     assert worst[0][0] <= TOL[prec] * (3 if prec == "bf16" else 1), worst[:5]
 
 
