@@ -131,6 +131,33 @@ int ptcg_ppo_loss(const float* dec_out, int nopt, const float* mask,
                   float* grad_dec, float* new_logp, float* ratio, float* stats,
                   float* scratch, void* stream);
 
+/* ptcg_ppo_loss without the `scratch` argument: the same kernels and results,
+ * with the scratch held in a fixed device array inside this library.  No
+ * counterpart in the reference (its loss keeps scratch in the trainer's
+ * PPOBuffersPuf).  For callers that cannot hand the loss a scratch buffer:
+ * a trainer whose device memory is carved up once at start-up and may not
+ * grow afterwards, or a plugin slot whose signature has no room for one.
+ * It allocates nothing, on any call.
+ *  - Limit: n_seg * horizon <= PTCG_PPO_NOALLOC_MAX_ROWS rows (the static
+ *    array is PTCG_PPO_SCRATCH_FLOATS(PTCG_PPO_NOALLOC_MAX_ROWS) floats,
+ *    224 KiB per device); larger minibatches return PTCG_ERANGE.
+ *  - Set-up: the first call on each device (with that device current)
+ *    looks up the array's device address once and caches it; make that
+ *    first call before any stream capture.
+ *  - Nothing in the array needs to start at zero: every value the kernels
+ *    read is written earlier in the same call.
+ *  - One array per device: calls that overlap on the same device (on
+ *    different streams or host threads) race on it and must be serialised
+ *    by the caller. */
+#define PTCG_PPO_NOALLOC_MAX_ROWS 65536
+int ptcg_ppo_loss_noalloc(const float* dec_out, int nopt, const float* mask,
+                          const float* actions, const float* old_logp,
+                          const float* advantages, const float* values,
+                          const float* returns, const float* prio, int n_seg, int horizon,
+                          float clip_coef, float vf_clip_coef, float vf_coef, float ent_coef,
+                          float* grad_dec, float* new_logp, float* ratio, float* stats,
+                          void* stream);
+
 /* Global-norm clip + fused mixed-precision Adam over the whole arena
  * (fp32 master weights and moments, bf16 compute copies refreshed in the
  * same pass).  Replaces muon_step (native/src/muon.cu:209-297) with the

@@ -25,6 +25,7 @@
 
 #include <string>
 #include <vector>
+#include <mutex>
 #include <unordered_map>
 
 long long g_ptcg_launches = 0;
@@ -1381,6 +1382,55 @@ int ptcg_ppo_loss(const float* dec_out, int nopt, const float* mask, const float
     ++g_ptcg_launches, k_ppo_reduce<<<1, 32, 0, s>>>(stats, partials, (int)g, adv_stats, 0);
     CKL();
     return PTCG_OK;
+}
+
+// Library-owned PPO scratch for ptcg_ppo_loss_noalloc: one fixed array per
+// device (the module's __device__ data), its address looked up once per
+// device and cached.
+static __device__ __align__(256) float g_ppo_noalloc_scratch[PTCG_PPO_SCRATCH_FLOATS(
+    PTCG_PPO_NOALLOC_MAX_ROWS)];
+static const int NOALLOC_MAX_DEVICES = 64;
+static float* g_ppo_noalloc_ptr[NOALLOC_MAX_DEVICES];
+static std::mutex g_ppo_noalloc_mu;
+
+static int ppo_noalloc_scratch(float** out) {
+    int dev = -1;
+    CK(cudaGetDevice(&dev));
+    REQ(dev >= 0 && dev < NOALLOC_MAX_DEVICES, PTCG_EINVAL,
+        "device ordinal %d beyond the %d this entry point serves", dev, NOALLOC_MAX_DEVICES);
+    std::lock_guard<std::mutex> lock(g_ppo_noalloc_mu);
+    if (!g_ppo_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_ppo_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            cudaGetLastError();
+            set_err("cudaGetSymbolAddress of the static PPO scratch failed on device %d: %s", dev,
+                    cudaGetErrorString(e));
+            return PTCG_ECUDA;
+        }
+        g_ppo_noalloc_ptr[dev] = (float*)p;
+    }
+    *out = g_ppo_noalloc_ptr[dev];
+    return PTCG_OK;
+}
+
+int ptcg_ppo_loss_noalloc(const float* dec_out, int nopt, const float* mask, const float* actions,
+                          const float* old_logp, const float* advantages, const float* values,
+                          const float* returns, const float* prio, int n_seg, int horizon,
+                          float clip_coef, float vf_clip_coef, float vf_coef, float ent_coef,
+                          float* grad_dec, float* new_logp, float* ratio, float* stats,
+                          void* stream) {
+    REQ(n_seg > 0 && horizon > 0, PTCG_EINVAL, "bad sizes");
+    REQ((long)n_seg * horizon <= PTCG_PPO_NOALLOC_MAX_ROWS, PTCG_ERANGE,
+        "ptcg_ppo_loss_noalloc: n_seg * horizon = %ld rows exceeds its static scratch limit of "
+        "%d rows; use ptcg_ppo_loss with caller scratch", (long)n_seg * horizon,
+        PTCG_PPO_NOALLOC_MAX_ROWS);
+    float* scratch = nullptr;
+    int e = ppo_noalloc_scratch(&scratch);
+    if (e) return e;
+    return ptcg_ppo_loss(dec_out, nopt, mask, actions, old_logp, advantages, values, returns,
+                         prio, n_seg, horizon, clip_coef, vf_clip_coef, vf_coef, ent_coef,
+                         grad_dec, new_logp, ratio, stats, scratch, stream);
 }
 
 static int adam_impl(PtcgModel* M, float lr, float b1, float b2, float eps, float max_norm,

@@ -52,6 +52,8 @@ _SIGS = {
     "ptcg_backward": (I, [P, P, P, I, F, I, P]),
     "ptcg_ppo_loss": (I, [P, I, P, P, P, P, P, P, P, I, I, F, F, F, F,
                           P, P, P, P, P, P]),
+    "ptcg_ppo_loss_noalloc": (I, [P, I, P, P, P, P, P, P, P, I, I, F, F, F, F,
+                                  P, P, P, P, P]),
     "ptcg_adam_step": (I, [P, F, F, F, F, F, P, P, P]),
     "ptcg_sample_logits": (I, [P, I, I, P, L, P, P, P, P, P]),
     "ptcg_puff_advantage": (I, [P, P, P, P, P, L, I, I, I, F, F, F, F, P, P]),
