@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-rollout", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--ref-rows", type=int, default=128,
+                    help="observations per step of the reference (CPU) arm")
     return ap.parse_args()
 
 
@@ -114,9 +116,24 @@ def measured_peaks():
 
 
 # ---------------------------------------------------------------- reference
-def cpu_oracle_step_rate(pkg, s, rows, seconds, threads):
-    """Samples/s of the CPU oracle train step (forward_train + PPO loss +
-    backward + clip + Adam) on `rows` config-shaped observations."""
+METRIC = "PPO train samples/sec (config 2 per GPU, aggregate)"
+
+
+def arm_config(args, s, world, micro):
+    nt = args.segments * args.horizon
+    return {"workload": f"ppo_train_step {args.preset}: {args.segments}x{args.horizon} "
+                        f"samples/GPU, micro-batch {micro}",
+            "model": "PTCGTransformer d%d L%d h%d ffn%d ltok%d nopt%d" % (
+                s.d, s.layers, s.heads, s.ffn, s.ltok, s.nopt),
+            "global_batch": nt * world, "seq_len": s.lseq,
+            "parallelism": f"dp{world}",
+            "l2": "inputs larger than L2 (obs %.0f MB per step per GPU)" % (
+                nt * s.obs_size * 4 / 1e6)}
+
+
+def cpu_oracle_step(pkg, s, rows, threads):
+    """One CPU oracle train step (forward_train + PPO loss + backward + clip +
+    Adam) on `rows` config-shaped observations, as a callable."""
     import torch
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import ptcg_oracle as oracle
@@ -139,7 +156,12 @@ def cpu_oracle_step_rate(pkg, s, rows, seconds, threads):
     def step():
         _, _, g = oracle.train_grads(P, T, obs, s, act, old, adv, val, ret, prio, 1, rows)
         oracle.adam_step(P, g, state)
+    return step
 
+
+def cpu_oracle_step_rate(pkg, s, rows, seconds, threads):
+    """Samples/s of the CPU oracle train step, median over ~`seconds`."""
+    step = cpu_oracle_step(pkg, s, rows, threads)
     step()                                  # warm-up
     times = []
     t_end = time.time() + seconds
@@ -150,20 +172,33 @@ def cpu_oracle_step_rate(pkg, s, rows, seconds, threads):
 
 
 def run_reference(args, pkg):
+    """The reference arm: the reference algorithm's CPU implementation (the
+    oracle port of ptcg/rl/model.py + PPO + torch Adam) on all host cores;
+    each step is a bounded sample of the config-2 workload (--ref-rows
+    observations of the same shapes); W warm-up then K timed steps."""
     s = pkg.config.PRESETS[args.preset]
     threads = os.cpu_count() or 1
-    rows = 64
-    rate, n, med = cpu_oracle_step_rate(pkg, s, rows, max(5.0, args.cpu_seconds), threads)
-    cpu = {"value": rate, "unit": "samples/s", "cores": threads, "kind": "port",
-           "sample": f"{rows}-row PPO train step (forward_train+loss+backward+Adam), "
-                     f"median of {n} steps, {med:.2f} s/step"}
-    line = {"impl": "reference", "metric": "PPO train samples/sec (config 2 shapes, aggregate)",
-            "value": rate, "unit": "samples/s", "n_gpus": args.gpus, "steps": n,
-            "warmup": 1, "ms_per_step": med * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"ppo_train_step {args.preset} (config 2), CPU sample of "
-                                   f"{rows} rows", "parallelism": "cpu"},
-            "cpu_baseline": cpu,
+    rows = args.ref_rows
+    step = cpu_oracle_step(pkg, s, rows, threads)
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    rate = rows * args.steps / dt
+    sample = (f"{rows}-row PPO train step of the CPU oracle port (forward_train + loss + "
+              f"backward + clip + Adam) per step, {threads} threads")
+    nt = args.segments * args.horizon
+    cfg = arm_config(args, s, args.gpus, min(args.micro, nt))
+    cfg["sample_rows_per_step"] = rows
+    line = {"impl": "reference", "metric": METRIC,
+            "value": rate, "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": cfg,
+            "cpu_baseline": {"value": rate, "unit": "samples/s", "cores": threads,
+                             "kind": "port", "sample": sample},
             "e2e": {"value": rate, "unit": "samples/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -226,31 +261,29 @@ def main():
                  betas=(0.9, 0.999), eps=1e-8, max_norm=1.0)
 
     # --- data parallel: bucketed all-reduce overlapped with the backward
-    comm = torch.cuda.Stream(device=dev) if world > 1 else None
     grads = pol.arena(1)
+    reducer = None
     if world > 1:
-        def hook(off, cnt, stream_ptr):
-            ev = torch.cuda.Event()
-            ev.record(torch.cuda.current_stream())
-            comm.wait_event(ev)
-            with torch.cuda.stream(comm):
-                dist.all_reduce(grads[off:off + cnt], op=dist.ReduceOp.AVG)
-        pol.set_grad_hook(hook)
+        from ptcg_b200.dp import BucketAllReduce, checksum_u64, weights_agree
+        reducer = BucketAllReduce(grads)
+        pol.set_grad_hook(reducer)
     ck = torch.zeros(max(1, args.steps + args.warmup), 2, dtype=torch.int64, device=dev)
     stats = torch.zeros(16, device=dev)
 
+    covered = []
+
     def step(i, o=obs, ac=act, ol=old, ad=adv, va=vals, re=ret):
+        if reducer is not None:
+            reducer.reset()
         pol.train_step(o, ac, ol, ad, va, re, prio, args.segments, args.horizon,
                        skip_adam=world > 1, stats=stats, **hyper)
-        if world > 1:
-            torch.cuda.current_stream().wait_stream(comm)
-            pol.adam_step(lr=hyper["lr"], betas=hyper["betas"], eps=hyper["eps"],
-                          max_norm=hyper["max_norm"])
-            c = pol.weights_checksum().to(torch.int64) & 0xFFFFFFFF
-            v = c[0] | (c[1] << 32)
-            mn = v.clone(); mx = v.clone()
-            dist.all_reduce(mn, op=dist.ReduceOp.MIN)
-            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        if reducer is not None:
+            covered.append(reducer.covered(grads.numel()))
+            reducer.wait()
+            st2 = pol.adam_step(lr=hyper["lr"], betas=hyper["betas"], eps=hyper["eps"],
+                                max_norm=hyper["max_norm"])
+            stats[8:10].copy_(st2)              # {grad norm, applied} as train_step writes them
+            mn, mx = weights_agree(checksum_u64(pol.weights_checksum()))
             ck[i, 0] = mn; ck[i, 1] = mx
 
     for i in range(args.warmup):
@@ -394,18 +427,11 @@ def main():
     flops_exec = train_flops(s, "first")       # what this build runs per sample
     flops_ref = train_flops(s, "all")          # same step with the critic over every row
     line = {
-        "metric": "PPO train samples/sec (config 2 per GPU, aggregate)",
+        "metric": METRIC,
         "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"ppo_train_step {args.preset}: {args.segments}x{args.horizon} "
-                               f"samples/GPU, micro-batch {micro}",
-                   "model": "PTCGTransformer d%d L%d h%d ffn%d ltok%d nopt%d" % (
-                       s.d, s.layers, s.heads, s.ffn, s.ltok, s.nopt),
-                   "global_batch": nt * world, "seq_len": s.lseq,
-                   "parallelism": f"dp{world}",
-                   "l2": "inputs larger than L2 (obs %.0f MB per step per GPU)" % (
-                       nt * s.obs_size * 4 / 1e6)},
+        "config": arm_config(args, s, world, micro),
         "e2e": {"value": e2e, "unit": "samples/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": int(launches),
@@ -418,6 +444,8 @@ def main():
         "cpu_baseline": cpu,
         "clocks": clk.summary(),
         "weights_identical_across_ranks": ok,
+        "grad_buckets": ({"per_step": len(reducer.spans), "cover_arena_once": all(covered)}
+                         if reducer is not None else None),
         "loss_stats": {"total": float(st[0]), "approx_kl": float(st[5]),
                        "grad_norm": float(st[8])},
     }

@@ -60,6 +60,7 @@ class PTCGPolicy:
         assert self.obs_size == shape.obs_size
         self.n_params = param_count(shape)
         self._hook_ref = None
+        self._hook_err = None
         if tables is not None:
             self.set_tables(tables)
         if weights is not None:
@@ -162,8 +163,10 @@ class PTCGPolicy:
     def backward(self, grad, returns, aux_norm_rows=0, prize_count=0.0, accumulate=False):
         grad = _f32(grad, self.device)
         returns = _f32(returns, self.device)
+        self._hook_err = None
         check(self.lib.ptcg_backward(self.h, _p(grad), _p(returns), int(aux_norm_rows),
                                      float(prize_count), int(accumulate), _stream()))
+        self._raise_hook_error()
 
     # -------------------------------------------------------- trainer hooks
     def ppo_loss(self, dec_out, mask, actions, old_logp, advantages, values, returns,
@@ -220,9 +223,23 @@ class PTCGPolicy:
             self._hook_ref = None
             check(self.lib.ptcg_set_grad_hook(self.h, native.GRAD_HOOK(), None))
             return
-        cb = native.GRAD_HOOK(lambda user, off, cnt, stream: fn(off, cnt, stream))
+        def call(user, off, cnt, stream):
+            # ctypes drops exceptions raised in callbacks: keep the first one
+            # and re-raise it when the library call that fired the hook returns
+            try:
+                fn(off, cnt, stream)
+            except BaseException as e:   # noqa: BLE001
+                if self._hook_err is None:
+                    self._hook_err = e
+
+        cb = native.GRAD_HOOK(call)
         self._hook_ref = cb
         check(self.lib.ptcg_set_grad_hook(self.h, cb, None))
+
+    def _raise_hook_error(self):
+        e, self._hook_err = getattr(self, "_hook_err", None), None
+        if e is not None:
+            raise RuntimeError("grad hook failed") from e
 
     def train_step(self, obs, actions, old_logp, advantages, values, returns, prio,
                    n_seg, horizon, clip=0.2, vf_clip=0.2, vf_coef=0.5, ent_coef=0.01,
@@ -233,10 +250,12 @@ class PTCGPolicy:
         args = [_f32(x, d) for x in (actions, old_logp, advantages, values, returns, prio)]
         if stats is None:
             stats = torch.zeros(16, device=d)
+        self._hook_err = None
         check(self.lib.ptcg_train_step(self.h, _p(obs), *[_p(a) for a in args], n_seg,
                                        horizon, clip, vf_clip, vf_coef, ent_coef, lr, betas[0],
                                        betas[1], eps, max_norm, int(skip_adam), _p(stats),
                                        _stream()))
+        self._raise_hook_error()
         return stats
 
     def kernel_timer(self, mode):
