@@ -222,14 +222,31 @@ PTCG_DEV void ldb_kn(uint32_t (&b)[4], const bf16* X, int k0, int n0, int lane) 
     ldsm4t(b, s_addr(X + (k0 + (mi & 1) * 8 + (lane & 7)) * RS + n0 + (mi >> 1) * 8));
 }
 
-// load rows [0, L) of a 32-wide head slice into smem (zero rows L..Lp)
+// Rows [0, L) of a 32-wide head slice into smem (zero rows L..Lp) with
+// cp.async: every 16-byte piece of every row is in flight at once; the
+// caller commits and waits (cp_async_wait_all + __syncthreads).
+PTCG_DEV void cp_async16(void* dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+                 :: "r"(s_addr(dst)), "l"(src), "r"(src_bytes) : "memory");
+}
+PTCG_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 PTCG_DEV void stage_rows(bf16* dst, const bf16* src, long ld, int L, int Lp) {
     for (int i = threadIdx.x; i < Lp * 4; i += blockDim.x) {
         int r = i >> 2, c = (i & 3) * 8;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < L) v = *(const uint4*)(src + (long)r * ld + c);
-        *(uint4*)(dst + r * RS + c) = v;
+        bool in = r < L;
+        cp_async16(dst + r * RS + c, src + (long)(in ? r : 0) * ld + c, in ? 16 : 0);
     }
+}
+PTCG_DEV float dot8_bf16(uint4 a, uint4 b) {
+    const __nv_bfloat162* x = (const __nv_bfloat162*)&a;
+    const __nv_bfloat162* y = (const __nv_bfloat162*)&b;
+    float d = 0.f;
+    #pragma unroll
+    for (int k = 0; k < 4; k++) {
+        float2 u = __bfloat1622float2(x[k]), v = __bfloat1622float2(y[k]);
+        d = fmaf(u.x, v.x, fmaf(u.y, v.y, d));
+    }
+    return d;
 }
 
 constexpr float LOG2E = 1.4426950408889634f;
@@ -257,6 +274,7 @@ __global__ void __launch_bounds__(128) k_attn_fwd_mma(
         kb_bias[j] = k ? 0.f : -INFINITY;
         if (k) kb_any[j >> 4] = 1;
     }
+    cp_async_wait_all();
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
@@ -373,23 +391,25 @@ __global__ void __launch_bounds__(128) k_attn_bwd_mma(
     __syncthreads();
     const float* lrow = lse + ((long)n * H + h) * L;
     const bf16* orow = out + (long)n * L * ldo + h * DH;
+    const bf16* grow = dout + (long)n * L * lddo + h * DH;
     for (int j = threadIdx.x; j < Lp; j += blockDim.x) {
         bool k = j < L && kp[j];
         kbias[j] = k ? 0.f : -INFINITY;
         if (k) kany[j >> 4] = 1;
-        if (j < L) {
-            lse2[j] = lrow[j] * LOG2E;
-            float d = 0.f;
-            const bf16* orr = orow + (long)j * ldo;
-            const bf16* grr = Gs + j * RS;
-            #pragma unroll 8
-            for (int c = 0; c < DH; c++) d += __bfloat162float(orr[c]) * __bfloat162float(grr[c]);
-            dl[j] = d;
-        } else {
-            lse2[j] = INFINITY;
-            dl[j] = 0.f;
-        }
+        lse2[j] = j < L ? lrow[j] * LOG2E : INFINITY;
     }
+    // delta_i = dO_i . O_i: four threads per row, 16-byte loads, shuffle sum
+    for (int i0 = 0; i0 < Lp * 4; i0 += blockDim.x) {
+        int i = i0 + threadIdx.x, r = i >> 2, c = (i & 3) * 8;
+        float d = 0.f;
+        if (r < L)
+            d = dot8_bf16(*(const uint4*)(orow + (long)r * ldo + c),
+                          *(const uint4*)(grow + (long)r * lddo + c));
+        d += __shfl_xor_sync(0xffffffffu, d, 1);
+        d += __shfl_xor_sync(0xffffffffu, d, 2);
+        if ((i & 3) == 0 && r < Lp) dl[r] = d;
+    }
+    cp_async_wait_all();
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;

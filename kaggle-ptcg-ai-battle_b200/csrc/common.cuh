@@ -7,6 +7,17 @@
 
 typedef __nv_bfloat16 bf16;
 
+// Build-time configuration of the tensor-core GEMM epilogue.
+#ifndef PTCG_EPI_WARPS
+#define PTCG_EPI_WARPS 16       // epilogue warps per CTA (multiple of 4)
+#endif
+#ifndef PTCG_STAGE_BUFS
+#define PTCG_STAGE_BUFS 1       // TMA-store staging buffers per epilogue warp (1 or 2)
+#endif
+#ifndef PTCG_BIAS_SMEM
+#define PTCG_BIAS_SMEM 1        // stage bias vectors in shared memory
+#endif
+
 #define PTCG_DEV __device__ __forceinline__
 
 template <typename T> PTCG_DEV float to_f(T v);
@@ -25,35 +36,75 @@ PTCG_DEV float gelu_grad_f(float x) {
     float pdf = 0.3989422804014327f * expf(-0.5f * x * x);
     return cdf + x * pdf;
 }
-// Fast GELU / GELU' for the tensor-core epilogues.  erf by Abramowitz &
-// Stegun, Handbook of Mathematical Functions, eq. 7.1.26 (Hastings):
-//   erf(a) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-a^2),
-//   t = 1 / (1 + p a), a >= 0, |error| <= 1.5e-7,
-// one branch-free path; exp(-x^2/2) is shared with the normal pdf that
-// GELU' needs.  The exact-fp32 (SIMT) path keeps erff.
-PTCG_DEV void gelu_parts_fast(float x, float& cdf, float& pdf) {
-    const float p = 0.3275911f, a1 = 0.254829592f, a2 = -0.284496736f,
-                a3 = 1.421413741f, a4 = -1.453152027f, a5 = 1.061405429f;
-    float u = x * 0.70710678118654752f;
-    float a = fabsf(u);
-    float t = __fdividef(1.f, fmaf(p, a, 1.f));
-    float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, a5, a4), a3), a2), a1);
-    float e = __expf(-a * a);                                // exp(-x^2 / 2)
-    float erf_a = 1.f - poly * e;
-    float erf_u = copysignf(erf_a, u);
-    cdf = 0.5f * (1.f + erf_u);
-    pdf = 0.3989422804014327f * e;
+// GELU and GELU' for the tensor-core epilogues (the exact-fp32 SIMT path
+// keeps erff): two values at once on the packed f32x2 FP32 path
+// (fma/mul/add.rn.f32x2), with one exponential per value and no division:
+//   Phi(x) = 1/2 + sign(x) (1/2 - erfc(a)/2),  a = |x| / sqrt(2),
+//   erfc(a) = exp(-a^2) * R(min(a, 4)),
+// R a degree-10 polynomial least-squares fit of the scaled complementary
+// error function erfcx(a) = exp(a^2) erfc(a) on [0, 4] (weight exp(-a^2),
+// fitted in float64 for this file; beyond a = 4 erfc(a) < 2e-8 so the
+// clamp changes nothing in fp32).  |GELU error| <= 2e-7 max(|x|, 1) and
+// |GELU' error| <= 3e-7 over [-12, 12] (checked against fp64 torch on the
+// device).  exp(-x^2/2) = 2^(-x^2 log2(e) / 2) on ex2.approx, shared with
+// the normal pdf that GELU' needs.
+PTCG_DEV unsigned long long pk2(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
 }
-PTCG_DEV float gelu_fast(float x) {
-    float c, p;
-    gelu_parts_fast(x, c, p);
-    return x * c;
+PTCG_DEV void upk2(unsigned long long r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
 }
-PTCG_DEV float gelu_grad_fast(float x) {
-    float c, p;
-    gelu_parts_fast(x, c, p);
-    return fmaf(x, p, c);
+PTCG_DEV unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
 }
+PTCG_DEV unsigned long long mul2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+PTCG_DEV unsigned long long add2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+PTCG_DEV float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+PTCG_DEV unsigned long long splat2(float c) { return pk2(c, c); }
+
+PTCG_DEV void gelu2(float x0, float x1, float& y0, float& y1, float& g0, float& g1) {
+    const unsigned long long x = pk2(x0, x1);
+    const float a0 = fminf(fabsf(x0) * 0.70710678118654752f, 4.f);
+    const float a1 = fminf(fabsf(x1) * 0.70710678118654752f, 4.f);
+    const unsigned long long a = pk2(a0, a1);
+    unsigned long long p = splat2(9.721369133e-05f);
+    p = fma2(p, a, splat2(-1.507143723e-03f));
+    p = fma2(p, a, splat2(1.044293307e-02f));
+    p = fma2(p, a, splat2(-4.352428019e-02f));
+    p = fma2(p, a, splat2(1.251842678e-01f));
+    p = fma2(p, a, splat2(-2.732950151e-01f));
+    p = fma2(p, a, splat2(4.882091582e-01f));
+    p = fma2(p, a, splat2(-7.492768168e-01f));
+    p = fma2(p, a, splat2(9.996129870e-01f));
+    p = fma2(p, a, splat2(-1.128359556e+00f));
+    p = fma2(p, a, splat2(9.999998212e-01f));
+    float s0, s1;
+    upk2(mul2(mul2(x, x), splat2(-0.72134752044448170f)), s0, s1);
+    const unsigned long long e = pk2(ex2_approx(s0), ex2_approx(s1));   // exp(-x^2/2)
+    float h0, h1;
+    upk2(fma2(mul2(e, p), splat2(-0.5f), splat2(0.5f)), h0, h1);        // erf(a) / 2
+    const unsigned long long cdf = add2(splat2(0.5f), pk2(copysignf(h0, x0), copysignf(h1, x1)));
+    const unsigned long long g = fma2(x, mul2(e, splat2(0.3989422804014327f)), cdf);
+    upk2(mul2(x, cdf), y0, y1);
+    upk2(g, g0, g1);
+}
+
 // torch F.softplus (beta 1, threshold 20)
 PTCG_DEV float softplus_f(float x) { return x > 20.f ? x : log1pf(expf(x)); }
 PTCG_DEV float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }

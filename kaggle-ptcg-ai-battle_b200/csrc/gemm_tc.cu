@@ -14,10 +14,16 @@
 //   M=128, N=BN into a double-buffered TMEM accumulator and releases ring
 //   slots with tcgen05.commit.  A 128-byte swizzled row holds 64 bf16 or 32
 //   fp32 K-elements, so both kinds share one byte-level smem layout.
-// * Four epilogue warps (one per TMEM lane quadrant) read the accumulator
-//   with tcgen05.ld.32x32b.x32 while the next tile's MMAs run, and apply
-//   bias / broadcast / GELU / GELU' / row remap / residual / accumulate /
-//   fp32 column sums before vectorised global stores.
+// * PTCG_EPI_WARPS epilogue warps (16: four per TMEM lane quadrant, each
+//   taking every fourth 32-column chunk) read the accumulator with
+//   tcgen05.ld.32x32b.x32 while the next tile's MMAs run, and apply bias
+//   (staged once per CTA in shared memory) / broadcast / GELU and GELU'
+//   (packed f32x2 math) / GELU' multiply / row remap / residual /
+//   accumulate / fp32 column sums.  Whole 32x32 chunks leave through a
+//   swizzled shared staging buffer and a TMA store; the rest through
+//   vectorised global stores.  The epilogue, not the MMA, bounds the K = 256
+//   GEMMs of this model, so its warp count hides the latency of TMEM loads,
+//   operand loads and store fences.
 // * Persistent CTAs (one per SM) walk an M-major tile order so that the
 //   N-tiles of one A row-block run together and share it through L2; weight
 //   gradients (long K) are split over K with fp32 atomic accumulation.
@@ -35,8 +41,12 @@
 namespace {
 
 constexpr int BM = 128;
-constexpr int NUM_EPI = 8;                   // epilogue warps (two per TMEM lane quadrant)
-constexpr int STAGE_W = 8192;                // TMA-store staging per epilogue warp (2 x 4 KB)
+constexpr int NUM_EPI = PTCG_EPI_WARPS;      // epilogue warps (NUM_EPI / 4 per TMEM lane quadrant)
+constexpr int EPI_GROUPS = NUM_EPI / 4;      // warps sharing a quadrant split its 32-column chunks
+constexpr int STAGE_BUFS = PTCG_STAGE_BUFS;  // TMA-store staging buffers per epilogue warp
+constexpr int STAGE_W = 4096 * STAGE_BUFS;   // staging bytes per epilogue warp
+constexpr int BIAS_SMEM_MAX = 4096;          // bias vectors up to this many columns live in smem
+static_assert(NUM_EPI % 4 == 0 && STAGE_BUFS >= 1 && STAGE_BUFS <= 2, "epilogue layout");
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI; // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
 constexpr long long WAIT_BUDGET = 4000000000LL;   // clock cycles (~2 s)
 
@@ -59,6 +69,7 @@ struct TcParams {
     uint32_t stage_bytes, a_bytes;
     uint32_t tmem_cols, acc_stride;
     int tma_out;             // outputs leave through smem staging + TMA stores
+    int bias_smem;           // columns of the bias staged in shared memory (0: read from global)
     GemmArgs ep;
 };
 
@@ -111,6 +122,7 @@ PTCG_DEV void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
 }
 PTCG_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 PTCG_DEV void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+PTCG_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 PTCG_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 PTCG_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -285,6 +297,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
     int* n_issued = (int*)(tmem_slot + 2);     // ring slots filled by TMA
     int* n_consumed = (int*)(tmem_slot + 3);   // ring slots read by the MMA warp
+    float* sbias = (float*)(((uintptr_t)(tmem_slot + 8) + 15) & ~(uintptr_t)15);   // [P.bias_smem]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
     const uint32_t tfull0 = smem_u32(bars + 2 * S), tempty0 = smem_u32(bars + 2 * S + 2);
@@ -300,6 +313,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
+    for (int i = threadIdx.x; i < P.bias_smem; i += blockDim.x) sbias[i] = P.ep.bias[i];
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      :: "r"(smem_u32(tmem_slot)), "r"(P.tmem_cols) : "memory");
@@ -402,7 +416,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     } else {
         // ------------------------------------------------ epilogue warps
         const int quad = warp & 3;           // TMEM lane quadrant this warp may read
-        const int half = (warp - 2) >> 2;    // which alternate 32-column chunks
+        const int grp = (warp - 2) >> 2;     // which of the quadrant's interleaved 32-column chunks
         const int row_in_tile = quad * 32 + lane;
         const GemmArgs& a = P.ep;
         int local = 0;
@@ -423,7 +437,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             if (a.remap_group > 0)
                 orow = (long)(m / a.remap_group) * a.remap_stride + a.remap_off + (m % a.remap_group);
             const uint32_t tbase = tmem + buf * P.acc_stride + ((uint32_t)(quad * 32) << 16);
-            for (int c0 = half * 32; c0 < P.bn; c0 += 64) {
+            for (int c0 = grp * 32; c0 < P.bn; c0 += 32 * EPI_GROUPS) {
                 uint32_t r[32];
                 long long ck0 = clock64();
                 tmem_ld32(tbase + c0, r);
@@ -457,13 +471,17 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     }
                     continue;
                 }
-                // double-buffered staging: the buffer written now was last
-                // used two chunks ago; at most one store group may still read
-                uint8_t* sbuf = staging + (warp - 2) * STAGE_W + (nchunk & 1) * 4096;
+                // staging: with two buffers the one written now was last used
+                // two chunks ago (at most one store group may still read it);
+                // with one, the previous store must have finished reading
+                uint8_t* sbuf = staging + (warp - 2) * STAGE_W + (nchunk % STAGE_BUFS) * 4096;
                 nchunk++;
                 long long ck2 = clock64();
                 if (P.tma_out) {
-                    if (lane == 0) bulk_wait_read1();
+                    if (lane == 0) {
+                        if (STAGE_BUFS == 2) bulk_wait_read1();
+                        else bulk_wait_read0();
+                    }
                     __syncwarp();
                 }
                 long long ck3 = clock64();
@@ -471,9 +489,22 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 if (row_ok) {
                 float t[32];
                 if (a.bias) {
-                    load32(t, a.bias, n0, DT_F32, nvalid);
-                    #pragma unroll
-                    for (int j = 0; j < 32; j++) v[j] += t[j];
+                    if (P.bias_smem) {
+                        if (nvalid == 32) {
+                            #pragma unroll
+                            for (int j = 0; j < 32; j += 4) {
+                                float4 b4 = *(const float4*)(sbias + n0 + j);
+                                v[j] += b4.x; v[j + 1] += b4.y; v[j + 2] += b4.z; v[j + 3] += b4.w;
+                            }
+                        } else {
+                            #pragma unroll
+                            for (int j = 0; j < 32; j++) if (j < nvalid) v[j] += sbias[n0 + j];
+                        }
+                    } else {
+                        load32(t, a.bias, n0, DT_F32, nvalid);
+                        #pragma unroll
+                        for (int j = 0; j < 32; j++) v[j] += t[j];
+                    }
                 }
                 if (a.bcast) {
                     load32(t, a.bcast, (long)(m / a.bcast_group) * a.ld_bcast + n0, DT_F32, nvalid);
@@ -483,17 +514,16 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 if (a.act == ACT_GELU) {
                     if (a.out2) {
                         #pragma unroll
-                        for (int j = 0; j < 32; j++) {
-                            float c, pd;
-                            gelu_parts_fast(v[j], c, pd);
-                            t[j] = fmaf(v[j], pd, c);         // GELU'(x), saved for backward
-                            v[j] *= c;
-                        }
+                        for (int j = 0; j < 32; j += 2)        // GELU'(x) saved for backward
+                            gelu2(v[j], v[j + 1], v[j], v[j + 1], t[j], t[j + 1]);
                         if (P.tma_out) stage32(sbuf + 2048, lane, DT_BF16, t);
                         else store32(a.out2, (long)m * a.ldo2 + n0, a.out2_dtype, t, nvalid);
                     } else {
                         #pragma unroll
-                        for (int j = 0; j < 32; j++) v[j] = gelu_fast(v[j]);
+                        for (int j = 0; j < 32; j += 2) {
+                            float g0, g1;
+                            gelu2(v[j], v[j + 1], v[j], v[j + 1], g0, g1);
+                        }
                     }
                 } else if (a.act == ACT_GELU_BWD) {
                     load32(t, a.aux, (long)m * a.ld_aux + n0, a.aux_dtype, nvalid);
@@ -711,7 +741,8 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
                 !((uintptr_t)a.out & 15) && (a.ldo * oeb) % 16 == 0 &&
                 (!a.out2 || (a.act == ACT_GELU && a.out2_dtype == DT_BF16 && a.out_dtype == DT_BF16 &&
                              !((uintptr_t)a.out2 & 15) && (a.ldo2 * 2) % 16 == 0));
-    int budget = 232448 - 1024 - 512 - (P.tma_out ? NUM_EPI * STAGE_W : 0);
+    P.bias_smem = (PTCG_BIAS_SMEM && a.bias && a.N <= BIAS_SMEM_MAX) ? a.N : 0;
+    int budget = 232448 - 1024 - 512 - (P.tma_out ? NUM_EPI * STAGE_W : 0) - P.bias_smem * 4;
     P.stages = budget / P.stage_bytes;
     if (P.stages > 6) P.stages = 6;
     if (P.stages < 2) return false;
@@ -742,7 +773,7 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
 void launch_tc(const TcPlan& pl, cudaStream_t s) {
     const TcParams& P = pl.P;
     size_t smem = 1024 + (size_t)P.stages * P.stage_bytes + (P.tma_out ? NUM_EPI * STAGE_W : 0) +
-                  (2 * P.stages + 5) * 8 + 32;
+                  (2 * P.stages + 5) * 8 + 48 + (size_t)P.bias_smem * 4;
     int total = P.m_tiles * P.n_tiles * P.splits;
     int grid = total < g_sms ? total : g_sms;
     if (pl.eb == 2) {

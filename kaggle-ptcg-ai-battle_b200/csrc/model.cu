@@ -1616,7 +1616,9 @@ int ptcg_attention_bwd(int operand_dtype, const void* qkv, long ldqkv, const uns
 
 static __global__ void k_eval_gelu(const float* x, float* g, float* dg, int n) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) { g[i] = gelu_fast(x[i]); dg[i] = gelu_grad_fast(x[i]); }
+    // the tensor-core epilogue's GELU pair (values 2i, 2i+1)
+    if (2 * i + 1 < n) gelu2(x[2 * i], x[2 * i + 1], g[2 * i], g[2 * i + 1], dg[2 * i], dg[2 * i + 1]);
+    else if (2 * i < n) { float t0, t1; gelu2(x[2 * i], 0.f, g[2 * i], t0, dg[2 * i], t1); }
 }
 
 int ptcg_eval_gelu(const float* x, float* gelu, float* gelu_grad, int n, void* stream) {
