@@ -725,7 +725,9 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     bool plain = a.accumulate && a.out_dtype == DT_F32 && !a.bias && !a.bcast &&
                  a.act == ACT_NONE && !a.resid && !a.out2 && a.remap_group == 0 && !a.colsum;
     if (plain && tiles < g_sms && P.kb_total >= 8) {
-        int want = (g_sms + tiles - 1) / tiles;
+        // one wave: tiles x splits <= SMs (a split item is a long K range,
+        // so even one CTA with a second item doubles the launch)
+        int want = g_sms / tiles;
         int maxs = P.kb_total / 4;
         P.splits = want < maxs ? want : maxs;
         if (P.splits < 1) P.splits = 1;
