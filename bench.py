@@ -324,6 +324,29 @@ def main():
     value = nt * world * args.steps / (ms_max / 1e3)
     st = stats.cpu().numpy()
 
+    # --- optimizer roofline (HBM): ptcg_adam_step = norm pass + fused
+    #     clip/Adam/bf16-copy pass, timed alone with CUDA events
+    from ptcg_b200.config import optimizer_bytes
+    ob = optimizer_bytes(s)["total"]
+    import ctypes
+    ost = torch.zeros(2, device=dev)
+    cstream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def adam_call():
+        pol.lib.ptcg_adam_step(pol.h, hyper["lr"], hyper["betas"][0], hyper["betas"][1],
+                               hyper["eps"], hyper["max_norm"], None,
+                               ctypes.c_void_p(ost.data_ptr()), cstream)
+    for _ in range(3):
+        adam_call()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a0.record()
+    for _ in range(20):
+        adam_call()
+    a1.record()
+    torch.cuda.synchronize()
+    adam_ms = a0.elapsed_time(a1) / 20
+
     # --- end to end through the public API: pinned host inputs -> device,
     #     train step, loss stats back to the host, every step
     host = dict(obs=obs_h, act=act_h, old=old.cpu().pin_memory(), adv=adv.cpu().pin_memory(),
@@ -440,6 +463,12 @@ def main():
                          "reference_equivalent": value * flops_ref / world / 1e12,
                          "gflop_per_sample": {"executed": flops_exec / 1e9,
                                               "reference_equivalent": flops_ref / 1e9}},
+        "roofline_optimizer": {
+            "kernel": "ptcg_adam_step (k_sumsq + k_adam)", "bound": "hbm",
+            "achieved": ob / (adam_ms / 1e3) / 1e9, "peak": peaks.get("hbm_gbs"),
+            "unit": "GB/s", "frac": ob / (adam_ms / 1e3) / 1e9 / peaks.get("hbm_gbs", 6650.0),
+            "traffic": ob, "ms": adam_ms,
+            "note": "algorithmic bytes: 32 B per arena float + 2 B per bf16-copied parameter"},
         "rollout": rollout,
         "cpu_baseline": cpu,
         "clocks": clk.summary(),

@@ -254,3 +254,23 @@ def train_flops(s: Shape, critic_rows: str = "first"):
     """Per-sample train-step FLOPs: forward plus a backward of twice the
     forward (dX and dW GEMMs)."""
     return 3 * forward_flops(s, critic_rows)["total"]
+
+
+def bf16_copied(name: str) -> bool:
+    """Parameters whose bf16 compute copy the Adam pass refreshes in bf16
+    mode: the block matrices, token_proj, oracle_proj and aux_hand."""
+    block = (len(name) > 3 and name[0] in "bc" and name[1].isdigit()
+             and any(k in name for k in ("qkv_w", "proj_w", "ffn1_w", "ffn2_w")))
+    return block or name in ("token_proj_w", "oracle_proj_w", "aux_hand_w")
+
+
+def optimizer_bytes(s: Shape, bf16: bool = True):
+    """Algorithmic HBM bytes of one clip + Adam step over the arena (every
+    tensor padded to 16 bytes): the norm pass reads the grads (4 B/float);
+    the update reads grad, param, m, v and writes param, m, v (28 B/float)
+    and writes the bf16 copies (2 B per copied parameter)."""
+    import numpy as np
+    arena = sum((int(np.prod(shp)) + 3) // 4 * 4 for _, shp in param_table(s))
+    copied = sum(int(np.prod(shp)) for name, shp in param_table(s) if bf16 and bf16_copied(name))
+    return {"norm_pass": 4 * arena, "update_pass": 28 * arena + 2 * copied,
+            "total": 32 * arena + 2 * copied}

@@ -1007,14 +1007,16 @@ __global__ void k_negamax_adv(const float* values, const float* rewards, const f
 }
 
 // ------------------------------------------------------------ Adam
-// pass 1: per-block partial sum of squared grads (fp64 accumulation)
+// pass 1: per-block partial sum of squared grads (fp64 accumulation);
+// n is a multiple of 4 (every arena tensor starts 16-byte aligned)
 __global__ void k_sumsq(double* partials, const float* g, long n) {
     __shared__ double sh[32];
     double s = 0.0;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < (n >> 2);
          i += (long)gridDim.x * blockDim.x) {
-        double v = g[i];
-        s += v * v;
+        float4 v = g4[i];
+        s += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
     }
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
@@ -1040,12 +1042,20 @@ __global__ void k_adam(float* p, float* m, float* v, const float* g, long n,
                        const int* chunk_copy, int chunk) {
     __shared__ float s_coef, s_bc1, s_bc2sqrt;
     __shared__ int s_ok;
+    __shared__ double s_red[32];
+    // every block re-reduces the partials in the same fixed order
+    // (deterministic, identical on every block)
+    double tp = 0.0;
+    for (int i = threadIdx.x; i < nparts; i += blockDim.x) tp += partials[i];
+    for (int o = 16; o > 0; o >>= 1) tp += __shfl_xor_sync(0xffffffffu, tp, o);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = tp;
+    __syncthreads();
     if (threadIdx.x == 0) {
         double t_step = (double)(step_dev[0] + 1);
         s_bc1 = (float)(1.0 - pow((double)b1, t_step));
         s_bc2sqrt = (float)sqrt(1.0 - pow((double)b2, t_step));
         double t = 0.0;
-        for (int i = 0; i < nparts; i++) t += partials[i];
+        for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += s_red[i];
         float norm = (float)sqrt(t);
         int ok = isfinite(norm) && (gate == nullptr || gate[0] != 0.f);
         float coef = max_norm / (norm + 1e-6f);
@@ -1058,22 +1068,48 @@ __global__ void k_adam(float* p, float* m, float* v, const float* g, long n,
     float coef = s_coef;
     float step_size = lr / s_bc1;
     float bc2sqrt = s_bc2sqrt;
+    float4* p4 = reinterpret_cast<float4*>(p);
+    float4* m4 = reinterpret_cast<float4*>(m);
+    float4* v4 = reinterpret_cast<float4*>(v);
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+    // float4 granules: n, chunk and every tensor offset are multiples of 4,
+    // so a granule never straddles two tensors
     for (long c0 = (long)blockIdx.x * chunk; c0 < n; c0 += (long)gridDim.x * chunk) {
         // first bf16 copy that ends after the chunk start (copies sorted by off)
         int ci = chunk_copy ? chunk_copy[c0 / chunk] : ncopies;
         long c1 = min(n, c0 + chunk);
-        for (long i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
-            float gi = g[i] * coef;
-            float mi = b1 * m[i] + (1.f - b1) * gi;
-            float vi = b2 * v[i] + (1.f - b2) * gi * gi;
-            m[i] = mi; v[i] = vi;
-            float pi = p[i] - step_size * mi / (sqrtf(vi) / bc2sqrt + eps);
-            p[i] = pi;
+        for (long i = c0 + 4 * threadIdx.x; i < c1; i += 4 * blockDim.x) {
+            float4 gg = g4[i >> 2], mm = m4[i >> 2], vv = v4[i >> 2], pp = p4[i >> 2];
+            float gs[4] = {gg.x, gg.y, gg.z, gg.w}, ms[4] = {mm.x, mm.y, mm.z, mm.w};
+            float vs[4] = {vv.x, vv.y, vv.z, vv.w}, ps[4] = {pp.x, pp.y, pp.z, pp.w};
+            #pragma unroll
+            for (int e = 0; e < 4; e++) {
+                float gi = gs[e] * coef;
+                ms[e] = b1 * ms[e] + (1.f - b1) * gi;
+                vs[e] = b2 * vs[e] + (1.f - b2) * gi * gi;
+                ps[e] = ps[e] - step_size * ms[e] / (sqrtf(vs[e]) / bc2sqrt + eps);
+            }
+            m4[i >> 2] = make_float4(ms[0], ms[1], ms[2], ms[3]);
+            v4[i >> 2] = make_float4(vs[0], vs[1], vs[2], vs[3]);
+            p4[i >> 2] = make_float4(ps[0], ps[1], ps[2], ps[3]);
             while (ci < ncopies && i >= copies[ci].off + copies[ci].n) ci++;
             if (ci < ncopies && i >= copies[ci].off) {
                 const BfCopy& cp = copies[ci];
                 long j = i - cp.off;
-                cp.dst[(j / cp.cols) * cp.ldp + (j % cp.cols)] = __float2bfloat16_rn(pi);
+                if (cp.ldp == cp.cols) {            // contiguous copy: one 8-byte store
+                    uint2 q;
+                    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&q);
+                    h[0] = __floats2bfloat162_rn(ps[0], ps[1]);
+                    h[1] = __floats2bfloat162_rn(ps[2], ps[3]);
+                    *reinterpret_cast<uint2*>(cp.dst + j) = q;
+                } else {                            // padded pitch (rows of cols < ldp)
+                    #pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        if (j + e >= cp.n) break;
+                        int jj = (int)(j + e), r = jj / cp.cols;
+                        cp.dst[(long)r * cp.ldp + (jj - r * cp.cols)] = __float2bfloat16_rn(ps[e]);
+                    }
+                }
             }
         }
     }

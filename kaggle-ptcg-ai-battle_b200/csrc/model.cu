@@ -1167,8 +1167,12 @@ int ptcg_create(const PtcgShape* s, int precision, int device, PtcgModel** out) 
     }
     cudaDeviceProp prop;
     CK(cudaGetDeviceProperties(&prop, device));
-    M->sumsq_grid = prop.multiProcessorCount * 4;
-    M->adam_grid = prop.multiProcessorCount * 8;
+    // one wave of resident blocks for both optimizer passes
+    int per_sm = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_adam, 256, 0));
+    M->adam_grid = prop.multiProcessorCount * (per_sm > 0 ? per_sm : 1);
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_sumsq, 256, 0));
+    M->sumsq_grid = prop.multiProcessorCount * (per_sm > 0 ? per_sm : 1);
     CK(cudaMalloc(&M->d_partials, sizeof(double) * M->sumsq_grid));
     CK(cudaMalloc(&M->d_misc, sizeof(float) * 64));
     CK(cudaMemset(M->d_misc, 0, sizeof(float) * 64));
