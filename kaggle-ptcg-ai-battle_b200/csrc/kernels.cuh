@@ -411,53 +411,59 @@ __global__ void k_q_in_bwd(float* d_temb, float* d_h, float* d_poc, float* d_poa
     else atomicAdd(&d_poa[(long)id_clamp(oi[4], L.na) * 64 + (c - 80 - 2 * D)], v);
 }
 
-// score input [q | r | g | dvec | q*r], r = h[n, 0] (k_sc_in, ptcg_model.cu:422-439)
-template <typename T>
-__global__ void k_sc_in(T* out, long ldo, const float* q, const float* h, const float* gd,
-                        int D, int lseq, int nopt, int R) {
-    const int W = 3 * D + 192;
+// ---- score1 split: score1(cat[q, r, g, d, q*r]) = [q | q*r] Wqq^T +
+//      ([r | g | d] Wrgd^T + b) broadcast over the sample's options
+// qq = [q | q*r] (NO x 2D): the second half from the first and r = h[n, 0]
+__global__ void k_qr_fill(float* qq, int D, const float* h, int lseq, int nopt, long total) {
     long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i >= (long)R * nopt * W) return;
-    int c = (int)(i % W);
-    long nj = i / W;
-    int n = (int)(nj / nopt);
-    const float* r = h + (long)n * lseq * D;
-    float v;
-    if (c < D) v = q[nj * D + c];
-    else if (c < 2 * D) v = r[c - D];
-    else if (c < 2 * D + 192) v = gd[(long)n * 192 + (c - 2 * D)];
-    else v = q[nj * D + (c - 2 * D - 192)] * r[c - 2 * D - 192];
-    st(&out[nj * ldo + c], v);
+    if (i >= total) return;
+    long nj = i / D;
+    int c = (int)(i % D), n = (int)(nj / nopt);
+    float* row = qq + nj * 2 * D;
+    row[D + c] = row[c] * h[(long)n * lseq * D + c];
 }
-
-// score-input backward, one block per sample (no atomics): d_q in T,
-// d_h[n, 0] += sum_j (ds_r + ds_qr * q), d_gd[n] += sum_j ds_{g,d}
+// per-sample [r | g | d] (R x (D + 192)), gd = [g | d] (R x 192)
+__global__ void k_rgd_fill(float* out, const float* h, int lseq, const float* gd, int D, int R) {
+    const int W = D + 192;
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)R * W) return;
+    int n = (int)(i / W), c = (int)(i % W);
+    out[i] = c < D ? h[(long)n * lseq * D + c] : gd[(long)n * 192 + (c - D)];
+}
+// [W_q | W_qr] (rows x 2D) from score1_w (rows x (3D + 192)): columns
+// [0, D) and [2D + 192, 3D + 192)
+__global__ void k_pack_wqq(float* out, const float* w, int D, long ldw, int rows) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)rows * 2 * D) return;
+    int o = (int)(i / (2 * D)), c = (int)(i % (2 * D));
+    out[i] = w[(long)o * ldw + (c < D ? c : c + D + 192)];
+}
+// backward of qq and of [r | g | d], one block per sample (no atomics):
+//   d_q[nj, c] = dqq[nj, c] + dqq[nj, D + c] r[c]        (+ q2 bias colsum)
+//   d_h[n, 0, c] += sum_j dqq[nj, D + c] q[nj, c] + drgd[n, c]
+//   d_gd[n, e]  += drgd[n, D + e]
 template <typename T>
-__global__ void k_sc_in_bwd(T* d_q, long lddq, float* d_h, float* d_gd, const float* ds,
-                            long ldds, const float* q, const float* h, int D, int lseq,
-                            int nopt, float* dq_colsum) {
+__global__ void k_qq_bwd(T* d_q, long lddq, float* d_h, float* d_gd, const float* dqq,
+                         const float* qq, const float* drgd, const float* h, int D, int lseq,
+                         int nopt, float* dq_colsum) {
     int n = blockIdx.x;
     const float* r = h + (long)n * lseq * D;
+    const float* dr = drgd + (long)n * (D + 192);
     for (int c = threadIdx.x; c < D + 192; c += blockDim.x) {
         if (c < D) {
             float rr = r[c], acc = 0.f, cs = 0.f;
             for (int j = 0; j < nopt; j++) {
                 long nj = (long)n * nopt + j;
-                const float* dr = ds + nj * ldds;
-                float qv = q[nj * D + c];
-                float dqv = dr[c] + dr[2 * D + 192 + c] * rr;
+                const float* g = dqq + nj * 2 * D;
+                float dqv = g[c] + g[D + c] * rr;
                 st(&d_q[nj * lddq + c], dqv);
                 cs += dqv;
-                acc += dr[D + c] + dr[2 * D + 192 + c] * qv;
+                acc += g[D + c] * qq[nj * 2 * D + c];
             }
-            d_h[(long)n * lseq * D + c] += acc;
+            d_h[(long)n * lseq * D + c] += acc + dr[c];
             if (dq_colsum) atomicAdd(&dq_colsum[c], cs);
         } else {
-            int e = c - D;
-            float acc = 0.f;
-            for (int j = 0; j < nopt; j++)
-                acc += ds[((long)n * nopt + j) * ldds + 2 * D + e];
-            d_gd[(long)n * 192 + e] += acc;
+            d_gd[(long)n * 192 + (c - D)] += dr[c];
         }
     }
 }
@@ -487,7 +493,8 @@ template <typename TI, typename TO>
 __global__ void k_rowdot_bwd(TO* d_pre, long ldd, const TI* pre, long ldp, const TI* in,
                              long ldi, const float* w, float* dw, float* db, const float* dsrc,
                              long ds_stride, const float* ret, float coef, int rows, int K,
-                             int rows_per_block, float* loss, float* dpre_colsum) {
+                             int rows_per_block, float* loss, float* dpre_colsum,
+                             float* dpre_blocksum = nullptr) {
     extern __shared__ float shd[];             // [K] dw partials, [1] db
     for (int k = threadIdx.x; k <= K; k += blockDim.x) shd[k] = 0.f;
     __syncthreads();
@@ -511,6 +518,7 @@ __global__ void k_rowdot_bwd(TO* d_pre, long ldd, const TI* pre, long ldp, const
         }
         shd[k] = acc;
         if (dpre_colsum) atomicAdd(&dpre_colsum[k], csum);
+        if (dpre_blocksum) dpre_blocksum[(long)blockIdx.x * K + k] = csum;   // [block, K]
     }
     if (threadIdx.x == 0) shd[K] = dbp;
     __syncthreads();

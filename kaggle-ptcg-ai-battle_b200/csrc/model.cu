@@ -134,7 +134,8 @@ struct Work {
     std::vector<float*> x;              // trunk states (LAYERS+1 train, 2 rollout)
     std::vector<BlkAct> blk;            // per layer (train) / 1 shared (rollout)
     float* h; float *muf, *rsf;
-    void *qin, *q1pre, *q1; float* q; void *scin, *s1pre, *s1;
+    void *qin, *q1pre, *q1; void *scin, *s1pre, *s1;
+    float *u, *rgd, *wqq, *du, *drgd;   // score1 split: per-sample term, inputs, packed W
     void* otokin; float* xc[2]; BlkAct cblk;
     float *ovin, *ov1pre, *ov1; float* out;
     // train-only heads
@@ -377,8 +378,10 @@ static void plan_work(Work& W, Bump& m, int R, bool train, const Dims& z, int es
     W.qin = m.f(NO * rup(z.Q_IN, 8));
     W.q1pre = train ? m.f(NO * z.D) : nullptr;
     W.q1 = m.f(NO * z.D);
-    W.q = m.f(NO * z.D);
-    W.scin = m.f(NO * z.SCORE_IN);
+    W.scin = m.f(NO * 2 * z.D);                 // qq = [q | q*r]
+    W.u = m.f((long)R * 256);
+    W.rgd = m.f((long)R * (z.D + 192));
+    W.wqq = m.f(256L * 2 * z.D);
     W.s1pre = train ? m.f(NO * 256) : nullptr;
     W.s1 = m.f(NO * 256);
     W.otokin = m.take((long)R * 56 * 136 * esz);
@@ -399,7 +402,9 @@ static void plan_work(Work& W, Bump& m, int R, bool train, const Dims& z, int es
     W.dbvin = m.f((long)R * z.VAL_IN);
     W.d_v1pre = m.f((long)R * 256);
     W.dscores = m.f(NO);
-    W.dscin = m.f(NO * z.SCORE_IN);
+    W.dscin = m.f(NO * 2 * z.D);                // d qq
+    W.du = m.f((long)R * 256);
+    W.drgd = m.f((long)R * (z.D + 192));
     W.dqin = m.f(NO * z.Q_IN);
     W.dtokcat = m.f(NT * z.TOK_IN);
     W.ddecin = m.f((long)R * 696);
@@ -611,15 +616,27 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     a.bias = M->w("q1_b").p; a.act = ACT_GELU; a.allow_tf32 = tf32;
     if (train) { a.out2 = Wk.q1pre; a.ldo2 = D; }
     gemm(M, a, s);
-    a = lin_fwd(DT_F32, (int)NO, D, D, Wk.q1, D, f32w(M->w("q2_w"), D), Wk.q, D, DT_F32);
+    // score1(cat[q, r, g, d, q*r]) (model.py:270-273) evaluated as
+    //   [q | q*r] Wqq^T + bcast_n([r | g | d] Wrgd^T + b):
+    // the per-sample columns r, g, d go through one GEMM per sample instead
+    // of NOPT copies per sample
+    float* qq = (float*)Wk.scin;
+    a = lin_fwd(DT_F32, (int)NO, D, D, Wk.q1, D, f32w(M->w("q2_w"), D), qq, 2 * D, DT_F32);
     a.bias = M->w("q2_b").p; a.allow_tf32 = tf32;
     gemm(M, a, s);
-    long nsc = NO * z.SCORE_IN;
-    ++g_ptcg_launches, k_sc_in<float><<<cdiv(nsc, TPB), TPB, 0, s>>>((float*)Wk.scin, z.SCORE_IN, Wk.q, Wk.h, Wk.gd,
-        D, z.LSEQ, z.NOPT, R);
-    a = lin_fwd(DT_F32, (int)NO, z.SCORE_IN, 256, Wk.scin, z.SCORE_IN,
-                f32w(M->w("score1_w"), z.SCORE_IN), Wk.s1, 256, DT_F32);
-    a.bias = M->w("score1_b").p; a.act = ACT_GELU; a.allow_tf32 = tf32;
+    ++g_ptcg_launches, k_qr_fill<<<cdiv(NO * D, TPB), TPB, 0, s>>>(qq, D, Wk.h, z.LSEQ, z.NOPT, NO * D);
+    ++g_ptcg_launches, k_rgd_fill<<<cdiv((long)R * (D + 192), TPB), TPB, 0, s>>>(Wk.rgd, Wk.h, z.LSEQ, Wk.gd,
+        D, R);
+    W ws1 = f32w(M->w("score1_w"), z.SCORE_IN);
+    W wrgd = ws1; wrgd.op = ws1.p + D;           // columns [D, 2D + 192)
+    a = lin_fwd(DT_F32, R, D + 192, 256, Wk.rgd, D + 192, wrgd, Wk.u, 256, DT_F32);
+    a.bias = M->w("score1_b").p; a.allow_tf32 = tf32;
+    gemm(M, a, s);
+    ++g_ptcg_launches, k_pack_wqq<<<cdiv(256L * 2 * D, TPB), TPB, 0, s>>>(Wk.wqq, ws1.p, D, z.SCORE_IN, 256);
+    W wqq = ws1; wqq.op = Wk.wqq; wqq.ld = 2 * D;
+    a = lin_fwd(DT_F32, (int)NO, 2 * D, 256, qq, 2 * D, wqq, Wk.s1, 256, DT_F32);
+    a.bcast = Wk.u; a.ld_bcast = 256; a.bcast_group = z.NOPT;
+    a.act = ACT_GELU; a.allow_tf32 = tf32;
     if (train) { a.out2 = Wk.s1pre; a.ldo2 = 256; }
     gemm(M, a, s);
     // score2 -> out[n, j]  (out row stride NOPT+1): rows r = n*NOPT + j map to
@@ -906,24 +923,40 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     // ---- option scorer (d scores = grad[:, :NOPT])
     ++g_ptcg_launches, k_scale_copy<<<cdiv(NO, TPB), TPB, 0, s>>>(Wk.dscores, z.NOPT, grad, z.NOPT + 1, R, z.NOPT, 1.f);
     {
-        int rpb = 64;
+        // one sample per block: the block sums of d s1pre are d u (the
+        // per-sample broadcast term of score1)
+        int rpb = z.NOPT;
         unsigned g = cdiv(NO, rpb);
         ++g_ptcg_launches, k_rowdot_bwd<float, float><<<g, 256, 257 * sizeof(float), s>>>((float*)Wk.ds1pre, 256,
                 (const float*)Wk.s1pre, 256, (const float*)Wk.s1, 256, M->w("score2_w").p,
                 M->w("score2_w").g, M->w("score2_b").g, Wk.dscores, 1, nullptr, 0.f, (int)NO, 256,
-                rpb, nullptr, M->w("score1_b").g);
+                rpb, nullptr, M->w("score1_b").g, Wk.du);
     }
     W ws1 = f32w(M->w("score1_w"), z.SCORE_IN);
+    const float* qq = (const float*)Wk.scin;
     {
-        GemmArgs a = lin_dw(DT_F32, (int)NO, z.SCORE_IN, 256, Wk.ds1pre, 256, Wk.scin, z.SCORE_IN, ws1.g);
+        // [q | q*r] part -> score1_w columns [0, D) and [2D + 192, 3D + 192)
+        GemmArgs a = lin_dw(DT_F32, (int)NO, D, 256, Wk.ds1pre, 256, qq, 2 * D, ws1.g);
+        a.ldo = z.SCORE_IN; a.allow_tf32 = tf32;
+        gemm(M, a, s);
+        a = lin_dw(DT_F32, (int)NO, D, 256, Wk.ds1pre, 256, qq + D, 2 * D, ws1.g + 2 * D + 192);
+        a.ldo = z.SCORE_IN; a.allow_tf32 = tf32;
+        gemm(M, a, s);
+        // per-sample part -> columns [D, 2D + 192)
+        a = lin_dw(DT_F32, R, D + 192, 256, Wk.du, 256, Wk.rgd, D + 192, ws1.g + D);
+        a.ldo = z.SCORE_IN; a.allow_tf32 = tf32;
+        gemm(M, a, s);
+        W wqq = ws1; wqq.op = Wk.wqq; wqq.ld = 2 * D;
+        a = lin_dx(DT_F32, (int)NO, 2 * D, 256, Wk.ds1pre, 256, wqq, Wk.dscin, 2 * D, DT_F32);
         a.allow_tf32 = tf32;
         gemm(M, a, s);
-        a = lin_dx(DT_F32, (int)NO, z.SCORE_IN, 256, Wk.ds1pre, 256, ws1, Wk.dscin, z.SCORE_IN, DT_F32);
+        W wrgd = ws1; wrgd.op = ws1.p + D;
+        a = lin_dx(DT_F32, R, D + 192, 256, Wk.du, 256, wrgd, Wk.drgd, D + 192, DT_F32);
         a.allow_tf32 = tf32;
         gemm(M, a, s);
     }
-    ++g_ptcg_launches, k_sc_in_bwd<float><<<R, 256, 0, s>>>((float*)Wk.dq, D, Wk.dh, Wk.dgd, Wk.dscin, z.SCORE_IN,
-            Wk.q, Wk.h, D, z.LSEQ, z.NOPT, M->w("q2_b").g);
+    ++g_ptcg_launches, k_qq_bwd<float><<<R, 256, 0, s>>>((float*)Wk.dq, D, Wk.dh, Wk.dgd, (const float*)Wk.dscin,
+            qq, Wk.drgd, Wk.h, D, z.LSEQ, z.NOPT, M->w("q2_b").g);
     W wq2 = f32w(M->w("q2_w"), D), wq1 = f32w(M->w("q1_w"), z.Q_IN);
     {
         GemmArgs a = lin_dw(DT_F32, (int)NO, D, D, Wk.dq, D, Wk.q1, D, wq2.g);
