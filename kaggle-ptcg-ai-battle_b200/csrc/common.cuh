@@ -120,6 +120,24 @@ PTCG_DEV float warp_max(float v) {
     return v;
 }
 
+// 16-byte vector helpers for the row-per-warp gather / scatter kernels
+PTCG_DEV float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+PTCG_DEV void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+PTCG_DEV void st4(bf16* p, float4 v) {
+    uint2 q;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&q);
+    h[0] = __floats2bfloat162_rn(v.x, v.y);
+    h[1] = __floats2bfloat162_rn(v.z, v.w);
+    *reinterpret_cast<uint2*>(p) = q;
+}
+PTCG_DEV float4 add4(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+PTCG_DEV bool nz4(float4 v) { return v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f; }
+// four fp32 atomic adds in one vector reduction (16-byte aligned target)
+PTCG_DEV void red_add4(float* p, float4 v) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};"
+                 :: "l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w) : "memory");
+}
+
 // id stored as float in the obs row -> int with C truncation, then clamp
 PTCG_DEV int id_clamp(float v, int hi_excl) {
     int i = (int)v;

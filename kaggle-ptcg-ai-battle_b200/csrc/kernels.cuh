@@ -273,30 +273,44 @@ template <typename T>
 __global__ void k_tok_cat(T* out, long ldo, const float* obs, ObsLayout L,
                           const float* cv, const float* zemb, const float* oemb,
                           int R, int tok_in) {
-    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i >= (long)R * L.ltok * tok_in) return;
-    int c = (int)(i % tok_in);
-    long nl = i / tok_in;
-    int l = (int)(nl % L.ltok), n = (int)(nl / L.ltok);
+    // one warp per token row, four consecutive columns per lane
+    long nl = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (nl >= (long)R * L.ltok) return;
+    const int n = (int)(nl / L.ltok), l = (int)(nl - (long)n * L.ltok);
     const float* row = obs + (long)n * L.obs;
     const float* ti = row + L.toki + l * 5;
-    float v;
-    if (c < 128) {
-        v = cv[(long)id_clamp(ti[0], L.nc) * 128 + c];
-    } else if (c < 256) {
-        int e = c - 128;
-        int t0 = (int)ti[3], t1 = (int)ti[4];
-        float a = t0 > 0 ? cv[(long)(t0 >= L.nc ? L.nc - 1 : t0) * 128 + e] : 0.f;
-        float b = t1 > 0 ? cv[(long)(t1 >= L.nc ? L.nc - 1 : t1) * 128 + e] : 0.f;
-        v = a + b;
-    } else if (c < 256 + L.tok_f) {
-        v = row[L.tokf + l * L.tok_f + (c - 256)];
-    } else if (c < 256 + L.tok_f + 8) {
-        v = zemb[id_clamp(ti[1], 16) * 8 + (c - 256 - L.tok_f)];
-    } else {
-        v = oemb[id_clamp(ti[2], 4) * 4 + (c - 264 - L.tok_f)];
+    const float* c0 = cv + (long)id_clamp(ti[0], L.nc) * 128;
+    const int t0 = (int)ti[3], t1 = (int)ti[4];
+    const float* ca = t0 > 0 ? cv + (long)(t0 >= L.nc ? L.nc - 1 : t0) * 128 : nullptr;
+    const float* cb = t1 > 0 ? cv + (long)(t1 >= L.nc ? L.nc - 1 : t1) * 128 : nullptr;
+    const float* ze = zemb + id_clamp(ti[1], 16) * 8;
+    const float* oe = oemb + id_clamp(ti[2], 4) * 4;
+    const float* tf = row + L.tokf + l * L.tok_f;
+    T* o = out + nl * ldo;
+    for (int c4 = lane * 4; c4 < tok_in; c4 += 128) {
+        float4 v;
+        if (c4 + 4 <= 128) {
+            v = ld4(c0 + c4);
+        } else if (c4 >= 128 && c4 + 4 <= 256) {
+            float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+            v = add4(ca ? ld4(ca + c4 - 128) : z, cb ? ld4(cb + c4 - 128) : z);
+        } else {
+            float e[4];
+            #pragma unroll
+            for (int k = 0; k < 4; k++) {
+                int c = c4 + k;
+                float x = 0.f;
+                if (c >= tok_in) x = 0.f;
+                else if (c < 256 + L.tok_f) x = tf[c - 256];
+                else if (c < 264 + L.tok_f) x = ze[c - 256 - L.tok_f];
+                else x = oe[c - 264 - L.tok_f];
+                e[k] = x;
+            }
+            v = make_float4(e[0], e[1], e[2], e[3]);
+        }
+        if (c4 + 4 <= tok_in || c4 + 4 <= ldo) st4(o + c4, v);
     }
-    st(&out[nl * ldo + c], v);
 }
 
 // x0 readout rows + key mask keep = [1, zone > 0] (k_x0, ptcg_model.cu:348-368)
@@ -364,63 +378,83 @@ __global__ void k_dec_in_bwd(float* d_cv, float* d_av, float* d_semb, float* d_c
 // The two projections are applied per table row beforehand (poc = opt_card
 // over all NC card vectors, poa = opt_attack over all NA attack vectors):
 // gathering a projected row equals projecting the gathered row.
-template <typename T>
-__global__ void k_q_in(T* out, long ldo, const float* obs, ObsLayout L, const float* h,
+// one warp per option row, four consecutive columns per lane (every
+// segment boundary is a multiple of 4)
+__global__ void k_q_in(float* out, long ldo, const float* obs, ObsLayout L, const float* h,
                        int D, const float* temb, const float* poc, const float* poa,
                        int R, int q_in) {
-    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i >= (long)R * L.nopt * q_in) return;
-    int c = (int)(i % q_in);
-    long nj = i / q_in;
-    int j = (int)(nj % L.nopt), n = (int)(nj / L.nopt);
+    long nj = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (nj >= (long)R * L.nopt) return;
+    const int n = (int)(nj / L.nopt), j = (int)(nj - (long)n * L.nopt);
     const float* row = obs + (long)n * L.obs;
     const float* oi = row + L.opti + j * 6;
-    float v;
-    if (c < 16) v = temb[id_clamp(oi[0], 33) * 16 + c];
-    else if (c < 16 + 2 * D) {
-        int which = (c - 16) >= D;
-        int p = (int)oi[1 + which];
-        v = (p <= 0 || p > L.ltok) ? 0.f
-            : h[((long)n * L.lseq + p) * D + (c - 16 - which * D)];
-    } else if (c < 16 + 2 * D + 64) v = poc[(long)id_clamp(oi[3], L.nc) * 64 + (c - 16 - 2 * D)];
-    else if (c < 16 + 2 * D + 128) v = poa[(long)id_clamp(oi[4], L.na) * 64 + (c - 80 - 2 * D)];
-    else v = row[L.optf + j * 8 + (c - 144 - 2 * D)];
-    st(&out[nj * ldo + c], v);
+    const float* te = temb + id_clamp(oi[0], 33) * 16;
+    const int p1 = (int)oi[1], p2 = (int)oi[2];
+    const float* h1 = (p1 <= 0 || p1 > L.ltok) ? nullptr : h + ((long)n * L.lseq + p1) * D;
+    const float* h2 = (p2 <= 0 || p2 > L.ltok) ? nullptr : h + ((long)n * L.lseq + p2) * D;
+    const float* pc = poc + (long)id_clamp(oi[3], L.nc) * 64;
+    const float* pa = poa + (long)id_clamp(oi[4], L.na) * 64;
+    const float* of = row + L.optf + j * 8;
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    float* o = out + nj * ldo;
+    for (int c = lane * 4; c < q_in; c += 128) {
+        float4 v;
+        if (c < 16) v = ld4(te + c);
+        else if (c < 16 + D) v = h1 ? ld4(h1 + (c - 16)) : z;
+        else if (c < 16 + 2 * D) v = h2 ? ld4(h2 + (c - 16 - D)) : z;
+        else if (c < 16 + 2 * D + 64) v = ld4(pc + (c - 16 - 2 * D));
+        else if (c < 16 + 2 * D + 128) v = ld4(pa + (c - 80 - 2 * D));
+        else {
+            int e = c - 144 - 2 * D;                    // the obs row may be unaligned here
+            v = make_float4(of[e], of[e + 1], of[e + 2], of[e + 3]);
+        }
+        st4(o + c, v);
+    }
 }
 
 __global__ void k_q_in_bwd(float* d_temb, float* d_h, float* d_poc, float* d_poa,
                            const float* g, long ldg, const float* obs, ObsLayout L,
                            int D, int R, int q_in) {
-    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i >= (long)R * L.nopt * q_in) return;
-    int c = (int)(i % q_in);
-    long nj = i / q_in;
-    int j = (int)(nj % L.nopt), n = (int)(nj / L.nopt);
-    if (c >= 16 + 2 * D + 128) return;
-    float v = g[nj * ldg + c];
-    if (v == 0.f) return;
+    long nj = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (nj >= (long)R * L.nopt) return;
+    const int n = (int)(nj / L.nopt), j = (int)(nj - (long)n * L.nopt);
     const float* oi = obs + (long)n * L.obs + L.opti + j * 6;
-    if (c < 16) atomicAdd(&d_temb[id_clamp(oi[0], 33) * 16 + c], v);
-    else if (c < 16 + 2 * D) {
-        int which = (c - 16) >= D;
-        int p = (int)oi[1 + which];
-        if (p > 0 && p <= L.ltok)
-            atomicAdd(&d_h[((long)n * L.lseq + p) * D + (c - 16 - which * D)], v);
-    } else if (c < 16 + 2 * D + 64)
-        atomicAdd(&d_poc[(long)id_clamp(oi[3], L.nc) * 64 + (c - 16 - 2 * D)], v);
-    else atomicAdd(&d_poa[(long)id_clamp(oi[4], L.na) * 64 + (c - 80 - 2 * D)], v);
+    float* te = d_temb + id_clamp(oi[0], 33) * 16;
+    const int p1 = (int)oi[1], p2 = (int)oi[2];
+    float* h1 = (p1 <= 0 || p1 > L.ltok) ? nullptr : d_h + ((long)n * L.lseq + p1) * D;
+    float* h2 = (p2 <= 0 || p2 > L.ltok) ? nullptr : d_h + ((long)n * L.lseq + p2) * D;
+    float* pc = d_poc + (long)id_clamp(oi[3], L.nc) * 64;
+    float* pa = d_poa + (long)id_clamp(oi[4], L.na) * 64;
+    const float* gr = g + nj * ldg;
+    for (int c = lane * 4; c < 16 + 2 * D + 128; c += 128) {
+        float4 v = ld4(gr + c);
+        if (!nz4(v)) continue;
+        float* t;
+        if (c < 16) t = te + c;
+        else if (c < 16 + D) t = h1 ? h1 + (c - 16) : nullptr;
+        else if (c < 16 + 2 * D) t = h2 ? h2 + (c - 16 - D) : nullptr;
+        else if (c < 16 + 2 * D + 64) t = pc + (c - 16 - 2 * D);
+        else t = pa + (c - 80 - 2 * D);
+        if (t) red_add4(t, v);
+    }
 }
 
 // ---- score1 split: score1(cat[q, r, g, d, q*r]) = [q | q*r] Wqq^T +
 //      ([r | g | d] Wrgd^T + b) broadcast over the sample's options
 // qq = [q | q*r] (NO x 2D): the second half from the first and r = h[n, 0]
-__global__ void k_qr_fill(float* qq, int D, const float* h, int lseq, int nopt, long total) {
-    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i >= total) return;
-    long nj = i / D;
-    int c = (int)(i % D), n = (int)(nj / nopt);
+__global__ void k_qr_fill(float* qq, int D, const float* h, int lseq, int nopt, long rows) {
+    long nj = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (nj >= rows) return;
+    const int n = (int)(nj / nopt);
+    const float* r = h + (long)n * lseq * D;
     float* row = qq + nj * 2 * D;
-    row[D + c] = row[c] * h[(long)n * lseq * D + c];
+    for (int c = lane * 4; c < D; c += 128) {
+        float4 q = ld4(row + c), rr = ld4(r + c);
+        st4(row + D + c, make_float4(q.x * rr.x, q.y * rr.y, q.z * rr.z, q.w * rr.w));
+    }
 }
 // per-sample [r | g | d] (R x (D + 192)), gd = [g | d] (R x 192)
 __global__ void k_rgd_fill(float* out, const float* h, int lseq, const float* gd, int D, int R) {
@@ -581,13 +615,13 @@ __global__ void k_otok_bwd(float* d_cv, const float* g, long ldg, const float* o
 // rows 1+LSEQ.. are written by the oracle_proj GEMM (row remap)
 __global__ void k_xc_fill(float* xc, const float* h, const float* cread, int lseq,
                           int lcrit, int D, int R) {
-    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    long per = (long)(1 + lseq) * D;
-    if (i >= (long)R * per) return;
-    int n = (int)(i / per);
-    long rem = i % per;
-    int l = (int)(rem / D), d = (int)(rem % D);
-    xc[((long)n * lcrit + l) * D + d] = l == 0 ? cread[d] : h[((long)n * lseq + l - 1) * D + d];
+    long r = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);   // warp per row
+    const int lane = threadIdx.x & 31;
+    if (r >= (long)R * (1 + lseq)) return;
+    const int n = (int)(r / (1 + lseq)), l = (int)(r - (long)n * (1 + lseq));
+    const float* src = l == 0 ? cread : h + ((long)n * lseq + l - 1) * D;
+    float* dst = xc + ((long)n * lcrit + l) * D;
+    for (int c = lane * 4; c < D; c += 128) st4(dst + c, ld4(src + c));
 }
 
 // [seq[n, 0] | g]  (k_val_in, ptcg_model.cu:500-506) in f32 and optional T copy
@@ -629,17 +663,22 @@ __global__ void k_add_rows(float* dst, long seq_stride, const float* src, int R,
 // critic input grad split: row 0 -> d_creadout, rows 1..LSEQ -> d_h +=,
 // rows 1+LSEQ.. -> d_otok (T, compact) (k_xc_bwd, ptcg_model2.cu:174-187)
 template <typename T>
-__global__ void k_xc_bwd(float* d_cread, float* d_h, T* d_otok, const float* dxc, int lseq,
-                         int lcrit, int D, int R) {
-    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i >= (long)R * lcrit * D) return;
-    int d = (int)(i % D);
-    long nl = i / D;
-    int l = (int)(nl % lcrit), n = (int)(nl / lcrit);
-    float g = dxc[i];
-    if (l == 0) { if (g != 0.f) atomicAdd(&d_cread[d], g); }
-    else if (l <= lseq) d_h[((long)n * lseq + l - 1) * D + d] += g;
-    else st(&d_otok[((long)n * 56 + (l - 1 - lseq)) * D + d], g);
+__global__ void k_xc_bwd(T* d_otok, float* d_h, const float* dxc, int lseq, int lcrit, int D,
+                         int R) {
+    // rows 1..lcrit-1 of every sample, warp per row (row 0 -> d_creadout is
+    // a column sum over samples, done separately)
+    long r = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= (long)R * (lcrit - 1)) return;
+    const int n = (int)(r / (lcrit - 1)), l = 1 + (int)(r - (long)n * (lcrit - 1));
+    const float* g = dxc + ((long)n * lcrit + l) * D;
+    if (l <= lseq) {
+        float* dh = d_h + ((long)n * lseq + l - 1) * D;
+        for (int c = lane * 4; c < D; c += 128) st4(dh + c, add4(ld4(dh + c), ld4(g + c)));
+    } else {
+        T* o = d_otok + ((long)n * 56 + (l - 1 - lseq)) * D;
+        for (int c = lane * 4; c < D; c += 128) st4(o + c, ld4(g + c));
+    }
 }
 
 // trunk input grad split: row 0 -> d_readout; rows 1.. -> d_tokp (T, compact);
@@ -664,23 +703,33 @@ __global__ void k_x0_bwd(float* d_read, T* d_tokp, float* d_bc, const float* dx0
 
 __global__ void k_tok_cat_bwd(float* d_cv, float* d_zemb, float* d_oemb, const float* g,
                               long ldg, const float* obs, ObsLayout L, int R, int tok_in) {
-    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i >= (long)R * L.ltok * tok_in) return;
-    int c = (int)(i % tok_in);
-    long nl = i / tok_in;
-    int l = (int)(nl % L.ltok), n = (int)(nl / L.ltok);
-    float v = g[nl * ldg + c];
-    if (v == 0.f) return;
+    long nl = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);   // warp per token row
+    const int lane = threadIdx.x & 31;
+    if (nl >= (long)R * L.ltok) return;
+    const int n = (int)(nl / L.ltok), l = (int)(nl - (long)n * L.ltok);
     const float* ti = obs + (long)n * L.obs + L.toki + l * 5;
-    if (c < 128) atomicAdd(&d_cv[(long)id_clamp(ti[0], L.nc) * 128 + c], v);
-    else if (c < 256) {
-        int e = c - 128;
-        int t0 = (int)ti[3], t1 = (int)ti[4];
-        if (t0 > 0) atomicAdd(&d_cv[(long)(t0 >= L.nc ? L.nc - 1 : t0) * 128 + e], v);
-        if (t1 > 0) atomicAdd(&d_cv[(long)(t1 >= L.nc ? L.nc - 1 : t1) * 128 + e], v);
-    } else if (c < 256 + L.tok_f) {
-    } else if (c < 264 + L.tok_f) atomicAdd(&d_zemb[id_clamp(ti[1], 16) * 8 + (c - 256 - L.tok_f)], v);
-    else atomicAdd(&d_oemb[id_clamp(ti[2], 4) * 4 + (c - 264 - L.tok_f)], v);
+    const float* gr = g + nl * ldg;
+    float* c0 = d_cv + (long)id_clamp(ti[0], L.nc) * 128;
+    const int t0 = (int)ti[3], t1 = (int)ti[4];
+    float* ca = t0 > 0 ? d_cv + (long)(t0 >= L.nc ? L.nc - 1 : t0) * 128 : nullptr;
+    float* cb = t1 > 0 ? d_cv + (long)(t1 >= L.nc ? L.nc - 1 : t1) * 128 : nullptr;
+    const bool vec = (ldg & 3) == 0;
+    for (int c = lane * 4; c < 256; c += 128) {
+        float4 v = vec ? ld4(gr + c) : make_float4(gr[c], gr[c + 1], gr[c + 2], gr[c + 3]);
+        if (!nz4(v)) continue;
+        if (c < 128) red_add4(c0 + c, v);
+        else {
+            if (ca) red_add4(ca + (c - 128), v);
+            if (cb) red_add4(cb + (c - 128), v);
+        }
+    }
+    if (lane < 12) {                                 // zone (8) and owner (4) embeddings
+        float v = gr[256 + L.tok_f + lane];
+        if (v != 0.f) {
+            if (lane < 8) atomicAdd(&d_zemb[id_clamp(ti[1], 16) * 8 + lane], v);
+            else atomicAdd(&d_oemb[id_clamp(ti[2], 4) * 4 + (lane - 8)], v);
+        }
+    }
 }
 
 // ------------------------------------------------------------ aux losses

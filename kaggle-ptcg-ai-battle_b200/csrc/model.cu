@@ -563,12 +563,11 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     const Tab& t = M->tab;
     // --- token path
     long ldtok = rup(z.TOK_IN, 8);
-    long ntc = (long)R * z.LTOK * z.TOK_IN;
     if (dt == DT_F32)
-        ++g_ptcg_launches, k_tok_cat<float><<<cdiv(ntc, TPB), TPB, 0, s>>>((float*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
+        ++g_ptcg_launches, k_tok_cat<float><<<cdiv((long)R * z.LTOK, TPB / 32), TPB, 0, s>>>((float*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
             M->w("zone_emb").p, M->w("owner_emb").p, R, z.TOK_IN);
     else
-        ++g_ptcg_launches, k_tok_cat<bf16><<<cdiv(ntc, TPB), TPB, 0, s>>>((bf16*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
+        ++g_ptcg_launches, k_tok_cat<bf16><<<cdiv((long)R * z.LTOK, TPB / 32), TPB, 0, s>>>((bf16*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
             M->w("zone_emb").p, M->w("owner_emb").p, R, z.TOK_IN);
     ++g_ptcg_launches, k_x0_readout<<<cdiv((long)R * (z.LSEQ > D ? z.LSEQ : D), TPB), TPB, 0, s>>>(Wk.x[0], Wk.keep,
         M->w("readout").p, obs, ol, R, D);
@@ -610,7 +609,7 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     // --- option scorer
     long NO = (long)R * z.NOPT;
     long ldq = rup(z.Q_IN, 8);
-    ++g_ptcg_launches, k_q_in<float><<<cdiv(NO * z.Q_IN, TPB), TPB, 0, s>>>((float*)Wk.qin, ldq, obs, ol, Wk.h, D,
+    ++g_ptcg_launches, k_q_in<<<cdiv(NO, TPB / 32), TPB, 0, s>>>((float*)Wk.qin, ldq, obs, ol, Wk.h, D,
         M->w("opt_type_emb").p, t.poc, t.poa, R, z.Q_IN);
     a = lin_fwd(DT_F32, (int)NO, z.Q_IN, D, Wk.qin, ldq, f32w(M->w("q1_w"), z.Q_IN), Wk.q1, D, DT_F32);
     a.bias = M->w("q1_b").p; a.act = ACT_GELU; a.allow_tf32 = tf32;
@@ -624,7 +623,7 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     a = lin_fwd(DT_F32, (int)NO, D, D, Wk.q1, D, f32w(M->w("q2_w"), D), qq, 2 * D, DT_F32);
     a.bias = M->w("q2_b").p; a.allow_tf32 = tf32;
     gemm(M, a, s);
-    ++g_ptcg_launches, k_qr_fill<<<cdiv(NO * D, TPB), TPB, 0, s>>>(qq, D, Wk.h, z.LSEQ, z.NOPT, NO * D);
+    ++g_ptcg_launches, k_qr_fill<<<cdiv(NO, TPB / 32), TPB, 0, s>>>(qq, D, Wk.h, z.LSEQ, z.NOPT, NO);
     ++g_ptcg_launches, k_rgd_fill<<<cdiv((long)R * (D + 192), TPB), TPB, 0, s>>>(Wk.rgd, Wk.h, z.LSEQ, Wk.gd,
         D, R);
     W ws1 = f32w(M->w("score1_w"), z.SCORE_IN);
@@ -658,7 +657,7 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     else
         ++g_ptcg_launches, k_otok_in<bf16><<<cdiv(no, TPB), TPB, 0, s>>>((bf16*)Wk.otokin, ldo_t, Wk.ckeep, obs, ol,
             t.card_vec, Wk.keep, R);
-    ++g_ptcg_launches, k_xc_fill<<<cdiv((long)R * (1 + z.LSEQ) * D, TPB), TPB, 0, s>>>(Wk.xc[0], Wk.h,
+    ++g_ptcg_launches, k_xc_fill<<<cdiv((long)R * (1 + z.LSEQ), TPB / 32), TPB, 0, s>>>(Wk.xc[0], Wk.h,
         M->w("critic_readout").p, z.LSEQ, z.LCRIT, D, R);
     a = lin_fwd(dt, R * 56, 134, D, Wk.otokin, ldo_t, M->w("oracle_proj_w"), Wk.xc[0], D, DT_F32);
     a.bias = M->w("oracle_proj_b").p;
@@ -898,18 +897,22 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
                      M->w("oracle_v1_w").g), s);
     gemm_simt(lin_dx(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, f32w(M->w("oracle_v1_w"), z.VAL_IN),
                      Wk.dbvin, z.VAL_IN, DT_F32), s);
-    long NC_ = (long)R * z.LCRIT;
     ++g_ptcg_launches, k_val_in_bwd<<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.dx0, 1, D, Wk.dgd, Wk.dbvin, R, 0);
     if (bf) ++g_ptcg_launches, k_cast<bf16><<<cdiv((long)R * D, TPB), TPB, 0, s>>>((bf16*)Wk.dx0c, D, Wk.dx0, D, R, D);
     // ---- critic block (evaluated at its readout row)
     block_bwd_row0(M, M->blk("c0_"), Wk.cblk, Wk.ckeep, Wk, R, z.LCRIT, s);
-    long nxc = NC_ * D;
-    if (bf)
-        ++g_ptcg_launches, k_xc_bwd<bf16><<<cdiv(nxc, TPB), TPB, 0, s>>>(M->w("critic_readout").g, Wk.dh, (bf16*)Wk.dotok,
-            Wk.dx, z.LSEQ, z.LCRIT, D, R);
-    else
-        ++g_ptcg_launches, k_xc_bwd<float><<<cdiv(nxc, TPB), TPB, 0, s>>>(M->w("critic_readout").g, Wk.dh,
-            (float*)Wk.dotok, Wk.dx, z.LSEQ, z.LCRIT, D, R);
+    {   // critic input grad: row 0 -> critic_readout (column sum over samples),
+        // rows 1..LSEQ -> d_h +=, rows 1+LSEQ.. -> d_otok (compact)
+        int gpb = 64;
+        dim3 g(cdiv(D, 128), cdiv(R, gpb));
+        ++g_ptcg_launches, k_colsum_groups<<<g, 128, 0, s>>>(M->w("critic_readout").g, Wk.dx, D, R, z.LCRIT,
+                                          0, 1, D, gpb);
+        unsigned gb = cdiv((long)R * (z.LCRIT - 1), TPB / 32);
+        if (bf)
+            ++g_ptcg_launches, k_xc_bwd<bf16><<<gb, TPB, 0, s>>>((bf16*)Wk.dotok, Wk.dh, Wk.dx, z.LSEQ, z.LCRIT, D, R);
+        else
+            ++g_ptcg_launches, k_xc_bwd<float><<<gb, TPB, 0, s>>>((float*)Wk.dotok, Wk.dh, Wk.dx, z.LSEQ, z.LCRIT, D, R);
+    }
     W wo = M->w("oracle_proj_w");
     {   // oracle_proj bias grad: fp32 sum of the critic-input grad rows 1+LSEQ..
         int gpb = 64;
@@ -976,7 +979,7 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
         a.allow_tf32 = tf32;
         gemm(M, a, s);
     }
-    ++g_ptcg_launches, k_q_in_bwd<<<cdiv(NO * z.Q_IN, TPB), TPB, 0, s>>>(M->w("opt_type_emb").g, Wk.dh, t.d_poc,
+    ++g_ptcg_launches, k_q_in_bwd<<<cdiv(NO, TPB / 32), TPB, 0, s>>>(M->w("opt_type_emb").g, Wk.dh, t.d_poc,
         t.d_poa, Wk.dqin, z.Q_IN, obs, ol, D, R, z.Q_IN);
     // opt_card / opt_attack per-table-row projections -> table grads
     colsum<float>(M->w("opt_card_b").g, t.d_poc, 64, z.NC, 64, s);
@@ -1016,7 +1019,7 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     colsum<float>(M->w("token_proj_b").g, Wk.dbc, D, R, D, s);
     gemm(M, lin_dw(dt, R * z.LTOK, z.TOK_IN, D, Wk.dtokp, D, Wk.tokcat, ldtok, wt.g), s);
     gemm(M, lin_dx(dt, R * z.LTOK, z.TOK_IN, D, Wk.dtokp, D, wt, Wk.dtokcat, z.TOK_IN, DT_F32), s);
-    ++g_ptcg_launches, k_tok_cat_bwd<<<cdiv((long)R * z.LTOK * z.TOK_IN, TPB), TPB, 0, s>>>(t.d_cv, M->w("zone_emb").g,
+    ++g_ptcg_launches, k_tok_cat_bwd<<<cdiv((long)R * z.LTOK, TPB / 32), TPB, 0, s>>>(t.d_cv, M->w("zone_emb").g,
         M->w("owner_emb").g, Wk.dtokcat, z.TOK_IN, obs, ol, R, z.TOK_IN);
     colsum<float>(M->w("bcast_b").g, Wk.dbc, D, R, D, s);
     gemm_simt(lin_dw(DT_F32, R, 192, D, Wk.dbc, D, Wk.gd, 192, M->w("bcast_w").g), s);
