@@ -145,20 +145,26 @@ template <typename TC, int VEC, int MAXC>
 __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long lddxc,
                          float* dw, float* db, const float* dy, long lddy,
                          const float* x, long ldx, const float* w, const float* mean,
-                         const float* rstd, int rows, int D, int rows_per_block) {
-    extern __shared__ float sh[];               // [2][D]
+                         const float* rstd, int rows, int D, int rows_per_block,
+                         float* out_cs) {
+    // out_cs (nullable): += column sums of the resulting dx (the bias grad
+    // of the layer that produced this residual stream)
+    extern __shared__ float sh[];               // [3][D]
     float* sw = sh;
     float* sb = sh + D;
-    for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) sh[i] = 0.f;
+    float* so = sh + 2 * D;
+    for (int i = threadIdx.x; i < 3 * D; i += blockDim.x) sh[i] = 0.f;
     __syncthreads();
     int nw = blockDim.x >> 5, wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int r0 = blockIdx.x * rows_per_block;
     int r1 = min(rows, r0 + rows_per_block);
     if (VEC > 0) {
         float4 pw[VEC > 0 ? VEC : 1], pb[VEC > 0 ? VEC : 1], wv[VEC > 0 ? VEC : 1];
+        float4 po[VEC > 0 ? VEC : 1];
         #pragma unroll
         for (int c = 0; c < VEC; c++) {
             pw[c] = make_float4(0, 0, 0, 0); pb[c] = make_float4(0, 0, 0, 0);
+            po[c] = make_float4(0, 0, 0, 0);
             wv[c] = *(const float4*)(w + c * 128 + lane * 4);
         }
         for (int row = r0 + wid; row < r1; row += nw) {
@@ -198,6 +204,7 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
                 float o2 = (gv[c].z - m1 - xv[c].z * m2) * rs + av[c].z;
                 float o3 = (gv[c].w - m1 - xv[c].w * m2) * rs + av[c].w;
                 *(float4*)(dxr + i) = make_float4(o0, o1, o2, o3);
+                po[c].x += o0; po[c].y += o1; po[c].z += o2; po[c].w += o3;
                 if (dxc) {
                     if (sizeof(TC) == 4) {
                         *(float4*)((float*)dxc + (long)row * lddxc + i) = make_float4(o0, o1, o2, o3);
@@ -216,11 +223,15 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
             atomicAdd(&sw[i + 2], pw[c].z); atomicAdd(&sw[i + 3], pw[c].w);
             atomicAdd(&sb[i], pb[c].x); atomicAdd(&sb[i + 1], pb[c].y);
             atomicAdd(&sb[i + 2], pb[c].z); atomicAdd(&sb[i + 3], pb[c].w);
+            if (out_cs) {
+                atomicAdd(&so[i], po[c].x); atomicAdd(&so[i + 1], po[c].y);
+                atomicAdd(&so[i + 2], po[c].z); atomicAdd(&so[i + 3], po[c].w);
+            }
         }
     } else {
-        float pw[MAXC], pb[MAXC];
+        float pw[MAXC], pb[MAXC], po[MAXC];
         #pragma unroll
-        for (int c = 0; c < MAXC; c++) { pw[c] = 0.f; pb[c] = 0.f; }
+        for (int c = 0; c < MAXC; c++) { pw[c] = 0.f; pb[c] = 0.f; po[c] = 0.f; }
         const int nc = (D + 31) / 32;
         for (int row = r0 + wid; row < r1; row += nw) {
             const float* xr = x + (long)row * ldx;
@@ -249,6 +260,7 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
                 if (c < nc && i < D) {
                     float v = (g[c] - m1 - xh[c] * m2) * rs + acc[c];
                     dxr[i] = v;
+                    po[c] += v;
                     if (dxc) st(&dxc[(long)row * lddxc + i], v);
                 }
             }
@@ -256,13 +268,17 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
         #pragma unroll
         for (int c = 0; c < MAXC; c++) {
             int i = lane + 32 * c;
-            if (c < nc && i < D) { atomicAdd(&sw[i], pw[c]); atomicAdd(&sb[i], pb[c]); }
+            if (c < nc && i < D) {
+                atomicAdd(&sw[i], pw[c]); atomicAdd(&sb[i], pb[c]);
+                if (out_cs) atomicAdd(&so[i], po[c]);
+            }
         }
     }
     __syncthreads();
     for (int i = threadIdx.x; i < D; i += blockDim.x) {
         if (sw[i] != 0.f) atomicAdd(&dw[i], sw[i]);
         if (sb[i] != 0.f) atomicAdd(&db[i], sb[i]);
+        if (out_cs && so[i] != 0.f) atomicAdd(&out_cs[i], so[i]);
     }
 }
 

@@ -307,14 +307,15 @@ static void ln_fwd(int dt, void* y, long ldy, float* mu, float* rs, const float*
 #undef LNF
 }
 // dx (f32, ld D) = LN'(dy) (+ dx), copy to dxc (T) unless dxc == nullptr
+// out_cs (nullable): += column sums of the resulting dx
 static void ln_bwd(int dt, float* dx, int accumulate, void* dxc, float* dw, float* db,
                    const float* dy, const float* x, const float* w, const float* mu,
-                   const float* rs, int rows, int D, cudaStream_t s) {
+                   const float* rs, int rows, int D, cudaStream_t s, float* out_cs = nullptr) {
     int rpb = 64;
     unsigned g = cdiv(rows, rpb);
-    size_t sm = 2 * D * sizeof(float);
+    size_t sm = 3 * D * sizeof(float);
 #define LNB(TC, V, MC) ++g_ptcg_launches, k_ln_bwd<TC, V, MC><<<g, 256, sm, s>>>(dx, D, accumulate, \
-        (TC*)dxc, D, dw, db, dy, D, x, D, w, mu, rs, rows, D, rpb)
+        (TC*)dxc, D, dw, db, dy, D, x, D, w, mu, rs, rows, D, rpb, out_cs)
     bool f = dt == DT_F32 || dxc == nullptr;
     if (D == 256) { if (f) LNB(float, 2, 1); else LNB(bf16, 2, 1); }
     else if (D == 512) { if (f) LNB(float, 4, 1); else LNB(bf16, 4, 1); }
@@ -707,8 +708,12 @@ static void fire_hook(PtcgModel* M, const char* first, const char* last_excl, cu
     if (b > a) M->hook(M->hook_user, a, b - a, (void*)s);
 }
 
+// On entry dx holds d(x_out) and the FFN2 bias grad of this block is
+// already accumulated (by the LayerNorm backward that produced dx); the LN1
+// backward at the end adds the column sums of d(x_in) to lower_f2b, the
+// FFN2 bias grad of the block below (nullptr for the first block).
 static void block_bwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* keep, Work& Wk,
-                      int R, int L, cudaStream_t s) {
+                      int R, int L, float* lower_f2b, cudaStream_t s) {
     const Dims& z = M->z;
     const int dt = M->dt(), D = z.D, F = z.FFN;
     const int NL = R * L;
@@ -716,7 +721,6 @@ static void block_bwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
     float* dx = Wk.dx;                 // f32, holds d(x_out) on entry
     void* dxc = Wk.dxc;                // operand-dtype copy of dx
     // FFN2
-    colsum<float>(P.f2b.g, dx, D, NL, D, s);
     gemm(M, lin_dw(dt, NL, F, D, dxc, D, b.fpost, F, P.f2w.g), s);
     GemmArgs a = lin_dx(dt, NL, F, D, dxc, D, P.f2w, Wk.df, F, dt);
     a.act = ACT_GELU_BWD; a.aux = b.fpre; a.ld_aux = F; a.aux_dtype = dt;
@@ -726,10 +730,10 @@ static void block_bwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
     gemm(M, lin_dw(dt, NL, D, F, Wk.df, F, b.ln2, D, P.f1w.g), s);
     gemm(M, lin_dx(dt, NL, D, F, Wk.df, F, P.f1w, Wk.dln, D, DT_F32), s);
     // LN2: dx <- d(x_mid) = dx + LN2'(dln)
+    // (+ proj bias grad = column sums of d(x_mid))
     ln_bwd(dt, dx, 1, bf ? dxc : nullptr, P.ln2w.g, P.ln2b.g, Wk.dln, b.xm, P.ln2w.p, b.mu2,
-           b.rs2, NL, D, s);
+           b.rs2, NL, D, s, P.projb.g);
     // proj
-    colsum<float>(P.projb.g, dx, D, NL, D, s);
     gemm(M, lin_dw(dt, NL, D, D, dxc, D, b.att, D, P.projw.g), s);
     gemm(M, lin_dx(dt, NL, D, D, dxc, D, P.projw, Wk.datt, D, dt), s);
     // attention
@@ -740,7 +744,7 @@ static void block_bwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
     gemm(M, lin_dx(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, P.qkvw, Wk.dln, D, DT_F32), s);
     // LN1: dx <- d(x_in) = dx + LN1'(dln)
     ln_bwd(dt, dx, 1, bf ? dxc : nullptr, P.ln1w.g, P.ln1b.g, Wk.dln, b.x_in, P.ln1w.p, b.mu1,
-           b.rs1, NL, D, s);
+           b.rs1, NL, D, s, lower_f2b);
 }
 
 // Backward of block_fwd_row0.  On entry Wk.dx0 (f32) / Wk.dx0c (operand
@@ -764,9 +768,8 @@ static void block_bwd_row0(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t
     gemm(M, lin_dw(dt, R, D, F, Wk.df, F, b.ln2, D, P.f1w.g), s);
     gemm(M, lin_dx(dt, R, D, F, Wk.df, F, P.f1w, Wk.dln, D, DT_F32), s);
     ln_bwd(dt, dx0, 1, bf ? dx0c : nullptr, P.ln2w.g, P.ln2b.g, Wk.dln, b.xm, P.ln2w.p, b.mu2,
-           b.rs2, R, D, s);
+           b.rs2, R, D, s, P.projb.g);
     // proj
-    colsum<float>(P.projb.g, dx0, D, R, D, s);
     gemm(M, lin_dw(dt, R, D, D, dx0c, D, b.att, D, P.projw.g), s);
     gemm(M, lin_dx(dt, R, D, D, dx0c, D, P.projw, Wk.datt, D, dt), s);
     // attention: dQ at row 0, dK / dV at every key
@@ -799,9 +802,9 @@ static void tables_bwd(PtcgModel* M, cudaStream_t s) {
     // card LayerNorm (input card_in, ld 634) -> d_cardin
     {
         int rpb = 64;
-        ++g_ptcg_launches, k_ln_bwd<float, 0, 20><<<cdiv(z.NC, rpb), 256, 2 * 634 * sizeof(float), s>>>(t.d_cardin, 634, 0,
+        ++g_ptcg_launches, k_ln_bwd<float, 0, 20><<<cdiv(z.NC, rpb), 256, 3 * 634 * sizeof(float), s>>>(t.d_cardin, 634, 0,
             nullptr, 634, M->w("card_ln_w").g, M->w("card_ln_b").g, t.d_cardln, 634, t.card_in, 634,
-            M->w("card_ln_w").p, t.ln_mu, t.ln_rs, z.NC, 634, rpb);
+            M->w("card_ln_w").p, t.ln_mu, t.ln_rs, z.NC, 634, rpb, nullptr);
     }
     ++g_ptcg_launches, k_slice_add<<<cdiv((long)z.NC * 64, TPB), TPB, 0, s>>>(M->w("card_id_emb").g, t.d_cardin,
         z.NC, 64, 634, 0);
@@ -999,13 +1002,16 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
         gemm_simt(a, s);
     }
     // ---- ln_f
+    // (+ the last block's FFN2 bias grad = column sums of d(x_L))
     ln_bwd(dt, Wk.dx, 0, bf ? Wk.dxc : nullptr, M->w("lnf_w").g, M->w("lnf_b").g, Wk.dh,
-           Wk.x[z.LAYERS], M->w("lnf_w").p, Wk.muf, Wk.rsf, (int)NS, D, s);
+           Wk.x[z.LAYERS], M->w("lnf_w").p, Wk.muf, Wk.rsf, (int)NS, D, s,
+           M->w(("b" + std::to_string(z.LAYERS - 1) + "_ffn2_b").c_str()).g);
     if (last) fire_hook(M, "lnf_w", nullptr, s);
     // ---- trunk
     for (int i = z.LAYERS - 1; i >= 0; i--) {
         std::string p = "b" + std::to_string(i) + "_";
-        block_bwd(M, M->blk(p), Wk.blk[i], Wk.keep, Wk, R, z.LSEQ, s);
+        block_bwd(M, M->blk(p), Wk.blk[i], Wk.keep, Wk, R, z.LSEQ,
+                  i > 0 ? M->w(("b" + std::to_string(i - 1) + "_ffn2_b").c_str()).g : nullptr, s);
         if (last) fire_hook(M, (p + "ln1_w").c_str(),
                             i == z.LAYERS - 1 ? "lnf_w" : ("b" + std::to_string(i + 1) + "_ln1_w").c_str(), s);
     }
