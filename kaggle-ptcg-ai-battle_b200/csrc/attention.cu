@@ -185,6 +185,9 @@ __global__ void __launch_bounds__(NW * 32) k_attn_bwd(
 // ldmatrix).  Softmax runs in the exp2 domain; key blocks whose 16 keys are
 // all masked are skipped (their probabilities are exactly 0).
 constexpr int RS = 40;                      // smem row stride (elements)
+// exponentials of the max-shifted (<= 0 or -inf) log2-domain scores use the
+// ex2.approx instruction directly (ex2_approx, common.cuh); the probabilities
+// are rounded to bf16 for the P.V products right after
 
 PTCG_DEV uint32_t s_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 PTCG_DEV void ldsm4(uint32_t (&r)[4], uint32_t a) {
@@ -318,17 +321,21 @@ __global__ void __launch_bounds__(128) k_attn_fwd_mma(
             bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, 1));
             bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, 2));
             float nm0 = fmaxf(m0, bm0), nm1 = fmaxf(m1, bm1);
-            float c0 = nm0 == -INFINITY ? 1.f : exp2f(m0 - nm0);
-            float c1 = nm1 == -INFINITY ? 1.f : exp2f(m1 - nm1);
+            // rescale the running sums only when some row's max moved (the
+            // factor is exactly 1 otherwise)
+            if (__any_sync(0xffffffffu, nm0 != m0 || nm1 != m1)) {
+                float c0 = nm0 == -INFINITY ? 1.f : ex2_approx(m0 - nm0);
+                float c1 = nm1 == -INFINITY ? 1.f : ex2_approx(m1 - nm1);
+                l0 *= c0; l1 *= c1;
+                #pragma unroll
+                for (int i = 0; i < 4; i++) { o[i][0] *= c0; o[i][1] *= c0; o[i][2] *= c1; o[i][3] *= c1; }
+            }
             m0 = nm0; m1 = nm1;
-            l0 *= c0; l1 *= c1;
-            #pragma unroll
-            for (int i = 0; i < 4; i++) { o[i][0] *= c0; o[i][1] *= c0; o[i][2] *= c1; o[i][3] *= c1; }
             float p[2][4];
             #pragma unroll
             for (int nt = 0; nt < 2; nt++) {
-                p[nt][0] = exp2f(s[nt][0] - m0); p[nt][1] = exp2f(s[nt][1] - m0);
-                p[nt][2] = exp2f(s[nt][2] - m1); p[nt][3] = exp2f(s[nt][3] - m1);
+                p[nt][0] = ex2_approx(s[nt][0] - m0); p[nt][1] = ex2_approx(s[nt][1] - m0);
+                p[nt][2] = ex2_approx(s[nt][2] - m1); p[nt][3] = ex2_approx(s[nt][3] - m1);
                 l0 += p[nt][0] + p[nt][1];
                 l1 += p[nt][2] + p[nt][3];
             }
@@ -452,10 +459,10 @@ __global__ void __launch_bounds__(128) k_attn_bwd_mma(
                     int q0 = qb * 16 + nt * 8 + 2 * t;
                     float la = lse2[q0], lb = lse2[q0 + 1];
                     float da = dl[q0], dd = dl[q0 + 1];
-                    p[nt][0] = exp2f(s[nt][0] * sc + kb0 - la);
-                    p[nt][1] = exp2f(s[nt][1] * sc + kb0 - lb);
-                    p[nt][2] = exp2f(s[nt][2] * sc + kb1 - la);
-                    p[nt][3] = exp2f(s[nt][3] * sc + kb1 - lb);
+                    p[nt][0] = ex2_approx(s[nt][0] * sc + kb0 - la);
+                    p[nt][1] = ex2_approx(s[nt][1] * sc + kb0 - lb);
+                    p[nt][2] = ex2_approx(s[nt][2] * sc + kb1 - la);
+                    p[nt][3] = ex2_approx(s[nt][3] * sc + kb1 - lb);
                     ds[nt][0] = p[nt][0] * (dp[nt][0] - da);
                     ds[nt][1] = p[nt][1] * (dp[nt][1] - dd);
                     ds[nt][2] = p[nt][2] * (dp[nt][2] - da);
@@ -527,8 +534,8 @@ __global__ void __launch_bounds__(128) k_attn_bwd_mma(
             #pragma unroll
             for (int nt = 0; nt < 2; nt++) {
                 float b0 = kbias[kb * 16 + nt * 8 + 2 * t], b1 = kbias[kb * 16 + nt * 8 + 2 * t + 1];
-                float p0 = exp2f(s[nt][0] * sc + b0 - la), p1 = exp2f(s[nt][1] * sc + b1 - la);
-                float p2 = exp2f(s[nt][2] * sc + b0 - lb), p3 = exp2f(s[nt][3] * sc + b1 - lb);
+                float p0 = ex2_approx(s[nt][0] * sc + b0 - la), p1 = ex2_approx(s[nt][1] * sc + b1 - la);
+                float p2 = ex2_approx(s[nt][2] * sc + b0 - lb), p3 = ex2_approx(s[nt][3] * sc + b1 - lb);
                 ds[nt][0] = p0 * (dp[nt][0] - da);
                 ds[nt][1] = p1 * (dp[nt][1] - da);
                 ds[nt][2] = p2 * (dp[nt][2] - dd);
