@@ -504,8 +504,10 @@ __global__ void __launch_bounds__(128) k_attn_bwd_mma(
             }
         }
     }
-    // ---- phase 2: dQ, one warp per 16-query block
-    for (int qb = warp; qb < nkb; qb += 4) {
+    // ---- phase 2: dQ, one warp per 16-query block; warps take the blocks in
+    // reverse order so that the warp with an extra key block in phase 1 has
+    // one fewer query block here
+    for (int qb = 3 - warp; qb < nkb; qb += 4) {
         float dq[4][4];
         #pragma unroll
         for (int i = 0; i < 4; i++) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;

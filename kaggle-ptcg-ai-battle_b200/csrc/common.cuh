@@ -78,6 +78,34 @@ PTCG_DEV float ex2_approx(float x) {
 }
 PTCG_DEV unsigned long long splat2(float c) { return pk2(c, c); }
 
+#ifndef PTCG_GELU_SCALAR
+#define PTCG_GELU_SCALAR 0
+#endif
+#if PTCG_GELU_SCALAR
+PTCG_DEV void gelu1(float x, float& y, float& g) {
+    const float a = fminf(fabsf(x) * 0.70710678118654752f, 4.f);
+    float p = 9.721369133e-05f;
+    p = fmaf(p, a, -1.507143723e-03f);
+    p = fmaf(p, a, 1.044293307e-02f);
+    p = fmaf(p, a, -4.352428019e-02f);
+    p = fmaf(p, a, 1.251842678e-01f);
+    p = fmaf(p, a, -2.732950151e-01f);
+    p = fmaf(p, a, 4.882091582e-01f);
+    p = fmaf(p, a, -7.492768168e-01f);
+    p = fmaf(p, a, 9.996129870e-01f);
+    p = fmaf(p, a, -1.128359556e+00f);
+    p = fmaf(p, a, 9.999998212e-01f);
+    const float e = ex2_approx(x * x * -0.72134752044448170f);
+    const float h = fmaf(e * p, -0.5f, 0.5f);
+    const float cdf = 0.5f + copysignf(h, x);
+    g = fmaf(x, e * 0.3989422804014327f, cdf);
+    y = x * cdf;
+}
+PTCG_DEV void gelu2(float x0, float x1, float& y0, float& y1, float& g0, float& g1) {
+    gelu1(x0, y0, g0);
+    gelu1(x1, y1, g1);
+}
+#else
 PTCG_DEV void gelu2(float x0, float x1, float& y0, float& y1, float& g0, float& g1) {
     const unsigned long long x = pk2(x0, x1);
     const float a0 = fminf(fabsf(x0) * 0.70710678118654752f, 4.f);
@@ -104,6 +132,7 @@ PTCG_DEV void gelu2(float x0, float x1, float& y0, float& y1, float& g0, float& 
     upk2(mul2(x, cdf), y0, y1);
     upk2(g, g0, g1);
 }
+#endif
 
 // torch F.softplus (beta 1, threshold 20)
 PTCG_DEV float softplus_f(float x) { return x > 20.f ? x : log1pf(expf(x)); }

@@ -558,9 +558,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                         bulk_commit();
                     }
                 }
-                #pragma unroll
-                for (int j = 0; j < 32; j++) if (j >= nvalid || !row_ok) v[j] = 0.f;
                 if (a.colsum) {
+                    #pragma unroll
+                    for (int j = 0; j < 32; j++) if (j >= nvalid || !row_ok) v[j] = 0.f;
                     float cs = warp_colsum32(v, lane);
                     if (lane < nvalid) atomicAdd(&a.colsum[n0 + lane], cs);
                 }
