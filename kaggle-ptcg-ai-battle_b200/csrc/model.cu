@@ -285,6 +285,14 @@ static GemmArgs lin_dw(int dt, int rows, int in, int out, const void* dy, long l
     a.out = dw; a.ldo = in; a.out_dtype = DT_F32; a.accumulate = 1;
     return a;
 }
+// fp32-operand GEMM of the small per-sample / per-table layers: TF32 tensor
+// cores in bf16 mode (shapes the TMA path cannot take fall back to SIMT),
+// the exact SIMT kernel in fp32 parity mode
+static void gemm32(PtcgModel* M, GemmArgs a, cudaStream_t s) {
+    a.allow_tf32 = M->prec == PTCG_BF16;
+    gemm(M, a, s);
+}
+
 // fp32 operand view of a parameter (per-sample / table GEMMs stay fp32)
 static W f32w(const W& w, long cols) { W r = w; r.op = w.p; r.ld = cols; return r; }
 
@@ -462,14 +470,14 @@ static void tables_fwd(PtcgModel* M, cudaStream_t s) {
     ++g_ptcg_launches, k_concat_rows<<<cdiv((long)z.NA * 127, TPB), TPB, 0, s>>>(t.att_in, 127, z.NA, 127, g);
     GemmArgs a = lin_fwd(DT_F32, z.NA, 127, 64, t.att_in, 127, f32w(M->w("attack_mlp_w"), 127), t.att_tab, 64, DT_F32);
     a.bias = M->w("attack_mlp_b").p; a.act = ACT_GELU; a.out2 = t.att_pre; a.ldo2 = 64;
-    gemm_simt(a, s);
+    gemm32(M, a, s);
     g.n = 2;
     g.s[0] = {M->w("skill_id_emb").p, 48, 0, 48, 0};
     g.s[1] = {M->skill_text, 64, 0, 64, 48};
     ++g_ptcg_launches, k_concat_rows<<<cdiv((long)z.NS * 112, TPB), TPB, 0, s>>>(t.sk_in, 112, z.NS, 112, g);
     a = lin_fwd(DT_F32, z.NS, 112, 128, t.sk_in, 112, f32w(M->w("skill_mlp_w"), 112), t.sk_tab, 128, DT_F32);
     a.bias = M->w("skill_mlp_b").p; a.act = ACT_GELU; a.out2 = t.sk_pre; a.ldo2 = 128;
-    gemm_simt(a, s);
+    gemm32(M, a, s);
     // pools written straight into their card_in columns
     ++g_ptcg_launches, k_pool<<<cdiv((long)z.NC * 64, TPB), TPB, 0, s>>>(t.card_in + 250, t.card_in + 314, 634, t.a_arg,
         t.att_tab, M->card_attacks, z.NC, 4, 64);
@@ -484,17 +492,17 @@ static void tables_fwd(PtcgModel* M, cudaStream_t s) {
            M->w("card_ln_b").p, z.NC, 634, s);
     a = lin_fwd(DT_F32, z.NC, 634, 256, t.card_ln, 634, f32w(M->w("card_mlp1_w"), 634), t.h1, 256, DT_F32);
     a.bias = M->w("card_mlp1_b").p; a.act = ACT_GELU; a.out2 = t.h1pre; a.ldo2 = 256;
-    gemm_simt(a, s);
+    gemm32(M, a, s);
     a = lin_fwd(DT_F32, z.NC, 256, 128, t.h1, 256, f32w(M->w("card_mlp2_w"), 256), t.card_vec, 128, DT_F32);
     a.bias = M->w("card_mlp2_b").p;
-    gemm_simt(a, s);
+    gemm32(M, a, s);
     // option-scorer card / attack projections, per table row
     a = lin_fwd(DT_F32, z.NC, 128, 64, t.card_vec, 128, f32w(M->w("opt_card_w"), 128), t.poc, 64, DT_F32);
     a.bias = M->w("opt_card_b").p;
-    gemm_simt(a, s);
+    gemm32(M, a, s);
     a = lin_fwd(DT_F32, z.NA, 64, 64, t.att_tab, 64, f32w(M->w("opt_attack_w"), 64), t.poa, 64, DT_F32);
     a.bias = M->w("opt_attack_b").p;
-    gemm_simt(a, s);
+    gemm32(M, a, s);
 }
 
 static void block_fwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* keep, int R, int L,
@@ -576,21 +584,21 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     GemmArgs a = lin_fwd(DT_F32, R, 64, 128, obs + ol.glob, ol.obs, f32w(M->w("global1_w"), 64),
                          Wk.g1, 128, DT_F32);
     a.bias = M->w("global1_b").p; a.act = ACT_GELU; a.out2 = Wk.g1pre; a.ldo2 = 128;
-    gemm_simt(a, s);
+    gemm32(M, a, s);
     a = lin_fwd(DT_F32, R, 128, 128, Wk.g1, 128, f32w(M->w("global2_w"), 128), Wk.gd, 192, DT_F32);
     a.bias = M->w("global2_b").p;
-    gemm_simt(a, s);
+    gemm32(M, a, s);
     ++g_ptcg_launches, k_dec_in<<<cdiv((long)R * 696, TPB), TPB, 0, s>>>(Wk.decin, obs, ol, t.card_vec, t.att_tab,
         M->w("sel_type_emb").p, M->w("ctx_emb").p, R);
     a = lin_fwd(DT_F32, R, 696, 64, Wk.decin, 696, f32w(M->w("dec1_w"), 696), Wk.d1, 64, DT_F32);
     a.bias = M->w("dec1_b").p; a.act = ACT_GELU; a.out2 = Wk.d1pre; a.ldo2 = 64;
-    gemm_simt(a, s);
+    gemm32(M, a, s);
     a = lin_fwd(DT_F32, R, 64, 64, Wk.d1, 64, f32w(M->w("dec2_w"), 64), Wk.gd + 128, 192, DT_F32);
     a.bias = M->w("dec2_b").p;
-    gemm_simt(a, s);
+    gemm32(M, a, s);
     a = lin_fwd(DT_F32, R, 192, D, Wk.gd, 192, f32w(M->w("bcast_w"), 192), Wk.bc, D, DT_F32);
     a.bias = M->w("bcast_b").p;
-    gemm_simt(a, s);
+    gemm32(M, a, s);
     // token_proj + broadcast, written into trunk rows 1..LTOK
     a = lin_fwd(dt, R * z.LTOK, z.TOK_IN, D, Wk.tokcat, ldtok, M->w("token_proj_w"), Wk.x[0], D, DT_F32);
     a.bias = M->w("token_proj_b").p;
@@ -671,7 +679,7 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     a = lin_fwd(DT_F32, R, z.VAL_IN, 256, Wk.ovin, z.VAL_IN, f32w(M->w("oracle_v1_w"), z.VAL_IN),
                 Wk.ov1, 256, DT_F32);
     a.bias = M->w("oracle_v1_b").p; a.act = ACT_GELU; a.out2 = Wk.ov1pre; a.ldo2 = 256;
-    gemm_simt(a, s);
+    gemm32(M, a, s);
     // fused output [scores | value]: expand staged scores, then the value column
     ++g_ptcg_launches, k_scale_copy<<<cdiv(NO, TPB), TPB, 0, s>>>(out, z.NOPT + 1, Wk.out, z.NOPT, R, z.NOPT, 1.f);
     rowdot<float>(out + z.NOPT, z.NOPT + 1, Wk.ov1, 256, M->w("oracle_v2_w").p,
@@ -687,7 +695,7 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     a = lin_fwd(DT_F32, R, z.VAL_IN, 256, Wk.bvin, z.VAL_IN, f32w(M->w("value1_w"), z.VAL_IN),
                 Wk.bv1, 256, DT_F32);
     a.bias = M->w("value1_b").p; a.act = ACT_GELU; a.out2 = Wk.bv1pre; a.ldo2 = 256;
-    gemm_simt(a, s);
+    gemm32(M, a, s);
     rowdot<float>(Wk.blind_v, 1, Wk.bv1, 256, M->w("value2_w").p, M->w("value2_b").p, R, 256,
                   0, 0, 0, s);
     a = lin_fwd(dt, R, z.VAL_IN, z.NC, dt == DT_F32 ? (const void*)Wk.bvin : Wk.bvinc, z.VAL_IN,
@@ -789,15 +797,15 @@ static void tables_bwd(PtcgModel* M, cudaStream_t s) {
     Tab& t = M->tab;
     // card_mlp2
     colsum<float>(M->w("card_mlp2_b").g, t.d_cv, 128, z.NC, 128, s);
-    gemm_simt(lin_dw(DT_F32, z.NC, 256, 128, t.d_cv, 128, t.h1, 256, M->w("card_mlp2_w").g), s);
+    gemm32(M, lin_dw(DT_F32, z.NC, 256, 128, t.d_cv, 128, t.h1, 256, M->w("card_mlp2_w").g), s);
     GemmArgs a = lin_dx(DT_F32, z.NC, 256, 128, t.d_cv, 128, f32w(M->w("card_mlp2_w"), 256),
                         t.d_h1, 256, DT_F32);
     a.act = ACT_GELU_BWD; a.aux = t.h1pre; a.ld_aux = 256; a.aux_dtype = DT_F32;
-    gemm_simt(a, s);
+    gemm32(M, a, s);
     // card_mlp1
     colsum<float>(M->w("card_mlp1_b").g, t.d_h1, 256, z.NC, 256, s);
-    gemm_simt(lin_dw(DT_F32, z.NC, 634, 256, t.d_h1, 256, t.card_ln, 634, M->w("card_mlp1_w").g), s);
-    gemm_simt(lin_dx(DT_F32, z.NC, 634, 256, t.d_h1, 256, f32w(M->w("card_mlp1_w"), 634),
+    gemm32(M, lin_dw(DT_F32, z.NC, 634, 256, t.d_h1, 256, t.card_ln, 634, M->w("card_mlp1_w").g), s);
+    gemm32(M, lin_dx(DT_F32, z.NC, 634, 256, t.d_h1, 256, f32w(M->w("card_mlp1_w"), 634),
                      t.d_cardln, 634, DT_F32), s);
     // card LayerNorm (input card_in, ld 634) -> d_cardin
     {
@@ -815,16 +823,16 @@ static void tables_bwd(PtcgModel* M, cudaStream_t s) {
     // attack mlp
     ++g_ptcg_launches, k_gelu_bwd<<<cdiv((long)z.NA * 64, TPB), TPB, 0, s>>>(t.d_att, t.att_pre, (long)z.NA * 64);
     colsum<float>(M->w("attack_mlp_b").g, t.d_att, 64, z.NA, 64, s);
-    gemm_simt(lin_dw(DT_F32, z.NA, 127, 64, t.d_att, 64, t.att_in, 127, M->w("attack_mlp_w").g), s);
-    gemm_simt(lin_dx(DT_F32, z.NA, 127, 64, t.d_att, 64, f32w(M->w("attack_mlp_w"), 127),
+    gemm32(M, lin_dw(DT_F32, z.NA, 127, 64, t.d_att, 64, t.att_in, 127, M->w("attack_mlp_w").g), s);
+    gemm32(M, lin_dx(DT_F32, z.NA, 127, 64, t.d_att, 64, f32w(M->w("attack_mlp_w"), 127),
                      t.d_attin, 127, DT_F32), s);
     ++g_ptcg_launches, k_slice_add<<<cdiv((long)z.NA * 48, TPB), TPB, 0, s>>>(M->w("attack_id_emb").g, t.d_attin,
         z.NA, 48, 127, 0);
     // skill mlp
     ++g_ptcg_launches, k_gelu_bwd<<<cdiv((long)z.NS * 128, TPB), TPB, 0, s>>>(t.d_sk, t.sk_pre, (long)z.NS * 128);
     colsum<float>(M->w("skill_mlp_b").g, t.d_sk, 128, z.NS, 128, s);
-    gemm_simt(lin_dw(DT_F32, z.NS, 112, 128, t.d_sk, 128, t.sk_in, 112, M->w("skill_mlp_w").g), s);
-    gemm_simt(lin_dx(DT_F32, z.NS, 112, 128, t.d_sk, 128, f32w(M->w("skill_mlp_w"), 112),
+    gemm32(M, lin_dw(DT_F32, z.NS, 112, 128, t.d_sk, 128, t.sk_in, 112, M->w("skill_mlp_w").g), s);
+    gemm32(M, lin_dx(DT_F32, z.NS, 112, 128, t.d_sk, 128, f32w(M->w("skill_mlp_w"), 112),
                      t.d_skin, 112, DT_F32), s);
     ++g_ptcg_launches, k_slice_add<<<cdiv((long)z.NS * 48, TPB), TPB, 0, s>>>(M->w("skill_id_emb").g, t.d_skin,
         z.NS, 48, 112, 0);
@@ -875,13 +883,13 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
             M->w("value2_b").g, Wk.blind_v, 1, returns, 1.0f / (float)norm_rows, R, 256, rpb,
             aux_loss + 0, M->w("value1_b").g);
     }
-    gemm_simt(lin_dw(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, Wk.bvin, z.VAL_IN,
+    gemm32(M, lin_dw(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, Wk.bvin, z.VAL_IN,
                      M->w("value1_w").g), s);
     {
         GemmArgs a = lin_dx(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256,
                             f32w(M->w("value1_w"), z.VAL_IN), Wk.dbvin, z.VAL_IN, DT_F32);
         a.accumulate = 1;
-        gemm_simt(a, s);
+        gemm32(M, a, s);
     }
     ++g_ptcg_launches, k_val_in_bwd<<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.dh, z.LSEQ, D, Wk.dgd, Wk.dbvin, R, 1);
     // ---- aux: prize BCE over MY_UNSEEN tokens
@@ -896,9 +904,9 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
             M->w("oracle_v2_w").g, M->w("oracle_v2_b").g, grad + z.NOPT, z.NOPT + 1, nullptr, 0.f,
             R, 256, rpb, nullptr, M->w("oracle_v1_b").g);
     }
-    gemm_simt(lin_dw(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, Wk.ovin, z.VAL_IN,
+    gemm32(M, lin_dw(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, Wk.ovin, z.VAL_IN,
                      M->w("oracle_v1_w").g), s);
-    gemm_simt(lin_dx(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, f32w(M->w("oracle_v1_w"), z.VAL_IN),
+    gemm32(M, lin_dx(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, f32w(M->w("oracle_v1_w"), z.VAL_IN),
                      Wk.dbvin, z.VAL_IN, DT_F32), s);
     ++g_ptcg_launches, k_val_in_bwd<<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.dx0, 1, D, Wk.dgd, Wk.dbvin, R, 0);
     if (bf) ++g_ptcg_launches, k_cast<bf16><<<cdiv((long)R * D, TPB), TPB, 0, s>>>((bf16*)Wk.dx0c, D, Wk.dx0, D, R, D);
@@ -986,20 +994,20 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
         t.d_poa, Wk.dqin, z.Q_IN, obs, ol, D, R, z.Q_IN);
     // opt_card / opt_attack per-table-row projections -> table grads
     colsum<float>(M->w("opt_card_b").g, t.d_poc, 64, z.NC, 64, s);
-    gemm_simt(lin_dw(DT_F32, z.NC, 128, 64, t.d_poc, 64, t.card_vec, 128, M->w("opt_card_w").g), s);
+    gemm32(M, lin_dw(DT_F32, z.NC, 128, 64, t.d_poc, 64, t.card_vec, 128, M->w("opt_card_w").g), s);
     {
         GemmArgs a = lin_dx(DT_F32, z.NC, 128, 64, t.d_poc, 64, f32w(M->w("opt_card_w"), 128),
                             t.d_cv, 128, DT_F32);
         a.accumulate = 1;
-        gemm_simt(a, s);
+        gemm32(M, a, s);
     }
     colsum<float>(M->w("opt_attack_b").g, t.d_poa, 64, z.NA, 64, s);
-    gemm_simt(lin_dw(DT_F32, z.NA, 64, 64, t.d_poa, 64, t.att_tab, 64, M->w("opt_attack_w").g), s);
+    gemm32(M, lin_dw(DT_F32, z.NA, 64, 64, t.d_poa, 64, t.att_tab, 64, M->w("opt_attack_w").g), s);
     {
         GemmArgs a = lin_dx(DT_F32, z.NA, 64, 64, t.d_poa, 64, f32w(M->w("opt_attack_w"), 64),
                             t.d_att, 64, DT_F32);
         a.accumulate = 1;
-        gemm_simt(a, s);
+        gemm32(M, a, s);
     }
     // ---- ln_f
     // (+ the last block's FFN2 bias grad = column sums of d(x_L))
@@ -1028,38 +1036,38 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     ++g_ptcg_launches, k_tok_cat_bwd<<<cdiv((long)R * z.LTOK, TPB / 32), TPB, 0, s>>>(t.d_cv, M->w("zone_emb").g,
         M->w("owner_emb").g, Wk.dtokcat, z.TOK_IN, obs, ol, R, z.TOK_IN);
     colsum<float>(M->w("bcast_b").g, Wk.dbc, D, R, D, s);
-    gemm_simt(lin_dw(DT_F32, R, 192, D, Wk.dbc, D, Wk.gd, 192, M->w("bcast_w").g), s);
+    gemm32(M, lin_dw(DT_F32, R, 192, D, Wk.dbc, D, Wk.gd, 192, M->w("bcast_w").g), s);
     {
         GemmArgs a = lin_dx(DT_F32, R, 192, D, Wk.dbc, D, f32w(M->w("bcast_w"), 192), Wk.dgd, 192, DT_F32);
         a.accumulate = 1;
-        gemm_simt(a, s);
+        gemm32(M, a, s);
     }
     // ---- decision encoder
     colsum<float>(M->w("dec2_b").g, Wk.dgd + 128, 192, R, 64, s);
-    gemm_simt(lin_dw(DT_F32, R, 64, 64, Wk.dgd + 128, 192, Wk.d1, 64, M->w("dec2_w").g), s);
+    gemm32(M, lin_dw(DT_F32, R, 64, 64, Wk.dgd + 128, 192, Wk.d1, 64, M->w("dec2_w").g), s);
     {
         GemmArgs a = lin_dx(DT_F32, R, 64, 64, Wk.dgd + 128, 192, f32w(M->w("dec2_w"), 64), Wk.dd1,
                             64, DT_F32);
         a.act = ACT_GELU_BWD; a.aux = Wk.d1pre; a.ld_aux = 64; a.aux_dtype = DT_F32;
-        gemm_simt(a, s);
+        gemm32(M, a, s);
     }
     colsum<float>(M->w("dec1_b").g, Wk.dd1, 64, R, 64, s);
-    gemm_simt(lin_dw(DT_F32, R, 696, 64, Wk.dd1, 64, Wk.decin, 696, M->w("dec1_w").g), s);
-    gemm_simt(lin_dx(DT_F32, R, 696, 64, Wk.dd1, 64, f32w(M->w("dec1_w"), 696), Wk.ddecin, 696,
+    gemm32(M, lin_dw(DT_F32, R, 696, 64, Wk.dd1, 64, Wk.decin, 696, M->w("dec1_w").g), s);
+    gemm32(M, lin_dx(DT_F32, R, 696, 64, Wk.dd1, 64, f32w(M->w("dec1_w"), 696), Wk.ddecin, 696,
                      DT_F32), s);
     ++g_ptcg_launches, k_dec_in_bwd<<<cdiv((long)R * 696, TPB), TPB, 0, s>>>(t.d_cv, t.d_att, M->w("sel_type_emb").g,
         M->w("ctx_emb").g, Wk.ddecin, obs, ol, R);
     // ---- global encoder
     colsum<float>(M->w("global2_b").g, Wk.dgd, 192, R, 128, s);
-    gemm_simt(lin_dw(DT_F32, R, 128, 128, Wk.dgd, 192, Wk.g1, 128, M->w("global2_w").g), s);
+    gemm32(M, lin_dw(DT_F32, R, 128, 128, Wk.dgd, 192, Wk.g1, 128, M->w("global2_w").g), s);
     {
         GemmArgs a = lin_dx(DT_F32, R, 128, 128, Wk.dgd, 192, f32w(M->w("global2_w"), 128), Wk.dg1,
                             128, DT_F32);
         a.act = ACT_GELU_BWD; a.aux = Wk.g1pre; a.ld_aux = 128; a.aux_dtype = DT_F32;
-        gemm_simt(a, s);
+        gemm32(M, a, s);
     }
     colsum<float>(M->w("global1_b").g, Wk.dg1, 128, R, 128, s);
-    gemm_simt(lin_dw(DT_F32, R, 64, 128, Wk.dg1, 128, obs + ol.glob, ol.obs, M->w("global1_w").g), s);
+    gemm32(M, lin_dw(DT_F32, R, 64, 128, Wk.dg1, 128, obs + ol.glob, ol.obs, M->w("global1_w").g), s);
     if (last) fire_hook(M, "zone_emb", "b0_ln1_w", s);
     return 0;
 }
