@@ -6,8 +6,9 @@
  *
  * All device pointers are CUDA global memory on the model's device; `stream`
  * is a cudaStream_t passed as void*.  Nothing in the forward / backward /
- * loss / optimizer entry points allocates or synchronises, so a caller may
- * capture them in a CUDA graph after ptcg_reserve().
+ * loss / optimizer entry points allocates device memory or waits on the host
+ * once ptcg_reserve() has sized the workspaces (the reference's trainer
+ * replays these calls inside CUDA graphs, native/src/pufferlib.cu:771-780).
  *
  * Each declaration names the reference interface it replaces
  * (paths relative to the dipamc/kaggle-ptcg-ai-battle checkout).
@@ -286,6 +287,10 @@ int ptcg_tensor_cores(void);
  * (0 = none; the kernel that timed out returned early).  Resets the flag. */
 int ptcg_device_error(void);
 int ptcg_kernel_timer_read(PtcgModel* m, double* ms, long* launches, double* flops);
+/* Algorithmic HBM bytes of the launches timed since ptcg_kernel_timer(m, mode)
+ * (operands read once, outputs written once; diagnostic, no counterpart in
+ * the reference). */
+int ptcg_kernel_timer_bytes(PtcgModel* m, double* bytes);
 
 #ifdef __cplusplus
 }

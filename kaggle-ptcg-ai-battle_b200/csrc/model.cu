@@ -163,6 +163,7 @@ struct KTimer {
     std::vector<cudaEvent_t> ev;
     int used = 0;
     double flops = 0.0;
+    double bytes = 0.0;                 // algorithmic HBM bytes of the timed launches
     long launches = 0;
     std::vector<int> meta;              // per timed launch: M N K a_kmajor b_kmajor act engine dtype
 };
@@ -236,6 +237,21 @@ static void kt_mark(PtcgModel* M, cudaStream_t s) {
     cudaEventRecord(k.ev[k.used++], s);
 }
 
+// Algorithmic HBM bytes of one GEMM launch: each operand read once, each
+// output written once, plus the epilogue's extra operand streams (saved
+// GELU' / residual / read-back of an accumulated output).  Bias and
+// broadcast rows are negligible and left out.
+static double gemm_bytes(const GemmArgs& a) {
+    double eb = a.dtype == DT_BF16 ? 2.0 : 4.0, ob = a.out_dtype == DT_BF16 ? 2.0 : 4.0;
+    double mn = (double)a.M * a.N;
+    double b = ((double)a.M + a.N) * a.K * eb + mn * ob;
+    if (a.out2) b += mn * (a.out2_dtype == DT_BF16 ? 2.0 : 4.0);
+    if (a.aux) b += mn * (a.aux_dtype == DT_BF16 ? 2.0 : 4.0);
+    if (a.resid) b += mn * 4.0;
+    if (a.accumulate) b += mn * ob;
+    return b;
+}
+
 static void gemm(PtcgModel* M, const GemmArgs& a, cudaStream_t s) {
     bool tc_ok = (a.dtype == DT_BF16 || a.allow_tf32) && gemm_tc_supported(a);
     int cls = tc_ok ? 1 : 2;
@@ -246,6 +262,7 @@ static void gemm(PtcgModel* M, const GemmArgs& a, cudaStream_t s) {
     if (timed) {
         kt_mark(M, s);
         M->kt.flops += 2.0 * a.M * a.N * a.K;
+        M->kt.bytes += gemm_bytes(a);
         M->kt.launches++;
         int meta[8] = {a.M, a.N, a.K, a.a_kmajor, a.b_kmajor, a.act, cls, a.dtype};
         M->kt.meta.insert(M->kt.meta.end(), meta, meta + 8);
@@ -1719,7 +1736,7 @@ int ptcg_gemm(int M, int N, int K, const void* A, long lda, int a_kmajor, const 
 
 int ptcg_kernel_timer(PtcgModel* M, int mode) {
     REQ(M && mode >= 0 && mode <= 3, PTCG_EINVAL, "bad arguments");
-    M->kt.mode = mode; M->kt.used = 0; M->kt.flops = 0; M->kt.launches = 0;
+    M->kt.mode = mode; M->kt.used = 0; M->kt.flops = 0; M->kt.bytes = 0; M->kt.launches = 0;
     M->kt.meta.clear();
     return PTCG_OK;
 }
@@ -1748,6 +1765,12 @@ int ptcg_kernel_timer_read(PtcgModel* M, double* ms, long* launches, double* flo
         t += e;
     }
     *ms = t; *launches = M->kt.launches; *flops = M->kt.flops;
+    return PTCG_OK;
+}
+
+int ptcg_kernel_timer_bytes(PtcgModel* M, double* bytes) {
+    REQ(M && bytes, PTCG_EINVAL, "null argument");
+    *bytes = M->kt.bytes;
     return PTCG_OK;
 }
 

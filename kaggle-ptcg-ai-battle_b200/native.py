@@ -76,6 +76,7 @@ _SIGS = {
     "ptcg_device_error": (I, []),
     "ptcg_gemm": (I, [I, I, I, P, L, I, P, L, I, I, P, L, I, I, P]),
     "ptcg_gemm_ex": (I, [I, I, I, P, L, I, P, L, I, I, P, L, I, P, I, P, L, P, L, P, I, I, P]),
+    "ptcg_kernel_timer_bytes": (I, [P, C.POINTER(C.c_double)]),
     "ptcg_kernel_timer_read": (I, [P, C.POINTER(C.c_double), C.POINTER(C.c_long),
                                    C.POINTER(C.c_double)]),
 }

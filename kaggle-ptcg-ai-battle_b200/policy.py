@@ -267,6 +267,12 @@ class PTCGPolicy:
         check(self.lib.ptcg_kernel_timer_read(self.h, C.byref(ms), C.byref(n), C.byref(fl)))
         return ms.value, n.value, fl.value
 
+    def kernel_timer_bytes(self):
+        """Algorithmic HBM bytes of the launches timed since kernel_timer(mode)."""
+        b = C.c_double()
+        check(self.lib.ptcg_kernel_timer_bytes(self.h, C.byref(b)))
+        return b.value
+
     def kernel_timer_entries(self, max_entries=100000):
         """[(ms, M, N, K, a_kmajor, b_kmajor, act, engine, dtype)] of the timed launches."""
         ms = np.zeros(max_entries, np.float32)
