@@ -17,6 +17,9 @@ typedef __nv_bfloat16 bf16;
 #ifndef PTCG_BIAS_SMEM
 #define PTCG_BIAS_SMEM 1        // stage bias vectors in shared memory
 #endif
+#ifndef PTCG_AUX_TMA
+#define PTCG_AUX_TMA 1          // prefetch the saved GELU' operand by TMA
+#endif
 
 #define PTCG_DEV __device__ __forceinline__
 

@@ -70,6 +70,8 @@ struct TcParams {
     uint32_t tmem_cols, acc_stride;
     int tma_out;             // outputs leave through smem staging + TMA stores
     int bias_smem;           // columns of the bias staged in shared memory (0: read from global)
+    int aux_tma;             // the GELU' operand arrives by TMA into two smem slots
+    uint32_t aux_bytes;      // bytes of one slot: BM rows x bn bf16, as bn/32 boxes of 8 KB
     GemmArgs ep;
 };
 
@@ -278,7 +280,7 @@ template <int EB>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
           const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_c2,
-          const __grid_constant__ TcParams P) {
+          const __grid_constant__ CUtensorMap map_aux, const __grid_constant__ TcParams P) {
     constexpr int BK = 128 / EB;            // K elements per 128-byte row
     constexpr int ATOM = 128 / EB;          // MN elements per MN-major box
     constexpr int KI = 32 / EB;             // K elements per MMA instruction
@@ -290,26 +292,33 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int S = P.stages;
-    uint8_t* staging = smem + (size_t)S * P.stage_bytes;          // NUM_EPI x 4 KB
-    uint64_t* bars = (uint64_t*)(staging + (P.tma_out ? NUM_EPI * STAGE_W : 0));
-    // bars: full[S], empty[S], tfull[2], tempty[2], drain[1]
-    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * S + 5);
+    uint8_t* staging = smem + (size_t)S * P.stage_bytes;          // NUM_EPI x STAGE_W
+    uint8_t* auxbuf = staging + (P.tma_out ? NUM_EPI * STAGE_W : 0); // 2 x aux_bytes
+    uint64_t* bars = (uint64_t*)(auxbuf + (P.aux_tma ? 2 * P.aux_bytes : 0));
+    // bars: full[S], empty[S], tfull[2], tempty[2], drain[1], afull[2], aempty[2]
+    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * S + 9);
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
     int* n_issued = (int*)(tmem_slot + 2);     // ring slots filled by TMA
     int* n_consumed = (int*)(tmem_slot + 3);   // ring slots read by the MMA warp
+    int* n_aux_issued = (int*)(tmem_slot + 4); // aux tiles requested by the producer
+    int* n_aux_done = (int*)(tmem_slot + 5);   // aux tiles the epilogue has waited for
     float* sbias = (float*)(((uintptr_t)(tmem_slot + 8) + 15) & ~(uintptr_t)15);   // [P.bias_smem]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
     const uint32_t tfull0 = smem_u32(bars + 2 * S), tempty0 = smem_u32(bars + 2 * S + 2);
     const uint32_t drain = smem_u32(bars + 2 * S + 4);
+    const uint32_t afull0 = smem_u32(bars + 2 * S + 5), aempty0 = smem_u32(bars + 2 * S + 7);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; i++) { mbar_init(full0 + 8 * i, 1); mbar_init(empty0 + 8 * i, 1); }
         for (int i = 0; i < 2; i++) { mbar_init(tfull0 + 8 * i, 1); mbar_init(tempty0 + 8 * i, NUM_EPI); }
         mbar_init(drain, 1);
+        for (int i = 0; i < 2; i++) { mbar_init(afull0 + 8 * i, 1); mbar_init(aempty0 + 8 * i, NUM_EPI); }
         *abort_flag = 0;
         *n_issued = 0;
         *n_consumed = 0;
+        *n_aux_issued = 0;
+        *n_aux_done = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -333,12 +342,28 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             uint32_t phase = 0;
             bool ok = true;
             long long w_empty = 0;
-            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            int plocal = 0;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, plocal++) {
                 int split = t % P.splits;
                 int mn = t / P.splits;
                 int mt = mn / P.n_tiles, nt = mn % P.n_tiles;
                 int kb0 = split * P.kb_per_split;
                 int kb1 = min(P.kb_total, kb0 + P.kb_per_split);
+                if (P.aux_tma) {
+                    // this tile's GELU' block into slot plocal & 1 once the
+                    // epilogue has finished the tile two back
+                    int slot = plocal & 1;
+                    if (!mbar_wait(aempty0 + 8 * slot, ((plocal >> 1) & 1) ^ 1, abort_flag, 5, &w_empty)) {
+                        ok = false;
+                        break;
+                    }
+                    uint32_t fb = afull0 + 8 * slot;
+                    mbar_expect_tx(fb, P.aux_bytes);
+                    uint32_t dst = smem_u32(auxbuf + (size_t)slot * P.aux_bytes);
+                    for (int c = 0; c < P.bn / 32; c++)
+                        tma_load_2d(dst + c * 8192, &map_aux, fb, nt * P.bn + 32 * c, mt * BM);
+                    (*n_aux_issued)++;
+                }
                 for (int kb = kb0; kb < kb1; kb++) {
                     if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, 1, &w_empty)) { ok = false; break; }
                     uint32_t fb = full0 + 8 * stage;
@@ -429,6 +454,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             int buf = local & 1;
             uint32_t tph = (local >> 1) & 1;
             if (!mbar_wait(tfull0 + 8 * buf, tph, abort_flag, 4, &w_tfull)) break;
+            if (P.aux_tma) {
+                if (!mbar_wait(afull0 + 8 * buf, tph, abort_flag, 6, &w_tfull)) break;
+                if (warp == 2 && lane == 0) *n_aux_done = local + 1;
+            }
             long long tb = clock64();
             fence_after();
             const int m = mt * BM + row_in_tile;
@@ -526,7 +555,23 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                         }
                     }
                 } else if (a.act == ACT_GELU_BWD) {
-                    load32(t, a.aux, (long)m * a.ld_aux + n0, a.aux_dtype, nvalid);
+                    if (P.aux_tma) {
+                        // row row_in_tile of box c0 / 32 (64-byte rows, 64-byte swizzle)
+                        const uint8_t* ab = auxbuf + (size_t)buf * P.aux_bytes + (c0 >> 5) * 8192 +
+                                            row_in_tile * 64;
+                        #pragma unroll
+                        for (int g = 0; g < 4; g++) {
+                            uint4 q = *(const uint4*)(ab + ((g ^ ((row_in_tile >> 1) & 3)) << 4));
+                            const __nv_bfloat162* h2 = (const __nv_bfloat162*)&q;
+                            #pragma unroll
+                            for (int k = 0; k < 4; k++) {
+                                float2 f = __bfloat1622float2(h2[k]);
+                                t[8 * g + 2 * k] = f.x; t[8 * g + 2 * k + 1] = f.y;
+                            }
+                        }
+                    } else {
+                        load32(t, a.aux, (long)m * a.ld_aux + n0, a.aux_dtype, nvalid);
+                    }
                     #pragma unroll
                     for (int j = 0; j < 32; j++) v[j] *= t[j];
                 }
@@ -568,7 +613,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             (void)split;
             fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
+            if (lane == 0) {
+                mbar_arrive(tempty0 + 8 * buf);
+                if (P.aux_tma) mbar_arrive(aempty0 + 8 * buf);
+            }
             busy += clock64() - tb;
         }
         if (P.tma_out && lane == 0) bulk_wait_all();
@@ -588,6 +636,14 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
         for (int i = *n_consumed; i < *n_issued; i++) {
             long long t0 = clock64();
             while (!mbar_try(full0 + 8 * (i % S), (uint32_t)((i / S) & 1)) &&
+                   clock64() - t0 < WAIT_BUDGET) {}
+        }
+    }
+    if (threadIdx.x == 0 && *n_aux_done < *n_aux_issued) {
+        // the same for GELU' tiles requested but never waited for
+        for (int i = *n_aux_done; i < *n_aux_issued; i++) {
+            long long t0 = clock64();
+            while (!mbar_try(afull0 + 8 * (i & 1), (uint32_t)((i >> 1) & 1)) &&
                    clock64() - t0 < WAIT_BUDGET) {}
         }
     }
@@ -678,8 +734,21 @@ bool make_map_eb(CUtensorMap* m, const void* ptr, long inner, long outer, long l
 struct TcPlan {
     TcParams P;
     int eb;
-    CUtensorMap ma, mb, mc, mc2;
+    CUtensorMap ma, mb, mc, mc2, mx;
 };
+
+// GELU' operand map for the TMA prefetch: box {32 columns, 128 rows} bf16,
+// 64-byte rows in the 64-byte swizzle
+bool make_aux_map(CUtensorMap* m, const void* ptr, long n, long rows, long ld) {
+    cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {32, (cuuint32_t)BM};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                          box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
 
 // output map for TMA stores: box {32 columns, 32 rows}
 bool make_out_map(CUtensorMap* m, void* ptr, long n, long rows, long ld, int dt) {
@@ -711,10 +780,16 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     TcParams& P = pl.P;
     P.M = a.M; P.N = a.N; P.K = a.K;
     P.a_mn = !a.a_kmajor; P.b_mn = !a.b_kmajor;
-    int ntl = (a.N + 255) / 256;
+    // the GELU' multiply reads its bf16 operand by TMA prefetch (two smem
+    // slots of BM x bn): tiles of at most 128 columns leave room for them
+    const bool aux_tma = PTCG_AUX_TMA && a.act == ACT_GELU_BWD && a.aux && a.aux_dtype == DT_BF16 &&
+                         !((uintptr_t)a.aux & 15) && (a.ld_aux * 2) % 16 == 0 && a.remap_group == 0;
+    const int bn_max = aux_tma ? 128 : 256;
+    int ntl = (a.N + bn_max - 1) / bn_max;
     int bn = ((a.N + ntl - 1) / ntl + 15) / 16 * 16;
     if (P.b_mn) bn = (bn + ATOM - 1) / ATOM * ATOM;
-    if (bn > 256) bn = 256;
+    if (bn > bn_max) bn = bn_max;
+    if (aux_tma && bn % 32) bn = (bn + 31) / 32 * 32;
     P.bn = bn;
     P.b_rows = bn;
     P.m_tiles = (a.M + BM - 1) / BM;
@@ -744,7 +819,10 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
                 (!a.out2 || (a.act == ACT_GELU && a.out2_dtype == DT_BF16 && a.out_dtype == DT_BF16 &&
                              !((uintptr_t)a.out2 & 15) && (a.ldo2 * 2) % 16 == 0));
     P.bias_smem = (PTCG_BIAS_SMEM && a.bias && a.N <= BIAS_SMEM_MAX) ? a.N : 0;
-    int budget = 232448 - 1024 - 512 - (P.tma_out ? NUM_EPI * STAGE_W : 0) - P.bias_smem * 4;
+    P.aux_tma = aux_tma && P.splits == 1;
+    P.aux_bytes = P.aux_tma ? (uint32_t)(bn / 32) * 8192u : 0u;
+    int budget = 232448 - 1024 - 512 - (P.tma_out ? NUM_EPI * STAGE_W : 0) - P.bias_smem * 4 -
+                 2 * (int)P.aux_bytes;
     P.stages = budget / P.stage_bytes;
     if (P.stages > 6) P.stages = 6;
     if (P.stages < 2) return false;
@@ -764,7 +842,8 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     if (P.b_mn) ok = make_map_eb(&pl.mb, a.B, a.N, a.K, a.ldb, ATOM, BK, eb, true);
     else ok = make_map_eb(&pl.mb, a.B, a.K, a.N, a.ldb, BK, bn, eb, false);
     if (!ok) return false;
-    pl.mc = pl.ma; pl.mc2 = pl.ma;
+    pl.mc = pl.ma; pl.mc2 = pl.ma; pl.mx = pl.ma;
+    if (P.aux_tma && !make_aux_map(&pl.mx, a.aux, a.N, a.M, a.ld_aux)) return false;
     if (P.tma_out) {
         if (!make_out_map(&pl.mc, a.out, a.N, a.M, a.ldo, a.out_dtype)) return false;
         if (a.out2 && !make_out_map(&pl.mc2, a.out2, a.N, a.M, a.ldo2, DT_BF16)) return false;
@@ -775,15 +854,15 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
 void launch_tc(const TcPlan& pl, cudaStream_t s) {
     const TcParams& P = pl.P;
     size_t smem = 1024 + (size_t)P.stages * P.stage_bytes + (P.tma_out ? NUM_EPI * STAGE_W : 0) +
-                  (2 * P.stages + 5) * 8 + 48 + (size_t)P.bias_smem * 4;
+                  2 * (size_t)P.aux_bytes + (2 * P.stages + 9) * 8 + 48 + (size_t)P.bias_smem * 4;
     int total = P.m_tiles * P.n_tiles * P.splits;
     int grid = total < g_sms ? total : g_sms;
     if (pl.eb == 2) {
         cudaFuncSetAttribute(k_gemm_tc<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        ++g_ptcg_launches, k_gemm_tc<2><<<grid, NUM_THREADS, smem, s>>>(pl.ma, pl.mb, pl.mc, pl.mc2, P);
+        ++g_ptcg_launches, k_gemm_tc<2><<<grid, NUM_THREADS, smem, s>>>(pl.ma, pl.mb, pl.mc, pl.mc2, pl.mx, P);
     } else {
         cudaFuncSetAttribute(k_gemm_tc<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        ++g_ptcg_launches, k_gemm_tc<4><<<grid, NUM_THREADS, smem, s>>>(pl.ma, pl.mb, pl.mc, pl.mc2, P);
+        ++g_ptcg_launches, k_gemm_tc<4><<<grid, NUM_THREADS, smem, s>>>(pl.ma, pl.mb, pl.mc, pl.mc2, pl.mx, P);
     }
 }
 
