@@ -141,9 +141,19 @@ __global__ void k_ln_fwd(TO* y, long ldy, float* mean, float* rstd, const float*
 // global memory once per block.  VEC > 0: D = 128 * VEC, float4 access (lane
 // owns 4 consecutive columns of each 128-column chunk); VEC == 0: generic D
 // (<= 32 * MAXC) with scalar access.
-template <typename TC, int VEC, int MAXC>
+// four consecutive values of a float or bf16 row as a float4
+PTCG_DEV float4 ld4any(const float* p) { return *reinterpret_cast<const float4*>(p); }
+PTCG_DEV float4 ld4any(const bf16* p) {
+    uint2 u = *reinterpret_cast<const uint2*>(p);
+    float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// dy is float or bf16 (TY); statistics, dx and the parameter grads are fp32
+template <typename TC, int VEC, int MAXC, typename TY = float>
 __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long lddxc,
-                         float* dw, float* db, const float* dy, long lddy,
+                         float* dw, float* db, const TY* dy, long lddy,
                          const float* x, long ldx, const float* w, const float* mean,
                          const float* rstd, int rows, int D, int rows_per_block,
                          float* out_cs) {
@@ -169,14 +179,14 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
         }
         for (int row = r0 + wid; row < r1; row += nw) {
             const float* xr = x + (long)row * ldx;
-            const float* dyr = dy + (long)row * lddy;
+            const TY* dyr = dy + (long)row * lddy;
             float* dxr = dx + (long)row * lddx;
             float4 xv[VEC > 0 ? VEC : 1], gv[VEC > 0 ? VEC : 1], av[VEC > 0 ? VEC : 1];
             #pragma unroll
             for (int c = 0; c < VEC; c++) {
                 int i = c * 128 + lane * 4;
                 xv[c] = *(const float4*)(xr + i);
-                gv[c] = *(const float4*)(dyr + i);
+                gv[c] = ld4any(dyr + i);
                 av[c] = accumulate ? *(const float4*)(dxr + i) : make_float4(0, 0, 0, 0);
             }
             float mu = mean[row], rs = rstd[row];
@@ -235,7 +245,7 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
         const int nc = (D + 31) / 32;
         for (int row = r0 + wid; row < r1; row += nw) {
             const float* xr = x + (long)row * ldx;
-            const float* dyr = dy + (long)row * lddy;
+            const TY* dyr = dy + (long)row * lddy;
             float* dxr = dx + (long)row * lddx;
             float mu = mean[row], rs = rstd[row];
             float xh[MAXC], g[MAXC], acc[MAXC];
@@ -245,7 +255,7 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
                 int i = lane + 32 * c;
                 if (c < nc && i < D) {
                     xh[c] = (xr[i] - mu) * rs;
-                    float dyv = dyr[i];
+                    float dyv = to_f<TY>(dyr[i]);
                     acc[c] = accumulate ? dxr[i] : 0.f;
                     g[c] = dyv * w[i];
                     s1 += g[c]; s2 += g[c] * xh[c];

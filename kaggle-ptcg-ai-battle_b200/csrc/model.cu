@@ -332,21 +332,25 @@ static void ln_fwd(int dt, void* y, long ldy, float* mu, float* rs, const float*
 #undef LNF
 }
 // dx (f32, ld D) = LN'(dy) (+ dx), copy to dxc (T) unless dxc == nullptr
-// out_cs (nullable): += column sums of the resulting dx
+// out_cs (nullable): += column sums of the resulting dx.  dy is fp32, or in
+// the operand dtype when dy_dt == DT_BF16 (the output of a dX GEMM)
 static void ln_bwd(int dt, float* dx, int accumulate, void* dxc, float* dw, float* db,
-                   const float* dy, const float* x, const float* w, const float* mu,
-                   const float* rs, int rows, int D, cudaStream_t s, float* out_cs = nullptr) {
+                   const void* dy, const float* x, const float* w, const float* mu,
+                   const float* rs, int rows, int D, cudaStream_t s, float* out_cs = nullptr,
+                   int dy_dt = DT_F32) {
     int rpb = 64;
     unsigned g = cdiv(rows, rpb);
     size_t sm = 3 * D * sizeof(float);
-#define LNB(TC, V, MC) ++g_ptcg_launches, k_ln_bwd<TC, V, MC><<<g, 256, sm, s>>>(dx, D, accumulate, \
-        (TC*)dxc, D, dw, db, dy, D, x, D, w, mu, rs, rows, D, rpb, out_cs)
+#define LNB(TC, V, MC, TY) ++g_ptcg_launches, k_ln_bwd<TC, V, MC, TY><<<g, 256, sm, s>>>(dx, D, \
+        accumulate, (TC*)dxc, D, dw, db, (const TY*)dy, D, x, D, w, mu, rs, rows, D, rpb, out_cs)
+#define LNB2(TC, V, MC) do { if (dy_dt == DT_BF16) LNB(TC, V, MC, bf16); else LNB(TC, V, MC, float); } while (0)
     bool f = dt == DT_F32 || dxc == nullptr;
-    if (D == 256) { if (f) LNB(float, 2, 1); else LNB(bf16, 2, 1); }
-    else if (D == 512) { if (f) LNB(float, 4, 1); else LNB(bf16, 4, 1); }
-    else if (D <= 256) { if (f) LNB(float, 0, 8); else LNB(bf16, 0, 8); }
-    else if (D <= 512) { if (f) LNB(float, 0, 16); else LNB(bf16, 0, 16); }
-    else { if (f) LNB(float, 0, 32); else LNB(bf16, 0, 32); }
+    if (D == 256) { if (f) LNB2(float, 2, 1); else LNB2(bf16, 2, 1); }
+    else if (D == 512) { if (f) LNB2(float, 4, 1); else LNB2(bf16, 4, 1); }
+    else if (D <= 256) { if (f) LNB2(float, 0, 8); else LNB2(bf16, 0, 8); }
+    else if (D <= 512) { if (f) LNB2(float, 0, 16); else LNB2(bf16, 0, 16); }
+    else { if (f) LNB2(float, 0, 32); else LNB2(bf16, 0, 32); }
+#undef LNB2
 #undef LNB
 }
 
@@ -753,11 +757,13 @@ static void block_bwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
     gemm(M, a, s);
     // FFN1
     gemm(M, lin_dw(dt, NL, D, F, Wk.df, F, b.ln2, D, P.f1w.g), s);
-    gemm(M, lin_dx(dt, NL, D, F, Wk.df, F, P.f1w, Wk.dln, D, DT_F32), s);
+    // d(LN2 output) in the operand dtype (bf16 mode: half the bytes of the
+    // GEMM's output and of the LayerNorm backward's input)
+    gemm(M, lin_dx(dt, NL, D, F, Wk.df, F, P.f1w, Wk.dln, D, dt), s);
     // LN2: dx <- d(x_mid) = dx + LN2'(dln)
     // (+ proj bias grad = column sums of d(x_mid))
     ln_bwd(dt, dx, 1, bf ? dxc : nullptr, P.ln2w.g, P.ln2b.g, Wk.dln, b.xm, P.ln2w.p, b.mu2,
-           b.rs2, NL, D, s, P.projb.g);
+           b.rs2, NL, D, s, P.projb.g, dt);
     // proj
     gemm(M, lin_dw(dt, NL, D, D, dxc, D, b.att, D, P.projw.g), s);
     gemm(M, lin_dx(dt, NL, D, D, dxc, D, P.projw, Wk.datt, D, dt), s);
@@ -766,10 +772,10 @@ static void block_bwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
              R, L, z.H, s);
     // QKV
     gemm(M, lin_dw(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, b.ln1, D, P.qkvw.g), s);
-    gemm(M, lin_dx(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, P.qkvw, Wk.dln, D, DT_F32), s);
+    gemm(M, lin_dx(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, P.qkvw, Wk.dln, D, dt), s);
     // LN1: dx <- d(x_in) = dx + LN1'(dln)
     ln_bwd(dt, dx, 1, bf ? dxc : nullptr, P.ln1w.g, P.ln1b.g, Wk.dln, b.x_in, P.ln1w.p, b.mu1,
-           b.rs1, NL, D, s, lower_f2b);
+           b.rs1, NL, D, s, lower_f2b, dt);
 }
 
 // Backward of block_fwd_row0.  On entry Wk.dx0 (f32) / Wk.dx0c (operand
@@ -802,10 +808,10 @@ static void block_bwd_row0(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t
                   R, L, z.H, s);
     // QKV over every row
     gemm(M, lin_dw(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, b.ln1, D, P.qkvw.g), s);
-    gemm(M, lin_dx(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, P.qkvw, Wk.dln, D, DT_F32), s);
+    gemm(M, lin_dx(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, P.qkvw, Wk.dln, D, dt), s);
     // d(x_in) = LN1'(dln) + the residual grad at row 0
     ln_bwd(dt, Wk.dx, 0, nullptr, P.ln1w.g, P.ln1b.g, Wk.dln, b.x_in, P.ln1w.p, b.mu1, b.rs1,
-           NL, D, s);
+           NL, D, s, nullptr, dt);
     ++g_ptcg_launches, k_add_rows<<<cdiv((long)R * D, TPB), TPB, 0, s>>>(Wk.dx, (long)L * D, dx0, R, D);
 }
 
