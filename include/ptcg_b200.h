@@ -169,6 +169,35 @@ int ptcg_ppo_loss_noalloc(const float* dec_out, int nopt, const float* mask,
 int ptcg_adam_step(PtcgModel* m, float lr, float beta1, float beta2, float eps,
                    float max_norm, const float* gate, float* stats, void* stream);
 
+/* Prioritised segment replay over (B, T) advantages: w_b = (sum_t |A_bt|)^alpha
+ * (0 when not finite), probs = (w + 1e-6) / (sum w + 1e-6), cdf = running sum
+ * in index order, idx[i] = first b with cdf[b] >= uniforms[i] (clamped to
+ * B - 1), mb_prio[i] = (total_agents * probs[idx[i]])^(-beta).  Replaces
+ * prio_replay_cuda (native/src/pufferlib.cu:1451-1591); the n_sel uniforms in
+ * [0, 1) come from the caller (the reference draws them from curand Philox).
+ * probs and cdf are B-float device scratch (probs is also an output). */
+int ptcg_prio_replay(const float* advantages, int B, int T, float alpha, float beta,
+                     int total_agents, int n_sel, const float* uniforms, int* idx,
+                     float* mb_prio, float* probs, float* cdf, void* stream);
+
+/* Gather the selected segments into the minibatch buffers: rows of the
+ * (B, T, ...) rollout arrays at idx -> (n_sel, T, ...); mb_returns = values +
+ * advantages of the selected rows.  mask (B, T, nopt) and mb_mask are
+ * optional (both NULL).  Replaces select_copy (native/src/pufferlib.cu:1777-1826)
+ * for the observation / action / logprob / value / advantage / mask channels
+ * (mb_prio comes from ptcg_prio_replay). */
+int ptcg_select_copy(const int* idx, int n_sel, int T, long obs_size, int nopt,
+                     const float* obs, const float* actions, const float* logprobs,
+                     const float* values, const float* advantages, const float* mask,
+                     float* mb_obs, float* mb_actions, float* mb_logprobs, float* mb_values,
+                     float* mb_advantages, float* mb_returns, float* mb_mask, void* stream);
+
+/* dst row idx[i] <- src row i (rows of row_floats floats): writes the new
+ * ratio / value of the trained segments back into the rollout buffers.
+ * Replaces index_copy (native/src/pufferlib.cu:2147-2160). */
+int ptcg_index_copy(float* dst, const int* idx, const float* src, int n, long row_floats,
+                    void* stream);
+
 /* Masked inverse-CDF sampling of the option scores + logprob + value copy.
  * Replaces sample_logits (native/src/pufferlib.cu:584-718); uniforms (n)
  * are supplied by the caller instead of a curand Philox state.  Masked

@@ -1228,3 +1228,89 @@ __global__ void k_checksum(unsigned int* out, const float* p, long n) {
     }
     atomicAdd((unsigned long long*)out, s1 ^ (s2 << 1));
 }
+
+// ------------------------------------------------- prioritised replay
+// (prio_replay_cuda, native/src/pufferlib.cu:1451-1591)
+// w[b] = (sum_t |adv[b, t]|)^alpha (0 when not finite); one warp per segment,
+// lane-strided partial sums then a shuffle-down tree, as the reference does
+__global__ void k_prio_rowsum(float* w, const float* adv, int T, float alpha) {
+    int b = blockIdx.x, lane = threadIdx.x;
+    float s = 0.f;
+    for (int t = lane; t < T; t += 32) s += fabsf(adv[(long)b * T + t]);
+    for (int o = 16; o >= 1; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o);
+    if (lane == 0) {
+        float p = powf(s, alpha);
+        w[b] = (isnan(p) || isinf(p)) ? 0.f : p;
+    }
+}
+// probs = (w + eps) / (sum w + eps), eps = 1e-6 (one block)
+__global__ void k_prio_normalize(float* w, int B) {
+    __shared__ float sh[32];
+    __shared__ float total;
+    float s = 0.f;
+    for (int i = threadIdx.x; i < B; i += blockDim.x) s += w[i];
+    for (int o = 16; o >= 1; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
+        for (int o = 16; o >= 1; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+        if (threadIdx.x == 0) total = v + 1e-6f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < B; i += blockDim.x) w[i] = (w[i] + 1e-6f) / total;
+}
+// inclusive running sum in index order (fp32, sequential like the reference)
+__global__ void k_prio_cdf(float* cdf, const float* probs, int B) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        float c = 0.f;
+        for (int i = 0; i < B; i++) { c += probs[i]; cdf[i] = c; }
+    }
+}
+// idx[i] = first b with cdf[b] >= u[i] (clamped to B-1);
+// mb_prio[i] = (total_agents * probs[idx[i]])^(-beta)
+__global__ void k_prio_sample(int* idx, float* mb_prio, const float* cdf, const float* probs,
+                              const float* u, int B, int n, int total_agents, float beta) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float x = u[i];
+    int lo = 0, hi = B - 1;
+    while (lo < hi) {
+        int mid = (lo + hi) / 2;
+        if (cdf[mid] < x) lo = mid + 1;
+        else hi = mid;
+    }
+    idx[i] = lo;
+    mb_prio[i] = powf(probs[lo] * (float)total_agents, -beta);
+}
+
+// dst row i <- src row idx[i] (rows of row_floats, 16-byte aligned when
+// row_floats % 4 == 0); gridDim.y = rows
+__global__ void k_gather_rows(float* dst, const float* src, const int* idx, long row_floats) {
+    long i = blockIdx.y;
+    const float* s = src + (long)idx[i] * row_floats;
+    float* d = dst + i * row_floats;
+    if ((row_floats & 3) == 0) {
+        for (long c = (blockIdx.x * (long)blockDim.x + threadIdx.x) * 4; c < row_floats;
+             c += (long)gridDim.x * blockDim.x * 4)
+            st4(d + c, ld4(s + c));
+    } else {
+        for (long c = blockIdx.x * (long)blockDim.x + threadIdx.x; c < row_floats;
+             c += (long)gridDim.x * blockDim.x)
+            d[c] = s[c];
+    }
+}
+// dst row idx[i] <- src row i (index_copy, pufferlib.cu:2147-2160)
+__global__ void k_scatter_rows(float* dst, const float* src, const int* idx, long row_floats) {
+    long i = blockIdx.y;
+    const float* s = src + i * row_floats;
+    float* d = dst + (long)idx[i] * row_floats;
+    for (long c = blockIdx.x * (long)blockDim.x + threadIdx.x; c < row_floats;
+         c += (long)gridDim.x * blockDim.x)
+        d[c] = s[c];
+}
+// returns = values + advantages of the selected segments (copy_values_adv_returns)
+__global__ void k_add_rows_flat(float* out, const float* a, const float* b, long n) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i < n) out[i] = a[i] + b[i];
+}

@@ -25,6 +25,7 @@
 
 #include <string>
 #include <vector>
+#include <algorithm>
 #include <mutex>
 #include <unordered_map>
 
@@ -1528,6 +1529,64 @@ int ptcg_adam_step(PtcgModel* M, float lr, float beta1, float beta2, float eps, 
     if (e) return e;
     CK(cudaSetDevice(M->dev));
     return adam_impl(M, lr, beta1, beta2, eps, max_norm, gate, stats, (cudaStream_t)stream);
+}
+
+int ptcg_prio_replay(const float* advantages, int B, int T, float alpha, float beta,
+                     int total_agents, int n_sel, const float* uniforms, int* idx,
+                     float* mb_prio, float* probs, float* cdf, void* stream) {
+    REQ(advantages && uniforms && idx && mb_prio && probs && cdf, PTCG_EINVAL, "null argument");
+    REQ(B > 0 && T > 0 && n_sel >= 0, PTCG_EINVAL, "bad sizes");
+    cudaStream_t s = (cudaStream_t)stream;
+    ++g_ptcg_launches, k_prio_rowsum<<<B, 32, 0, s>>>(probs, advantages, T, alpha);
+    ++g_ptcg_launches, k_prio_normalize<<<1, 256, 0, s>>>(probs, B);
+    ++g_ptcg_launches, k_prio_cdf<<<1, 1, 0, s>>>(cdf, probs, B);
+    if (n_sel > 0)
+        ++g_ptcg_launches, k_prio_sample<<<cdiv(n_sel, 256), 256, 0, s>>>(idx, mb_prio, cdf, probs, uniforms, B,
+            n_sel, total_agents, beta);
+    CKL();
+    return PTCG_OK;
+}
+
+static void gather_rows(float* dst, const float* src, const int* idx, int n, long row_floats,
+                        cudaStream_t s) {
+    if (n <= 0 || row_floats <= 0) return;
+    long per = (row_floats & 3) == 0 ? row_floats / 4 : row_floats;
+    unsigned gx = (unsigned)std::min<long>(cdiv(per, 256), 64);
+    ++g_ptcg_launches, k_gather_rows<<<dim3(gx, n), 256, 0, s>>>(dst, src, idx, row_floats);
+}
+
+int ptcg_select_copy(const int* idx, int n_sel, int T, long obs_size, int nopt,
+                     const float* obs, const float* actions, const float* logprobs,
+                     const float* values, const float* advantages, const float* mask,
+                     float* mb_obs, float* mb_actions, float* mb_logprobs, float* mb_values,
+                     float* mb_advantages, float* mb_returns, float* mb_mask, void* stream) {
+    REQ(idx && obs && actions && logprobs && values && advantages && mb_obs && mb_actions &&
+        mb_logprobs && mb_values && mb_advantages && mb_returns, PTCG_EINVAL, "null argument");
+    REQ(n_sel >= 0 && T > 0 && obs_size > 0, PTCG_EINVAL, "bad sizes");
+    REQ((mask == nullptr) == (mb_mask == nullptr) && (mask == nullptr || nopt > 0), PTCG_EINVAL,
+        "mask and mb_mask must both be given (with nopt > 0) or both be NULL");
+    cudaStream_t s = (cudaStream_t)stream;
+    gather_rows(mb_obs, obs, idx, n_sel, (long)T * obs_size, s);
+    gather_rows(mb_actions, actions, idx, n_sel, T, s);
+    gather_rows(mb_logprobs, logprobs, idx, n_sel, T, s);
+    gather_rows(mb_values, values, idx, n_sel, T, s);
+    gather_rows(mb_advantages, advantages, idx, n_sel, T, s);
+    if (mask) gather_rows(mb_mask, mask, idx, n_sel, (long)T * nopt, s);
+    long n = (long)n_sel * T;
+    if (n > 0)
+        ++g_ptcg_launches, k_add_rows_flat<<<cdiv(n, TPB), TPB, 0, s>>>(mb_returns, mb_values, mb_advantages, n);
+    CKL();
+    return PTCG_OK;
+}
+
+int ptcg_index_copy(float* dst, const int* idx, const float* src, int n, long row_floats,
+                    void* stream) {
+    REQ(dst && idx && src && n >= 0 && row_floats > 0, PTCG_EINVAL, "bad arguments");
+    if (n == 0) return PTCG_OK;
+    unsigned gx = (unsigned)std::min<long>(cdiv(row_floats, 256), 64);
+    ++g_ptcg_launches, k_scatter_rows<<<dim3(gx, n), 256, 0, (cudaStream_t)stream>>>(dst, src, idx, row_floats);
+    CKL();
+    return PTCG_OK;
 }
 
 int ptcg_sample_logits(const float* dec_out, int n, int nopt, const float* mask, long mask_stride,

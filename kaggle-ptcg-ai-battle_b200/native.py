@@ -55,6 +55,9 @@ _SIGS = {
     "ptcg_ppo_loss_noalloc": (I, [P, I, P, P, P, P, P, P, P, I, I, F, F, F, F,
                                   P, P, P, P, P]),
     "ptcg_adam_step": (I, [P, F, F, F, F, F, P, P, P]),
+    "ptcg_prio_replay": (I, [P, I, I, F, F, I, I, P, P, P, P, P, P]),
+    "ptcg_select_copy": (I, [P, I, I, L, I, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
+    "ptcg_index_copy": (I, [P, P, P, I, L, P]),
     "ptcg_sample_logits": (I, [P, I, I, P, L, P, P, P, P, P]),
     "ptcg_puff_advantage": (I, [P, P, P, P, P, L, I, I, I, F, F, F, F, P, P]),
     "ptcg_set_grad_hook": (I, [P, GRAD_HOOK, P]),

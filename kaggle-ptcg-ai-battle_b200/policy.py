@@ -192,6 +192,54 @@ class PTCGPolicy:
                                       _p(gate), _p(stats), _stream()))
         return stats
 
+    # ---------------------------------------------- minibatch selection
+    def prio_replay(self, advantages, alpha, beta, total_agents, uniforms):
+        """(idx int32, mb_prio, probs) of prioritised segment replay over
+        (B, T) advantages (ptcg_prio_replay)."""
+        d = self.device
+        adv, u = _f32(advantages, d), _f32(uniforms, d)
+        B, T = adv.shape
+        n = u.numel()
+        idx = torch.empty(n, dtype=torch.int32, device=d)
+        mb_prio = torch.empty(n, device=d)
+        probs = torch.empty(B, device=d)
+        cdf = torch.empty(B, device=d)
+        check(self.lib.ptcg_prio_replay(_p(adv), B, T, float(alpha), float(beta),
+                                        int(total_agents), n, _p(u), _p(idx), _p(mb_prio),
+                                        _p(probs), _p(cdf), _stream()))
+        return idx, mb_prio, probs
+
+    def select_copy(self, idx, obs, actions, logprobs, values, advantages, mask=None):
+        """Gather segments idx of (B, T, ...) rollout arrays (ptcg_select_copy);
+        returns a dict with obs, actions, logprobs, values, advantages,
+        returns (= values + advantages) and mask."""
+        d = self.device
+        idx = idx.to(device=d, dtype=torch.int32).contiguous()
+        obs = _f32(obs, d)
+        B, T = obs.shape[0], obs.shape[1]
+        src = [_f32(x, d) for x in (actions, logprobs, values, advantages)]
+        m = _f32(mask, d) if mask is not None else None
+        n = idx.numel()
+        out = dict(obs=torch.empty(n, T, obs.shape[2], device=d))
+        for k in ("actions", "logprobs", "values", "advantages", "returns"):
+            out[k] = torch.empty(n, T, device=d)
+        out["mask"] = torch.empty(n, T, m.shape[2], device=d) if m is not None else None
+        check(self.lib.ptcg_select_copy(_p(idx), n, T, obs.shape[2],
+                                        m.shape[2] if m is not None else 0, _p(obs),
+                                        *[_p(x) for x in src], _p(m), _p(out["obs"]),
+                                        _p(out["actions"]), _p(out["logprobs"]),
+                                        _p(out["values"]), _p(out["advantages"]),
+                                        _p(out["returns"]), _p(out["mask"]), _stream()))
+        return out
+
+    def index_copy(self, dst, idx, src):
+        """dst[idx[i]] = src[i] over rows (ptcg_index_copy), in place."""
+        idx = idx.to(device=self.device, dtype=torch.int32).contiguous()
+        n = idx.numel()
+        row = src.numel() // max(n, 1)
+        check(self.lib.ptcg_index_copy(_p(dst), _p(idx), _p(src), n, row, _stream()))
+        return dst
+
     def sample(self, dec_out, mask, uniforms):
         d = self.device
         dec_out, mask, uniforms = _f32(dec_out, d), _f32(mask, d), _f32(uniforms, d)

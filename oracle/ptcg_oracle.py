@@ -442,3 +442,45 @@ def negamax_advantage(values, rewards, dones, importance, seats, gamma, lam,
             last = f(delta + f(gamma) * f(lam) * cc * sg * last)
             adv[b, t] = last
     return adv
+
+
+def prio_replay(adv, alpha, beta, total_agents, uniforms):
+    """prio_replay_cuda (native/src/pufferlib.cu:1451-1591) in float32:
+    w_b = (sum_t |A_bt|)^alpha (0 when not finite; the per-row sum in the
+    kernel's order: 32 lane-strided partial sums, then a shuffle-down tree),
+    probs = (w + 1e-6) / (sum w + 1e-6), cdf = sequential running sum,
+    idx = first b with cdf[b] >= u (clamped to B - 1),
+    mb_prio = (total_agents * probs[idx])^(-beta).
+    Returns idx, mb_prio, probs, and the distance of each u to the nearest
+    cdf entry (index choices closer than rounding to a boundary are ties)."""
+    f = np.float32
+    a = np.abs(np.asarray(adv, np.float32))
+    B, T = a.shape
+    lanes = np.zeros((B, 32), np.float32)
+    for t in range(T):
+        lanes[:, t % 32] = lanes[:, t % 32] + a[:, t]
+    x = lanes
+    for o in (16, 8, 4, 2, 1):
+        x = (x[:, :o] + x[:, o:2 * o]).astype(np.float32)
+    s = x[:, 0]
+    with np.errstate(all="ignore"):
+        w = np.power(s.astype(np.float64), float(alpha)).astype(np.float32)
+    w[~np.isfinite(w)] = 0
+    total = f(np.float64(w.astype(np.float64).sum()) + 1e-6)
+    probs = ((w + f(1e-6)) / total).astype(np.float32)
+    cdf = np.cumsum(probs, dtype=np.float32)
+    u = np.asarray(uniforms, np.float32)
+    idx = np.minimum(np.searchsorted(cdf, u, side="left"), B - 1).astype(np.int32)
+    mb_prio = np.power(probs[idx].astype(np.float64) * total_agents,
+                       -float(beta)).astype(np.float32)
+    margin = np.abs(cdf[None, :] - u[:, None]).min(1) if B else np.zeros(len(u))
+    return idx, mb_prio, probs, margin
+
+
+def select_copy(idx, obs, actions, logprobs, values, advantages, mask=None):
+    """select_copy (native/src/pufferlib.cu:1777-1826): rows of the (B, T, ...)
+    rollout arrays at idx; returns = values + advantages."""
+    sel = lambda x: None if x is None else np.asarray(x)[idx]
+    v, a = sel(values), sel(advantages)
+    return dict(obs=sel(obs), actions=sel(actions), logprobs=sel(logprobs), values=v,
+                advantages=a, returns=(v + a).astype(np.float32), mask=sel(mask))
