@@ -81,6 +81,24 @@ int ptcg_set_tables(PtcgModel* m, const float* card_static, const int* card_atta
 int ptcg_load_weights(PtcgModel* m, const float* packed, long n);
 int ptcg_save_weights(PtcgModel* m, float* packed, long n);
 
+/* Files.  Weight files are the packed fp32 blob, exactly
+ * (native/src/bindings.cu:202-215 save_weights, :343-367 load_weights, which
+ * rejects a size mismatch).  State files, written atomically (tmp, fsync,
+ * rename):
+ *  - format 0, "PTCGSTA1" (bindings.cu:252-341): header {char magic[8];
+ *    long global_step, epoch, n_params} (LP64, 32 bytes), packed weights,
+ *    packed momentum.  The momentum slot carries the first-moment arena
+ *    (Adam m, or the Muon momentum), so a state file round-trips with the
+ *    reference's trainer;
+ *  - format 1, "PTCGADM1" (new, for Adam resumes): header {magic; long
+ *    global_step, epoch, n_params, adam_step} (40 bytes), packed weights, m, v.
+ * ptcg_load_state reads either (by magic), restores weights (and bf16 copies),
+ * the moments present in the file and, for PTCGADM1, the Adam step. */
+int ptcg_save_weights_file(PtcgModel* m, const char* path);
+int ptcg_load_weights_file(PtcgModel* m, const char* path);
+int ptcg_save_state(PtcgModel* m, const char* path, long global_step, long epoch, int format);
+int ptcg_load_state(PtcgModel* m, const char* path, long* global_step, long* epoch);
+
 /* Size activation workspaces: rollout forward for up to `rollout_rows`
  * observations and train forward/backward for up to `train_rows` rows per
  * call (a minibatch larger than train_rows is processed in micro-batches by

@@ -21,6 +21,7 @@
 
 #include <stdarg.h>
 #include <stdio.h>
+#include <unistd.h>
 #include <string.h>
 
 #include <string>
@@ -1345,6 +1346,161 @@ int ptcg_save_weights(PtcgModel* M, float* packed, long n) {
         CK(cudaMemcpy(packed + o, M->params + M->off[i], k * 4, cudaMemcpyDeviceToHost));
         o += k;
     }
+    return PTCG_OK;
+}
+
+// ---- on-disk formats (native/src/bindings.cu:202-367)
+static long packed_total(const PtcgModel* M) {
+    long tot = 0;
+    for (auto& p : M->defs) tot += numel(p);
+    return tot;
+}
+// device arena (16-byte aligned per tensor) <-> packed PT_PARAMS order
+static int arena_to_packed(PtcgModel* M, const float* arena, std::vector<float>& out) {
+    out.assign(packed_total(M), 0.f);
+    long o = 0;
+    for (size_t i = 0; i < M->defs.size(); i++) {
+        long k = numel(M->defs[i]);
+        CK(cudaMemcpy(out.data() + o, arena + M->off[i], k * 4, cudaMemcpyDeviceToHost));
+        o += k;
+    }
+    return PTCG_OK;
+}
+static int packed_to_arena(PtcgModel* M, const float* packed, float* arena) {
+    long o = 0;
+    for (size_t i = 0; i < M->defs.size(); i++) {
+        long k = numel(M->defs[i]);
+        CK(cudaMemcpy(arena + M->off[i], packed + o, k * 4, cudaMemcpyHostToDevice));
+        o += k;
+    }
+    return PTCG_OK;
+}
+// write whole buffers to path + ".tmp", flush, fsync, rename onto path
+static int write_atomic(const char* path, const std::vector<std::pair<const void*, size_t>>& parts) {
+    std::string tmp = std::string(path) + ".tmp";
+    FILE* f = fopen(tmp.c_str(), "wb");
+    REQ(f, PTCG_EINVAL, "cannot open %s for writing", tmp.c_str());
+    bool ok = true;
+    for (auto& pr : parts) ok = ok && fwrite(pr.first, 1, pr.second, f) == pr.second;
+    ok = ok && fflush(f) == 0 && fsync(fileno(f)) == 0;
+    fclose(f);
+    REQ(ok, PTCG_EINVAL, "short write to %s", tmp.c_str());
+    REQ(rename(tmp.c_str(), path) == 0, PTCG_EINVAL, "cannot rename %s -> %s", tmp.c_str(), path);
+    return PTCG_OK;
+}
+
+// "PTCGSTA1" header of the reference's trainer state (bindings.cu:257-262),
+// LP64: 8 + 3 x 8 bytes
+struct StateHeader { char magic[8]; long global_step, epoch, n_params; };
+// "PTCGADM1": the same fields plus the Adam step counter, then weights, m, v
+struct AdamHeader { char magic[8]; long global_step, epoch, n_params, adam_step; };
+static_assert(sizeof(StateHeader) == 32 && sizeof(AdamHeader) == 40, "LP64 header layout");
+
+int ptcg_save_weights_file(PtcgModel* M, const char* path) {
+    REQ(M && path, PTCG_EINVAL, "null argument");
+    CK(cudaSetDevice(M->dev));
+    CK(cudaDeviceSynchronize());
+    std::vector<float> w;
+    int e = arena_to_packed(M, M->params, w);
+    if (e) return e;
+    FILE* f = fopen(path, "wb");
+    REQ(f, PTCG_EINVAL, "cannot open %s for writing", path);
+    size_t nw = fwrite(w.data(), sizeof(float), w.size(), f);
+    fclose(f);
+    REQ(nw == w.size(), PTCG_EINVAL, "short write to %s", path);
+    return PTCG_OK;
+}
+
+int ptcg_load_weights_file(PtcgModel* M, const char* path) {
+    REQ(M && path, PTCG_EINVAL, "null argument");
+    FILE* f = fopen(path, "rb");
+    REQ(f, PTCG_EINVAL, "cannot open %s for reading", path);
+    fseek(f, 0, SEEK_END);
+    long bytes = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    long n = packed_total(M);
+    if (bytes != n * 4) {
+        fclose(f);
+        set_err("weight file size mismatch: expected %ld bytes, got %ld", n * 4, bytes);
+        return PTCG_EINVAL;
+    }
+    std::vector<float> w(n);
+    size_t nr = fread(w.data(), sizeof(float), n, f);
+    fclose(f);
+    REQ((long)nr == n, PTCG_EINVAL, "failed to read %s", path);
+    return ptcg_load_weights(M, w.data(), n);
+}
+
+int ptcg_save_state(PtcgModel* M, const char* path, long global_step, long epoch, int format) {
+    REQ(M && path, PTCG_EINVAL, "null argument");
+    REQ(format == 0 || format == 1, PTCG_EINVAL, "format must be 0 (PTCGSTA1) or 1 (PTCGADM1)");
+    CK(cudaSetDevice(M->dev));
+    CK(cudaDeviceSynchronize());
+    std::vector<float> w, m, v;
+    int e = arena_to_packed(M, M->params, w);
+    if (!e) e = arena_to_packed(M, M->am, m);
+    if (e) return e;
+    size_t nb = w.size() * sizeof(float);
+    if (format == 0) {
+        StateHeader h;
+        memcpy(h.magic, "PTCGSTA1", 8);
+        h.global_step = global_step; h.epoch = epoch; h.n_params = (long)w.size();
+        return write_atomic(path, {{&h, sizeof h}, {w.data(), nb}, {m.data(), nb}});
+    }
+    e = arena_to_packed(M, M->av, v);
+    if (e) return e;
+    long long step = 0;
+    CK(cudaMemcpy(&step, M->step_dev, sizeof step, cudaMemcpyDeviceToHost));
+    AdamHeader h;
+    memcpy(h.magic, "PTCGADM1", 8);
+    h.global_step = global_step; h.epoch = epoch; h.n_params = (long)w.size();
+    h.adam_step = (long)step;
+    return write_atomic(path, {{&h, sizeof h}, {w.data(), nb}, {m.data(), nb}, {v.data(), nb}});
+}
+
+int ptcg_load_state(PtcgModel* M, const char* path, long* global_step, long* epoch) {
+    REQ(M && path, PTCG_EINVAL, "null argument");
+    FILE* f = fopen(path, "rb");
+    REQ(f, PTCG_EINVAL, "cannot open %s for reading", path);
+    char magic[8] = {0};
+    size_t got = fread(magic, 1, 8, f);
+    fseek(f, 0, SEEK_SET);
+    bool sta = got == 8 && memcmp(magic, "PTCGSTA1", 8) == 0;
+    bool adm = got == 8 && memcmp(magic, "PTCGADM1", 8) == 0;
+    if (!sta && !adm) {
+        fclose(f);
+        set_err("%s is not a PTCGSTA1 / PTCGADM1 state file", path);
+        return PTCG_EINVAL;
+    }
+    long n = packed_total(M);
+    AdamHeader h{};
+    size_t hb = sta ? sizeof(StateHeader) : sizeof(AdamHeader);
+    bool ok = fread(&h, 1, hb, f) == hb;
+    if (ok && h.n_params != n) {
+        fclose(f);
+        set_err("state param count mismatch: file %ld, model %ld", h.n_params, n);
+        return PTCG_EINVAL;
+    }
+    std::vector<float> w(n), m(n), v;
+    ok = ok && fread(w.data(), sizeof(float), n, f) == (size_t)n;
+    ok = ok && fread(m.data(), sizeof(float), n, f) == (size_t)n;
+    if (adm) {
+        v.resize(n);
+        ok = ok && fread(v.data(), sizeof(float), n, f) == (size_t)n;
+    }
+    fclose(f);
+    REQ(ok, PTCG_EINVAL, "truncated state file %s", path);
+    CK(cudaSetDevice(M->dev));
+    int e = ptcg_load_weights(M, w.data(), n);
+    if (!e) e = packed_to_arena(M, m.data(), M->am);
+    if (!e && adm) e = packed_to_arena(M, v.data(), M->av);
+    if (e) return e;
+    if (adm) {
+        long long step = h.adam_step;
+        CK(cudaMemcpy(M->step_dev, &step, sizeof step, cudaMemcpyHostToDevice));
+    }
+    if (global_step) *global_step = h.global_step;
+    if (epoch) *epoch = h.epoch;
     return PTCG_OK;
 }
 

@@ -47,6 +47,10 @@ _SIGS = {
     "ptcg_load_weights": (I, [P, P, L]),
     "ptcg_save_weights": (I, [P, P, L]),
     "ptcg_reserve": (I, [P, I, I]),
+    "ptcg_save_weights_file": (I, [P, C.c_char_p]),
+    "ptcg_load_weights_file": (I, [P, C.c_char_p]),
+    "ptcg_save_state": (I, [P, C.c_char_p, L, L, I]),
+    "ptcg_load_state": (I, [P, C.c_char_p, C.POINTER(C.c_long), C.POINTER(C.c_long)]),
     "ptcg_forward": (I, [P, P, I, P, P]),
     "ptcg_forward_train": (I, [P, P, I, P, P]),
     "ptcg_backward": (I, [P, P, P, I, F, I, P]),

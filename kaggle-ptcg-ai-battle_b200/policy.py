@@ -99,6 +99,30 @@ class PTCGPolicy:
         check(self.lib.ptcg_save_weights(self.h, b.ctypes.data_as(C.c_void_p), b.size))
         return b
 
+    # files: packed fp32 weight blobs and PTCGSTA1 / PTCGADM1 state files
+    def save_weights_file(self, path):
+        check(self.lib.ptcg_save_weights_file(self.h, str(path).encode()))
+
+    def load_weights_file(self, path):
+        check(self.lib.ptcg_load_weights_file(self.h, str(path).encode()))
+
+    def save_state(self, path, global_step=0, epoch=0, fmt="PTCGADM1"):
+        f = {"PTCGSTA1": 0, "PTCGADM1": 1}[fmt]
+        check(self.lib.ptcg_save_state(self.h, str(path).encode(), int(global_step), int(epoch), f))
+
+    def load_state(self, path):
+        """-> (global_step, epoch) from a PTCGSTA1 or PTCGADM1 file."""
+        gs, ep = C.c_long(), C.c_long()
+        check(self.lib.ptcg_load_state(self.h, str(path).encode(), C.byref(gs), C.byref(ep)))
+        return gs.value, ep.value
+
+    def packed(self, which):
+        """An arena (0 params, 1 grads, 2 Adam m / Muon momentum, 3 Adam v) in
+        packed PT_PARAMS order (numpy)."""
+        a = self.arena(which).cpu().numpy()
+        return np.concatenate([a[o:o + int(np.prod(shp))] for (_, shp), o in
+                               zip(param_table(self.shape), self.param_offsets())])
+
     def reserve(self, rollout_rows, train_rows):
         check(self.lib.ptcg_reserve(self.h, int(rollout_rows), int(train_rows)))
         self.rollout_rows, self.train_rows = rollout_rows, train_rows
