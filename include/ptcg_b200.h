@@ -187,6 +187,22 @@ int ptcg_ppo_loss_noalloc(const float* dec_out, int nopt, const float* mask,
 int ptcg_adam_step(PtcgModel* m, float lr, float beta1, float beta2, float eps,
                    float max_norm, const float* gate, float* stats, void* stream);
 
+/* Muon step over the whole arena, the reference trainer's optimizer
+ * (muon_step, native/src/muon.cu:209-297, with its local patches):
+ *  - clip: g *= min(1, max_norm / (||g|| + 1e-6)) (always applied);
+ *  - tensors with two dimensions: nesterov m = mu m + g, g += mu m; g / ||g||;
+ *    five Newton-Schulz steps X <- a X + (b G + c G^2) X (G = X X^T, or
+ *    X (b G + c G^2) with G = X^T X when rows > cols) with the reference's
+ *    coefficient table; w = w (1 - lr wd) - lr sqrt(max(1, rows/cols)) X;
+ *  - 1-D tensors: m = mu m + (1 - mu) g, w = w (1 - lr wd_1d) - lr (g + m).
+ * The momentum lives in arena 2 (shared with Adam's first moment: use one
+ * optimizer per model).  gate (device float or NULL) = 0 skips every state
+ * and weight write.  stats (device, 2 floats) = {grad norm, applied}.  The
+ * grad arena is overwritten (clipped, then the Nesterov / orthogonalised
+ * update), as in the reference. */
+int ptcg_muon_step(PtcgModel* m, float lr, float momentum, float weight_decay, float wd_1d,
+                   float max_norm, const float* gate, float* stats, void* stream);
+
 /* Prioritised segment replay over (B, T) advantages: w_b = (sum_t |A_bt|)^alpha
  * (0 when not finite), probs = (w + 1e-6) / (sum w + 1e-6), cdf = running sum
  * in index order, idx[i] = first b with cdf[b] >= uniforms[i] (clamped to

@@ -1090,8 +1090,8 @@ __global__ void k_negamax_adv(const float* values, const float* rewards, const f
 }
 
 // ------------------------------------------------------------ Adam
-// pass 1: per-block partial sum of squared grads (fp64 accumulation);
-// n is a multiple of 4 (every arena tensor starts 16-byte aligned)
+// pass 1: per-block partial sum of squares (fp64 accumulation); g is
+// 16-byte aligned (arena tensors start on 16 bytes), n is any length
 __global__ void k_sumsq(double* partials, const float* g, long n) {
     __shared__ double sh[32];
     double s = 0.0;
@@ -1100,6 +1100,10 @@ __global__ void k_sumsq(double* partials, const float* g, long n) {
          i += (long)gridDim.x * blockDim.x) {
         float4 v = g4[i];
         s += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+    }
+    if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+        double v = g[(n & ~3L) + threadIdx.x];
+        s += v * v;
     }
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
@@ -1313,4 +1317,86 @@ __global__ void k_scatter_rows(float* dst, const float* src, const int* idx, lon
 __global__ void k_add_rows_flat(float* out, const float* a, const float* b, long n) {
     long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
     if (i < n) out[i] = a[i] + b[i];
+}
+
+// ---------------------------------------------------------------- Muon
+// (muon_step, native/src/muon.cu:209-297; the gate vetoes a step by
+// returning before any state or weight is touched, muon.cu:54-60, 89-99)
+// grads *= min(1, max_norm / (||g|| + 1e-6)) from the k_sumsq partials
+__global__ void k_muon_clip(float* g, long n, const double* partials, int nparts, float max_norm,
+                            float* stats) {
+    __shared__ double s_red[32];
+    __shared__ float s_coef;
+    double tp = 0.0;
+    for (int i = threadIdx.x; i < nparts; i += blockDim.x) tp += partials[i];
+    for (int o = 16; o > 0; o >>= 1) tp += __shfl_xor_sync(0xffffffffu, tp, o);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = tp;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += s_red[i];
+        float norm = (float)sqrt(t);
+        s_coef = fminf(max_norm / (norm + 1e-6f), 1.f);
+        if (blockIdx.x == 0 && stats) stats[0] = norm;
+    }
+    __syncthreads();
+    float c = s_coef;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+        g[i] *= c;
+}
+// >= 2-D parameters: nesterov with a sum accumulator, m = mu m + g; g += mu m
+__global__ void k_muon_nesterov(float* mb, float* g, const float* gate, float mu, long n) {
+    if (gate && *gate == 0.f) return;
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i < n) {
+        float m = mu * mb[i] + g[i];
+        mb[i] = m;
+        g[i] = g[i] + mu * m;
+    }
+}
+// 1-D parameters: EMA momentum, m = mu m + (1 - mu) g; g += m
+__global__ void k_muon_nesterov_ema(float* mb, float* g, const float* gate, float mu, long n) {
+    if (gate && *gate == 0.f) return;
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i < n) {
+        float gi = g[i];
+        float m = mu * mb[i] + (1.f - mu) * gi;
+        mb[i] = m;
+        g[i] = gi + m;
+    }
+}
+// x *= 1 / max(||x||, eps) with the norm from k_sumsq partials (one block)
+__global__ void k_muon_normalize(float* x, long n, const double* partials, int nparts, float eps) {
+    __shared__ double s_red[32];
+    __shared__ float s_inv;
+    double tp = 0.0;
+    for (int i = threadIdx.x; i < nparts; i += blockDim.x) tp += partials[i];
+    for (int o = 16; o > 0; o >>= 1) tp += __shfl_xor_sync(0xffffffffu, tp, o);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = tp;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += s_red[i];
+        s_inv = 1.f / fmaxf((float)sqrt(t), eps);
+    }
+    __syncthreads();
+    float inv = s_inv;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+        x[i] *= inv;
+}
+// y = a x (elementwise)
+__global__ void k_scale_to(float* y, const float* x, float a, long n) {
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i < n) y[i] = a * x[i];
+}
+// w = w (1 - lr wd) - lr scale u
+__global__ void k_muon_update(float* w, const float* u, float lr, const float* gate, float wd,
+                              float scale, long n) {
+    if (gate && *gate == 0.f) return;
+    float wd_scale = 1.f - lr * wd;
+    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i < n) w[i] = w[i] * wd_scale - lr * scale * u[i];
+}
+__global__ void k_gate_stat(float* stats, const float* gate) {
+    stats[1] = (gate && *gate == 0.f) ? 0.f : 1.f;
 }

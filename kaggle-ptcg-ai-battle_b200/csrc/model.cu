@@ -190,6 +190,9 @@ struct PtcgModel {
     int* d_chunk_copy = nullptr;
     int adam_chunk = 4096, adam_grid = 0, sumsq_grid = 0;
     double* d_partials = nullptr;
+    // Muon scratch (orthogonalisation of the >= 2-D parameters)
+    float *mu_gram = nullptr, *mu_gram2 = nullptr, *mu_x = nullptr;
+    double* mu_partials = nullptr;
     float* d_misc = nullptr;            // [0..1] adv stats, [2] prize count, [4..19] stats, [32..] adam stats
     unsigned int* d_ck = nullptr;
     // static tables
@@ -1249,6 +1252,17 @@ int ptcg_create(const PtcgShape* s, int precision, int device, PtcgModel** out) 
     CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_sumsq, 256, 0));
     M->sumsq_grid = prop.multiProcessorCount * (per_sm > 0 ? per_sm : 1);
     CK(cudaMalloc(&M->d_partials, sizeof(double) * M->sumsq_grid));
+    {   // Muon scratch: gram pair [maxM^2] and the iterate [maxM x maxN]
+        long mm = 0, mn = 0;
+        for (auto& d : M->defs)
+            if (d.c > 0) { mm = std::max(mm, std::min(d.r, d.c)); mn = std::max(mn, std::max(d.r, d.c)); }
+        if (mm > 0) {
+            CK(cudaMalloc(&M->mu_gram, sizeof(float) * mm * mm));
+            CK(cudaMalloc(&M->mu_gram2, sizeof(float) * mm * mm));
+            CK(cudaMalloc(&M->mu_x, sizeof(float) * mm * mn));
+        }
+        CK(cudaMalloc(&M->mu_partials, sizeof(double) * M->sumsq_grid));
+    }
     CK(cudaMalloc(&M->d_misc, sizeof(float) * 64));
     CK(cudaMemset(M->d_misc, 0, sizeof(float) * 64));
     CK(cudaMalloc(&M->d_ck, 16));
@@ -1273,7 +1287,8 @@ int ptcg_destroy(PtcgModel* M) {
     void* ptrs[] = {M->params, M->grads, M->am, M->av, M->step_dev, M->wbf, M->d_copies,
                     M->d_chunk_copy, M->d_partials, M->d_misc, M->d_ck, M->card_static,
                     M->att_static, M->card_text, M->att_text, M->skill_text, M->card_attacks,
-                    M->card_skills, M->tab_base};
+                    M->card_skills, M->tab_base, M->mu_gram, M->mu_gram2, M->mu_x,
+                    M->mu_partials};
     for (void* p : ptrs) if (p) cudaFree(p);
     delete M;
     return PTCG_OK;
@@ -1685,6 +1700,88 @@ int ptcg_adam_step(PtcgModel* M, float lr, float beta1, float beta2, float eps, 
     if (e) return e;
     CK(cudaSetDevice(M->dev));
     return adam_impl(M, lr, beta1, beta2, eps, max_norm, gate, stats, (cudaStream_t)stream);
+}
+
+// Newton-Schulz quintic coefficients (a, b, c) per iteration, muon.cu:116-122:
+// X <- a X + (b G + c G^2) X (wide) / X (b G + c G^2) (tall), G = X X^T / X^T X
+static const double kMuonNS[5][3] = {
+    {4.0848, -6.8946, 2.9270}, {3.9505, -6.3029, 2.6377}, {3.7418, -5.5913, 2.3037},
+    {2.8769, -3.1427, 1.2046}, {2.8366, -3.0525, 1.2012}};
+
+// fp32-operand GEMM C[M x N] (ldc) = alpha * op + (accumulate ? C : 0) with
+// A(m, k) at a (K-major: a[m * lda + k]; else a[k * lda + m]), B likewise
+static void gemm_f(PtcgModel* M, int Mr, int N, int K, const float* a, long lda, int ak,
+                   const float* b, long ldb, int bk, float* c, long ldc, float alpha, int acc,
+                   cudaStream_t s) {
+    GemmArgs g;
+    g.M = Mr; g.N = N; g.K = K; g.dtype = DT_F32;
+    g.A = a; g.lda = lda; g.a_kmajor = ak;
+    g.B = b; g.ldb = ldb; g.b_kmajor = bk;
+    g.out = c; g.ldo = ldc; g.out_dtype = DT_F32; g.alpha = alpha; g.accumulate = acc;
+    gemm32(M, g, s);
+}
+
+static int muon_impl(PtcgModel* M, float lr, float mu, float wd, float wd_1d, float max_norm,
+                     const float* gate, float* stats, cudaStream_t s) {
+    float* st = stats ? stats : M->d_misc + 32;
+    // global clip (always applied; the gate only vetoes state / weight writes)
+    ++g_ptcg_launches, k_sumsq<<<M->sumsq_grid, 256, 0, s>>>(M->d_partials, M->grads, M->n_arena);
+    ++g_ptcg_launches, k_muon_clip<<<M->sumsq_grid, 256, 0, s>>>(M->grads, M->n_arena, M->d_partials,
+        M->sumsq_grid, max_norm, st);
+    ++g_ptcg_launches, k_gate_stat<<<1, 1, 0, s>>>(st, gate);
+    for (size_t i = 0; i < M->defs.size(); i++) {
+        const ParamDef& d = M->defs[i];
+        long n = numel(d);
+        float* g = M->grads + M->off[i];
+        float* w = M->params + M->off[i];
+        float* mb = M->am + M->off[i];
+        const float* upd = g;
+        float scale = 1.f, wdi = wd;
+        if (d.c > 0) {
+            ++g_ptcg_launches, k_muon_nesterov<<<cdiv(n, TPB), TPB, 0, s>>>(mb, g, gate, mu, n);
+            int np = (int)std::min<long>(M->sumsq_grid, cdiv(n, 256 * 4));
+            if (np < 1) np = 1;
+            ++g_ptcg_launches, k_sumsq<<<np, 256, 0, s>>>(M->mu_partials, g, n);
+            ++g_ptcg_launches, k_muon_normalize<<<np, 256, 0, s>>>(g, n, M->mu_partials, np, 1e-7f);
+            const long R = d.r, C = d.c, Mg = std::min(R, C);
+            const bool tall = R > C;
+            float* bufs[2] = {g, M->mu_x};
+            for (int it = 0; it < 5; it++) {
+                float* src = bufs[it & 1];
+                float* dst = bufs[(it + 1) & 1];
+                // G = X^T X (tall, C x C) or X X^T (wide, R x R)
+                if (tall) gemm_f(M, (int)C, (int)C, (int)R, src, C, 0, src, C, 0, M->mu_gram, C, 1.f, 0, s);
+                else gemm_f(M, (int)R, (int)R, (int)C, src, C, 1, src, C, 1, M->mu_gram, R, 1.f, 0, s);
+                // B = b G + c G^2  (into mu_gram2)
+                ++g_ptcg_launches, k_scale_to<<<cdiv(Mg * Mg, TPB), TPB, 0, s>>>(M->mu_gram2, M->mu_gram,
+                    (float)kMuonNS[it][1], Mg * Mg);
+                gemm_f(M, (int)Mg, (int)Mg, (int)Mg, M->mu_gram, Mg, 1, M->mu_gram, Mg, 0, M->mu_gram2,
+                       Mg, (float)kMuonNS[it][2], 1, s);
+                // X' = a X + X B (tall) / B X (wide)
+                ++g_ptcg_launches, k_scale_to<<<cdiv(n, TPB), TPB, 0, s>>>(dst, src, (float)kMuonNS[it][0], n);
+                if (tall) gemm_f(M, (int)R, (int)C, (int)C, src, C, 1, M->mu_gram2, C, 0, dst, C, 1.f, 1, s);
+                else gemm_f(M, (int)R, (int)C, (int)R, M->mu_gram2, R, 1, src, C, 0, dst, C, 1.f, 1, s);
+            }
+            upd = M->mu_x;                                   // five iterations end in the scratch
+            scale = sqrtf(fmaxf(1.f, (float)R / (float)C));
+        } else {
+            ++g_ptcg_launches, k_muon_nesterov_ema<<<cdiv(n, TPB), TPB, 0, s>>>(mb, g, gate, mu, n);
+            wdi = wd_1d;
+        }
+        ++g_ptcg_launches, k_muon_update<<<cdiv(n, TPB), TPB, 0, s>>>(w, upd, lr, gate, wdi, scale, n);
+    }
+    return refresh_copies(M, s);
+}
+
+int ptcg_muon_step(PtcgModel* M, float lr, float momentum, float weight_decay, float wd_1d,
+                   float max_norm, const float* gate, float* stats, void* stream) {
+    int e = ready(M);
+    if (e) return e;
+    CK(cudaSetDevice(M->dev));
+    e = muon_impl(M, lr, momentum, weight_decay, wd_1d, max_norm, gate, stats, (cudaStream_t)stream);
+    if (e) return e;
+    CKL();
+    return PTCG_OK;
 }
 
 int ptcg_prio_replay(const float* advantages, int B, int T, float alpha, float beta,

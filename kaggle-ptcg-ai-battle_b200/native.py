@@ -59,6 +59,7 @@ _SIGS = {
     "ptcg_ppo_loss_noalloc": (I, [P, I, P, P, P, P, P, P, P, I, I, F, F, F, F,
                                   P, P, P, P, P]),
     "ptcg_adam_step": (I, [P, F, F, F, F, F, P, P, P]),
+    "ptcg_muon_step": (I, [P, F, F, F, F, F, P, P, P]),
     "ptcg_prio_replay": (I, [P, I, I, F, F, I, I, P, P, P, P, P, P]),
     "ptcg_select_copy": (I, [P, I, I, L, I, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
     "ptcg_index_copy": (I, [P, P, P, I, L, P]),

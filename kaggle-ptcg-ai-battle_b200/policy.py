@@ -264,6 +264,15 @@ class PTCGPolicy:
         check(self.lib.ptcg_index_copy(_p(dst), _p(idx), _p(src), n, row, _stream()))
         return dst
 
+    def muon_step(self, lr=0.02, momentum=0.95, weight_decay=0.0, wd_1d=0.0, max_norm=1.5,
+                  gate=None):
+        """The reference trainer's Muon optimizer (ptcg_muon_step); the
+        momentum is arena 2.  Returns device stats {grad norm, applied}."""
+        stats = torch.zeros(2, device=self.device)
+        check(self.lib.ptcg_muon_step(self.h, lr, momentum, weight_decay, wd_1d, max_norm,
+                                      _p(gate), _p(stats), _stream()))
+        return stats
+
     def sample(self, dec_out, mask, uniforms):
         d = self.device
         dec_out, mask, uniforms = _f32(dec_out, d), _f32(mask, d), _f32(uniforms, d)

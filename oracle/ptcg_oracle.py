@@ -484,3 +484,39 @@ def select_copy(idx, obs, actions, logprobs, values, advantages, mask=None):
     v, a = sel(values), sel(advantages)
     return dict(obs=sel(obs), actions=sel(actions), logprobs=sel(logprobs), values=v,
                 advantages=a, returns=(v + a).astype(np.float32), mask=sel(mask))
+
+
+MUON_NS = ((4.0848, -6.8946, 2.9270), (3.9505, -6.3029, 2.6377), (3.7418, -5.5913, 2.3037),
+           (2.8769, -3.1427, 1.2046), (2.8366, -3.0525, 1.2012))       # muon.cu:116-122
+
+
+def muon_step(params, grads, mom, shapes, lr, mu, wd, wd_1d, max_norm, gate=True):
+    """muon_step (native/src/muon.cu:209-297) on dicts of float64 tensors, in
+    place; returns the pre-clip grad norm.  shapes[name] = (rows, cols),
+    cols == 0 for 1-D parameters (PT_PARAMS, ptcg_model.cu:90-126)."""
+    norm = torch.sqrt(sum((g.double() ** 2).sum() for g in grads.values()))
+    coef = min(max_norm / (float(norm) + 1e-6), 1.0)                  # muon.cu:107-113, 231
+    for name, (r, c) in shapes.items():
+        g = grads[name].double().reshape(-1) * coef
+        m = mom[name].reshape(-1)
+        w = params[name].reshape(-1)
+        if c > 0:                                                     # muon.cu:255-286
+            if gate:
+                m.mul_(mu).add_(g)
+                g = g + mu * m
+            x = g.reshape(r, c)
+            x = x / max(float(x.norm()), 1e-7)
+            tall = r > c
+            for a, b, cc in MUON_NS:
+                G = x.T @ x if tall else x @ x.T
+                B = b * G + cc * (G @ G)
+                x = a * x + (x @ B if tall else B @ x)
+            upd, scale, wdi = x.reshape(-1), max(1.0, r / c) ** 0.5, wd
+        else:                                                         # muon.cu:287-292, 79-88
+            if gate:
+                m.mul_(mu).add_((1 - mu) * g)
+                g = g + m
+            upd, scale, wdi = g, 1.0, wd_1d
+        if gate:                                                      # muon.cu:94-99
+            w.mul_(1 - lr * wdi).add_(-lr * scale * upd)
+    return float(norm)
