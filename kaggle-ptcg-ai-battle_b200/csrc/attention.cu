@@ -650,21 +650,24 @@ PTCG_DEV void st8(bf16* p, const float* f) {
     *reinterpret_cast<uint4*>(p) = u;
 }
 
-// out[n, :] = softmax(q0 K^T / sqrt(32)) V per head; lse[n, h] natural-log
+// out[n, :] = softmax(q_n K^T / sqrt(32)) V per head; lse[n, h] natural-log
 // log-sum-exp of the scaled scores (-inf when every key is masked).
+// q: the query row of sequence n at q + n * ldq; kv: rows [K | V] (2D wide,
+// row stride ldkv) of every position, sequence n at rows n * L ..
 template <typename T>
 __global__ void __launch_bounds__(512) k_attn_row0_fwd(
-        const T* __restrict__ qkv, long ldqkv, const uint8_t* __restrict__ keep,
-        T* __restrict__ out, long ldo, float* __restrict__ lse, int L, int H) {
+        const T* __restrict__ qrows, long ldq, const T* __restrict__ kv, long ldkv,
+        const uint8_t* __restrict__ keep, T* __restrict__ out, long ldo,
+        float* __restrict__ lse, int L, int H) {
     extern __shared__ float sm[];
     const int n = blockIdx.x, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int D = H * DH, Lr = (L + 31) & ~31;
     float* qs = sm + h * DH;
     float* p = sm + H * DH + h * Lr;
-    const T* base = qkv + (long)n * L * ldqkv;
+    const T* base = kv + (long)n * L * ldkv;
     const uint8_t* kp = keep + (long)n * L;
     const float scale = 0.17677669529663687f;   // 1/sqrt(32)
-    qs[lane] = to_f<T>(base[h * DH + lane]) * scale;
+    qs[lane] = to_f<T>(qrows[(long)n * ldq + h * DH + lane]) * scale;
     __syncwarp();
     float q[DH];
     #pragma unroll
@@ -673,7 +676,7 @@ __global__ void __launch_bounds__(512) k_attn_row0_fwd(
     for (int j = lane; j < L; j += 32) {
         float s = -INFINITY;
         if (kp[j]) {
-            const T* kr = base + (long)j * ldqkv + D + h * DH;
+            const T* kr = base + (long)j * ldkv + h * DH;
             s = 0.f;
             #pragma unroll
             for (int c = 0; c < DH; c += 8) {
@@ -695,26 +698,27 @@ __global__ void __launch_bounds__(512) k_attn_row0_fwd(
     }
     sum = warp_sum(sum);
     __syncwarp();
-    const T* vb = base + 2 * D + h * DH + lane;
+    const T* vb = base + D + h * DH + lane;
     float o = 0.f;
     for (int j = 0; j < L; j++) {
         float pj = p[j];
-        if (pj != 0.f) o = fmaf(pj, to_f<T>(vb[(long)j * ldqkv]), o);
+        if (pj != 0.f) o = fmaf(pj, to_f<T>(vb[(long)j * ldkv]), o);
     }
     out[(long)n * ldo + h * DH + lane] = from_f<T>(sum > 0.f ? o / sum : 0.f);
     if (lane == 0) lse[(long)n * H + h] = sum > 0.f ? mx + logf(sum) : -INFINITY;
 }
 
-// Backward of k_attn_row0_fwd.  Writes every row of dqkv: dQ at row 0 and
-// zeros in the Q columns of rows 1.., dK / dV at every key (zero where
-// masked).  The QKV bias gradient (fp32, before rounding) accumulates into
-// dbias[3D]: per-thread partials over the sequences a CTA visits, one
-// atomic per column per CTA.
+// Backward of k_attn_row0_fwd: dq (one row per sequence, dq + n * lddq) and
+// dK / dV at every key of dkv (rows [dK | dV], zero where masked).  The QKV
+// bias gradient (fp32, before rounding) accumulates into dbias[3D] = [q | k |
+// v]: per-thread partials over the sequences a CTA visits, one atomic per
+// column per CTA.
 template <typename T>
 __global__ void __launch_bounds__(512) k_attn_row0_bwd(
-        const T* __restrict__ qkv, long ldqkv, const uint8_t* __restrict__ keep,
-        const T* __restrict__ out, long ldo, const T* __restrict__ dout, long lddo,
-        const float* __restrict__ lse, T* __restrict__ dqkv, long lddqkv,
+        const T* __restrict__ qv, long ldq, const T* __restrict__ kv, long ldkv,
+        const uint8_t* __restrict__ keep, const T* __restrict__ out, long ldo,
+        const T* __restrict__ dout, long lddo, const float* __restrict__ lse,
+        T* __restrict__ dqo, long lddq, T* __restrict__ dkv, long lddkv,
         float* __restrict__ dbias, int R, int L, int H) {
     extern __shared__ float sm[];
     const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -725,10 +729,10 @@ __global__ void __launch_bounds__(512) k_attn_row0_bwd(
     const float scale = 0.17677669529663687f;
     float cq = 0.f, ck = 0.f, cv = 0.f;
     for (int n = blockIdx.x; n < R; n += gridDim.x) {
-        const T* base = qkv + (long)n * L * ldqkv;
-        T* dbase = dqkv + (long)n * L * lddqkv;
+        const T* base = kv + (long)n * L * ldkv;
+        T* dbase = dkv + (long)n * L * lddkv;
         const uint8_t* kp = keep + (long)n * L;
-        float qd = to_f<T>(base[h * DH + lane]);
+        float qd = to_f<T>(qv[(long)n * ldq + h * DH + lane]);
         float gd = to_f<T>(dout[(long)n * lddo + h * DH + lane]);
         float od = to_f<T>(out[(long)n * ldo + h * DH + lane]);
         float delta = warp_sum(gd * od);
@@ -742,7 +746,7 @@ __global__ void __launch_bounds__(512) k_attn_row0_bwd(
         for (int j = lane; j < L; j += 32) {
             float dsj = 0.f, pj = 0.f;
             if (kp[j] && l != -INFINITY) {
-                const T* kr = base + (long)j * ldqkv + D + h * DH;
+                const T* kr = base + (long)j * ldkv + h * DH;
                 const T* vr = kr + D;
                 float s = 0.f, dp = 0.f;
                 #pragma unroll
@@ -761,32 +765,27 @@ __global__ void __launch_bounds__(512) k_attn_row0_bwd(
             }
             dsb[j] = dsj;
             sds += dsj; sp += pj;
-            T* dr = dbase + (long)j * lddqkv + h * DH;
+            T* dr = dbase + (long)j * lddkv + h * DH;
             float t8[8];
             #pragma unroll
             for (int c = 0; c < DH; c += 8) {
                 #pragma unroll
                 for (int e = 0; e < 8; e++) t8[e] = scale * dsj * q[c + e];
-                st8(dr + D + c, t8);
+                st8(dr + c, t8);
                 #pragma unroll
                 for (int e = 0; e < 8; e++) t8[e] = pj * g[c + e];
-                st8(dr + 2 * D + c, t8);
-                if (j > 0) {
-                    #pragma unroll
-                    for (int e = 0; e < 8; e++) t8[e] = 0.f;
-                    st8(dr + c, t8);
-                }
+                st8(dr + D + c, t8);
             }
         }
         __syncwarp();
-        const T* kb = base + D + h * DH + lane;
+        const T* kb = base + h * DH + lane;
         float dq = 0.f;
         for (int j = 0; j < L; j++) {
             float d = dsb[j];
-            if (d != 0.f) dq = fmaf(d, to_f<T>(kb[(long)j * ldqkv]), dq);
+            if (d != 0.f) dq = fmaf(d, to_f<T>(kb[(long)j * ldkv]), dq);
         }
         dq *= scale;
-        dbase[h * DH + lane] = from_f<T>(dq);
+        dqo[(long)n * lddq + h * DH + lane] = from_f<T>(dq);
         sds = warp_sum(sds);
         sp = warp_sum(sp);
         cq += dq;
@@ -836,39 +835,40 @@ void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
     }
 }
 
-void attn_row0_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
-                   void* out, long ldo, float* lse, int nseq, int L, int H, cudaStream_t s) {
+void attn_row0_fwd(int dtype, const void* q, long ldq, const void* kv, long ldkv,
+                   const uint8_t* keep, void* out, long ldo, float* lse, int nseq, int L, int H,
+                   cudaStream_t s) {
     if (nseq <= 0) return;
     size_t sm = sizeof(float) * H * (DH + ((L + 31) & ~31));
     if (dtype == DT_F32) {
         set_smem(k_attn_row0_fwd<float>, sm);
-        ++g_ptcg_launches, k_attn_row0_fwd<float><<<nseq, H * 32, sm, s>>>((const float*)qkv, ldqkv,
-            keep, (float*)out, ldo, lse, L, H);
+        ++g_ptcg_launches, k_attn_row0_fwd<float><<<nseq, H * 32, sm, s>>>((const float*)q, ldq,
+            (const float*)kv, ldkv, keep, (float*)out, ldo, lse, L, H);
     } else {
         set_smem(k_attn_row0_fwd<bf16>, sm);
-        ++g_ptcg_launches, k_attn_row0_fwd<bf16><<<nseq, H * 32, sm, s>>>((const bf16*)qkv, ldqkv,
-            keep, (bf16*)out, ldo, lse, L, H);
+        ++g_ptcg_launches, k_attn_row0_fwd<bf16><<<nseq, H * 32, sm, s>>>((const bf16*)q, ldq,
+            (const bf16*)kv, ldkv, keep, (bf16*)out, ldo, lse, L, H);
     }
 }
 
-void attn_row0_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
-                   const void* out, long ldo, const void* dout, long lddo,
-                   const float* lse, void* dqkv, long lddqkv, float* dbias, int nseq, int L,
-                   int H, cudaStream_t s) {
+void attn_row0_bwd(int dtype, const void* q, long ldq, const void* kv, long ldkv,
+                   const uint8_t* keep, const void* out, long ldo, const void* dout, long lddo,
+                   const float* lse, void* dq, long lddq, void* dkv, long lddkv, float* dbias,
+                   int nseq, int L, int H, cudaStream_t s) {
     if (nseq <= 0) return;
     size_t sm = sizeof(float) * H * (2 * DH + ((L + 31) & ~31));
     int per_sm = H * 32 <= 256 ? 8 : 4;
     unsigned grid = (unsigned)std::min<long>(nseq, (long)num_sms() * per_sm);
     if (dtype == DT_F32) {
         set_smem(k_attn_row0_bwd<float>, sm);
-        ++g_ptcg_launches, k_attn_row0_bwd<float><<<grid, H * 32, sm, s>>>((const float*)qkv, ldqkv,
-            keep, (const float*)out, ldo, (const float*)dout, lddo, lse, (float*)dqkv, lddqkv,
-            dbias, nseq, L, H);
+        ++g_ptcg_launches, k_attn_row0_bwd<float><<<grid, H * 32, sm, s>>>((const float*)q, ldq,
+            (const float*)kv, ldkv, keep, (const float*)out, ldo, (const float*)dout, lddo, lse,
+            (float*)dq, lddq, (float*)dkv, lddkv, dbias, nseq, L, H);
     } else {
         set_smem(k_attn_row0_bwd<bf16>, sm);
-        ++g_ptcg_launches, k_attn_row0_bwd<bf16><<<grid, H * 32, sm, s>>>((const bf16*)qkv, ldqkv,
-            keep, (const bf16*)out, ldo, (const bf16*)dout, lddo, lse, (bf16*)dqkv, lddqkv,
-            dbias, nseq, L, H);
+        ++g_ptcg_launches, k_attn_row0_bwd<bf16><<<grid, H * 32, sm, s>>>((const bf16*)q, ldq,
+            (const bf16*)kv, ldkv, keep, (const bf16*)out, ldo, (const bf16*)dout, lddo, lse,
+            (bf16*)dq, lddq, (bf16*)dkv, lddkv, dbias, nseq, L, H);
     }
 }
 

@@ -54,15 +54,18 @@ int ptcg_tc_profile_ctl(int enable, unsigned long long* out8);
 void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
               void* out, long ldo, float* lse, int nseq, int L, int H,
               cudaStream_t s);
-// first query row of each sequence only: out / dout [n * ldo + h*32 + d],
-// lse [n * H + h]; every row of dqkv is written (Q columns zero past row 0).
-// H <= 16.
-void attn_row0_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
-                   void* out, long ldo, float* lse, int nseq, int L, int H, cudaStream_t s);
-void attn_row0_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
-                   const void* out, long ldo, const void* dout, long lddo,
-                   const float* lse, void* dqkv, long lddqkv, float* dbias, int nseq, int L,
-                   int H, cudaStream_t s);
+// first query row of each sequence only: q row of sequence n at
+// q + n * ldq, keys / values as rows [K | V] of kv (row stride ldkv,
+// sequence n at rows n * L ..); out / dout [n * ldo + h*32 + d], lse
+// [n * H + h]; the backward writes dq (one row per sequence) and dK / dV of
+// every row, and adds the [q | k | v] bias grads to dbias.  H <= 16.
+void attn_row0_fwd(int dtype, const void* q, long ldq, const void* kv, long ldkv,
+                   const uint8_t* keep, void* out, long ldo, float* lse, int nseq, int L, int H,
+                   cudaStream_t s);
+void attn_row0_bwd(int dtype, const void* q, long ldq, const void* kv, long ldkv,
+                   const uint8_t* keep, const void* out, long ldo, const void* dout, long lddo,
+                   const float* lse, void* dq, long lddq, void* dkv, long lddkv, float* dbias,
+                   int nseq, int L, int H, cudaStream_t s);
 // dbias (nullable, 3*H*32 floats): += column sums of dqkv in fp32
 void attn_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
               const void* out, long ldo, const void* dout, long lddo,

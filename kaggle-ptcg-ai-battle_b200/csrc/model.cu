@@ -124,6 +124,7 @@ struct BlkW { W ln1w, ln1b, qkvw, qkvb, projw, projb, ln2w, ln2b, f1w, f1b, f2w,
 struct BlkAct {
     float *x_in, *x_out;
     void *ln1, *qkv, *att, *ln2, *fpre, *fpost;
+    void* q0;                           // readout-row blocks: query rows [R, D]; qkv holds [K | V]
     float *mu1, *rs1, *mu2, *rs2, *lse, *xm;
 };
 
@@ -145,6 +146,7 @@ struct Work {
     // backward scratch
     float *dh, *dgd, *dbvin, *d_v1pre, *dscores, *dscin, *dqin, *dtokcat, *ddecin, *dd1,
           *dg1, *dbc, *dotokin, *dx, *dln, *dx0;
+    void* dq0;                          // readout-row block: d query rows [R, D]
     void *dx0c, *dxc, *dhand, *ds1pre, *dq, *dq1, *dotok, *dtokp, *df, *datt, *dqkv;
     float* dgrad;                       // PPO grad for one micro-batch (train_step)
     float* fused;                       // fused [scores | value] of one micro-batch
@@ -315,6 +317,14 @@ static void gemm32(PtcgModel* M, GemmArgs a, cudaStream_t s) {
     gemm(M, a, s);
 }
 
+// view of rows r0.. of a [rows x cols] parameter (operand, master and grad)
+static W wrows(const W& w, long r0, long cols, int esz) {
+    W r = w;
+    r.p = w.p + r0 * cols;
+    r.g = w.g + r0 * cols;
+    r.op = (const char*)w.op + r0 * w.ld * esz;
+    return r;
+}
 // fp32 operand view of a parameter (per-sample / table GEMMs stay fp32)
 static W f32w(const W& w, long cols) { W r = w; r.op = w.p; r.ld = cols; return r; }
 
@@ -384,6 +394,7 @@ static void plan_blk(BlkAct& b, Bump& m, int R, int L, int rows_out, const Dims&
     b.fpre = train ? m.take(NQ * z.FFN * esz) : nullptr;
     b.fpost = m.take(NQ * z.FFN * esz);
     b.mu1 = m.f(NL); b.rs1 = m.f(NL); b.mu2 = m.f(NQ); b.rs2 = m.f(NQ);
+    b.q0 = rows_out == 1 ? m.take((long)R * z.D * esz) : nullptr;
     b.lse = m.f(NQ * z.H);
     b.xm = m.f(NQ * z.D);
 }
@@ -449,6 +460,7 @@ static void plan_work(Work& W, Bump& m, int R, bool train, const Dims& z, int es
     W.dotokin = m.f((long)R * 56 * 134);
     W.dx = m.f(NC * z.D);
     W.dx0 = m.f((long)R * z.D);
+    W.dq0 = m.take((long)R * z.D * esz);
     W.dx0c = bf16mode ? m.take((long)R * z.D * esz) : (void*)W.dx0;
     W.dln = m.f(NC * z.D);
     W.dxc = bf16mode ? m.take(NC * z.D * esz) : (void*)W.dx;
@@ -564,10 +576,15 @@ static void block_fwd_row0(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t
     const int dt = M->dt(), D = z.D;
     const int NL = R * L;
     ln_fwd(dt, b.ln1, D, b.mu1, b.rs1, b.x_in, D, P.ln1w.p, P.ln1b.p, NL, D, s);
-    GemmArgs a = lin_fwd(dt, NL, D, 3 * D, b.ln1, D, P.qkvw, b.qkv, 3 * D, dt);
+    // keys and values of every row (weight rows D..3D), queries of the
+    // readout rows only (weight rows 0..D; A rows at stride L * D)
+    GemmArgs a = lin_fwd(dt, NL, D, 2 * D, b.ln1, D, wrows(P.qkvw, D, D, M->esz()), b.qkv, 2 * D, dt);
+    a.bias = P.qkvb.p + D;
+    gemm(M, a, s);
+    a = lin_fwd(dt, R, D, D, b.ln1, (long)L * D, P.qkvw, b.q0, D, dt);
     a.bias = P.qkvb.p;
     gemm(M, a, s);
-    attn_row0_fwd(dt, b.qkv, 3 * D, keep, b.att, D, b.lse, R, L, z.H, s);
+    attn_row0_fwd(dt, b.q0, D, b.qkv, 2 * D, keep, b.att, D, b.lse, R, L, z.H, s);
     a = lin_fwd(dt, R, D, D, b.att, D, P.projw, b.xm, D, DT_F32);
     a.bias = P.projb.p; a.resid = b.x_in; a.ld_resid = (long)L * D;
     gemm(M, a, s);
@@ -808,12 +825,21 @@ static void block_bwd_row0(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t
     // proj
     gemm(M, lin_dw(dt, R, D, D, dx0c, D, b.att, D, P.projw.g), s);
     gemm(M, lin_dx(dt, R, D, D, dx0c, D, P.projw, Wk.datt, D, dt), s);
-    // attention: dQ at row 0, dK / dV at every key
-    attn_row0_bwd(dt, b.qkv, 3 * D, keep, b.att, D, Wk.datt, D, b.lse, Wk.dqkv, 3 * D, P.qkvb.g,
-                  R, L, z.H, s);
-    // QKV over every row
-    gemm(M, lin_dw(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, b.ln1, D, P.qkvw.g), s);
-    gemm(M, lin_dx(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, P.qkvw, Wk.dln, D, dt), s);
+    // attention: dQ of the readout rows, dK / dV at every key
+    attn_row0_bwd(dt, b.q0, D, b.qkv, 2 * D, keep, b.att, D, Wk.datt, D, b.lse, Wk.dq0, D,
+                  Wk.dqkv, 2 * D, P.qkvb.g, R, L, z.H, s);
+    // QKV weight grads: query rows from the readout rows, key / value rows
+    // from every row
+    W wkv = wrows(P.qkvw, D, D, M->esz());
+    gemm(M, lin_dw(dt, R, D, D, Wk.dq0, D, b.ln1, (long)L * D, P.qkvw.g), s);
+    gemm(M, lin_dw(dt, NL, D, 2 * D, Wk.dqkv, 2 * D, b.ln1, D, wkv.g), s);
+    // d(LN1 out) = dKV Wkv at every row, + dQ Wq at the readout rows
+    gemm(M, lin_dx(dt, NL, D, 2 * D, Wk.dqkv, 2 * D, wkv, Wk.dln, D, dt), s);
+    {
+        GemmArgs a = lin_dx(dt, R, D, D, Wk.dq0, D, P.qkvw, Wk.dln, (long)L * D, dt);
+        a.accumulate = 1;
+        gemm(M, a, s);
+    }
     // d(x_in) = LN1'(dln) + the residual grad at row 0
     ln_bwd(dt, Wk.dx, 0, nullptr, P.ln1w.g, P.ln1b.g, Wk.dln, b.x_in, P.ln1w.p, b.mu1, b.rs1,
            NL, D, s, nullptr, dt);
