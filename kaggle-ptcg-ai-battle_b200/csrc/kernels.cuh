@@ -707,16 +707,15 @@ __global__ void k_xc_bwd(T* d_otok, float* d_h, const float* dxc, int lseq, int 
     }
 }
 
-// trunk input grad split: row 0 -> d_readout; rows 1.. -> d_tokp (T, compact);
-// d_bc[n] = sum over token rows (one block per sample, no atomics on d_bc)
+// trunk input grad split: rows 1.. -> d_tokp (T, compact); d_bc[n] = sum
+// over token rows (one block per sample, no atomics); row 0 -> d_readout is
+// a column sum over samples, done separately
 template <typename T>
-__global__ void k_x0_bwd(float* d_read, T* d_tokp, float* d_bc, const float* dx0, int ltok,
-                         int D) {
+__global__ void k_x0_bwd(T* d_tokp, float* d_bc, const float* dx0, int ltok, int D) {
     int n = blockIdx.x;
     int lseq = ltok + 1;
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         const float* base = dx0 + (long)n * lseq * D + d;
-        atomicAdd(&d_read[d], base[0]);
         float acc = 0.f;
         for (int l = 1; l < lseq; l++) {
             float g = base[(long)l * D];
@@ -729,33 +728,45 @@ __global__ void k_x0_bwd(float* d_read, T* d_tokp, float* d_bc, const float* dx0
 
 __global__ void k_tok_cat_bwd(float* d_cv, float* d_zemb, float* d_oemb, const float* g,
                               long ldg, const float* obs, ObsLayout L, int R, int tok_in) {
-    long nl = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);   // warp per token row
+    // warp per token row, grid-stride; the zone (16 x 8) and owner (4 x 4)
+    // embedding grads, which every token hits, accumulate in shared memory
+    // and leave with one atomic per entry per block
+    __shared__ float sz[16 * 8], so[4 * 4];
+    for (int i = threadIdx.x; i < 16 * 8; i += blockDim.x) sz[i] = 0.f;
+    if (threadIdx.x < 16) so[threadIdx.x] = 0.f;
+    __syncthreads();
     const int lane = threadIdx.x & 31;
-    if (nl >= (long)R * L.ltok) return;
-    const int n = (int)(nl / L.ltok), l = (int)(nl - (long)n * L.ltok);
-    const float* ti = obs + (long)n * L.obs + L.toki + l * 5;
-    const float* gr = g + nl * ldg;
-    float* c0 = d_cv + (long)id_clamp(ti[0], L.nc) * 128;
-    const int t0 = (int)ti[3], t1 = (int)ti[4];
-    float* ca = t0 > 0 ? d_cv + (long)(t0 >= L.nc ? L.nc - 1 : t0) * 128 : nullptr;
-    float* cb = t1 > 0 ? d_cv + (long)(t1 >= L.nc ? L.nc - 1 : t1) * 128 : nullptr;
+    const long nrows = (long)R * L.ltok;
     const bool vec = (ldg & 3) == 0;
-    for (int c = lane * 4; c < 256; c += 128) {
-        float4 v = vec ? ld4(gr + c) : make_float4(gr[c], gr[c + 1], gr[c + 2], gr[c + 3]);
-        if (!nz4(v)) continue;
-        if (c < 128) red_add4(c0 + c, v);
-        else {
-            if (ca) red_add4(ca + (c - 128), v);
-            if (cb) red_add4(cb + (c - 128), v);
+    for (long nl = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); nl < nrows;
+         nl += (long)gridDim.x * (blockDim.x >> 5)) {
+        const int n = (int)(nl / L.ltok), l = (int)(nl - (long)n * L.ltok);
+        const float* ti = obs + (long)n * L.obs + L.toki + l * 5;
+        const float* gr = g + nl * ldg;
+        float* c0 = d_cv + (long)id_clamp(ti[0], L.nc) * 128;
+        const int t0 = (int)ti[3], t1 = (int)ti[4];
+        float* ca = t0 > 0 ? d_cv + (long)(t0 >= L.nc ? L.nc - 1 : t0) * 128 : nullptr;
+        float* cb = t1 > 0 ? d_cv + (long)(t1 >= L.nc ? L.nc - 1 : t1) * 128 : nullptr;
+        for (int c = lane * 4; c < 256; c += 128) {
+            float4 v = vec ? ld4(gr + c) : make_float4(gr[c], gr[c + 1], gr[c + 2], gr[c + 3]);
+            if (!nz4(v)) continue;
+            if (c < 128) red_add4(c0 + c, v);
+            else {
+                if (ca) red_add4(ca + (c - 128), v);
+                if (cb) red_add4(cb + (c - 128), v);
+            }
+        }
+        if (lane < 12) {
+            float v = gr[256 + L.tok_f + lane];
+            if (v != 0.f) {
+                if (lane < 8) atomicAdd(&sz[id_clamp(ti[1], 16) * 8 + lane], v);
+                else atomicAdd(&so[id_clamp(ti[2], 4) * 4 + (lane - 8)], v);
+            }
         }
     }
-    if (lane < 12) {                                 // zone (8) and owner (4) embeddings
-        float v = gr[256 + L.tok_f + lane];
-        if (v != 0.f) {
-            if (lane < 8) atomicAdd(&d_zemb[id_clamp(ti[1], 16) * 8 + lane], v);
-            else atomicAdd(&d_oemb[id_clamp(ti[2], 4) * 4 + (lane - 8)], v);
-        }
-    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 16 * 8; i += blockDim.x) if (sz[i] != 0.f) atomicAdd(&d_zemb[i], sz[i]);
+    if (threadIdx.x < 16 && so[threadIdx.x] != 0.f) atomicAdd(&d_oemb[threadIdx.x], so[threadIdx.x]);
 }
 
 // ------------------------------------------------------------ aux losses
@@ -810,31 +821,44 @@ __global__ void k_count_unseen(float* cnt, const float* obs, ObsLayout L, int R)
 __global__ void k_prize_bwd(float* d_h, float* dw, float* db, const float* logit,
                             const float* h, const float* w, const float* obs, ObsLayout L,
                             const float* cnt_dev, float cnt_host, int D, int R, float* loss) {
-    int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    int lane = threadIdx.x & 31;
-    if (t >= R * L.ltok) return;
-    int n = t / L.ltok, l = t % L.ltok;
-    const float* row = obs + (long)n * L.obs;
-    if ((int)row[L.toki + l * 5 + 1] != 9) return;
-    int cid = id_clamp(row[L.toki + l * 5], L.nc);
-    float tgt = 0.f;
-    const float* o = row + L.orc;
-    for (int k = 0; k < 8; k++) {
-        int id = (int)o[120 + 2 * k];
-        if (id > 0 && id < L.nc && o[121 + 2 * k] > 0.f && id == cid) tgt = 1.f;
+    // warp per token, grid-stride.  dw (D), db and the loss accumulate in
+    // shared memory (every counted token hits them); each token's d_h row
+    // belongs to this warp alone, so it is a plain add.
+    extern __shared__ float sp[];               // [D] dw, [1] db, [1] loss
+    for (int i = threadIdx.x; i < D + 2; i += blockDim.x) sp[i] = 0.f;
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const float c = cnt_host > 0.f ? cnt_host : (cnt_dev[0] > 0.f ? cnt_dev[0] : 1.f);
+    for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < R * L.ltok;
+         t += gridDim.x * (blockDim.x >> 5)) {
+        int n = t / L.ltok, l = t % L.ltok;
+        const float* row = obs + (long)n * L.obs;
+        if ((int)row[L.toki + l * 5 + 1] != 9) continue;
+        int cid = id_clamp(row[L.toki + l * 5], L.nc);
+        float tgt = 0.f;
+        const float* o = row + L.orc;
+        for (int k = 0; k < 8; k++) {
+            int id = (int)o[120 + 2 * k];
+            if (id > 0 && id < L.nc && o[121 + 2 * k] > 0.f && id == cid) tgt = 1.f;
+        }
+        float x = logit[t];
+        float g = 0.1f * (sigmoid_f(x) - tgt) / c;
+        if (lane == 0) {
+            float bce = fmaxf(x, 0.f) - x * tgt + log1pf(expf(-fabsf(x)));
+            atomicAdd(&sp[D + 1], 0.1f * bce / c);
+            atomicAdd(&sp[D], g);
+        }
+        long hr = ((long)n * L.lseq + 1 + l) * D;
+        for (int d = lane; d < D; d += 32) {
+            d_h[hr + d] += g * w[d];
+            atomicAdd(&sp[d], g * h[hr + d]);
+        }
     }
-    float c = cnt_host > 0.f ? cnt_host : (cnt_dev[0] > 0.f ? cnt_dev[0] : 1.f);
-    float x = logit[t];
-    float g = 0.1f * (sigmoid_f(x) - tgt) / c;
-    if (lane == 0) {
-        float bce = fmaxf(x, 0.f) - x * tgt + log1pf(expf(-fabsf(x)));
-        atomicAdd(loss, 0.1f * bce / c);
-        atomicAdd(db, g);
-    }
-    long hr = ((long)n * L.lseq + 1 + l) * D;
-    for (int d = lane; d < D; d += 32) {
-        atomicAdd(&d_h[hr + d], g * w[d]);
-        atomicAdd(&dw[d], g * h[hr + d]);
+    __syncthreads();
+    for (int i = threadIdx.x; i < D; i += blockDim.x) if (sp[i] != 0.f) atomicAdd(&dw[i], sp[i]);
+    if (threadIdx.x == 0) {
+        if (sp[D] != 0.f) atomicAdd(db, sp[D]);
+        if (sp[D + 1] != 0.f) atomicAdd(loss, sp[D + 1]);
     }
 }
 

@@ -947,7 +947,7 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     }
     ++g_ptcg_launches, k_val_in_bwd<<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.dh, z.LSEQ, D, Wk.dgd, Wk.dbvin, R, 1);
     // ---- aux: prize BCE over MY_UNSEEN tokens
-    ++g_ptcg_launches, k_prize_bwd<<<cdiv((long)R * z.LTOK, 8), 256, 0, s>>>(Wk.dh, M->w("aux_prize_w").g,
+    ++g_ptcg_launches, k_prize_bwd<<<std::min<unsigned>(cdiv((long)R * z.LTOK, 8), M->adam_grid), 256, (D + 2) * sizeof(float), s>>>(Wk.dh, M->w("aux_prize_w").g,
         M->w("aux_prize_b").g, Wk.prize_logit, Wk.h, M->w("aux_prize_w").p, obs, ol, prize_cnt_dev,
         prize_cnt_host, D, R, aux_loss + 2);
     // ---- oracle value head (PPO value grad = grad[:, NOPT])
@@ -1078,16 +1078,21 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
                             i == z.LAYERS - 1 ? "lnf_w" : ("b" + std::to_string(i + 1) + "_ln1_w").c_str(), s);
     }
     // ---- x0 split, token projection, broadcast
+    {   // readout grad: column sum of row 0 over samples
+        int gpb = 64;
+        dim3 g(cdiv(D, 128), cdiv(R, gpb));
+        ++g_ptcg_launches, k_colsum_groups<<<g, 128, 0, s>>>(M->w("readout").g, Wk.dx, D, R, z.LSEQ, 0, 1, D, gpb);
+    }
     if (bf)
-        ++g_ptcg_launches, k_x0_bwd<bf16><<<R, 256, 0, s>>>(M->w("readout").g, (bf16*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D);
+        ++g_ptcg_launches, k_x0_bwd<bf16><<<R, 256, 0, s>>>((bf16*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D);
     else
-        ++g_ptcg_launches, k_x0_bwd<float><<<R, 256, 0, s>>>(M->w("readout").g, (float*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D);
+        ++g_ptcg_launches, k_x0_bwd<float><<<R, 256, 0, s>>>((float*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D);
     W wt = M->w("token_proj_w");
     long ldtok = rup(z.TOK_IN, 8);
     colsum<float>(M->w("token_proj_b").g, Wk.dbc, D, R, D, s);
     gemm(M, lin_dw(dt, R * z.LTOK, z.TOK_IN, D, Wk.dtokp, D, Wk.tokcat, ldtok, wt.g), s);
     gemm(M, lin_dx(dt, R * z.LTOK, z.TOK_IN, D, Wk.dtokp, D, wt, Wk.dtokcat, z.TOK_IN, DT_F32), s);
-    ++g_ptcg_launches, k_tok_cat_bwd<<<cdiv((long)R * z.LTOK, TPB / 32), TPB, 0, s>>>(t.d_cv, M->w("zone_emb").g,
+    ++g_ptcg_launches, k_tok_cat_bwd<<<std::min<unsigned>(cdiv((long)R * z.LTOK, TPB / 32), M->adam_grid), TPB, 0, s>>>(t.d_cv, M->w("zone_emb").g,
         M->w("owner_emb").g, Wk.dtokcat, z.TOK_IN, obs, ol, R, z.TOK_IN);
     colsum<float>(M->w("bcast_b").g, Wk.dbc, D, R, D, s);
     gemm32(M, lin_dw(DT_F32, R, 192, D, Wk.dbc, D, Wk.gd, 192, M->w("bcast_w").g), s);
