@@ -45,7 +45,7 @@ def parse():
     ap.add_argument("--micro", type=int, default=8192, help="rows per micro-batch")
     ap.add_argument("--rollout-agents", type=int, default=1024)
     ap.add_argument("--rollout-steps", type=int, default=64)
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=4)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-rollout", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -363,22 +363,30 @@ def main():
     write_gbs = 10 * wbuf.numel() * 2 / (w0.elapsed_time(w1) / 1e3) / 1e9
     del wbuf
 
-    # --- end to end through the public API: pinned host inputs -> device,
-    #     train step, loss stats back to the host, every step
-    host = dict(obs=obs_h, act=act_h, old=old.cpu().pin_memory(), adv=adv.cpu().pin_memory(),
-                val=vals.cpu().pin_memory(), ret=ret.cpu().pin_memory())
-    bufs = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
-    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    # --- end to end through the public API: every step copies its inputs
+    #     from pinned host memory (HostFeed: on a copy stream, the next
+    #     step's inputs crossing PCIe while this step computes), runs the
+    #     train step and reads the loss stats back to the host
+    from ptcg_b200.feed import HostFeed
+    host = dict(obs=obs_h, act=act_h.pin_memory(), old=old.cpu().pin_memory(),
+                adv=adv.cpu().pin_memory(), val=vals.cpu().pin_memory(),
+                ret=ret.cpu().pin_memory())
+    feed = HostFeed(host, dev, depth=2)
+    h2d = feed.bytes_per_put
     d2h = 16 * 4
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record()
+    feed.start()
+    feed.put(host)
     for i in range(args.e2e_steps):
-        for k in host:
-            bufs[k].copy_(host[k], non_blocking=True)
-        step(0, bufs["obs"], bufs["act"], bufs["old"], bufs["adv"], bufs["val"], bufs["ret"])
+        fb = feed.get()
+        if i + 1 < args.e2e_steps:
+            feed.put(host)
+        step(0, fb["obs"], fb["act"], fb["old"], fb["adv"], fb["val"], fb["ret"])
+        feed.release()
         _ = stats.cpu()
     f1.record()
     torch.cuda.synchronize()

@@ -14,7 +14,7 @@ __all__ = ["config", "synth"]
 
 def __getattr__(name):
     # computing pieces import lazily so config / synth work without the .so
-    if name in ("native", "policy", "build", "smoke", "dp"):
+    if name in ("native", "policy", "build", "smoke", "dp", "feed"):
         import importlib
         return importlib.import_module(f"{__name__}.{name}")
     if name == "PTCGPolicy":

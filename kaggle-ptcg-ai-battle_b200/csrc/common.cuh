@@ -11,6 +11,9 @@ typedef __nv_bfloat16 bf16;
 #ifndef PTCG_EPI_WARPS
 #define PTCG_EPI_WARPS 16       // epilogue warps per CTA (multiple of 4)
 #endif
+#ifndef PTCG_EPI_WARPS_LIGHT
+#define PTCG_EPI_WARPS_LIGHT 12 // epilogue warps of the GEMMs without GELU math
+#endif
 #ifndef PTCG_STAGE_BUFS
 #define PTCG_STAGE_BUFS 1       // TMA-store staging buffers per epilogue warp (1 or 2)
 #endif

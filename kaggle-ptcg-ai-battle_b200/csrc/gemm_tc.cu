@@ -14,8 +14,10 @@
 //   M=128, N=BN into a double-buffered TMEM accumulator and releases ring
 //   slots with tcgen05.commit.  A 128-byte swizzled row holds 64 bf16 or 32
 //   fp32 K-elements, so both kinds share one byte-level smem layout.
-// * PTCG_EPI_WARPS epilogue warps (16: four per TMEM lane quadrant, each
-//   taking every fourth 32-column chunk) read the accumulator with
+// * PTCG_EPI_WARPS epilogue warps for the GELU / GELU' epilogues,
+//   PTCG_EPI_WARPS_LIGHT for the rest (16 / 12: four / three per TMEM lane
+//   quadrant, each taking every fourth / third 32-column chunk) read the
+//   accumulator with
 //   tcgen05.ld.32x32b.x32 while the next tile's MMAs run, and apply bias
 //   (staged once per CTA in shared memory) / broadcast / GELU and GELU'
 //   (packed f32x2 math) / GELU' multiply / row remap / residual /
@@ -41,13 +43,20 @@
 namespace {
 
 constexpr int BM = 128;
-constexpr int NUM_EPI = PTCG_EPI_WARPS;      // epilogue warps (NUM_EPI / 4 per TMEM lane quadrant)
-constexpr int EPI_GROUPS = NUM_EPI / 4;      // warps sharing a quadrant split its 32-column chunks
+// epilogue warps per CTA (a multiple of 4: NEPI / 4 per TMEM lane quadrant,
+// splitting its 32-column chunks).  The GELU / GELU' epilogues are
+// instruction-bound and run PTCG_EPI_WARPS warps; the others run
+// PTCG_EPI_WARPS_LIGHT, whose larger register budget (the 64K registers
+// split over fewer threads) keeps their epilogue free of spills.
+constexpr int NUM_EPI = PTCG_EPI_WARPS;
+constexpr int NUM_EPI_LIGHT = PTCG_EPI_WARPS_LIGHT;
 constexpr int STAGE_BUFS = PTCG_STAGE_BUFS;  // TMA-store staging buffers per epilogue warp
 constexpr int STAGE_W = 4096 * STAGE_BUFS;   // staging bytes per epilogue warp
 constexpr int BIAS_SMEM_MAX = 4096;          // bias vectors up to this many columns live in smem
-static_assert(NUM_EPI % 4 == 0 && STAGE_BUFS >= 1 && STAGE_BUFS <= 2, "epilogue layout");
-constexpr int NUM_THREADS = 64 + 32 * NUM_EPI; // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
+static_assert(NUM_EPI % 4 == 0 && NUM_EPI_LIGHT % 4 == 0 && STAGE_BUFS >= 1 && STAGE_BUFS <= 2,
+              "epilogue layout");
+// warp 0 TMA, warp 1 MMA, warps 2.. epilogue
+constexpr int threads_for(int nepi) { return 64 + 32 * nepi; }
 constexpr long long WAIT_BUDGET = 4000000000LL;   // clock cycles (~2 s)
 
 __device__ int g_tc_error_dev;
@@ -72,6 +81,7 @@ struct TcParams {
     int bias_smem;           // columns of the bias staged in shared memory (0: read from global)
     int aux_tma;             // the GELU' operand arrives by TMA into two smem slots
     uint32_t aux_bytes;      // bytes of one slot: BM rows x bn bf16, as bn/32 boxes of 8 KB
+    int nepi;                // epilogue warps of the instantiation that runs the plan
     GemmArgs ep;
 };
 
@@ -181,7 +191,6 @@ PTCG_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
                  : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-
 // UMMA shared-memory descriptor, sm_100 version bits.  layout 2 = 128-byte
 // swizzle (16-byte granules, 8-row atoms); layout 1 = 128-byte swizzle with
 // 32-byte granules and 4-row atoms (the only MN-major layout for 32-bit
@@ -274,15 +283,28 @@ PTCG_DEV float warp_colsum32(float (&v)[32], int lane) {
     return v[0];
 }
 
+// one operand tile of a ring stage: `rows` MN rows x one 128-byte K row.
+// K-major: one box {BK, rows}; MN-major: rows / ATOM boxes {ATOM, BK}
+template <int EB>
+PTCG_DEV void load_operand(uint32_t dst, const CUtensorMap* map, uint32_t bar, int mn_major,
+                           int rows, int mn0, int k0) {
+    constexpr int ATOM = 128 / EB;
+    constexpr uint32_t BOX = (128 / EB) * 128;
+    if (mn_major) {
+        for (int j = 0; j < rows / ATOM; j++) tma_load_2d(dst + j * BOX, map, bar, mn0 + ATOM * j, k0);
+    } else {
+        tma_load_2d(dst, map, bar, k0, mn0);
+    }
+}
+
 // -------------------------------------------------------------- the kernel
 // EB = operand element bytes (2: bf16 / kind::f16, 4: fp32 / kind::tf32)
-template <int EB>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+template <int EB, int NEPI>
+__global__ void __launch_bounds__(threads_for(NEPI), 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
           const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_c2,
           const __grid_constant__ CUtensorMap map_aux, const __grid_constant__ TcParams P) {
     constexpr int BK = 128 / EB;            // K elements per 128-byte row
-    constexpr int ATOM = 128 / EB;          // MN elements per MN-major box
     constexpr int KI = 32 / EB;             // K elements per MMA instruction
     constexpr uint32_t BOX = BK * 128;      // bytes of one MN-major box {ATOM, BK}
     // MN-major K-direction atom: 8 rows (bf16, 128B swizzle) or 4 rows
@@ -292,8 +314,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int S = P.stages;
-    uint8_t* staging = smem + (size_t)S * P.stage_bytes;          // NUM_EPI x STAGE_W
-    uint8_t* auxbuf = staging + (P.tma_out ? NUM_EPI * STAGE_W : 0); // 2 x aux_bytes
+    constexpr int EPI_GROUPS = NEPI / 4;    // warps sharing a quadrant split its 32-column chunks
+    uint8_t* staging = smem + (size_t)S * P.stage_bytes;          // NEPI x STAGE_W
+    uint8_t* auxbuf = staging + (P.tma_out ? NEPI * STAGE_W : 0); // 2 x aux_bytes
     uint64_t* bars = (uint64_t*)(auxbuf + (P.aux_tma ? 2 * P.aux_bytes : 0));
     // bars: full[S], empty[S], tfull[2], tempty[2], drain[1], afull[2], aempty[2]
     uint32_t* tmem_slot = (uint32_t*)(bars + 2 * S + 9);
@@ -311,9 +334,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; i++) { mbar_init(full0 + 8 * i, 1); mbar_init(empty0 + 8 * i, 1); }
-        for (int i = 0; i < 2; i++) { mbar_init(tfull0 + 8 * i, 1); mbar_init(tempty0 + 8 * i, NUM_EPI); }
+        for (int i = 0; i < 2; i++) { mbar_init(tfull0 + 8 * i, 1); mbar_init(tempty0 + 8 * i, NEPI); }
         mbar_init(drain, 1);
-        for (int i = 0; i < 2; i++) { mbar_init(afull0 + 8 * i, 1); mbar_init(aempty0 + 8 * i, NUM_EPI); }
+        for (int i = 0; i < 2; i++) { mbar_init(afull0 + 8 * i, 1); mbar_init(aempty0 + 8 * i, NEPI); }
         *abort_flag = 0;
         *n_issued = 0;
         *n_consumed = 0;
@@ -369,21 +392,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     uint32_t fb = full0 + 8 * stage;
                     mbar_expect_tx(fb, P.stage_bytes);
                     uint32_t sa = smem_u32(smem + (size_t)stage * P.stage_bytes);
-                    uint32_t sb = sa + P.a_bytes;
                     int k0 = kb * BK;
-                    if (P.a_mn) {
-                        #pragma unroll
-                        for (int j = 0; j < BM / ATOM; j++)
-                            tma_load_2d(sa + j * BOX, &map_a, fb, mt * BM + ATOM * j, k0);
-                    } else {
-                        tma_load_2d(sa, &map_a, fb, k0, mt * BM);
-                    }
-                    if (P.b_mn) {
-                        for (int j = 0; j < P.b_rows / ATOM; j++)
-                            tma_load_2d(sb + j * BOX, &map_b, fb, nt * P.bn + ATOM * j, k0);
-                    } else {
-                        tma_load_2d(sb, &map_b, fb, k0, nt * P.bn);
-                    }
+                    load_operand<EB>(sa, &map_a, fb, P.a_mn, BM, mt * BM, k0);
+                    load_operand<EB>(sa + P.a_bytes, &map_b, fb, P.b_mn, P.b_rows, nt * P.bn, k0);
                     if (++stage == S) { stage = 0; phase ^= 1; }
                     (*n_issued)++;
                 }
@@ -821,7 +832,8 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     P.bias_smem = (PTCG_BIAS_SMEM && a.bias && a.N <= BIAS_SMEM_MAX) ? a.N : 0;
     P.aux_tma = aux_tma && P.splits == 1;
     P.aux_bytes = P.aux_tma ? (uint32_t)(bn / 32) * 8192u : 0u;
-    int budget = 232448 - 1024 - 512 - (P.tma_out ? NUM_EPI * STAGE_W : 0) - P.bias_smem * 4 -
+    P.nepi = a.act != ACT_NONE ? NUM_EPI : NUM_EPI_LIGHT;
+    int budget = 232448 - 1024 - 512 - (P.tma_out ? P.nepi * STAGE_W : 0) - P.bias_smem * 4 -
                  2 * (int)P.aux_bytes;
     P.stages = budget / P.stage_bytes;
     if (P.stages > 6) P.stages = 6;
@@ -853,17 +865,22 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
 
 void launch_tc(const TcPlan& pl, cudaStream_t s) {
     const TcParams& P = pl.P;
-    size_t smem = 1024 + (size_t)P.stages * P.stage_bytes + (P.tma_out ? NUM_EPI * STAGE_W : 0) +
+    size_t smem = 1024 + (size_t)P.stages * P.stage_bytes + (P.tma_out ? P.nepi * STAGE_W : 0) +
                   2 * (size_t)P.aux_bytes + (2 * P.stages + 9) * 8 + 48 + (size_t)P.bias_smem * 4;
     int total = P.m_tiles * P.n_tiles * P.splits;
     int grid = total < g_sms ? total : g_sms;
-    if (pl.eb == 2) {
-        cudaFuncSetAttribute(k_gemm_tc<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        ++g_ptcg_launches, k_gemm_tc<2><<<grid, NUM_THREADS, smem, s>>>(pl.ma, pl.mb, pl.mc, pl.mc2, pl.mx, P);
-    } else {
-        cudaFuncSetAttribute(k_gemm_tc<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        ++g_ptcg_launches, k_gemm_tc<4><<<grid, NUM_THREADS, smem, s>>>(pl.ma, pl.mb, pl.mc, pl.mc2, pl.mx, P);
-    }
+#define PTCG_TC_LAUNCH(EBV, NV)                                                              \
+    do {                                                                                     \
+        cudaFuncSetAttribute(k_gemm_tc<EBV, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                             (int)smem);                                                     \
+        ++g_ptcg_launches, k_gemm_tc<EBV, NV><<<grid, threads_for(NV), smem, s>>>(            \
+            pl.ma, pl.mb, pl.mc, pl.mc2, pl.mx, P);                                          \
+    } while (0)
+    if (pl.eb == 2 && P.nepi == NUM_EPI) PTCG_TC_LAUNCH(2, NUM_EPI);
+    else if (pl.eb == 2) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT);
+    else if (P.nepi == NUM_EPI) PTCG_TC_LAUNCH(4, NUM_EPI);
+    else PTCG_TC_LAUNCH(4, NUM_EPI_LIGHT);
+#undef PTCG_TC_LAUNCH
 }
 
 }  // namespace

@@ -287,7 +287,6 @@ static GemmArgs lin_fwd(int dt, int rows, int in, int out, const void* x, long l
     a.M = rows; a.N = out; a.K = in; a.dtype = dt;
     a.A = x; a.lda = ldx; a.a_kmajor = 1;
     a.B = w.op; a.ldb = w.ld; a.b_kmajor = 1;
-    a.bias = w.p == nullptr ? nullptr : nullptr;
     a.out = y; a.ldo = ldy; a.out_dtype = y_dt;
     return a;
 }
