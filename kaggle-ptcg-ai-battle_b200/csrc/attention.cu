@@ -386,14 +386,15 @@ __global__ void __launch_bounds__(128) k_attn_bwd_mma(
     float* lse2 = kbias + Lp;                       // [Lp] lse (log2 domain), +inf past L
     float* dl = lse2 + Lp;                          // [Lp] delta = dO . O
     int* kany = (int*)(dl + Lp);                    // [nkb]
-    float* cs = (float*)(kany + nkb);               // [3][32] bias-grad column sums
+    int* qany = kany + nkb;                         // [nkb] query block has a nonzero dO row
+    float* cs = (float*)(qany + nkb);               // [3][32] bias-grad column sums
     const bf16* base = qkv + (long)n * L * ldqkv + h * DH;
     stage_rows(Qs, base, ldqkv, L, Lp);
     stage_rows(Ks, base + D, ldqkv, L, Lp);
     stage_rows(Vs, base + 2 * D, ldqkv, L, Lp);
     stage_rows(Gs, dout + (long)n * L * lddo + h * DH, lddo, L, Lp);
     const uint8_t* kp = keep + (long)n * L;
-    for (int i = threadIdx.x; i < nkb; i += blockDim.x) kany[i] = 0;
+    for (int i = threadIdx.x; i < nkb; i += blockDim.x) kany[i] = qany[i] = 0;
     for (int i = threadIdx.x; i < 96; i += blockDim.x) cs[i] = 0.f;
     __syncthreads();
     const float* lrow = lse + ((long)n * H + h) * L;
@@ -405,16 +406,23 @@ __global__ void __launch_bounds__(128) k_attn_bwd_mma(
         if (k) kany[j >> 4] = 1;
         lse2[j] = j < L ? lrow[j] * LOG2E : INFINITY;
     }
-    // delta_i = dO_i . O_i: four threads per row, 16-byte loads, shuffle sum
+    // delta_i = dO_i . O_i: four threads per row, 16-byte loads, shuffle sum.
+    // A query block whose dO rows are all zero (rows nothing downstream
+    // reads, e.g. padding) contributes exactly nothing to dQ, dK or dV
+    // (dP = dO V^T = 0 and delta = 0, so dS = 0): qany marks the others.
     for (int i0 = 0; i0 < Lp * 4; i0 += blockDim.x) {
         int i = i0 + threadIdx.x, r = i >> 2, c = (i & 3) * 8;
         float d = 0.f;
-        if (r < L)
-            d = dot8_bf16(*(const uint4*)(orow + (long)r * ldo + c),
-                          *(const uint4*)(grow + (long)r * lddo + c));
+        bool nz = false;
+        if (r < L) {
+            const uint4 gv = *(const uint4*)(grow + (long)r * lddo + c);
+            d = dot8_bf16(*(const uint4*)(orow + (long)r * ldo + c), gv);
+            nz = ((gv.x | gv.y | gv.z | gv.w) & 0x7fff7fffu) != 0u;   // +-0 count as zero
+        }
         d += __shfl_xor_sync(0xffffffffu, d, 1);
         d += __shfl_xor_sync(0xffffffffu, d, 2);
         if ((i & 3) == 0 && r < Lp) dl[r] = d;
+        if (nz) qany[r >> 4] = 1;
     }
     cp_async_wait_all();
     __syncthreads();
@@ -441,6 +449,7 @@ __global__ void __launch_bounds__(128) k_attn_bwd_mma(
             lda(va[1], Vs, kb * 16, 16, lane);
             float kb0 = kbias[kb * 16 + g], kb1 = kbias[kb * 16 + g + 8];
             for (int qb = 0; qb < nkb; qb++) {
+                if (!qany[qb]) continue;
                 float s[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
                 float dp[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
                 #pragma unroll
@@ -518,7 +527,8 @@ __global__ void __launch_bounds__(128) k_attn_bwd_mma(
         lda(ga[1], Gs, qb * 16, 16, lane);
         int q0 = qb * 16 + g, q1 = q0 + 8;
         float la = lse2[q0], lb = lse2[q1], da = dl[q0], dd = dl[q1];
-        for (int kb = 0; kb < nkb; kb++) {
+        const int nkq = qany[qb] ? nkb : 0;         // all-zero dO rows: dQ = 0
+        for (int kb = 0; kb < nkq; kb++) {
             if (!kany[kb]) continue;
             float s[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
             float dp[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
@@ -605,7 +615,7 @@ size_t fwd_mma_smem(int L) {
 }
 size_t bwd_mma_smem(int L) {
     int Lp = (L + 15) & ~15;
-    return (size_t)4 * Lp * RS * 2 + 3 * Lp * 4 + (Lp / 16) * 4 + 96 * 4 + 16;
+    return (size_t)4 * Lp * RS * 2 + 3 * Lp * 4 + 2 * (Lp / 16) * 4 + 96 * 4 + 16;
 }
 
 size_t fwd_smem(int L) {

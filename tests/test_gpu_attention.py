@@ -61,3 +61,48 @@ def test_attention_matches_sdpa(pkg, dtype, L, H):
         cs = dbias[part * D:(part + 1) * D]
         scale = b.abs().sum(0).norm().item()
         assert (cs - b.sum(0)).norm().item() <= (3e-2 if dtype == "bf16" else 1e-4) * scale, part
+
+
+@pytest.mark.parametrize("L,H", [(129, 8), (186, 8), (33, 4)])
+def test_attention_bwd_zero_dout_blocks(pkg, L, H):
+    """Query blocks whose dO rows are all zero (unread rows such as padding)
+    are skipped by the bf16 backward: the result must equal the dense one,
+    with exactly zero dQ on those rows."""
+    import ptcg_b200.native as n
+    lib = n.lib()
+    torch.manual_seed(L + H)
+    nseq, D = 4, H * 32
+    qkv = torch.randn(nseq * L, 3 * D, device="cuda").to(torch.bfloat16)
+    keep = torch.rand(nseq, L, device="cuda") < 0.8
+    keep[:, 0] = True
+    nvalid = [L, L // 2, L - 17, 5]
+    for i, nv in enumerate(nvalid):
+        keep[i, nv:] = False                          # padded suffix
+    keep_u8 = keep.to(torch.uint8).contiguous()
+    out = torch.zeros(nseq * L, D, device="cuda", dtype=torch.bfloat16)
+    lse = torch.zeros(nseq, H, L, device="cuda")
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert lib.ptcg_attention_fwd(1, _p(qkv), 3 * D, _p(keep_u8), _p(out), D, _p(lse), nseq, L, H, s) == 0
+    dout = torch.randn(nseq * L, D, device="cuda")
+    rowmask = torch.ones(nseq, L, device="cuda")
+    for i, nv in enumerate(nvalid):
+        rowmask[i, nv:] = 0                           # nothing reads the padded rows
+    rowmask[0, 16:48] = 0                             # and two whole blocks in the middle
+    dout = (dout * rowmask.view(-1, 1)).to(torch.bfloat16)
+    dout[rowmask.view(-1) == 0] = -0.0                # negative zero counts as zero
+    q, k, v = qkv.float().view(nseq, L, 3, H, 32).permute(2, 0, 3, 1, 4).unbind(0)
+    q.requires_grad_(True); k.requires_grad_(True); v.requires_grad_(True)
+    ref = F.scaled_dot_product_attention(q, k, v, attn_mask=keep.view(nseq, 1, 1, L))
+    ref.transpose(1, 2).reshape(nseq * L, D).backward(dout.float())
+    dqkv = torch.full_like(qkv, 7.0)                  # every element must be written
+    dbias = torch.zeros(3 * D, device="cuda")
+    assert lib.ptcg_attention_bwd(1, _p(qkv), 3 * D, _p(keep_u8), _p(out), D, _p(dout), D,
+                                  _p(lse), _p(dqkv), 3 * D, _p(dbias), nseq, L, H, s) == 0
+    torch.cuda.synchronize()
+    refd = torch.stack([q.grad, k.grad, v.grad], 2).permute(0, 3, 2, 1, 4).reshape(nseq * L, 3 * D)
+    for part in range(3):
+        a = dqkv.float()[:, part * D:(part + 1) * D]
+        b = refd[:, part * D:(part + 1) * D]
+        assert (a - b).norm().item() / b.norm().item() < 3e-2, part
+    zero_rows = rowmask.view(-1) == 0
+    assert (dqkv.float()[zero_rows, :D] == 0).all()
