@@ -64,7 +64,7 @@ __device__ int g_tc_error_dev;
 // free slots, 1 MMA waiting on loaded slots, 2 MMA waiting on a free TMEM
 // buffer, 3 epilogue waiting on a finished accumulator, 4 epilogue working,
 // 5 CTA lifetime, 6 tiles, 7 launches
-__device__ unsigned long long g_tc_prof[12];   // 8: TMEM load, 9: math, 10: store path
+__device__ unsigned long long g_tc_prof[12];   // 8..11 unused
 __device__ int g_tc_prof_on;
 
 struct TcParams {
@@ -82,6 +82,7 @@ struct TcParams {
     int aux_tma;             // the GELU' operand arrives by TMA into two smem slots
     uint32_t aux_bytes;      // bytes of one slot: BM rows x bn bf16, as bn/32 boxes of 8 KB
     int nepi;                // epilogue warps of the instantiation that runs the plan
+    int ek;                  // epilogue kind (EPI_*) of that instantiation
     GemmArgs ep;
 };
 
@@ -299,7 +300,11 @@ PTCG_DEV void load_operand(uint32_t dst, const CUtensorMap* map, uint32_t bar, i
 
 // -------------------------------------------------------------- the kernel
 // EB = operand element bytes (2: bf16 / kind::f16, 4: fp32 / kind::tf32)
-template <int EB, int NEPI>
+// epilogue kinds with a specialised chunk loop (compile-time), the rest
+// through the generic one
+enum { EPI_GENERIC = 0, EPI_GELU_SAVE = 1, EPI_GELU_AUX = 2 };
+
+template <int EB, int NEPI, int EK>
 __global__ void __launch_bounds__(threads_for(NEPI), 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
           const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_c2,
@@ -457,7 +462,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
         const GemmArgs& a = P.ep;
         int local = 0;
         int nchunk = 0;
-        long long w_tfull = 0, busy = 0, c_ld = 0, c_math = 0, c_st = 0;
+        long long w_tfull = 0, busy = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, local++) {
             int split = t % P.splits;
             int mn = t / P.splits;
@@ -479,10 +484,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             const uint32_t tbase = tmem + buf * P.acc_stride + ((uint32_t)(quad * 32) << 16);
             for (int c0 = grp * 32; c0 < P.bn; c0 += 32 * EPI_GROUPS) {
                 uint32_t r[32];
-                long long ck0 = clock64();
                 tmem_ld32(tbase + c0, r);
-                long long ck1 = clock64();
-                c_ld += ck1 - ck0;
                 const int n0 = nt * P.bn + c0;
                 float v[32];
                 #pragma unroll
@@ -495,6 +497,81 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 if (nvalid > P.bn - c0) nvalid = P.bn - c0;
                 if (nvalid > 32) nvalid = 32;
                 if (nvalid <= 0) continue;                       // warp-uniform
+                if constexpr (EK == EPI_GELU_SAVE) {
+                    // bias (staged in smem) + GELU, GELU' saved; bf16 out and
+                    // out2 through the staging buffer and TMA stores (rows
+                    // past M are computed on zero-filled operands and clipped)
+                    uint8_t* sbuf = staging + (warp - 2) * STAGE_W + (nchunk % STAGE_BUFS) * 4096;
+                    nchunk++;
+                    if (lane == 0) {
+                        if (STAGE_BUFS == 2) bulk_wait_read1();
+                        else bulk_wait_read0();
+                    }
+                    __syncwarp();
+                    if (nvalid == 32) {
+                        #pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            float4 b4 = *(const float4*)(sbias + n0 + j);
+                            v[j] += b4.x; v[j + 1] += b4.y; v[j + 2] += b4.z; v[j + 3] += b4.w;
+                        }
+                    } else {
+                        #pragma unroll
+                        for (int j = 0; j < 32; j++) if (j < nvalid) v[j] += sbias[n0 + j];
+                    }
+                    float g[32];
+                    #pragma unroll
+                    for (int j = 0; j < 32; j += 2)
+                        gelu2(v[j], v[j + 1], v[j], v[j + 1], g[j], g[j + 1]);
+                    stage32(sbuf + 2048, lane, DT_BF16, g);
+                    stage32(sbuf, lane, DT_BF16, v);
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        const int y = mt * BM + quad * 32;
+                        tma_store_2d(&map_c, smem_u32(sbuf), n0, y);
+                        tma_store_2d(&map_c2, smem_u32(sbuf + 2048), n0, y);
+                        bulk_commit();
+                    }
+                    continue;
+                } else if constexpr (EK == EPI_GELU_AUX) {
+                    // v *= GELU' (prefetched by TMA into the tile's aux slot),
+                    // out through staging + TMA store, optional fp32 column sums
+                    uint8_t* sbuf = staging + (warp - 2) * STAGE_W + (nchunk % STAGE_BUFS) * 4096;
+                    nchunk++;
+                    if (lane == 0) {
+                        if (STAGE_BUFS == 2) bulk_wait_read1();
+                        else bulk_wait_read0();
+                    }
+                    __syncwarp();
+                    // row row_in_tile of box c0 / 32 (64-byte rows, 64-byte swizzle)
+                    const uint8_t* ab = auxbuf + (size_t)buf * P.aux_bytes + (c0 >> 5) * 8192 +
+                                        row_in_tile * 64;
+                    #pragma unroll
+                    for (int gq = 0; gq < 4; gq++) {
+                        uint4 q = *(const uint4*)(ab + ((gq ^ ((row_in_tile >> 1) & 3)) << 4));
+                        const __nv_bfloat162* h2 = (const __nv_bfloat162*)&q;
+                        #pragma unroll
+                        for (int k = 0; k < 4; k++) {
+                            float2 f = __bfloat1622float2(h2[k]);
+                            v[8 * gq + 2 * k] *= f.x;
+                            v[8 * gq + 2 * k + 1] *= f.y;
+                        }
+                    }
+                    stage32(sbuf, lane, a.out_dtype, v);
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&map_c, smem_u32(sbuf), n0, mt * BM + quad * 32);
+                        bulk_commit();
+                    }
+                    if (a.colsum) {
+                        #pragma unroll
+                        for (int j = 0; j < 32; j++) if (j >= nvalid || !row_ok) v[j] = 0.f;
+                        float cs = warp_colsum32(v, lane);
+                        if (lane < nvalid) atomicAdd(&a.colsum[n0 + lane], cs);
+                    }
+                    continue;
+                }
                 if (P.splits > 1) {                              // warp-uniform
                     if (row_ok) {
                         float* o = (float*)a.out + orow * a.ldo + n0;
@@ -516,7 +593,6 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 // with one, the previous store must have finished reading
                 uint8_t* sbuf = staging + (warp - 2) * STAGE_W + (nchunk % STAGE_BUFS) * 4096;
                 nchunk++;
-                long long ck2 = clock64();
                 if (P.tma_out) {
                     if (lane == 0) {
                         if (STAGE_BUFS == 2) bulk_wait_read1();
@@ -524,8 +600,6 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     }
                     __syncwarp();
                 }
-                long long ck3 = clock64();
-                c_st += ck3 - ck2;
                 if (row_ok) {
                 float t[32];
                 if (a.bias) {
@@ -601,8 +675,6 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 if (!P.tma_out && a.act != ACT_GELU && a.out2)
                     store32(a.out2, orow * a.ldo2 + n0, a.out2_dtype, v, nvalid);
                 }   // row_ok
-                long long ck4 = clock64();
-                c_math += ck4 - ck3;
                 if (P.tma_out) {
                     // rows past M and columns past N are clipped by the TMA unit
                     fence_async_smem();
@@ -633,9 +705,6 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
         if (P.tma_out && lane == 0) bulk_wait_all();
         if (g_tc_prof_on && lane == 0) {
             atomicAdd(&g_tc_prof[3], (unsigned long long)w_tfull);
-            atomicAdd(&g_tc_prof[8], (unsigned long long)c_ld);
-            atomicAdd(&g_tc_prof[9], (unsigned long long)c_math);
-            atomicAdd(&g_tc_prof[10], (unsigned long long)c_st);
             atomicAdd(&g_tc_prof[4], (unsigned long long)busy);
         }
     }
@@ -833,6 +902,16 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     P.aux_tma = aux_tma && P.splits == 1;
     P.aux_bytes = P.aux_tma ? (uint32_t)(bn / 32) * 8192u : 0u;
     P.nepi = a.act != ACT_NONE ? NUM_EPI : NUM_EPI_LIGHT;
+    // specialised epilogues: exactly the argument sets of the FFN1 forward
+    // (bias + GELU + saved GELU') and the FFN2 dX (GELU' multiply + FFN1
+    // bias column sums) of the transformer blocks in bf16
+    const bool simple = eb == 2 && P.tma_out && a.alpha == 1.f && !a.bcast && !a.resid &&
+                        !a.accumulate && a.remap_group == 0 && P.splits == 1;
+    P.ek = EPI_GENERIC;
+    if (simple && a.act == ACT_GELU && a.out2 && P.bias_smem > 0 && !a.colsum)
+        P.ek = EPI_GELU_SAVE;
+    else if (simple && a.act == ACT_GELU_BWD && P.aux_tma && !a.bias && !a.out2)
+        P.ek = EPI_GELU_AUX;
     int budget = 232448 - 1024 - 512 - (P.tma_out ? P.nepi * STAGE_W : 0) - P.bias_smem * 4 -
                  2 * (int)P.aux_bytes;
     P.stages = budget / P.stage_bytes;
@@ -869,17 +948,19 @@ void launch_tc(const TcPlan& pl, cudaStream_t s) {
                   2 * (size_t)P.aux_bytes + (2 * P.stages + 9) * 8 + 48 + (size_t)P.bias_smem * 4;
     int total = P.m_tiles * P.n_tiles * P.splits;
     int grid = total < g_sms ? total : g_sms;
-#define PTCG_TC_LAUNCH(EBV, NV)                                                              \
+#define PTCG_TC_LAUNCH(EBV, NV, EKV)                                                         \
     do {                                                                                     \
-        cudaFuncSetAttribute(k_gemm_tc<EBV, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
-                             (int)smem);                                                     \
-        ++g_ptcg_launches, k_gemm_tc<EBV, NV><<<grid, threads_for(NV), smem, s>>>(            \
+        cudaFuncSetAttribute(k_gemm_tc<EBV, NV, EKV>,                                        \
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);        \
+        ++g_ptcg_launches, k_gemm_tc<EBV, NV, EKV><<<grid, threads_for(NV), smem, s>>>(       \
             pl.ma, pl.mb, pl.mc, pl.mc2, pl.mx, P);                                          \
     } while (0)
-    if (pl.eb == 2 && P.nepi == NUM_EPI) PTCG_TC_LAUNCH(2, NUM_EPI);
-    else if (pl.eb == 2) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT);
-    else if (P.nepi == NUM_EPI) PTCG_TC_LAUNCH(4, NUM_EPI);
-    else PTCG_TC_LAUNCH(4, NUM_EPI_LIGHT);
+    if (P.ek == EPI_GELU_SAVE) PTCG_TC_LAUNCH(2, NUM_EPI, EPI_GELU_SAVE);
+    else if (P.ek == EPI_GELU_AUX) PTCG_TC_LAUNCH(2, NUM_EPI, EPI_GELU_AUX);
+    else if (pl.eb == 2 && P.nepi == NUM_EPI) PTCG_TC_LAUNCH(2, NUM_EPI, EPI_GENERIC);
+    else if (pl.eb == 2) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_GENERIC);
+    else if (P.nepi == NUM_EPI) PTCG_TC_LAUNCH(4, NUM_EPI, EPI_GENERIC);
+    else PTCG_TC_LAUNCH(4, NUM_EPI_LIGHT, EPI_GENERIC);
 #undef PTCG_TC_LAUNCH
 }
 
