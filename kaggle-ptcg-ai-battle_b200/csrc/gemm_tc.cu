@@ -302,7 +302,8 @@ PTCG_DEV void load_operand(uint32_t dst, const CUtensorMap* map, uint32_t bar, i
 // EB = operand element bytes (2: bf16 / kind::f16, 4: fp32 / kind::tf32)
 // epilogue kinds with a specialised chunk loop (compile-time), the rest
 // through the generic one
-enum { EPI_GENERIC = 0, EPI_GELU_SAVE = 1, EPI_GELU_AUX = 2 };
+enum { EPI_GENERIC = 0, EPI_GELU_SAVE = 1, EPI_GELU_AUX = 2,
+       EPI_PLAIN = 3, EPI_BIAS = 4, EPI_RESID = 5, EPI_BIAS_RESID = 6 };  // 3 + bias + 2 resid
 
 template <int EB, int NEPI, int EK>
 __global__ void __launch_bounds__(threads_for(NEPI), 1)
@@ -555,6 +556,51 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                             float2 f = __bfloat1622float2(h2[k]);
                             v[8 * gq + 2 * k] *= f.x;
                             v[8 * gq + 2 * k + 1] *= f.y;
+                        }
+                    }
+                    stage32(sbuf, lane, a.out_dtype, v);
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&map_c, smem_u32(sbuf), n0, mt * BM + quad * 32);
+                        bulk_commit();
+                    }
+                    if (a.colsum) {
+                        #pragma unroll
+                        for (int j = 0; j < 32; j++) if (j >= nvalid || !row_ok) v[j] = 0.f;
+                        float cs = warp_colsum32(v, lane);
+                        if (lane < nvalid) atomicAdd(&a.colsum[n0 + lane], cs);
+                    }
+                    continue;
+                } else if constexpr (EK >= EPI_PLAIN) {
+                    // [bias (smem)] [+ fp32 residual] -> out through staging +
+                    // TMA store, optional fp32 column sums
+                    constexpr bool HB = (EK - EPI_PLAIN) & 1, HR = (EK - EPI_PLAIN) & 2;
+                    uint8_t* sbuf = staging + (warp - 2) * STAGE_W + (nchunk % STAGE_BUFS) * 4096;
+                    nchunk++;
+                    if (lane == 0) {
+                        if (STAGE_BUFS == 2) bulk_wait_read1();
+                        else bulk_wait_read0();
+                    }
+                    __syncwarp();
+                    if constexpr (HB) {
+                        if (nvalid == 32) {
+                            #pragma unroll
+                            for (int j = 0; j < 32; j += 4) {
+                                float4 b4 = *(const float4*)(sbias + n0 + j);
+                                v[j] += b4.x; v[j + 1] += b4.y; v[j + 2] += b4.z; v[j + 3] += b4.w;
+                            }
+                        } else {
+                            #pragma unroll
+                            for (int j = 0; j < 32; j++) if (j < nvalid) v[j] += sbias[n0 + j];
+                        }
+                    }
+                    if constexpr (HR) {
+                        if (row_ok) {
+                            float t[32];
+                            load32(t, a.resid, (long)m * a.ld_resid + n0, DT_F32, nvalid);
+                            #pragma unroll
+                            for (int j = 0; j < 32; j++) v[j] += t[j];
                         }
                     }
                     stage32(sbuf, lane, a.out_dtype, v);
@@ -905,13 +951,15 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     // specialised epilogues: exactly the argument sets of the FFN1 forward
     // (bias + GELU + saved GELU') and the FFN2 dX (GELU' multiply + FFN1
     // bias column sums) of the transformer blocks in bf16
-    const bool simple = eb == 2 && P.tma_out && a.alpha == 1.f && !a.bcast && !a.resid &&
+    const bool simple = eb == 2 && P.tma_out && a.alpha == 1.f && !a.bcast &&
                         !a.accumulate && a.remap_group == 0 && P.splits == 1;
     P.ek = EPI_GENERIC;
-    if (simple && a.act == ACT_GELU && a.out2 && P.bias_smem > 0 && !a.colsum)
+    if (simple && a.act == ACT_GELU && a.out2 && P.bias_smem > 0 && !a.colsum && !a.resid)
         P.ek = EPI_GELU_SAVE;
-    else if (simple && a.act == ACT_GELU_BWD && P.aux_tma && !a.bias && !a.out2)
+    else if (simple && a.act == ACT_GELU_BWD && P.aux_tma && !a.bias && !a.out2 && !a.resid)
         P.ek = EPI_GELU_AUX;
+    else if (simple && a.act == ACT_NONE && !a.out2 && (!a.bias || P.bias_smem > 0))
+        P.ek = EPI_PLAIN + (a.bias ? 1 : 0) + (a.resid ? 2 : 0);
     int budget = 232448 - 1024 - 512 - (P.tma_out ? P.nepi * STAGE_W : 0) - P.bias_smem * 4 -
                  2 * (int)P.aux_bytes;
     P.stages = budget / P.stage_bytes;
@@ -957,6 +1005,10 @@ void launch_tc(const TcPlan& pl, cudaStream_t s) {
     } while (0)
     if (P.ek == EPI_GELU_SAVE) PTCG_TC_LAUNCH(2, NUM_EPI, EPI_GELU_SAVE);
     else if (P.ek == EPI_GELU_AUX) PTCG_TC_LAUNCH(2, NUM_EPI, EPI_GELU_AUX);
+    else if (P.ek == EPI_PLAIN) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_PLAIN);
+    else if (P.ek == EPI_BIAS) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_BIAS);
+    else if (P.ek == EPI_RESID) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_RESID);
+    else if (P.ek == EPI_BIAS_RESID) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_BIAS_RESID);
     else if (pl.eb == 2 && P.nepi == NUM_EPI) PTCG_TC_LAUNCH(2, NUM_EPI, EPI_GENERIC);
     else if (pl.eb == 2) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_GENERIC);
     else if (P.nepi == NUM_EPI) PTCG_TC_LAUNCH(4, NUM_EPI, EPI_GENERIC);
