@@ -171,6 +171,26 @@ def cpu_oracle_step_rate(pkg, s, rows, seconds, threads):
     return rows / med, len(times), med
 
 
+def cpu_oracle_rollout_rate(pkg, s, rows, seconds, threads):
+    """Observations/s of the CPU oracle's rollout forward (forward_eval under
+    no_grad) on `rows` config-shaped observations, median over ~`seconds`."""
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ptcg_oracle as oracle
+    torch.set_num_threads(threads)
+    P = oracle.params_from_blob(pkg.synth.make_weights(s, 21), s)
+    T = oracle.tables_to_torch(pkg.synth.make_tables(s, 11))
+    obs = torch.from_numpy(pkg.synth.make_obs_batch(s, rows, 6))
+    times = []
+    with torch.no_grad():
+        oracle.forward_eval(P, T, obs, s)           # warm-up
+        t_end = time.time() + seconds
+        while time.time() < t_end or len(times) < 2:
+            t0 = time.time(); oracle.forward_eval(P, T, obs, s); times.append(time.time() - t0)
+    med = float(np.median(times))
+    return rows / med, len(times), med
+
+
 def run_reference(args, pkg):
     """The reference arm: the reference algorithm's CPU implementation (the
     oracle port of ptcg/rl/model.py + PPO + torch Adam) on all host cores;
@@ -485,6 +505,16 @@ def main():
         cpu = {"value": rate, "unit": "samples/s", "cores": threads, "kind": "port",
                "sample": f"64-row PPO train step of the CPU oracle (forward_train + loss + "
                          f"backward + Adam), median of {n} steps ({med:.2f} s/step)"}
+        # the other two CPU figures of the measurement plan: the rollout
+        # forward (config 1 shapes) and the scaled config 4 at 16 rows
+        rr, rn, rmed = cpu_oracle_rollout_rate(pkg, s, 256, args.cpu_seconds / 3, threads)
+        cpu["rollout"] = {"value": rr, "unit": "obs/s",
+                          "sample": f"forward_eval of 256 observations under no_grad, median of "
+                                    f"{rn} ({rmed:.2f} s)"}
+        s4 = pkg.config.PRESETS["c4"]
+        r4, n4, m4 = cpu_oracle_step_rate(pkg, s4, 16, args.cpu_seconds / 3, threads)
+        cpu["c4_train"] = {"value": 1e3 / r4, "unit": "ms/sample",
+                           "sample": f"16-row c4 PPO train step, median of {n4} ({m4:.2f} s/step)"}
     from ptcg_b200.config import train_flops
     flops_exec = train_flops(s, "first")       # what this build runs per sample
     flops_ref = train_flops(s, "all")          # same step with the critic over every row
