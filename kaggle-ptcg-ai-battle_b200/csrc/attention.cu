@@ -256,7 +256,8 @@ constexpr float LOG2E = 1.4426950408889634f;
 
 __global__ void __launch_bounds__(128) k_attn_fwd_mma(
         const bf16* __restrict__ qkv, long ldqkv, const uint8_t* __restrict__ keep,
-        bf16* __restrict__ out, long ldo, float* __restrict__ lse, int L, int H) {
+        bf16* __restrict__ out, long ldo, float* __restrict__ lse, int L, int H,
+        const int* __restrict__ extent) {
     extern __shared__ __align__(16) uint8_t smraw[];
     const int nh = blockIdx.x, n = nh / H, h = nh % H, D = H * DH;
     const int Lp = (L + 15) & ~15, nkb = Lp / 16;
@@ -266,9 +267,12 @@ __global__ void __launch_bounds__(128) k_attn_fwd_mma(
     float* kb_bias = (float*)(Vs + Lp * RS);        // [Lp] 0 or -inf (log2 domain)
     int* kb_any = (int*)(kb_bias + Lp);             // [nkb] block has a kept key
     const bf16* base = qkv + (long)n * L * ldqkv + h * DH;
-    stage_rows(Qs, base, ldqkv, L, Lp);
-    stage_rows(Ks, base + D, ldqkv, L, Lp);
-    stage_rows(Vs, base + 2 * D, ldqkv, L, Lp);
+    // rows at or past the extent are neither queries anyone reads nor kept
+    // keys: they are zero-filled instead of loaded
+    const int ext = extent ? min(extent[n], L) : L;
+    stage_rows(Qs, base, ldqkv, ext, Lp);
+    stage_rows(Ks, base + D, ldqkv, ext, Lp);
+    stage_rows(Vs, base + 2 * D, ldqkv, ext, Lp);
     const uint8_t* kp = keep + (long)n * L;
     for (int i = threadIdx.x; i < nkb; i += blockDim.x) kb_any[i] = 0;
     __syncthreads();
@@ -282,7 +286,19 @@ __global__ void __launch_bounds__(128) k_attn_fwd_mma(
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const float sc = 0.17677669529663687f * LOG2E;
+    // query rows at or past the sequence's extent are read by nothing
+    // downstream: they get zero output (finite for the row-wise layers
+    // after) and a zero log-sum-exp instead of the softmax
     for (int qb = warp; qb < nkb; qb += 4) {
+        if (qb * 16 >= ext) {
+            bf16* ob = out + (long)n * L * ldo + h * DH;
+            for (int i = lane; i < 16 * 4; i += 32) {
+                const int r = qb * 16 + (i >> 2);
+                if (r < L) *(uint4*)(ob + (long)r * ldo + (i & 3) * 8) = make_uint4(0, 0, 0, 0);
+            }
+            if (lane < 16 && qb * 16 + lane < L) lse[((long)n * H + h) * L + qb * 16 + lane] = 0.f;
+            continue;
+        }
         uint32_t qa[2][4];
         lda(qa[0], Qs, qb * 16, 0, lane);
         lda(qa[1], Qs, qb * 16, 16, lane);
@@ -374,10 +390,13 @@ __global__ void __launch_bounds__(128) k_attn_bwd_mma(
         const bf16* __restrict__ qkv, long ldqkv, const uint8_t* __restrict__ keep,
         const bf16* __restrict__ out, long ldo, const bf16* __restrict__ dout, long lddo,
         const float* __restrict__ lse, bf16* __restrict__ dqkv, long lddqkv,
-        float* __restrict__ dbias, int L, int H) {
+        float* __restrict__ dbias, int L, int H, const int* __restrict__ extent) {
     extern __shared__ __align__(16) uint8_t smraw[];
     const int nh = blockIdx.x, n = nh / H, h = nh % H, D = H * DH;
     const int Lp = (L + 15) & ~15, nkb = Lp / 16;
+    // rows at or past the extent: masked keys, and queries whose dO is zero
+    // (nothing reads them): zero-filled instead of loaded
+    const int ext = extent ? min(extent[n], L) : L;
     bf16* Qs = (bf16*)smraw;
     bf16* Ks = Qs + Lp * RS;
     bf16* Vs = Ks + Lp * RS;
@@ -389,10 +408,10 @@ __global__ void __launch_bounds__(128) k_attn_bwd_mma(
     int* qany = kany + nkb;                         // [nkb] query block has a nonzero dO row
     float* cs = (float*)(qany + nkb);               // [3][32] bias-grad column sums
     const bf16* base = qkv + (long)n * L * ldqkv + h * DH;
-    stage_rows(Qs, base, ldqkv, L, Lp);
-    stage_rows(Ks, base + D, ldqkv, L, Lp);
-    stage_rows(Vs, base + 2 * D, ldqkv, L, Lp);
-    stage_rows(Gs, dout + (long)n * L * lddo + h * DH, lddo, L, Lp);
+    stage_rows(Qs, base, ldqkv, ext, Lp);
+    stage_rows(Ks, base + D, ldqkv, ext, Lp);
+    stage_rows(Vs, base + 2 * D, ldqkv, ext, Lp);
+    stage_rows(Gs, dout + (long)n * L * lddo + h * DH, lddo, ext, Lp);
     const uint8_t* kp = keep + (long)n * L;
     for (int i = threadIdx.x; i < nkb; i += blockDim.x) kany[i] = qany[i] = 0;
     for (int i = threadIdx.x; i < 96; i += blockDim.x) cs[i] = 0.f;
@@ -414,7 +433,7 @@ __global__ void __launch_bounds__(128) k_attn_bwd_mma(
         int i = i0 + threadIdx.x, r = i >> 2, c = (i & 3) * 8;
         float d = 0.f;
         bool nz = false;
-        if (r < L) {
+        if (r < ext) {
             const uint4 gv = *(const uint4*)(grow + (long)r * lddo + c);
             d = dot8_bf16(*(const uint4*)(orow + (long)r * ldo + c), gv);
             nz = ((gv.x | gv.y | gv.z | gv.w) & 0x7fff7fffu) != 0u;   // +-0 count as zero
@@ -830,7 +849,8 @@ void set_smem(K k, size_t bytes) {
 }  // namespace
 
 void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
-              void* out, long ldo, float* lse, int nseq, int L, int H, cudaStream_t s) {
+              void* out, long ldo, float* lse, int nseq, int L, int H, cudaStream_t s,
+              const int* extent) {
     if (nseq <= 0) return;
     size_t sm = fwd_smem(L);
     if (dtype == DT_F32) {
@@ -841,7 +861,7 @@ void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
         size_t sm2 = fwd_mma_smem(L);
         set_smem(k_attn_fwd_mma, sm2);
         ++g_ptcg_launches, k_attn_fwd_mma<<<nseq * H, 128, sm2, s>>>((const bf16*)qkv, ldqkv, keep,
-            (bf16*)out, ldo, lse, L, H);
+            (bf16*)out, ldo, lse, L, H, extent);
     }
 }
 
@@ -885,7 +905,7 @@ void attn_row0_bwd(int dtype, const void* q, long ldq, const void* kv, long ldkv
 void attn_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
               const void* out, long ldo, const void* dout, long lddo,
               const float* lse, void* dqkv, long lddqkv, float* dbias, int nseq, int L, int H,
-              cudaStream_t s) {
+              cudaStream_t s, const int* extent) {
     if (nseq <= 0) return;
     size_t sm = bwd_smem(L);
     if (dtype == DT_F32) {
@@ -896,6 +916,7 @@ void attn_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
         size_t sm2 = bwd_mma_smem(L);
         set_smem(k_attn_bwd_mma, sm2);
         ++g_ptcg_launches, k_attn_bwd_mma<<<nseq * H, 128, sm2, s>>>((const bf16*)qkv, ldqkv, keep,
-            (const bf16*)out, ldo, (const bf16*)dout, lddo, lse, (bf16*)dqkv, lddqkv, dbias, L, H);
+            (const bf16*)out, ldo, (const bf16*)dout, lddo, lse, (bf16*)dqkv, lddqkv, dbias, L, H,
+            extent);
     }
 }

@@ -51,9 +51,11 @@ int ptcg_tc_error_read_reset();
 int ptcg_tc_profile_ctl(int enable, unsigned long long* out8);
 
 // attention over packed qkv rows: qkv [(n*L + l) * ldqkv + {0,D,2D} + h*32 + d]
+// extent (nullable, bf16 path): per sequence, the rows anything reads;
+// query rows at or past it get zero output and a zero log-sum-exp
 void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
               void* out, long ldo, float* lse, int nseq, int L, int H,
-              cudaStream_t s);
+              cudaStream_t s, const int* extent = nullptr);
 // first query row of each sequence only: q row of sequence n at
 // q + n * ldq, keys / values as rows [K | V] of kv (row stride ldkv,
 // sequence n at rows n * L ..); out / dout [n * ldo + h*32 + d], lse
@@ -70,4 +72,4 @@ void attn_row0_bwd(int dtype, const void* q, long ldq, const void* kv, long ldkv
 void attn_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
               const void* out, long ldo, const void* dout, long lddo,
               const float* lse, void* dqkv, long lddqkv, float* dbias, int nseq, int L,
-              int H, cudaStream_t s);
+              int H, cudaStream_t s, const int* extent = nullptr);

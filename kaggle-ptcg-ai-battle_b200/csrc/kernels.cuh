@@ -356,6 +356,29 @@ __global__ void k_x0_readout(float* x0, uint8_t* keep, const float* readout,
     }
 }
 
+// Rows of each trunk sequence that anything reads: 1 + the largest of the
+// last kept row (readout row 0 and tokens with zone > 0: attention keys,
+// the aux heads' rows) and the largest option pointer in [1, LTOK] (the
+// gathers of ln_f rows).  Rows past it are read by nothing (masked as keys,
+// never gathered), so the attention forward may skip them.  One warp per
+// sequence.
+__global__ void k_row_extent(int* ext, const uint8_t* keep, const float* obs, ObsLayout L, int R) {
+    const int n = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (n >= R) return;
+    int e = 0;
+    for (int l = lane; l < L.lseq; l += 32)
+        if (keep[(long)n * L.lseq + l]) e = max(e, l);
+    const float* oi = obs + (long)n * L.obs + L.opti;
+    for (int j = lane; j < L.nopt; j += 32) {
+        const int p1 = (int)oi[j * 6 + 1], p2 = (int)oi[j * 6 + 2];
+        if (p1 >= 1 && p1 <= L.ltok) e = max(e, p1);
+        if (p2 >= 1 && p2 <= L.ltok) e = max(e, p2);
+    }
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) e = max(e, __shfl_xor_sync(0xffffffffu, e, o));
+    if (lane == 0) ext[n] = e + 1;
+}
+
 // decision-encoder input (696): [sel8, ctx32, cv_eff, cv_ctx, av_my, av_opp,
 // cv_msup, cv_osup, decf16] (k_dec_in, ptcg_model.cu:324-344)
 __global__ void k_dec_in(float* out, const float* obs, ObsLayout L, const float* cv,

@@ -140,6 +140,7 @@ struct Work {
     void *qin, *q1pre, *q1; void *scin, *s1pre, *s1;
     float *u, *rgd, *wqq, *du, *drgd;   // score1 split: per-sample term, inputs, packed W
     void* otokin; float* xc[2]; BlkAct cblk;
+    int* ext;                                 // [R] trunk rows anything reads (k_row_extent)
     float *ovin, *ov1pre, *ov1; float* out;
     // train-only heads
     float *bvin; void* bvinc; float *bv1pre, *bv1, *blind_v, *hand_lin, *prize_logit;
@@ -405,6 +406,7 @@ static void plan_work(Work& W, Bump& m, int R, bool train, const Dims& z, int es
          NC = (long)R * z.LCRIT;
     W.tokcat = m.take(NT * rup(z.TOK_IN, 8) * esz);
     W.keep = (uint8_t*)m.take(NS);
+    W.ext = (int*)m.take((long)R * sizeof(int));
     W.ckeep = (uint8_t*)m.take(NC);
     W.g1pre = m.f((long)R * 128); W.g1 = m.f((long)R * 128);
     W.gd = m.f((long)R * 192);
@@ -542,8 +544,9 @@ static void tables_fwd(PtcgModel* M, cudaStream_t s) {
     gemm32(M, a, s);
 }
 
+// ext (nullable): per sequence, the rows anything reads (k_row_extent)
 static void block_fwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* keep, int R, int L,
-                      bool train, cudaStream_t s) {
+                      bool train, cudaStream_t s, const int* ext = nullptr) {
     const Dims& z = M->z;
     const int dt = M->dt(), D = z.D;
     const int NL = R * L;
@@ -551,7 +554,7 @@ static void block_fwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
     GemmArgs a = lin_fwd(dt, NL, D, 3 * D, b.ln1, D, P.qkvw, b.qkv, 3 * D, dt);
     a.bias = P.qkvb.p;
     gemm(M, a, s);
-    attn_fwd(dt, b.qkv, 3 * D, keep, b.att, D, b.lse, R, L, z.H, s);
+    attn_fwd(dt, b.qkv, 3 * D, keep, b.att, D, b.lse, R, L, z.H, s, ext);
     a = lin_fwd(dt, NL, D, D, b.att, D, P.projw, b.xm, D, DT_F32);
     a.bias = P.projb.p; a.resid = b.x_in; a.ld_resid = D;
     gemm(M, a, s);
@@ -622,6 +625,7 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
             M->w("zone_emb").p, M->w("owner_emb").p, R, z.TOK_IN);
     ++g_ptcg_launches, k_x0_readout<<<cdiv((long)R * (z.LSEQ > D ? z.LSEQ : D), TPB), TPB, 0, s>>>(Wk.x[0], Wk.keep,
         M->w("readout").p, obs, ol, R, D);
+    ++g_ptcg_launches, k_row_extent<<<cdiv(R, TPB / 32), TPB, 0, s>>>(Wk.ext, Wk.keep, obs, ol, R);
     // --- global / decision encoders (fp32)
     GemmArgs a = lin_fwd(DT_F32, R, 64, 128, obs + ol.glob, ol.obs, f32w(M->w("global1_w"), 64),
                          Wk.g1, 128, DT_F32);
@@ -653,7 +657,7 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
         BlkAct& b = train ? Wk.blk[i] : Wk.blk[0];
         b.x_in = train ? Wk.x[i] : Wk.x[i % 2];
         b.x_out = train ? Wk.x[i + 1] : Wk.x[(i + 1) % 2];
-        block_fwd(M, M->blk("b" + std::to_string(i) + "_"), b, Wk.keep, R, z.LSEQ, train, s);
+        block_fwd(M, M->blk("b" + std::to_string(i) + "_"), b, Wk.keep, R, z.LSEQ, train, s, Wk.ext);
         xl = b.x_out;
     }
     ln_fwd(DT_F32, Wk.h, D, Wk.muf, Wk.rsf, xl, D, M->w("lnf_w").p, M->w("lnf_b").p, R * z.LSEQ, D, s);
@@ -790,7 +794,7 @@ static void block_bwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
     gemm(M, lin_dx(dt, NL, D, D, dxc, D, P.projw, Wk.datt, D, dt), s);
     // attention
     attn_bwd(dt, b.qkv, 3 * D, keep, b.att, D, Wk.datt, D, b.lse, Wk.dqkv, 3 * D, P.qkvb.g,
-             R, L, z.H, s);
+             R, L, z.H, s, Wk.ext);
     // QKV
     gemm(M, lin_dw(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, b.ln1, D, P.qkvw.g), s);
     gemm(M, lin_dx(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, P.qkvw, Wk.dln, D, dt), s);
