@@ -12,7 +12,7 @@ typedef __nv_bfloat16 bf16;
 #define PTCG_EPI_WARPS 16       // epilogue warps per CTA (multiple of 4)
 #endif
 #ifndef PTCG_EPI_WARPS_LIGHT
-#define PTCG_EPI_WARPS_LIGHT 12 // epilogue warps of the GEMMs without GELU math
+#define PTCG_EPI_WARPS_LIGHT 12 // epilogue warps of the GEMMs without a GELU forward
 #endif
 #ifndef PTCG_STAGE_BUFS
 #define PTCG_STAGE_BUFS 1       // TMA-store staging buffers per epilogue warp (1 or 2)

@@ -14,7 +14,7 @@
 //   M=128, N=BN into a double-buffered TMEM accumulator and releases ring
 //   slots with tcgen05.commit.  A 128-byte swizzled row holds 64 bf16 or 32
 //   fp32 K-elements, so both kinds share one byte-level smem layout.
-// * PTCG_EPI_WARPS epilogue warps for the GELU / GELU' epilogues,
+// * PTCG_EPI_WARPS epilogue warps for the GELU forward epilogues,
 //   PTCG_EPI_WARPS_LIGHT for the rest (16 / 12: four / three per TMEM lane
 //   quadrant, each taking every fourth / third 32-column chunk) read the
 //   accumulator with
@@ -44,7 +44,7 @@ namespace {
 
 constexpr int BM = 128;
 // epilogue warps per CTA (a multiple of 4: NEPI / 4 per TMEM lane quadrant,
-// splitting its 32-column chunks).  The GELU / GELU' epilogues are
+// splitting its 32-column chunks).  The GELU forward epilogues are
 // instruction-bound and run PTCG_EPI_WARPS warps; the others run
 // PTCG_EPI_WARPS_LIGHT, whose larger register budget (the 64K registers
 // split over fewer threads) keeps their epilogue free of spills.
@@ -727,6 +727,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     __syncwarp();
                     if (lane == 0) {
                         int y = mt * BM + quad * 32;
+                        if (a.remap_group > 0)                   // the box's first output row
+                            y = (y / a.remap_group) * a.remap_stride + a.remap_off + y % a.remap_group;
                         tma_store_2d(&map_c, smem_u32(sbuf), n0, y);
                         if (a.act == ACT_GELU && a.out2) tma_store_2d(&map_c2, smem_u32(sbuf + 2048), n0, y);
                         bulk_commit();
@@ -940,14 +942,20 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     // outputs through smem + TMA store: plain row mapping, no read-modify-
     // write, whole 32-column chunks per tile, 16-byte aligned pitch
     int oeb = a.out_dtype == DT_F32 ? 4 : 2;
-    P.tma_out = P.splits == 1 && a.remap_group == 0 && !a.accumulate && (bn % 32) == 0 &&
+    // a row remap keeps the TMA store when its groups are whole 32-row boxes
+    // (each box then lands on consecutive output rows); the map then spans
+    // the remapped rows
+    const bool remap_ok = a.remap_group == 0 ||
+        (a.remap_group % 32 == 0 && a.M % a.remap_group == 0 && !a.out2 &&
+         a.remap_off + a.remap_group <= a.remap_stride);
+    P.tma_out = P.splits == 1 && remap_ok && !a.accumulate && (bn % 32) == 0 &&
                 !((uintptr_t)a.out & 15) && (a.ldo * oeb) % 16 == 0 &&
                 (!a.out2 || (a.act == ACT_GELU && a.out2_dtype == DT_BF16 && a.out_dtype == DT_BF16 &&
                              !((uintptr_t)a.out2 & 15) && (a.ldo2 * 2) % 16 == 0));
     P.bias_smem = (PTCG_BIAS_SMEM && a.bias && a.N <= BIAS_SMEM_MAX) ? a.N : 0;
     P.aux_tma = aux_tma && P.splits == 1;
     P.aux_bytes = P.aux_tma ? (uint32_t)(bn / 32) * 8192u : 0u;
-    P.nepi = a.act != ACT_NONE ? NUM_EPI : NUM_EPI_LIGHT;
+    P.nepi = a.act == ACT_GELU ? NUM_EPI : NUM_EPI_LIGHT;
     // specialised epilogues: exactly the argument sets of the FFN1 forward
     // (bias + GELU + saved GELU') and the FFN2 dX (GELU' multiply + FFN1
     // bias column sums) of the transformer blocks in bf16
@@ -984,7 +992,8 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     pl.mc = pl.ma; pl.mc2 = pl.ma; pl.mx = pl.ma;
     if (P.aux_tma && !make_aux_map(&pl.mx, a.aux, a.N, a.M, a.ld_aux)) return false;
     if (P.tma_out) {
-        if (!make_out_map(&pl.mc, a.out, a.N, a.M, a.ldo, a.out_dtype)) return false;
+        const long out_rows = a.remap_group > 0 ? (long)(a.M / a.remap_group) * a.remap_stride : a.M;
+        if (!make_out_map(&pl.mc, a.out, a.N, out_rows, a.ldo, a.out_dtype)) return false;
         if (a.out2 && !make_out_map(&pl.mc2, a.out2, a.N, a.M, a.ldo2, DT_BF16)) return false;
     }
     return true;
@@ -1004,7 +1013,7 @@ void launch_tc(const TcPlan& pl, cudaStream_t s) {
             pl.ma, pl.mb, pl.mc, pl.mc2, pl.mx, P);                                          \
     } while (0)
     if (P.ek == EPI_GELU_SAVE) PTCG_TC_LAUNCH(2, NUM_EPI, EPI_GELU_SAVE);
-    else if (P.ek == EPI_GELU_AUX) PTCG_TC_LAUNCH(2, NUM_EPI, EPI_GELU_AUX);
+    else if (P.ek == EPI_GELU_AUX) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_GELU_AUX);
     else if (P.ek == EPI_PLAIN) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_PLAIN);
     else if (P.ek == EPI_BIAS) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_BIAS);
     else if (P.ek == EPI_RESID) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_RESID);
