@@ -59,6 +59,27 @@ def test_forward_parity(pkg, oracle, preset, prec):
     np.testing.assert_allclose(ft, out, rtol=0, atol=1e-6 if prec == "fp32" else 1e-3)
 
 
+@pytest.mark.parametrize("preset", ["c0", "default"])
+def test_pointer_into_padding(pkg, oracle, preset):
+    """Option 2's first pointer is moved onto a padded token row (past the
+    row's last valid token, within the batch's longest prefix, where the
+    reference still computes and gathers it).  The bf16 attention skips rows
+    past each sequence's extent, which must include pointed-to rows: option
+    2's raw score is checked on its own, legal or not."""
+    torch.set_float32_matmul_precision("highest")
+    n = ROWS[preset]
+    s, tabs, blob, obs, pol = make(pkg, preset, "bf16", n, edge=False)
+    ti0 = s.offsets["tok_int"][0]
+    nv = (obs[:, ti0:ti0 + s.ltok * 5].reshape(n, s.ltok, 5)[:, :, 1] > 0).sum(1)
+    rows = np.nonzero(nv + 2 <= nv.max())[0]
+    assert len(rows) >= 2
+    a0 = s.offsets["opt_int"][0]
+    obs[rows, a0 + 2 * 6 + 1] = nv[rows] + 2        # token index nv + 1: padding
+    out = pol.forward(obs).cpu().numpy()
+    sc, _ = oracle_fwd(oracle, s, tabs, blob, obs)
+    assert rel(out[rows, 2], sc[rows, 2]) <= TOL["bf16"], rel(out[rows, 2], sc[rows, 2])
+
+
 def _rollout_tensors(pkg, oracle, s, obs, scores, seed):
     n = obs.shape[0]
     a, b = s.offsets["opt_mask"]
