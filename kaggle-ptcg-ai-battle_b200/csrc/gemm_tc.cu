@@ -83,6 +83,7 @@ struct TcParams {
     uint32_t aux_bytes;      // bytes of one slot: BM rows x bn bf16, as bn/32 boxes of 8 KB
     int nepi;                // epilogue warps of the instantiation that runs the plan
     int ek;                  // epilogue kind (EPI_*) of that instantiation
+    int box_rows;            // rows of one TMA store box: 32, or 8 for a remap in 8-row groups
     GemmArgs ep;
 };
 
@@ -727,10 +728,20 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     __syncwarp();
                     if (lane == 0) {
                         int y = mt * BM + quad * 32;
-                        if (a.remap_group > 0)                   // the box's first output row
-                            y = (y / a.remap_group) * a.remap_stride + a.remap_off + y % a.remap_group;
-                        tma_store_2d(&map_c, smem_u32(sbuf), n0, y);
-                        if (a.act == ACT_GELU && a.out2) tma_store_2d(&map_c2, smem_u32(sbuf + 2048), n0, y);
+                        if (P.box_rows == 8) {                   // four 8-row boxes, each remapped
+                            const uint32_t rb = a.out_dtype == DT_F32 ? 128u : 64u;
+                            for (int i = 0; i < 4; i++) {
+                                const int yi = y + 8 * i;
+                                const int yo = (yi / a.remap_group) * a.remap_stride + a.remap_off +
+                                               yi % a.remap_group;
+                                tma_store_2d(&map_c, smem_u32(sbuf) + i * 8 * rb, n0, yo);
+                            }
+                        } else {
+                            if (a.remap_group > 0)               // the box's first output row
+                                y = (y / a.remap_group) * a.remap_stride + a.remap_off + y % a.remap_group;
+                            tma_store_2d(&map_c, smem_u32(sbuf), n0, y);
+                            if (a.act == ACT_GELU && a.out2) tma_store_2d(&map_c2, smem_u32(sbuf + 2048), n0, y);
+                        }
                         bulk_commit();
                     }
                 }
@@ -878,12 +889,12 @@ bool make_aux_map(CUtensorMap* m, const void* ptr, long n, long rows, long ld) {
     return r == CUDA_SUCCESS;
 }
 
-// output map for TMA stores: box {32 columns, 32 rows}
-bool make_out_map(CUtensorMap* m, void* ptr, long n, long rows, long ld, int dt) {
+// output map for TMA stores: box {32 columns, box_rows rows}
+bool make_out_map(CUtensorMap* m, void* ptr, long n, long rows, long ld, int dt, int box_rows = 32) {
     int eb = dt == DT_F32 ? 4 : 2;
     cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)ld * eb};
-    cuuint32_t box[2] = {32, 32};
+    cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
     cuuint32_t es[2] = {1, 1};
     CUresult r = g_encode(m, dt == DT_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                           2, ptr, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -942,12 +953,14 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     // outputs through smem + TMA store: plain row mapping, no read-modify-
     // write, whole 32-column chunks per tile, 16-byte aligned pitch
     int oeb = a.out_dtype == DT_F32 ? 4 : 2;
-    // a row remap keeps the TMA store when its groups are whole 32-row boxes
-    // (each box then lands on consecutive output rows); the map then spans
-    // the remapped rows
+    // a row remap keeps the TMA store when its groups are whole store boxes
+    // (each box then lands on consecutive output rows): 32-row boxes, or
+    // four 8-row boxes per chunk when the groups are multiples of 8 only;
+    // the map then spans the remapped rows
     const bool remap_ok = a.remap_group == 0 ||
-        (a.remap_group % 32 == 0 && a.M % a.remap_group == 0 && !a.out2 &&
+        (a.remap_group % 8 == 0 && a.M % a.remap_group == 0 && !a.out2 &&
          a.remap_off + a.remap_group <= a.remap_stride);
+    P.box_rows = (a.remap_group > 0 && a.remap_group % 32 != 0) ? 8 : 32;
     P.tma_out = P.splits == 1 && remap_ok && !a.accumulate && (bn % 32) == 0 &&
                 !((uintptr_t)a.out & 15) && (a.ldo * oeb) % 16 == 0 &&
                 (!a.out2 || (a.act == ACT_GELU && a.out2_dtype == DT_BF16 && a.out_dtype == DT_BF16 &&
@@ -993,7 +1006,7 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     if (P.aux_tma && !make_aux_map(&pl.mx, a.aux, a.N, a.M, a.ld_aux)) return false;
     if (P.tma_out) {
         const long out_rows = a.remap_group > 0 ? (long)(a.M / a.remap_group) * a.remap_stride : a.M;
-        if (!make_out_map(&pl.mc, a.out, a.N, out_rows, a.ldo, a.out_dtype)) return false;
+        if (!make_out_map(&pl.mc, a.out, a.N, out_rows, a.ldo, a.out_dtype, P.box_rows)) return false;
         if (a.out2 && !make_out_map(&pl.mc2, a.out2, a.N, a.M, a.ldo2, DT_BF16)) return false;
     }
     return true;

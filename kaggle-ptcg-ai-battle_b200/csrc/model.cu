@@ -458,7 +458,7 @@ static void plan_work(Work& W, Bump& m, int R, bool train, const Dims& z, int es
     W.dd1 = m.f((long)R * 64);
     W.dg1 = m.f((long)R * 128);
     W.dbc = m.f((long)R * z.D);
-    W.dotokin = m.f((long)R * 56 * 134);
+    W.dotokin = m.f((long)R * 56 * 136);      // row pitch 136: 16-byte rows for the TMA store
     W.dx = m.f(NC * z.D);
     W.dx0 = m.f((long)R * z.D);
     W.dq0 = m.take((long)R * z.D * esz);
@@ -989,8 +989,8 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
                                           1 + z.LSEQ, 56, D, gpb);
     }
     gemm(M, lin_dw(dt, R * 56, 134, D, Wk.dotok, D, Wk.otokin, rup(134, 8), wo.g), s);
-    gemm(M, lin_dx(dt, R * 56, 134, D, Wk.dotok, D, wo, Wk.dotokin, 134, DT_F32), s);
-    ++g_ptcg_launches, k_otok_bwd<<<cdiv((long)R * 56 * 128, TPB), TPB, 0, s>>>(t.d_cv, Wk.dotokin, 134, obs, ol, R);
+    gemm(M, lin_dx(dt, R * 56, 134, D, Wk.dotok, D, wo, Wk.dotokin, 136, DT_F32), s);
+    ++g_ptcg_launches, k_otok_bwd<<<cdiv((long)R * 56 * 128, TPB), TPB, 0, s>>>(t.d_cv, Wk.dotokin, 136, obs, ol, R);
     // ---- option scorer (d scores = grad[:, :NOPT])
     ++g_ptcg_launches, k_scale_copy<<<cdiv(NO, TPB), TPB, 0, s>>>(Wk.dscores, z.NOPT, grad, z.NOPT + 1, R, z.NOPT, 1.f);
     {
