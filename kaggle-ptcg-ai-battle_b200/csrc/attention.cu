@@ -306,29 +306,39 @@ __global__ void __launch_bounds__(128) k_attn_fwd_mma(
         #pragma unroll
         for (int i = 0; i < 4; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
         float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-        for (int kb = 0; kb < nkb; kb++) {
-            if (!kb_any[kb]) continue;
-            float s[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+        // the key blocks with a kept key, two at a time: one max / rescale
+        // step per 32 keys (the second slot is empty for an odd count)
+        uint32_t rem = __ballot_sync(0xffffffffu, lane < nkb && kb_any[lane]);
+        while (rem) {
+            const int k0 = __ffs(rem) - 1;
+            rem &= rem - 1;
+            const bool two = rem != 0;
+            const int k1 = two ? __ffs(rem) - 1 : k0;
+            if (two) rem &= rem - 1;
+            float s[4][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}, {0, 0, 0, 0}, {0, 0, 0, 0}};
             #pragma unroll
             for (int ks = 0; ks < 2; ks++) {
                 uint32_t b[4];
-                ldb_nk(b, Ks, kb * 16, ks * 16, lane);
+                ldb_nk(b, Ks, k0 * 16, ks * 16, lane);
                 mma(s[0], qa[ks], b[0], b[1]);
                 mma(s[1], qa[ks], b[2], b[3]);
-            }
-            float bias[2][2];
-            #pragma unroll
-            for (int nt = 0; nt < 2; nt++) {
-                bias[nt][0] = kb_bias[kb * 16 + nt * 8 + 2 * t];
-                bias[nt][1] = kb_bias[kb * 16 + nt * 8 + 2 * t + 1];
+                if (two) {
+                    ldb_nk(b, Ks, k1 * 16, ks * 16, lane);
+                    mma(s[2], qa[ks], b[0], b[1]);
+                    mma(s[3], qa[ks], b[2], b[3]);
+                }
             }
             float bm0 = -INFINITY, bm1 = -INFINITY;
             #pragma unroll
-            for (int nt = 0; nt < 2; nt++) {
-                s[nt][0] = s[nt][0] * sc + bias[nt][0];
-                s[nt][1] = s[nt][1] * sc + bias[nt][1];
-                s[nt][2] = s[nt][2] * sc + bias[nt][0];
-                s[nt][3] = s[nt][3] * sc + bias[nt][1];
+            for (int nt = 0; nt < 4; nt++) {
+                const int kb = nt < 2 ? k0 : k1;
+                float b0 = kb_bias[kb * 16 + (nt & 1) * 8 + 2 * t];
+                float b1 = kb_bias[kb * 16 + (nt & 1) * 8 + 2 * t + 1];
+                if (nt >= 2 && !two) b0 = b1 = -INFINITY;
+                s[nt][0] = s[nt][0] * sc + b0;
+                s[nt][1] = s[nt][1] * sc + b1;
+                s[nt][2] = s[nt][2] * sc + b0;
+                s[nt][3] = s[nt][3] * sc + b1;
                 bm0 = fmaxf(bm0, fmaxf(s[nt][0], s[nt][1]));
                 bm1 = fmaxf(bm1, fmaxf(s[nt][2], s[nt][3]));
             }
@@ -347,22 +357,27 @@ __global__ void __launch_bounds__(128) k_attn_fwd_mma(
                 for (int i = 0; i < 4; i++) { o[i][0] *= c0; o[i][1] *= c0; o[i][2] *= c1; o[i][3] *= c1; }
             }
             m0 = nm0; m1 = nm1;
-            float p[2][4];
             #pragma unroll
-            for (int nt = 0; nt < 2; nt++) {
-                p[nt][0] = ex2_approx(s[nt][0] - m0); p[nt][1] = ex2_approx(s[nt][1] - m0);
-                p[nt][2] = ex2_approx(s[nt][2] - m1); p[nt][3] = ex2_approx(s[nt][3] - m1);
-                l0 += p[nt][0] + p[nt][1];
-                l1 += p[nt][2] + p[nt][3];
+            for (int nt = 0; nt < 4; nt++) {
+                s[nt][0] = ex2_approx(s[nt][0] - m0); s[nt][1] = ex2_approx(s[nt][1] - m0);
+                s[nt][2] = ex2_approx(s[nt][2] - m1); s[nt][3] = ex2_approx(s[nt][3] - m1);
+                l0 += s[nt][0] + s[nt][1];
+                l1 += s[nt][2] + s[nt][3];
             }
-            uint32_t pa[4] = {pack2(p[0][0], p[0][1]), pack2(p[0][2], p[0][3]),
-                              pack2(p[1][0], p[1][1]), pack2(p[1][2], p[1][3])};
             #pragma unroll
-            for (int dn = 0; dn < 2; dn++) {
-                uint32_t b[4];
-                ldb_kn(b, Vs, kb * 16, dn * 16, lane);
-                mma(o[dn * 2], pa, b[0], b[1]);
-                mma(o[dn * 2 + 1], pa, b[2], b[3]);
+            for (int j = 0; j < 2; j++) {
+                if (j == 1 && !two) break;
+                const uint32_t pa[4] = {pack2(s[2 * j][0], s[2 * j][1]), pack2(s[2 * j][2], s[2 * j][3]),
+                                        pack2(s[2 * j + 1][0], s[2 * j + 1][1]),
+                                        pack2(s[2 * j + 1][2], s[2 * j + 1][3])};
+                const int kb = j == 0 ? k0 : k1;
+                #pragma unroll
+                for (int dn = 0; dn < 2; dn++) {
+                    uint32_t b[4];
+                    ldb_kn(b, Vs, kb * 16, dn * 16, lane);
+                    mma(o[dn * 2], pa, b[0], b[1]);
+                    mma(o[dn * 2 + 1], pa, b[2], b[3]);
+                }
             }
         }
         l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
