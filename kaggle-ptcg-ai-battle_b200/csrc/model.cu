@@ -336,11 +336,14 @@ template <typename T> static void colsum(float* out, const T* in, long ld, int r
     ++g_ptcg_launches, k_colsum<T><<<g, 128, 0, s>>>(out, in, ld, rows, cols, rpb);
 }
 
+// ext / lseq (nullable / unused): rows of each lseq-row sequence anything
+// reads (k_row_extent); the rest are skipped
 static void ln_fwd(int dt, void* y, long ldy, float* mu, float* rs, const float* x, long ldx,
-                   const float* w, const float* b, int rows, int D, cudaStream_t s) {
+                   const float* w, const float* b, int rows, int D, cudaStream_t s,
+                   const int* ext = nullptr, int lseq = 1) {
     unsigned g = cdiv(rows, 8);
     bool vec = D % 128 == 0 && D <= 1024 && ldx % 4 == 0 && ldy % 4 == 0;
-#define LNF(TO, V) ++g_ptcg_launches, k_ln_fwd<TO, V><<<g, 256, 0, s>>>((TO*)y, ldy, mu, rs, x, ldx, w, b, rows, D)
+#define LNF(TO, V) ++g_ptcg_launches, k_ln_fwd<TO, V><<<g, 256, 0, s>>>((TO*)y, ldy, mu, rs, x, ldx, w, b, rows, D, ext, lseq)
     if (vec && D == 256) { if (dt == DT_F32) LNF(float, 2); else LNF(bf16, 2); }
     else if (vec && D == 512) { if (dt == DT_F32) LNF(float, 4); else LNF(bf16, 4); }
     else { if (dt == DT_F32) LNF(float, 0); else LNF(bf16, 0); }
@@ -352,12 +355,14 @@ static void ln_fwd(int dt, void* y, long ldy, float* mu, float* rs, const float*
 static void ln_bwd(int dt, float* dx, int accumulate, void* dxc, float* dw, float* db,
                    const void* dy, const float* x, const float* w, const float* mu,
                    const float* rs, int rows, int D, cudaStream_t s, float* out_cs = nullptr,
-                   int dy_dt = DT_F32) {
+                   int dy_dt = DT_F32, const int* ext = nullptr, int lseq = 1) {
     int rpb = 64;
     unsigned g = cdiv(rows, rpb);
     size_t sm = 3 * D * sizeof(float);
+    if (D % 128 != 0 || D > 512) ext = nullptr;   // only the vector kernels skip rows
 #define LNB(TC, V, MC, TY) ++g_ptcg_launches, k_ln_bwd<TC, V, MC, TY><<<g, 256, sm, s>>>(dx, D, \
-        accumulate, (TC*)dxc, D, dw, db, (const TY*)dy, D, x, D, w, mu, rs, rows, D, rpb, out_cs)
+        accumulate, (TC*)dxc, D, dw, db, (const TY*)dy, D, x, D, w, mu, rs, rows, D, rpb, out_cs, \
+        ext, lseq)
 #define LNB2(TC, V, MC) do { if (dy_dt == DT_BF16) LNB(TC, V, MC, bf16); else LNB(TC, V, MC, float); } while (0)
     bool f = dt == DT_F32 || dxc == nullptr;
     if (D == 256) { if (f) LNB2(float, 2, 1); else LNB2(bf16, 2, 1); }
@@ -550,7 +555,7 @@ static void block_fwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
     const Dims& z = M->z;
     const int dt = M->dt(), D = z.D;
     const int NL = R * L;
-    ln_fwd(dt, b.ln1, D, b.mu1, b.rs1, b.x_in, D, P.ln1w.p, P.ln1b.p, NL, D, s);
+    ln_fwd(dt, b.ln1, D, b.mu1, b.rs1, b.x_in, D, P.ln1w.p, P.ln1b.p, NL, D, s, ext, L);
     GemmArgs a = lin_fwd(dt, NL, D, 3 * D, b.ln1, D, P.qkvw, b.qkv, 3 * D, dt);
     a.bias = P.qkvb.p;
     gemm(M, a, s);
@@ -558,7 +563,7 @@ static void block_fwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
     a = lin_fwd(dt, NL, D, D, b.att, D, P.projw, b.xm, D, DT_F32);
     a.bias = P.projb.p; a.resid = b.x_in; a.ld_resid = D;
     gemm(M, a, s);
-    ln_fwd(dt, b.ln2, D, b.mu2, b.rs2, b.xm, D, P.ln2w.p, P.ln2b.p, NL, D, s);
+    ln_fwd(dt, b.ln2, D, b.mu2, b.rs2, b.xm, D, P.ln2w.p, P.ln2b.p, NL, D, s, ext, L);
     a = lin_fwd(dt, NL, D, z.FFN, b.ln2, D, P.f1w, b.fpost, z.FFN, dt);
     a.bias = P.f1b.p; a.act = ACT_GELU;
     if (train) { a.out2 = b.fpre; a.ldo2 = z.FFN; a.out2_dtype = dt; }
@@ -660,7 +665,8 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
         block_fwd(M, M->blk("b" + std::to_string(i) + "_"), b, Wk.keep, R, z.LSEQ, train, s, Wk.ext);
         xl = b.x_out;
     }
-    ln_fwd(DT_F32, Wk.h, D, Wk.muf, Wk.rsf, xl, D, M->w("lnf_w").p, M->w("lnf_b").p, R * z.LSEQ, D, s);
+    ln_fwd(DT_F32, Wk.h, D, Wk.muf, Wk.rsf, xl, D, M->w("lnf_w").p, M->w("lnf_b").p, R * z.LSEQ, D, s,
+           Wk.ext, z.LSEQ);
     // --- option scorer
     long NO = (long)R * z.NOPT;
     long ldq = rup(z.Q_IN, 8);
@@ -788,7 +794,7 @@ static void block_bwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
     // LN2: dx <- d(x_mid) = dx + LN2'(dln)
     // (+ proj bias grad = column sums of d(x_mid))
     ln_bwd(dt, dx, 1, bf ? dxc : nullptr, P.ln2w.g, P.ln2b.g, Wk.dln, b.xm, P.ln2w.p, b.mu2,
-           b.rs2, NL, D, s, P.projb.g, dt);
+           b.rs2, NL, D, s, P.projb.g, dt, Wk.ext, L);
     // proj
     gemm(M, lin_dw(dt, NL, D, D, dxc, D, b.att, D, P.projw.g), s);
     gemm(M, lin_dx(dt, NL, D, D, dxc, D, P.projw, Wk.datt, D, dt), s);
@@ -800,7 +806,7 @@ static void block_bwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
     gemm(M, lin_dx(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, P.qkvw, Wk.dln, D, dt), s);
     // LN1: dx <- d(x_in) = dx + LN1'(dln)
     ln_bwd(dt, dx, 1, bf ? dxc : nullptr, P.ln1w.g, P.ln1b.g, Wk.dln, b.x_in, P.ln1w.p, b.mu1,
-           b.rs1, NL, D, s, lower_f2b, dt);
+           b.rs1, NL, D, s, lower_f2b, dt, Wk.ext, L);
 }
 
 // Backward of block_fwd_row0.  On entry Wk.dx0 (f32) / Wk.dx0c (operand
@@ -1070,7 +1076,7 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     // (+ the last block's FFN2 bias grad = column sums of d(x_L))
     ln_bwd(dt, Wk.dx, 0, bf ? Wk.dxc : nullptr, M->w("lnf_w").g, M->w("lnf_b").g, Wk.dh,
            Wk.x[z.LAYERS], M->w("lnf_w").p, Wk.muf, Wk.rsf, (int)NS, D, s,
-           M->w(("b" + std::to_string(z.LAYERS - 1) + "_ffn2_b").c_str()).g);
+           M->w(("b" + std::to_string(z.LAYERS - 1) + "_ffn2_b").c_str()).g, DT_F32, Wk.ext, z.LSEQ);
     if (last) fire_hook(M, "lnf_w", nullptr, s);
     // ---- trunk
     for (int i = z.LAYERS - 1; i >= 0; i--) {
