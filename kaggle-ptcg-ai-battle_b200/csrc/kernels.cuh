@@ -324,12 +324,15 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
 template <typename T>
 __global__ void k_tok_cat(T* out, long ldo, const float* obs, ObsLayout L,
                           const float* cv, const float* zemb, const float* oemb,
-                          int R, int tok_in) {
-    // one warp per token row, four consecutive columns per lane
+                          int R, int tok_in, const int* ext = nullptr) {
+    // one warp per token row, four consecutive columns per lane; tokens at
+    // or past the sequence's extent (row l + 1) are read by nothing and are
+    // left as they are
     long nl = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (nl >= (long)R * L.ltok) return;
     const int n = (int)(nl / L.ltok), l = (int)(nl - (long)n * L.ltok);
+    if (ext && l + 1 >= ext[n]) return;
     const float* row = obs + (long)n * L.obs;
     const float* ti = row + L.toki + l * 5;
     const float* c0 = cv + (long)id_clamp(ti[0], L.nc) * 128;
@@ -689,11 +692,14 @@ __global__ void k_otok_bwd(float* d_cv, const float* g, long ldg, const float* o
 // critic sequence rows 0 (critic readout) and 1..LSEQ (trunk output h);
 // rows 1+LSEQ.. are written by the oracle_proj GEMM (row remap)
 __global__ void k_xc_fill(float* xc, const float* h, const float* cread, int lseq,
-                          int lcrit, int D, int R) {
+                          int lcrit, int D, int R, const int* ext = nullptr) {
     long r = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);   // warp per row
     const int lane = threadIdx.x & 31;
     if (r >= (long)R * (1 + lseq)) return;
     const int n = (int)(r / (1 + lseq)), l = (int)(r - (long)n * (1 + lseq));
+    // trunk rows past the extent are masked critic keys: left as they are
+    // (finite), since they contribute nothing
+    if (ext && l > 0 && l - 1 >= ext[n]) return;
     const float* src = l == 0 ? cread : h + ((long)n * lseq + l - 1) * D;
     float* dst = xc + ((long)n * lcrit + l) * D;
     for (int c = lane * 4; c < D; c += 128) st4(dst + c, ld4(src + c));
@@ -739,7 +745,7 @@ __global__ void k_add_rows(float* dst, long seq_stride, const float* src, int R,
 // rows 1+LSEQ.. -> d_otok (T, compact) (k_xc_bwd, ptcg_model2.cu:174-187)
 template <typename T>
 __global__ void k_xc_bwd(T* d_otok, float* d_h, const float* dxc, int lseq, int lcrit, int D,
-                         int R) {
+                         int R, const int* ext = nullptr) {
     // rows 1..lcrit-1 of every sample, warp per row (row 0 -> d_creadout is
     // a column sum over samples, done separately)
     long r = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -748,6 +754,7 @@ __global__ void k_xc_bwd(T* d_otok, float* d_h, const float* dxc, int lseq, int 
     const int n = (int)(r / (lcrit - 1)), l = 1 + (int)(r - (long)n * (lcrit - 1));
     const float* g = dxc + ((long)n * lcrit + l) * D;
     if (l <= lseq) {
+        if (ext && l - 1 >= ext[n]) return;    // trunk rows past the extent: masked keys, zero grad
         float* dh = d_h + ((long)n * lseq + l - 1) * D;
         for (int c = lane * 4; c < D; c += 128) st4(dh + c, add4(ld4(dh + c), ld4(g + c)));
     } else {
@@ -776,7 +783,8 @@ __global__ void k_x0_bwd(T* d_tokp, float* d_bc, const float* dx0, int ltok, int
 }
 
 __global__ void k_tok_cat_bwd(float* d_cv, float* d_zemb, float* d_oemb, const float* g,
-                              long ldg, const float* obs, ObsLayout L, int R, int tok_in) {
+                              long ldg, const float* obs, ObsLayout L, int R, int tok_in,
+                              const int* ext = nullptr) {
     // warp per token row, grid-stride; the zone (16 x 8) and owner (4 x 4)
     // embedding grads, which every token hits, accumulate in shared memory
     // and leave with one atomic per entry per block
@@ -790,6 +798,7 @@ __global__ void k_tok_cat_bwd(float* d_cv, float* d_zemb, float* d_oemb, const f
     for (long nl = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); nl < nrows;
          nl += (long)gridDim.x * (blockDim.x >> 5)) {
         const int n = (int)(nl / L.ltok), l = (int)(nl - (long)n * L.ltok);
+        if (ext && l + 1 >= ext[n]) continue;   // zero gradient past the extent
         const float* ti = obs + (long)n * L.obs + L.toki + l * 5;
         const float* gr = g + nl * ldg;
         float* c0 = d_cv + (long)id_clamp(ti[0], L.nc) * 128;

@@ -622,15 +622,15 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     const Tab& t = M->tab;
     // --- token path
     long ldtok = rup(z.TOK_IN, 8);
-    if (dt == DT_F32)
-        ++g_ptcg_launches, k_tok_cat<float><<<cdiv((long)R * z.LTOK, TPB / 32), TPB, 0, s>>>((float*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
-            M->w("zone_emb").p, M->w("owner_emb").p, R, z.TOK_IN);
-    else
-        ++g_ptcg_launches, k_tok_cat<bf16><<<cdiv((long)R * z.LTOK, TPB / 32), TPB, 0, s>>>((bf16*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
-            M->w("zone_emb").p, M->w("owner_emb").p, R, z.TOK_IN);
     ++g_ptcg_launches, k_x0_readout<<<cdiv((long)R * (z.LSEQ > D ? z.LSEQ : D), TPB), TPB, 0, s>>>(Wk.x[0], Wk.keep,
         M->w("readout").p, obs, ol, R, D);
     ++g_ptcg_launches, k_row_extent<<<cdiv(R, TPB / 32), TPB, 0, s>>>(Wk.ext, Wk.keep, obs, ol, R);
+    if (dt == DT_F32)
+        ++g_ptcg_launches, k_tok_cat<float><<<cdiv((long)R * z.LTOK, TPB / 32), TPB, 0, s>>>((float*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
+            M->w("zone_emb").p, M->w("owner_emb").p, R, z.TOK_IN, Wk.ext);
+    else
+        ++g_ptcg_launches, k_tok_cat<bf16><<<cdiv((long)R * z.LTOK, TPB / 32), TPB, 0, s>>>((bf16*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
+            M->w("zone_emb").p, M->w("owner_emb").p, R, z.TOK_IN, Wk.ext);
     // --- global / decision encoders (fp32)
     GemmArgs a = lin_fwd(DT_F32, R, 64, 128, obs + ol.glob, ol.obs, f32w(M->w("global1_w"), 64),
                          Wk.g1, 128, DT_F32);
@@ -719,7 +719,7 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
         ++g_ptcg_launches, k_otok_in<bf16><<<cdiv(no, TPB), TPB, 0, s>>>((bf16*)Wk.otokin, ldo_t, Wk.ckeep, obs, ol,
             t.card_vec, Wk.keep, R);
     ++g_ptcg_launches, k_xc_fill<<<cdiv((long)R * (1 + z.LSEQ), TPB / 32), TPB, 0, s>>>(Wk.xc[0], Wk.h,
-        M->w("critic_readout").p, z.LSEQ, z.LCRIT, D, R);
+        M->w("critic_readout").p, z.LSEQ, z.LCRIT, D, R, Wk.ext);
     a = lin_fwd(dt, R * 56, 134, D, Wk.otokin, ldo_t, M->w("oracle_proj_w"), Wk.xc[0], D, DT_F32);
     a.bias = M->w("oracle_proj_b").p;
     a.remap_group = 56; a.remap_stride = z.LCRIT; a.remap_off = 1 + z.LSEQ;
@@ -983,9 +983,9 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
                                           0, 1, D, gpb);
         unsigned gb = cdiv((long)R * (z.LCRIT - 1), TPB / 32);
         if (bf)
-            ++g_ptcg_launches, k_xc_bwd<bf16><<<gb, TPB, 0, s>>>((bf16*)Wk.dotok, Wk.dh, Wk.dx, z.LSEQ, z.LCRIT, D, R);
+            ++g_ptcg_launches, k_xc_bwd<bf16><<<gb, TPB, 0, s>>>((bf16*)Wk.dotok, Wk.dh, Wk.dx, z.LSEQ, z.LCRIT, D, R, Wk.ext);
         else
-            ++g_ptcg_launches, k_xc_bwd<float><<<gb, TPB, 0, s>>>((float*)Wk.dotok, Wk.dh, Wk.dx, z.LSEQ, z.LCRIT, D, R);
+            ++g_ptcg_launches, k_xc_bwd<float><<<gb, TPB, 0, s>>>((float*)Wk.dotok, Wk.dh, Wk.dx, z.LSEQ, z.LCRIT, D, R, Wk.ext);
     }
     W wo = M->w("oracle_proj_w");
     {   // oracle_proj bias grad: fp32 sum of the critic-input grad rows 1+LSEQ..
@@ -1102,7 +1102,7 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     gemm(M, lin_dw(dt, R * z.LTOK, z.TOK_IN, D, Wk.dtokp, D, Wk.tokcat, ldtok, wt.g), s);
     gemm(M, lin_dx(dt, R * z.LTOK, z.TOK_IN, D, Wk.dtokp, D, wt, Wk.dtokcat, z.TOK_IN, DT_F32), s);
     ++g_ptcg_launches, k_tok_cat_bwd<<<std::min<unsigned>(cdiv((long)R * z.LTOK, TPB / 32), M->adam_grid), TPB, 0, s>>>(t.d_cv, M->w("zone_emb").g,
-        M->w("owner_emb").g, Wk.dtokcat, z.TOK_IN, obs, ol, R, z.TOK_IN);
+        M->w("owner_emb").g, Wk.dtokcat, z.TOK_IN, obs, ol, R, z.TOK_IN, Wk.ext);
     colsum<float>(M->w("bcast_b").g, Wk.dbc, D, R, D, s);
     gemm32(M, lin_dw(DT_F32, R, 192, D, Wk.dbc, D, Wk.gd, 192, M->w("bcast_w").g), s);
     {
