@@ -948,6 +948,37 @@ __global__ void k_colsum_groups(float* out, const float* src, long ld, int ngrou
     atomicAdd(&out[c], s);
 }
 
+// out[c] += sum over the rows {g * group_stride + row_off + r : g < ngroups,
+// r < rows_per_group} of src[row * ld + c]: warp per row (grid-stride), each
+// lane owning 4 consecutive columns of every 128 (float4 loads, NC chunks:
+// cols = 128 NC), per-block sums in shared memory, one atomic per column per
+// block
+template <int NC>
+__global__ void k_colsum_rowset(float* out, const float* src, long ld, int ngroups,
+                                int group_stride, int row_off, int rows_per_group) {
+    __shared__ float part[8][128 * NC];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float4 acc[NC];
+    #pragma unroll
+    for (int k = 0; k < NC; k++) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const long nrows = (long)ngroups * rows_per_group;
+    for (long i = (long)blockIdx.x * 8 + warp; i < nrows; i += (long)gridDim.x * 8) {
+        const int g = (int)(i / rows_per_group), r = (int)(i - (long)g * rows_per_group);
+        const float* row = src + ((long)g * group_stride + row_off + r) * ld;
+        #pragma unroll
+        for (int k = 0; k < NC; k++) acc[k] = add4(acc[k], ld4(row + k * 128 + lane * 4));
+    }
+    #pragma unroll
+    for (int k = 0; k < NC; k++) st4(&part[warp][k * 128 + lane * 4], acc[k]);
+    __syncthreads();
+    for (int c = threadIdx.x; c < 128 * NC; c += blockDim.x) {
+        float v = 0.f;
+        #pragma unroll
+        for (int w = 0; w < 8; w++) v += part[w][c];
+        if (v != 0.f) atomicAdd(&out[c], v);
+    }
+}
+
 // dst[r, c] += src[r * lds + off + c]
 __global__ void k_slice_add(float* dst, const float* src, int rows, int width, long lds,
                             int off) {

@@ -605,6 +605,28 @@ static void block_fwd_row0(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t
     gemm(M, a, s);
 }
 
+// out[c] += column sums over a set of rows (see k_colsum_rowset); the
+// vector kernel when the columns are 128 or 256 wide and rows 16-byte aligned
+static void colsum_rows(PtcgModel* M, float* out, const float* src, long ld, int ngroups,
+                        int group_stride, int row_off, int rows_per_group, int cols,
+                        cudaStream_t s) {
+    const long nrows = (long)ngroups * rows_per_group;
+    if ((cols == 128 || cols == 256) && ld % 4 == 0 && !((uintptr_t)src & 15)) {
+        unsigned g = std::min<unsigned>(cdiv(nrows, 8), M->adam_grid);
+        if (cols == 128)
+            ++g_ptcg_launches, k_colsum_rowset<1><<<g, 256, 0, s>>>(out, src, ld, ngroups, group_stride,
+                                                                    row_off, rows_per_group);
+        else
+            ++g_ptcg_launches, k_colsum_rowset<2><<<g, 256, 0, s>>>(out, src, ld, ngroups, group_stride,
+                                                                    row_off, rows_per_group);
+        return;
+    }
+    int gpb = 64;
+    dim3 g(cdiv(cols, 128), cdiv(ngroups, gpb));
+    ++g_ptcg_launches, k_colsum_groups<<<g, 128, 0, s>>>(out, src, ld, ngroups, group_stride, row_off,
+                                                         rows_per_group, cols, gpb);
+}
+
 // rows-dot launcher
 template <typename TI>
 static void rowdot(float* out, long os, const TI* in, long ldi, const float* w, const float* b,
@@ -977,10 +999,7 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     block_bwd_row0(M, M->blk("c0_"), Wk.cblk, Wk.ckeep, Wk, R, z.LCRIT, s);
     {   // critic input grad: row 0 -> critic_readout (column sum over samples),
         // rows 1..LSEQ -> d_h +=, rows 1+LSEQ.. -> d_otok (compact)
-        int gpb = 64;
-        dim3 g(cdiv(D, 128), cdiv(R, gpb));
-        ++g_ptcg_launches, k_colsum_groups<<<g, 128, 0, s>>>(M->w("critic_readout").g, Wk.dx, D, R, z.LCRIT,
-                                          0, 1, D, gpb);
+        colsum_rows(M, M->w("critic_readout").g, Wk.dx, D, R, z.LCRIT, 0, 1, D, s);
         unsigned gb = cdiv((long)R * (z.LCRIT - 1), TPB / 32);
         if (bf)
             ++g_ptcg_launches, k_xc_bwd<bf16><<<gb, TPB, 0, s>>>((bf16*)Wk.dotok, Wk.dh, Wk.dx, z.LSEQ, z.LCRIT, D, R, Wk.ext);
@@ -989,10 +1008,7 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     }
     W wo = M->w("oracle_proj_w");
     {   // oracle_proj bias grad: fp32 sum of the critic-input grad rows 1+LSEQ..
-        int gpb = 64;
-        dim3 g(cdiv(D, 128), cdiv(R, gpb));
-        ++g_ptcg_launches, k_colsum_groups<<<g, 128, 0, s>>>(M->w("oracle_proj_b").g, Wk.dx, D, R, z.LCRIT,
-                                          1 + z.LSEQ, 56, D, gpb);
+        colsum_rows(M, M->w("oracle_proj_b").g, Wk.dx, D, R, z.LCRIT, 1 + z.LSEQ, 56, D, s);
     }
     gemm(M, lin_dw(dt, R * 56, 134, D, Wk.dotok, D, Wk.otokin, rup(134, 8), wo.g), s);
     gemm(M, lin_dx(dt, R * 56, 134, D, Wk.dotok, D, wo, Wk.dotokin, 136, DT_F32), s);
@@ -1088,9 +1104,7 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     }
     // ---- x0 split, token projection, broadcast
     {   // readout grad: column sum of row 0 over samples
-        int gpb = 64;
-        dim3 g(cdiv(D, 128), cdiv(R, gpb));
-        ++g_ptcg_launches, k_colsum_groups<<<g, 128, 0, s>>>(M->w("readout").g, Wk.dx, D, R, z.LSEQ, 0, 1, D, gpb);
+        colsum_rows(M, M->w("readout").g, Wk.dx, D, R, z.LSEQ, 0, 1, D, s);
     }
     if (bf)
         ++g_ptcg_launches, k_x0_bwd<bf16><<<R, 256, 0, s>>>((bf16*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D);
