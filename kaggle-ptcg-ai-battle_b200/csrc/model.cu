@@ -331,6 +331,15 @@ static W f32w(const W& w, long cols) { W r = w; r.op = w.p; r.ld = cols; return 
 template <typename T> static void colsum(float* out, const T* in, long ld, int rows, int cols,
                                          cudaStream_t s) {
     if (rows <= 0) return;
+    if (sizeof(T) == 4 && (cols == 128 || cols == 256) && ld % 4 == 0 && !((uintptr_t)in & 15)) {
+        // warp per row, float4 columns, block partials (k_colsum_rowset)
+        unsigned g = std::min<unsigned>(cdiv(rows, 8), 1184);
+        if (cols == 128)
+            ++g_ptcg_launches, k_colsum_rowset<1><<<g, 256, 0, s>>>(out, (const float*)in, ld, rows, 1, 0, 1);
+        else
+            ++g_ptcg_launches, k_colsum_rowset<2><<<g, 256, 0, s>>>(out, (const float*)in, ld, rows, 1, 0, 1);
+        return;
+    }
     int rpb = 256;
     dim3 g(cdiv(cols, 128), cdiv(rows, rpb));
     ++g_ptcg_launches, k_colsum<T><<<g, 128, 0, s>>>(out, in, ld, rows, cols, rpb);
