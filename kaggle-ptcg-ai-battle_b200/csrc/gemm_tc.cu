@@ -304,7 +304,8 @@ PTCG_DEV void load_operand(uint32_t dst, const CUtensorMap* map, uint32_t bar, i
 // epilogue kinds with a specialised chunk loop (compile-time), the rest
 // through the generic one
 enum { EPI_GENERIC = 0, EPI_GELU_SAVE = 1, EPI_GELU_AUX = 2,
-       EPI_PLAIN = 3, EPI_BIAS = 4, EPI_RESID = 5, EPI_BIAS_RESID = 6 };  // 3 + bias + 2 resid
+       EPI_PLAIN = 3, EPI_BIAS = 4, EPI_RESID = 5, EPI_BIAS_RESID = 6,  // 3 + bias + 2 resid
+       EPI_GELU = 7 };                                                   // bias + GELU, no GELU'
 
 template <int EB, int NEPI, int EK>
 __global__ void __launch_bounds__(threads_for(NEPI), 1)
@@ -499,10 +500,11 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 if (nvalid > P.bn - c0) nvalid = P.bn - c0;
                 if (nvalid > 32) nvalid = 32;
                 if (nvalid <= 0) continue;                       // warp-uniform
-                if constexpr (EK == EPI_GELU_SAVE) {
-                    // bias (staged in smem) + GELU, GELU' saved; bf16 out and
-                    // out2 through the staging buffer and TMA stores (rows
-                    // past M are computed on zero-filled operands and clipped)
+                if constexpr (EK == EPI_GELU_SAVE || EK == EPI_GELU) {
+                    // bias (staged in smem) + GELU, GELU' saved (EPI_GELU_SAVE);
+                    // bf16 out (and out2) through the staging buffer and TMA
+                    // stores (rows past M are computed on zero-filled operands
+                    // and clipped)
                     uint8_t* sbuf = staging + (warp - 2) * STAGE_W + (nchunk % STAGE_BUFS) * 4096;
                     nchunk++;
                     if (lane == 0) {
@@ -520,18 +522,27 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                         #pragma unroll
                         for (int j = 0; j < 32; j++) if (j < nvalid) v[j] += sbias[n0 + j];
                     }
-                    float g[32];
-                    #pragma unroll
-                    for (int j = 0; j < 32; j += 2)
-                        gelu2(v[j], v[j + 1], v[j], v[j + 1], g[j], g[j + 1]);
-                    stage32(sbuf + 2048, lane, DT_BF16, g);
-                    stage32(sbuf, lane, DT_BF16, v);
+                    if constexpr (EK == EPI_GELU_SAVE) {
+                        float g[32];
+                        #pragma unroll
+                        for (int j = 0; j < 32; j += 2)
+                            gelu2(v[j], v[j + 1], v[j], v[j + 1], g[j], g[j + 1]);
+                        stage32(sbuf + 2048, lane, DT_BF16, g);
+                    } else {
+                        #pragma unroll
+                        for (int j = 0; j < 32; j += 2) {
+                            float g0, g1;
+                            gelu2(v[j], v[j + 1], v[j], v[j + 1], g0, g1);
+                        }
+                    }
+                    stage32(sbuf, lane, a.out_dtype, v);
                     fence_async_smem();
                     __syncwarp();
                     if (lane == 0) {
                         const int y = mt * BM + quad * 32;
                         tma_store_2d(&map_c, smem_u32(sbuf), n0, y);
-                        tma_store_2d(&map_c2, smem_u32(sbuf + 2048), n0, y);
+                        if constexpr (EK == EPI_GELU_SAVE)
+                            tma_store_2d(&map_c2, smem_u32(sbuf + 2048), n0, y);
                         bulk_commit();
                     }
                     continue;
@@ -977,6 +988,8 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     P.ek = EPI_GENERIC;
     if (simple && a.act == ACT_GELU && a.out2 && P.bias_smem > 0 && !a.colsum && !a.resid)
         P.ek = EPI_GELU_SAVE;
+    else if (simple && a.act == ACT_GELU && !a.out2 && P.bias_smem > 0 && !a.colsum && !a.resid)
+        P.ek = EPI_GELU;
     else if (simple && a.act == ACT_GELU_BWD && P.aux_tma && !a.bias && !a.out2 && !a.resid)
         P.ek = EPI_GELU_AUX;
     else if (simple && a.act == ACT_NONE && !a.out2 && (!a.bias || P.bias_smem > 0))
@@ -1026,6 +1039,7 @@ void launch_tc(const TcPlan& pl, cudaStream_t s) {
             pl.ma, pl.mb, pl.mc, pl.mc2, pl.mx, P);                                          \
     } while (0)
     if (P.ek == EPI_GELU_SAVE) PTCG_TC_LAUNCH(2, NUM_EPI, EPI_GELU_SAVE);
+    else if (P.ek == EPI_GELU) PTCG_TC_LAUNCH(2, NUM_EPI, EPI_GELU);
     else if (P.ek == EPI_GELU_AUX) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_GELU_AUX);
     else if (P.ek == EPI_PLAIN) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_PLAIN);
     else if (P.ek == EPI_BIAS) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_BIAS);
