@@ -767,18 +767,41 @@ __global__ void k_xc_bwd(T* d_otok, float* d_h, const float* dxc, int lseq, int 
 // over token rows (one block per sample, no atomics); row 0 -> d_readout is
 // a column sum over samples, done separately
 template <typename T>
-__global__ void k_x0_bwd(T* d_tokp, float* d_bc, const float* dx0, int ltok, int D) {
-    int n = blockIdx.x;
-    int lseq = ltok + 1;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        const float* base = dx0 + (long)n * lseq * D + d;
-        float acc = 0.f;
-        for (int l = 1; l < lseq; l++) {
-            float g = base[(long)l * D];
-            acc += g;
-            st(&d_tokp[((long)n * ltok + l - 1) * D + d], g);
+__global__ void k_x0_bwd(T* d_tokp, float* d_bc, const float* dx0, int ltok, int D,
+                         const int* ext = nullptr) {
+    // one block (8 warps) per sample: warp w takes token rows w, w + 8, ..;
+    // each lane 4 consecutive columns of every 128 (float4 loads); rows past
+    // the extent carry a zero gradient and are written as zeros unread.  D is
+    // a multiple of 4 and at most 512.
+    __shared__ float part[8][512];
+    const int n = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int lseq = ltok + 1;
+    const int e = ext ? ext[n] : lseq;
+    float4 acc[4];
+    #pragma unroll
+    for (int k = 0; k < 4; k++) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int l = 1 + warp; l < lseq; l += 8) {
+        T* o = d_tokp + ((long)n * ltok + l - 1) * D;
+        const float* g = dx0 + ((long)n * lseq + l) * D;
+        #pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int c = k * 128 + lane * 4;
+            if (c >= D) break;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (l < e) v = ld4(g + c);
+            st4(o + c, v);
+            acc[k] = add4(acc[k], v);
         }
-        d_bc[(long)n * D + d] = acc;
+    }
+    #pragma unroll
+    for (int k = 0; k < 4; k++)
+        if (k * 128 + lane * 4 < D) st4(&part[warp][k * 128 + lane * 4], acc[k]);
+    __syncthreads();
+    for (int c = threadIdx.x; c < D; c += blockDim.x) {
+        float v = 0.f;
+        #pragma unroll
+        for (int w = 0; w < 8; w++) v += part[w][c];
+        d_bc[(long)n * D + c] = v;
     }
 }
 

@@ -1116,9 +1116,9 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
         colsum_rows(M, M->w("readout").g, Wk.dx, D, R, z.LSEQ, 0, 1, D, s);
     }
     if (bf)
-        ++g_ptcg_launches, k_x0_bwd<bf16><<<R, 256, 0, s>>>((bf16*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D);
+        ++g_ptcg_launches, k_x0_bwd<bf16><<<R, 256, 0, s>>>((bf16*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D, Wk.ext);
     else
-        ++g_ptcg_launches, k_x0_bwd<float><<<R, 256, 0, s>>>((float*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D);
+        ++g_ptcg_launches, k_x0_bwd<float><<<R, 256, 0, s>>>((float*)Wk.dtokp, Wk.dbc, Wk.dx, z.LTOK, D, Wk.ext);
     W wt = M->w("token_proj_w");
     long ldtok = rup(z.TOK_IN, 8);
     colsum<float>(M->w("token_proj_b").g, Wk.dbc, D, R, D, s);
