@@ -83,13 +83,16 @@ __global__ void k_pool_bwd(float* d_tab, const float* dsrc, int ld, int off_mean
 // one warp per row, eps 1e-5 (torch nn.LayerNorm), two-pass statistics.
 // VEC: D % 128 == 0 and 16-byte aligned rows -> each lane owns 4 consecutive
 // columns of every 128-column chunk (float4 loads, 8-byte bf16 stores).
-// ext (nullable): rows of each lseq-row sequence that anything reads; the
-// rows past it are left as they are (finite: the workspace starts zeroed
-// and only ever holds finite values), since nothing reads them
+// ext (nullable): rows of each lseq-row sequence that anything reads;
+// rowkeep (nullable): per row, 0 for rows read by nothing (masked keys of a
+// sequence whose only query is its first row).  Skipped rows are left as
+// they are (finite: the workspace starts zeroed and only ever holds finite
+// values), since nothing reads them
 template <typename TO, int VEC>
 __global__ void k_ln_fwd(TO* y, long ldy, float* mean, float* rstd, const float* x,
                          long ldx, const float* w, const float* b, int rows, int D,
-                         const int* ext = nullptr, int lseq = 1) {
+                         const int* ext = nullptr, int lseq = 1,
+                         const uint8_t* rowkeep = nullptr) {
     int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -97,6 +100,7 @@ __global__ void k_ln_fwd(TO* y, long ldy, float* mean, float* rstd, const float*
         const int n = row / lseq;
         if (row - n * lseq >= ext[n]) return;
     }
+    if (rowkeep && !rowkeep[row]) return;
     const float* xr = x + (long)row * ldx;
     TO* yr = y + (long)row * ldy;
     if (VEC > 0) {
@@ -164,12 +168,13 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
                          float* dw, float* db, const TY* dy, long lddy,
                          const float* x, long ldx, const float* w, const float* mean,
                          const float* rstd, int rows, int D, int rows_per_block,
-                         float* out_cs, const int* ext = nullptr, int lseq = 1) {
+                         float* out_cs, const int* ext = nullptr, int lseq = 1,
+                         const uint8_t* rowkeep = nullptr) {
     // out_cs (nullable): += column sums of the resulting dx (the bias grad
     // of the layer that produced this residual stream).  ext (nullable):
     // rows of each lseq-row sequence that anything reads; past it dy is zero
     // and so is the residual gradient, which is written as zeros without
-    // reading anything
+    // reading anything.  rowkeep (nullable): the same for rows marked 0
     extern __shared__ float sh[];               // [3][D]
     float* sw = sh;
     float* sb = sh + D;
@@ -192,20 +197,22 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
             const float* xr = x + (long)row * ldx;
             const TY* dyr = dy + (long)row * lddy;
             float* dxr = dx + (long)row * lddx;
+            bool unread = rowkeep && !rowkeep[row];
             if (ext) {
                 const int n = row / lseq;
-                if (row - n * lseq >= ext[n]) {
-                    #pragma unroll
-                    for (int c = 0; c < VEC; c++) {
-                        const int i = c * 128 + lane * 4;
-                        *(float4*)(dxr + i) = make_float4(0.f, 0.f, 0.f, 0.f);
-                        if (dxc) {
-                            if (sizeof(TC) == 4) *(float4*)((float*)dxc + (long)row * lddxc + i) = make_float4(0.f, 0.f, 0.f, 0.f);
-                            else *(uint2*)((bf16*)dxc + (long)row * lddxc + i) = make_uint2(0u, 0u);
-                        }
+                unread = unread || row - n * lseq >= ext[n];
+            }
+            if (unread) {
+                #pragma unroll
+                for (int c = 0; c < VEC; c++) {
+                    const int i = c * 128 + lane * 4;
+                    *(float4*)(dxr + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (dxc) {
+                        if (sizeof(TC) == 4) *(float4*)((float*)dxc + (long)row * lddxc + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+                        else *(uint2*)((bf16*)dxc + (long)row * lddxc + i) = make_uint2(0u, 0u);
                     }
-                    continue;
                 }
+                continue;
             }
             float4 xv[VEC > 0 ? VEC : 1], gv[VEC > 0 ? VEC : 1], av[VEC > 0 ? VEC : 1];
             #pragma unroll

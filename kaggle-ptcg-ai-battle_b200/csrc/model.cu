@@ -349,10 +349,10 @@ template <typename T> static void colsum(float* out, const T* in, long ld, int r
 // reads (k_row_extent); the rest are skipped
 static void ln_fwd(int dt, void* y, long ldy, float* mu, float* rs, const float* x, long ldx,
                    const float* w, const float* b, int rows, int D, cudaStream_t s,
-                   const int* ext = nullptr, int lseq = 1) {
+                   const int* ext = nullptr, int lseq = 1, const uint8_t* rowkeep = nullptr) {
     unsigned g = cdiv(rows, 8);
     bool vec = D % 128 == 0 && D <= 1024 && ldx % 4 == 0 && ldy % 4 == 0;
-#define LNF(TO, V) ++g_ptcg_launches, k_ln_fwd<TO, V><<<g, 256, 0, s>>>((TO*)y, ldy, mu, rs, x, ldx, w, b, rows, D, ext, lseq)
+#define LNF(TO, V) ++g_ptcg_launches, k_ln_fwd<TO, V><<<g, 256, 0, s>>>((TO*)y, ldy, mu, rs, x, ldx, w, b, rows, D, ext, lseq, rowkeep)
     if (vec && D == 256) { if (dt == DT_F32) LNF(float, 2); else LNF(bf16, 2); }
     else if (vec && D == 512) { if (dt == DT_F32) LNF(float, 4); else LNF(bf16, 4); }
     else { if (dt == DT_F32) LNF(float, 0); else LNF(bf16, 0); }
@@ -364,14 +364,15 @@ static void ln_fwd(int dt, void* y, long ldy, float* mu, float* rs, const float*
 static void ln_bwd(int dt, float* dx, int accumulate, void* dxc, float* dw, float* db,
                    const void* dy, const float* x, const float* w, const float* mu,
                    const float* rs, int rows, int D, cudaStream_t s, float* out_cs = nullptr,
-                   int dy_dt = DT_F32, const int* ext = nullptr, int lseq = 1) {
+                   int dy_dt = DT_F32, const int* ext = nullptr, int lseq = 1,
+                   const uint8_t* rowkeep = nullptr) {
     int rpb = 64;
     unsigned g = cdiv(rows, rpb);
     size_t sm = 3 * D * sizeof(float);
-    if (D % 128 != 0 || D > 512) ext = nullptr;   // only the vector kernels skip rows
+    if (D % 128 != 0 || D > 512) { ext = nullptr; rowkeep = nullptr; }   // vector kernels only
 #define LNB(TC, V, MC, TY) ++g_ptcg_launches, k_ln_bwd<TC, V, MC, TY><<<g, 256, sm, s>>>(dx, D, \
         accumulate, (TC*)dxc, D, dw, db, (const TY*)dy, D, x, D, w, mu, rs, rows, D, rpb, out_cs, \
-        ext, lseq)
+        ext, lseq, rowkeep)
 #define LNB2(TC, V, MC) do { if (dy_dt == DT_BF16) LNB(TC, V, MC, bf16); else LNB(TC, V, MC, float); } while (0)
     bool f = dt == DT_F32 || dxc == nullptr;
     if (D == 256) { if (f) LNB2(float, 2, 1); else LNB2(bf16, 2, 1); }
@@ -591,7 +592,8 @@ static void block_fwd_row0(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t
     const Dims& z = M->z;
     const int dt = M->dt(), D = z.D;
     const int NL = R * L;
-    ln_fwd(dt, b.ln1, D, b.mu1, b.rs1, b.x_in, D, P.ln1w.p, P.ln1b.p, NL, D, s);
+    // rows other than the query row and the kept keys are read by nothing
+    ln_fwd(dt, b.ln1, D, b.mu1, b.rs1, b.x_in, D, P.ln1w.p, P.ln1b.p, NL, D, s, nullptr, 1, keep);
     // keys and values of every row (weight rows D..3D), queries of the
     // readout rows only (weight rows 0..D; A rows at stride L * D)
     GemmArgs a = lin_fwd(dt, NL, D, 2 * D, b.ln1, D, wrows(P.qkvw, D, D, M->esz()), b.qkv, 2 * D, dt);
@@ -882,7 +884,7 @@ static void block_bwd_row0(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t
     }
     // d(x_in) = LN1'(dln) + the residual grad at row 0
     ln_bwd(dt, Wk.dx, 0, nullptr, P.ln1w.g, P.ln1b.g, Wk.dln, b.x_in, P.ln1w.p, b.mu1, b.rs1,
-           NL, D, s, nullptr, dt);
+           NL, D, s, nullptr, dt, nullptr, 1, keep);
     ++g_ptcg_launches, k_add_rows<<<cdiv((long)R * D, TPB), TPB, 0, s>>>(Wk.dx, (long)L * D, dx0, R, D);
 }
 
