@@ -754,16 +754,22 @@ template <typename T>
 __global__ void k_xc_bwd(T* d_otok, float* d_h, const float* dxc, int lseq, int lcrit, int D,
                          int R, const int* ext = nullptr) {
     // rows 1..lcrit-1 of every sample, warp per row (row 0 -> d_creadout is
-    // a column sum over samples, done separately)
+    // a column sum over samples, done separately).  The first writer of d_h:
+    // every trunk row is stored (no read-modify-write, no prior zeroing);
+    // rows past the extent are masked keys with a zero gradient, stored as
+    // zeros without reading
     long r = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (r >= (long)R * (lcrit - 1)) return;
     const int n = (int)(r / (lcrit - 1)), l = 1 + (int)(r - (long)n * (lcrit - 1));
     const float* g = dxc + ((long)n * lcrit + l) * D;
     if (l <= lseq) {
-        if (ext && l - 1 >= ext[n]) return;    // trunk rows past the extent: masked keys, zero grad
         float* dh = d_h + ((long)n * lseq + l - 1) * D;
-        for (int c = lane * 4; c < D; c += 128) st4(dh + c, add4(ld4(dh + c), ld4(g + c)));
+        if (ext && l - 1 >= ext[n]) {
+            for (int c = lane * 4; c < D; c += 128) st4(dh + c, make_float4(0.f, 0.f, 0.f, 0.f));
+            return;
+        }
+        for (int c = lane * 4; c < D; c += 128) st4(dh + c, ld4(g + c));
     } else {
         T* o = d_otok + ((long)n * 56 + (l - 1 - lseq)) * D;
         for (int c = lane * 4; c < D; c += 128) st4(o + c, ld4(g + c));

@@ -954,10 +954,37 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     const ObsLayout& ol = z.ol;
     Tab& t = M->tab;
     long NS = (long)R * z.LSEQ, NO = (long)R * z.NOPT;
-    cudaMemsetAsync(Wk.dh, 0, NS * D * 4, s);
     cudaMemsetAsync(Wk.dgd, 0, (size_t)R * 192 * 4, s);
     cudaMemsetAsync(t.d_poc, 0, (size_t)z.NC * 64 * 4, s);
     cudaMemsetAsync(t.d_poa, 0, (size_t)z.NA * 64 * 4, s);
+    // The oracle value head and the critic block go first: the critic input
+    // grad is the first writer of d_h (every row stored), so d_h needs no
+    // zeroing; the heads after it add into d_h
+    // ---- oracle value head (PPO value grad = grad[:, NOPT])
+    {
+        int rpb = 64;
+        ++g_ptcg_launches, k_rowdot_bwd<float, float><<<cdiv(R, rpb), 256, (256 + 1) * sizeof(float), s>>>(
+            Wk.d_v1pre, 256, Wk.ov1pre, 256, Wk.ov1, 256, M->w("oracle_v2_w").p,
+            M->w("oracle_v2_w").g, M->w("oracle_v2_b").g, grad + z.NOPT, z.NOPT + 1, nullptr, 0.f,
+            R, 256, rpb, nullptr, M->w("oracle_v1_b").g);
+    }
+    gemm32(M, lin_dw(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, Wk.ovin, z.VAL_IN,
+                     M->w("oracle_v1_w").g), s);
+    gemm32(M, lin_dx(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, f32w(M->w("oracle_v1_w"), z.VAL_IN),
+                     Wk.dbvin, z.VAL_IN, DT_F32), s);
+    ++g_ptcg_launches, k_val_in_bwd<<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.dx0, 1, D, Wk.dgd, Wk.dbvin, R, 0);
+    if (bf) ++g_ptcg_launches, k_cast<bf16><<<cdiv((long)R * D, TPB), TPB, 0, s>>>((bf16*)Wk.dx0c, D, Wk.dx0, D, R, D);
+    // ---- critic block (evaluated at its readout row)
+    block_bwd_row0(M, M->blk("c0_"), Wk.cblk, Wk.ckeep, Wk, R, z.LCRIT, s);
+    {   // critic input grad: row 0 -> critic_readout (column sum over samples),
+        // rows 1..LSEQ -> d_h (stored), rows 1+LSEQ.. -> d_otok (compact)
+        colsum_rows(M, M->w("critic_readout").g, Wk.dx, D, R, z.LCRIT, 0, 1, D, s);
+        unsigned gb = cdiv((long)R * (z.LCRIT - 1), TPB / 32);
+        if (bf)
+            ++g_ptcg_launches, k_xc_bwd<bf16><<<gb, TPB, 0, s>>>((bf16*)Wk.dotok, Wk.dh, Wk.dx, z.LSEQ, z.LCRIT, D, R, Wk.ext);
+        else
+            ++g_ptcg_launches, k_xc_bwd<float><<<gb, TPB, 0, s>>>((float*)Wk.dotok, Wk.dh, Wk.dx, z.LSEQ, z.LCRIT, D, R, Wk.ext);
+    }
     // ---- aux: opponent-hand counts
     float hscale = 0.1f / ((float)norm_rows * (float)z.NC);
     if (bf)
@@ -992,31 +1019,6 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     ++g_ptcg_launches, k_prize_bwd<<<std::min<unsigned>(cdiv((long)R * z.LTOK, 8), M->adam_grid), 256, (D + 2) * sizeof(float), s>>>(Wk.dh, M->w("aux_prize_w").g,
         M->w("aux_prize_b").g, Wk.prize_logit, Wk.h, M->w("aux_prize_w").p, obs, ol, prize_cnt_dev,
         prize_cnt_host, D, R, aux_loss + 2);
-    // ---- oracle value head (PPO value grad = grad[:, NOPT])
-    {
-        int rpb = 64;
-        ++g_ptcg_launches, k_rowdot_bwd<float, float><<<cdiv(R, rpb), 256, (256 + 1) * sizeof(float), s>>>(
-            Wk.d_v1pre, 256, Wk.ov1pre, 256, Wk.ov1, 256, M->w("oracle_v2_w").p,
-            M->w("oracle_v2_w").g, M->w("oracle_v2_b").g, grad + z.NOPT, z.NOPT + 1, nullptr, 0.f,
-            R, 256, rpb, nullptr, M->w("oracle_v1_b").g);
-    }
-    gemm32(M, lin_dw(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, Wk.ovin, z.VAL_IN,
-                     M->w("oracle_v1_w").g), s);
-    gemm32(M, lin_dx(DT_F32, R, z.VAL_IN, 256, Wk.d_v1pre, 256, f32w(M->w("oracle_v1_w"), z.VAL_IN),
-                     Wk.dbvin, z.VAL_IN, DT_F32), s);
-    ++g_ptcg_launches, k_val_in_bwd<<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.dx0, 1, D, Wk.dgd, Wk.dbvin, R, 0);
-    if (bf) ++g_ptcg_launches, k_cast<bf16><<<cdiv((long)R * D, TPB), TPB, 0, s>>>((bf16*)Wk.dx0c, D, Wk.dx0, D, R, D);
-    // ---- critic block (evaluated at its readout row)
-    block_bwd_row0(M, M->blk("c0_"), Wk.cblk, Wk.ckeep, Wk, R, z.LCRIT, s);
-    {   // critic input grad: row 0 -> critic_readout (column sum over samples),
-        // rows 1..LSEQ -> d_h +=, rows 1+LSEQ.. -> d_otok (compact)
-        colsum_rows(M, M->w("critic_readout").g, Wk.dx, D, R, z.LCRIT, 0, 1, D, s);
-        unsigned gb = cdiv((long)R * (z.LCRIT - 1), TPB / 32);
-        if (bf)
-            ++g_ptcg_launches, k_xc_bwd<bf16><<<gb, TPB, 0, s>>>((bf16*)Wk.dotok, Wk.dh, Wk.dx, z.LSEQ, z.LCRIT, D, R, Wk.ext);
-        else
-            ++g_ptcg_launches, k_xc_bwd<float><<<gb, TPB, 0, s>>>((float*)Wk.dotok, Wk.dh, Wk.dx, z.LSEQ, z.LCRIT, D, R, Wk.ext);
-    }
     W wo = M->w("oracle_proj_w");
     {   // oracle_proj bias grad: fp32 sum of the critic-input grad rows 1+LSEQ..
         colsum_rows(M, M->w("oracle_proj_b").g, Wk.dx, D, R, z.LCRIT, 1 + z.LSEQ, 56, D, s);
