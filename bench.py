@@ -42,7 +42,7 @@ def parse():
     ap.add_argument("--preset", default="c0")
     ap.add_argument("--segments", type=int, default=512)
     ap.add_argument("--horizon", type=int, default=64)
-    ap.add_argument("--micro", type=int, default=8192, help="rows per micro-batch")
+    ap.add_argument("--micro", type=int, default=16384, help="rows per micro-batch")
     ap.add_argument("--rollout-agents", type=int, default=1024)
     ap.add_argument("--rollout-steps", type=int, default=64)
     ap.add_argument("--e2e-steps", type=int, default=4)
