@@ -1,0 +1,113 @@
+"""The rollout forward + sampler and the train step are CUDA-graph
+capturable (no host synchronisation or allocation inside them): captured
+once, replayed on new inputs copied into the captured buffers, they must
+match eager execution."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _pol(pkg, preset, n):
+    s = pkg.config.PRESETS[preset]
+    pol = pkg.PTCGPolicy(s, precision="bf16", tables=pkg.synth.make_tables(s, 11),
+                         weights=pkg.synth.make_weights(s, 21), rollout_rows=n, train_rows=n)
+    return s, pol
+
+
+@pytest.mark.parametrize("preset", ["c0", "small"])
+def test_rollout_forward_sample_graph(pkg, preset):
+    n = 256
+    s, pol = _pol(pkg, preset, n)
+    a, b = s.offsets["opt_mask"]
+    obs0 = torch.from_numpy(pkg.synth.make_obs_batch(s, n, 1)).cuda()
+    obs1 = torch.from_numpy(pkg.synth.make_obs_batch(s, n, 2)).cuda()
+    u = torch.rand(n, device="cuda", generator=torch.Generator(device="cuda").manual_seed(5))
+    static = obs0.clone()
+
+    def step(x):
+        out = pol.forward(x)
+        act, lp, v = pol.sample(out, x[:, a:b], u)
+        return out, act, lp, v
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            step(static)                    # warm-up: plans and tensor maps built
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        g_out, g_act, g_lp, g_v = step(static)
+    for x in (obs1, obs0):
+        static.copy_(x)
+        g.replay()
+        torch.cuda.synchronize()
+        cap = [t.clone() for t in (g_out, g_act, g_lp, g_v)]
+        ref = [t.clone() for t in step(x)]
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(cap[1].cpu().numpy(), ref[1].cpu().numpy())
+        for c, r in zip((cap[0], cap[2], cap[3]), (ref[0], ref[2], ref[3])):
+            np.testing.assert_allclose(c.cpu().numpy(), r.cpu().numpy(), rtol=0, atol=1e-5)
+
+
+def test_train_step_graph(pkg):
+    """ptcg_train_step (forward, PPO loss, backward, clip + Adam) captured once
+    and replayed: same statistics and weights as eager execution from the
+    same state (up to the order of fp32 atomic accumulations)."""
+    n_seg, horizon = 4, 64
+    n = n_seg * horizon
+    s, pol = _pol(pkg, "small", n)
+    a, b = s.offsets["opt_mask"]
+    obs = torch.from_numpy(pkg.synth.make_obs_batch(s, n, 3)).cuda()
+    act = torch.from_numpy(pkg.synth.sample_legal(obs[:, a:b].cpu().numpy(), 1)).cuda().float()
+    g = torch.Generator(device="cuda").manual_seed(9)
+    old = torch.randn(n, device="cuda", generator=g) * 0.3 - 2.0
+    adv = torch.randn(n, device="cuda", generator=g)
+    val = torch.randn(n, device="cuda", generator=g) * 0.1
+    ret = torch.randn(n, device="cuda", generator=g)
+    prio = torch.ones(n_seg, device="cuda")
+    stats = torch.zeros(16, device="cuda")
+    blob = pkg.synth.make_weights(s, 21)
+
+    def reset():
+        pol.load_weights(blob)
+        pol.arena(2).zero_()
+        pol.arena(3).zero_()
+        pol.step = 0
+        torch.cuda.synchronize()
+
+    def step():
+        pol.train_step(obs, act, old, adv, val, ret, prio, n_seg, horizon, stats=stats)
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()                              # warm-up: plans and tensor maps built
+    torch.cuda.current_stream().wait_stream(side)
+    reset()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+
+    def run(fn):
+        reset()
+        fn()
+        torch.cuda.synchronize()
+        return pol.arena(1).clone(), pol.arena(0).clone(), stats.clone()
+
+    g_graph, w_graph, st_graph = run(graph.replay)
+    g_eager, w_eager, st_eager = run(step)
+    g_eager2, w_eager2, _ = run(step)
+    assert torch.isfinite(w_graph).all() and torch.isfinite(g_graph).all()
+
+    def rel(x, y):
+        return ((x - y).norm() / y.norm()).item()
+    # the fp32 atomic accumulations (split-K weight gradients, column sums)
+    # make two eager runs differ slightly; the replay must be as close
+    noise = rel(g_eager2, g_eager)
+    assert rel(g_graph, g_eager) <= max(4 * noise, 1e-6), (rel(g_graph, g_eager), noise)
+    assert rel(w_graph, w_eager) <= max(4 * rel(w_eager2, w_eager), 1e-6)
+    np.testing.assert_allclose(st_graph.cpu().numpy(), st_eager.cpu().numpy(), rtol=1e-4, atol=1e-6)
