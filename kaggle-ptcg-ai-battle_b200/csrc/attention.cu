@@ -665,9 +665,13 @@ size_t bwd_smem(int L) {
 // The critic block's output is read at its readout row alone
 // (ptcg/rl/model.py:305-308: oracle_v1(cat[x[:, 0], g])), so only query row
 // 0 of each sequence needs attention; keys and values still span every row.
-// One CTA per sequence, one warp per head, lane = key in the score pass and
-// lane = head dimension in the weighted sums.  fp32 arithmetic throughout
-// (memory-bound: it streams K and V once).
+// One warp per head.  Lane 4 * rg + c covers key row rg of each group of 8
+// consecutive keys and head columns [8c, 8c + 8): one 16-byte access per
+// lane reads or writes 8 whole 64-byte head rows of K, V, dK or dV, and a
+// dot product over the head takes two shuffles.  (A lane per key made
+// every access touch 32 rows 1 KB apart, and the L1 wavefronts, not DRAM,
+// bounded the kernels.)  fp32 arithmetic throughout; K and V are streamed
+// once.
 
 PTCG_DEV void ld8(const float* p, float* f) {
     float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
@@ -698,6 +702,7 @@ PTCG_DEV void st8(bf16* p, const float* f) {
 // log-sum-exp of the scaled scores (-inf when every key is masked).
 // q: the query row of sequence n at q + n * ldq; kv: rows [K | V] (2D wide,
 // row stride ldkv) of every position, sequence n at rows n * L ..
+// One CTA per sequence; shared memory holds each head's scores [H][Lr].
 template <typename T>
 __global__ void __launch_bounds__(512) k_attn_row0_fwd(
         const T* __restrict__ qrows, long ldq, const T* __restrict__ kv, long ldkv,
@@ -705,35 +710,35 @@ __global__ void __launch_bounds__(512) k_attn_row0_fwd(
         float* __restrict__ lse, int L, int H) {
     extern __shared__ float sm[];
     const int n = blockIdx.x, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rg = lane >> 2, c8 = (lane & 3) * 8;
     const int D = H * DH, Lr = (L + 31) & ~31;
-    float* qs = sm + h * DH;
-    float* p = sm + H * DH + h * Lr;
-    const T* base = kv + (long)n * L * ldkv;
+    float* p = sm + h * Lr;
+    const T* base = kv + (long)n * L * ldkv + h * DH + c8;
     const uint8_t* kp = keep + (long)n * L;
     const float scale = 0.17677669529663687f;   // 1/sqrt(32)
-    qs[lane] = to_f<T>(qrows[(long)n * ldq + h * DH + lane]) * scale;
-    __syncwarp();
-    float q[DH];
+    float q8[8];
+    ld8(qrows + (long)n * ldq + h * DH + c8, q8);
     #pragma unroll
-    for (int d = 0; d < DH; d++) q[d] = qs[d];
+    for (int e = 0; e < 8; e++) q8[e] *= scale;
     float mx = -INFINITY;
-    for (int j = lane; j < L; j += 32) {
-        float s = -INFINITY;
-        if (kp[j]) {
-            const T* kr = base + (long)j * ldkv + h * DH;
-            s = 0.f;
+    for (int j0 = 0; j0 < L; j0 += 8) {
+        const int j = j0 + rg;
+        const bool live = j < L && kp[j];
+        float s = 0.f;
+        if (live) {
+            float k8[8];
+            ld8(base + (long)j * ldkv, k8);
             #pragma unroll
-            for (int c = 0; c < DH; c += 8) {
-                float k8[8];
-                ld8(kr + c, k8);
-                #pragma unroll
-                for (int e = 0; e < 8; e++) s = fmaf(q[c + e], k8[e], s);
-            }
+            for (int e = 0; e < 8; e++) s = fmaf(q8[e], k8[e], s);
         }
-        p[j] = s;
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        if (!live) s = -INFINITY;
+        if (j < L && (lane & 3) == 0) p[j] = s;
         mx = fmaxf(mx, s);
     }
     mx = warp_max(mx);
+    __syncwarp();
     float sum = 0.f;
     for (int j = lane; j < L; j += 32) {
         float e = p[j] == -INFINITY ? 0.f : expf(p[j] - mx);
@@ -742,21 +747,32 @@ __global__ void __launch_bounds__(512) k_attn_row0_fwd(
     }
     sum = warp_sum(sum);
     __syncwarp();
-    const T* vb = base + D + h * DH + lane;
-    float o = 0.f;
-    for (int j = 0; j < L; j++) {
-        float pj = p[j];
-        if (pj != 0.f) o = fmaf(pj, to_f<T>(vb[(long)j * ldkv]), o);
+    float o8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j0 = 0; j0 < L; j0 += 8) {
+        const int j = j0 + rg;
+        const float pj = j < L ? p[j] : 0.f;
+        if (pj != 0.f) {
+            float v8[8];
+            ld8(base + (long)j * ldkv + D, v8);
+            #pragma unroll
+            for (int e = 0; e < 8; e++) o8[e] = fmaf(pj, v8[e], o8[e]);
+        }
     }
-    out[(long)n * ldo + h * DH + lane] = from_f<T>(sum > 0.f ? o / sum : 0.f);
+    #pragma unroll
+    for (int e = 0; e < 8; e++) {
+        #pragma unroll
+        for (int o = 4; o < 32; o <<= 1) o8[e] += __shfl_xor_sync(0xffffffffu, o8[e], o);
+        o8[e] = sum > 0.f ? o8[e] / sum : 0.f;
+    }
+    if (rg == 0) st8(out + (long)n * ldo + h * DH + c8, o8);
     if (lane == 0) lse[(long)n * H + h] = sum > 0.f ? mx + logf(sum) : -INFINITY;
 }
 
 // Backward of k_attn_row0_fwd: dq (one row per sequence, dq + n * lddq) and
 // dK / dV at every key of dkv (rows [dK | dV], zero where masked).  The QKV
 // bias gradient (fp32, before rounding) accumulates into dbias[3D] = [q | k |
-// v]: per-thread partials over the sequences a CTA visits, one atomic per
-// column per CTA.
+// v]: per-head partials over the sequences a CTA visits in shared memory
+// [H][96], one atomic per column per CTA.
 template <typename T>
 __global__ void __launch_bounds__(512) k_attn_row0_bwd(
         const T* __restrict__ qv, long ldq, const T* __restrict__ kv, long ldkv,
@@ -766,82 +782,87 @@ __global__ void __launch_bounds__(512) k_attn_row0_bwd(
         float* __restrict__ dbias, int R, int L, int H) {
     extern __shared__ float sm[];
     const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int D = H * DH, Lr = (L + 31) & ~31;
-    float* qs = sm + h * 2 * DH;
-    float* gs = qs + DH;
-    float* dsb = sm + H * 2 * DH + h * Lr;
+    const int rg = lane >> 2, c8 = (lane & 3) * 8;
+    const int D = H * DH;
+    float* acc = sm + h * 96;                    // [q | k | v] bias-grad columns of the head
+    for (int i = lane; i < 96; i += 32) acc[i] = 0.f;
+    __syncwarp();
     const float scale = 0.17677669529663687f;
-    float cq = 0.f, ck = 0.f, cv = 0.f;
     for (int n = blockIdx.x; n < R; n += gridDim.x) {
-        const T* base = kv + (long)n * L * ldkv;
-        T* dbase = dkv + (long)n * L * lddkv;
+        const T* base = kv + (long)n * L * ldkv + h * DH + c8;
+        T* dbase = dkv + (long)n * L * lddkv + h * DH + c8;
         const uint8_t* kp = keep + (long)n * L;
-        float qd = to_f<T>(qv[(long)n * ldq + h * DH + lane]);
-        float gd = to_f<T>(dout[(long)n * lddo + h * DH + lane]);
-        float od = to_f<T>(out[(long)n * ldo + h * DH + lane]);
-        float delta = warp_sum(gd * od);
-        float l = lse[(long)n * H + h];
-        qs[lane] = qd; gs[lane] = gd;
-        __syncwarp();
-        float q[DH], g[DH];
+        float q8[8], g8[8], t8[8];
+        ld8(qv + (long)n * ldq + h * DH + c8, q8);
+        ld8(dout + (long)n * lddo + h * DH + c8, g8);
+        ld8(out + (long)n * ldo + h * DH + c8, t8);
+        float delta = 0.f;
         #pragma unroll
-        for (int d = 0; d < DH; d++) { q[d] = qs[d]; g[d] = gs[d]; }
+        for (int e = 0; e < 8; e++) delta = fmaf(g8[e], t8[e], delta);
+        delta += __shfl_xor_sync(0xffffffffu, delta, 1);
+        delta += __shfl_xor_sync(0xffffffffu, delta, 2);
+        const float l = lse[(long)n * H + h];
+        float dq8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         float sds = 0.f, sp = 0.f;
-        for (int j = lane; j < L; j += 32) {
-            float dsj = 0.f, pj = 0.f;
-            if (kp[j] && l != -INFINITY) {
-                const T* kr = base + (long)j * ldkv + h * DH;
-                const T* vr = kr + D;
-                float s = 0.f, dp = 0.f;
+        for (int j0 = 0; j0 < L; j0 += 8) {
+            const int j = j0 + rg;
+            const bool live = j < L && kp[j] && l != -INFINITY;
+            float k8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            float s = 0.f, dp = 0.f;
+            if (live) {
+                float v8[8];
+                ld8(base + (long)j * ldkv, k8);
+                ld8(base + (long)j * ldkv + D, v8);
                 #pragma unroll
-                for (int c = 0; c < DH; c += 8) {
-                    float k8[8], v8[8];
-                    ld8(kr + c, k8);
-                    ld8(vr + c, v8);
-                    #pragma unroll
-                    for (int e = 0; e < 8; e++) {
-                        s = fmaf(q[c + e], k8[e], s);
-                        dp = fmaf(g[c + e], v8[e], dp);
-                    }
+                for (int e = 0; e < 8; e++) {
+                    s = fmaf(q8[e], k8[e], s);
+                    dp = fmaf(g8[e], v8[e], dp);
                 }
+            }
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            s += __shfl_xor_sync(0xffffffffu, s, 2);
+            dp += __shfl_xor_sync(0xffffffffu, dp, 1);
+            dp += __shfl_xor_sync(0xffffffffu, dp, 2);
+            float pj = 0.f, dsj = 0.f;
+            if (live) {
                 pj = expf(s * scale - l);
                 dsj = pj * (dp - delta);
             }
-            dsb[j] = dsj;
-            sds += dsj; sp += pj;
-            T* dr = dbase + (long)j * lddkv + h * DH;
-            float t8[8];
             #pragma unroll
-            for (int c = 0; c < DH; c += 8) {
+            for (int e = 0; e < 8; e++) dq8[e] = fmaf(dsj, k8[e], dq8[e]);
+            if (j < L) {
+                const float sd = scale * dsj;
                 #pragma unroll
-                for (int e = 0; e < 8; e++) t8[e] = scale * dsj * q[c + e];
-                st8(dr + c, t8);
+                for (int e = 0; e < 8; e++) t8[e] = sd * q8[e];
+                st8(dbase + (long)j * lddkv, t8);
                 #pragma unroll
-                for (int e = 0; e < 8; e++) t8[e] = pj * g[c + e];
-                st8(dr + D + c, t8);
+                for (int e = 0; e < 8; e++) t8[e] = pj * g8[e];
+                st8(dbase + (long)j * lddkv + D, t8);
             }
+            if ((lane & 3) == 0) { sds += dsj; sp += pj; }
         }
-        __syncwarp();
-        const T* kb = base + h * DH + lane;
-        float dq = 0.f;
-        for (int j = 0; j < L; j++) {
-            float d = dsb[j];
-            if (d != 0.f) dq = fmaf(d, to_f<T>(kb[(long)j * ldkv]), dq);
+        // dq: the 8 key-row groups' partial sums; sds / sp: one lane per row
+        #pragma unroll
+        for (int e = 0; e < 8; e++) {
+            #pragma unroll
+            for (int o = 4; o < 32; o <<= 1) dq8[e] += __shfl_xor_sync(0xffffffffu, dq8[e], o);
+            dq8[e] *= scale;
         }
-        dq *= scale;
-        dqo[(long)n * lddq + h * DH + lane] = from_f<T>(dq);
         sds = warp_sum(sds);
         sp = warp_sum(sp);
-        cq += dq;
-        ck += scale * sds * qd;
-        cv += sp * gd;
-        __syncwarp();
+        if (rg == 0) {
+            st8(dqo + (long)n * lddq + h * DH + c8, dq8);
+            #pragma unroll
+            for (int e = 0; e < 8; e++) {
+                acc[c8 + e] += dq8[e];
+                acc[32 + c8 + e] += scale * sds * q8[e];
+                acc[64 + c8 + e] += sp * g8[e];
+            }
+        }
     }
-    if (dbias) {
-        atomicAdd(&dbias[h * DH + lane], cq);
-        atomicAdd(&dbias[D + h * DH + lane], ck);
-        atomicAdd(&dbias[2 * D + h * DH + lane], cv);
-    }
+    __syncwarp();
+    if (dbias)
+        for (int i = lane; i < 96; i += 32) atomicAdd(&dbias[(i >> 5) * D + h * DH + (i & 31)], acc[i]);
 }
 
 int num_sms() {
@@ -884,7 +905,7 @@ void attn_row0_fwd(int dtype, const void* q, long ldq, const void* kv, long ldkv
                    const uint8_t* keep, void* out, long ldo, float* lse, int nseq, int L, int H,
                    cudaStream_t s) {
     if (nseq <= 0) return;
-    size_t sm = sizeof(float) * H * (DH + ((L + 31) & ~31));
+    size_t sm = sizeof(float) * H * ((L + 31) & ~31);
     if (dtype == DT_F32) {
         set_smem(k_attn_row0_fwd<float>, sm);
         ++g_ptcg_launches, k_attn_row0_fwd<float><<<nseq, H * 32, sm, s>>>((const float*)q, ldq,
@@ -901,7 +922,7 @@ void attn_row0_bwd(int dtype, const void* q, long ldq, const void* kv, long ldkv
                    const float* lse, void* dq, long lddq, void* dkv, long lddkv, float* dbias,
                    int nseq, int L, int H, cudaStream_t s) {
     if (nseq <= 0) return;
-    size_t sm = sizeof(float) * H * (2 * DH + ((L + 31) & ~31));
+    size_t sm = sizeof(float) * H * 96;
     int per_sm = H * 32 <= 256 ? 8 : 4;
     unsigned grid = (unsigned)std::min<long>(nseq, (long)num_sms() * per_sm);
     if (dtype == DT_F32) {
