@@ -648,52 +648,54 @@ __global__ void k_rowdot_bwd(TO* d_pre, long ldd, const TI* pre, long ldp, const
 // ------------------------------------------------------------ critic
 // oracle tokens [card_vec(id) | is_hand, is_split, is_prize, f3, f4, f5] and
 // critic keep [1, keep(LSEQ), id > 0] (k_otok_in, ptcg_model.cu:442-490)
+// One warp per oracle token: lanes 0..31 move the 128-float card vector as
+// float4s, lanes 0..5 the six trailing columns
 template <typename T>
 __global__ void k_otok_in(T* out, long ldo, uint8_t* ckeep, const float* obs, ObsLayout L,
                           const float* cv, const uint8_t* keep, int R) {
-    const int W = 134, NO = 56;
-    int lcrit = 1 + L.lseq + NO;
-    long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i >= (long)R * NO * W) return;
-    int c = (int)(i % W);
-    long nk = i / W;
-    int k = (int)(nk % NO), n = (int)(nk / NO);
+    const int NO = 56;
+    const int lcrit = 1 + L.lseq + NO;
+    const long nk = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (nk >= (long)R * NO) return;
+    const int n = (int)(nk / NO), k = (int)(nk - (long)n * NO);
     const float* o = obs + (long)n * L.obs + L.orc;
     float idf, f3 = 0.f, f4 = 0.f, f5 = 0.f;
     int kind;
     if (k < 24) { kind = 0; idf = o[k * 2]; f3 = o[k * 2 + 1]; }
     else if (k < 48) { kind = 1; int s = k - 24; idf = o[48 + s * 3]; f4 = o[49 + s * 3]; f5 = o[50 + s * 3]; }
     else { kind = 2; int s = k - 48; idf = o[120 + s * 2]; f3 = o[121 + s * 2]; }
-    float v;
-    if (c < 128) v = cv[(long)id_clamp(idf, L.nc) * 128 + c];
-    else if (c < 131) v = (c - 128) == kind ? 1.f : 0.f;
-    else if (c == 131) v = f3;
-    else if (c == 132) v = f4;
-    else v = f5;
-    st(&out[nk * ldo + c], v);
-    if (c == 0) {
-        uint8_t* ck = ckeep + (long)n * lcrit;
-        if (k == 0) {
-            ck[0] = 1;
-            for (int l = 0; l < L.lseq; l++) ck[1 + l] = keep[(long)n * L.lseq + l];
-        }
-        ck[1 + L.lseq + k] = (int)idf > 0;
+    T* orow = out + nk * ldo;
+    st4(orow + lane * 4, ld4(cv + (long)id_clamp(idf, L.nc) * 128 + lane * 4));
+    if (lane < 6) {
+        const int c = 128 + lane;
+        const float v = c < 131 ? ((c - 128) == kind ? 1.f : 0.f) : c == 131 ? f3 : c == 132 ? f4 : f5;
+        st(&orow[c], v);
     }
+    uint8_t* ck = ckeep + (long)n * lcrit;
+    if (k == 0) {
+        if (lane == 0) ck[0] = 1;
+        for (int l = lane; l < L.lseq; l += 32) ck[1 + l] = keep[(long)n * L.lseq + l];
+    }
+    if (lane == 0) ck[1 + L.lseq + k] = (int)idf > 0;
 }
 
+// d card_vec rows += the card-vector columns of the oracle-token input
+// gradient (g: [R * 56, >= 128], 16-byte rows); one thread per 4 columns,
+// vector reductions
 __global__ void k_otok_bwd(float* d_cv, const float* g, long ldg, const float* obs,
                            ObsLayout L, int R) {
     const int NO = 56;
     long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i >= (long)R * NO * 128) return;
-    int c = (int)(i % 128);
-    long nk = i / 128;
-    int k = (int)(nk % NO), n = (int)(nk / NO);
-    float v = g[nk * ldg + c];
-    if (v == 0.f) return;
+    if (i >= (long)R * NO * 32) return;
+    const int c = (int)(i & 31) * 4;
+    const long nk = i >> 5;
+    const int k = (int)(nk % NO), n = (int)(nk / NO);
+    const float4 v = ld4(g + nk * ldg + c);
+    if (!nz4(v)) return;
     const float* o = obs + (long)n * L.obs + L.orc;
     float idf = k < 24 ? o[k * 2] : k < 48 ? o[48 + (k - 24) * 3] : o[120 + (k - 48) * 2];
-    atomicAdd(&d_cv[(long)id_clamp(idf, L.nc) * 128 + c], v);
+    red_add4(&d_cv[(long)id_clamp(idf, L.nc) * 128 + c], v);
 }
 
 // critic sequence rows 0 (critic readout) and 1..LSEQ (trunk output h);

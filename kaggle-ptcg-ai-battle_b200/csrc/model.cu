@@ -744,12 +744,12 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     //  expanded to the fused layout at the end)
     // --- oracle critic top
     long ldo_t = rup(134, 8);
-    long no = (long)R * 56 * 134;
+    long no = (long)R * 56;                     // oracle tokens, one warp each
     if (dt == DT_F32)
-        ++g_ptcg_launches, k_otok_in<float><<<cdiv(no, TPB), TPB, 0, s>>>((float*)Wk.otokin, ldo_t, Wk.ckeep, obs, ol,
+        ++g_ptcg_launches, k_otok_in<float><<<cdiv(no, TPB / 32), TPB, 0, s>>>((float*)Wk.otokin, ldo_t, Wk.ckeep, obs, ol,
             t.card_vec, Wk.keep, R);
     else
-        ++g_ptcg_launches, k_otok_in<bf16><<<cdiv(no, TPB), TPB, 0, s>>>((bf16*)Wk.otokin, ldo_t, Wk.ckeep, obs, ol,
+        ++g_ptcg_launches, k_otok_in<bf16><<<cdiv(no, TPB / 32), TPB, 0, s>>>((bf16*)Wk.otokin, ldo_t, Wk.ckeep, obs, ol,
             t.card_vec, Wk.keep, R);
     ++g_ptcg_launches, k_xc_fill<<<cdiv((long)R * (1 + z.LSEQ), TPB / 32), TPB, 0, s>>>(Wk.xc[0], Wk.h,
         M->w("critic_readout").p, z.LSEQ, z.LCRIT, D, R, Wk.ext);
@@ -1025,7 +1025,7 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
     }
     gemm(M, lin_dw(dt, R * 56, 134, D, Wk.dotok, D, Wk.otokin, rup(134, 8), wo.g), s);
     gemm(M, lin_dx(dt, R * 56, 134, D, Wk.dotok, D, wo, Wk.dotokin, 136, DT_F32), s);
-    ++g_ptcg_launches, k_otok_bwd<<<cdiv((long)R * 56 * 128, TPB), TPB, 0, s>>>(t.d_cv, Wk.dotokin, 136, obs, ol, R);
+    ++g_ptcg_launches, k_otok_bwd<<<cdiv((long)R * 56 * 32, TPB), TPB, 0, s>>>(t.d_cv, Wk.dotokin, 136, obs, ol, R);
     // ---- option scorer (d scores = grad[:, :NOPT])
     ++g_ptcg_launches, k_scale_copy<<<cdiv(NO, TPB), TPB, 0, s>>>(Wk.dscores, z.NOPT, grad, z.NOPT + 1, R, z.NOPT, 1.f);
     {
