@@ -557,34 +557,52 @@ __global__ void k_pack_wqq(float* out, const float* w, int D, long ldw, int rows
     int o = (int)(i / (2 * D)), c = (int)(i % (2 * D));
     out[i] = w[(long)o * ldw + (c < D ? c : c + D + 192)];
 }
-// backward of qq and of [r | g | d], one block per sample (no atomics):
+// backward of qq and of [r | g | d], one block per sample:
 //   d_q[nj, c] = dqq[nj, c] + dqq[nj, D + c] r[c]        (+ q2 bias colsum)
 //   d_h[n, 0, c] += sum_j dqq[nj, D + c] q[nj, c] + drgd[n, c]
 //   d_gd[n, e]  += drgd[n, D + e]
+// Thread t takes the 4 columns 4 (t % (D/4)) .. of the options j = t / (D/4)
+// (mod blockDim / (D/4)); the option groups' sums meet in shared memory.
+// D % 4 == 0, D / 4 <= blockDim.x, 16-byte aligned rows.
 template <typename T>
 __global__ void k_qq_bwd(T* d_q, long lddq, float* d_h, float* d_gd, const float* dqq,
                          const float* qq, const float* drgd, const float* h, int D, int lseq,
                          int nopt, float* dq_colsum) {
-    int n = blockIdx.x;
-    const float* r = h + (long)n * lseq * D;
+    __shared__ float4 part[2][256];
+    const int n = blockIdx.x, t = threadIdx.x;
+    const int nc4 = D >> 2, G = blockDim.x / nc4;
+    const int grp = t / nc4, c = (t - grp * nc4) * 4;
     const float* dr = drgd + (long)n * (D + 192);
-    for (int c = threadIdx.x; c < D + 192; c += blockDim.x) {
-        if (c < D) {
-            float rr = r[c], acc = 0.f, cs = 0.f;
-            for (int j = 0; j < nopt; j++) {
-                long nj = (long)n * nopt + j;
-                const float* g = dqq + nj * 2 * D;
-                float dqv = g[c] + g[D + c] * rr;
-                st(&d_q[nj * lddq + c], dqv);
-                cs += dqv;
-                acc += g[D + c] * qq[nj * 2 * D + c];
-            }
-            d_h[(long)n * lseq * D + c] += acc + dr[c];
-            if (dq_colsum) atomicAdd(&dq_colsum[c], cs);
-        } else {
-            d_gd[(long)n * 192 + (c - D)] += dr[c];
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f), cs = acc;
+    if (grp < G) {
+        const float4 rr = ld4(h + (long)n * lseq * D + c);
+        for (int j = grp; j < nopt; j += G) {
+            const long nj = (long)n * nopt + j;
+            const float4 ga = ld4(dqq + nj * 2 * D + c), gb = ld4(dqq + nj * 2 * D + D + c);
+            const float4 q = ld4(qq + nj * 2 * D + c);
+            const float4 dqv = make_float4(ga.x + gb.x * rr.x, ga.y + gb.y * rr.y,
+                                           ga.z + gb.z * rr.z, ga.w + gb.w * rr.w);
+            st4(d_q + nj * lddq + c, dqv);
+            cs = add4(cs, dqv);
+            acc = make_float4(acc.x + gb.x * q.x, acc.y + gb.y * q.y,
+                              acc.z + gb.z * q.z, acc.w + gb.w * q.w);
         }
     }
+    part[0][t] = acc;
+    part[1][t] = cs;
+    __syncthreads();
+    if (t < nc4) {
+        for (int g = 1; g < G; g++) {
+            acc = add4(acc, part[0][g * nc4 + t]);
+            cs = add4(cs, part[1][g * nc4 + t]);
+        }
+        float* dh = d_h + (long)n * lseq * D + c;
+        const float4 o = ld4(dh);
+        st4(dh, make_float4(o.x + (acc.x + dr[c]), o.y + (acc.y + dr[c + 1]),
+                            o.z + (acc.z + dr[c + 2]), o.w + (acc.w + dr[c + 3])));
+        if (dq_colsum) red_add4(dq_colsum + c, cs);
+    }
+    for (int e = t; e < 192; e += blockDim.x) d_gd[(long)n * 192 + e] += dr[D + e];
 }
 
 // ------------------------------------------------------------ N=1 heads
