@@ -163,18 +163,24 @@ PTCG_DEV float4 ld4any(const bf16* p) {
 }
 
 // dy is float or bf16 (TY); statistics, dx and the parameter grads are fp32
-template <typename TC, int VEC, int MAXC, typename TY = float>
-__global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long lddxc,
+template <typename TC, int VEC, int MAXC, typename TY = float, bool CRIT = false>
+__global__ void __launch_bounds__(256, VEC == 2 ? 3 : 1) k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long lddxc,
                          float* dw, float* db, const TY* dy, long lddy,
                          const float* x, long ldx, const float* w, const float* mean,
                          const float* rstd, int rows, int D, int rows_per_block,
                          float* out_cs, const int* ext = nullptr, int lseq = 1,
-                         const uint8_t* rowkeep = nullptr) {
+                         const uint8_t* rowkeep = nullptr, float* crit_dh = nullptr,
+                         int crit_lseq = 0, int crit_lcrit = 0) {
     // out_cs (nullable): += column sums of the resulting dx (the bias grad
     // of the layer that produced this residual stream).  ext (nullable):
     // rows of each lseq-row sequence that anything reads; past it dy is zero
     // and so is the residual gradient, which is written as zeros without
-    // reading anything.  rowkeep (nullable): the same for rows marked 0
+    // reading anything.  rowkeep (nullable): the same for rows marked 0.
+    // crit_dh (CRIT instantiations, vector path): the rows are the critic's
+    // crit_lcrit-row sequences [readout | trunk rows | oracle tokens]; the
+    // crit_lseq trunk rows of sequence n go to crit_dh rows n * crit_lseq ..
+    // (d_h, ld D) instead of dx, the oracle-token rows also to dxc rows
+    // n * (crit_lcrit - 1 - crit_lseq) .., and row 0 to dx alone
     extern __shared__ float sh[];               // [3][D]
     float* sw = sh;
     float* sb = sh + D;
@@ -197,6 +203,18 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
             const float* xr = x + (long)row * ldx;
             const TY* dyr = dy + (long)row * lddy;
             float* dxr = dx + (long)row * lddx;
+            TC* dxcr = dxc ? dxc + (long)row * lddxc : nullptr;
+            if (CRIT) {
+                const int n = row / crit_lcrit, l = row - n * crit_lcrit;
+                if (l >= 1 && l <= crit_lseq) {
+                    dxr = crit_dh + ((long)n * crit_lseq + l - 1) * D;
+                    dxcr = nullptr;
+                } else if (l == 0) {
+                    dxcr = nullptr;
+                } else if (dxc) {
+                    dxcr = dxc + ((long)n * (crit_lcrit - 1 - crit_lseq) + (l - 1 - crit_lseq)) * lddxc;
+                }
+            }
             bool unread = rowkeep && !rowkeep[row];
             if (ext) {
                 const int n = row / lseq;
@@ -207,9 +225,9 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
                 for (int c = 0; c < VEC; c++) {
                     const int i = c * 128 + lane * 4;
                     *(float4*)(dxr + i) = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (dxc) {
-                        if (sizeof(TC) == 4) *(float4*)((float*)dxc + (long)row * lddxc + i) = make_float4(0.f, 0.f, 0.f, 0.f);
-                        else *(uint2*)((bf16*)dxc + (long)row * lddxc + i) = make_uint2(0u, 0u);
+                    if (dxcr) {
+                        if (sizeof(TC) == 4) *(float4*)((float*)dxcr + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+                        else *(uint2*)((bf16*)dxcr + i) = make_uint2(0u, 0u);
                     }
                 }
                 continue;
@@ -248,13 +266,13 @@ __global__ void k_ln_bwd(float* dx, long lddx, int accumulate, TC* dxc, long ldd
                 float o3 = (gv[c].w - m1 - xv[c].w * m2) * rs + av[c].w;
                 *(float4*)(dxr + i) = make_float4(o0, o1, o2, o3);
                 po[c].x += o0; po[c].y += o1; po[c].z += o2; po[c].w += o3;
-                if (dxc) {
+                if (dxcr) {
                     if (sizeof(TC) == 4) {
-                        *(float4*)((float*)dxc + (long)row * lddxc + i) = make_float4(o0, o1, o2, o3);
+                        *(float4*)((float*)dxcr + i) = make_float4(o0, o1, o2, o3);
                     } else {
                         __nv_bfloat162 q0 = __floats2bfloat162_rn(o0, o1), q1 = __floats2bfloat162_rn(o2, o3);
                         uint2 u; u.x = *(uint32_t*)&q0; u.y = *(uint32_t*)&q1;
-                        *(uint2*)((bf16*)dxc + (long)row * lddxc + i) = u;
+                        *(uint2*)((bf16*)dxcr + i) = u;
                     }
                 }
             }

@@ -361,11 +361,16 @@ static void ln_fwd(int dt, void* y, long ldy, float* mu, float* rs, const float*
 // dx (f32, ld D) = LN'(dy) (+ dx), copy to dxc (T) unless dxc == nullptr
 // out_cs (nullable): += column sums of the resulting dx.  dy is fp32, or in
 // the operand dtype when dy_dt == DT_BF16 (the output of a dX GEMM)
+// the vector LayerNorm backward (D = 256 or 512) can write the critic's
+// trunk-row input grads straight into d_h (crit_dh)
+static bool crit_rows_direct(int D) { return D == 256 || D == 512; }
+
 static void ln_bwd(int dt, float* dx, int accumulate, void* dxc, float* dw, float* db,
                    const void* dy, const float* x, const float* w, const float* mu,
                    const float* rs, int rows, int D, cudaStream_t s, float* out_cs = nullptr,
                    int dy_dt = DT_F32, const int* ext = nullptr, int lseq = 1,
-                   const uint8_t* rowkeep = nullptr) {
+                   const uint8_t* rowkeep = nullptr, float* crit_dh = nullptr,
+                   int crit_lseq = 0, int crit_lcrit = 0) {
     int rpb = 64;
     unsigned g = cdiv(rows, rpb);
     size_t sm = 3 * D * sizeof(float);
@@ -375,6 +380,15 @@ static void ln_bwd(int dt, float* dx, int accumulate, void* dxc, float* dw, floa
         ext, lseq, rowkeep)
 #define LNB2(TC, V, MC) do { if (dy_dt == DT_BF16) LNB(TC, V, MC, bf16); else LNB(TC, V, MC, float); } while (0)
     bool f = dt == DT_F32 || dxc == nullptr;
+    if (crit_dh) {                              // critic rows: crit_rows_direct(D), dy in dt
+#define LNBC(TC, V) ++g_ptcg_launches, k_ln_bwd<TC, V, 1, TC, true><<<g, 256, sm, s>>>(dx, D, \
+        accumulate, (TC*)dxc, D, dw, db, (const TC*)dy, D, x, D, w, mu, rs, rows, D, rpb, out_cs, \
+        ext, lseq, rowkeep, crit_dh, crit_lseq, crit_lcrit)
+        if (D == 256) { if (f) LNBC(float, 2); else LNBC(bf16, 2); }
+        else { if (f) LNBC(float, 4); else LNBC(bf16, 4); }
+#undef LNBC
+        return;
+    }
     if (D == 256) { if (f) LNB2(float, 2, 1); else LNB2(bf16, 2, 1); }
     else if (D == 512) { if (f) LNB2(float, 4, 1); else LNB2(bf16, 4, 1); }
     else if (D <= 256) { if (f) LNB2(float, 0, 8); else LNB2(bf16, 0, 8); }
@@ -882,9 +896,14 @@ static void block_bwd_row0(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t
         a.accumulate = 1;
         gemm(M, a, s);
     }
-    // d(x_in) = LN1'(dln) + the residual grad at row 0
-    ln_bwd(dt, Wk.dx, 0, nullptr, P.ln1w.g, P.ln1b.g, Wk.dln, b.x_in, P.ln1w.p, b.mu1, b.rs1,
-           NL, D, s, nullptr, dt, nullptr, 1, keep);
+    // d(x_in) = LN1'(dln) + the residual grad at row 0.  With the vector
+    // kernel the trunk rows 1..LSEQ go straight to d_h (its first writer)
+    // and the oracle-token rows also to d_otok, the oracle_proj GEMMs'
+    // operand; otherwise k_xc_bwd splits Wk.dx afterwards
+    const bool direct = crit_rows_direct(D);
+    ln_bwd(dt, Wk.dx, 0, direct ? Wk.dotok : nullptr, P.ln1w.g, P.ln1b.g, Wk.dln, b.x_in, P.ln1w.p,
+           b.mu1, b.rs1, NL, D, s, nullptr, dt, nullptr, 1, keep, direct ? Wk.dh : nullptr,
+           M->z.LSEQ, L);
     ++g_ptcg_launches, k_add_rows<<<cdiv((long)R * D, TPB), TPB, 0, s>>>(Wk.dx, (long)L * D, dx0, R, D);
 }
 
@@ -980,7 +999,8 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
         // rows 1..LSEQ -> d_h (stored), rows 1+LSEQ.. -> d_otok (compact)
         colsum_rows(M, M->w("critic_readout").g, Wk.dx, D, R, z.LCRIT, 0, 1, D, s);
         unsigned gb = cdiv((long)R * (z.LCRIT - 1), TPB / 32);
-        if (bf)
+        if (crit_rows_direct(D)) {}                 // done by the critic LN1 backward
+        else if (bf)
             ++g_ptcg_launches, k_xc_bwd<bf16><<<gb, TPB, 0, s>>>((bf16*)Wk.dotok, Wk.dh, Wk.dx, z.LSEQ, z.LCRIT, D, R, Wk.ext);
         else
             ++g_ptcg_launches, k_xc_bwd<float><<<gb, TPB, 0, s>>>((float*)Wk.dotok, Wk.dh, Wk.dx, z.LSEQ, z.LCRIT, D, R, Wk.ext);
