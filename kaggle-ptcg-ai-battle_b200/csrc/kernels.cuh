@@ -88,11 +88,15 @@ __global__ void k_pool_bwd(float* d_tab, const float* dsrc, int ld, int off_mean
 // sequence whose only query is its first row).  Skipped rows are left as
 // they are (finite: the workspace starts zeroed and only ever holds finite
 // values), since nothing reads them
-template <typename TO, int VEC>
+// CRIT (vector path): the rows are the critic's crit_lcrit-row sequences
+// [readout | trunk rows | oracle tokens], whose crit_lseq trunk rows are read
+// from crit_h (the trunk output, rows n * crit_lseq .., ld D) instead of x
+template <typename TO, int VEC, bool CRIT = false>
 __global__ void k_ln_fwd(TO* y, long ldy, float* mean, float* rstd, const float* x,
                          long ldx, const float* w, const float* b, int rows, int D,
                          const int* ext = nullptr, int lseq = 1,
-                         const uint8_t* rowkeep = nullptr) {
+                         const uint8_t* rowkeep = nullptr, const float* crit_h = nullptr,
+                         int crit_lseq = 0, int crit_lcrit = 0) {
     int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -102,6 +106,10 @@ __global__ void k_ln_fwd(TO* y, long ldy, float* mean, float* rstd, const float*
     }
     if (rowkeep && !rowkeep[row]) return;
     const float* xr = x + (long)row * ldx;
+    if (CRIT) {
+        const int n = row / crit_lcrit, l = row - n * crit_lcrit;
+        if (l >= 1 && l <= crit_lseq) xr = crit_h + ((long)n * crit_lseq + l - 1) * D;
+    }
     TO* yr = y + (long)row * ldy;
     if (VEC > 0) {
         float4 v[VEC > 0 ? VEC : 1];
@@ -170,7 +178,7 @@ __global__ void __launch_bounds__(256, VEC == 2 ? 3 : 1) k_ln_bwd(float* dx, lon
                          const float* rstd, int rows, int D, int rows_per_block,
                          float* out_cs, const int* ext = nullptr, int lseq = 1,
                          const uint8_t* rowkeep = nullptr, float* crit_dh = nullptr,
-                         int crit_lseq = 0, int crit_lcrit = 0) {
+                         int crit_lseq = 0, int crit_lcrit = 0, const float* crit_h = nullptr) {
     // out_cs (nullable): += column sums of the resulting dx (the bias grad
     // of the layer that produced this residual stream).  ext (nullable):
     // rows of each lseq-row sequence that anything reads; past it dy is zero
@@ -180,7 +188,9 @@ __global__ void __launch_bounds__(256, VEC == 2 ? 3 : 1) k_ln_bwd(float* dx, lon
     // crit_lcrit-row sequences [readout | trunk rows | oracle tokens]; the
     // crit_lseq trunk rows of sequence n go to crit_dh rows n * crit_lseq ..
     // (d_h, ld D) instead of dx, the oracle-token rows also to dxc rows
-    // n * (crit_lcrit - 1 - crit_lseq) .., and row 0 to dx alone
+    // n * (crit_lcrit - 1 - crit_lseq) .., and row 0 to dx alone.  crit_h
+    // (nullable): the trunk rows' x is read from there (rows n * crit_lseq
+    // .., ld D), as the CRIT forward did
     extern __shared__ float sh[];               // [3][D]
     float* sw = sh;
     float* sb = sh + D;
@@ -209,6 +219,7 @@ __global__ void __launch_bounds__(256, VEC == 2 ? 3 : 1) k_ln_bwd(float* dx, lon
                 if (l >= 1 && l <= crit_lseq) {
                     dxr = crit_dh + ((long)n * crit_lseq + l - 1) * D;
                     dxcr = nullptr;
+                    if (crit_h) xr = crit_h + ((long)n * crit_lseq + l - 1) * D;
                 } else if (l == 0) {
                     dxcr = nullptr;
                 } else if (dxc) {

@@ -347,11 +347,26 @@ template <typename T> static void colsum(float* out, const T* in, long ld, int r
 
 // ext / lseq (nullable / unused): rows of each lseq-row sequence anything
 // reads (k_row_extent); the rest are skipped
+// the vector LayerNorm kernels (D = 256 or 512) can read the critic's trunk
+// rows straight from h and write their input grads straight into d_h
+static bool crit_rows_direct(int D) { return D == 256 || D == 512; }
+
+// crit_h (nullable; crit_rows_direct(D)): the rows are critic sequences whose
+// trunk rows are read from crit_h (k_ln_fwd CRIT)
 static void ln_fwd(int dt, void* y, long ldy, float* mu, float* rs, const float* x, long ldx,
                    const float* w, const float* b, int rows, int D, cudaStream_t s,
-                   const int* ext = nullptr, int lseq = 1, const uint8_t* rowkeep = nullptr) {
+                   const int* ext = nullptr, int lseq = 1, const uint8_t* rowkeep = nullptr,
+                   const float* crit_h = nullptr, int crit_lseq = 0, int crit_lcrit = 0) {
     unsigned g = cdiv(rows, 8);
     bool vec = D % 128 == 0 && D <= 1024 && ldx % 4 == 0 && ldy % 4 == 0;
+    if (crit_h) {
+#define LNFC(TO, V) ++g_ptcg_launches, k_ln_fwd<TO, V, true><<<g, 256, 0, s>>>((TO*)y, ldy, mu, rs, x, ldx, \
+        w, b, rows, D, ext, lseq, rowkeep, crit_h, crit_lseq, crit_lcrit)
+        if (D == 256) { if (dt == DT_F32) LNFC(float, 2); else LNFC(bf16, 2); }
+        else { if (dt == DT_F32) LNFC(float, 4); else LNFC(bf16, 4); }
+#undef LNFC
+        return;
+    }
 #define LNF(TO, V) ++g_ptcg_launches, k_ln_fwd<TO, V><<<g, 256, 0, s>>>((TO*)y, ldy, mu, rs, x, ldx, w, b, rows, D, ext, lseq, rowkeep)
     if (vec && D == 256) { if (dt == DT_F32) LNF(float, 2); else LNF(bf16, 2); }
     else if (vec && D == 512) { if (dt == DT_F32) LNF(float, 4); else LNF(bf16, 4); }
@@ -361,16 +376,12 @@ static void ln_fwd(int dt, void* y, long ldy, float* mu, float* rs, const float*
 // dx (f32, ld D) = LN'(dy) (+ dx), copy to dxc (T) unless dxc == nullptr
 // out_cs (nullable): += column sums of the resulting dx.  dy is fp32, or in
 // the operand dtype when dy_dt == DT_BF16 (the output of a dX GEMM)
-// the vector LayerNorm backward (D = 256 or 512) can write the critic's
-// trunk-row input grads straight into d_h (crit_dh)
-static bool crit_rows_direct(int D) { return D == 256 || D == 512; }
-
 static void ln_bwd(int dt, float* dx, int accumulate, void* dxc, float* dw, float* db,
                    const void* dy, const float* x, const float* w, const float* mu,
                    const float* rs, int rows, int D, cudaStream_t s, float* out_cs = nullptr,
                    int dy_dt = DT_F32, const int* ext = nullptr, int lseq = 1,
                    const uint8_t* rowkeep = nullptr, float* crit_dh = nullptr,
-                   int crit_lseq = 0, int crit_lcrit = 0) {
+                   int crit_lseq = 0, int crit_lcrit = 0, const float* crit_h = nullptr) {
     int rpb = 64;
     unsigned g = cdiv(rows, rpb);
     size_t sm = 3 * D * sizeof(float);
@@ -383,7 +394,7 @@ static void ln_bwd(int dt, float* dx, int accumulate, void* dxc, float* dw, floa
     if (crit_dh) {                              // critic rows: crit_rows_direct(D), dy in dt
 #define LNBC(TC, V) ++g_ptcg_launches, k_ln_bwd<TC, V, 1, TC, true><<<g, 256, sm, s>>>(dx, D, \
         accumulate, (TC*)dxc, D, dw, db, (const TC*)dy, D, x, D, w, mu, rs, rows, D, rpb, out_cs, \
-        ext, lseq, rowkeep, crit_dh, crit_lseq, crit_lcrit)
+        ext, lseq, rowkeep, crit_dh, crit_lseq, crit_lcrit, crit_h)
         if (D == 256) { if (f) LNBC(float, 2); else LNBC(bf16, 2); }
         else { if (f) LNBC(float, 4); else LNBC(bf16, 4); }
 #undef LNBC
@@ -601,13 +612,16 @@ static void block_fwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
 // output is read there alone): LN1 and QKV over every row (keys / values),
 // then single-query attention, proj, LN2 and the FFN on R rows.  x_out and
 // the post-attention activations are compact [R, ...].
+// h (nullable): the trunk output; when given, the critic's trunk rows are
+// read from it (crit_rows_direct(D)) and b.x_in holds rows 0 and LSEQ+1..
 static void block_fwd_row0(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* keep, int R,
-                           int L, bool train, cudaStream_t s) {
+                           int L, bool train, cudaStream_t s, const float* h = nullptr) {
     const Dims& z = M->z;
     const int dt = M->dt(), D = z.D;
     const int NL = R * L;
     // rows other than the query row and the kept keys are read by nothing
-    ln_fwd(dt, b.ln1, D, b.mu1, b.rs1, b.x_in, D, P.ln1w.p, P.ln1b.p, NL, D, s, nullptr, 1, keep);
+    ln_fwd(dt, b.ln1, D, b.mu1, b.rs1, b.x_in, D, P.ln1w.p, P.ln1b.p, NL, D, s, nullptr, 1, keep,
+           h, z.LSEQ, L);
     // keys and values of every row (weight rows D..3D), queries of the
     // readout rows only (weight rows 0..D; A rows at stride L * D)
     GemmArgs a = lin_fwd(dt, NL, D, 2 * D, b.ln1, D, wrows(P.qkvw, D, D, M->esz()), b.qkv, 2 * D, dt);
@@ -765,14 +779,19 @@ static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* 
     else
         ++g_ptcg_launches, k_otok_in<bf16><<<cdiv(no, TPB / 32), TPB, 0, s>>>((bf16*)Wk.otokin, ldo_t, Wk.ckeep, obs, ol,
             t.card_vec, Wk.keep, R);
-    ++g_ptcg_launches, k_xc_fill<<<cdiv((long)R * (1 + z.LSEQ), TPB / 32), TPB, 0, s>>>(Wk.xc[0], Wk.h,
-        M->w("critic_readout").p, z.LSEQ, z.LCRIT, D, R, Wk.ext);
+    // critic rows 0 and 1..LSEQ; with crit_rows_direct(D) the trunk rows are
+    // read from h by the critic's LN1 and only row 0 is written
+    const bool crit_direct = crit_rows_direct(D);
+    const int xc_rows = crit_direct ? 0 : z.LSEQ;
+    ++g_ptcg_launches, k_xc_fill<<<cdiv((long)R * (1 + xc_rows), TPB / 32), TPB, 0, s>>>(Wk.xc[0], Wk.h,
+        M->w("critic_readout").p, xc_rows, z.LCRIT, D, R, Wk.ext);
     a = lin_fwd(dt, R * 56, 134, D, Wk.otokin, ldo_t, M->w("oracle_proj_w"), Wk.xc[0], D, DT_F32);
     a.bias = M->w("oracle_proj_b").p;
     a.remap_group = 56; a.remap_stride = z.LCRIT; a.remap_off = 1 + z.LSEQ;
     gemm(M, a, s);
     Wk.cblk.x_in = Wk.xc[0]; Wk.cblk.x_out = Wk.xc[1];
-    block_fwd_row0(M, M->blk("c0_"), Wk.cblk, Wk.ckeep, R, z.LCRIT, train, s);
+    block_fwd_row0(M, M->blk("c0_"), Wk.cblk, Wk.ckeep, R, z.LCRIT, train, s,
+                   crit_direct ? Wk.h : nullptr);
     ++g_ptcg_launches, k_val_in<float><<<cdiv((long)R * z.VAL_IN, TPB), TPB, 0, s>>>(Wk.ovin, nullptr, 0, Wk.xc[1],
         1, D, Wk.gd, R);
     a = lin_fwd(DT_F32, R, z.VAL_IN, 256, Wk.ovin, z.VAL_IN, f32w(M->w("oracle_v1_w"), z.VAL_IN),
@@ -903,7 +922,7 @@ static void block_bwd_row0(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t
     const bool direct = crit_rows_direct(D);
     ln_bwd(dt, Wk.dx, 0, direct ? Wk.dotok : nullptr, P.ln1w.g, P.ln1b.g, Wk.dln, b.x_in, P.ln1w.p,
            b.mu1, b.rs1, NL, D, s, nullptr, dt, nullptr, 1, keep, direct ? Wk.dh : nullptr,
-           M->z.LSEQ, L);
+           M->z.LSEQ, L, direct ? Wk.h : nullptr);
     ++g_ptcg_launches, k_add_rows<<<cdiv((long)R * D, TPB), TPB, 0, s>>>(Wk.dx, (long)L * D, dx0, R, D);
 }
 
