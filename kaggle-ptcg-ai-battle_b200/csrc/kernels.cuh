@@ -692,6 +692,49 @@ __global__ void k_rowdot_bwd(TO* d_pre, long ldd, const TI* pre, long ldp, const
     if (threadIdx.x == 0) atomicAdd(db, shd[K]);
 }
 
+// k_rowdot_bwd for fp32 rows with a saved GELU' and no aux-loss mode (the
+// option scorer's score2, NOPT rows per block): float4 columns, the block's
+// rows split over blockDim / (K/4) thread groups whose partial sums meet in
+// shared memory.  K % 4 == 0, K / 4 <= blockDim.x <= 256, 16-byte aligned
+// rows and vectors.
+__global__ void k_rowdot_bwd_v4(float* d_pre, long ldd, const float* pre, long ldp,
+                                const float* in, long ldi, const float* w, float* dw, float* db,
+                                const float* dsrc, long ds_stride, int rows, int K,
+                                int rows_per_block, float* dpre_colsum, float* dpre_blocksum) {
+    __shared__ float4 part[2][256];
+    const int t = threadIdx.x, nc4 = K >> 2, G = blockDim.x / nc4;
+    const int grp = t / nc4, c = (t - grp * nc4) * 4;
+    const int r0 = blockIdx.x * rows_per_block, r1 = min(rows, r0 + rows_per_block);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f), cs = acc;
+    float dsum = 0.f;
+    if (grp < G) {
+        const float4 w4 = ld4(w + c);
+        for (int r = r0 + grp; r < r1; r += G) {
+            const float d = dsrc[(long)r * ds_stride];
+            const float4 x = ld4(in + (long)r * ldi + c);
+            const float4 p = ld4(pre + (long)r * ldp + c);
+            acc = make_float4(acc.x + d * x.x, acc.y + d * x.y, acc.z + d * x.z, acc.w + d * x.w);
+            const float4 v = make_float4(d * w4.x * p.x, d * w4.y * p.y, d * w4.z * p.z, d * w4.w * p.w);
+            st4(d_pre + (long)r * ldd + c, v);
+            cs = add4(cs, v);
+            dsum += d;
+        }
+    }
+    part[0][t] = acc;
+    part[1][t] = cs;
+    __syncthreads();
+    if (t < nc4) {
+        for (int g = 1; g < G; g++) {
+            acc = add4(acc, part[0][g * nc4 + t]);
+            cs = add4(cs, part[1][g * nc4 + t]);
+        }
+        red_add4(dw + c, acc);
+        if (dpre_colsum) red_add4(dpre_colsum + c, cs);
+        if (dpre_blocksum) st4(dpre_blocksum + (long)blockIdx.x * K + c, cs);
+    }
+    if (c == 0 && grp < G && dsum != 0.f) atomicAdd(db, dsum);
+}
+
 // ------------------------------------------------------------ critic
 // oracle tokens [card_vec(id) | is_hand, is_split, is_prize, f3, f4, f5] and
 // critic keep [1, keep(LSEQ), id > 0] (k_otok_in, ptcg_model.cu:442-490)

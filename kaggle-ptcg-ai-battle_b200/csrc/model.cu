@@ -1072,10 +1072,10 @@ static int backward_impl(PtcgModel* M, Work& Wk, const float* obs, const float* 
         // per-sample broadcast term of score1)
         int rpb = z.NOPT;
         unsigned g = cdiv(NO, rpb);
-        ++g_ptcg_launches, k_rowdot_bwd<float, float><<<g, 256, 257 * sizeof(float), s>>>((float*)Wk.ds1pre, 256,
+        ++g_ptcg_launches, k_rowdot_bwd_v4<<<g, 256, 0, s>>>((float*)Wk.ds1pre, 256,
                 (const float*)Wk.s1pre, 256, (const float*)Wk.s1, 256, M->w("score2_w").p,
-                M->w("score2_w").g, M->w("score2_b").g, Wk.dscores, 1, nullptr, 0.f, (int)NO, 256,
-                rpb, nullptr, M->w("score1_b").g, Wk.du);
+                M->w("score2_w").g, M->w("score2_b").g, Wk.dscores, 1, (int)NO, 256, rpb,
+                M->w("score1_b").g, Wk.du);
     }
     W ws1 = f32w(M->w("score1_w"), z.SCORE_IN);
     const float* qq = (const float*)Wk.scin;
