@@ -32,6 +32,13 @@ enum {
 
 enum { PTCG_FP32 = 0, PTCG_BF16 = 1 };
 
+/* Flag bits of ptcg_backward's `accumulate` argument. */
+enum {
+    PTCG_BWD_ACCUMULATE = 1,   /* add into the grad arena instead of zeroing it first */
+    PTCG_BWD_PARTIAL = 2       /* more micro-batches of this step follow: the grads are
+                                  not final, so the grad hook does not fire */
+};
+
 /* Runtime model shape.  Replaces the compile-time PT_D/PT_H/PT_FFN/PT_LAYERS,
  * PT_LTOK, PT_NOPT, PT_NC/PT_NA/PT_NS and the token feature width
  * (native/model/ptcg_model.cu:14-82; native/tools/native_weights.py:24-37).
@@ -51,6 +58,10 @@ int ptcg_abi_version(void);
  * Packed fp32 weight blob order = PT_PARAMS (native/model/ptcg_model.cu:95-126,
  * mirrored by native/tools/native_weights.py:45-91).  cols == 0 for 1-D. */
 long ptcg_obs_size(const PtcgShape* s);
+/* Column of the acting seat in an observation row: global_f[31]
+ * (GlobF.ACTOR_SEAT, ptcg/rl/buffers.py:170; PT_SEAT_COL_M of
+ * native/model/ptcg_model2.cu:287). */
+long ptcg_seat_column(const PtcgShape* s);
 int  ptcg_num_params(const PtcgShape* s);
 int  ptcg_param_info(const PtcgShape* s, int i, const char** name, long* rows, long* cols);
 long ptcg_param_total(const PtcgShape* s);
@@ -119,15 +130,41 @@ int ptcg_forward(PtcgModel* m, const float* obs, int n, float* out, void* stream
  * native/model/ptcg_model3.cu:357-369). */
 int ptcg_forward_train(PtcgModel* m, const float* obs, int n, float* out, void* stream);
 
+/* Caller-owned rollout workspace: activation buffers for `rows` rollout
+ * rows plus the static-table activations, separate from the model's own
+ * (ptcg_reserve).  The reference gives each rollout buffer its own
+ * activation set (native/src/pufferlib.cu:2618-2627) and runs the buffers'
+ * forwards concurrently on per-buffer streams (:503-509); one workspace per
+ * buffer lets forwards on different streams run without sharing anything
+ * they write.  Allocates once, at creation. */
+typedef struct PtcgWorkspace PtcgWorkspace;
+int ptcg_workspace_create(PtcgModel* m, int rows, PtcgWorkspace** out);
+int ptcg_workspace_destroy(PtcgWorkspace* ws);
+/* ptcg_forward into a caller-owned workspace (n <= its rows). */
+int ptcg_forward_ws(PtcgModel* m, PtcgWorkspace* ws, const float* obs, int n, float* out,
+                    void* stream);
+
+/* Copy an fp32 parameter arena in this model's layout (PT_PARAMS order,
+ * each tensor at a 16-byte-aligned offset, the layout of the reference's
+ * Allocator, native/src/kernels.cu:433-466) into the model's master weights
+ * and refresh the bf16 compute copies, on `stream`.  For trainers whose own
+ * optimizer updates their own copy of the weights (the reference's
+ * muon_step on its params arena).  n_floats may stop short of the model's
+ * padded arena end. */
+int ptcg_import_params(PtcgModel* m, const float* arena, long n_floats, void* stream);
+
 /* Backward of the last ptcg_forward_train: grad (n x (nopt+1)) =
  * [d raw scores | d oracle value]; `returns` (n) feeds the blind-V aux loss
  * (the reference binds it through ptcg_bind_train_graph,
  * native/model/ptcg_model2.cu:323-330).  aux_norm_rows / prize_count give the
  * minibatch-wide normalisers of the aux losses (rows of the whole minibatch;
  * number of MY_UNSEEN tokens in it, <= 0 means "count these rows").
- * accumulate = 0 zeroes the grad arena first (native/model/ptcg_model4.cu:15-21),
- * 1 adds to it (micro-batching).  Replaces Encoder.backward + Decoder.backward
- * (ptcg_model4.cu:10-190, 277-306). */
+ * accumulate is a set of PTCG_BWD_* bits: without PTCG_BWD_ACCUMULATE the
+ * grad arena is zeroed first (native/model/ptcg_model4.cu:15-21), with it the
+ * call adds to the arena (micro-batching).  A micro-batched step passes
+ * PTCG_BWD_PARTIAL on every call but its last, so that the grad hook
+ * (ptcg_set_grad_hook) fires once per step, on final grads.  Replaces
+ * Encoder.backward + Decoder.backward (ptcg_model4.cu:10-190, 277-306). */
 int ptcg_backward(PtcgModel* m, const float* grad, const float* returns,
                   int aux_norm_rows, float prize_count, int accumulate, void* stream);
 
@@ -162,7 +199,10 @@ int ptcg_ppo_loss(const float* dec_out, int nopt, const float* mask,
  *    224 KiB per device); larger minibatches return PTCG_ERANGE.
  *  - Set-up: the first call on each device (with that device current)
  *    looks up the array's device address once and caches it; make that
- *    first call before any stream capture.
+ *    first call before any stream capture.  The cached address lives for
+ *    the process: a cudaDeviceReset (or any teardown of the device's
+ *    primary context) after that first call is not supported, since the
+ *    library may be loaded again at another address.
  *  - Nothing in the array needs to start at zero: every value the kernels
  *    read is written earlier in the same call.
  *  - One array per device: calls that overlap on the same device (on
@@ -240,18 +280,21 @@ int ptcg_sample_logits(const float* dec_out, int n, int nopt, const float* mask,
                        long mask_stride, const float* uniforms, float* actions,
                        float* logprobs, float* values, void* stream);
 
-/* Seat-flipping GAE / V-trace over (B, T) rollouts; seats are read from
- * obs[:, :, seat_col].  Replaces ptcg_puff_advantage
- * (native/model/ptcg_model2.cu:288-321). */
-int ptcg_puff_advantage(const float* values, const float* rewards,
-                        const float* dones, const float* importance,
-                        const float* obs, long obs_size, int seat_col, int B, int T,
-                        float gamma, float lambda, float rho_clip, float c_clip,
-                        float* advantages, void* stream);
+/* Seat-flipping GAE / V-trace over (B, T) rollouts on raw device pointers;
+ * seats are read from obs[:, :, seat_col] with rows of obs_size floats.  The
+ * computation of the reference's ptcg_puff_advantage
+ * (native/model/ptcg_model2.cu:288-321); the export with the reference's
+ * own name and PrecisionTensor signature is in ptcg_puffer.h. */
+int ptcg_negamax_advantage(const float* values, const float* rewards,
+                           const float* dones, const float* importance,
+                           const float* obs, long obs_size, int seat_col, int B, int T,
+                           float gamma, float lambda, float rho_clip, float c_clip,
+                           float* advantages, void* stream);
 
 /* Gradient-bucket hook for data parallelism: called on the host, in backward
  * order, each time the grads in arena floats [offset, offset+count) are final
- * for this step (only during the last micro-batch), with the compute stream.
+ * for this step, with the compute stream: during ptcg_train_step's last
+ * micro-batch, and during each ptcg_backward call without PTCG_BWD_PARTIAL.
  * The callee typically records an event and starts an all-reduce of that
  * bucket on its own stream.  Replaces the post-backward ncclAllReduce of
  * native/src/muon.cu:212-213. */
@@ -325,9 +368,10 @@ int ptcg_attention_bwd(int operand_dtype, const void* qkv, long ldqkv, const uns
                        const void* out, long ldo, const void* dout, long lddo, const float* lse,
                        void* dqkv, long lddqkv, float* dbias, int nseq, int L, int H,
                        void* stream);
-/* The GELU and GELU' that the tensor-core GEMM epilogues evaluate (erf by
- * Abramowitz & Stegun 7.1.26), exposed so tests can bound their error
- * against the exact erf form of torch nn.GELU. */
+/* The GELU and GELU' that the tensor-core GEMM epilogues evaluate (erfc as
+ * exp(-a^2) times a degree-10 least-squares fit of erfcx on [0, 4], made for
+ * this library), exposed so tests can bound their error against the exact
+ * erf form of torch nn.GELU. */
 int ptcg_eval_gelu(const float* x, float* gelu, float* gelu_grad, int n, void* stream);
 /* tcgen05 GEMM role counters (clock cycles, summed over CTAs): {producer
  * waiting for free ring slots, MMA waiting for loaded slots, MMA waiting for

@@ -3,10 +3,12 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 enum { DT_F32 = 0, DT_BF16 = 1 };
 
 // number of kernels this library has launched (every launch site increments it)
-extern long long g_ptcg_launches;
+extern std::atomic<long long> g_ptcg_launches;
 enum { ACT_NONE = 0, ACT_GELU = 1, ACT_GELU_BWD = 2 };
 
 // C[m, n] = epilogue( alpha * sum_k A(m, k) * B(n, k) )

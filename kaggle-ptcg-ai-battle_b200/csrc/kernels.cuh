@@ -1448,6 +1448,19 @@ __global__ void k_step_inc(long long* step_dev, const float* stats) {
     if (stats[1] != 0.f) step_dev[0] += 1;
 }
 
+// Zero a workspace after a step whose gradient norm was not finite.  Rows
+// past a sequence's extent keep whatever an earlier micro-batch left there,
+// and the weight-gradient GEMMs multiply them by exact-zero gradients; one
+// Inf / NaN kept in such a row would make 0 * Inf = NaN in every later
+// weight gradient.  A finite norm makes this a one-load no-op per block.
+__global__ void k_zero_if_nonfinite(const float* stats, uint4* base, long n16) {
+    if (isfinite(stats[0])) return;
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n16;
+         i += (long)gridDim.x * blockDim.x)
+        base[i] = z;
+}
+
 __global__ void k_gelu_bwd(float* d, const float* pre, long n) {
     long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
     if (i < n) d[i] *= pre[i];                                    // saved GELU'

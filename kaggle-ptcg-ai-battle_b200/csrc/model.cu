@@ -30,7 +30,7 @@
 #include <mutex>
 #include <unordered_map>
 
-long long g_ptcg_launches = 0;
+std::atomic<long long> g_ptcg_launches{0};
 
 // ------------------------------------------------------------------ errors
 static thread_local char g_err[1024];
@@ -538,9 +538,8 @@ static void plan_tab(Tab& t, Bump& m, const Dims& z) {
 }
 
 // --------------------------------------------------------------- forward
-static void tables_fwd(PtcgModel* M, cudaStream_t s) {
+static void tables_fwd(PtcgModel* M, Tab& t, cudaStream_t s) {
     const Dims& z = M->z;
-    Tab& t = M->tab;
     Segs g{};
     g.n = 3;
     g.s[0] = {M->w("attack_id_emb").p, 48, 0, 48, 0};
@@ -673,14 +672,13 @@ static void rowdot(float* out, long os, const TI* in, long ldi, const float* w, 
     ++g_ptcg_launches, k_rowdot<TI><<<cdiv(rows, 8), 256, 0, s>>>(out, os, in, ldi, w, b, rows, K, g, gs, go);
 }
 
-static int forward_impl(PtcgModel* M, Work& Wk, const float* obs, int R, float* out, bool train,
-                        bool do_tables, cudaStream_t s) {
+static int forward_impl(PtcgModel* M, Work& Wk, Tab& t, const float* obs, int R, float* out,
+                        bool train, bool do_tables, cudaStream_t s) {
     const Dims& z = M->z;
     const int dt = M->dt(), D = z.D, esz = M->esz();
     const ObsLayout& ol = z.ol;
     const int tf32 = M->prec == PTCG_BF16;   // fp32-operand GEMMs may use TF32 in bf16 mode
-    if (do_tables) tables_fwd(M, s);
-    const Tab& t = M->tab;
+    if (do_tables) tables_fwd(M, t, s);
     // --- token path
     long ldtok = rup(z.TOK_IN, 8);
     ++g_ptcg_launches, k_x0_readout<<<cdiv((long)R * (z.LSEQ > D ? z.LSEQ : D), TPB), TPB, 0, s>>>(Wk.x[0], Wk.keep,
@@ -1247,6 +1245,11 @@ long ptcg_obs_size(const PtcgShape* s) {
     return make_layout(*s).obs;
 }
 
+long ptcg_seat_column(const PtcgShape* s) {
+    if (check_shape(s)) return -1;
+    return make_layout(*s).glob + 31;              // global_f[31], GlobF.ACTOR_SEAT
+}
+
 int ptcg_num_params(const PtcgShape* s) {
     if (check_shape(s)) return -1;
     return (int)param_defs(*s).size();
@@ -1631,7 +1634,7 @@ static int reserve_one(PtcgModel* M, Work& W, int rows, bool train) {
     free_work(W);
     Bump b{nullptr, 0, true};
     plan_work(W, b, rows, train, M->z, M->esz(), M->prec == PTCG_BF16);
-    size_t bytes = b.off;
+    size_t bytes = (b.off + 255) & ~(size_t)255;
     void* base = nullptr;
     cudaError_t e = cudaMalloc(&base, bytes);
     if (e != cudaSuccess) {
@@ -1670,7 +1673,7 @@ int ptcg_forward(PtcgModel* M, const float* obs, int n, float* out, void* stream
         M->roll.R);
     if (n == 0) return PTCG_OK;
     CK(cudaSetDevice(M->dev));
-    forward_impl(M, M->roll, obs, n, out, false, true, (cudaStream_t)stream);
+    forward_impl(M, M->roll, M->tab, obs, n, out, false, true, (cudaStream_t)stream);
     CKL();
     return PTCG_OK;
 }
@@ -1681,9 +1684,82 @@ int ptcg_forward_train(PtcgModel* M, const float* obs, int n, float* out, void* 
     REQ(obs && out && n > 0, PTCG_EINVAL, "bad arguments");
     REQ(M->trn.base && n <= M->trn.R, PTCG_ERANGE, "train batch %d exceeds reserved %d", n, M->trn.R);
     CK(cudaSetDevice(M->dev));
-    forward_impl(M, M->trn, obs, n, out, true, true, (cudaStream_t)stream);
+    forward_impl(M, M->trn, M->tab, obs, n, out, true, true, (cudaStream_t)stream);
     M->trn_last_obs = obs; M->trn_last_n = n;
     CKL();
+    return PTCG_OK;
+}
+
+// Caller-owned rollout workspace: activations and static-table activations
+// of their own, so rollout forwards on different streams (one per buffer)
+// share nothing they write.
+struct PtcgWorkspace {
+    PtcgModel* M = nullptr;
+    Work w;
+    Tab tab;
+    void* tab_base = nullptr;
+};
+
+int ptcg_workspace_create(PtcgModel* M, int rows, PtcgWorkspace** out) {
+    REQ(M && out && rows > 0, PTCG_EINVAL, "bad arguments");
+    *out = nullptr;
+    CK(cudaSetDevice(M->dev));
+    PtcgWorkspace* W = new PtcgWorkspace();
+    W->M = M;
+    int e = reserve_one(M, W->w, rows, false);
+    if (e) { delete W; return e; }
+    Bump b{nullptr, 0, true};
+    plan_tab(W->tab, b, M->z);
+    cudaError_t ce = cudaMalloc(&W->tab_base, b.off);
+    if (ce != cudaSuccess) {
+        cudaGetLastError();
+        free_work(W->w);
+        delete W;
+        set_err("workspace: cannot allocate %.1f MB of table activations: %s", b.off / 1e6,
+                cudaGetErrorString(ce));
+        return PTCG_ECUDA;
+    }
+    CK(cudaMemset(W->tab_base, 0, b.off));
+    Bump b2{(char*)W->tab_base, 0, false};
+    plan_tab(W->tab, b2, M->z);
+    *out = W;
+    return PTCG_OK;
+}
+
+int ptcg_workspace_destroy(PtcgWorkspace* W) {
+    if (!W) return PTCG_OK;
+    CK(cudaSetDevice(W->M->dev));
+    CK(cudaDeviceSynchronize());
+    free_work(W->w);
+    if (W->tab_base) cudaFree(W->tab_base);
+    delete W;
+    return PTCG_OK;
+}
+
+int ptcg_forward_ws(PtcgModel* M, PtcgWorkspace* W, const float* obs, int n, float* out,
+                    void* stream) {
+    int e = ready(M);
+    if (e) return e;
+    REQ(W && W->M == M, PTCG_EINVAL, "workspace belongs to another model");
+    REQ(obs && out && n >= 0, PTCG_EINVAL, "bad arguments");
+    REQ(n <= W->w.R, PTCG_ERANGE, "rollout batch %d exceeds the workspace's %d rows", n, W->w.R);
+    if (n == 0) return PTCG_OK;
+    CK(cudaSetDevice(M->dev));
+    forward_impl(M, W->w, W->tab, obs, n, out, false, true, (cudaStream_t)stream);
+    CKL();
+    return PTCG_OK;
+}
+
+int ptcg_import_params(PtcgModel* M, const float* arena, long n_floats, void* stream) {
+    REQ(M && arena, PTCG_EINVAL, "null argument");
+    REQ(n_floats > 0 && n_floats <= M->n_arena, PTCG_EINVAL,
+        "arena of %ld floats, the model's holds %ld", n_floats, M->n_arena);
+    CK(cudaSetDevice(M->dev));
+    cudaStream_t s = (cudaStream_t)stream;
+    CK(cudaMemcpyAsync(M->params, arena, (size_t)n_floats * 4, cudaMemcpyDeviceToDevice, s));
+    int e = refresh_copies(M, s);
+    if (e) return e;
+    M->weights_ready = true;
     return PTCG_OK;
 }
 
@@ -1706,12 +1782,18 @@ int ptcg_backward(PtcgModel* M, const float* grad, const float* returns, int aux
         CK(cudaMemsetAsync(cnt, 0, sizeof(float), s));
         ++g_ptcg_launches, k_count_unseen<<<64, 256, 0, s>>>(cnt, M->trn_last_obs, M->z.ol, R);
     }
-    if (!accumulate) CK(cudaMemsetAsync(M->grads, 0, (size_t)M->n_arena * 4, s));
+    // bit 0: add into the arena; bit 1: more micro-batches follow, so the
+    // grads are not final and the bucket hook must not fire yet
+    const bool acc = (accumulate & PTCG_BWD_ACCUMULATE) != 0;
+    const bool last = (accumulate & PTCG_BWD_PARTIAL) == 0;
+    REQ((accumulate & ~(PTCG_BWD_ACCUMULATE | PTCG_BWD_PARTIAL)) == 0, PTCG_EINVAL,
+        "ptcg_backward: unknown flag bits");
+    if (!acc) CK(cudaMemsetAsync(M->grads, 0, (size_t)M->n_arena * 4, s));
     zero_table_grads(M, s);
     backward_impl(M, M->trn, M->trn_last_obs, grad, returns, R, norm,
-                  prize_count > 0.f ? nullptr : cnt, prize_count, aux, true, s);
+                  prize_count > 0.f ? nullptr : cnt, prize_count, aux, last, s);
     tables_bwd(M, s);
-    if (M->hook) fire_hook(M, "card_id_emb", "zone_emb", s);
+    if (M->hook && last) fire_hook(M, "card_id_emb", "zone_emb", s);
     CKL();
     return PTCG_OK;
 }
@@ -1788,6 +1870,15 @@ int ptcg_ppo_loss_noalloc(const float* dec_out, int nopt, const float* mask, con
                          grad_dec, new_logp, ratio, stats, scratch, stream);
 }
 
+// After a vetoed step with a non-finite gradient norm (stats[0]), clear the
+// train workspace on the device, so no Inf / NaN stays in rows that later
+// forwards skip (k_zero_if_nonfinite).
+static void clear_work_if_nonfinite(PtcgModel* M, const float* st, cudaStream_t s) {
+    if (!M->trn.base) return;
+    ++g_ptcg_launches, k_zero_if_nonfinite<<<M->adam_grid, 256, 0, s>>>(st, (uint4*)M->trn.base,
+        (long)(M->trn.bytes / 16));
+}
+
 static int adam_impl(PtcgModel* M, float lr, float b1, float b2, float eps, float max_norm,
                      const float* gate, float* stats, cudaStream_t s) {
     float* st = stats ? stats : M->d_misc + 32;
@@ -1796,6 +1887,7 @@ static int adam_impl(PtcgModel* M, float lr, float b1, float b2, float eps, floa
         M->d_partials, M->sumsq_grid, lr, b1, b2, eps, max_norm, M->step_dev, gate, st,
         M->d_copies, (int)M->copies.size(), M->d_chunk_copy, M->adam_chunk);
     ++g_ptcg_launches, k_step_inc<<<1, 1, 0, s>>>(M->step_dev, st);
+    clear_work_if_nonfinite(M, st, s);
     CKL();
     return PTCG_OK;
 }
@@ -1886,6 +1978,7 @@ int ptcg_muon_step(PtcgModel* M, float lr, float momentum, float weight_decay, f
     CK(cudaSetDevice(M->dev));
     e = muon_impl(M, lr, momentum, weight_decay, wd_1d, max_norm, gate, stats, (cudaStream_t)stream);
     if (e) return e;
+    clear_work_if_nonfinite(M, stats ? stats : M->d_misc + 32, (cudaStream_t)stream);
     CKL();
     return PTCG_OK;
 }
@@ -1960,7 +2053,7 @@ int ptcg_sample_logits(const float* dec_out, int n, int nopt, const float* mask,
     return PTCG_OK;
 }
 
-int ptcg_puff_advantage(const float* values, const float* rewards, const float* dones,
+int ptcg_negamax_advantage(const float* values, const float* rewards, const float* dones,
                         const float* importance, const float* obs, long obs_size, int seat_col,
                         int B, int T, float gamma, float lambda, float rho_clip, float c_clip,
                         float* advantages, void* stream) {
@@ -2003,12 +2096,12 @@ int ptcg_train_step(PtcgModel* M, const float* obs, const float* actions, const 
     ++g_ptcg_launches, k_count_unseen<<<128, 256, 0, s>>>(cnt, obs, z.ol, nt);
     CK(cudaMemsetAsync(M->grads, 0, (size_t)M->n_arena * 4, s));
     zero_table_grads(M, s);
-    tables_fwd(M, s);
+    tables_fwd(M, M->tab, s);
     int nmb = (nt + R - 1) / R;
     for (int mb = 0; mb < nmb; mb++) {
         int r0 = mb * R, rows = nt - r0 < R ? nt - r0 : R;
         const float* ob = obs + (long)r0 * z.ol.obs;
-        forward_impl(M, Wk, ob, rows, Wk.fused, true, false, s);
+        forward_impl(M, Wk, M->tab, ob, rows, Wk.fused, true, false, s);
         unsigned g = cdiv(rows, PPO_ROWS_PER_BLOCK);
         ++g_ptcg_launches, k_ppo_loss<<<g, PPO_ROWS_PER_BLOCK * 32, 0, s>>>(Wk.fused, z.NOPT, ob + z.ol.mask, z.ol.obs,
             actions + r0, old_logp + r0, advantages + r0, values + r0, returns + r0, prio, horizon,

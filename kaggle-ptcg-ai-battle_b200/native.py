@@ -11,7 +11,8 @@ import re
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libptcg_b200.so")
-HEADER = os.path.join(os.path.dirname(HERE), "include", "ptcg_b200.h")
+INCLUDE = os.path.join(os.path.dirname(HERE), "include")
+HEADER = os.path.join(INCLUDE, "ptcg_b200.h")
 
 P = C.c_void_p
 F = C.c_float
@@ -37,6 +38,7 @@ _SIGS = {
     "ptcg_last_error": (C.c_char_p, []),
     "ptcg_abi_version": (I, []),
     "ptcg_obs_size": (L, [C.POINTER(PtcgShape)]),
+    "ptcg_seat_column": (L, [C.POINTER(PtcgShape)]),
     "ptcg_num_params": (I, [C.POINTER(PtcgShape)]),
     "ptcg_param_info": (I, [C.POINTER(PtcgShape), I, C.POINTER(C.c_char_p),
                             C.POINTER(C.c_long), C.POINTER(C.c_long)]),
@@ -54,6 +56,10 @@ _SIGS = {
     "ptcg_forward": (I, [P, P, I, P, P]),
     "ptcg_forward_train": (I, [P, P, I, P, P]),
     "ptcg_backward": (I, [P, P, P, I, F, I, P]),
+    "ptcg_workspace_create": (I, [P, I, C.POINTER(P)]),
+    "ptcg_workspace_destroy": (I, [P]),
+    "ptcg_forward_ws": (I, [P, P, P, I, P, P]),
+    "ptcg_import_params": (I, [P, P, L, P]),
     "ptcg_ppo_loss": (I, [P, I, P, P, P, P, P, P, P, I, I, F, F, F, F,
                           P, P, P, P, P, P]),
     "ptcg_ppo_loss_noalloc": (I, [P, I, P, P, P, P, P, P, P, I, I, F, F, F, F,
@@ -64,7 +70,7 @@ _SIGS = {
     "ptcg_select_copy": (I, [P, I, I, L, I, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
     "ptcg_index_copy": (I, [P, P, P, I, L, P]),
     "ptcg_sample_logits": (I, [P, I, I, P, L, P, P, P, P, P]),
-    "ptcg_puff_advantage": (I, [P, P, P, P, P, L, I, I, I, F, F, F, F, P, P]),
+    "ptcg_negamax_advantage": (I, [P, P, P, P, P, L, I, I, I, F, F, F, F, P, P]),
     "ptcg_set_grad_hook": (I, [P, GRAD_HOOK, P]),
     "ptcg_train_step": (I, [P, P, P, P, P, P, P, P, I, I, F, F, F, F, F, F, F,
                             F, F, I, P, P]),
@@ -97,10 +103,17 @@ class PtcgError(RuntimeError):
 
 
 def header_symbols():
-    """Function names declared in include/ptcg_b200.h."""
-    txt = open(HEADER).read()
-    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
-    return sorted(set(re.findall(r"\b(ptcg_[a-z_0-9]+)\s*\(", txt)))
+    """Function names declared in the headers under include/ (the typedef'd
+    function-pointer types of the plug-in header are not exports)."""
+    names = set()
+    for f in sorted(os.listdir(INCLUDE)):
+        if not f.endswith(".h"):
+            continue
+        txt = open(os.path.join(INCLUDE, f)).read()
+        txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+        txt = re.sub(r"typedef[^;]*;", "", txt)
+        names.update(re.findall(r"\b(ptcg_[a-z_0-9]+)\s*\(", txt))
+    return sorted(names)
 
 
 def lib():

@@ -184,12 +184,17 @@ class PTCGPolicy:
         check(self.lib.ptcg_forward_train(self.h, _p(obs), obs.shape[0], _p(out), _stream()))
         return out
 
-    def backward(self, grad, returns, aux_norm_rows=0, prize_count=0.0, accumulate=False):
+    def backward(self, grad, returns, aux_norm_rows=0, prize_count=0.0, accumulate=False,
+                 last=True):
+        """Backward of the last forward_train.  accumulate adds into the grad
+        arena; last=False marks a micro-batch that more of the same step
+        follow, so the grad hook waits for the final one."""
         grad = _f32(grad, self.device)
         returns = _f32(returns, self.device)
         self._hook_err = None
+        flags = (1 if accumulate else 0) | (0 if last else 2)
         check(self.lib.ptcg_backward(self.h, _p(grad), _p(returns), int(aux_norm_rows),
-                                     float(prize_count), int(accumulate), _stream()))
+                                     float(prize_count), flags, _stream()))
         self._raise_hook_error()
 
     # -------------------------------------------------------- trainer hooks
@@ -292,7 +297,7 @@ class PTCGPolicy:
         obs = _f32(obs, d)
         B, T = values.shape
         adv = torch.zeros(B, T, device=d)
-        check(self.lib.ptcg_puff_advantage(_p(values), _p(rewards), _p(dones), _p(importance),
+        check(self.lib.ptcg_negamax_advantage(_p(values), _p(rewards), _p(dones), _p(importance),
                                            _p(obs), self.obs_size, self.shape.seat_col, B, T,
                                            gamma, lam, rho_clip, c_clip, _p(adv), _stream()))
         return adv

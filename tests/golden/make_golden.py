@@ -35,7 +35,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 PKG = os.path.join(ROOT, "kaggle-ptcg-ai-battle_b200")
 
-PRESET_ROWS = {"tiny": 8, "small": 4, "c0": 4, "default": 3}
+PRESET_ROWS = {"tiny": 8, "small": 4, "c0": 4, "default": 3, "c4": 2}
 WEIGHT_SEED, TABLE_SEED, OBS_SEED, GRAD_SEED = 1234, 99, 7, 4242
 
 
@@ -214,9 +214,12 @@ def run_one(ref, preset, out_path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("PTCG_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("PTCG_REFERENCE"),
+                    help="reference checkout (or set PTCG_REFERENCE)")
     ap.add_argument("--preset", default=None)
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("--ref (or PTCG_REFERENCE) must name a checkout of the reference")
     if a.preset:
         run_one(a.ref, a.preset, os.path.join(HERE, f"ref_{a.preset}.npz"))
         return

@@ -9,7 +9,7 @@ import torch
 from conftest import ROOT
 
 GOLD = os.path.join(ROOT, "tests", "golden")
-PRESETS = ["tiny", "small", "c0", "default"]
+PRESETS = ["tiny", "small", "c0", "default", "c4"]
 
 
 def _close(a, b, rtol=2e-4, atol=2e-5):
