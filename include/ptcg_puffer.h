@@ -51,11 +51,23 @@ extern "C" {
 #define PTCG_PUF_BOOL _Bool
 #endif
 
+/* A translation unit that already has the trainer's own types (the
+ * replacement ocean.cu, compiled inside pufferlib.cu) defines
+ * PTCG_PUF_TENSOR to PrecisionTensor and PTCG_PUF_ALLOCATOR to Allocator
+ * before including this header, so that the trainer's calls to
+ * ptcg_puff_advantage / ptcg_bind_train_graph type-check unchanged. */
+#ifdef PTCG_PUF_TENSOR
+typedef PTCG_PUF_TENSOR PtcgPufTensor;
+#else
 typedef struct PtcgPufTensor {
     float* data;
     int64_t shape[PTCG_PUF_MAX_DIMS];
 } PtcgPufTensor;
+#endif
 
+#ifdef PTCG_PUF_ALLOCATOR
+typedef PTCG_PUF_ALLOCATOR PtcgPufAllocator;
+#else
 typedef struct PtcgPufAllocEntry {
     void** data_ptr;
     int64_t* shape;
@@ -69,6 +81,7 @@ typedef struct PtcgPufAllocator {
     long total_elems;
     long total_bytes;
 } PtcgPufAllocator;
+#endif
 
 typedef void (*ptcg_puf_init_weights_fn)(void* weights, unsigned long* seed, void* stream);
 typedef void (*ptcg_puf_reg_params_fn)(void* weights, PtcgPufAllocator* alloc);
