@@ -15,8 +15,11 @@ forward + masked sampling), end-to-end numbers through the public API with
 host<->device copies, the roofline of the dominant kernel, and the CPU
 baseline (the CPU oracle on the host cores).
 
---impl reference times the reference algorithm's CPU implementation (the
-oracle restatement of ptcg/rl/model.py + PPO + torch Adam) on the host cores.
+--impl reference times the reference's own CPU implementation on the host
+cores: its torch model (ptcg/rl/model.py PTCGTransformer, from the offline
+install under baseline/_ref) with the PPO loss gradients of its kernel,
+autograd and torch Adam.  Where that install is absent, the CPU oracle port
+stands in and the line says kind "port".
 """
 import argparse
 import datetime
@@ -117,6 +120,47 @@ def measured_peaks():
 
 # ---------------------------------------------------------------- reference
 METRIC = "PPO train samples/sec (config 2 per GPU, aggregate)"
+REF_INSTALL = os.path.join(ROOT, "baseline", "_ref")
+
+
+def reference_installed():
+    """The reference's torch model is importable from baseline/_ref."""
+    return os.path.exists(os.path.join(REF_INSTALL, "ptcg", "rl", "model.py"))
+
+
+def _ref_model(pkg, s):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ref_torch
+    tabs = pkg.synth.make_tables(s, 11)
+    blob = pkg.synth.make_weights(s, 21)
+    return ref_torch, ref_torch.load(REF_INSTALL, s, tabs, blob, pkg.config.param_table)
+
+
+def cpu_reference_step(pkg, s, rows, threads):
+    """One train step of the reference's own torch model (forward_train, PPO
+    loss gradients, aux losses, backward, clip, torch Adam) on `rows`
+    config-shaped observations, as a callable."""
+    import torch
+    torch.set_num_threads(threads)
+    ref_torch, model = _ref_model(pkg, s)
+    obs = pkg.synth.make_obs_batch(s, rows, 5)
+    a, b = s.offsets["opt_mask"]
+    act = pkg.synth.sample_legal(obs[:, a:b], 1)
+    rng = np.random.default_rng(0)
+    adv = rng.standard_normal(rows).astype(np.float32)
+    ret = rng.standard_normal(rows).astype(np.float32)
+    old = np.full(rows, -2.0, np.float32)
+    val = np.zeros(rows, np.float32)
+    return ref_torch.train_step(model, s, obs, act, old, adv, val, ret, np.ones(1, np.float32),
+                                1, rows)
+
+
+def cpu_step(pkg, s, rows, threads):
+    """(step callable, kind): the reference's torch model when installed,
+    else the CPU oracle port."""
+    if reference_installed():
+        return cpu_reference_step(pkg, s, rows, threads), "reference"
+    return cpu_oracle_step(pkg, s, rows, threads), "port"
 
 
 def arm_config(args, s, world, micro):
@@ -159,47 +203,57 @@ def cpu_oracle_step(pkg, s, rows, threads):
     return step
 
 
-def cpu_oracle_step_rate(pkg, s, rows, seconds, threads):
-    """Samples/s of the CPU oracle train step, median over ~`seconds`."""
-    step = cpu_oracle_step(pkg, s, rows, threads)
+def cpu_step_rate(pkg, s, rows, seconds, threads, port_only=False):
+    """Samples/s of a CPU train step (cpu_step), median over ~`seconds`."""
+    if port_only:
+        step, kind = cpu_oracle_step(pkg, s, rows, threads), "port"
+    else:
+        step, kind = cpu_step(pkg, s, rows, threads)
     step()                                  # warm-up
     times = []
     t_end = time.time() + seconds
     while time.time() < t_end or len(times) < 2:
         t0 = time.time(); step(); times.append(time.time() - t0)
     med = float(np.median(times))
-    return rows / med, len(times), med
+    return rows / med, len(times), med, kind
 
 
-def cpu_oracle_rollout_rate(pkg, s, rows, seconds, threads):
-    """Observations/s of the CPU oracle's rollout forward (forward_eval under
-    no_grad) on `rows` config-shaped observations, median over ~`seconds`."""
+def cpu_rollout_rate(pkg, s, rows, seconds, threads):
+    """Observations/s of a CPU rollout forward (forward_eval under no_grad)
+    on `rows` config-shaped observations, median over ~`seconds`: the
+    reference's torch model when installed, else the CPU oracle port."""
     import torch
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import ptcg_oracle as oracle
     torch.set_num_threads(threads)
-    P = oracle.params_from_blob(pkg.synth.make_weights(s, 21), s)
-    T = oracle.tables_to_torch(pkg.synth.make_tables(s, 11))
     obs = torch.from_numpy(pkg.synth.make_obs_batch(s, rows, 6))
+    if reference_installed():
+        _, model = _ref_model(pkg, s)
+        fwd, kind = (lambda: model.forward_eval(obs)), "reference"
+    else:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import ptcg_oracle as oracle
+        P = oracle.params_from_blob(pkg.synth.make_weights(s, 21), s)
+        T = oracle.tables_to_torch(pkg.synth.make_tables(s, 11))
+        fwd, kind = (lambda: oracle.forward_eval(P, T, obs, s)), "port"
     times = []
     with torch.no_grad():
-        oracle.forward_eval(P, T, obs, s)           # warm-up
+        fwd()                                         # warm-up
         t_end = time.time() + seconds
         while time.time() < t_end or len(times) < 2:
-            t0 = time.time(); oracle.forward_eval(P, T, obs, s); times.append(time.time() - t0)
+            t0 = time.time(); fwd(); times.append(time.time() - t0)
     med = float(np.median(times))
-    return rows / med, len(times), med
+    return rows / med, len(times), med, kind
 
 
 def run_reference(args, pkg):
-    """The reference arm: the reference algorithm's CPU implementation (the
-    oracle port of ptcg/rl/model.py + PPO + torch Adam) on all host cores;
-    each step is a bounded sample of the config-2 workload (--ref-rows
-    observations of the same shapes); W warm-up then K timed steps."""
+    """The reference arm: the reference's own CPU implementation (its torch
+    PTCGTransformer, PPO loss gradients, autograd, torch Adam; the oracle
+    port where baseline/_ref is absent) on all host cores; each step is a
+    bounded sample of the config-2 workload (--ref-rows observations of the
+    same shapes); W warm-up then K timed steps."""
     s = pkg.config.PRESETS[args.preset]
     threads = os.cpu_count() or 1
     rows = args.ref_rows
-    step = cpu_oracle_step(pkg, s, rows, threads)
+    step, kind = cpu_step(pkg, s, rows, threads)
     for _ in range(args.warmup):
         step()
     t0 = time.perf_counter()
@@ -207,7 +261,9 @@ def run_reference(args, pkg):
         step()
     dt = time.perf_counter() - t0
     rate = rows * args.steps / dt
-    sample = (f"{rows}-row PPO train step of the CPU oracle port (forward_train + loss + "
+    what = ("the reference's torch PTCGTransformer (baseline/_ref)" if kind == "reference"
+            else "the CPU oracle port")
+    sample = (f"{rows}-row PPO train step of {what} (forward_train + PPO loss + aux losses + "
               f"backward + clip + Adam) per step, {threads} threads")
     nt = args.segments * args.horizon
     cfg = arm_config(args, s, args.gpus, min(args.micro, nt))
@@ -218,7 +274,7 @@ def run_reference(args, pkg):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "config": cfg,
             "cpu_baseline": {"value": rate, "unit": "samples/s", "cores": threads,
-                             "kind": "port", "sample": sample},
+                             "kind": kind, "sample": sample},
             "e2e": {"value": rate, "unit": "samples/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -501,19 +557,21 @@ def main():
     cpu = None
     if world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
-        rate, n, med = cpu_oracle_step_rate(pkg, s, 64, args.cpu_seconds, threads)
-        cpu = {"value": rate, "unit": "samples/s", "cores": threads, "kind": "port",
-               "sample": f"64-row PPO train step of the CPU oracle (forward_train + loss + "
+        rate, n, med, kind = cpu_step_rate(pkg, s, 64, args.cpu_seconds, threads)
+        what = "the reference's torch model" if kind == "reference" else "the CPU oracle port"
+        cpu = {"value": rate, "unit": "samples/s", "cores": threads, "kind": kind,
+               "sample": f"64-row PPO train step of {what} (forward_train + PPO loss + aux + "
                          f"backward + Adam), median of {n} steps ({med:.2f} s/step)"}
         # the other two CPU figures of the measurement plan: the rollout
-        # forward (config 1 shapes) and the scaled config 4 at 16 rows
-        rr, rn, rmed = cpu_oracle_rollout_rate(pkg, s, 256, args.cpu_seconds / 3, threads)
-        cpu["rollout"] = {"value": rr, "unit": "obs/s",
+        # forward (config 1 shapes) and the scaled config 4 at 16 rows (the
+        # port: the reference binds its shapes at import, one per process)
+        rr, rn, rmed, rkind = cpu_rollout_rate(pkg, s, 256, args.cpu_seconds / 3, threads)
+        cpu["rollout"] = {"value": rr, "unit": "obs/s", "kind": rkind,
                           "sample": f"forward_eval of 256 observations under no_grad, median of "
                                     f"{rn} ({rmed:.2f} s)"}
         s4 = pkg.config.PRESETS["c4"]
-        r4, n4, m4 = cpu_oracle_step_rate(pkg, s4, 16, args.cpu_seconds / 3, threads)
-        cpu["c4_train"] = {"value": 1e3 / r4, "unit": "ms/sample",
+        r4, n4, m4, _ = cpu_step_rate(pkg, s4, 16, args.cpu_seconds / 3, threads, port_only=True)
+        cpu["c4_train"] = {"value": 1e3 / r4, "unit": "ms/sample", "kind": "port",
                            "sample": f"16-row c4 PPO train step, median of {n4} ({m4:.2f} s/step)"}
     from ptcg_b200.config import train_flops
     flops_exec = train_flops(s, "first")       # what this build runs per sample
