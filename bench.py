@@ -43,10 +43,15 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--preset", default="c0")
-    ap.add_argument("--segments", type=int, default=512)
+    ap.add_argument("--segments", type=int, default=None,
+                    help="train segments per GPU (config 2: 512; config 4: 1024)")
     ap.add_argument("--horizon", type=int, default=64)
-    ap.add_argument("--micro", type=int, default=16384, help="rows per micro-batch")
-    ap.add_argument("--rollout-agents", type=int, default=1024)
+    ap.add_argument("--micro", type=int, default=None,
+                    help="rows per micro-batch (c0: 16384; c4: 1024)")
+    ap.add_argument("--rollout-agents", type=int, default=None,
+                    help="rollout agents per GPU (config 1: 1024; config 4: 4096)")
+    ap.add_argument("--rollout-graph", type=int, default=1,
+                    help="replay the rollout forward + sampler as a CUDA graph")
     ap.add_argument("--rollout-steps", type=int, default=64)
     ap.add_argument("--e2e-steps", type=int, default=4)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
@@ -54,7 +59,19 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--ref-rows", type=int, default=128,
                     help="observations per step of the reference (CPU) arm")
-    return ap.parse_args()
+    a = ap.parse_args()
+    # c0 shapes for configs 0-3, the scaled policy for 4
+    d = PRESET_DEFAULTS.get(a.preset, PRESET_DEFAULTS["c0"])
+    a.segments = a.segments or d["segments"]
+    a.micro = a.micro or d["micro"]
+    a.rollout_agents = a.rollout_agents or d["rollout_agents"]
+    return a
+
+
+PRESET_DEFAULTS = {
+    "c0": {"segments": 512, "micro": 16384, "rollout_agents": 1024},
+    "c4": {"segments": 1024, "micro": 1024, "rollout_agents": 4096},
+}
 
 
 # ------------------------------------------------------------------ clocks
@@ -119,7 +136,12 @@ def measured_peaks():
 
 
 # ---------------------------------------------------------------- reference
-METRIC = "PPO train samples/sec (config 2 per GPU, aggregate)"
+METRICS = {"c0": "PPO train samples/sec (config 2 per GPU, aggregate)",
+           "c4": "PPO train samples/sec (config 4 per GPU, aggregate)"}
+
+
+def metric_name(preset):
+    return METRICS.get(preset, f"PPO train samples/sec ({preset} per GPU, aggregate)")
 REF_INSTALL = os.path.join(ROOT, "baseline", "_ref")
 
 
@@ -268,7 +290,7 @@ def run_reference(args, pkg):
     nt = args.segments * args.horizon
     cfg = arm_config(args, s, args.gpus, min(args.micro, nt))
     cfg["sample_rows_per_step"] = rows
-    line = {"impl": "reference", "metric": METRIC,
+    line = {"impl": "reference", "metric": metric_name(args.preset),
             "value": rate, "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -471,23 +493,51 @@ def main():
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e = nt * world * args.e2e_steps / (float(te.item()) / 1e3)
 
-    # --- rollout forward (config 1): fresh observations every env step
+    # --- rollout forward (config 1): fresh observations every env step.
+    #     With --rollout-graph the forward + sampler are one CUDA graph
+    #     replayed per env step (the reference replays its rollout graph,
+    #     pufferlib.cu:771-780); each step's observations and uniforms are
+    #     copied into the graph's input buffers first, inside the timed loop.
     rollout = None
+    graph = None
     if not args.no_rollout:
         A = args.rollout_agents
         nroll = 8
         ro_h = torch.from_numpy(pkg.synth.make_obs_batch(s, A * nroll, 500 + rank)).pin_memory()
         ro = ro_h.to(dev)
         uni = torch.rand(args.rollout_steps, A, device=dev)
-        buf = torch.empty(A, s.obs_size, device=dev)
+        gsrc = torch.empty(A, s.obs_size, device=dev)
+        guni = torch.empty(A, device=dev)
+
+        def rstep_static():
+            out = pol.forward(gsrc)
+            return pol.sample(out, gsrc[:, a:b], guni)
+
+        gsrc.copy_(ro[:A])
+        guni.copy_(uni[0])
+        if args.rollout_graph:
+            side = torch.cuda.Stream(device=dev)
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    rstep_static()
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                gout = rstep_static()
 
         def rstep(j, src):
-            out = pol.forward(src)
-            return pol.sample(out, src[:, a:b], uni[j])
+            gsrc.copy_(src, non_blocking=True)
+            guni.copy_(uni[j])
+            if graph is not None:
+                graph.replay()
+                return gout
+            return rstep_static()
 
         for j in range(3):
             rstep(j, ro[:A])
         torch.cuda.synchronize()
+        l0r = pol.lib.ptcg_launch_count()
         r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         r0.record()
         for j in range(args.rollout_steps):
@@ -501,8 +551,7 @@ def main():
         q0.record()
         for j in range(args.rollout_steps):
             k = j % nroll
-            buf.copy_(ro_h[k * A:(k + 1) * A], non_blocking=True)
-            acts, lp, v = rstep(j, buf)
+            acts, lp, v = rstep(j, ro_h[k * A:(k + 1) * A])
             acts.cpu()
         q1.record()
         torch.cuda.synchronize()
@@ -511,12 +560,27 @@ def main():
         if world > 1:
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         rms, qms = [float(x) for x in tt.cpu()]
-        rollout = {"metric": "rollout forward/sec (config 1)", "unit": "obs/s",
+        from ptcg_b200.config import forward_flops
+        peaks_r, src_r = measured_peaks()
+        fl = forward_flops(s, "first")["total"]
+        ach = A * args.rollout_steps * fl / (rms / 1e3) / 1e12
+        pk = peaks_r.get("bf16_tflops_sustained", 1400.0)
+        rollout = {"metric": "rollout forward/sec (config 1)" if args.preset == "c0"
+                   else f"rollout forward/sec ({args.preset})", "unit": "obs/s",
                    "value": A * args.rollout_steps * world / (rms / 1e3),
                    "e2e": A * args.rollout_steps * world / (qms / 1e3),
                    "agents_per_gpu": A, "env_steps": args.rollout_steps,
                    "ms_per_env_step": rms / args.rollout_steps,
-                   "h2d_bytes_per_step": A * s.obs_size * 4, "d2h_bytes_per_step": A * 4}
+                   "cuda_graph": graph is not None,
+                   "h2d_bytes_per_step": A * s.obs_size * 4, "d2h_bytes_per_step": A * 4,
+                   "roofline": {"kernel": "whole rollout forward + sampler (all kernels)",
+                                "bound": "tensor", "achieved": ach, "peak": pk,
+                                "unit": "TFLOP/s", "frac": ach / pk,
+                                "peak_source": f"bf16_tflops_sustained ({src_r})",
+                                "gflop_per_obs": fl / 1e9}}
+        if graph is None:
+            rollout["gpu_launches_per_step"] = (pol.lib.ptcg_launch_count() - l0r) / max(
+                1, args.rollout_steps)
 
     if world > 1:
         pol.set_grad_hook(None)
@@ -532,8 +596,13 @@ def main():
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     kname = "gemm_tc (tcgen05)" if timer_mode == 1 else "gemm_simt"
+    traffic_note = None
     if os.path.exists(tp):
-        traffic = json.load(open(tp)).get(kname)
+        # ncu DRAM bytes per launch, captured per preset (a capture of a
+        # smaller micro-batch scaled by rows is labelled "scaled")
+        t = json.load(open(tp)).get(args.preset, {}).get(kname)
+        if t:
+            traffic, traffic_note = t["bytes_per_launch"], t["measured"]
     # The class's two roofs: the tensor pipe (FLOPs) and HBM (algorithmic
     # bytes: operands read once, outputs written once).  The bound reported
     # is the roof the class is closer to.
@@ -550,7 +619,8 @@ def main():
     main = hbm if (hbm["frac"] or 0) > (tens["frac"] or 0) else tens
     roof = {"kernel": kname, "bound": "hbm" if main is hbm else "tensor",
             "achieved": main["achieved"], "peak": main["peak"], "unit": main["unit"],
-            "frac": main["frac"], "traffic": traffic, "peak_source": main["peak_source"],
+            "frac": main["frac"], "traffic": traffic, "traffic_source": traffic_note,
+            "peak_source": main["peak_source"],
             "tensor": tens, "hbm": hbm, "launches": klaunch,
             "device_ms": kms, "share_of_step_time": kms / ms if ms else None}
 
@@ -577,7 +647,7 @@ def main():
     flops_exec = train_flops(s, "first")       # what this build runs per sample
     flops_ref = train_flops(s, "all")          # same step with the critic over every row
     line = {
-        "metric": METRIC,
+        "metric": metric_name(args.preset),
         "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
