@@ -50,6 +50,9 @@ def parse():
                     help="rows per micro-batch (c0: 16384; c4: 1024)")
     ap.add_argument("--rollout-agents", type=int, default=None,
                     help="rollout agents per GPU (config 1: 1024; config 4: 4096)")
+    ap.add_argument("--dp", default="allreduce", choices=["allreduce", "sharded"],
+                    help="N>1 gradient exchange: bucketed all-reduce + Adam on every rank, or "
+                         "bucketed reduce-scatter + Adam on each rank's shard + all-gather")
     ap.add_argument("--rollout-graph", type=int, default=1,
                     help="replay the rollout forward + sampler as a CUDA graph")
     ap.add_argument("--rollout-steps", type=int, default=64)
@@ -192,7 +195,7 @@ def arm_config(args, s, world, micro):
             "model": "PTCGTransformer d%d L%d h%d ffn%d ltok%d nopt%d" % (
                 s.d, s.layers, s.heads, s.ffn, s.ltok, s.nopt),
             "global_batch": nt * world, "seq_len": s.lseq,
-            "parallelism": f"dp{world}",
+            "parallelism": f"dp{world}" + ("" if world == 1 else f" ({args.dp})"),
             "l2": "inputs larger than L2 (obs %.0f MB per step per GPU)" % (
                 nt * s.obs_size * 4 / 1e6)}
 
@@ -363,8 +366,11 @@ def main():
     reducer = None
     if world > 1:
         from ptcg_b200.dp import BucketAllReduce, checksum_u64, weights_agree
-        reducer = BucketAllReduce(grads)
-        pol.set_grad_hook(reducer)
+        if args.dp == "sharded":
+            reducer = pol.sharded_adam(lr=3e-4, betas=(0.9, 0.999), eps=1e-8, max_norm=1.0)
+        else:
+            reducer = BucketAllReduce(grads)
+            pol.set_grad_hook(reducer)
     ck = torch.zeros(max(1, args.steps + args.warmup), 2, dtype=torch.int64, device=dev)
     stats = torch.zeros(16, device=dev)
 
@@ -377,10 +383,13 @@ def main():
                        skip_adam=world > 1, stats=stats, **hyper)
         if reducer is not None:
             covered.append(reducer.covered(grads.numel()))
-            reducer.wait()
-            st2 = pol.adam_step(lr=hyper["lr"], betas=hyper["betas"], eps=hyper["eps"],
-                                max_norm=hyper["max_norm"])
-            stats[8:10].copy_(st2)              # {grad norm, applied} as train_step writes them
+            if args.dp == "sharded":
+                reducer.step(stats[8:10])       # {grad norm, applied} as train_step writes them
+            else:
+                reducer.wait()
+                st2 = pol.adam_step(lr=hyper["lr"], betas=hyper["betas"], eps=hyper["eps"],
+                                    max_norm=hyper["max_norm"])
+                stats[8:10].copy_(st2)
             mn, mx = weights_agree(checksum_u64(pol.weights_checksum()))
             ck[i, 0] = mn; ck[i, 1] = mx
 

@@ -227,6 +227,27 @@ int ptcg_ppo_loss_noalloc(const float* dec_out, int nopt, const float* mask,
 int ptcg_adam_step(PtcgModel* m, float lr, float beta1, float beta2, float eps,
                    float max_norm, const float* gate, float* stats, void* stream);
 
+/* ---- sharded Adam for data parallelism ----------------------------------
+ * The reference reduces the whole gradient arena with one ncclAllReduce and
+ * then every rank runs the same optimizer over all of it
+ * (native/src/muon.cu:209-214).  These three calls let each rank update
+ * only its own shard after a reduce-scatter and all-gather the result:
+ *  - ptcg_sumsq: fp64 sum of squares of n device floats x into out[0]
+ *    (device double); a rank's shard norm, summed over ranks by the caller;
+ *  - ptcg_adam_segments: the Adam update of ptcg_adam_step (same clip,
+ *    gate, non-finite veto, step counter and stats) applied to nseg arena
+ *    segments, seg a device array of nseg triples {arena offset, offset in
+ *    grad_src, length} in floats, with gradients read from grad_src and the
+ *    clip taken from the global sum of squares sumsq[0] (device double).  It
+ *    does not refresh the bf16 compute copies;
+ *  - ptcg_refresh_copies: refresh every bf16 compute copy from the master
+ *    weights (after the updated segments of all ranks are gathered). */
+int ptcg_sumsq(PtcgModel* m, const float* x, long n, double* out, void* stream);
+int ptcg_adam_segments(PtcgModel* m, const float* grad_src, const long* seg, int nseg,
+                       const double* sumsq, float lr, float beta1, float beta2, float eps,
+                       float max_norm, const float* gate, float* stats, void* stream);
+int ptcg_refresh_copies(PtcgModel* m, void* stream);
+
 /* Muon step over the whole arena, the reference trainer's optimizer
  * (muon_step, native/src/muon.cu:209-297, with its local patches):
  *  - clip: g *= min(1, max_norm / (||g|| + 1e-6)) (always applied);
@@ -391,8 +412,15 @@ int ptcg_gemm_ex(int M, int N, int K, const void* A, long lda, int a_kmajor, con
 /* 1 when the tcgen05 engine is usable on the current device (sm_100). */
 int ptcg_tensor_cores(void);
 /* First error code a bounded device-side wait recorded since the last call
- * (0 = none; the kernel that timed out returned early).  Resets the flag. */
+ * (0 = none; the kernel that timed out returned early; 100 + code for the
+ * tcgen05 attention).  Resets the flag. */
 int ptcg_device_error(void);
+
+/* Kernels of the bf16 attention (no counterpart in the reference, whose
+ * attention materialises fp32 probabilities, native/model/ptcg_kernels.cuh:
+ * 223-289): 0 = mma.sync flash attention (default), 1 = tcgen05 / TMEM
+ * flash attention.  Process-wide; takes effect at the next launch. */
+int ptcg_set_attention_impl(int impl);
 int ptcg_kernel_timer_read(PtcgModel* m, double* ms, long* launches, double* flops);
 /* Algorithmic HBM bytes of the launches timed since ptcg_kernel_timer(m, mode)
  * (operands read once, outputs written once; diagnostic, no counterpart in

@@ -18,7 +18,8 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I" + INCLUDE, "-I" + CSRC]
-SOURCES = ["model.cu", "gemm_simt.cu", "gemm_tc.cu", "attention.cu", "puffer_plugin.cu"]
+SOURCES = ["model.cu", "gemm_simt.cu", "gemm_tc.cu", "attention.cu", "attention_tc.cu",
+           "puffer_plugin.cu"]
 
 
 def _needs(obj, deps):

@@ -8,6 +8,7 @@
 // head stays in shared memory (L <= 257 -> <= 142 KB), so neither pass needs
 // atomics.  This SIMT version is the exact-fp32 path.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -865,6 +866,29 @@ __global__ void __launch_bounds__(512) k_attn_row0_bwd(
         for (int i = lane; i < 96; i += 32) atomicAdd(&dbias[(i >> 5) * D + h * DH + (i & 31)], acc[i]);
 }
 
+}  // namespace
+
+// attention implementation for bf16 operands: 0 = mma.sync (default),
+// 1 = tcgen05 / TMEM; set by ptcg_set_attention_impl or, at load, by
+// PTCG_ATTN_TC=1
+static std::atomic<int> g_attn_impl{-1};
+
+bool attn_tc_enabled() {
+    int v = g_attn_impl.load();
+    if (v < 0) {
+        const char* e = getenv("PTCG_ATTN_TC");
+        v = (e && e[0] == '1') ? 1 : 0;
+        int expect = -1;
+        g_attn_impl.compare_exchange_strong(expect, v);
+        v = g_attn_impl.load();
+    }
+    return v == 1;
+}
+
+void attn_set_impl(int impl) { g_attn_impl.store(impl == 1 ? 1 : 0); }
+
+namespace {
+
 int num_sms() {
     static int n = 0;
     if (!n) {
@@ -894,6 +918,11 @@ void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
         ++g_ptcg_launches, k_attn_fwd<float><<<nseq * H, NW * 32, sm, s>>>((const float*)qkv, ldqkv, keep,
             (float*)out, ldo, lse, L, H);
     } else {
+        // tcgen05 / TMEM path first; the mma.sync kernel serves shapes it
+        // does not take and runs when PTCG_ATTN_TC=0
+        if (attn_tc_enabled() &&
+            attn_fwd_tc(qkv, ldqkv, keep, out, ldo, lse, nseq, L, H, s, extent))
+            return;
         size_t sm2 = fwd_mma_smem(L);
         set_smem(k_attn_fwd_mma, sm2);
         ++g_ptcg_launches, k_attn_fwd_mma<<<nseq * H, 128, sm2, s>>>((const bf16*)qkv, ldqkv, keep,

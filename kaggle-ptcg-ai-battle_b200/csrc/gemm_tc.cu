@@ -863,6 +863,30 @@ bool gemm_tc_available() {
     return g_ok;
 }
 
+bool tc_make_map_2d(CUtensorMap* m, const void* ptr, int dtype, long inner, long outer, long ld,
+                    int box_in, int box_out, int swizzle_bytes) {
+    if (!gemm_tc_available()) return false;
+    const int eb = dtype == DT_F32 ? 4 : 2;
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * eb};
+    cuuint32_t box[2] = {(cuuint32_t)box_in, (cuuint32_t)box_out};
+    cuuint32_t es[2] = {1, 1};
+    CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                          : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                : CU_TENSOR_MAP_SWIZZLE_NONE;
+    CUresult r = g_encode(m, eb == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                          2, const_cast<void*>(ptr), dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+int tc_num_sms() {
+    std::call_once(g_once, init_once);
+    return g_sms;
+}
+
 namespace {
 
 // 2-D tensor map of `eb`-byte elements

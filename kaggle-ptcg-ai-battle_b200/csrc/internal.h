@@ -1,5 +1,6 @@
 // Internal launcher interfaces shared by the ptcg_b200 translation units.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -48,6 +49,11 @@ void gemm_simt(const GemmArgs& a, cudaStream_t s);
 bool gemm_tc(const GemmArgs& a, cudaStream_t s);
 bool gemm_tc_supported(const GemmArgs& a);
 bool gemm_tc_available();
+// 2-D TMA tensor map (inner x outer elements, row pitch ld elements, box
+// box_in x box_out, swizzle 0 / 32 / 64 / 128 bytes); false if unavailable
+bool tc_make_map_2d(CUtensorMap* m, const void* ptr, int dtype, long inner, long outer, long ld,
+                    int box_in, int box_out, int swizzle_bytes);
+int tc_num_sms();
 // first error code recorded by a tcgen05 kernel since the last call (0 = none)
 int ptcg_tc_error_read_reset();
 int ptcg_tc_profile_ctl(int enable, unsigned long long* out8);
@@ -70,6 +76,16 @@ void attn_row0_bwd(int dtype, const void* q, long ldq, const void* kv, long ldkv
                    const uint8_t* keep, const void* out, long ldo, const void* dout, long lddo,
                    const float* lse, void* dq, long lddq, void* dkv, long lddkv, float* dbias,
                    int nseq, int L, int H, cudaStream_t s);
+// tcgen05 / TMEM attention (attention_tc.cu), bf16 operands: false when the
+// shape or alignment is not supported (the caller runs the mma.sync kernels)
+bool attn_fwd_tc(const void* qkv, long ldqkv, const uint8_t* keep, void* out, long ldo,
+                 float* lse, int nseq, int L, int H, cudaStream_t s, const int* extent);
+// whether bf16 attention runs the tcgen05 kernels (attn_set_impl(1), or
+// PTCG_ATTN_TC=1 at load) instead of the mma.sync ones
+bool attn_tc_enabled();
+void attn_set_impl(int impl);
+// first error code recorded by a tcgen05 attention kernel since the last call
+int attn_tc_error_read_reset();
 // dbias (nullable, 3*H*32 floats): += column sums of dqkv in fp32
 void attn_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
               const void* out, long ldo, const void* dout, long lddo,

@@ -1443,6 +1443,59 @@ __global__ void k_adam(float* p, float* m, float* v, const float* g, long n,
     }
 }
 
+// fp64 sum of the partials of k_sumsq, in a fixed order, into out[0] (one block)
+__global__ void k_sumsq_final(double* out, const double* partials, int nparts) {
+    __shared__ double sh[32];
+    double t = 0.0;
+    for (int i = threadIdx.x; i < nparts; i += blockDim.x) t += partials[i];
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = t;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0;
+        for (int i = 0; i < (int)(blockDim.x >> 5); i++) s += sh[i];
+        out[0] = s;
+    }
+}
+
+// The Adam update of k_adam over a list of arena segments whose gradients
+// sit elsewhere (a rank's reduce-scattered shard): segment y = blockIdx.y
+// covers arena floats [seg[3y], seg[3y] + seg[3y+2]) with gradients from
+// gsrc + seg[3y+1].  The clip uses the global sum of squares sumsq[0] (all
+// ranks' shards).  No bf16 copies here: the caller refreshes them once the
+// updated weights are gathered.
+__global__ void k_adam_seg(float* p, float* m, float* v, const float* gsrc, const long* seg,
+                           const double* sumsq, float lr, float b1, float b2, float eps,
+                           float max_norm, const long long* step_dev, const float* gate,
+                           float* stats) {
+    __shared__ float s_coef, s_step, s_bc2sqrt;
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        const double t_step = (double)(step_dev[0] + 1);
+        const float norm = (float)sqrt(sumsq[0]);
+        const int ok = isfinite(norm) && (gate == nullptr || gate[0] != 0.f);
+        const float coef = max_norm / (norm + 1e-6f);
+        s_coef = coef < 1.f ? coef : 1.f;
+        s_step = lr / (float)(1.0 - pow((double)b1, t_step));
+        s_bc2sqrt = (float)sqrt(1.0 - pow((double)b2, t_step));
+        s_ok = ok;
+        if (blockIdx.x == 0 && blockIdx.y == 0 && stats) { stats[0] = norm; stats[1] = ok ? 1.f : 0.f; }
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    const long a = seg[3 * blockIdx.y], so = seg[3 * blockIdx.y + 1], len = seg[3 * blockIdx.y + 2];
+    const float coef = s_coef, step_size = s_step, bc2sqrt = s_bc2sqrt;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < len;
+         i += (long)gridDim.x * blockDim.x) {
+        const float gi = gsrc[so + i] * coef;
+        const float mi = b1 * m[a + i] + (1.f - b1) * gi;
+        const float vi = b2 * v[a + i] + (1.f - b2) * gi * gi;
+        m[a + i] = mi;
+        v[a + i] = vi;
+        p[a + i] = p[a + i] - step_size * mi / (sqrtf(vi) / bc2sqrt + eps);
+    }
+}
+
 // advance the Adam step counter when the step was applied (after k_adam)
 __global__ void k_step_inc(long long* step_dev, const float* stats) {
     if (stats[1] != 0.f) step_dev[0] += 1;

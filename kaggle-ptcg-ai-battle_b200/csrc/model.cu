@@ -1892,6 +1892,42 @@ static int adam_impl(PtcgModel* M, float lr, float b1, float b2, float eps, floa
     return PTCG_OK;
 }
 
+int ptcg_sumsq(PtcgModel* M, const float* x, long n, double* out, void* stream) {
+    REQ(M && x && out && n >= 0, PTCG_EINVAL, "bad arguments");
+    CK(cudaSetDevice(M->dev));
+    cudaStream_t s = (cudaStream_t)stream;
+    ++g_ptcg_launches, k_sumsq<<<M->sumsq_grid, 256, 0, s>>>(M->d_partials, x, n);
+    ++g_ptcg_launches, k_sumsq_final<<<1, 256, 0, s>>>(out, M->d_partials, M->sumsq_grid);
+    CKL();
+    return PTCG_OK;
+}
+
+int ptcg_adam_segments(PtcgModel* M, const float* grad_src, const long* seg, int nseg,
+                       const double* sumsq, float lr, float beta1, float beta2, float eps,
+                       float max_norm, const float* gate, float* stats, void* stream) {
+    int e = ready(M);
+    if (e) return e;
+    REQ(grad_src && seg && sumsq && nseg >= 0 && nseg <= 65535, PTCG_EINVAL, "bad arguments");
+    CK(cudaSetDevice(M->dev));
+    cudaStream_t s = (cudaStream_t)stream;
+    float* st = stats ? stats : M->d_misc + 32;
+    if (nseg > 0) {
+        dim3 g((unsigned)std::max(1, M->adam_grid / std::max(1, nseg)), (unsigned)nseg);
+        ++g_ptcg_launches, k_adam_seg<<<g, 256, 0, s>>>(M->params, M->am, M->av, grad_src, seg,
+            sumsq, lr, beta1, beta2, eps, max_norm, M->step_dev, gate, st);
+    }
+    ++g_ptcg_launches, k_step_inc<<<1, 1, 0, s>>>(M->step_dev, st);
+    clear_work_if_nonfinite(M, st, s);
+    CKL();
+    return PTCG_OK;
+}
+
+int ptcg_refresh_copies(PtcgModel* M, void* stream) {
+    REQ(M, PTCG_EINVAL, "null model");
+    CK(cudaSetDevice(M->dev));
+    return refresh_copies(M, (cudaStream_t)stream);
+}
+
 int ptcg_adam_step(PtcgModel* M, float lr, float beta1, float beta2, float eps, float max_norm,
                    const float* gate, float* stats, void* stream) {
     int e = ready(M);
@@ -2226,7 +2262,16 @@ int ptcg_tc_profile(int enable, unsigned long long* counters) {
 
 int ptcg_tensor_cores(void) { return gemm_tc_available() ? 1 : 0; }
 
-int ptcg_device_error(void) { return ptcg_tc_error_read_reset(); }
+int ptcg_set_attention_impl(int impl) {
+    REQ(impl == 0 || impl == 1, PTCG_EINVAL, "attention implementation must be 0 or 1");
+    attn_set_impl(impl);
+    return PTCG_OK;
+}
+
+int ptcg_device_error(void) {
+    const int g = ptcg_tc_error_read_reset(), a = attn_tc_error_read_reset();
+    return g ? g : (a ? 100 + a : 0);
+}
 
 int ptcg_gemm(int M, int N, int K, const void* A, long lda, int a_kmajor, const void* B, long ldb,
               int b_kmajor, int operand_dtype, float* C, long ldc, int accumulate, int engine,

@@ -65,6 +65,9 @@ _SIGS = {
     "ptcg_ppo_loss_noalloc": (I, [P, I, P, P, P, P, P, P, P, I, I, F, F, F, F,
                                   P, P, P, P, P]),
     "ptcg_adam_step": (I, [P, F, F, F, F, F, P, P, P]),
+    "ptcg_sumsq": (I, [P, P, L, P, P]),
+    "ptcg_adam_segments": (I, [P, P, P, I, P, F, F, F, F, F, P, P, P]),
+    "ptcg_refresh_copies": (I, [P, P]),
     "ptcg_muon_step": (I, [P, F, F, F, F, F, P, P, P]),
     "ptcg_prio_replay": (I, [P, I, I, F, F, I, I, P, P, P, P, P, P]),
     "ptcg_select_copy": (I, [P, I, I, L, I, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
@@ -88,6 +91,7 @@ _SIGS = {
     "ptcg_attention_fwd": (I, [I, P, L, P, P, L, P, I, I, I, P]),
     "ptcg_attention_bwd": (I, [I, P, L, P, P, L, P, L, P, P, L, P, I, I, I, P]),
     "ptcg_device_error": (I, []),
+    "ptcg_set_attention_impl": (I, [I]),
     "ptcg_gemm": (I, [I, I, I, P, L, I, P, L, I, I, P, L, I, I, P]),
     "ptcg_gemm_ex": (I, [I, I, I, P, L, I, P, L, I, I, P, L, I, P, I, P, L, P, L, P, I, I, P]),
     "ptcg_kernel_timer_bytes": (I, [P, C.POINTER(C.c_double)]),

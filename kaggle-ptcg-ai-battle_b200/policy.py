@@ -221,6 +221,38 @@ class PTCGPolicy:
                                       _p(gate), _p(stats), _stream()))
         return stats
 
+    # ------------------------------------------------ sharded optimizer
+    def sumsq(self, x, out):
+        """out[0] (float64 device tensor) = sum of squares of the fp32 device
+        tensor x (ptcg_sumsq)."""
+        check(self.lib.ptcg_sumsq(self.h, _p(x), x.numel(), _p(out), _stream()))
+        return out
+
+    def adam_segments(self, grad_src, seg, nseg, sumsq, stats, lr=3e-4, betas=(0.9, 0.999),
+                      eps=1e-8, max_norm=1.0, gate=None):
+        """Adam over arena segments (ptcg_adam_segments): seg int64 device
+        triples {arena offset, offset in grad_src, length}, global clip from
+        sumsq (float64 device scalar)."""
+        check(self.lib.ptcg_adam_segments(self.h, _p(grad_src), _p(seg), int(nseg), _p(sumsq),
+                                          lr, betas[0], betas[1], eps, max_norm, _p(gate),
+                                          _p(stats), _stream()))
+        return stats
+
+    def refresh_copies(self):
+        check(self.lib.ptcg_refresh_copies(self.h, _stream()))
+
+    def sharded_adam(self, group=None, lr=3e-4, betas=(0.9, 0.999), eps=1e-8, max_norm=1.0):
+        """A dp.ShardedAdam over this model's arenas, installed as its grad
+        hook: reduce-scatter per bucket during backward, then .step(stats)."""
+        from .dp import ShardedAdam
+        red = ShardedAdam(self.arena(1), self.arena(0),
+                          update=lambda g, seg, n, ss, st: self.adam_segments(
+                              g, seg, n, ss, st, lr=lr, betas=betas, eps=eps, max_norm=max_norm),
+                          sumsq=lambda x, out: self.sumsq(x, out),
+                          refresh=self.refresh_copies, group=group)
+        self.set_grad_hook(red)
+        return red
+
     # ---------------------------------------------- minibatch selection
     def prio_replay(self, advantages, alpha, beta, total_agents, uniforms):
         """(idx int32, mb_prio, probs) of prioritised segment replay over

@@ -73,6 +73,64 @@ def _agree_worker(rank, world, port):
     dist.destroy_process_group()
 
 
+def _torch_adam(p, m, v, g, t, lr=1e-2, b1=0.9, b2=0.999, eps=1e-8):
+    """The update formula of the fused Adam kernels, in torch."""
+    m.mul_(b1).add_((1 - b1) * g)
+    v.mul_(b2).add_((1 - b2) * g * g)
+    p.sub_(lr / (1 - b1 ** t) * m / (v.sqrt() / (1 - b2 ** t) ** 0.5 + eps))
+
+
+def _sharded_worker(rank, world, port):
+    _init(rank, world, port)
+    from ptcg_b200.dp import ShardedAdam
+    n, max_norm = 1000, 1.0
+    torch.manual_seed(0)
+    p0 = torch.randn(n)                                   # identical start on every rank
+    params, m, v = p0.clone(), torch.zeros(n), torch.zeros(n)
+    step = [0]
+
+    def update(shard, seg, nseg, ss, stats):
+        norm = float(ss[0].sqrt())
+        coef = min(1.0, max_norm / (norm + 1e-6))
+        t = step[0] + 1
+        for k in range(nseg):
+            a, so, ln = [int(x) for x in seg[3 * k:3 * k + 3]]
+            _torch_adam(params[a:a + ln], m[a:a + ln], v[a:a + ln], shard[so:so + ln] * coef, t)
+        step[0] += 1
+        stats[0], stats[1] = norm, 1.0
+
+    grads = torch.zeros(n)
+    red = ShardedAdam(grads, params, update,
+                      sumsq=lambda x, out: out.copy_((x.double() ** 2).sum().view(1)),
+                      refresh=lambda: None)
+    bounds = [0, 92, 300, 304, 700, 1000]                # spans in backward order
+    ref_p, ref_m, ref_v = p0.clone(), torch.zeros(n), torch.zeros(n)
+    for it in range(3):
+        g_all = [torch.randn(n, generator=torch.Generator().manual_seed(100 * it + r))
+                 for r in range(world)]
+        grads.copy_(g_all[rank])
+        red.reset()
+        for a, b in reversed(list(zip(bounds[:-1], bounds[1:]))):
+            red(a, b - a, None)
+        assert red.covered(n)
+        stats = torch.zeros(2)
+        red.step(stats)
+        # reference: the averaged gradient, clipped, full Adam on every rank
+        g = torch.stack(g_all).mean(0)
+        norm = float(g.double().norm())
+        assert abs(float(stats[0]) - norm) <= 1e-5 * norm
+        _torch_adam(ref_p, ref_m, ref_v, g * min(1.0, max_norm / (norm + 1e-6)), it + 1)
+        torch.testing.assert_close(params, ref_p, rtol=1e-5, atol=1e-6)
+    # this rank's segments: disjoint pieces that, over all ranks, tile the arena
+    seg = red.segments().view(-1, 3)
+    mine = torch.zeros(n, dtype=torch.int32)
+    for a, _, ln in seg.tolist():
+        mine[a:a + ln] += 1
+    dist.all_reduce(mine)
+    assert torch.equal(mine, torch.ones(n, dtype=torch.int32))
+    dist.destroy_process_group()
+
+
 def _leaver_worker(rank, world, port, flag):
     _init(rank, world, port, timeout_s=5)
     t = torch.ones(4)
@@ -98,6 +156,12 @@ def test_bucket_allreduce_averages_and_tiles():
 
 def test_weights_agree_detects_divergence():
     _run(_agree_worker)
+
+
+def test_sharded_adam_matches_allreduce_adam():
+    """Reduce-scatter per bucket + Adam on each rank's shard + all-gather ==
+    all-reduce + Adam over the whole arena, on every rank."""
+    _run(_sharded_worker)
 
 
 @pytest.mark.timeout(120)

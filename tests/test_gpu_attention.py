@@ -13,11 +13,23 @@ def _p(t):
     return C.c_void_p(t.data_ptr()) if t is not None else None
 
 
-@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
-@pytest.mark.parametrize("L,H", [(129, 8), (186, 8), (17, 2), (257, 16), (314, 16), (33, 4)])
-def test_attention_matches_sdpa(pkg, dtype, L, H):
+@pytest.fixture(params=["mma", "tc"])
+def attn_impl(request, pkg):
+    """bf16 attention kernels under test: mma.sync or tcgen05 / TMEM."""
     import ptcg_b200.native as n
     lib = n.lib()
+    assert lib.ptcg_set_attention_impl(1 if request.param == "tc" else 0) == 0
+    yield request.param
+    lib.ptcg_set_attention_impl(0)
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+@pytest.mark.parametrize("L,H", [(129, 8), (186, 8), (17, 2), (257, 16), (314, 16), (33, 4)])
+def test_attention_matches_sdpa(pkg, dtype, L, H, attn_impl):
+    import ptcg_b200.native as n
+    lib = n.lib()
+    if dtype == "fp32" and attn_impl == "tc":
+        pytest.skip("the tcgen05 kernels take bf16 operands")
     torch.manual_seed(L * 10 + H)
     nseq, D = 5, H * 32
     tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
@@ -31,6 +43,7 @@ def test_attention_matches_sdpa(pkg, dtype, L, H):
     s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
     dt = 1 if dtype == "bf16" else 0
     assert lib.ptcg_attention_fwd(dt, _p(qkv), 3 * D, _p(keep_u8), _p(out), D, _p(lse), nseq, L, H, s) == 0
+    assert lib.ptcg_device_error() == 0
     q, k, v = qkv.float().view(nseq, L, 3, H, 32).permute(2, 0, 3, 1, 4).unbind(0)
     q.requires_grad_(True); k.requires_grad_(True); v.requires_grad_(True)
     ref = F.scaled_dot_product_attention(q, k, v, attn_mask=keep.view(nseq, 1, 1, L))
@@ -106,3 +119,34 @@ def test_attention_bwd_zero_dout_blocks(pkg, L, H):
         assert (a - b).norm().item() / b.norm().item() < 3e-2, part
     zero_rows = rowmask.view(-1) == 0
     assert (dqkv.float()[zero_rows, :D] == 0).all()
+
+
+@pytest.mark.parametrize("preset", ["c0", "c4", "default"])
+def test_model_forward_with_tc_attention(pkg, oracle, preset):
+    """The whole bf16 forward with the tcgen05 attention kernels (row
+    extents, multi-chunk keys at c4) against the CPU oracle."""
+    import numpy as np
+    import ptcg_b200.native as n
+    lib = n.lib()
+    torch.set_float32_matmul_precision("highest")
+    s = pkg.config.PRESETS[preset]
+    nrows = 6
+    tabs = pkg.synth.make_tables(s, 11)
+    blob = pkg.synth.make_weights(s, 21)
+    obs = pkg.synth.make_obs(s, nrows, 3, edge=True)
+    pol = pkg.PTCGPolicy(s, precision="bf16", tables=tabs, weights=blob, rollout_rows=nrows)
+    assert lib.ptcg_set_attention_impl(1) == 0
+    try:
+        out = pol.forward(obs).cpu().numpy()
+        assert lib.ptcg_device_error() == 0
+    finally:
+        lib.ptcg_set_attention_impl(0)
+    P = oracle.params_from_blob(blob, s)
+    T = oracle.tables_to_torch(tabs)
+    with torch.no_grad():
+        sc, _, v = oracle.forward_eval(P, T, torch.from_numpy(obs), s)
+    a, b = s.offsets["opt_mask"]
+    legal = obs[:, a:b] != 0
+    rel = lambda x, y: float(np.linalg.norm(x - y) / np.linalg.norm(y))
+    assert rel(out[:, :-1][legal], sc.numpy()[legal]) <= 2e-2
+    assert rel(out[:, -1], v.numpy()) <= 2e-2

@@ -354,3 +354,44 @@ def test_backward_hook_fires_on_final_microbatch_only(pkg):
         cur += cnt
     assert cur == pol.arena(1).numel()
     assert rel(pol.grads_packed(), g_whole) <= 1e-5
+
+
+@pytest.mark.parametrize("prec", ["fp32", "bf16"])
+def test_adam_segments_equal_adam_step(pkg, prec):
+    """ptcg_sumsq + ptcg_adam_segments over segments that tile the arena
+    (gradients read from a separate buffer) + ptcg_refresh_copies ==
+    ptcg_adam_step: the sharded optimizer's kernels at world size 1."""
+    s = pkg.config.PRESETS["small"]
+    tabs = pkg.synth.make_tables(s, 11)
+    blob = pkg.synth.make_weights(s, 21)
+    pols = [pkg.PTCGPolicy(s, precision=prec, tables=tabs, weights=blob) for _ in range(2)]
+    n = pols[0].arena(1).numel()
+    g = torch.randn(n, device="cuda", generator=torch.Generator("cuda").manual_seed(5)) * 0.3
+    for it in range(2):
+        for pol in pols:
+            pol.arena(1).copy_(g * (it + 1))
+        st0 = pols[0].adam_step(lr=1e-3, max_norm=1.0)
+        cut = [0, n // 3 // 4 * 4, n // 2 // 4 * 4 + 4, n]
+        rows = [(a, n - b, b - a) for a, b in zip(cut[:-1], cut[1:])]
+        seg = torch.tensor(rows, dtype=torch.int64, device="cuda").view(-1)
+        gsrc = torch.empty_like(g)
+        for a, so, ln in rows:                                 # segment k reads src[so:so+ln]
+            gsrc[so:so + ln] = g[a:a + ln] * (it + 1)
+        ss = torch.zeros(1, dtype=torch.float64, device="cuda")
+        pols[1].sumsq(gsrc, ss)
+        st1 = torch.zeros(2, device="cuda")
+        pols[1].adam_segments(gsrc, seg, 3, ss, st1, lr=1e-3, max_norm=1.0)
+        pols[1].refresh_copies()
+        assert abs(float(st0[0]) - float(st1[0])) <= 1e-6 * float(st0[0])
+        assert float(st1[1]) == 1.0
+    w0, w1 = pols[0].save_weights(), pols[1].save_weights()
+    assert rel(w1 - blob, w0 - blob) <= 1e-6
+    assert pols[0].step == pols[1].step == 2
+    # the refreshed bf16 copies are exactly the copies of the master weights:
+    # the same forward as a model loaded with those weights (the two Adam
+    # kernels may differ by an fp32 ulp, which can flip a bf16 rounding, so
+    # the two paths are compared through the masters above, not here)
+    obs = pkg.synth.make_obs(s, 4, 2)
+    pols[1].reserve(4, 0)
+    fresh = pkg.PTCGPolicy(s, precision=prec, tables=tabs, weights=w1, rollout_rows=4)
+    assert np.array_equal(pols[1].forward(obs).cpu().numpy(), fresh.forward(obs).cpu().numpy())
