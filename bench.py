@@ -519,8 +519,9 @@ def main():
         guni = torch.empty(A, device=dev)
 
         def rstep_static():
-            out = pol.forward(gsrc)
-            return pol.sample(out, gsrc[:, a:b], guni)
+            # forward with the sampler fused into its output kernel
+            _, act_, lp_, v_ = pol.forward_sample(gsrc, guni)
+            return act_, lp_, v_
 
         gsrc.copy_(ro[:A])
         guni.copy_(uni[0])

@@ -124,6 +124,17 @@ int ptcg_reserve(PtcgModel* m, int rollout_rows, int train_rows);
  * ptcg_forward_core native/model/ptcg_model3.cu:246-356). */
 int ptcg_forward(PtcgModel* m, const float* obs, int n, float* out, void* stream);
 
+/* Rollout forward with the sampler fused into its output step: writes out as
+ * ptcg_forward does and, per row, the action drawn from the masked softmax
+ * of the scores with the caller's uniform, its logprob and the value, in the
+ * same kernel that assembles out -- bit-identical to ptcg_forward followed
+ * by ptcg_sample_logits.  mask NULL takes the opt_mask columns of the obs
+ * rows (mask_stride ignored).  Replaces the rollout's decoder forward +
+ * sample_logits pair (native/src/pufferlib.cu:860-901, 584-718). */
+int ptcg_forward_sample(PtcgModel* m, const float* obs, int n, const float* mask,
+                        long mask_stride, const float* uniforms, float* out, float* actions,
+                        float* logprobs, float* values, void* stream);
+
 /* Train-path forward (saves activations for ptcg_backward, adds blind-V and
  * the belief aux heads).  Replaces policy_forward_train ->
  * ptcg_forward_core(train=1) (native/src/models.cu:791-797;

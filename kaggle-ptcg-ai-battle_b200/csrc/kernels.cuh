@@ -1306,6 +1306,57 @@ __global__ void k_sample(const float* dec, int n, int nopt, const float* mask, l
     }
 }
 
+// The rollout forward's last step with the sampler fused in (one warp per
+// row): the fused output row [scores | value] (scores from the contiguous
+// staging buffer, value = dot(v1 row, w2) + b2 in k_rowdot's order), then
+// k_sample's draw on those values: masked (-1e4) log-sum-exp, inverse CDF
+// on the caller's uniform, fallback to the last legal slot, logprob, value.
+// Bit-identical to the unfused output + k_sample.
+__global__ void k_out_sample(float* out, const float* staged, int nopt, const float* v1,
+                             const float* w2, const float* b2, int K, const float* mask,
+                             long mstride, const float* uni, float* actions, float* logprobs,
+                             float* values, int n) {
+    int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (r >= n) return;
+    const float* sc = staged + (long)r * nopt;
+    float* o = out + (long)r * (nopt + 1);
+    const float* x = v1 + (long)r * K;
+    float v = 0.f;
+    for (int k = lane; k < K; k += 32) v += x[k] * w2[k];
+    v = warp_sum(v) + b2[0];
+    const float* mk = mask + (long)r * mstride;
+    float mx = -INFINITY;
+    for (int a = lane; a < nopt; a += 32) {
+        const float l = sc[a];
+        o[a] = l;
+        mx = fmaxf(mx, mk[a] == 0.f ? -1e4f : l);
+    }
+    mx = warp_max(mx);
+    float se = 0.f;
+    for (int a = lane; a < nopt; a += 32) se += expf((mk[a] == 0.f ? -1e4f : sc[a]) - mx);
+    se = warp_sum(se);
+    const float lse = mx + logf(se);
+    if (lane == 0) {
+        o[nopt] = v;
+        float u = uni[r], cum = 0.f;
+        int pick = -1;
+        for (int a = 0; a < nopt; a++) {
+            float l = mk[a] == 0.f ? -1e4f : sc[a];
+            cum += expf(l - lse);
+            if (u < cum) { pick = a; break; }
+        }
+        if (pick < 0) {
+            pick = nopt - 1;
+            for (int a = nopt - 1; a >= 0; a--) if (mk[a] != 0.f) { pick = a; break; }
+        }
+        float l = mk[pick] == 0.f ? -1e4f : sc[pick];
+        actions[r] = (float)pick;
+        logprobs[r] = l - lse;
+        values[r] = v;
+    }
+}
+
 // seat-flipping GAE / V-trace (k_negamax_adv, ptcg_model2.cu:288-311)
 __global__ void k_negamax_adv(const float* values, const float* rewards, const float* dones,
                               const float* imp, const float* obs, long obs_size, int seat_col,

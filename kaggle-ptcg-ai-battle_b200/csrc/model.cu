@@ -672,8 +672,15 @@ static void rowdot(float* out, long os, const TI* in, long ldi, const float* w, 
     ++g_ptcg_launches, k_rowdot<TI><<<cdiv(rows, 8), 256, 0, s>>>(out, os, in, ldi, w, b, rows, K, g, gs, go);
 }
 
+// the sampler fused into the rollout forward's output step (k_out_sample)
+struct SampleArgs {
+    const float* mask; long mstride; const float* uni;
+    float *actions, *logprobs, *values;
+};
+
 static int forward_impl(PtcgModel* M, Work& Wk, Tab& t, const float* obs, int R, float* out,
-                        bool train, bool do_tables, cudaStream_t s) {
+                        bool train, bool do_tables, cudaStream_t s,
+                        const SampleArgs* smp = nullptr) {
     const Dims& z = M->z;
     const int dt = M->dt(), D = z.D, esz = M->esz();
     const ObsLayout& ol = z.ol;
@@ -796,7 +803,15 @@ static int forward_impl(PtcgModel* M, Work& Wk, Tab& t, const float* obs, int R,
                 Wk.ov1, 256, DT_F32);
     a.bias = M->w("oracle_v1_b").p; a.act = ACT_GELU; a.out2 = Wk.ov1pre; a.ldo2 = 256;
     gemm32(M, a, s);
-    // fused output [scores | value]: expand staged scores, then the value column
+    // fused output [scores | value]: expand staged scores, then the value
+    // column -- with the sampler in the same kernel when one is requested
+    if (smp) {
+        ++g_ptcg_launches, k_out_sample<<<cdiv(R, TPB / 32), TPB, 0, s>>>(out, Wk.out, z.NOPT, Wk.ov1,
+            M->w("oracle_v2_w").p, M->w("oracle_v2_b").p, 256,
+            smp->mask ? smp->mask : obs + ol.mask, smp->mask ? smp->mstride : ol.obs, smp->uni,
+            smp->actions, smp->logprobs, smp->values, R);
+        return 0;
+    }
     ++g_ptcg_launches, k_scale_copy<<<cdiv(NO, TPB), TPB, 0, s>>>(out, z.NOPT + 1, Wk.out, z.NOPT, R, z.NOPT, 1.f);
     rowdot<float>(out + z.NOPT, z.NOPT + 1, Wk.ov1, 256, M->w("oracle_v2_w").p,
                   M->w("oracle_v2_b").p, R, 256, 0, 0, 0, s);
@@ -1674,6 +1689,24 @@ int ptcg_forward(PtcgModel* M, const float* obs, int n, float* out, void* stream
     if (n == 0) return PTCG_OK;
     CK(cudaSetDevice(M->dev));
     forward_impl(M, M->roll, M->tab, obs, n, out, false, true, (cudaStream_t)stream);
+    CKL();
+    return PTCG_OK;
+}
+
+int ptcg_forward_sample(PtcgModel* M, const float* obs, int n, const float* mask,
+                        long mask_stride, const float* uniforms, float* out, float* actions,
+                        float* logprobs, float* values, void* stream) {
+    int e = ready(M);
+    if (e) return e;
+    REQ(obs && out && uniforms && actions && logprobs && values && n >= 0, PTCG_EINVAL,
+        "bad arguments");
+    REQ(!mask || mask_stride >= M->z.NOPT, PTCG_EINVAL, "mask stride below the option count");
+    REQ(M->roll.base && n <= M->roll.R, PTCG_ERANGE, "rollout batch %d exceeds reserved %d", n,
+        M->roll.R);
+    if (n == 0) return PTCG_OK;
+    CK(cudaSetDevice(M->dev));
+    SampleArgs sa{mask, mask_stride, uniforms, actions, logprobs, values};
+    forward_impl(M, M->roll, M->tab, obs, n, out, false, true, (cudaStream_t)stream, &sa);
     CKL();
     return PTCG_OK;
 }

@@ -55,6 +55,7 @@ _SIGS = {
     "ptcg_load_state": (I, [P, C.c_char_p, C.POINTER(C.c_long), C.POINTER(C.c_long)]),
     "ptcg_forward": (I, [P, P, I, P, P]),
     "ptcg_forward_train": (I, [P, P, I, P, P]),
+    "ptcg_forward_sample": (I, [P, P, I, P, L, P, P, P, P, P, P]),
     "ptcg_backward": (I, [P, P, P, I, F, I, P]),
     "ptcg_workspace_create": (I, [P, I, C.POINTER(P)]),
     "ptcg_workspace_destroy": (I, [P]),

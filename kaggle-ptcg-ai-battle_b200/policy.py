@@ -165,6 +165,23 @@ class PTCGPolicy:
         check(self.lib.ptcg_forward(self.h, _p(obs), obs.shape[0], _p(out), _stream()))
         return out
 
+    def forward_sample(self, obs, uniforms, mask=None):
+        """Rollout forward with the sampler fused into its last kernel ->
+        (out, actions, logprobs, values); the same values as forward()
+        followed by sample() on the obs rows' option mask (or `mask`)."""
+        obs = _f32(obs, self.device)
+        u = _f32(uniforms, self.device)
+        n = obs.shape[0]
+        out = torch.empty(n, self.shape.nopt + 1, device=self.device)
+        act = torch.empty(n, device=self.device)
+        logp = torch.empty(n, device=self.device)
+        val = torch.empty(n, device=self.device)
+        m = _f32(mask, self.device) if mask is not None else None
+        check(self.lib.ptcg_forward_sample(self.h, _p(obs), n, _p(m),
+                                           m.stride(0) if m is not None else 0, _p(u), _p(out),
+                                           _p(act), _p(logp), _p(val), _stream()))
+        return out, act, logp, val
+
     def forward_eval(self, obs):
         """(masked logits (-1e9 on illegal slots), oracle value) like
         PTCGTransformer.forward_eval (ptcg/rl/model.py:315-321)."""

@@ -395,3 +395,33 @@ def test_adam_segments_equal_adam_step(pkg, prec):
     pols[1].reserve(4, 0)
     fresh = pkg.PTCGPolicy(s, precision=prec, tables=tabs, weights=w1, rollout_rows=4)
     assert np.array_equal(pols[1].forward(obs).cpu().numpy(), fresh.forward(obs).cpu().numpy())
+
+
+@pytest.mark.parametrize("prec,preset", [("bf16", "c0"), ("fp32", "small"), ("bf16", "c4")])
+def test_forward_sample_equals_forward_then_sample(pkg, oracle, prec, preset):
+    """ptcg_forward_sample (sampler fused into the output kernel) gives the
+    same out, actions, logprobs and values, bit for bit, as ptcg_forward
+    followed by ptcg_sample_logits; the actions agree with the oracle's
+    inverse CDF on the same uniforms."""
+    n = 48
+    s, tabs, blob, obs, pol = make(pkg, preset, prec, n)
+    rng = np.random.default_rng(4)
+    u = rng.random(n).astype(np.float32)
+    u[0] = 0.9999999
+    a, b = s.offsets["opt_mask"]
+    out1 = pol.forward(obs)
+    act1, lp1, v1 = pol.sample(out1, obs[:, a:b], u)
+    out2, act2, lp2, v2 = pol.forward_sample(obs, u)
+    for x, y in ((out1, out2), (act1, act2), (lp1, lp2), (v1, v2)):
+        assert torch.equal(x, y)
+    assert torch.equal(v2, out2[:, -1])
+    # an explicit mask (here a subset of the legal slots, one slot always on)
+    m = obs[:, a:b].copy()
+    m[:, 1::2] = 0
+    m[np.arange(n), np.argmax(obs[:, a:b], 1)] = 1
+    out3, act3, lp3, _ = pol.forward_sample(obs, u, mask=m)
+    act4, lp4, _ = pol.sample(out1, m, u)
+    assert torch.equal(act3, act4) and torch.equal(lp3, lp4)
+    oact, ologp, margin = oracle.sample_logits(out2[:, :-1].cpu().numpy(), m, u)
+    ok = margin > 1e-5
+    assert np.array_equal(act3.cpu().numpy()[ok].astype(np.int64), oact[ok])
