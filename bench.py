@@ -50,7 +50,7 @@ def parse():
                     help="rows per micro-batch (c0: 16384; c4: 1024)")
     ap.add_argument("--rollout-agents", type=int, default=None,
                     help="rollout agents per GPU (config 1: 1024; config 4: 4096)")
-    ap.add_argument("--dp", default="allreduce", choices=["allreduce", "sharded"],
+    ap.add_argument("--dp", default="sharded", choices=["allreduce", "sharded"],
                     help="N>1 gradient exchange: bucketed all-reduce + Adam on every rank, or "
                          "bucketed reduce-scatter + Adam on each rank's shard + all-gather")
     ap.add_argument("--rollout-graph", type=int, default=1,
