@@ -566,10 +566,31 @@ def main():
         q1.record()
         torch.cuda.synchronize()
         qms = q0.elapsed_time(q1)
-        tt = torch.tensor([rms, qms], device=dev)
+        # end to end with the compact transfer form (int16 ids): the packed
+        # rows cross PCIe and the device expands them into the graph's input
+        import ptcg_b200.native as pnative
+        pk_h = torch.from_numpy(pnative.obs_pack(s, ro_h.numpy())).pin_memory()
+        pk_d = torch.empty(A, pk_h.shape[1], dtype=torch.uint8, device=dev)
+        c0_, c1_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0_.record()
+        for j in range(args.rollout_steps):
+            k = j % nroll
+            pk_d.copy_(pk_h[k * A:(k + 1) * A], non_blocking=True)
+            pol.obs_unpack(pk_d, out=gsrc)
+            guni.copy_(uni[j])
+            if graph is not None:
+                graph.replay()
+                acts = gout[0]
+            else:
+                acts = rstep_static()[0]
+            acts.cpu()
+        c1_.record()
+        torch.cuda.synchronize()
+        cms = c0_.elapsed_time(c1_)
+        tt = torch.tensor([rms, qms, cms], device=dev)
         if world > 1:
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        rms, qms = [float(x) for x in tt.cpu()]
+        rms, qms, cms = [float(x) for x in tt.cpu()]
         from ptcg_b200.config import forward_flops
         peaks_r, src_r = measured_peaks()
         fl = forward_flops(s, "first")["total"]
@@ -583,6 +604,8 @@ def main():
                    "ms_per_env_step": rms / args.rollout_steps,
                    "cuda_graph": graph is not None,
                    "h2d_bytes_per_step": A * s.obs_size * 4, "d2h_bytes_per_step": A * 4,
+                   "e2e_compact_obs": {"value": A * args.rollout_steps * world / (cms / 1e3),
+                                       "h2d_bytes_per_step": A * int(pk_h.shape[1])},
                    "roofline": {"kernel": "whole rollout forward + sampler (all kernels)",
                                 "bound": "tensor", "achieved": ach, "peak": pk,
                                 "unit": "TFLOP/s", "frac": ach / pk,

@@ -58,6 +58,21 @@ int ptcg_abi_version(void);
  * Packed fp32 weight blob order = PT_PARAMS (native/model/ptcg_model.cu:95-126,
  * mirrored by native/tools/native_weights.py:45-91).  cols == 0 for 1-D. */
 long ptcg_obs_size(const PtcgShape* s);
+/* Compact transfer form of observation rows, for the host -> device copy of
+ * every rollout step (the reference copies fp32 rows, native/src/vecenv.h:
+ * 310-345).  A packed row holds the fields that carry ids -- token ints,
+ * option ints, the option mask, the decision ints and the oracle block's
+ * card ids -- as int16, then every other field as fp32, in row order within
+ * each part; ptcg_obs_packed_bytes gives its size (a 16-byte multiple; c0:
+ * 21,376 bytes against 23,680 for the fp32 row).  ptcg_obs_pack (host)
+ * refuses, with PTCG_EINVAL and *bad_index = row * obs_size + column, any id
+ * field that is not an integer in [-32768, 32767], so the round trip is
+ * exact (a -0.0 id comes back as +0.0); ptcg_obs_unpack (device, packed 16-
+ * byte aligned) writes the fp32 rows the model reads. */
+long ptcg_obs_packed_bytes(const PtcgShape* s);
+int ptcg_obs_pack(const PtcgShape* s, const float* rows, long n, void* packed, long* bad_index);
+int ptcg_obs_unpack(const PtcgShape* s, const void* packed, long n, float* rows, void* stream);
+
 /* Column of the acting seat in an observation row: global_f[31]
  * (GlobF.ACTOR_SEAT, ptcg/rl/buffers.py:170; PT_SEAT_COL_M of
  * native/model/ptcg_model2.cu:287). */

@@ -1357,6 +1357,44 @@ __global__ void k_out_sample(float* out, const float* staged, int nopt, const fl
     }
 }
 
+// ------------------------------------------------------ compact observations
+// An observation row in transfer form: the id fields as int16, then the
+// float fields as fp32 (ptcg_obs_pack / ptcg_obs_unpack).  Each part is a
+// list of strided runs of the fp32 row: run k covers count[k] values at
+// row offsets dst[k] + e * stride[k], in the packed order.
+constexpr int OBS_RUNS = 8;
+struct ObsRuns {
+    int n;
+    int dst[OBS_RUNS], count[OBS_RUNS], stride[OBS_RUNS];
+};
+struct ObsPacking {
+    ObsRuns ints, floats;
+    int obs;                 // fp32 row length
+    long row_bytes;          // packed row bytes (16-byte multiple)
+    long float_off;          // byte offset of the fp32 part in a packed row
+};
+
+// one block per packed row: expand it into the fp32 row layout
+__global__ void k_obs_unpack(float* rows, const uint8_t* packed, ObsPacking pk, long n) {
+    const long r = blockIdx.x;
+    if (r >= n) return;
+    const int16_t* iv = (const int16_t*)(packed + r * pk.row_bytes);
+    const float* fv = (const float*)(packed + r * pk.row_bytes + pk.float_off);
+    float* out = rows + r * pk.obs;
+    int base = 0;
+    for (int k = 0; k < pk.ints.n; k++) {
+        const int c = pk.ints.count[k], d = pk.ints.dst[k], st = pk.ints.stride[k];
+        for (int e = threadIdx.x; e < c; e += blockDim.x) out[d + e * st] = (float)iv[base + e];
+        base += c;
+    }
+    base = 0;
+    for (int k = 0; k < pk.floats.n; k++) {
+        const int c = pk.floats.count[k], d = pk.floats.dst[k], st = pk.floats.stride[k];
+        for (int e = threadIdx.x; e < c; e += blockDim.x) out[d + e * st] = fv[base + e];
+        base += c;
+    }
+}
+
 // seat-flipping GAE / V-trace (k_negamax_adv, ptcg_model2.cu:288-311)
 __global__ void k_negamax_adv(const float* values, const float* rewards, const float* dones,
                               const float* imp, const float* obs, long obs_size, int seat_col,

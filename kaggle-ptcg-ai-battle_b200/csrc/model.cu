@@ -1260,6 +1260,91 @@ long ptcg_obs_size(const PtcgShape* s) {
     return make_layout(*s).obs;
 }
 
+// The transfer form of an observation row: the fields that hold ids (token
+// and option ints, the option mask, the decision ints, the oracle block's
+// card ids) as int16, every other field as fp32, in row order within each
+// part.  Oracle block (buffers.py): 24 hand (id, count) pairs, 24 split
+// (id, count, count) triples, 8 prize (id, count) pairs.
+static ObsPacking obs_packing(const PtcgShape& s) {
+    const ObsLayout L = make_layout(s);
+    ObsPacking p{};
+    auto add = [](ObsRuns& r, int dst, int count, int stride) {
+        r.dst[r.n] = dst; r.count[r.n] = count; r.stride[r.n] = stride; r.n++;
+    };
+    add(p.ints, L.toki, s.ltok * 5, 1);
+    add(p.ints, L.opti, s.nopt * 6, 1);
+    add(p.ints, L.mask, s.nopt, 1);
+    add(p.ints, L.deci, 8, 1);
+    add(p.ints, L.orc, 24, 2);
+    add(p.ints, L.orc + 48, 24, 3);
+    add(p.ints, L.orc + 120, 8, 2);
+    add(p.floats, L.tokf, s.ltok * s.tok_f, 1);
+    add(p.floats, L.optf, s.nopt * 8, 1);
+    add(p.floats, L.glob, 64, 1);
+    add(p.floats, L.decf, 16, 1);
+    add(p.floats, L.orc + 1, 24, 2);
+    add(p.floats, L.orc + 49, 24, 3);
+    add(p.floats, L.orc + 50, 24, 3);
+    add(p.floats, L.orc + 121, 8, 2);
+    long ni = 0, nf = 0;
+    for (int k = 0; k < p.ints.n; k++) ni += p.ints.count[k];
+    for (int k = 0; k < p.floats.n; k++) nf += p.floats.count[k];
+    p.obs = L.obs;
+    p.float_off = (ni * 2 + 15) / 16 * 16;
+    p.row_bytes = (p.float_off + nf * 4 + 15) / 16 * 16;
+    return p;
+}
+
+long ptcg_obs_packed_bytes(const PtcgShape* s) {
+    if (check_shape(s)) return -1;
+    return obs_packing(*s).row_bytes;
+}
+
+int ptcg_obs_pack(const PtcgShape* s, const float* rows, long n, void* packed, long* bad_index) {
+    if (check_shape(s)) return PTCG_EINVAL;
+    REQ(rows && packed && n >= 0, PTCG_EINVAL, "bad arguments");
+    const ObsPacking p = obs_packing(*s);
+    for (long r = 0; r < n; r++) {
+        const float* in = rows + r * p.obs;
+        uint8_t* row = (uint8_t*)packed + r * p.row_bytes;
+        int16_t* iv = (int16_t*)row;
+        float* fv = (float*)(row + p.float_off);
+        long b = 0;
+        for (int k = 0; k < p.ints.n; k++)
+            for (int e = 0; e < p.ints.count[k]; e++) {
+                const long col = p.ints.dst[k] + (long)e * p.ints.stride[k];
+                const float x = in[col];
+                if (!(x == truncf(x) && x >= -32768.f && x <= 32767.f)) {
+                    if (bad_index) *bad_index = r * p.obs + col;
+                    set_err("obs row %ld column %ld holds %g: not an integer in the int16 range "
+                            "of the compact form", r, col, (double)x);
+                    return PTCG_EINVAL;
+                }
+                iv[b++] = (int16_t)x;
+            }
+        for (long i = b * 2; i < p.float_off; i++) row[i] = 0;
+        b = 0;
+        for (int k = 0; k < p.floats.n; k++)
+            for (int e = 0; e < p.floats.count[k]; e++)
+                fv[b++] = in[p.floats.dst[k] + (long)e * p.floats.stride[k]];
+        for (long i = p.float_off + b * 4; i < p.row_bytes; i++) row[i] = 0;
+    }
+    return PTCG_OK;
+}
+
+int ptcg_obs_unpack(const PtcgShape* s, const void* packed, long n, float* rows, void* stream) {
+    if (check_shape(s)) return PTCG_EINVAL;
+    REQ(packed && rows && n >= 0, PTCG_EINVAL, "bad arguments");
+    REQ(((uintptr_t)packed & 15) == 0, PTCG_EINVAL, "packed rows must be 16-byte aligned");
+    if (n == 0) return PTCG_OK;
+    const ObsPacking p = obs_packing(*s);
+    REQ(n <= 0x7fffffffL, PTCG_ERANGE, "too many rows");
+    ++g_ptcg_launches, k_obs_unpack<<<(unsigned)n, 256, 0, (cudaStream_t)stream>>>(
+        rows, (const uint8_t*)packed, p, n);
+    CKL();
+    return PTCG_OK;
+}
+
 long ptcg_seat_column(const PtcgShape* s) {
     if (check_shape(s)) return -1;
     return make_layout(*s).glob + 31;              // global_f[31], GlobF.ACTOR_SEAT

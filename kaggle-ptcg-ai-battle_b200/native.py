@@ -39,6 +39,9 @@ _SIGS = {
     "ptcg_abi_version": (I, []),
     "ptcg_obs_size": (L, [C.POINTER(PtcgShape)]),
     "ptcg_seat_column": (L, [C.POINTER(PtcgShape)]),
+    "ptcg_obs_packed_bytes": (L, [C.POINTER(PtcgShape)]),
+    "ptcg_obs_pack": (I, [C.POINTER(PtcgShape), P, L, P, C.POINTER(C.c_long)]),
+    "ptcg_obs_unpack": (I, [C.POINTER(PtcgShape), P, L, P, P]),
     "ptcg_num_params": (I, [C.POINTER(PtcgShape)]),
     "ptcg_param_info": (I, [C.POINTER(PtcgShape), I, C.POINTER(C.c_char_p),
                             C.POINTER(C.c_long), C.POINTER(C.c_long)]),
@@ -144,3 +147,18 @@ def check(rc):
     if rc != 0:
         raise PtcgError(f"ptcg error {rc}: {lib().ptcg_last_error().decode()}")
     return rc
+
+
+def obs_pack(shape, rows):
+    """Observation rows (n, obs_size) float32 -> their compact transfer form,
+    (n, ptcg_obs_packed_bytes) uint8 (ptcg_obs_pack, host only)."""
+    import numpy as np
+    h = lib()
+    cs = PtcgShape.from_shape(shape)
+    rows = np.ascontiguousarray(rows, np.float32)
+    nb = h.ptcg_obs_packed_bytes(C.byref(cs))
+    out = np.empty((rows.shape[0], nb), np.uint8)
+    bad = C.c_long(-1)
+    check(h.ptcg_obs_pack(C.byref(cs), rows.ctypes.data_as(P), rows.shape[0],
+                          out.ctypes.data_as(P), C.byref(bad)))
+    return out

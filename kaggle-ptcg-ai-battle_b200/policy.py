@@ -182,6 +182,15 @@ class PTCGPolicy:
                                            _p(act), _p(logp), _p(val), _stream()))
         return out, act, logp, val
 
+    def obs_unpack(self, packed, out=None):
+        """Compact rows (device uint8 tensor, n x ptcg_obs_packed_bytes, see
+        native.obs_pack) -> fp32 observation rows on the device."""
+        n = packed.shape[0]
+        if out is None:
+            out = torch.empty(n, self.obs_size, device=self.device)
+        check(self.lib.ptcg_obs_unpack(C.byref(self._cs), _p(packed), n, _p(out), _stream()))
+        return out
+
     def forward_eval(self, obs):
         """(masked logits (-1e9 on illegal slots), oracle value) like
         PTCGTransformer.forward_eval (ptcg/rl/model.py:315-321)."""
