@@ -50,9 +50,11 @@ def parse():
                     help="rows per micro-batch (c0: 16384; c4: 1024)")
     ap.add_argument("--rollout-agents", type=int, default=None,
                     help="rollout agents per GPU (config 1: 1024; config 4: 4096)")
-    ap.add_argument("--dp", default="sharded", choices=["allreduce", "sharded"],
-                    help="N>1 gradient exchange: bucketed all-reduce + Adam on every rank, or "
-                         "bucketed reduce-scatter + Adam on each rank's shard + all-gather")
+    ap.add_argument("--dp", default="sharded", choices=["allreduce", "sharded", "native"],
+                    help="N>1 gradient exchange: bucketed all-reduce + Adam on every rank; "
+                         "bucketed reduce-scatter + Adam on each rank's shard + all-gather "
+                         "driven from Python (sharded); or the same exchange issued by the "
+                         "library itself over NCCL (native)")
     ap.add_argument("--rollout-graph", type=int, default=1,
                     help="replay the rollout forward + sampler as a CUDA graph")
     ap.add_argument("--rollout-steps", type=int, default=64)
@@ -364,7 +366,10 @@ def main():
     # --- data parallel: bucketed all-reduce overlapped with the backward
     grads = pol.arena(1)
     reducer = None
-    if world > 1:
+    native_dp = world > 1 and args.dp == "native"
+    if native_dp:
+        pol.dp_init()
+    elif world > 1:
         from ptcg_b200.dp import BucketAllReduce, checksum_u64, weights_agree
         if args.dp == "sharded":
             reducer = pol.sharded_adam(lr=3e-4, betas=(0.9, 0.999), eps=1e-8, max_norm=1.0)
@@ -380,7 +385,9 @@ def main():
         if reducer is not None:
             reducer.reset()
         pol.train_step(o, ac, ol, ad, va, re, prio, args.segments, args.horizon,
-                       skip_adam=world > 1, stats=stats, **hyper)
+                       skip_adam=world > 1 and not native_dp, stats=stats, **hyper)
+        if native_dp:
+            pol.dp_weights_agree(ck[i])
         if reducer is not None:
             covered.append(reducer.covered(grads.numel()))
             if args.dp == "sharded":
@@ -432,6 +439,42 @@ def main():
     value = nt * world * args.steps / (ms_max / 1e3)
     st = stats.cpu().numpy()
 
+    # --- end to end through the public API: every step copies its inputs
+    #     from pinned host memory (HostFeed: on a copy stream, the next
+    #     step's inputs crossing PCIe while this step computes), runs the
+    #     train step and reads the loss stats back to the host
+    from ptcg_b200.feed import HostFeed
+    host = dict(obs=obs_h, act=act_h.pin_memory(), old=old.cpu().pin_memory(),
+                adv=adv.cpu().pin_memory(), val=vals.cpu().pin_memory(),
+                ret=ret.cpu().pin_memory())
+    feed = HostFeed(host, dev, depth=2)
+    h2d = feed.bytes_per_put
+    d2h = 16 * 4
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    feed.start()
+    feed.put(host)
+    for i in range(args.e2e_steps):
+        fb = feed.get()
+        if i + 1 < args.e2e_steps:
+            feed.put(host)
+        step(0, fb["obs"], fb["act"], fb["old"], fb["adv"], fb["val"], fb["ret"])
+        feed.release()
+        _ = stats.cpu()
+    f1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([f0.elapsed_time(f1)], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e = nt * world * args.e2e_steps / (float(te.item()) / 1e3)
+
+    # the library's own exchange is done: the timings below are per GPU
+    if native_dp:
+        pol.dp_finalize()
+
     # --- optimizer roofline (HBM): ptcg_adam_step = norm pass + fused
     #     clip/Adam/bf16-copy pass, timed alone with CUDA events
     from ptcg_b200.config import optimizer_bytes
@@ -469,38 +512,6 @@ def main():
     torch.cuda.synchronize()
     write_gbs = 10 * wbuf.numel() * 2 / (w0.elapsed_time(w1) / 1e3) / 1e9
     del wbuf
-
-    # --- end to end through the public API: every step copies its inputs
-    #     from pinned host memory (HostFeed: on a copy stream, the next
-    #     step's inputs crossing PCIe while this step computes), runs the
-    #     train step and reads the loss stats back to the host
-    from ptcg_b200.feed import HostFeed
-    host = dict(obs=obs_h, act=act_h.pin_memory(), old=old.cpu().pin_memory(),
-                adv=adv.cpu().pin_memory(), val=vals.cpu().pin_memory(),
-                ret=ret.cpu().pin_memory())
-    feed = HostFeed(host, dev, depth=2)
-    h2d = feed.bytes_per_put
-    d2h = 16 * 4
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record()
-    feed.start()
-    feed.put(host)
-    for i in range(args.e2e_steps):
-        fb = feed.get()
-        if i + 1 < args.e2e_steps:
-            feed.put(host)
-        step(0, fb["obs"], fb["act"], fb["old"], fb["adv"], fb["val"], fb["ret"])
-        feed.release()
-        _ = stats.cpu()
-    f1.record()
-    torch.cuda.synchronize()
-    te = torch.tensor([f0.elapsed_time(f1)], device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e = nt * world * args.e2e_steps / (float(te.item()) / 1e3)
 
     # --- rollout forward (config 1): fresh observations every env step.
     #     With --rollout-graph the forward + sampler are one CUDA graph
@@ -704,7 +715,11 @@ def main():
         "clocks": clk.summary(),
         "weights_identical_across_ranks": ok,
         "grad_buckets": ({"per_step": len(reducer.spans), "cover_arena_once": all(covered)}
-                         if reducer is not None else None),
+                         if reducer is not None else
+                         # the library checks at ptcg_dp_init that its spans tile the arena
+                         # and, every step, that all of them were reduce-scattered
+                         {"exchange": "library (NCCL)", "cover_arena_once": True}
+                         if native_dp else None),
         "loss_stats": {"total": float(st[0]), "approx_kl": float(st[5]),
                        "grad_norm": float(st[8])},
     }

@@ -27,7 +27,8 @@ enum {
     PTCG_EINVAL = 1,     /* bad argument / shape */
     PTCG_ECUDA = 2,      /* CUDA runtime error */
     PTCG_ESTATE = 3,     /* call out of order (no weights, not reserved...) */
-    PTCG_ERANGE = 4      /* size beyond what was reserved */
+    PTCG_ERANGE = 4,     /* size beyond what was reserved */
+    PTCG_ENCCL = 5       /* NCCL unavailable or a collective could not be issued */
 };
 
 enum { PTCG_FP32 = 0, PTCG_BF16 = 1 };
@@ -377,6 +378,36 @@ int ptcg_set_step(PtcgModel* m, long step);
 /* 64-bit checksum of the master weights (device, written to out[0] as two
  * uint32 halves) for the cross-rank "weights identical" check. */
 int ptcg_weights_checksum(PtcgModel* m, unsigned int* out_dev, void* stream);
+
+/* ---- native data-parallel exchange --------------------------------------------
+ * The gradient average of data parallelism fused with a sharded Adam, run by
+ * the library over NCCL (opened at run time: libnccl.so.2, or the file named
+ * by $PTCG_NCCL_LIB).  Replaces the post-backward ncclAllReduce of the grad
+ * arena and the optimizer every rank runs over all of it
+ * (native/src/muon.cu:209-214).  Once ptcg_dp_init returned on every rank:
+ *  - each final gradient span of backward (the spans ptcg_set_grad_hook would
+ *    report, which it no longer does) is reduce-scattered (average) on a
+ *    library stream while the rest of backward runs: in ptcg_train_step's last
+ *    micro-batch and in ptcg_backward without PTCG_BWD_PARTIAL;
+ *  - the Adam of ptcg_train_step (skip_adam == 0) and ptcg_adam_step clips
+ *    with the global gradient norm (one fp64 all-reduce), updates this rank's
+ *    piece of every span, all-gathers the updated master weights and
+ *    refreshes the bf16 copies.  Weights stay identical on every rank; the
+ *    grad arena keeps this rank's own (unaveraged) gradients, and the Adam
+ *    moments are valid on this rank's pieces only.
+ * Every rank must make the same calls in the same order (they are
+ * collectives).  uid: ptcg_dp_unique_id on one rank (128 bytes), passed to
+ * every rank by the caller.  ptcg_dp_init blocks until all `world` ranks
+ * joined.  ptcg_dp_weights_agree takes the min and max over ranks of the
+ * weight checksum (ptcg_weights_checksum) in one collective (a MAX
+ * all-reduce of [v, ~v]) and writes them, in stream order, to minmax_dev
+ * (2 device int64): equal when every rank holds the same weights.
+ * ptcg_dp_finalize ends the exchange (abort != 0: ncclCommAbort, callable
+ * while a peer is gone); ptcg_destroy also ends it. */
+int ptcg_dp_unique_id(void* uid_out);
+int ptcg_dp_init(PtcgModel* m, const void* uid, int rank, int world);
+int ptcg_dp_weights_agree(PtcgModel* m, long long* minmax_dev, void* stream);
+int ptcg_dp_finalize(PtcgModel* m, int abort);
 
 /* CUDA-event timing of every launch of one GEMM kernel class (1 = tcgen05
  * tensor-core GEMM, 2 = SIMT GEMM, 0 = off) until the next call; read back

@@ -19,7 +19,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I" + INCLUDE, "-I" + CSRC]
 SOURCES = ["model.cu", "gemm_simt.cu", "gemm_tc.cu", "attention.cu", "attention_tc.cu",
-           "puffer_plugin.cu"]
+           "puffer_plugin.cu", "dp_nccl.cu"]
 
 
 def _needs(obj, deps):
@@ -53,7 +53,7 @@ def build_all(verbose=False, force=False):
         list(ex.map(run, jobs))
     objs = [os.path.join(BUILD, s.replace(".cu", ".o")) for s in SOURCES]
     if force or jobs or not os.path.exists(LIB):
-        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart", "-ldl"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

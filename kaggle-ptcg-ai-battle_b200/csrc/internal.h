@@ -91,3 +91,23 @@ void attn_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
               const void* out, long ldo, const void* dout, long lddo,
               const float* lse, void* dqkv, long lddqkv, float* dbias, int nseq, int L,
               int H, cudaStream_t s, const int* extent = nullptr);
+
+// ---- native data-parallel exchange (dp_nccl.cu); every int function
+// returns 0 on success, else nonzero with the text in dp_last_error()
+constexpr int DP_UID_BYTES = 128;
+struct DpState;
+const char* dp_last_error();
+int dp_unique_id(void* out128);
+// spans: nspans {arena offset, count} pairs in the order backward finalises
+// them; they must tile [0, n_arena).  Collective over the world's ranks.
+int dp_create(DpState** out, const void* uid, int rank, int world, int dev, const long* spans,
+              int nspans, long n_arena);
+void dp_destroy(DpState* d, bool abort);
+int dp_bucket(DpState* d, const float* grads, long off, long count, cudaStream_t s);
+int dp_join(DpState* d, cudaStream_t s, int* spans_seen);
+int dp_nbuckets(DpState* d);
+float* dp_shard(DpState* d, long* used, const long** seg, int* nseg, double** sumsq);
+int dp_allreduce_sum_f64(DpState* d, double* x, cudaStream_t s);
+int dp_gather_params(DpState* d, float* params, cudaStream_t s);
+int dp_weights_agree(DpState* d, const unsigned int* ck_dev, long long* minmax_dev,
+                     cudaStream_t s);

@@ -208,6 +208,8 @@ struct PtcgModel {
     Work roll, trn;
     ptcg_grad_hook hook = nullptr;
     void* hook_user = nullptr;
+    DpState* dp = nullptr;              // native data-parallel exchange (ptcg_dp_init)
+    bool dp_fail = false;               // a span's reduce-scatter could not be issued
     const float* trn_last_obs = nullptr;
     int trn_last_n = 0;
     int esz() const { return prec == PTCG_BF16 ? 2 : 4; }
@@ -840,11 +842,38 @@ static int forward_impl(PtcgModel* M, Work& Wk, Tab& t, const float* obs, int R,
 }
 
 // --------------------------------------------------------------- backward
+// A span of the grad arena is final: with the native data-parallel exchange
+// on, start its reduce-scatter; else hand it to the caller's hook.
 static void fire_hook(PtcgModel* M, const char* first, const char* last_excl, cudaStream_t s) {
-    if (!M->hook) return;
+    if (!M->hook && !M->dp) return;
     long a = M->off[M->idx[first]];
     long b = last_excl ? M->off[M->idx[last_excl]] : M->n_arena;
-    if (b > a) M->hook(M->hook_user, a, b - a, (void*)s);
+    if (b <= a) return;
+    if (M->dp) {
+        if (dp_bucket(M->dp, M->grads, a, b - a, s)) {
+            set_err("data-parallel reduce-scatter: %s", dp_last_error());
+            M->dp_fail = true;
+        }
+    } else {
+        M->hook(M->hook_user, a, b - a, (void*)s);
+    }
+}
+
+// The spans fire_hook reports in one step, in firing order: ln_f and the
+// heads after it, each block from the last to the first, the encoders, then
+// the tables ({offset, count} pairs).
+static std::vector<long> hook_spans(const PtcgModel* M) {
+    auto o = [&](const std::string& n) { return M->off[M->idx.at(n)]; };
+    std::vector<long> v;
+    auto add = [&](long a, long b) { if (b > a) { v.push_back(a); v.push_back(b - a); } };
+    const int L = M->z.LAYERS;
+    add(o("lnf_w"), M->n_arena);
+    for (int i = L - 1; i >= 0; i--)
+        add(o("b" + std::to_string(i) + "_ln1_w"),
+            i == L - 1 ? o("lnf_w") : o("b" + std::to_string(i + 1) + "_ln1_w"));
+    add(o("zone_emb"), o("b0_ln1_w"));
+    add(o("card_id_emb"), o("zone_emb"));
+    return v;
 }
 
 // On entry dx holds d(x_out) and the FFN2 bias grad of this block is
@@ -1492,6 +1521,8 @@ int ptcg_destroy(PtcgModel* M) {
     if (!M) return PTCG_OK;
     cudaSetDevice(M->dev);
     cudaDeviceSynchronize();
+    dp_destroy(M->dp, false);
+    M->dp = nullptr;
     free_work(M->roll); free_work(M->trn);
     void* ptrs[] = {M->params, M->grads, M->am, M->av, M->step_dev, M->wbf, M->d_copies,
                     M->d_chunk_copy, M->d_partials, M->d_misc, M->d_ck, M->card_static,
@@ -1911,7 +1942,8 @@ int ptcg_backward(PtcgModel* M, const float* grad, const float* returns, int aux
     backward_impl(M, M->trn, M->trn_last_obs, grad, returns, R, norm,
                   prize_count > 0.f ? nullptr : cnt, prize_count, aux, last, s);
     tables_bwd(M, s);
-    if (M->hook && last) fire_hook(M, "card_id_emb", "zone_emb", s);
+    if (last) fire_hook(M, "card_id_emb", "zone_emb", s);
+    if (M->dp_fail) { M->dp_fail = false; return PTCG_ENCCL; }
     CKL();
     return PTCG_OK;
 }
@@ -1997,9 +2029,43 @@ static void clear_work_if_nonfinite(PtcgModel* M, const float* st, cudaStream_t 
         (long)(M->trn.bytes / 16));
 }
 
+// Adam with the native data-parallel exchange: wait for the reduce-scatters
+// of every span, clip with the global norm (this rank's shard sum of squares,
+// all-reduced), update this rank's pieces, all-gather the updated weights and
+// refresh the bf16 copies.  The same update as all-reduce + k_adam on every
+// rank (native/src/muon.cu:209-214 then the optimizer).
+static int dp_adam(PtcgModel* M, float lr, float b1, float b2, float eps, float max_norm,
+                   const float* gate, float* st, cudaStream_t s) {
+    int seen = 0;
+    REQ(!dp_join(M->dp, s, &seen), PTCG_ENCCL, "data-parallel join: %s", dp_last_error());
+    REQ(seen == dp_nbuckets(M->dp), PTCG_ESTATE,
+        "data-parallel Adam: %d of %d gradient spans were reduce-scattered since the last step "
+        "(run the final backward first)", seen, dp_nbuckets(M->dp));
+    long used = 0;
+    const long* seg = nullptr;
+    int nseg = 0;
+    double* ss = nullptr;
+    float* shard = dp_shard(M->dp, &used, &seg, &nseg, &ss);
+    ++g_ptcg_launches, k_sumsq<<<M->sumsq_grid, 256, 0, s>>>(M->d_partials, shard, used);
+    ++g_ptcg_launches, k_sumsq_final<<<1, 256, 0, s>>>(ss, M->d_partials, M->sumsq_grid);
+    REQ(!dp_allreduce_sum_f64(M->dp, ss, s), PTCG_ENCCL, "data-parallel norm: %s", dp_last_error());
+    if (nseg > 0) {
+        dim3 g((unsigned)std::max(1, M->adam_grid / nseg), (unsigned)nseg);
+        ++g_ptcg_launches, k_adam_seg<<<g, 256, 0, s>>>(M->params, M->am, M->av, shard, seg, ss, lr,
+            b1, b2, eps, max_norm, M->step_dev, gate, st);
+    }
+    ++g_ptcg_launches, k_step_inc<<<1, 1, 0, s>>>(M->step_dev, st);
+    clear_work_if_nonfinite(M, st, s);
+    REQ(!dp_gather_params(M->dp, M->params, s), PTCG_ENCCL, "data-parallel gather: %s",
+        dp_last_error());
+    CKL();
+    return refresh_copies(M, s);
+}
+
 static int adam_impl(PtcgModel* M, float lr, float b1, float b2, float eps, float max_norm,
                      const float* gate, float* stats, cudaStream_t s) {
     float* st = stats ? stats : M->d_misc + 32;
+    if (M->dp) return dp_adam(M, lr, b1, b2, eps, max_norm, gate, st, s);
     ++g_ptcg_launches, k_sumsq<<<M->sumsq_grid, 256, 0, s>>>(M->d_partials, M->grads, M->n_arena);
     ++g_ptcg_launches, k_adam<<<M->adam_grid, 256, 0, s>>>(M->params, M->am, M->av, M->grads, M->n_arena,
         M->d_partials, M->sumsq_grid, lr, b1, b2, eps, max_norm, M->step_dev, gate, st,
@@ -2266,7 +2332,8 @@ int ptcg_train_step(PtcgModel* M, const float* obs, const float* actions, const 
                       mb == nmb - 1, s);
     }
     tables_bwd(M, s);
-    if (M->hook) fire_hook(M, "card_id_emb", "zone_emb", s);
+    fire_hook(M, "card_id_emb", "zone_emb", s);
+    if (M->dp_fail) { M->dp_fail = false; return PTCG_ENCCL; }
     if (!skip_adam) {
         e = adam_impl(M, lr, beta1, beta2, eps, max_norm, nullptr, stats + 8, s);
         if (e) return e;
@@ -2451,6 +2518,48 @@ int ptcg_kernel_timer_read(PtcgModel* M, double* ms, long* launches, double* flo
 int ptcg_kernel_timer_bytes(PtcgModel* M, double* bytes) {
     REQ(M && bytes, PTCG_EINVAL, "null argument");
     *bytes = M->kt.bytes;
+    return PTCG_OK;
+}
+
+int ptcg_dp_unique_id(void* out) {
+    REQ(out, PTCG_EINVAL, "null argument");
+    REQ(!dp_unique_id(out), PTCG_ENCCL, "ptcg_dp_unique_id: %s", dp_last_error());
+    return PTCG_OK;
+}
+
+int ptcg_dp_init(PtcgModel* M, const void* uid, int rank, int world) {
+    REQ(M && uid, PTCG_EINVAL, "null argument");
+    REQ(world >= 1 && rank >= 0 && rank < world, PTCG_EINVAL, "bad rank %d / world %d", rank, world);
+    REQ(!M->dp, PTCG_ESTATE, "ptcg_dp_init: the data-parallel exchange is already on");
+    CK(cudaSetDevice(M->dev));
+    CK(cudaDeviceSynchronize());
+    std::vector<long> sp = hook_spans(M);
+    DpState* d = nullptr;
+    REQ(!dp_create(&d, uid, rank, world, M->dev, sp.data(), (int)(sp.size() / 2), M->n_arena),
+        PTCG_ENCCL, "ptcg_dp_init: %s", dp_last_error());
+    M->dp = d;
+    return PTCG_OK;
+}
+
+int ptcg_dp_weights_agree(PtcgModel* M, long long* minmax_dev, void* stream) {
+    REQ(M && minmax_dev, PTCG_EINVAL, "null argument");
+    REQ(M->dp, PTCG_ESTATE, "ptcg_dp_weights_agree: no data-parallel exchange (ptcg_dp_init)");
+    CK(cudaSetDevice(M->dev));
+    cudaStream_t s = (cudaStream_t)stream;
+    CK(cudaMemsetAsync(M->d_ck, 0, 8, s));
+    ++g_ptcg_launches, k_checksum<<<256, 256, 0, s>>>(M->d_ck, M->params, M->n_arena);
+    CKL();
+    REQ(!dp_weights_agree(M->dp, M->d_ck, minmax_dev, s), PTCG_ENCCL,
+        "ptcg_dp_weights_agree: %s", dp_last_error());
+    return PTCG_OK;
+}
+
+int ptcg_dp_finalize(PtcgModel* M, int abort) {
+    REQ(M, PTCG_EINVAL, "null model");
+    if (!M->dp) return PTCG_OK;
+    CK(cudaSetDevice(M->dev));
+    dp_destroy(M->dp, abort != 0);
+    M->dp = nullptr;
     return PTCG_OK;
 }
 

@@ -86,6 +86,10 @@ _SIGS = {
     "ptcg_get_step": (I, [P, C.POINTER(C.c_long)]),
     "ptcg_set_step": (I, [P, L]),
     "ptcg_weights_checksum": (I, [P, P, P]),
+    "ptcg_dp_unique_id": (I, [P]),
+    "ptcg_dp_init": (I, [P, P, I, I]),
+    "ptcg_dp_weights_agree": (I, [P, P, P]),
+    "ptcg_dp_finalize": (I, [P, I]),
     "ptcg_kernel_timer": (I, [P, I]),
     "ptcg_launch_count": (C.c_longlong, []),
     "ptcg_kernel_timer_entries": (I, [P, I, P, P]),

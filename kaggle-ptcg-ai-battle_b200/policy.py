@@ -279,6 +279,38 @@ class PTCGPolicy:
         self.set_grad_hook(red)
         return red
 
+    def dp_init(self, group=None):
+        """Turn on the library's own data-parallel exchange over NCCL
+        (ptcg_dp_init): rank 0 of the torch.distributed `group` makes the
+        NCCL id and broadcasts it; every rank of the group must call this.
+        From then on the final gradient spans are reduce-scattered during
+        backward and train_step / adam_step run the sharded Adam and the
+        all-gather of the weights inside the library."""
+        import torch.distributed as dist
+        uid = np.zeros(128, np.uint8)
+        if dist.get_rank(group) == 0:
+            check(self.lib.ptcg_dp_unique_id(uid.ctypes.data_as(C.c_void_p)))
+        t = torch.from_numpy(uid)
+        if dist.get_backend(group) == "nccl":
+            t = t.to(self.device)
+        dist.broadcast(t, src=dist.get_global_rank(group, 0) if group is not None else 0,
+                       group=group)
+        uid = t.cpu().numpy().copy()
+        check(self.lib.ptcg_dp_init(self.h, uid.ctypes.data_as(C.c_void_p),
+                                    dist.get_rank(group), dist.get_world_size(group)))
+
+    def dp_weights_agree(self, out=None):
+        """int64 device tensor {min, max} over the exchange's ranks of the
+        weight checksum (one collective, no host wait): equal iff every rank
+        holds the same weights."""
+        if out is None:
+            out = torch.zeros(2, dtype=torch.int64, device=self.device)
+        check(self.lib.ptcg_dp_weights_agree(self.h, _p(out), _stream()))
+        return out
+
+    def dp_finalize(self, abort=False):
+        check(self.lib.ptcg_dp_finalize(self.h, int(bool(abort))))
+
     # ---------------------------------------------- minibatch selection
     def prio_replay(self, advantages, alpha, beta, total_agents, uniforms):
         """(idx int32, mb_prio, probs) of prioritised segment replay over

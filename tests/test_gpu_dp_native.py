@@ -1,0 +1,129 @@
+"""The library's own data-parallel exchange (ptcg_dp_init) on two GPUs.
+
+Two NCCL ranks, each with its own minibatch, run the same PPO train steps
+twice: once with the exchange inside the library (reduce-scatter of every
+final gradient span during backward, Adam on the rank's shard, all-gather of
+the weights, all issued by ptcg_train_step), once with the Python-driven
+dp.ShardedAdam (the same exchange through torch.distributed).  The weights,
+the loss stats and the gradient norm after each step must agree, and the
+one-collective checksum check must find the ranks' weights identical.
+Skipped with fewer than two GPUs.
+"""
+import datetime
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                                 reason="needs two GPUs")]
+
+STEPS = 2
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _case(pkg, s, rank):
+    n_seg, horizon = 16, 8
+    nt = n_seg * horizon
+    obs = pkg.synth.make_obs_batch(s, nt, 40 + rank)
+    a, b = s.offsets["opt_mask"]
+    act = pkg.synth.sample_legal(obs[:, a:b], 5 + rank)
+    rng = np.random.default_rng(60 + rank)
+    old = rng.normal(-1.5, 0.3, nt).astype(np.float32)
+    adv = rng.standard_normal(nt).astype(np.float32)
+    ret = rng.standard_normal(nt).astype(np.float32)
+    val = (0.1 * rng.standard_normal(nt)).astype(np.float32)
+    prio = np.ones(n_seg, np.float32)
+    return (obs, act, old, adv, val, ret, prio, n_seg, horizon)
+
+
+def _worker(rank, world, port, out_dir, preset, prec):
+    sys.path.insert(0, ROOT)
+    import __graft_entry__
+    __graft_entry__.load_package()
+    import ptcg_b200 as pkg
+    torch.cuda.set_device(rank)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    s = pkg.config.PRESETS[preset]
+    tabs = pkg.synth.make_tables(s, 11)
+    blob = pkg.synth.make_weights(s, 21)
+    case = _case(pkg, s, rank)
+    res = {}
+    for mode in ("native", "python"):
+        pol = pkg.PTCGPolicy(s, precision=prec, tables=tabs, weights=blob, train_rows=64,
+                             device=rank)
+        red = None
+        if mode == "native":
+            pol.dp_init()
+        else:
+            red = pol.sharded_adam()
+        stats = torch.zeros(16, device=pol.device)
+        ws, sts, ck = [], [], []
+        for _ in range(STEPS):
+            if red is not None:
+                red.reset()
+            pol.train_step(*case, skip_adam=red is not None, stats=stats)
+            if red is not None:
+                red.step(stats[8:10])
+                c = pol.weights_checksum().to(torch.int64)
+                v = (c[0] & 0xFFFFFFFF) | (c[1] << 32)
+                both = torch.stack([v, torch.bitwise_not(v)])
+                dist.all_reduce(both, op=dist.ReduceOp.MAX)
+                mm = torch.stack([torch.bitwise_not(both[1]), both[0]])
+            else:
+                mm = pol.dp_weights_agree()
+            torch.cuda.synchronize()
+            ws.append(pol.save_weights())
+            sts.append(stats.cpu().numpy().copy())
+            ck.append(mm.cpu().numpy())
+        if mode == "native":
+            pol.dp_finalize()
+        else:
+            pol.set_grad_hook(None)
+        pol.close()
+        res[mode] = (np.stack(ws), np.stack(sts), np.stack(ck))
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"),
+             **{f"{m}_{k}": v for m, t in res.items() for k, v in zip(("w", "st", "ck"), t)})
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("preset,prec", [("small", "bf16"), ("tiny", "fp32")])
+def test_native_exchange_equals_python_sharded_adam(tmp_path, preset, prec):
+    world = 2
+    mp.start_processes(_worker, args=(world, _port(), str(tmp_path), preset, prec), nprocs=world,
+                       join=True, start_method="spawn")
+    z = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
+    for r in range(world):
+        wn, wp = z[r]["native_w"], z[r]["python_w"]
+        for k in range(STEPS):
+            d = np.linalg.norm(wn[k] - wp[k]) / np.linalg.norm(wp[k])
+            assert d <= 1e-5, (r, k, d)
+        # loss stats and {grad norm, applied}: same minibatch, same exchange
+        np.testing.assert_allclose(z[r]["native_st"][:, :10], z[r]["python_st"][:, :10],
+                                   rtol=1e-4, atol=1e-6)
+        assert (z[r]["native_st"][:, 9] == 1.0).all()
+        # the checksum's min and max over ranks agree: identical weights
+        for mode in ("native", "python"):
+            ck = z[r][f"{mode}_ck"]
+            assert (ck[:, 0] == ck[:, 1]).all(), (mode, ck)
+    # both ranks hold the same weights after every step
+    np.testing.assert_array_equal(z[0]["native_w"], z[1]["native_w"])
+    # the weights moved (the exchange did run an update)
+    assert np.abs(z[0]["native_w"][-1] - z[0]["native_w"][0]).max() > 0
