@@ -475,9 +475,14 @@ int ptcg_device_error(void);
 
 /* Kernels of the bf16 attention (no counterpart in the reference, whose
  * attention materialises fp32 probabilities, native/model/ptcg_kernels.cuh:
- * 223-289): 0 = mma.sync flash attention (default), 1 = tcgen05 / TMEM
- * flash attention.  Process-wide; takes effect at the next launch. */
+ * 223-289): 0 = mma.sync flash attention for both passes, 1 = tcgen05 / TMEM
+ * kernels for both, 2 = tcgen05 / TMEM backward with the mma.sync forward.
+ * The tcgen05 backward takes the sequences whose row extent fits one
+ * 128-row tile and leaves longer ones to the mma.sync backward.
+ * Process-wide; takes effect at the next launch; PTCG_ATTN_TC=<impl> sets
+ * it at load. */
 int ptcg_set_attention_impl(int impl);
+int ptcg_get_attention_impl(void);
 int ptcg_kernel_timer_read(PtcgModel* m, double* ms, long* launches, double* flops);
 /* Algorithmic HBM bytes of the launches timed since ptcg_kernel_timer(m, mode)
  * (operands read once, outputs written once; diagnostic, no counterpart in

@@ -406,13 +406,16 @@ __global__ void __launch_bounds__(128) k_attn_bwd_mma(
         const bf16* __restrict__ qkv, long ldqkv, const uint8_t* __restrict__ keep,
         const bf16* __restrict__ out, long ldo, const bf16* __restrict__ dout, long lddo,
         const float* __restrict__ lse, bf16* __restrict__ dqkv, long lddqkv,
-        float* __restrict__ dbias, int L, int H, const int* __restrict__ extent) {
+        float* __restrict__ dbias, int L, int H, const int* __restrict__ extent,
+        int skip_ext_le) {
     extern __shared__ __align__(16) uint8_t smraw[];
     const int nh = blockIdx.x, n = nh / H, h = nh % H, D = H * DH;
     const int Lp = (L + 15) & ~15, nkb = Lp / 16;
     // rows at or past the extent: masked keys, and queries whose dO is zero
     // (nothing reads them): zero-filled instead of loaded
     const int ext = extent ? min(extent[n], L) : L;
+    // sequences the tcgen05 backward took (extent <= skip_ext_le)
+    if (ext <= skip_ext_le) return;
     bf16* Qs = (bf16*)smraw;
     bf16* Ks = Qs + Lp * RS;
     bf16* Vs = Ks + Lp * RS;
@@ -868,24 +871,31 @@ __global__ void __launch_bounds__(512) k_attn_row0_bwd(
 
 }  // namespace
 
-// attention implementation for bf16 operands: 0 = mma.sync (default),
-// 1 = tcgen05 / TMEM; set by ptcg_set_attention_impl or, at load, by
-// PTCG_ATTN_TC=1
+// attention implementation for bf16 operands: 0 = mma.sync both passes,
+// 1 = tcgen05 / TMEM both passes, 2 = tcgen05 backward with the mma.sync
+// forward; set by ptcg_set_attention_impl or, at load, by PTCG_ATTN_TC
+#ifndef ATTN_IMPL_DEFAULT
+#define ATTN_IMPL_DEFAULT 0
+#endif
 static std::atomic<int> g_attn_impl{-1};
 
-bool attn_tc_enabled() {
+static int attn_impl() {
     int v = g_attn_impl.load();
     if (v < 0) {
         const char* e = getenv("PTCG_ATTN_TC");
-        v = (e && e[0] == '1') ? 1 : 0;
+        v = (e && (e[0] == '0' || e[0] == '1' || e[0] == '2') && !e[1]) ? e[0] - '0'
+                                                                         : ATTN_IMPL_DEFAULT;
         int expect = -1;
         g_attn_impl.compare_exchange_strong(expect, v);
         v = g_attn_impl.load();
     }
-    return v == 1;
+    return v;
 }
+bool attn_tc_fwd() { return attn_impl() == 1; }
+int attn_get_impl() { return attn_impl(); }
+bool attn_tc_bwd() { return attn_impl() != 0; }
 
-void attn_set_impl(int impl) { g_attn_impl.store(impl == 1 ? 1 : 0); }
+void attn_set_impl(int impl) { g_attn_impl.store(impl >= 0 && impl <= 2 ? impl : 0); }
 
 namespace {
 
@@ -908,9 +918,26 @@ void set_smem(K k, size_t bytes) {
 
 }  // namespace
 
+// run fn(key words): the caller's, or, for callers without them (the
+// attention test entries), words built in stream-ordered scratch
+template <class F>
+static bool with_key_words(const uint32_t* kw, const uint8_t* keep, const int* extent, int nseq,
+                           int L, cudaStream_t s, F fn) {
+    if (kw) return fn(kw);
+    uint32_t* tmp = nullptr;
+    if (cudaMallocAsync((void**)&tmp, (size_t)nseq * ATTN_KW_WORDS * 4, s) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    attn_keep_words(tmp, keep, extent, nseq, L, s);
+    const bool done = fn(tmp);
+    cudaFreeAsync(tmp, s);
+    return done;
+}
+
 void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
               void* out, long ldo, float* lse, int nseq, int L, int H, cudaStream_t s,
-              const int* extent) {
+              const int* extent, const uint32_t* kw) {
     if (nseq <= 0) return;
     size_t sm = fwd_smem(L);
     if (dtype == DT_F32) {
@@ -920,8 +947,9 @@ void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
     } else {
         // tcgen05 / TMEM path first; the mma.sync kernel serves shapes it
         // does not take and runs when PTCG_ATTN_TC=0
-        if (attn_tc_enabled() &&
-            attn_fwd_tc(qkv, ldqkv, keep, out, ldo, lse, nseq, L, H, s, extent))
+        if (attn_tc_fwd() && with_key_words(kw, keep, extent, nseq, L, s, [&](const uint32_t* w) {
+                return attn_fwd_tc(qkv, ldqkv, w, out, ldo, lse, nseq, L, H, s);
+            }))
             return;
         size_t sm2 = fwd_mma_smem(L);
         set_smem(k_attn_fwd_mma, sm2);
@@ -970,18 +998,31 @@ void attn_row0_bwd(int dtype, const void* q, long ldq, const void* kv, long ldkv
 void attn_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
               const void* out, long ldo, const void* dout, long lddo,
               const float* lse, void* dqkv, long lddqkv, float* dbias, int nseq, int L, int H,
-              cudaStream_t s, const int* extent) {
+              cudaStream_t s, const int* extent, const uint32_t* kw) {
     if (nseq <= 0) return;
     size_t sm = bwd_smem(L);
     if (dtype == DT_F32) {
         set_smem(k_attn_bwd<float>, sm);
         ++g_ptcg_launches, k_attn_bwd<float><<<nseq * H, NW * 32, sm, s>>>((const float*)qkv, ldqkv, keep,
             (const float*)out, ldo, (const float*)dout, lddo, lse, (float*)dqkv, lddqkv, dbias, L, H);
-    } else {
-        size_t sm2 = bwd_mma_smem(L);
-        set_smem(k_attn_bwd_mma, sm2);
-        ++g_ptcg_launches, k_attn_bwd_mma<<<nseq * H, 128, sm2, s>>>((const bf16*)qkv, ldqkv, keep,
-            (const bf16*)out, ldo, (const bf16*)dout, lddo, lse, (bf16*)dqkv, lddqkv, dbias, L, H,
-            extent);
+        return;
     }
+    // tcgen05 backward for the sequences whose extent fits one 128-row
+    // tile; the mma.sync kernel takes the rest (all of them without it)
+    int skip = 0;
+    if (attn_tc_bwd()) {
+        const bool done = with_key_words(kw, keep, extent, nseq, L, s, [&](const uint32_t* w) {
+            return attn_bwd_tc(qkv, ldqkv, w, out, ldo, dout, lddo, lse, dqkv, lddqkv, dbias, nseq,
+                               L, H, s);
+        });
+        if (done) {
+            if (L <= 128) return;
+            skip = 128;
+        }
+    }
+    size_t sm2 = bwd_mma_smem(L);
+    set_smem(k_attn_bwd_mma, sm2);
+    ++g_ptcg_launches, k_attn_bwd_mma<<<nseq * H, 128, sm2, s>>>((const bf16*)qkv, ldqkv, keep,
+        (const bf16*)out, ldo, (const bf16*)dout, lddo, lse, (bf16*)dqkv, lddqkv, dbias, L, H,
+        extent, skip);
 }

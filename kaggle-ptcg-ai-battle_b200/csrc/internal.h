@@ -58,12 +58,19 @@ int tc_num_sms();
 int ptcg_tc_error_read_reset();
 int ptcg_tc_profile_ctl(int enable, unsigned long long* out8);
 
+// per-sequence key words of the tcgen05 attention: word j < 15 holds the
+// kept bits of keys 32j .. 32j+31 (none at or past the extent), word 15 the
+// extent; ATTN_KW_WORDS uint32 per sequence, rows 64-byte aligned
+constexpr int ATTN_KW_WORDS = 16;
+
 // attention over packed qkv rows: qkv [(n*L + l) * ldqkv + {0,D,2D} + h*32 + d]
 // extent (nullable, bf16 path): per sequence, the rows anything reads;
-// query rows at or past it get zero output and a zero log-sum-exp
+// query rows at or past it get zero output and a zero log-sum-exp.
+// kw (nullable): the key words of (keep, extent), which the tcgen05 path
+// otherwise builds itself
 void attn_fwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
               void* out, long ldo, float* lse, int nseq, int L, int H,
-              cudaStream_t s, const int* extent = nullptr);
+              cudaStream_t s, const int* extent = nullptr, const uint32_t* kw = nullptr);
 // first query row of each sequence only: q row of sequence n at
 // q + n * ldq, keys / values as rows [K | V] of kv (row stride ldkv,
 // sequence n at rows n * L ..); out / dout [n * ldo + h*32 + d], lse
@@ -78,19 +85,31 @@ void attn_row0_bwd(int dtype, const void* q, long ldq, const void* kv, long ldkv
                    int nseq, int L, int H, cudaStream_t s);
 // tcgen05 / TMEM attention (attention_tc.cu), bf16 operands: false when the
 // shape or alignment is not supported (the caller runs the mma.sync kernels)
-bool attn_fwd_tc(const void* qkv, long ldqkv, const uint8_t* keep, void* out, long ldo,
-                 float* lse, int nseq, int L, int H, cudaStream_t s, const int* extent);
-// whether bf16 attention runs the tcgen05 kernels (attn_set_impl(1), or
-// PTCG_ATTN_TC=1 at load) instead of the mma.sync ones
-bool attn_tc_enabled();
+bool attn_fwd_tc(const void* qkv, long ldqkv, const uint32_t* kw, void* out, long ldo,
+                 float* lse, int nseq, int L, int H, cudaStream_t s);
+// backward of the sequences whose extent is at most 128 rows (one tile);
+// their rows past 128 get zero dqkv; the caller runs the mma.sync backward
+// for the others
+bool attn_bwd_tc(const void* qkv, long ldqkv, const uint32_t* kw, const void* out, long ldo,
+                 const void* dout, long lddo, const float* lse, void* dqkv, long lddqkv,
+                 float* dbias, int nseq, int L, int H, cudaStream_t s);
+// the key words of (keep, extent) (extent nullable: every row) into kw
+void attn_keep_words(uint32_t* kw, const uint8_t* keep, const int* extent, int nseq, int L,
+                     cudaStream_t s);
+// which bf16 attention passes run the tcgen05 kernels instead of the
+// mma.sync ones: impl 0 none, 1 both, 2 the backward only (attn_set_impl,
+// or PTCG_ATTN_TC=<impl> at load)
+bool attn_tc_fwd();
+bool attn_tc_bwd();
 void attn_set_impl(int impl);
+int attn_get_impl();
 // first error code recorded by a tcgen05 attention kernel since the last call
 int attn_tc_error_read_reset();
 // dbias (nullable, 3*H*32 floats): += column sums of dqkv in fp32
 void attn_bwd(int dtype, const void* qkv, long ldqkv, const uint8_t* keep,
               const void* out, long ldo, const void* dout, long lddo,
               const float* lse, void* dqkv, long lddqkv, float* dbias, int nseq, int L,
-              int H, cudaStream_t s, const int* extent = nullptr);
+              int H, cudaStream_t s, const int* extent = nullptr, const uint32_t* kw = nullptr);
 
 // ---- native data-parallel exchange (dp_nccl.cu); every int function
 // returns 0 on success, else nonzero with the text in dp_last_error()

@@ -427,12 +427,22 @@ __global__ void k_x0_readout(float* x0, uint8_t* keep, const float* readout,
 // gathers of ln_f rows).  Rows past it are read by nothing (masked as keys,
 // never gathered), so the attention forward may skip them.  One warp per
 // sequence.
-__global__ void k_row_extent(int* ext, const uint8_t* keep, const float* obs, ObsLayout L, int R) {
+// kw (nullable): also the key words of the tcgen05 attention, ATTN_KW_WORDS
+// per sequence: bits of the kept keys 32j.. in word j, the extent in the last
+// (no key at or past the extent is kept, so the bits need no clipping)
+__global__ void k_row_extent(int* ext, const uint8_t* keep, const float* obs, ObsLayout L, int R,
+                             uint32_t* kw) {
     const int n = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (n >= R) return;
     int e = 0;
-    for (int l = lane; l < L.lseq; l += 32)
-        if (keep[(long)n * L.lseq + l]) e = max(e, l);
+    uint32_t word = 0;
+    for (int j = 0; j * 32 < L.lseq; j++) {
+        const int l = 32 * j + lane;
+        const bool k = l < L.lseq && keep[(long)n * L.lseq + l];
+        if (k) e = max(e, l);
+        const uint32_t b = __ballot_sync(0xffffffffu, k);
+        if (lane == j) word = b;
+    }
     const float* oi = obs + (long)n * L.obs + L.opti;
     for (int j = lane; j < L.nopt; j += 32) {
         const int p1 = (int)oi[j * 6 + 1], p2 = (int)oi[j * 6 + 2];
@@ -442,6 +452,8 @@ __global__ void k_row_extent(int* ext, const uint8_t* keep, const float* obs, Ob
     #pragma unroll
     for (int o = 16; o > 0; o >>= 1) e = max(e, __shfl_xor_sync(0xffffffffu, e, o));
     if (lane == 0) ext[n] = e + 1;
+    if (kw && lane < ATTN_KW_WORDS)
+        kw[(long)n * ATTN_KW_WORDS + lane] = lane == ATTN_KW_WORDS - 1 ? (uint32_t)(e + 1) : word;
 }
 
 // decision-encoder input (696): [sel8, ctx32, cv_eff, cv_ctx, av_my, av_opp,

@@ -141,6 +141,7 @@ struct Work {
     float *u, *rgd, *wqq, *du, *drgd;   // score1 split: per-sample term, inputs, packed W
     void* otokin; float* xc[2]; BlkAct cblk;
     int* ext;                                 // [R] trunk rows anything reads (k_row_extent)
+    uint32_t* kw;                             // [R][ATTN_KW_WORDS] attention key words
     float *ovin, *ov1pre, *ov1; float* out;
     // train-only heads
     float *bvin; void* bvinc; float *bv1pre, *bv1, *blind_v, *hand_lin, *prize_logit;
@@ -449,6 +450,7 @@ static void plan_work(Work& W, Bump& m, int R, bool train, const Dims& z, int es
     W.tokcat = m.take(NT * rup(z.TOK_IN, 8) * esz);
     W.keep = (uint8_t*)m.take(NS);
     W.ext = (int*)m.take((long)R * sizeof(int));
+    W.kw = (uint32_t*)m.take((long)R * ATTN_KW_WORDS * sizeof(uint32_t));
     W.ckeep = (uint8_t*)m.take(NC);
     W.g1pre = m.f((long)R * 128); W.g1 = m.f((long)R * 128);
     W.gd = m.f((long)R * 192);
@@ -587,7 +589,8 @@ static void tables_fwd(PtcgModel* M, Tab& t, cudaStream_t s) {
 
 // ext (nullable): per sequence, the rows anything reads (k_row_extent)
 static void block_fwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* keep, int R, int L,
-                      bool train, cudaStream_t s, const int* ext = nullptr) {
+                      bool train, cudaStream_t s, const int* ext = nullptr,
+                      const uint32_t* kw = nullptr) {
     const Dims& z = M->z;
     const int dt = M->dt(), D = z.D;
     const int NL = R * L;
@@ -595,7 +598,7 @@ static void block_fwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
     GemmArgs a = lin_fwd(dt, NL, D, 3 * D, b.ln1, D, P.qkvw, b.qkv, 3 * D, dt);
     a.bias = P.qkvb.p;
     gemm(M, a, s);
-    attn_fwd(dt, b.qkv, 3 * D, keep, b.att, D, b.lse, R, L, z.H, s, ext);
+    attn_fwd(dt, b.qkv, 3 * D, keep, b.att, D, b.lse, R, L, z.H, s, ext, kw);
     a = lin_fwd(dt, NL, D, D, b.att, D, P.projw, b.xm, D, DT_F32);
     a.bias = P.projb.p; a.resid = b.x_in; a.ld_resid = D;
     gemm(M, a, s);
@@ -692,7 +695,7 @@ static int forward_impl(PtcgModel* M, Work& Wk, Tab& t, const float* obs, int R,
     long ldtok = rup(z.TOK_IN, 8);
     ++g_ptcg_launches, k_x0_readout<<<cdiv((long)R * (z.LSEQ > D ? z.LSEQ : D), TPB), TPB, 0, s>>>(Wk.x[0], Wk.keep,
         M->w("readout").p, obs, ol, R, D);
-    ++g_ptcg_launches, k_row_extent<<<cdiv(R, TPB / 32), TPB, 0, s>>>(Wk.ext, Wk.keep, obs, ol, R);
+    ++g_ptcg_launches, k_row_extent<<<cdiv(R, TPB / 32), TPB, 0, s>>>(Wk.ext, Wk.keep, obs, ol, R, Wk.kw);
     if (dt == DT_F32)
         ++g_ptcg_launches, k_tok_cat<float><<<cdiv((long)R * z.LTOK, TPB / 32), TPB, 0, s>>>((float*)Wk.tokcat, ldtok, obs, ol, t.card_vec,
             M->w("zone_emb").p, M->w("owner_emb").p, R, z.TOK_IN, Wk.ext);
@@ -730,7 +733,8 @@ static int forward_impl(PtcgModel* M, Work& Wk, Tab& t, const float* obs, int R,
         BlkAct& b = train ? Wk.blk[i] : Wk.blk[0];
         b.x_in = train ? Wk.x[i] : Wk.x[i % 2];
         b.x_out = train ? Wk.x[i + 1] : Wk.x[(i + 1) % 2];
-        block_fwd(M, M->blk("b" + std::to_string(i) + "_"), b, Wk.keep, R, z.LSEQ, train, s, Wk.ext);
+        block_fwd(M, M->blk("b" + std::to_string(i) + "_"), b, Wk.keep, R, z.LSEQ, train, s, Wk.ext,
+                  Wk.kw);
         xl = b.x_out;
     }
     ln_fwd(DT_F32, Wk.h, D, Wk.muf, Wk.rsf, xl, D, M->w("lnf_w").p, M->w("lnf_b").p, R * z.LSEQ, D, s,
@@ -908,7 +912,7 @@ static void block_bwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
     gemm(M, lin_dx(dt, NL, D, D, dxc, D, P.projw, Wk.datt, D, dt), s);
     // attention
     attn_bwd(dt, b.qkv, 3 * D, keep, b.att, D, Wk.datt, D, b.lse, Wk.dqkv, 3 * D, P.qkvb.g,
-             R, L, z.H, s, Wk.ext);
+             R, L, z.H, s, Wk.ext, Wk.kw);
     // QKV
     gemm(M, lin_dw(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, b.ln1, D, P.qkvw.g), s);
     gemm(M, lin_dx(dt, NL, D, 3 * D, Wk.dqkv, 3 * D, P.qkvw, Wk.dln, D, dt), s);
@@ -2448,10 +2452,12 @@ int ptcg_tc_profile(int enable, unsigned long long* counters) {
 int ptcg_tensor_cores(void) { return gemm_tc_available() ? 1 : 0; }
 
 int ptcg_set_attention_impl(int impl) {
-    REQ(impl == 0 || impl == 1, PTCG_EINVAL, "attention implementation must be 0 or 1");
+    REQ(impl >= 0 && impl <= 2, PTCG_EINVAL, "attention implementation must be 0, 1 or 2");
     attn_set_impl(impl);
     return PTCG_OK;
 }
+
+int ptcg_get_attention_impl(void) { return attn_get_impl(); }
 
 int ptcg_device_error(void) {
     const int g = ptcg_tc_error_read_reset(), a = attn_tc_error_read_reset();

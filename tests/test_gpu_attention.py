@@ -13,14 +13,19 @@ def _p(t):
     return C.c_void_p(t.data_ptr()) if t is not None else None
 
 
-@pytest.fixture(params=["mma", "tc"])
+IMPL = {"mma": 0, "tc": 1, "tc_bwd": 2}
+
+
+@pytest.fixture(params=["mma", "tc", "tc_bwd"])
 def attn_impl(request, pkg):
-    """bf16 attention kernels under test: mma.sync or tcgen05 / TMEM."""
+    """bf16 attention kernels under test: mma.sync, tcgen05 / TMEM for both
+    passes, or the tcgen05 backward after the mma.sync forward."""
     import ptcg_b200.native as n
     lib = n.lib()
-    assert lib.ptcg_set_attention_impl(1 if request.param == "tc" else 0) == 0
+    old = lib.ptcg_get_attention_impl()
+    assert lib.ptcg_set_attention_impl(IMPL[request.param]) == 0
     yield request.param
-    lib.ptcg_set_attention_impl(0)
+    lib.ptcg_set_attention_impl(old)
 
 
 @pytest.mark.parametrize("dtype", ["fp32", "bf16"])
@@ -28,7 +33,7 @@ def attn_impl(request, pkg):
 def test_attention_matches_sdpa(pkg, dtype, L, H, attn_impl):
     import ptcg_b200.native as n
     lib = n.lib()
-    if dtype == "fp32" and attn_impl == "tc":
+    if dtype == "fp32" and attn_impl != "mma":
         pytest.skip("the tcgen05 kernels take bf16 operands")
     torch.manual_seed(L * 10 + H)
     nseq, D = 5, H * 32
@@ -135,12 +140,13 @@ def test_model_forward_with_tc_attention(pkg, oracle, preset):
     blob = pkg.synth.make_weights(s, 21)
     obs = pkg.synth.make_obs(s, nrows, 3, edge=True)
     pol = pkg.PTCGPolicy(s, precision="bf16", tables=tabs, weights=blob, rollout_rows=nrows)
+    old = lib.ptcg_get_attention_impl()
     assert lib.ptcg_set_attention_impl(1) == 0
     try:
         out = pol.forward(obs).cpu().numpy()
         assert lib.ptcg_device_error() == 0
     finally:
-        lib.ptcg_set_attention_impl(0)
+        lib.ptcg_set_attention_impl(old)
     P = oracle.params_from_blob(blob, s)
     T = oracle.tables_to_torch(tabs)
     with torch.no_grad():
@@ -150,3 +156,81 @@ def test_model_forward_with_tc_attention(pkg, oracle, preset):
     rel = lambda x, y: float(np.linalg.norm(x - y) / np.linalg.norm(y))
     assert rel(out[:, :-1][legal], sc.numpy()[legal]) <= 2e-2
     assert rel(out[:, -1], v.numpy()) <= 2e-2
+
+
+@pytest.mark.parametrize("preset", ["small", "c0", "default", "c4"])
+def test_train_grads_with_tc_backward(pkg, oracle, preset):
+    """bf16 gradients of forward_train -> PPO loss -> backward with the
+    tcgen05 attention backward (sequences whose extent fits one 128-row tile;
+    longer ones, e.g. the edge rows, through the mma.sync backward) against
+    the CPU oracle, and against the same step with the mma.sync backward."""
+    import numpy as np
+    import ptcg_b200.native as n
+    from test_gpu_parity import ROWS, TOL, _rollout_tensors, make, oracle_fwd, rel
+    lib = n.lib()
+    torch.set_float32_matmul_precision("highest")
+    rows = ROWS[preset]
+    s, tabs, blob, obs, pol = make(pkg, preset, "bf16", rows)
+    sc, v = oracle_fwd(oracle, s, tabs, blob, obs)
+    mask, act, old_lp, adv, ret, val = _rollout_tensors(pkg, oracle, s, obs, sc, 5)
+    prio = np.ones(1, np.float32)
+    old = lib.ptcg_get_attention_impl()
+    grads = {}
+    try:
+        for impl in (0, 2):
+            assert lib.ptcg_set_attention_impl(impl) == 0
+            out = pol.forward_train(obs)
+            grad, _, _, _ = pol.ppo_loss(out, mask, act, old_lp, adv, val, ret, prio, 1, rows)
+            pol.backward(grad, ret)
+            grads[impl] = pol.grads_packed()
+            assert lib.ptcg_device_error() == 0
+    finally:
+        lib.ptcg_set_attention_impl(old)
+    P = oracle.params_from_blob(blob, s, requires_grad=True)
+    T = oracle.tables_to_torch(tabs)
+    _, _, og = oracle.train_grads(P, T, obs, s, act, old_lp, adv, val, ret, prio, 1, rows)
+    ref = np.concatenate([og[name].detach().numpy().ravel() for name, _ in pkg.config.param_table(s)])
+    g2 = grads[2][:ref.size]
+    assert np.isfinite(g2).all()
+    assert rel(g2, ref) <= TOL["bf16"], rel(g2, ref)
+    assert rel(g2, grads[0][:ref.size]) <= TOL["bf16"], rel(g2, grads[0][:ref.size])
+
+
+def test_tc_backward_matches_mma_backward_many_rows(pkg):
+    """The PPO step's gradients at c0 over 512 synthetic rows (every extent
+    the generator draws, padded and full sequences) with the tcgen05
+    backward against the mma.sync backward, same forward."""
+    import numpy as np
+    import ptcg_b200.native as n
+    from test_gpu_parity import rel
+    lib = n.lib()
+    s = pkg.config.PRESETS["c0"]
+    n_seg, horizon = 8, 64
+    nt = n_seg * horizon
+    tabs = pkg.synth.make_tables(s, 11)
+    blob = pkg.synth.make_weights(s, 21)
+    obs = pkg.synth.make_obs_batch(s, nt, 5)
+    a, b = s.offsets["opt_mask"]
+    act = pkg.synth.sample_legal(obs[:, a:b], 3)
+    rng = np.random.default_rng(4)
+    old_lp = rng.normal(-2.0, 0.5, nt).astype(np.float32)
+    adv = rng.standard_normal(nt).astype(np.float32)
+    ret = rng.standard_normal(nt).astype(np.float32)
+    val = (0.1 * rng.standard_normal(nt)).astype(np.float32)
+    prio = np.ones(n_seg, np.float32)
+    pol = pkg.PTCGPolicy(s, precision="bf16", tables=tabs, weights=blob, train_rows=256)
+    old = lib.ptcg_get_attention_impl()
+    res = {}
+    try:
+        for impl in (0, 2):
+            assert lib.ptcg_set_attention_impl(impl) == 0
+            st = pol.train_step(obs, act, old_lp, adv, val, ret, prio, n_seg, horizon,
+                                skip_adam=True).cpu().numpy()
+            res[impl] = (st, pol.grads_packed())
+            assert lib.ptcg_device_error() == 0
+    finally:
+        lib.ptcg_set_attention_impl(old)
+    (s0, g0), (s2, g2) = res[0], res[2]
+    assert np.isfinite(g2).all()
+    assert rel(g2, g0) <= 1e-2, rel(g2, g0)
+    np.testing.assert_allclose(s2[:8], s0[:8], rtol=1e-3, atol=1e-5)
