@@ -110,11 +110,17 @@ def test_native_exchange_equals_python_sharded_adam(tmp_path, preset, prec):
     mp.start_processes(_worker, args=(world, _port(), str(tmp_path), preset, prec), nprocs=world,
                        join=True, start_method="spawn")
     z = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
+    # fp32: the two exchanges agree to rounding.  bf16: the backward's
+    # split-K atomics sum in a different order on each run, and Adam's first
+    # steps turn a noise-level difference of a near-zero gradient into a
+    # full +-lr step (update = lr * m / sqrt(v)), so the whole-vector bound
+    # is looser; the loss stats and gradient norm below stay tight
+    tol = 1e-5 if prec == "fp32" else 2e-4
     for r in range(world):
         wn, wp = z[r]["native_w"], z[r]["python_w"]
         for k in range(STEPS):
             d = np.linalg.norm(wn[k] - wp[k]) / np.linalg.norm(wp[k])
-            assert d <= 1e-5, (r, k, d)
+            assert d <= tol, (r, k, d)
         # loss stats and {grad norm, applied}: same minibatch, same exchange
         np.testing.assert_allclose(z[r]["native_st"][:, :10], z[r]["python_st"][:, :10],
                                    rtol=1e-4, atol=1e-6)
