@@ -204,6 +204,10 @@ struct PtcgModel {
           *att_text = nullptr, *skill_text = nullptr;
     int *card_attacks = nullptr, *card_skills = nullptr;
     bool tables_ready = false, weights_ready = false;
+    // tab holds the static-table activations of the current weights: every
+    // call that changes the master weights (optimizer steps, loads, imports,
+    // ptcg_refresh_copies) recomputes them, so forwards skip that work
+    bool tab_fresh = false;
     Tab tab;
     void* tab_base = nullptr;
     Work roll, trn;
@@ -1538,6 +1542,8 @@ int ptcg_destroy(PtcgModel* M) {
     return PTCG_OK;
 }
 
+static void refresh_tables(PtcgModel* M, cudaStream_t s);
+
 int ptcg_set_tables(PtcgModel* M, const float* card_static, const int* card_attacks,
                     const int* card_skills, const float* att_static, const float* card_text,
                     const float* att_text, const float* skill_text) {
@@ -1562,13 +1568,32 @@ int ptcg_set_tables(PtcgModel* M, const float* card_static, const int* card_atta
     UP(skill_text, skill_text, (long)z.NS * 64, float);
 #undef UP
     M->tables_ready = true;
+    M->tab_fresh = false;
+    if (M->weights_ready) {
+        refresh_tables(M, 0);
+        CKL();
+        CK(cudaDeviceSynchronize());
+    }
     return PTCG_OK;
 }
 
+// The static-table activations (tables_fwd) of the current master weights,
+// into M->tab.  Batch-independent: recomputed when the weights change, not
+// per forward.
+static void refresh_tables(PtcgModel* M, cudaStream_t s) {
+    if (!M->tables_ready) { M->tab_fresh = false; return; }
+    tables_fwd(M, M->tab, s);
+    M->tab_fresh = true;
+}
+
+// After the master weights changed: the bf16 compute copies and the table
+// activations
 static int refresh_copies(PtcgModel* M, cudaStream_t s) {
-    if (M->copies.empty()) return PTCG_OK;
-    dim3 g(64, (unsigned)M->copies.size());
-    ++g_ptcg_launches, k_refresh_copies<<<g, 256, 0, s>>>(M->params, M->d_copies, (int)M->copies.size());
+    if (!M->copies.empty()) {
+        dim3 g(64, (unsigned)M->copies.size());
+        ++g_ptcg_launches, k_refresh_copies<<<g, 256, 0, s>>>(M->params, M->d_copies, (int)M->copies.size());
+    }
+    refresh_tables(M, s);
     CKL();
     return PTCG_OK;
 }
@@ -1808,7 +1833,8 @@ int ptcg_forward(PtcgModel* M, const float* obs, int n, float* out, void* stream
         M->roll.R);
     if (n == 0) return PTCG_OK;
     CK(cudaSetDevice(M->dev));
-    forward_impl(M, M->roll, M->tab, obs, n, out, false, true, (cudaStream_t)stream);
+    forward_impl(M, M->roll, M->tab, obs, n, out, false, !M->tab_fresh, (cudaStream_t)stream);
+    M->tab_fresh = true;
     CKL();
     return PTCG_OK;
 }
@@ -1826,7 +1852,8 @@ int ptcg_forward_sample(PtcgModel* M, const float* obs, int n, const float* mask
     if (n == 0) return PTCG_OK;
     CK(cudaSetDevice(M->dev));
     SampleArgs sa{mask, mask_stride, uniforms, actions, logprobs, values};
-    forward_impl(M, M->roll, M->tab, obs, n, out, false, true, (cudaStream_t)stream, &sa);
+    forward_impl(M, M->roll, M->tab, obs, n, out, false, !M->tab_fresh, (cudaStream_t)stream, &sa);
+    M->tab_fresh = true;
     CKL();
     return PTCG_OK;
 }
@@ -1837,7 +1864,8 @@ int ptcg_forward_train(PtcgModel* M, const float* obs, int n, float* out, void* 
     REQ(obs && out && n > 0, PTCG_EINVAL, "bad arguments");
     REQ(M->trn.base && n <= M->trn.R, PTCG_ERANGE, "train batch %d exceeds reserved %d", n, M->trn.R);
     CK(cudaSetDevice(M->dev));
-    forward_impl(M, M->trn, M->tab, obs, n, out, true, true, (cudaStream_t)stream);
+    forward_impl(M, M->trn, M->tab, obs, n, out, true, !M->tab_fresh, (cudaStream_t)stream);
+    M->tab_fresh = true;
     M->trn_last_obs = obs; M->trn_last_n = n;
     CKL();
     return PTCG_OK;
@@ -2076,6 +2104,7 @@ static int adam_impl(PtcgModel* M, float lr, float b1, float b2, float eps, floa
         M->d_copies, (int)M->copies.size(), M->d_chunk_copy, M->adam_chunk);
     ++g_ptcg_launches, k_step_inc<<<1, 1, 0, s>>>(M->step_dev, st);
     clear_work_if_nonfinite(M, st, s);
+    refresh_tables(M, s);                   // k_adam refreshed the bf16 copies itself
     CKL();
     return PTCG_OK;
 }
@@ -2106,6 +2135,7 @@ int ptcg_adam_segments(PtcgModel* M, const float* grad_src, const long* seg, int
     }
     ++g_ptcg_launches, k_step_inc<<<1, 1, 0, s>>>(M->step_dev, st);
     clear_work_if_nonfinite(M, st, s);
+    M->tab_fresh = false;                   // the caller gathers, then ptcg_refresh_copies
     CKL();
     return PTCG_OK;
 }
@@ -2320,7 +2350,7 @@ int ptcg_train_step(PtcgModel* M, const float* obs, const float* actions, const 
     ++g_ptcg_launches, k_count_unseen<<<128, 256, 0, s>>>(cnt, obs, z.ol, nt);
     CK(cudaMemsetAsync(M->grads, 0, (size_t)M->n_arena * 4, s));
     zero_table_grads(M, s);
-    tables_fwd(M, M->tab, s);
+    if (!M->tab_fresh) refresh_tables(M, s);
     int nmb = (nt + R - 1) / R;
     for (int mb = 0; mb < nmb; mb++) {
         int r0 = mb * R, rows = nt - r0 < R ? nt - r0 : R;
@@ -2350,6 +2380,7 @@ int ptcg_arena(PtcgModel* M, int which, float** ptr, long* n_floats) {
     REQ(M && ptr && n_floats, PTCG_EINVAL, "null argument");
     float* p[] = {M->params, M->grads, M->am, M->av};
     REQ(which >= 0 && which < 4, PTCG_EINVAL, "bad arena %d", which);
+    if (which == 0) M->tab_fresh = false;   // the caller may write the weights
     *ptr = p[which];
     *n_floats = M->n_arena;
     return PTCG_OK;

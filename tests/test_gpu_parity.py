@@ -425,3 +425,30 @@ def test_forward_sample_equals_forward_then_sample(pkg, oracle, prec, preset):
     oact, ologp, margin = oracle.sample_logits(out2[:, :-1].cpu().numpy(), m, u)
     ok = margin > 1e-5
     assert np.array_equal(act3.cpu().numpy()[ok].astype(np.int64), oact[ok])
+
+
+def test_table_activations_follow_weight_changes(pkg):
+    """The static-table activations are computed once per weight version,
+    not per forward: after an optimizer step, and after a direct write to
+    the master weights followed by refresh_copies, the rollout forward must
+    equal a fresh model's forward on the same weights."""
+    s, tabs, blob, obs, pol = make(pkg, "small", "fp32", 6)
+    rng = np.random.default_rng(2)
+    pol.forward(obs)                                   # tables computed here or at load
+    a, b = s.offsets["opt_mask"]
+    act = np.array([rng.choice(np.nonzero(m)[0]) for m in obs[:, a:b]], np.float32)
+    z = lambda: rng.standard_normal(6).astype(np.float32)
+    pol.train_step(obs, act, z() - 2, z(), 0.1 * z(), z(), np.ones(1, np.float32), 1, 6, lr=1e-2)
+
+    def fresh_forward():
+        ref = pkg.PTCGPolicy(s, precision="fp32", tables=tabs, weights=pol.save_weights(),
+                             rollout_rows=6)
+        out = ref.forward(obs).cpu().numpy()
+        ref.close()
+        return out
+
+    np.testing.assert_allclose(pol.forward(obs).cpu().numpy(), fresh_forward(), rtol=1e-6, atol=1e-7)
+    w = pol.arena(0)
+    w.mul_(0.9)
+    pol.refresh_copies()
+    np.testing.assert_allclose(pol.forward(obs).cpu().numpy(), fresh_forward(), rtol=1e-6, atol=1e-7)
