@@ -267,8 +267,9 @@ int ptcg_adam_step(PtcgModel* m, float lr, float beta1, float beta2, float eps,
  *    grad_src, length} in floats, with gradients read from grad_src and the
  *    clip taken from the global sum of squares sumsq[0] (device double).  It
  *    does not refresh the bf16 compute copies;
- *  - ptcg_refresh_copies: refresh every bf16 compute copy from the master
- *    weights (after the updated segments of all ranks are gathered). */
+ *  - ptcg_refresh_copies: refresh every bf16 compute copy, and the
+ *    static-table activations, from the master weights (after the updated
+ *    segments of all ranks are gathered, or after any other write to them). */
 int ptcg_sumsq(PtcgModel* m, const float* x, long n, double* out, void* stream);
 int ptcg_adam_segments(PtcgModel* m, const float* grad_src, const long* seg, int nseg,
                        const double* sumsq, float lr, float beta1, float beta2, float eps,
@@ -369,7 +370,11 @@ int ptcg_train_step(PtcgModel* m, const float* obs, const float* actions,
 /* ---- arenas (device memory owned by the model) -------------------------------
  * which: 0 = fp32 master params, 1 = fp32 grads, 2 = Adam m, 3 = Adam v.
  * n_floats includes the 16-byte alignment padding; arena offsets of each
- * parameter come from ptcg_param_offset. */
+ * parameter come from ptcg_param_offset.  The model keeps the static-table
+ * activations (card / attack / skill tables through their MLPs) of the
+ * current weights between forwards, recomputed by every call that changes
+ * the weights; after writing the master weights through this pointer, call
+ * ptcg_refresh_copies. */
 int ptcg_arena(PtcgModel* m, int which, float** ptr, long* n_floats);
 long ptcg_param_offset(PtcgModel* m, int i);
 /* Adam step counter (for checkpoint/resume). */
