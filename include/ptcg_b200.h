@@ -415,9 +415,10 @@ int ptcg_dp_weights_agree(PtcgModel* m, long long* minmax_dev, void* stream);
 int ptcg_dp_finalize(PtcgModel* m, int abort);
 
 /* CUDA-event timing of every launch of one GEMM kernel class (1 = tcgen05
- * tensor-core GEMM, 2 = SIMT GEMM, 0 = off) until the next call; read back
- * total device milliseconds, launch count and algorithmic FLOPs (2*M*N*K per
- * launch).  The reference's analogue is its cudaEvent phase timing
+ * tensor-core GEMM, 2 = SIMT GEMM, 3 = both, 0 = off), or of the optimizer
+ * kernels of each ptcg_adam_step (4: norm and fused Adam, not the table
+ * refresh after them), until the next call; read back total device
+ * milliseconds, launch count and algorithmic FLOPs (2*M*N*K per GEMM launch).  The reference's analogue is its cudaEvent phase timing
  * (ProfileT, native/src/pufferlib.cu:59-63, 1851-1953). */
 int ptcg_kernel_timer(PtcgModel* m, int mode);
 /* Per-launch record of the timed region (mode 3 times every GEMM): for up to

@@ -165,7 +165,8 @@ struct Tab {                            // batch-independent table activations +
 
 // CUDA-event timing of one GEMM kernel class over a region (bench roofline)
 struct KTimer {
-    int mode = 0;                       // 0 off, 1 tensor-core GEMM, 2 SIMT GEMM, 3 all GEMMs
+    int mode = 0;                       // 0 off, 1 tensor-core GEMM, 2 SIMT GEMM, 3 all GEMMs,
+                                        // 4 the Adam kernels of ptcg_adam_step
     std::vector<cudaEvent_t> ev;
     int used = 0;
     double flops = 0.0;
@@ -2098,11 +2099,14 @@ static int adam_impl(PtcgModel* M, float lr, float b1, float b2, float eps, floa
                      const float* gate, float* stats, cudaStream_t s) {
     float* st = stats ? stats : M->d_misc + 32;
     if (M->dp) return dp_adam(M, lr, b1, b2, eps, max_norm, gate, st, s);
+    const bool timed = M->kt.mode == 4;
+    if (timed) kt_mark(M, s);
     ++g_ptcg_launches, k_sumsq<<<M->sumsq_grid, 256, 0, s>>>(M->d_partials, M->grads, M->n_arena);
     ++g_ptcg_launches, k_adam<<<M->adam_grid, 256, 0, s>>>(M->params, M->am, M->av, M->grads, M->n_arena,
         M->d_partials, M->sumsq_grid, lr, b1, b2, eps, max_norm, M->step_dev, gate, st,
         M->d_copies, (int)M->copies.size(), M->d_chunk_copy, M->adam_chunk);
     ++g_ptcg_launches, k_step_inc<<<1, 1, 0, s>>>(M->step_dev, st);
+    if (timed) { kt_mark(M, s); M->kt.launches++; }
     clear_work_if_nonfinite(M, st, s);
     refresh_tables(M, s);                   // k_adam refreshed the bf16 copies itself
     CKL();
@@ -2519,7 +2523,7 @@ int ptcg_gemm(int M, int N, int K, const void* A, long lda, int a_kmajor, const 
 }
 
 int ptcg_kernel_timer(PtcgModel* M, int mode) {
-    REQ(M && mode >= 0 && mode <= 3, PTCG_EINVAL, "bad arguments");
+    REQ(M && mode >= 0 && mode <= 4, PTCG_EINVAL, "bad arguments");
     M->kt.mode = mode; M->kt.used = 0; M->kt.flops = 0; M->kt.bytes = 0; M->kt.launches = 0;
     M->kt.meta.clear();
     return PTCG_OK;

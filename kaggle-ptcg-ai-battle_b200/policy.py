@@ -435,7 +435,8 @@ class PTCGPolicy:
         return stats
 
     def kernel_timer(self, mode):
-        """mode 1 = tcgen05 GEMM, 2 = SIMT GEMM, 0 = off (resets counters)."""
+        """mode 1 = tcgen05 GEMM, 2 = SIMT GEMM, 3 = both, 4 = the optimizer
+        kernels of adam_step, 0 = off (resets counters)."""
         check(self.lib.ptcg_kernel_timer(self.h, int(mode)))
 
     def kernel_timer_read(self):
