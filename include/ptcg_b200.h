@@ -476,7 +476,7 @@ int ptcg_gemm_ex(int M, int N, int K, const void* A, long lda, int a_kmajor, con
 int ptcg_tensor_cores(void);
 /* First error code a bounded device-side wait recorded since the last call
  * (0 = none; the kernel that timed out returned early; 100 + code for the
- * tcgen05 attention).  Resets the flag. */
+ * tcgen05 attention, 200 + code for the fused rollout MLP).  Resets the flag. */
 int ptcg_device_error(void);
 
 /* Kernels of the bf16 attention (no counterpart in the reference, whose
@@ -489,6 +489,15 @@ int ptcg_device_error(void);
  * it at load. */
 int ptcg_set_attention_impl(int impl);
 int ptcg_get_attention_impl(void);
+
+/* The rollout forward (ptcg_forward, ptcg_forward_sample, bf16, d_model 256)
+ * runs each block's FFN1 -> GELU -> FFN2 (+ bias + residual) as one tcgen05
+ * kernel that keeps the hidden activation on chip (on = 1), or as the two
+ * GEMMs of the training forward (on = 0, the default: faster here).  The reference runs
+ * them as two linear layers around a GELU kernel
+ * (native/model/ptcg_model3.cu:36-38).  Process-wide; takes effect at the
+ * next launch. */
+int ptcg_set_fused_mlp(int on);
 int ptcg_kernel_timer_read(PtcgModel* m, double* ms, long* launches, double* flops);
 /* Algorithmic HBM bytes of the launches timed since ptcg_kernel_timer(m, mode)
  * (operands read once, outputs written once; diagnostic, no counterpart in

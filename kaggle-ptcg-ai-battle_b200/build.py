@@ -19,7 +19,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I" + INCLUDE, "-I" + CSRC]
 SOURCES = ["model.cu", "gemm_simt.cu", "gemm_tc.cu", "attention.cu", "attention_tc.cu",
-           "puffer_plugin.cu", "dp_nccl.cu"]
+           "puffer_plugin.cu", "dp_nccl.cu", "mlp_tc.cu"]
 
 
 def _needs(obj, deps):

@@ -471,7 +471,10 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) k_attn_fwd_tc(
         bool ok = true;
         for (int k = w; ok; k += NWG) {
             const int st = k % ns;
-            if (!bar_wait(full0 + 8 * st, (uint32_t)((k / ns) & 1), abort_flag, 3)) break;
+            // warp-uniform outcomes: the tcgen05.ld / wait below are
+            // warp-collective, so no lane may leave while the others load
+            if (!__all_sync(0xffffffffu, bar_wait(full0 + 8 * st, (uint32_t)((k / ns) & 1), abort_flag, 3)))
+                break;
             const uint8_t* sp = smem + (size_t)st * P.stage_bytes;
             const Meta m = read_meta(sp + P.mask_off + MASK_BYTES);
             if (m.n < 0) break;
@@ -480,7 +483,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) k_attn_fwd_tc(
             float mrow = -INFINITY, l = 0.f;
             for (int c = 0; c < nkc && ok; c++) {
                 const int nblk = (chunk_n(m.ext, c) + 31) >> 5;
-                ok = bar_wait(sfull, (uint32_t)(g & 1), abort_flag, 4);
+                ok = __all_sync(0xffffffffu, bar_wait(sfull, (uint32_t)(g & 1), abort_flag, 4));
                 if (!ok) break;
                 tc_fence_after();
                 // pass 1: the chunk's max over kept keys, 64 columns per
@@ -503,7 +506,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) k_attn_fwd_tc(
                 // it): once the previous chunk's PV landed, rescale O from
                 // the previous max to this one; that also frees P
                 if (c > 0) {
-                    ok = bar_wait(pvfull, (uint32_t)((g - 1) & 1), abort_flag, 5);
+                    ok = __all_sync(0xffffffffu, bar_wait(pvfull, (uint32_t)((g - 1) & 1), abort_flag, 5));
                     if (!ok) break;
                     tc_fence_after();
                     float ov[DH];
@@ -563,7 +566,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) k_attn_fwd_tc(
             }
             if (!ok) break;
             // the last chunk's PV
-            ok = bar_wait(pvfull, (uint32_t)((g - 1) & 1), abort_flag, 6);
+            ok = __all_sync(0xffffffffu, bar_wait(pvfull, (uint32_t)((g - 1) & 1), abort_flag, 6));
             if (!ok) break;
             tc_fence_after();
             float o[DH];

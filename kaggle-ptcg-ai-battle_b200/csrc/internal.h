@@ -130,3 +130,11 @@ int dp_allreduce_sum_f64(DpState* d, double* x, cudaStream_t s);
 int dp_gather_params(DpState* d, float* params, cudaStream_t s);
 int dp_weights_agree(DpState* d, const unsigned int* ck_dev, long long* minmax_dev,
                      cudaStream_t s);
+
+// ---- fused rollout MLP (mlp_tc.cu): out = res + b2 + GELU(a W1^T + b1) W2^T on
+// tcgen05 with the hidden activation kept on chip; false when the shape or
+// alignment is not supported (the caller runs the two GEMMs).  D must be 256.
+bool mlp_fwd_tc(const void* a, long lda, const void* w1, long ldw1, const float* b1,
+                const void* w2, long ldw2, const float* b2, const float* res, long ld_res,
+                float* out, long ld_out, int rows, int D, int F, cudaStream_t s);
+int mlp_tc_error_read_reset();

@@ -31,6 +31,9 @@
 #include <unordered_map>
 
 std::atomic<long long> g_ptcg_launches{0};
+// the rollout forward's fused MLP kernel (ptcg_set_fused_mlp; off: slower
+// than the two GEMMs on this part, see mlp_tc.cu)
+static std::atomic<int> g_fused_mlp{0};
 
 // ------------------------------------------------------------------ errors
 static thread_local char g_err[1024];
@@ -608,6 +611,12 @@ static void block_fwd(PtcgModel* M, const BlkW& P, BlkAct& b, const uint8_t* kee
     a.bias = P.projb.p; a.resid = b.x_in; a.ld_resid = D;
     gemm(M, a, s);
     ln_fwd(dt, b.ln2, D, b.mu2, b.rs2, b.xm, D, P.ln2w.p, P.ln2b.p, NL, D, s, ext, L);
+    // rollout: FFN1 -> GELU -> FFN2 in one kernel, the hidden activation on
+    // chip (the backward of a training forward needs it written)
+    if (!train && dt == DT_BF16 && g_fused_mlp.load() &&
+        mlp_fwd_tc(b.ln2, D, P.f1w.op, P.f1w.ld, P.f1b.p, P.f2w.op, P.f2w.ld, P.f2b.p, b.xm, D,
+                   b.x_out, D, NL, D, z.FFN, s))
+        return;
     a = lin_fwd(dt, NL, D, z.FFN, b.ln2, D, P.f1w, b.fpost, z.FFN, dt);
     a.bias = P.f1b.p; a.act = ACT_GELU;
     if (train) { a.out2 = b.fpre; a.ldo2 = z.FFN; a.out2_dtype = dt; }
@@ -2494,9 +2503,15 @@ int ptcg_set_attention_impl(int impl) {
 
 int ptcg_get_attention_impl(void) { return attn_get_impl(); }
 
+int ptcg_set_fused_mlp(int on) {
+    g_fused_mlp.store(on ? 1 : 0);
+    return PTCG_OK;
+}
+
 int ptcg_device_error(void) {
-    const int g = ptcg_tc_error_read_reset(), a = attn_tc_error_read_reset();
-    return g ? g : (a ? 100 + a : 0);
+    const int g = ptcg_tc_error_read_reset(), a = attn_tc_error_read_reset(),
+              m = mlp_tc_error_read_reset();
+    return g ? g : (a ? 100 + a : (m ? 200 + m : 0));
 }
 
 int ptcg_gemm(int M, int N, int K, const void* A, long lda, int a_kmajor, const void* B, long ldb,

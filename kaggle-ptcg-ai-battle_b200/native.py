@@ -101,6 +101,7 @@ _SIGS = {
     "ptcg_device_error": (I, []),
     "ptcg_set_attention_impl": (I, [I]),
     "ptcg_get_attention_impl": (I, []),
+    "ptcg_set_fused_mlp": (I, [I]),
     "ptcg_gemm": (I, [I, I, I, P, L, I, P, L, I, I, P, L, I, I, P]),
     "ptcg_gemm_ex": (I, [I, I, I, P, L, I, P, L, I, I, P, L, I, P, I, P, L, P, L, P, I, I, P]),
     "ptcg_kernel_timer_bytes": (I, [P, C.POINTER(C.c_double)]),
