@@ -34,6 +34,7 @@
 // copies and MMAs land, frees its TMEM and returns.
 #include "common.cuh"
 #include "internal.h"
+#include "tc_ptx.cuh"
 
 #include <algorithm>
 
@@ -47,68 +48,15 @@ constexpr uint32_t TILE_BYTES = 128 * DH * 2;   // one {32 cols, 128 rows} bf16 
 constexpr uint32_t P_BYTES = 2 * 128 * 128;     // P: 128 rows x 128 keys bf16, two 64-key blocks
 constexpr uint32_t MASK_BYTES = ATTN_KW_WORDS * 4;
 constexpr int SMEM_MAX = 227 * 1024;
-constexpr long long WAIT_BUDGET = 4000000000LL; // clock cycles (~2 s)
 constexpr float LOG2E = 1.4426950408889634f;
 
 __device__ int g_attn_tc_error;
 
 // ------------------------------------------------------------ PTX helpers
-PTCG_DEV uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-PTCG_DEV void bar_init(uint32_t b, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(b), "r"(count));
-}
-PTCG_DEV void bar_expect_tx(uint32_t b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(b), "r"(bytes)
-                 : "memory");
-}
-PTCG_DEV void bar_arrive(uint32_t b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(b) : "memory");
-}
-PTCG_DEV bool bar_try(uint32_t b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile("{\n\t.reg .pred P;\n\t"
-                 "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
-                 "selp.u32 %0, 1, 0, P;\n\t}"
-                 : "=r"(ok) : "r"(b), "r"(parity) : "memory");
-    return ok != 0;
-}
-// bounded wait; false once the CTA's abort flag is set (by this wait on
-// expiry, recording `code`, or by another role)
+// (the shared ones in tc_ptx.cuh; the wait records this file's error code)
+using namespace tcx;
 PTCG_DEV bool bar_wait(uint32_t b, uint32_t parity, volatile int* abort_flag, int code) {
-    if (*abort_flag) return false;
-    const long long t0 = clock64();
-    while (!bar_try(b, parity)) {
-        if (*abort_flag) return false;
-        if (clock64() - t0 > WAIT_BUDGET) {
-            *abort_flag = 1;
-            atomicCAS(&g_attn_tc_error, 0, code);
-            return false;
-        }
-    }
-    return true;
-}
-// wait for a barrier phase regardless of the abort flag, still bounded (the
-// exit path: copies already issued must land before the CTA leaves)
-PTCG_DEV void bar_drain(uint32_t b, uint32_t parity) {
-    const long long t0 = clock64();
-    while (!bar_try(b, parity) && clock64() - t0 < WAIT_BUDGET) {}
-}
-PTCG_DEV void tma_2d(uint32_t dst, const CUtensorMap* map, uint32_t b, int x, int y) {
-    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%3, %4}], [%2];"
-                 :: "r"(dst), "l"((uint64_t)map), "r"(b), "r"(x), "r"(y) : "memory");
-}
-PTCG_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-PTCG_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-PTCG_DEV void mma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile("{\n\t.reg .pred p;\n\t"
-                 "setp.ne.b32 p, %4, 0;\n\t"
-                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-                 :: "r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc) : "memory");
-}
-PTCG_DEV void mma_commit_to(uint32_t b) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                 :: "r"(b) : "memory");
+    return tcx::bar_wait(b, parity, abort_flag, &g_attn_tc_error, code);
 }
 PTCG_DEV void tmem_ld32x32(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
@@ -125,30 +73,11 @@ PTCG_DEV void tmem_ld32x32(uint32_t taddr, float (&v)[32]) {
     #pragma unroll
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
-PTCG_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 PTCG_DEV void tmem_st32x32(uint32_t taddr, const float (&v)[32]) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
                  :: "r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31])) : "memory");
 }
 PTCG_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-// UMMA shared-memory descriptor (sm_100): start, leading / stride byte
-// offsets, layout (2 = 128-byte swizzle, 4 = 64-byte swizzle)
-PTCG_DEV uint64_t sdesc(uint32_t a, uint32_t lbo, uint32_t sbo, uint32_t layout) {
-    uint64_t d = 0;
-    d |= (uint64_t)((a >> 4) & 0x3FFF);
-    d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
-    d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-    d |= (uint64_t)1 << 46;
-    d |= (uint64_t)layout << 61;
-    return d;
-}
-// instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B, A / B
-// major-ness (1 = MN-major), N, M = 128
-__host__ __device__ inline uint32_t idesc_bf16(int n, int a_mn, int b_mn) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
-           ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-}
-
 
 // non-blocking probe of a barrier phase (the MMA lane polls several)
 PTCG_DEV bool bar_test(uint32_t b, uint32_t parity) {
