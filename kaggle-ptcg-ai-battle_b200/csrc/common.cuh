@@ -23,6 +23,12 @@ typedef __nv_bfloat16 bf16;
 #ifndef PTCG_AUX_TMA
 #define PTCG_AUX_TMA 1          // prefetch the saved GELU' operand by TMA
 #endif
+#ifndef PTCG_EPI_WARPS_AUX
+#define PTCG_EPI_WARPS_AUX 12   // epilogue warps of the GELU'-multiply GEMM (FFN2 dX)
+#endif
+#ifndef PTCG_AUX_BN_MAX
+#define PTCG_AUX_BN_MAX 256     // widest CTA tile of the GELU'-multiply GEMM
+#endif
 
 #define PTCG_DEV __device__ __forceinline__
 

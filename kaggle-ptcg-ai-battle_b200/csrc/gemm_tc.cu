@@ -50,10 +50,11 @@ constexpr int BM = 128;
 // split over fewer threads) keeps their epilogue free of spills.
 constexpr int NUM_EPI = PTCG_EPI_WARPS;
 constexpr int NUM_EPI_LIGHT = PTCG_EPI_WARPS_LIGHT;
+constexpr int NUM_EPI_AUX = PTCG_EPI_WARPS_AUX;
 constexpr int STAGE_BUFS = PTCG_STAGE_BUFS;  // TMA-store staging buffers per epilogue warp
 constexpr int STAGE_W = 4096 * STAGE_BUFS;   // staging bytes per epilogue warp
 constexpr int BIAS_SMEM_MAX = 4096;          // bias vectors up to this many columns live in smem
-static_assert(NUM_EPI % 4 == 0 && NUM_EPI_LIGHT % 4 == 0 && STAGE_BUFS >= 1 && STAGE_BUFS <= 2,
+static_assert(NUM_EPI % 4 == 0 && NUM_EPI_LIGHT % 4 == 0 && NUM_EPI_AUX % 4 == 0 && STAGE_BUFS >= 1 && STAGE_BUFS <= 2,
               "epilogue layout");
 // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
 constexpr int threads_for(int nepi) { return 64 + 32 * nepi; }
@@ -77,7 +78,8 @@ struct TcParams {
     uint32_t idesc;
     uint32_t stage_bytes, a_bytes;
     uint32_t tmem_cols, acc_stride;
-    int tma_out;             // outputs leave through smem staging + TMA stores
+    int tma_out;             // outputs leave through smem + TMA stores
+    uint32_t staging_bytes;  // per-warp TMA-store staging (0 when the epilogue stores in place)
     int bias_smem;           // columns of the bias staged in shared memory (0: read from global)
     int aux_tma;             // the GELU' operand arrives by TMA into two smem slots
     uint32_t aux_bytes;      // bytes of one slot: BM rows x bn bf16, as bn/32 boxes of 8 KB
@@ -323,8 +325,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int S = P.stages;
     constexpr int EPI_GROUPS = NEPI / 4;    // warps sharing a quadrant split its 32-column chunks
-    uint8_t* staging = smem + (size_t)S * P.stage_bytes;          // NEPI x STAGE_W
-    uint8_t* auxbuf = staging + (P.tma_out ? NEPI * STAGE_W : 0); // 2 x aux_bytes
+    uint8_t* staging = smem + (size_t)S * P.stage_bytes;          // NEPI x STAGE_W, or none
+    uint8_t* auxbuf = staging + P.staging_bytes;                  // 2 x aux_bytes
     uint64_t* bars = (uint64_t*)(auxbuf + (P.aux_tma ? 2 * P.aux_bytes : 0));
     // bars: full[S], empty[S], tfull[2], tempty[2], drain[1], afull[2], aempty[2]
     uint32_t* tmem_slot = (uint32_t*)(bars + 2 * S + 9);
@@ -547,34 +549,33 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     }
                     continue;
                 } else if constexpr (EK == EPI_GELU_AUX) {
-                    // v *= GELU' (prefetched by TMA into the tile's aux slot),
-                    // out through staging + TMA store, optional fp32 column sums
-                    uint8_t* sbuf = staging + (warp - 2) * STAGE_W + (nchunk % STAGE_BUFS) * 4096;
-                    nchunk++;
-                    if (lane == 0) {
-                        if (STAGE_BUFS == 2) bulk_wait_read1();
-                        else bulk_wait_read0();
-                    }
-                    __syncwarp();
-                    // row row_in_tile of box c0 / 32 (64-byte rows, 64-byte swizzle)
-                    const uint8_t* ab = auxbuf + (size_t)buf * P.aux_bytes + (c0 >> 5) * 8192 +
-                                        row_in_tile * 64;
+                    // v *= GELU' (prefetched by TMA into the tile's aux slot);
+                    // the bf16 product overwrites this row of the slot in
+                    // place (same 64-byte swizzle, so no staging buffer) and
+                    // leaves by a TMA store of the warp's 32-row box; the slot
+                    // is handed back to the producer once the stores have
+                    // read it.  Optional fp32 column sums of the product.
+                    uint8_t* box = auxbuf + (size_t)buf * P.aux_bytes + (c0 >> 5) * 8192;
+                    uint8_t* ab = box + row_in_tile * 64;
+                    const int sw = (row_in_tile >> 1) & 3;
                     #pragma unroll
                     for (int gq = 0; gq < 4; gq++) {
-                        uint4 q = *(const uint4*)(ab + ((gq ^ ((row_in_tile >> 1) & 3)) << 4));
-                        const __nv_bfloat162* h2 = (const __nv_bfloat162*)&q;
+                        uint4* p = (uint4*)(ab + ((gq ^ sw) << 4));
+                        uint4 q = *p;
+                        __nv_bfloat162* h2 = (__nv_bfloat162*)&q;
                         #pragma unroll
                         for (int k = 0; k < 4; k++) {
                             float2 f = __bfloat1622float2(h2[k]);
                             v[8 * gq + 2 * k] *= f.x;
                             v[8 * gq + 2 * k + 1] *= f.y;
+                            h2[k] = __floats2bfloat162_rn(v[8 * gq + 2 * k], v[8 * gq + 2 * k + 1]);
                         }
+                        *p = q;
                     }
-                    stage32(sbuf, lane, a.out_dtype, v);
                     fence_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        tma_store_2d(&map_c, smem_u32(sbuf), n0, mt * BM + quad * 32);
+                        tma_store_2d(&map_c, smem_u32(box + quad * 2048), n0, mt * BM + quad * 32);
                         bulk_commit();
                     }
                     if (a.colsum) {
@@ -768,7 +769,11 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(tempty0 + 8 * buf);
-                if (P.aux_tma) mbar_arrive(aempty0 + 8 * buf);
+                if (P.aux_tma) {
+                    // the in-place epilogue's stores read the slot itself
+                    if constexpr (EK == EPI_GELU_AUX) bulk_wait_read0();
+                    mbar_arrive(aempty0 + 8 * buf);
+                }
             }
             busy += clock64() - tb;
         }
@@ -958,7 +963,7 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     // slots of BM x bn): tiles of at most 128 columns leave room for them
     const bool aux_tma = PTCG_AUX_TMA && a.act == ACT_GELU_BWD && a.aux && a.aux_dtype == DT_BF16 &&
                          !((uintptr_t)a.aux & 15) && (a.ld_aux * 2) % 16 == 0 && a.remap_group == 0;
-    const int bn_max = aux_tma ? 128 : 256;
+    const int bn_max = aux_tma ? PTCG_AUX_BN_MAX : 256;
     int ntl = (a.N + bn_max - 1) / bn_max;
     int bn = ((a.N + ntl - 1) / ntl + 15) / 16 * 16;
     if (P.b_mn) bn = (bn + ATOM - 1) / ATOM * ATOM;
@@ -1014,12 +1019,15 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
         P.ek = EPI_GELU_SAVE;
     else if (simple && a.act == ACT_GELU && !a.out2 && P.bias_smem > 0 && !a.colsum && !a.resid)
         P.ek = EPI_GELU;
-    else if (simple && a.act == ACT_GELU_BWD && P.aux_tma && !a.bias && !a.out2 && !a.resid)
+    else if (simple && a.act == ACT_GELU_BWD && P.aux_tma && !a.bias && !a.out2 && !a.resid &&
+             a.out_dtype == DT_BF16 && P.box_rows == 32)
         P.ek = EPI_GELU_AUX;
     else if (simple && a.act == ACT_NONE && !a.out2 && (!a.bias || P.bias_smem > 0))
         P.ek = EPI_PLAIN + (a.bias ? 1 : 0) + (a.resid ? 2 : 0);
-    int budget = 232448 - 1024 - 512 - (P.tma_out ? P.nepi * STAGE_W : 0) - P.bias_smem * 4 -
-                 2 * (int)P.aux_bytes;
+    if (P.ek == EPI_GELU_AUX) P.nepi = NUM_EPI_AUX;
+    // the GELU'-multiply epilogue stores from the aux slot itself
+    P.staging_bytes = (P.tma_out && P.ek != EPI_GELU_AUX) ? (uint32_t)(P.nepi * STAGE_W) : 0u;
+    int budget = 232448 - 1024 - 512 - (int)P.staging_bytes - P.bias_smem * 4 - 2 * (int)P.aux_bytes;
     P.stages = budget / P.stage_bytes;
     if (P.stages > 6) P.stages = 6;
     if (P.stages < 2) return false;
@@ -1051,7 +1059,7 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
 
 void launch_tc(const TcPlan& pl, cudaStream_t s) {
     const TcParams& P = pl.P;
-    size_t smem = 1024 + (size_t)P.stages * P.stage_bytes + (P.tma_out ? P.nepi * STAGE_W : 0) +
+    size_t smem = 1024 + (size_t)P.stages * P.stage_bytes + (size_t)P.staging_bytes +
                   2 * (size_t)P.aux_bytes + (2 * P.stages + 9) * 8 + 48 + (size_t)P.bias_smem * 4;
     int total = P.m_tiles * P.n_tiles * P.splits;
     int grid = total < g_sms ? total : g_sms;
@@ -1064,7 +1072,7 @@ void launch_tc(const TcPlan& pl, cudaStream_t s) {
     } while (0)
     if (P.ek == EPI_GELU_SAVE) PTCG_TC_LAUNCH(2, NUM_EPI, EPI_GELU_SAVE);
     else if (P.ek == EPI_GELU) PTCG_TC_LAUNCH(2, NUM_EPI, EPI_GELU);
-    else if (P.ek == EPI_GELU_AUX) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_GELU_AUX);
+    else if (P.ek == EPI_GELU_AUX) PTCG_TC_LAUNCH(2, NUM_EPI_AUX, EPI_GELU_AUX);
     else if (P.ek == EPI_PLAIN) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_PLAIN);
     else if (P.ek == EPI_BIAS) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_BIAS);
     else if (P.ek == EPI_RESID) PTCG_TC_LAUNCH(2, NUM_EPI_LIGHT, EPI_RESID);

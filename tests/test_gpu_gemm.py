@@ -102,3 +102,35 @@ def test_fast_gelu_error_bound(pkg):
     ref_g, ref_dg = xd * cdf, cdf + xd * pdf
     assert ((g.double() - ref_g).abs() / xd.abs().clamp(min=1)).max().item() < 5e-7
     assert (dg.double() - ref_dg).abs().max().item() < 2e-6
+
+
+@pytest.mark.parametrize("M,N,K", [(264192 // 16, 1024, 256), (1000, 1024, 256), (777, 1000, 256),
+                                   (4099, 512, 128), (300, 96, 256)])
+def test_tc_gemm_gelu_grad_epilogue(pkg, M, N, K):
+    """the FFN2 dX form: bf16 out = (A B^T) * aux (the saved GELU'), fp32
+    column sums of the product added into colsum (the FFN1 bias gradient)"""
+    import ptcg_b200.native as n
+    lib = n.lib()
+    if not lib.ptcg_tensor_cores():
+        pytest.skip("no sm_100 device")
+    g = torch.Generator(device="cpu").manual_seed(M + N + K)
+    A = torch.randn(M, K, generator=g).bfloat16().cuda()
+    B = torch.randn(N, K, generator=g).bfloat16().cuda()
+    aux = torch.rand(M, N, generator=g).bfloat16().cuda()
+    out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+    colsum = torch.randn(N, generator=g).cuda()
+    prod = (A.float() @ B.float().t()) * aux.float()
+    ref_cs = colsum + prod.sum(0)
+    rc = lib.ptcg_gemm_ex(M, N, K, C.c_void_p(A.data_ptr()), K, 1, C.c_void_p(B.data_ptr()), K, 1,
+                          1, C.c_void_p(out.data_ptr()), N, 1, None, 2,
+                          C.c_void_p(aux.data_ptr()), N, None, 0,
+                          C.c_void_p(colsum.data_ptr()), 0, 1,
+                          C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert lib.ptcg_device_error() == 0
+    assert rc == 0, lib.ptcg_last_error()
+    assert not out.float().isnan().any()
+    err = (out.float() - prod).abs().max().item() / prod.abs().max().item()
+    assert err < 1e-2, err      # bf16 output rounding
+    cerr = (colsum - ref_cs).abs().max().item() / prod.abs().sum(0).max().item()
+    assert cerr < 1e-4, cerr
