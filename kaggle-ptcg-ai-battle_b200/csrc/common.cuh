@@ -48,18 +48,19 @@ PTCG_DEV float gelu_grad_f(float x) {
     float pdf = 0.3989422804014327f * expf(-0.5f * x * x);
     return cdf + x * pdf;
 }
-// GELU and GELU' for the tensor-core epilogues (the exact-fp32 SIMT path
-// keeps erff): two values at once on the packed f32x2 FP32 path
-// (fma/mul/add.rn.f32x2), with one exponential per value and no division:
-//   Phi(x) = 1/2 + sign(x) (1/2 - erfc(a)/2),  a = |x| / sqrt(2),
-//   erfc(a) = exp(-a^2) * R(min(a, 4)),
-// R a degree-10 polynomial least-squares fit of the scaled complementary
-// error function erfcx(a) = exp(a^2) erfc(a) on [0, 4] (weight exp(-a^2),
-// fitted in float64 for this file; beyond a = 4 erfc(a) < 2e-8 so the
-// clamp changes nothing in fp32).  |GELU error| <= 2e-7 max(|x|, 1) and
-// |GELU' error| <= 3e-7 over [-12, 12] (checked against fp64 torch on the
-// device).  exp(-x^2/2) = 2^(-x^2 log2(e) / 2) on ex2.approx, shared with
-// the normal pdf that GELU' needs.
+// GELU and GELU' for the tensor-core epilogues (bf16 mode; the exact-fp32
+// SIMT path keeps erff): two values at once on the packed f32x2 FP32 path
+// (fma/mul/add.rn.f32x2), one exponential per value and no division:
+//   pdf(x)   = 2^(-x^2 log2(e) / 2 + log2(1 / sqrt(2 pi)))      (ex2.approx)
+//   q(x)     = erfc(|x| / sqrt 2) / 2 = pdf(x) P(min(|x|, 4 sqrt 2))
+//   Phi(x)   = 1/2 + sign(x) (1/2 - q(x)),  GELU = x Phi,  GELU' = Phi + x pdf
+// P(u) = sqrt(pi / 2) erfcx(u / sqrt 2), a degree-7 polynomial fitted with
+// its error weighted by pdf (the error that reaches Phi; fit_gelu.py beside
+// this file prints the coefficients, negated so that 1/2 - q is one fma).
+// Beyond |x| = 4 sqrt 2, q < 1e-8 and the clamp changes nothing in fp32.
+// |Phi error| <= 4e-6, so |GELU error| <= 4e-6 max(|x|, 1) and |GELU'
+// error| <= 5e-6 over [-12, 12] (checked against fp64 torch on the device),
+// far below the bf16 rounding (2^-9 relative) of the stored activations.
 PTCG_DEV unsigned long long pk2(float a, float b) {
     unsigned long long r;
     asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
@@ -90,27 +91,35 @@ PTCG_DEV float ex2_approx(float x) {
 }
 PTCG_DEV unsigned long long splat2(float c) { return pk2(c, c); }
 
+// coefficients of -P (fit_gelu.py, degree 7), highest first
+#define PTCG_GELU_PN7 4.224045551e-04f
+#define PTCG_GELU_PN6 -5.811933428e-03f
+#define PTCG_GELU_PN5 3.489678726e-02f
+#define PTCG_GELU_PN4 -1.251721382e-01f
+#define PTCG_GELU_PN3 3.153921962e-01f
+#define PTCG_GELU_PN2 -6.215380430e-01f
+#define PTCG_GELU_PN1 9.994421005e-01f
+#define PTCG_GELU_PN0 -1.253304124e+00f
+#define PTCG_GELU_UMAX 5.656854249f            // 4 sqrt 2
+#define PTCG_GELU_S2 -0.72134752044448170f     // -log2(e) / 2
+#define PTCG_GELU_S0 -1.3257480647361595f      // log2(1 / sqrt(2 pi))
 #ifndef PTCG_GELU_SCALAR
 #define PTCG_GELU_SCALAR 0
 #endif
 #if PTCG_GELU_SCALAR
 PTCG_DEV void gelu1(float x, float& y, float& g) {
-    const float a = fminf(fabsf(x) * 0.70710678118654752f, 4.f);
-    float p = 9.721369133e-05f;
-    p = fmaf(p, a, -1.507143723e-03f);
-    p = fmaf(p, a, 1.044293307e-02f);
-    p = fmaf(p, a, -4.352428019e-02f);
-    p = fmaf(p, a, 1.251842678e-01f);
-    p = fmaf(p, a, -2.732950151e-01f);
-    p = fmaf(p, a, 4.882091582e-01f);
-    p = fmaf(p, a, -7.492768168e-01f);
-    p = fmaf(p, a, 9.996129870e-01f);
-    p = fmaf(p, a, -1.128359556e+00f);
-    p = fmaf(p, a, 9.999998212e-01f);
-    const float e = ex2_approx(x * x * -0.72134752044448170f);
-    const float h = fmaf(e * p, -0.5f, 0.5f);
-    const float cdf = 0.5f + copysignf(h, x);
-    g = fmaf(x, e * 0.3989422804014327f, cdf);
+    const float u = fminf(fabsf(x), PTCG_GELU_UMAX);
+    float p = PTCG_GELU_PN7;
+    p = fmaf(p, u, PTCG_GELU_PN6);
+    p = fmaf(p, u, PTCG_GELU_PN5);
+    p = fmaf(p, u, PTCG_GELU_PN4);
+    p = fmaf(p, u, PTCG_GELU_PN3);
+    p = fmaf(p, u, PTCG_GELU_PN2);
+    p = fmaf(p, u, PTCG_GELU_PN1);
+    p = fmaf(p, u, PTCG_GELU_PN0);
+    const float e = ex2_approx(fmaf(x * x, PTCG_GELU_S2, PTCG_GELU_S0));   // pdf(x)
+    const float cdf = 0.5f + copysignf(fmaf(e, p, 0.5f), x);
+    g = fmaf(x, e, cdf);
     y = x * cdf;
 }
 PTCG_DEV void gelu2(float x0, float x1, float& y0, float& y1, float& g0, float& g1) {
@@ -120,31 +129,29 @@ PTCG_DEV void gelu2(float x0, float x1, float& y0, float& y1, float& g0, float& 
 #else
 PTCG_DEV void gelu2(float x0, float x1, float& y0, float& y1, float& g0, float& g1) {
     const unsigned long long x = pk2(x0, x1);
-    const float a0 = fminf(fabsf(x0) * 0.70710678118654752f, 4.f);
-    const float a1 = fminf(fabsf(x1) * 0.70710678118654752f, 4.f);
-    const unsigned long long a = pk2(a0, a1);
-    unsigned long long p = splat2(9.721369133e-05f);
-    p = fma2(p, a, splat2(-1.507143723e-03f));
-    p = fma2(p, a, splat2(1.044293307e-02f));
-    p = fma2(p, a, splat2(-4.352428019e-02f));
-    p = fma2(p, a, splat2(1.251842678e-01f));
-    p = fma2(p, a, splat2(-2.732950151e-01f));
-    p = fma2(p, a, splat2(4.882091582e-01f));
-    p = fma2(p, a, splat2(-7.492768168e-01f));
-    p = fma2(p, a, splat2(9.996129870e-01f));
-    p = fma2(p, a, splat2(-1.128359556e+00f));
-    p = fma2(p, a, splat2(9.999998212e-01f));
+    const unsigned long long u = pk2(fminf(fabsf(x0), PTCG_GELU_UMAX), fminf(fabsf(x1), PTCG_GELU_UMAX));
+    unsigned long long p = splat2(PTCG_GELU_PN7);
+    p = fma2(p, u, splat2(PTCG_GELU_PN6));
+    p = fma2(p, u, splat2(PTCG_GELU_PN5));
+    p = fma2(p, u, splat2(PTCG_GELU_PN4));
+    p = fma2(p, u, splat2(PTCG_GELU_PN3));
+    p = fma2(p, u, splat2(PTCG_GELU_PN2));
+    p = fma2(p, u, splat2(PTCG_GELU_PN1));
+    p = fma2(p, u, splat2(PTCG_GELU_PN0));
     float s0, s1;
-    upk2(mul2(mul2(x, x), splat2(-0.72134752044448170f)), s0, s1);
-    const unsigned long long e = pk2(ex2_approx(s0), ex2_approx(s1));   // exp(-x^2/2)
+    upk2(fma2(mul2(x, x), splat2(PTCG_GELU_S2), splat2(PTCG_GELU_S0)), s0, s1);
+    const unsigned long long e = pk2(ex2_approx(s0), ex2_approx(s1));   // pdf(x)
     float h0, h1;
-    upk2(fma2(mul2(e, p), splat2(-0.5f), splat2(0.5f)), h0, h1);        // erf(a) / 2
+    upk2(fma2(e, p, splat2(0.5f)), h0, h1);                              // 1/2 - q(x)
     const unsigned long long cdf = add2(splat2(0.5f), pk2(copysignf(h0, x0), copysignf(h1, x1)));
-    const unsigned long long g = fma2(x, mul2(e, splat2(0.3989422804014327f)), cdf);
     upk2(mul2(x, cdf), y0, y1);
-    upk2(g, g0, g1);
+    upk2(fma2(x, e, cdf), g0, g1);
 }
 #endif
+// a0 += b0, a1 += b1 as one packed add
+PTCG_DEV void add_pair(float& a0, float& a1, float b0, float b1) {
+    upk2(add2(pk2(a0, a1), pk2(b0, b1)), a0, a1);
+}
 
 // torch F.softplus (beta 1, threshold 20)
 PTCG_DEV float softplus_f(float x) { return x > 20.f ? x : log1pf(expf(x)); }

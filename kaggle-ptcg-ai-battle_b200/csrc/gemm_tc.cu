@@ -518,7 +518,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                         #pragma unroll
                         for (int j = 0; j < 32; j += 4) {
                             float4 b4 = *(const float4*)(sbias + n0 + j);
-                            v[j] += b4.x; v[j + 1] += b4.y; v[j + 2] += b4.z; v[j + 3] += b4.w;
+                            add_pair(v[j], v[j + 1], b4.x, b4.y);
+                            add_pair(v[j + 2], v[j + 3], b4.z, b4.w);
                         }
                     } else {
                         #pragma unroll
