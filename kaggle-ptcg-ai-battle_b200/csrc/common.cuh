@@ -26,6 +26,9 @@ typedef __nv_bfloat16 bf16;
 #ifndef PTCG_EPI_WARPS_AUX
 #define PTCG_EPI_WARPS_AUX 12   // epilogue warps of the GELU'-multiply GEMM (FFN2 dX)
 #endif
+#ifndef PTCG_GEMM_M2
+#define PTCG_GEMM_M2 1          // 256-row CTA tiles for the fp32-accumulate (weight-gradient) GEMMs
+#endif
 #ifndef PTCG_AUX_BN_MAX
 #define PTCG_AUX_BN_MAX 256     // widest CTA tile of the GELU'-multiply GEMM
 #endif

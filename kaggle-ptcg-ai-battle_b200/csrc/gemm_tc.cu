@@ -86,6 +86,8 @@ struct TcParams {
     int nepi;                // epilogue warps of the instantiation that runs the plan
     int ek;                  // epilogue kind (EPI_*) of that instantiation
     int box_rows;            // rows of one TMA store box: 32, or 8 for a remap in 8-row groups
+    int m2;                  // CTA tile of two 128-row halves sharing each B stage (accumulators
+                             // at TMEM columns 0 and 256, one TMEM buffer); 0: one 128-row tile
     GemmArgs ep;
 };
 
@@ -324,6 +326,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int S = P.stages;
+    // 256-row tiles exist only in the generic light-epilogue instantiation
+    // (the plain fp32-accumulate GEMMs); elsewhere m2 folds to 0
+    const int m2 = (EK == EPI_GENERIC && NEPI == NUM_EPI_LIGHT) ? P.m2 : 0;
     constexpr int EPI_GROUPS = NEPI / 4;    // warps sharing a quadrant split its 32-column chunks
     uint8_t* staging = smem + (size_t)S * P.stage_bytes;          // NEPI x STAGE_W, or none
     uint8_t* auxbuf = staging + P.staging_bytes;                  // 2 x aux_bytes
@@ -403,7 +408,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     mbar_expect_tx(fb, P.stage_bytes);
                     uint32_t sa = smem_u32(smem + (size_t)stage * P.stage_bytes);
                     int k0 = kb * BK;
-                    load_operand<EB>(sa, &map_a, fb, P.a_mn, BM, mt * BM, k0);
+                    for (int h = 0; h <= m2; h++)
+                        load_operand<EB>(sa + h * BM * 128, &map_a, fb, P.a_mn, BM,
+                                         (mt << m2) * BM + h * BM, k0);
                     load_operand<EB>(sa + P.a_bytes, &map_b, fb, P.b_mn, P.b_rows, nt * P.bn, k0);
                     if (++stage == S) { stage = 0; phase ^= 1; }
                     (*n_issued)++;
@@ -423,8 +430,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                 int split = t % P.splits;
                 int kb0 = split * P.kb_per_split;
                 int kb1 = min(P.kb_total, kb0 + P.kb_per_split);
-                int buf = local & 1;
-                uint32_t tph = (local >> 1) & 1;
+                // two TMEM buffers alternate over tiles, or one (both halves) with m2
+                int buf = m2 ? 0 : local & 1;
+                uint32_t tph = m2 ? local & 1 : (local >> 1) & 1;
                 if (!mbar_wait(tempty0 + 8 * buf, tph ^ 1, abort_flag, 2, &w_tempty)) { ok = false; break; }
                 fence_after();
                 uint32_t dcol = tmem + buf * P.acc_stride;
@@ -440,6 +448,12 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                         uint64_t bd = P.b_mn ? make_desc(sb + s * KI * 128, BOX, MN_SBO, MN_LAYOUT)
                                              : make_desc(sb + s * 32, 16, 1024);
                         mma_issue<EB>(dcol, ad, bd, P.idesc, (kb > kb0 || s > 0) ? 1u : 0u);
+                        if (m2) {                   // rows 128..255: A half 16 KB on, same B
+                            const uint32_t sa2 = sa + BM * 128;
+                            uint64_t ad2 = P.a_mn ? make_desc(sa2 + s * KI * 128, BOX, MN_SBO, MN_LAYOUT)
+                                                  : make_desc(sa2 + s * 32, 16, 1024);
+                            mma_issue<EB>(dcol + 256, ad2, bd, P.idesc, (kb > kb0 || s > 0) ? 1u : 0u);
+                        }
                     }
                     mma_commit(empty0 + 8 * stage);
                     if (++stage == S) { stage = 0; phase ^= 1; }
@@ -472,8 +486,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             int split = t % P.splits;
             int mn = t / P.splits;
             int mt = mn / P.n_tiles, nt = mn % P.n_tiles;
-            int buf = local & 1;
-            uint32_t tph = (local >> 1) & 1;
+            int buf = m2 ? 0 : local & 1;
+            uint32_t tph = m2 ? local & 1 : (local >> 1) & 1;
             if (!mbar_wait(tfull0 + 8 * buf, tph, abort_flag, 4, &w_tfull)) break;
             if (P.aux_tma) {
                 if (!mbar_wait(afull0 + 8 * buf, tph, abort_flag, 6, &w_tfull)) break;
@@ -481,12 +495,14 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
             }
             long long tb = clock64();
             fence_after();
-            const int m = mt * BM + row_in_tile;
+            for (int h = 0; h <= m2; h++) {
+            const int row0 = (mt << m2) * BM + h * BM;   // first row of this 128-row half
+            const int m = row0 + row_in_tile;
             const bool row_ok = m < a.M;
             long orow = m;
             if (a.remap_group > 0)
                 orow = (long)(m / a.remap_group) * a.remap_stride + a.remap_off + (m % a.remap_group);
-            const uint32_t tbase = tmem + buf * P.acc_stride + ((uint32_t)(quad * 32) << 16);
+            const uint32_t tbase = tmem + (m2 ? h * 256 : buf * P.acc_stride) + ((uint32_t)(quad * 32) << 16);
             for (int c0 = grp * 32; c0 < P.bn; c0 += 32 * EPI_GROUPS) {
                 uint32_t r[32];
                 tmem_ld32(tbase + c0, r);
@@ -542,7 +558,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     fence_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        const int y = mt * BM + quad * 32;
+                        const int y = row0 + quad * 32;
                         tma_store_2d(&map_c, smem_u32(sbuf), n0, y);
                         if constexpr (EK == EPI_GELU_SAVE)
                             tma_store_2d(&map_c2, smem_u32(sbuf + 2048), n0, y);
@@ -576,7 +592,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     fence_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        tma_store_2d(&map_c, smem_u32(box + quad * 2048), n0, mt * BM + quad * 32);
+                        tma_store_2d(&map_c, smem_u32(box + quad * 2048), n0, row0 + quad * 32);
                         bulk_commit();
                     }
                     if (a.colsum) {
@@ -621,7 +637,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     fence_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        tma_store_2d(&map_c, smem_u32(sbuf), n0, mt * BM + quad * 32);
+                        tma_store_2d(&map_c, smem_u32(sbuf), n0, row0 + quad * 32);
                         bulk_commit();
                     }
                     if (a.colsum) {
@@ -740,7 +756,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     fence_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        int y = mt * BM + quad * 32;
+                        int y = row0 + quad * 32;
                         if (P.box_rows == 8) {                   // four 8-row boxes, each remapped
                             const uint32_t rb = a.out_dtype == DT_F32 ? 128u : 64u;
                             for (int i = 0; i < 4; i++) {
@@ -765,6 +781,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     if (lane < nvalid) atomicAdd(&a.colsum[n0 + lane], cs);
                 }
             }
+            }   // halves
             (void)split;
             fence_before();
             __syncwarp();
@@ -972,13 +989,17 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     if (aux_tma && bn % 32) bn = (bn + 31) / 32 * 32;
     P.bn = bn;
     P.b_rows = bn;
-    P.m_tiles = (a.M + BM - 1) / BM;
+    bool plain = a.accumulate && a.out_dtype == DT_F32 && !a.bias && !a.bcast &&
+                 a.act == ACT_NONE && !a.resid && !a.out2 && a.remap_group == 0 && !a.colsum;
+    // the weight-gradient form (fp32 accumulate, no epilogue operand): CTA
+    // tiles of 256 rows, two M = 128 MMAs on each B stage, which cuts the
+    // operand bytes each SM pulls through L2 per FLOP by a third
+    P.m2 = (PTCG_GEMM_M2 && plain && a.M > BM) ? 1 : 0;   // runs on <EB, NUM_EPI_LIGHT, EPI_GENERIC>
+    P.m_tiles = (a.M + (BM << P.m2) - 1) / (BM << P.m2);
     P.n_tiles = (a.N + bn - 1) / bn;
     P.kb_total = (a.K + BK - 1) / BK;
     int tiles = P.m_tiles * P.n_tiles;
     P.splits = 1;
-    bool plain = a.accumulate && a.out_dtype == DT_F32 && !a.bias && !a.bcast &&
-                 a.act == ACT_NONE && !a.resid && !a.out2 && a.remap_group == 0 && !a.colsum;
     if (plain && tiles < g_sms && P.kb_total >= 8) {
         // one wave: tiles x splits <= SMs (a split item is a long K range,
         // so even one CTA with a second item doubles the launch)
@@ -989,7 +1010,7 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     }
     P.kb_per_split = (P.kb_total + P.splits - 1) / P.splits;
     P.splits = (P.kb_total + P.kb_per_split - 1) / P.kb_per_split;   // no empty splits
-    P.a_bytes = BM * 128;
+    P.a_bytes = (BM * 128) << P.m2;
     P.stage_bytes = P.a_bytes + P.b_rows * 128;
     // outputs through smem + TMA store: plain row mapping, no read-modify-
     // write, whole 32-column chunks per tile, 16-byte aligned pitch
@@ -1032,7 +1053,7 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     P.stages = budget / P.stage_bytes;
     if (P.stages > 6) P.stages = 6;
     if (P.stages < 2) return false;
-    P.acc_stride = bn <= 128 ? 128 : 256;
+    P.acc_stride = (bn <= 128 && !P.m2) ? 128 : 256;
     P.tmem_cols = 2 * P.acc_stride;
     // instruction descriptor: f32 accumulate, A/B format (1 bf16, 2 tf32),
     // majorness, N>>3, M>>4

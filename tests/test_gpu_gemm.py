@@ -65,6 +65,24 @@ def test_tc_gemm_split_k_accumulate(pkg, M, N, K):
     assert err < 1e-3, err
 
 
+@pytest.mark.parametrize("a_k,b_k", [(1, 1), (1, 0), (0, 0), (0, 1)])
+@pytest.mark.parametrize("M,N,K", [(300, 144, 9000), (129, 1000, 3000), (640, 264, 4000),
+                                   (1000, 256, 777)])
+def test_tc_gemm_accumulate_row_pairs(pkg, a_k, b_k, M, N, K):
+    """fp32-accumulate GEMMs run 256-row CTA tiles (two 128-row halves on one
+    B stage): ragged M (a half past M, a tile half past M), every majorness,
+    with and without the split over K"""
+    import ptcg_b200.native as n
+    lib = n.lib()
+    if not lib.ptcg_tensor_cores():
+        pytest.skip("no sm_100 device")
+    rc, out, ref = run_gemm(lib, M, N, K, a_k, b_k, engine=1, acc=True, seed=M + K)
+    assert lib.ptcg_device_error() == 0
+    assert rc == 0, lib.ptcg_last_error()
+    err = (out - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-3, err
+
+
 def _tf32(x):
     """round-toward-zero to the 10-bit TF32 mantissa (what kind::tf32 reads)"""
     return (x.view(torch.int32) & ~0x1FFF).view(torch.float32)
