@@ -452,10 +452,11 @@ int ptcg_attention_bwd(int operand_dtype, const void* qkv, long ldqkv, const uns
                        const void* out, long ldo, const void* dout, long lddo, const float* lse,
                        void* dqkv, long lddqkv, float* dbias, int nseq, int L, int H,
                        void* stream);
-/* The GELU and GELU' that the tensor-core GEMM epilogues evaluate (erfc as
- * exp(-a^2) times a degree-10 least-squares fit of erfcx on [0, 4], made for
- * this library), exposed so tests can bound their error against the exact
- * erf form of torch nn.GELU. */
+/* The GELU and GELU' that the tensor-core GEMM epilogues evaluate (the
+ * normal tail erfc(|x|/sqrt 2)/2 as the normal pdf times a degree-7
+ * polynomial in |x|, fitted for this library with its error weighted by the
+ * pdf; |error| <= 5e-6), exposed so tests can bound their error against the
+ * exact erf form of torch nn.GELU. */
 int ptcg_eval_gelu(const float* x, float* gelu, float* gelu_grad, int n, void* stream);
 /* tcgen05 GEMM role counters (clock cycles, summed over CTAs): {producer
  * waiting for free ring slots, MMA waiting for loaded slots, MMA waiting for
