@@ -676,6 +676,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     }
                     __syncwarp();
                 }
+                // fp32 GELU with its fp32 GELU' (TF32 GEMMs): both chunks go
+                // through the one staging buffer, GELU' first (stored below)
+                const bool f32pair = P.tma_out && a.act == ACT_GELU && a.out2 && a.out_dtype == DT_F32;
                 if (row_ok) {
                 float t[32];
                 if (a.bias) {
@@ -706,7 +709,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                         #pragma unroll
                         for (int j = 0; j < 32; j += 2)        // GELU'(x) saved for backward
                             gelu2(v[j], v[j + 1], v[j], v[j + 1], t[j], t[j + 1]);
-                        if (P.tma_out) stage32(sbuf + 2048, lane, DT_BF16, t);
+                        if (P.tma_out) {
+                            if (f32pair) stage32(sbuf, lane, DT_F32, t);
+                            else stage32(sbuf + 2048, lane, DT_BF16, t);
+                        }
                         else store32(a.out2, (long)m * a.ldo2 + n0, a.out2_dtype, t, nvalid);
                     } else {
                         #pragma unroll
@@ -746,12 +752,27 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                     #pragma unroll
                     for (int j = 0; j < 32; j++) v[j] += t[j];
                 }
-                if (P.tma_out) stage32(sbuf, lane, a.out_dtype, v);
-                else store32(a.out, orow * a.ldo + n0, a.out_dtype, v, nvalid);
+                if (P.tma_out) {
+                    if (!f32pair) stage32(sbuf, lane, a.out_dtype, v);
+                } else {
+                    store32(a.out, orow * a.ldo + n0, a.out_dtype, v, nvalid);
+                }
                 if (!P.tma_out && a.act != ACT_GELU && a.out2)
                     store32(a.out2, orow * a.ldo2 + n0, a.out2_dtype, v, nvalid);
                 }   // row_ok
                 if (P.tma_out) {
+                    if (f32pair) {
+                        // GELU' (staged above) out first, then GELU (v) into the same buffer
+                        fence_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&map_c2, smem_u32(sbuf), n0, row0 + quad * 32);
+                            bulk_commit();
+                            bulk_wait_read0();
+                        }
+                        __syncwarp();
+                        if (row_ok) stage32(sbuf, lane, DT_F32, v);
+                    }
                     // rows past M and columns past N are clipped by the TMA unit
                     fence_async_smem();
                     __syncwarp();
@@ -769,7 +790,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
                             if (a.remap_group > 0)               // the box's first output row
                                 y = (y / a.remap_group) * a.remap_stride + a.remap_off + y % a.remap_group;
                             tma_store_2d(&map_c, smem_u32(sbuf), n0, y);
-                            if (a.act == ACT_GELU && a.out2) tma_store_2d(&map_c2, smem_u32(sbuf + 2048), n0, y);
+                            if (a.act == ACT_GELU && a.out2 && !f32pair)
+                                tma_store_2d(&map_c2, smem_u32(sbuf + 2048), n0, y);
                         }
                         bulk_commit();
                     }
@@ -1025,8 +1047,9 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     P.box_rows = (a.remap_group > 0 && a.remap_group % 32 != 0) ? 8 : 32;
     P.tma_out = P.splits == 1 && remap_ok && !a.accumulate && (bn % 32) == 0 &&
                 !((uintptr_t)a.out & 15) && (a.ldo * oeb) % 16 == 0 &&
-                (!a.out2 || (a.act == ACT_GELU && a.out2_dtype == DT_BF16 && a.out_dtype == DT_BF16 &&
-                             !((uintptr_t)a.out2 & 15) && (a.ldo2 * 2) % 16 == 0));
+                (!a.out2 || (a.act == ACT_GELU && a.out2_dtype == a.out_dtype &&
+                             (a.out_dtype == DT_BF16 || !a.resid) &&   // fp32: t holds GELU' to the store
+                             !((uintptr_t)a.out2 & 15) && (a.ldo2 * oeb) % 16 == 0));
     P.bias_smem = (PTCG_BIAS_SMEM && a.bias && a.N <= BIAS_SMEM_MAX) ? a.N : 0;
     P.aux_tma = aux_tma && P.splits == 1;
     P.aux_bytes = P.aux_tma ? (uint32_t)(bn / 32) * 8192u : 0u;
@@ -1074,7 +1097,7 @@ bool plan_tc(const GemmArgs& a, TcPlan& pl) {
     if (P.tma_out) {
         const long out_rows = a.remap_group > 0 ? (long)(a.M / a.remap_group) * a.remap_stride : a.M;
         if (!make_out_map(&pl.mc, a.out, a.N, out_rows, a.ldo, a.out_dtype, P.box_rows)) return false;
-        if (a.out2 && !make_out_map(&pl.mc2, a.out2, a.N, a.M, a.ldo2, DT_BF16)) return false;
+        if (a.out2 && !make_out_map(&pl.mc2, a.out2, a.N, a.M, a.ldo2, a.out2_dtype)) return false;
     }
     return true;
 }
