@@ -127,10 +127,12 @@ def test_fast_gelu_error_bound(pkg):
 
 
 @pytest.mark.parametrize("M,N,K", [(264192 // 16, 1024, 256), (1000, 1024, 256), (777, 1000, 256),
-                                   (4099, 512, 128), (300, 96, 256)])
+                                   (4099, 512, 128), (300, 96, 256), (20000, 768, 256)])
 def test_tc_gemm_gelu_grad_epilogue(pkg, M, N, K):
     """the FFN2 dX form: bf16 out = (A B^T) * aux (the saved GELU'), fp32
-    column sums of the product added into colsum (the FFN1 bias gradient)"""
+    column sums of the product added into colsum (the FFN1 bias gradient);
+    the last shape has 3 column tiles on a 148-CTA grid, so a CTA's tiles
+    change columns"""
     import ptcg_b200.native as n
     lib = n.lib()
     if not lib.ptcg_tensor_cores():
