@@ -38,8 +38,11 @@ def run_gemm(lib, M, N, K, a_k, b_k, engine, acc=False, seed=0, dtype=torch.bflo
 @pytest.mark.parametrize("a_k,b_k", [(1, 1), (1, 0), (0, 0), (0, 1)])
 @pytest.mark.parametrize("M,N,K", [(256, 256, 256), (300, 144, 200), (1000, 768, 256),
                                    (129, 1024, 64), (4096, 300, 256), (514, 1536, 512),
-                                   (514, 512, 2048), (514, 2048, 512), (1536, 512, 514)])
+                                   (514, 512, 2048), (514, 2048, 512), (1536, 512, 514),
+                                   (1000, 256, 1024), (777, 200, 768)])
 def test_tc_gemm_matches_fp32(pkg, a_k, b_k, M, N, K):
+    """(the last two shapes: long-K GEMMs of at most 256 columns, the FFN1 /
+    QKV dX form, with ragged M)"""
     import ptcg_b200.native as n
     lib = n.lib()
     if not lib.ptcg_tensor_cores():
