@@ -105,9 +105,22 @@ def test_train_step_graph(pkg):
 
     def rel(x, y):
         return ((x - y).norm() / y.norm()).item()
-    # the fp32 atomic accumulations (split-K weight gradients, column sums)
-    # make two eager runs differ slightly; the replay must be as close
-    noise = rel(g_eager2, g_eager)
-    assert rel(g_graph, g_eager) <= max(4 * noise, 1e-6), (rel(g_graph, g_eager), noise)
-    assert rel(w_graph, w_eager) <= max(4 * rel(w_eager2, w_eager), 1e-6)
+    # The split-K weight gradients and the bias-gradient column sums add
+    # with fp32 atomics in an order that follows the launch timing: runs of
+    # one launch mode tend to agree with each other, and a replay and an
+    # eager run differ at that rounding level (measured 2e-6 to 7e-5 of the
+    # gradient norm between runs at this size).  One eager-vs-eager pair is
+    # no estimate of it, since two eager runs can agree by timing alone.
+    assert rel(g_graph, g_eager) <= 2e-4, rel(g_graph, g_eager)
+    assert rel(g_eager2, g_eager) <= 2e-4, rel(g_eager2, g_eager)
+    # Adam's first step moves a weight by lr * g / (|g| + eps): about lr *
+    # sign(g).  Where the gradient is well above rounding noise the two
+    # updates agree; elsewhere a rounding-level gradient may change sign,
+    # which moves that weight by at most 2 lr.
+    lr = 3e-4
+    dw = (w_graph - w_eager).abs()
+    big = g_eager.abs() > 1e-4 * g_eager.abs().max()
+    assert big.any()
+    assert dw[big].max().item() <= 1e-6, dw[big].max().item()
+    assert dw.max().item() <= 2 * lr * 1.001, dw.max().item()
     np.testing.assert_allclose(st_graph.cpu().numpy(), st_eager.cpu().numpy(), rtol=1e-4, atol=1e-6)
