@@ -501,9 +501,11 @@ def main():
     pol.kernel_timer(0)
     adam_ms = adam_kms / max(1, adam_n)
 
-    # --- write-only HBM bandwidth of this GPU (a 2 GiB fill): the roof of
-    #     GEMMs whose traffic is mostly their bf16 outputs
-    wbuf = torch.empty(1 << 30, dtype=torch.bfloat16, device=dev)
+    # --- write-only HBM bandwidth of this GPU (a 2 GiB fp32 fill): the roof
+    #     of GEMMs whose traffic is mostly their outputs.  torch's 1- and
+    #     2-byte fills reach about half the rate of its 4-byte fill here, so
+    #     the buffer is fp32
+    wbuf = torch.empty(1 << 29, dtype=torch.float32, device=dev)
     for _ in range(3):
         wbuf.fill_(1.0)
     w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -513,7 +515,7 @@ def main():
         wbuf.fill_(2.0)
     w1.record()
     torch.cuda.synchronize()
-    write_gbs = 10 * wbuf.numel() * 2 / (w0.elapsed_time(w1) / 1e3) / 1e9
+    write_gbs = 10 * wbuf.numel() * wbuf.element_size() / (w0.elapsed_time(w1) / 1e3) / 1e9
     del wbuf
 
     # --- rollout forward (config 1): fresh observations every env step.
