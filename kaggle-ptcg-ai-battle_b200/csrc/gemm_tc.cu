@@ -4,7 +4,9 @@
 //   C[M, N] = epilogue( sum_k A(m, k) * B(n, k) )
 //
 // * CTA tile 128 x BN (BN <= 256, multiple of 16; multiple of 64 when B is
-//   MN-major), K block 64 elements (one 128-byte swizzled row).
+//   MN-major), K block 64 elements (one 128-byte swizzled row).  The
+//   fp32-accumulate GEMMs (weight gradients) run 256 x BN tiles: two M = 128
+//   MMAs per K step on one B stage, accumulators at TMEM columns 0 and 256.
 // * Operands arrive by TMA (cp.async.bulk.tensor, 128B swizzle, no
 //   multicast) into a multi-stage shared-memory ring.  K-major operands load
 //   one box {64 K, rows}; MN-major operands (the transposed side of dX / dW
@@ -22,8 +24,9 @@
 //   (staged once per CTA in shared memory) / broadcast / GELU and GELU'
 //   (packed f32x2 math) / GELU' multiply / row remap / residual /
 //   accumulate / fp32 column sums.  Whole 32x32 chunks leave through a
-//   swizzled shared staging buffer and a TMA store; the rest through
-//   vectorised global stores.  The epilogue, not the MMA, bounds the K = 256
+//   swizzled shared staging buffer and a TMA store (the GELU'-multiply
+//   epilogue stores from the TMA-filled GELU' slot itself, overwritten in
+//   place); the rest through vectorised global stores.  The epilogue, not the MMA, bounds the K = 256
 //   GEMMs of this model, so its warp count hides the latency of TMEM loads,
 //   operand loads and store fences.
 // * Persistent CTAs (one per SM) walk an M-major tile order so that the
