@@ -21,10 +21,10 @@
 // the chunks in the unfused FFN2's K order.  Every wait is bounded.
 //
 // Measured on a B200 (c0, 1024 agents, the rollout graph): 3.41 ms per
-// forward with this kernel against 3.01-3.05 ms with the two GEMMs, so it is
-// off by default (ptcg_set_fused_mlp).  The GELU of the hidden units, which
-// the unfused FFN1 epilogue also computes, bounds both; here it sits between
-// each chunk's H and Y MMAs instead of overlapping another tile's MMAs.
+// forward with this kernel against 2.91-3.05 ms with the two GEMMs, with
+// either epilogue GELU, so it is off by default (ptcg_set_fused_mlp).  Each
+// 128-row tile streams all of W1 and W2 (1 MB at d 256, ffn 1024) through
+// L2 into shared memory, more than L2 delivers at the MMA rate.
 #include <algorithm>
 
 #include "common.cuh"
